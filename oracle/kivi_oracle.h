@@ -1,0 +1,122 @@
+/*
+ * kivi_oracle.h -- CPU restatement of the reference kivi-cache crate (v0.6.0,
+ * bieli/kivi-cache-rs) for the KIVI decode hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY. This library is the parity checker for the GPU
+ * implementation and the timed CPU baseline. Only tests/, __graft_entry__.smoke()
+ * and bench.py (cpu_baseline leg and --impl reference) load it. The product
+ * library (libkivi_gpu.so) never links or calls it.
+ *
+ * Every routine restates the reference arithmetic in the same order with the
+ * same fp32 operations (fmaf where Rust calls mul_add, plain ops elsewhere,
+ * compiled with -ffp-contract=off and no fast-math), so that its outputs are
+ * bit-identical to the Rust crate. Parity is pinned against the reference's
+ * own known-answer tests (tests/quant.rs, examples/pytorch_golden.rs,
+ * tests/cache.rs, tests/attention.rs, tests/prefix.rs, tests/budget.rs),
+ * ported in tests/test_oracle_pins.py.
+ */
+#ifndef KIVI_ORACLE_H
+#define KIVI_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Error codes: identical numbering to include/kivi_gpu.h (KiviError variants,
+ * src/error.rs:4-45). */
+enum {
+    KO_OK = 0,
+    KO_INVALID_BITS = 1,
+    KO_MISALIGNED_GROUP = 2,
+    KO_RESIDUAL_LENGTH = 3,
+    KO_HEAD_DIM = 4,
+    KO_TOKEN_GROUP = 5,
+    KO_ZERO_DIMENSION = 6,
+    KO_SHAPE = 7,
+    KO_QUERY_HEADS = 8,
+    KO_EARLY_LAYERS = 9
+};
+
+typedef struct ko_error {
+    int32_t code;
+    uint64_t a; /* first payload field (e.g. expected, bits, group_size) */
+    uint64_t b; /* second payload field (e.g. actual) */
+    const char *name; /* ZeroDimension name */
+} ko_error;
+
+typedef struct ko_cache ko_cache;
+typedef struct ko_prefix ko_prefix;
+typedef struct ko_session ko_session;
+
+/* config.rs:31-55 */
+int ko_config_check(uint8_t bits, size_t group_size, size_t residual_length, ko_error *err);
+
+/* cache.rs:87-120 */
+ko_cache *ko_cache_new(uint8_t bits, size_t group_size, size_t residual_length,
+                       size_t batch, size_t heads, size_t head_dim, ko_error *err);
+void ko_cache_free(ko_cache *c);
+/* cache.rs:186-214 ; keys/values [batch, heads, seq, head_dim] */
+int ko_cache_append(ko_cache *c, const float *keys, size_t keys_len, const float *values,
+                    size_t values_len, size_t seq, ko_error *err);
+/* cache.rs:224-279 ; threads = worker threads over (b, qh) pairs (1 = the
+ * reference's own serial loop; results are bit-identical for any count). */
+int ko_cache_attention(const ko_cache *c, const float *query, size_t query_len,
+                       size_t num_q_heads, float scale, float *out, int threads, ko_error *err);
+/* Same attention evaluated in fp64 over the fp32 dequantized cache (for error attribution). */
+int ko_cache_attention_f64(const ko_cache *c, const float *query, size_t num_q_heads,
+                           float scale, double *out);
+/* cache.rs:282-325 ; keys/values sized batch*heads*seq*head_dim */
+void ko_cache_dequantize(const ko_cache *c, float *keys, float *values);
+/* cache.rs:362-380 ; out[10] = tokens, key_code, key_meta, value_code, value_meta,
+ * key_residual, value_residual, residual_capacity, fp16_baseline, fp32_baseline */
+void ko_cache_memory(const ko_cache *c, uint64_t out[10]);
+/* out[5] = seq, key_res_len, value_res_len, quantized_key_tokens, quantized_value_tokens */
+void ko_cache_state(const ko_cache *c, uint64_t out[5]);
+/* PackedStream export: stream hi of keys (axis 0) or values (axis 1). Pass NULL to query sizes. */
+void ko_cache_export_stream(const ko_cache *c, size_t hi, int axis, uint32_t *codes,
+                            size_t *ncodes, float *params, size_t *nparams);
+
+/* prefix.rs:74-153 */
+ko_prefix *ko_prefix_from_cache(const ko_cache *c);
+void ko_prefix_free(ko_prefix *p);
+ko_session *ko_session_new(const ko_prefix *p);
+void ko_session_free(ko_session *s);
+/* prefix.rs:173-223 */
+int ko_session_append(ko_session *s, const float *keys, size_t keys_len, const float *values,
+                      size_t values_len, size_t seq, ko_error *err);
+/* prefix.rs:228-290 */
+int ko_session_attention(const ko_session *s, const float *query, size_t query_len,
+                         size_t num_q_heads, float scale, float *out, int threads, ko_error *err);
+size_t ko_session_question_tokens(const ko_session *s);
+
+/* quant.rs:154-233: codes/params concatenated over the batch*heads streams, in
+ * PackedStream order. Pass NULL outputs to query sizes. */
+int ko_quantize(int per_channel, const float *data, size_t data_len, size_t batch, size_t heads,
+                size_t tokens, size_t head_dim, uint8_t bits, size_t group_size, uint32_t *codes,
+                size_t *ncodes, float *params, size_t *nparams, ko_error *err);
+/* quant.rs:124-150 (QuantizedTensor::dequantize) over the concatenated layout above */
+void ko_dequantize_packed(int per_channel, const uint32_t *codes, const float *params,
+                          size_t batch, size_t heads, size_t tokens, size_t head_dim,
+                          uint8_t bits, size_t group_size, float *out);
+/* quant.rs:77-112 (QuantizedTensor::pytorch_codes) */
+void ko_pytorch_codes(int per_channel, const uint32_t *codes, size_t batch, size_t heads,
+                      size_t tokens, size_t head_dim, uint8_t bits, size_t group_size,
+                      uint32_t *out);
+
+/* budget.rs:317-371 */
+uint64_t ko_layer_kv_bytes(uint8_t bits, size_t group_size, size_t residual_length,
+                           size_t num_kv_heads, size_t head_dim, size_t tokens);
+uint64_t ko_marginal_bytes_per_layer(uint8_t bits, size_t group_size, size_t num_kv_heads,
+                                     size_t head_dim);
+
+/* quant.rs:474-485 */
+float ko_round_half_even(float x);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif
