@@ -1,0 +1,320 @@
+/*
+ * kivi_gpu.h -- C ABI of the B200-native KIVI decode path (libkivi_gpu.so).
+ *
+ * This is the drop-in boundary for the public Rust API of kivi-cache v0.6.0
+ * (bieli/kivi-cache-rs, exports at src/lib.rs:49-65).  A `kivi-cache-sys`
+ * crate binds these symbols one-to-one and the safe
+ * crate keeps the reference signatures (KiviConfig, KiviCache, SharedPrefix,
+ * RagSession, RuntimeKv, MemoryReport, budget math).
+ *
+ * Conventions
+ *  - Every fallible call returns int32_t: 0 (KIVI_OK) or a kivi_status code,
+ *    and fills the optional kivi_error* with the KiviError payload
+ *    (src/error.rs:4-45).  Argument checks run before any mutation, in the
+ *    reference's order, so a failed call leaves the handle unchanged.
+ *  - Dense buffers are fp32, row-major [batch, num_kv_heads, seq, head_dim]
+ *    (cache.rs:62-63); queries/outputs [batch, num_q_heads, head_dim].
+ *    Every host buffer is passed with its element count so Shape errors
+ *    match the reference's slice-length checks.
+ *  - Host-pointer calls are synchronous (drop-in semantics).  `_dev` calls
+ *    take device pointers and a cudaStream_t (passed as void*, used exactly as
+ *    given: NULL is the legacy default stream) and are stream-ordered; they
+ *    return once the work is enqueued.  A host-pointer call on a handle waits
+ *    for the handle's last `_dev` call, so the two kinds can be mixed.
+ *  - A handle is externally synchronised: one writer or many readers, as with
+ *    Rust's &mut / & borrows.  Counters are mirrored on the host, so getters
+ *    and kivi_cache_memory never synchronise the device.
+ *  - No torch or CUDA types appear in these signatures.
+ */
+#ifndef KIVI_GPU_H
+#define KIVI_GPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KIVI_GPU_ABI_VERSION 1
+
+/* KiviError variants (src/error.rs:4-45) plus device-side failures. */
+typedef enum kivi_status {
+    KIVI_OK = 0,
+    KIVI_ERR_INVALID_BITS = 1,       /* InvalidBits(a = bits) */
+    KIVI_ERR_MISALIGNED_GROUP = 2,   /* MisalignedGroup{a = group_size, b = bits} */
+    KIVI_ERR_RESIDUAL_LENGTH = 3,    /* ResidualLength{a = residual_length, b = group_size} */
+    KIVI_ERR_HEAD_DIM = 4,           /* HeadDim{a = head_dim, b = group_size} */
+    KIVI_ERR_TOKEN_GROUP = 5,        /* TokenGroup{a = tokens, b = group_size} */
+    KIVI_ERR_ZERO_DIMENSION = 6,     /* ZeroDimension(name) */
+    KIVI_ERR_SHAPE = 7,              /* Shape{a = expected, b = actual} */
+    KIVI_ERR_QUERY_HEADS = 8,        /* QueryHeads{a = num_q_heads, b = num_kv_heads} */
+    KIVI_ERR_EARLY_LAYERS = 9,       /* EarlyLayers{a = early_layers, b = num_layers} */
+    KIVI_ERR_CUDA = 100,             /* a = cudaError_t value; message holds its name */
+    KIVI_ERR_INVALID_ARGUMENT = 101, /* null handle/pointer, index out of range, mixed prefixes */
+    KIVI_ERR_OUT_OF_MEMORY = 102,    /* device allocation failed */
+    KIVI_ERR_UNSUPPORTED = 103       /* shape beyond what the device kernels support */
+} kivi_status;
+
+typedef struct kivi_error {
+    int32_t code;
+    uint64_t a;
+    uint64_t b;
+    const char *name;   /* ZeroDimension field name (static string) or NULL */
+    char message[192];  /* human-readable text, KiviError's Display (error.rs:102-150) */
+} kivi_error;
+
+/* KiviConfig (src/config.rs:8-18). */
+typedef struct kivi_config {
+    uint32_t bits;
+    uint64_t group_size;
+    uint64_t residual_length;
+} kivi_config;
+
+/* MemoryReport (src/cache.rs:24-36). */
+typedef struct kivi_memory_report {
+    uint64_t tokens;
+    uint64_t key_code_bytes;
+    uint64_t key_metadata_bytes;
+    uint64_t value_code_bytes;
+    uint64_t value_metadata_bytes;
+    uint64_t key_residual_bytes;
+    uint64_t value_residual_bytes;
+    uint64_t residual_capacity_bytes;
+    uint64_t fp16_baseline_bytes;
+    uint64_t fp32_baseline_bytes;
+} kivi_memory_report;
+
+/* Getters of KiviCache / SharedPrefix (cache.rs:122-156, prefix.rs:94-117). */
+typedef struct kivi_cache_state {
+    kivi_config config;
+    uint64_t batch;
+    uint64_t num_kv_heads;
+    uint64_t head_dim;
+    uint64_t sequence_length;
+    uint64_t key_residual_len;
+    uint64_t value_residual_len;
+    uint64_t quantized_key_tokens;
+    uint64_t quantized_value_tokens;
+    uint64_t capacity_tokens; /* device capacity per stream (packed tokens) */
+    int32_t device;
+} kivi_cache_state;
+
+/* MemoryBudgetSnapshot (src/budget.rs:21-35). */
+typedef struct kivi_budget_snapshot {
+    uint64_t tokens_until_key_flush;
+    uint64_t key_residual_tokens;
+    uint64_t value_residual_tokens;
+    uint64_t sequence_tokens;
+    uint64_t current_layer_bytes;
+    uint64_t marginal_bytes_per_token;
+    uint64_t residual_capacity_bytes;
+} kivi_budget_snapshot;
+
+/* SharedPrefixFootprint (src/prefix.rs:50-60). */
+typedef struct kivi_prefix_footprint {
+    uint64_t prefix_tokens;
+    uint64_t question_tokens;
+    uint64_t sessions;
+    uint64_t prefix_bytes;
+    uint64_t question_bytes;
+    uint64_t shared_total_bytes;
+    uint64_t fp16_per_user_bytes;
+    uint64_t fp16_all_users_bytes;
+} kivi_prefix_footprint;
+
+typedef struct kivi_cache kivi_cache;     /* KiviCache (cache.rs:71-83) */
+typedef struct kivi_prefix kivi_prefix;   /* SharedPrefix (prefix.rs:32-35), refcounted */
+typedef struct kivi_session kivi_session; /* RagSession (prefix.rs:41-46) */
+
+/* ---------------------------------------------------------------- library */
+
+int32_t kivi_abi_version(void);
+/* KiviError's Display text for a status (error.rs:102-150). */
+const char *kivi_status_string(int32_t code);
+/* Number of this library's kernels launched so far in this process. */
+uint64_t kivi_kernel_launches(void);
+
+/* ---------------------------------------------------------------- config.rs */
+
+/* KiviConfig::default() (config.rs:20-28): 2 bits, group 32, residual 128. */
+int32_t kivi_config_default(kivi_config *out);
+/* KiviConfig::try_new (config.rs:31-45). */
+int32_t kivi_config_try_new(uint32_t bits, uint64_t group_size, uint64_t residual_length,
+                            kivi_config *out, kivi_error *err);
+
+/* ---------------------------------------------------------------- cache.rs */
+
+/* KiviCache::new (cache.rs:87-120).  The packed store, fp32 key residual and
+ * fp32 value window live on `device`. */
+int32_t kivi_cache_new(const kivi_config *config, uint64_t batch, uint64_t num_kv_heads,
+                       uint64_t head_dim, int32_t device, kivi_cache **out, kivi_error *err);
+void kivi_cache_free(kivi_cache *cache);
+/* Pre-size the device store for `tokens` per stream (no counterpart in the
+ * reference, whose Vec storage grows on demand; growth here doubles). */
+int32_t kivi_cache_reserve(kivi_cache *cache, uint64_t tokens, kivi_error *err);
+
+/* KiviCache::append (cache.rs:186-214). */
+int32_t kivi_cache_append(kivi_cache *cache, const float *keys, uint64_t keys_len,
+                          const float *values, uint64_t values_len, uint64_t seq_len,
+                          kivi_error *err);
+int32_t kivi_cache_append_dev(kivi_cache *cache, const float *d_keys, const float *d_values,
+                              uint64_t seq_len, void *stream, kivi_error *err);
+
+/* KiviCache::attention (cache.rs:224-279).  out: [batch, num_q_heads, head_dim]. */
+int32_t kivi_cache_attention(const kivi_cache *cache, const float *query, uint64_t query_len,
+                             uint64_t num_q_heads, float scale, float *out, uint64_t out_len,
+                             kivi_error *err);
+int32_t kivi_cache_attention_dev(const kivi_cache *cache, const float *d_query,
+                                 uint64_t num_q_heads, float scale, float *d_out, void *stream,
+                                 kivi_error *err);
+
+/* RuntimeKv::decode (runtime.rs:46-56): append one token, then attend. */
+int32_t kivi_cache_decode(kivi_cache *cache, const float *key, uint64_t key_len,
+                          const float *value, uint64_t value_len, const float *query,
+                          uint64_t query_len, uint64_t num_q_heads, float scale, float *out,
+                          uint64_t out_len, kivi_error *err);
+int32_t kivi_cache_decode_dev(kivi_cache *cache, const float *d_key, const float *d_value,
+                              const float *d_query, uint64_t num_q_heads, float scale,
+                              float *d_out, void *stream, kivi_error *err);
+
+/* Sequence sharding (no counterpart in the reference, which is single-device).
+ * Partial softmax state of this cache's tokens for every query row:
+ * d_m, d_l: [batch*num_q_heads], d_o: [batch*num_q_heads, head_dim] with
+ * o = sum_t exp(x_t - m) v_t, l = sum_t exp(x_t - m), x_t = scale * q.k_t. */
+int32_t kivi_cache_attention_partial_dev(const kivi_cache *cache, const float *d_query,
+                                         uint64_t num_q_heads, float scale, float *d_m,
+                                         float *d_l, float *d_o, void *stream, kivi_error *err);
+/* Log-sum-exp merge of `parts` partial states laid out part-major
+ * ([parts][rows] for m/l, [parts][rows][head_dim] for o), merged in part
+ * order (deterministic).  d_out: [rows, head_dim]. */
+int32_t kivi_merge_partials_dev(uint64_t parts, uint64_t rows, uint64_t head_dim,
+                                const float *d_m, const float *d_l, const float *d_o,
+                                float *d_out, void *stream, kivi_error *err);
+/* Quantize the fp32 value window into the packed store (no counterpart in the
+ * reference).  Used for an interior sequence shard, whose tokens a single-device
+ * cache would already have evicted: the packed values are bit-identical to
+ * what the reference's later evictions produce (append_value_block is per
+ * token).  Keys must be flushed (key_residual_len == 0). */
+int32_t kivi_cache_seal(kivi_cache *cache, kivi_error *err);
+
+/* KiviCache::dequantize (cache.rs:282-325): keys/values each
+ * batch*num_kv_heads*sequence_length*head_dim floats. */
+int32_t kivi_cache_dequantize(const kivi_cache *cache, float *keys, float *values, uint64_t len,
+                              kivi_error *err);
+/* KiviCache::memory (cache.rs:362-380). */
+int32_t kivi_cache_memory(const kivi_cache *cache, kivi_memory_report *out);
+/* Getters (cache.rs:122-156). */
+int32_t kivi_cache_get_state(const kivi_cache *cache, kivi_cache_state *out);
+/* KiviCache::budget_snapshot (cache.rs:340-355). */
+int32_t kivi_cache_budget_snapshot(const kivi_cache *cache, kivi_budget_snapshot *out);
+/* PackedStream of stream `stream_index` (b*num_kv_heads + h) in the reference
+ * layout (quant.rs:37-44): axis 0 = keys, 1 = values.  Pass codes/params NULL
+ * to query the sizes.  Bit-exact parity hook. */
+int32_t kivi_cache_export_stream(const kivi_cache *cache, uint64_t stream_index, int32_t axis,
+                                 uint32_t *codes, uint64_t *ncodes, float *params,
+                                 uint64_t *nparams, kivi_error *err);
+
+/* ---------------------------------------------------------------- prefix.rs */
+
+/* KiviCache::share_prefix -> SharedPrefix::from_cache (cache.rs:178-180,
+ * prefix.rs:74-92): frozen device copy, refcount 1. */
+int32_t kivi_cache_share_prefix(const kivi_cache *cache, kivi_prefix **out, kivi_error *err);
+/* SharedPrefix::clone (Arc clone). */
+kivi_prefix *kivi_prefix_retain(kivi_prefix *prefix);
+void kivi_prefix_release(kivi_prefix *prefix);
+/* config/batch/num_kv_heads/head_dim/prefix_tokens getters (prefix.rs:94-112). */
+int32_t kivi_prefix_get_state(const kivi_prefix *prefix, kivi_cache_state *out);
+/* SharedPrefix::prefix_bytes (prefix.rs:114-117). */
+uint64_t kivi_prefix_bytes(const kivi_prefix *prefix);
+/* SharedPrefix::shares_allocation_with (prefix.rs:119-122): 1 / 0. */
+int32_t kivi_prefix_shares_allocation_with(const kivi_prefix *a, const kivi_prefix *b);
+/* SharedPrefix::footprint (prefix.rs:133-152). */
+int32_t kivi_prefix_get_footprint(const kivi_prefix *prefix, uint64_t sessions,
+                              uint64_t question_tokens, kivi_prefix_footprint *out);
+
+/* SharedPrefix::session (prefix.rs:124-131); the session retains the prefix. */
+int32_t kivi_session_new(kivi_prefix *prefix, kivi_session **out, kivi_error *err);
+void kivi_session_free(kivi_session *session);
+/* RagSession::prefix (borrowed pointer). */
+kivi_prefix *kivi_session_prefix(const kivi_session *session);
+/* RagSession::question_tokens (prefix.rs:164-166). */
+uint64_t kivi_session_question_tokens(const kivi_session *session);
+/* RagSession::append (prefix.rs:173-223): preallocated device suffix, no re-splice. */
+int32_t kivi_session_append(kivi_session *session, const float *keys, uint64_t keys_len,
+                            const float *values, uint64_t values_len, uint64_t seq_len,
+                            kivi_error *err);
+int32_t kivi_session_append_dev(kivi_session *session, const float *d_keys,
+                                const float *d_values, uint64_t seq_len, void *stream,
+                                kivi_error *err);
+/* RagSession::attention (prefix.rs:228-290). */
+int32_t kivi_session_attention(const kivi_session *session, const float *query,
+                               uint64_t query_len, uint64_t num_q_heads, float scale, float *out,
+                               uint64_t out_len, kivi_error *err);
+int32_t kivi_session_attention_dev(const kivi_session *session, const float *d_query,
+                                   uint64_t num_q_heads, float scale, float *d_out, void *stream,
+                                   kivi_error *err);
+/* RagSession::attention for n sessions of ONE prefix in a single pass that
+ * reads the packed prefix once for all of them (no reference counterpart; each
+ * session's result equals its own RagSession::attention).
+ * queries: [n][batch][num_q_heads][head_dim]; out: same shape. */
+int32_t kivi_sessions_attention_batched(const kivi_session *const *sessions, uint64_t n,
+                                        const float *queries, uint64_t queries_len,
+                                        uint64_t num_q_heads, float scale, float *out,
+                                        uint64_t out_len, kivi_error *err);
+int32_t kivi_sessions_attention_batched_dev(const kivi_session *const *sessions, uint64_t n,
+                                            const float *d_queries, uint64_t num_q_heads,
+                                            float scale, float *d_out, void *stream,
+                                            kivi_error *err);
+
+/* ---------------------------------------------------------------- quant.rs */
+
+/* Output sizes of a packed tensor (QuantizedTensor::code_bytes/4 and
+ * metadata_bytes/4, quant.rs:63-69). axis 0 = per channel, 1 = per token. */
+int32_t kivi_quantized_sizes(int32_t axis, uint64_t batch, uint64_t heads, uint64_t tokens,
+                             uint64_t head_dim, uint32_t bits, uint64_t group_size,
+                             uint64_t *ncodes, uint64_t *nparams, kivi_error *err);
+/* quantize_per_channel (quant.rs:153-191) / quantize_per_token (quant.rs:193-233):
+ * codes/params of all batch*heads streams, concatenated in PackedStream order. */
+int32_t kivi_quantize_per_channel(const float *data, uint64_t data_len, uint64_t batch,
+                                  uint64_t heads, uint64_t tokens, uint64_t head_dim,
+                                  uint32_t bits, uint64_t group_size, uint32_t *codes,
+                                  uint64_t ncodes, float *params, uint64_t nparams,
+                                  int32_t device, kivi_error *err);
+int32_t kivi_quantize_per_token(const float *data, uint64_t data_len, uint64_t batch,
+                                uint64_t heads, uint64_t tokens, uint64_t head_dim, uint32_t bits,
+                                uint64_t group_size, uint32_t *codes, uint64_t ncodes,
+                                float *params, uint64_t nparams, int32_t device,
+                                kivi_error *err);
+int32_t kivi_quantize_dev(int32_t axis, const float *d_data, uint64_t batch, uint64_t heads,
+                          uint64_t tokens, uint64_t head_dim, uint32_t bits, uint64_t group_size,
+                          uint32_t *d_codes, float *d_params, void *stream, kivi_error *err);
+/* QuantizedTensor::dequantize (quant.rs:123-150). */
+int32_t kivi_dequantize_packed(int32_t axis, const uint32_t *codes, uint64_t ncodes,
+                               const float *params, uint64_t nparams, uint64_t batch,
+                               uint64_t heads, uint64_t tokens, uint64_t head_dim, uint32_t bits,
+                               uint64_t group_size, float *out, uint64_t out_len, int32_t device,
+                               kivi_error *err);
+int32_t kivi_dequantize_packed_dev(int32_t axis, const uint32_t *d_codes, const float *d_params,
+                                   uint64_t batch, uint64_t heads, uint64_t tokens,
+                                   uint64_t head_dim, uint32_t bits, uint64_t group_size,
+                                   float *d_out, void *stream, kivi_error *err);
+/* QuantizedTensor::pytorch_codes (quant.rs:71-112): PyTorch-KIVI word order. */
+int32_t kivi_pytorch_codes(int32_t axis, const uint32_t *codes, uint64_t ncodes, uint64_t batch,
+                           uint64_t heads, uint64_t tokens, uint64_t head_dim, uint32_t bits,
+                           uint64_t group_size, uint32_t *out, uint64_t out_len, kivi_error *err);
+
+/* ---------------------------------------------------------------- budget.rs */
+
+/* layer_kv_bytes (budget.rs:316-347): equals memory().compressed_bytes(). */
+uint64_t kivi_layer_kv_bytes(const kivi_config *config, uint64_t num_kv_heads,
+                             uint64_t head_dim, uint64_t tokens);
+/* marginal_bytes_per_layer (budget.rs:349-364). */
+uint64_t kivi_marginal_bytes_per_layer(const kivi_config *config, uint64_t num_kv_heads,
+                                       uint64_t head_dim);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KIVI_GPU_H */

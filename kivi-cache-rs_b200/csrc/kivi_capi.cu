@@ -1,0 +1,1386 @@
+// kivi_capi.cu -- C ABI (include/kivi_gpu.h) over the device-resident KIVI store.
+//
+// The host side mirrors the reference's state machine counters
+// (cache.rs:71-83: key_res_len, value_res_len, seq_len, quantized token counts)
+// and decides, per append, which kernels run -- the same decisions as
+// cache.rs:382-484, with the value window kept as a ring instead of being
+// shifted (cache.rs:559-578).  All tensor work happens in kernels on the
+// handle's device.
+#include <atomic>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "../../include/kivi_gpu.h"
+#include "kivi_internal.cuh"
+
+namespace kivi {
+
+static std::atomic<uint64_t> g_launches{0};
+void count_launch(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
+uint64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
+
+} // namespace kivi
+
+using kivi::Geom;
+using kivi::Store;
+
+namespace {
+
+// ---------------------------------------------------------------- errors
+
+void fmt_message(kivi_error *e) {
+    char *m = e->message;
+    const size_t n = sizeof(e->message);
+    const unsigned long long a = (unsigned long long)e->a, b = (unsigned long long)e->b;
+    switch (e->code) { // Display strings of error.rs:102-150
+    case KIVI_OK: snprintf(m, n, "ok"); break;
+    case KIVI_ERR_INVALID_BITS: snprintf(m, n, "bit width %llu is not supported; use 2, 4, or 8", a); break;
+    case KIVI_ERR_MISALIGNED_GROUP: snprintf(m, n, "group_size %llu * bits %llu must be a multiple of 32", a, b); break;
+    case KIVI_ERR_RESIDUAL_LENGTH: snprintf(m, n, "residual_length %llu must be a positive multiple of group_size %llu", a, b); break;
+    case KIVI_ERR_HEAD_DIM: snprintf(m, n, "head_dim %llu must be a positive multiple of group_size %llu", a, b); break;
+    case KIVI_ERR_TOKEN_GROUP: snprintf(m, n, "token count %llu must be a positive multiple of group_size %llu for per-channel quantization", a, b); break;
+    case KIVI_ERR_ZERO_DIMENSION: snprintf(m, n, "%s must be greater than zero", e->name ? e->name : "dimension"); break;
+    case KIVI_ERR_SHAPE: snprintf(m, n, "expected %llu elements, got %llu", a, b); break;
+    case KIVI_ERR_QUERY_HEADS: snprintf(m, n, "num_q_heads %llu must be a positive multiple of num_kv_heads %llu", a, b); break;
+    case KIVI_ERR_EARLY_LAYERS: snprintf(m, n, "early layer count %llu exceeds model depth %llu", a, b); break;
+    default: break; // CUDA / argument messages are written by the caller
+    }
+}
+
+int32_t set_err(kivi_error *err, int32_t code, uint64_t a = 0, uint64_t b = 0,
+                const char *name = nullptr) {
+    if (err) {
+        err->code = code;
+        err->a = a;
+        err->b = b;
+        err->name = name;
+        err->message[0] = 0;
+        fmt_message(err);
+    }
+    return code;
+}
+
+int32_t set_msg(kivi_error *err, int32_t code, const char *fmt, ...) {
+    if (err) {
+        err->code = code;
+        err->a = err->b = 0;
+        err->name = nullptr;
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(err->message, sizeof(err->message), fmt, ap);
+        va_end(ap);
+    }
+    return code;
+}
+
+int32_t cuda_fail(kivi_error *err, cudaError_t e, const char *where) {
+    if (e == cudaErrorMemoryAllocation) {
+        cudaGetLastError();
+        return set_msg(err, KIVI_ERR_OUT_OF_MEMORY, "%s: device allocation failed (%s)", where,
+                       cudaGetErrorString(e));
+    }
+    int32_t rc = set_msg(err, KIVI_ERR_CUDA, "%s: %s (%s)", where, cudaGetErrorName(e),
+                         cudaGetErrorString(e));
+    if (err) err->a = (uint64_t)e;
+    return rc;
+}
+
+#define CUDA_TRY(expr, where)                                                                      \
+    do {                                                                                           \
+        cudaError_t _e = (expr);                                                                   \
+        if (_e != cudaSuccess) return cuda_fail(err, _e, where);                                   \
+    } while (0)
+
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+// config.rs:47-55
+int32_t check_bits_group(uint64_t bits, uint64_t group, kivi_error *err) {
+    if (!(bits == 2 || bits == 4 || bits == 8)) return set_err(err, KIVI_ERR_INVALID_BITS, bits);
+    if (group == 0 || (group * bits) % 32 != 0)
+        return set_err(err, KIVI_ERR_MISALIGNED_GROUP, group, bits);
+    return KIVI_OK;
+}
+
+// config.rs:31-45
+int32_t check_config(const kivi_config *c, kivi_error *err) {
+    if (!c) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null config");
+    int32_t rc = check_bits_group(c->bits, c->group_size, err);
+    if (rc) return rc;
+    if (c->residual_length == 0 || c->residual_length % c->group_size != 0)
+        return set_err(err, KIVI_ERR_RESIDUAL_LENGTH, c->residual_length, c->group_size);
+    return KIVI_OK;
+}
+
+constexpr uint64_t kMaxGroup = 256;  // row table size of the key quant kernels
+constexpr uint64_t kMaxHeadDim = 1024;
+
+// ---------------------------------------------------------------- device buffers
+
+template <class T> cudaError_t dalloc(T **p, size_t n) {
+    *p = nullptr;
+    if (n == 0) return cudaSuccess;
+    return cudaMalloc((void **)p, n * sizeof(T));
+}
+
+template <class T> void dfree(T *&p) {
+    if (p) cudaFree(p);
+    p = nullptr;
+}
+
+void free_store(Store &st) {
+    dfree(st.kcodes);
+    dfree(st.kparams);
+    dfree(st.vcodes);
+    dfree(st.vparams);
+    dfree(st.kres);
+    dfree(st.vres);
+    st.cap = 0;
+}
+
+// Scratch that grows monotonically (attention partials, staging).
+struct Scratch {
+    void *p = nullptr;
+    size_t bytes = 0;
+    cudaError_t ensure(size_t need) {
+        if (need <= bytes) return cudaSuccess;
+        const size_t n = need < 2 * bytes ? 2 * bytes : need;
+        if (p) cudaFree(p);
+        p = nullptr;
+        bytes = 0;
+        cudaError_t e = cudaMalloc(&p, n);
+        if (e == cudaSuccess) bytes = n;
+        return e;
+    }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        bytes = 0;
+    }
+    template <class T> T *as(size_t byte_off = 0) const { return (T *)((char *)p + byte_off); }
+};
+
+// State shared by KiviCache and a frozen SharedPrefix.
+struct KvState {
+    kivi_config cfg{};
+    Geom g{};
+    uint64_t B = 0, H = 0, D = 0;
+    int device = 0;
+    Store st;
+    uint64_t seq = 0, kres_len = 0, vres_len = 0, kq = 0, vq = 0, vhead = 0;
+    uint64_t n() const { return B * H; }
+};
+
+// MemoryReport byte counts (cache.rs:362-380) from the host counters: the
+// reference's codes.len()*4 / params.len()*4 per stream equal these products.
+kivi_memory_report memory_of(const KvState &s) {
+    kivi_memory_report r{};
+    const uint64_t n = s.n(), D = s.D, G = s.cfg.group_size, bits = s.cfg.bits;
+    const uint64_t elements = n * D;
+    r.tokens = s.seq;
+    r.key_code_bytes = n * (s.kq * D * bits / 32) * 4;
+    r.key_metadata_bytes = n * (2 * (s.kq / G) * D) * 4;
+    r.value_code_bytes = n * (s.vq * D * bits / 32) * 4;
+    r.value_metadata_bytes = n * (2 * s.vq * (D / G)) * 4;
+    r.key_residual_bytes = s.kres_len * elements * 4;
+    r.value_residual_bytes = s.vres_len * elements * 4;
+    r.residual_capacity_bytes = 2 * s.cfg.residual_length * elements * 4;
+    r.fp16_baseline_bytes = 2 * s.seq * elements * 2;
+    r.fp32_baseline_bytes = 2 * s.seq * elements * 4;
+    return r;
+}
+
+uint64_t compressed_bytes(const kivi_memory_report &r) {
+    return r.key_code_bytes + r.key_metadata_bytes + r.value_code_bytes + r.value_metadata_bytes +
+           r.key_residual_bytes + r.value_residual_bytes;
+}
+
+void fill_state(const KvState &s, kivi_cache_state *o) {
+    o->config = s.cfg;
+    o->batch = s.B;
+    o->num_kv_heads = s.H;
+    o->head_dim = s.D;
+    o->sequence_length = s.seq;
+    o->key_residual_len = s.kres_len;
+    o->value_residual_len = s.vres_len;
+    o->quantized_key_tokens = s.kq;
+    o->quantized_value_tokens = s.vq;
+    o->capacity_tokens = (uint64_t)s.st.cap;
+    o->device = s.device;
+}
+
+// Grow the packed arrays to hold at least `tokens` per stream, keeping the
+// occupied prefix of every stream.  Ordered on `stream`, synchronised before
+// the old buffers are freed.
+int32_t ensure_capacity(KvState &s, uint64_t tokens, cudaStream_t stream, kivi_error *err) {
+    if ((int64_t)tokens <= s.st.cap) return KIVI_OK;
+    const uint64_t R = s.cfg.residual_length;
+    uint64_t cap = (uint64_t)s.st.cap * 2;
+    if (cap < tokens) cap = tokens;
+    if (cap < 4 * R) cap = 4 * R;
+    cap = (cap + R - 1) / R * R;
+    const Geom &g = s.g;
+    const uint64_t n = s.n();
+    Store ns = s.st;
+    ns.cap = (int64_t)cap;
+    ns.kcodes = nullptr;
+    ns.kparams = nullptr;
+    ns.vcodes = nullptr;
+    ns.vparams = nullptr;
+    cudaError_t e;
+    if ((e = dalloc(&ns.kcodes, n * kivi::code_stride(g, cap))) != cudaSuccess ||
+        (e = dalloc(&ns.kparams, n * kivi::kparam_stride(g, cap))) != cudaSuccess ||
+        (e = dalloc(&ns.vcodes, n * kivi::code_stride(g, cap))) != cudaSuccess ||
+        (e = dalloc(&ns.vparams, n * kivi::vparam_stride(g, cap))) != cudaSuccess) {
+        dfree(ns.kcodes);
+        dfree(ns.kparams);
+        dfree(ns.vcodes);
+        dfree(ns.vparams);
+        return cuda_fail(err, e, "grow packed store");
+    }
+    const int64_t oc = s.st.cap;
+    if (oc > 0 && n > 0) {
+        auto copy2d = [&](void *dst, size_t dpitch, const void *src, size_t spitch, size_t width) {
+            if (width == 0) return cudaSuccess;
+            return cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, n, cudaMemcpyDeviceToDevice,
+                                     stream);
+        };
+        CUDA_TRY(copy2d(ns.kcodes, kivi::code_stride(g, cap) * 4, s.st.kcodes,
+                        kivi::code_stride(g, oc) * 4, kivi::code_stride(g, s.kq) * 4),
+                 "grow copy");
+        CUDA_TRY(copy2d(ns.kparams, kivi::kparam_stride(g, cap) * 8, s.st.kparams,
+                        kivi::kparam_stride(g, oc) * 8, (s.kq / g.G) * g.D * 8),
+                 "grow copy");
+        CUDA_TRY(copy2d(ns.vcodes, kivi::code_stride(g, cap) * 4, s.st.vcodes,
+                        kivi::code_stride(g, oc) * 4, kivi::code_stride(g, s.vq) * 4),
+                 "grow copy");
+        CUDA_TRY(copy2d(ns.vparams, kivi::vparam_stride(g, cap) * 8, s.st.vparams,
+                        kivi::vparam_stride(g, oc) * 8, kivi::vparam_stride(g, s.vq) * 8),
+                 "grow copy");
+        CUDA_TRY(cudaStreamSynchronize(stream), "grow sync");
+    }
+    dfree(s.st.kcodes);
+    dfree(s.st.kparams);
+    dfree(s.st.vcodes);
+    dfree(s.st.vparams);
+    s.st.kcodes = ns.kcodes;
+    s.st.kparams = ns.kparams;
+    s.st.vcodes = ns.vcodes;
+    s.st.vparams = ns.vparams;
+    s.st.cap = (int64_t)cap;
+    return KIVI_OK;
+}
+
+// Appends [n][seq][D] device rows (cache.rs:186-214, 382-484).
+int32_t append_device(KvState &s, const float *dk, const float *dv, uint64_t seq,
+                      cudaStream_t stream, kivi_error *err) {
+    if (seq == 0) return KIVI_OK;
+    const uint64_t R = s.cfg.residual_length, G = s.cfg.group_size;
+    const int n = (int)s.n();
+    const Geom &g = s.g;
+    // Counters after this append.
+    const uint64_t ktotal = s.kres_len + seq;
+    const uint64_t nblk = ktotal / R;
+    const uint64_t kq_new = s.kq + nblk * R;
+    uint64_t vq_new, vres_new, vhead_new;
+    if (seq >= R) {
+        vq_new = s.vq + s.vres_len + (seq - R);
+        vres_new = R;
+        vhead_new = 0;
+    } else {
+        const uint64_t drop = s.vres_len + seq > R ? s.vres_len + seq - R : 0;
+        vq_new = s.vq + drop;
+        vres_new = s.vres_len - drop + seq;
+        vhead_new = (s.vhead + drop) % R;
+    }
+    int32_t rc = ensure_capacity(s, kq_new > vq_new ? kq_new : vq_new, stream, err);
+    if (rc) return rc;
+
+    if (seq < R) {
+        CUDA_TRY(kivi::launch_append_small(g, s.st, n, dk, dv, (int)seq, (int)s.kres_len,
+                                           (int64_t)s.kq, (int)s.vres_len, (int64_t)s.vq,
+                                           (int)s.vhead, stream),
+                 "append");
+    } else {
+        // Keys: flush every complete R-block of [residual ++ input], then keep
+        // the tail in the residual (cache.rs:382-405).
+        CUDA_TRY(kivi::launch_key_groups(g, s.st, n, s.st.kres, (int)s.kres_len, dk, (int64_t)seq,
+                                         (int64_t)(nblk * R / G), (int64_t)(s.kq / G), stream),
+                 "append keys");
+        const uint64_t tail = ktotal % R;
+        CUDA_TRY(kivi::launch_copy_rows(s.st.kres, (int64_t)R, 0, 0, (int64_t)R, dk, (int64_t)seq,
+                                        (int64_t)(seq - tail), (int64_t)tail, n, (int)s.D, stream),
+                 "append keys tail");
+        // Values, seq >= R: quantize the window and input[0, seq-R), keep the
+        // last R input rows (cache.rs:434-454).
+        CUDA_TRY(kivi::launch_value_tokens(g, s.st, n, (int)s.vres_len, (int)s.vhead, dv,
+                                           (int64_t)seq, 0, (int64_t)(s.vres_len + seq - R),
+                                           (int64_t)s.vq, stream),
+                 "append values");
+        CUDA_TRY(kivi::launch_copy_rows(s.st.vres, (int64_t)R, 0, 0, (int64_t)R, dv, (int64_t)seq,
+                                        (int64_t)(seq - R), (int64_t)R, n, (int)s.D, stream),
+                 "append window");
+    }
+    s.kq = kq_new;
+    s.kres_len = ktotal % R;
+    s.vq = vq_new;
+    s.vres_len = vres_new;
+    s.vhead = vhead_new;
+    s.seq += seq;
+    return KIVI_OK;
+}
+
+// ---------------------------------------------------------------- attention plan
+
+constexpr int64_t kChunkTokens = 256;
+
+struct SessionView {
+    const float *k;
+    const float *v;
+    uint64_t len;
+    uint64_t cap;
+};
+
+// Runs the chunk kernel + merge for sessions [s0, s0+ns) of `sv` over prefix
+// state `p`; query rows of session i at d_q + i*B*Hq*D, outputs likewise.
+int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, const float *d_q,
+                      uint64_t Hq, float scale, float *d_out, float *d_m, float *d_l,
+                      Scratch &scratch, cudaStream_t stream, kivi_error *err) {
+    const Geom &g = p.g;
+    const uint64_t Gq = Hq / p.H;
+    const int maxrows = kivi::attention_max_rows((int)p.D);
+    if (maxrows < (int)Gq)
+        return set_msg(err, KIVI_ERR_UNSUPPORTED, "head_dim %llu with %llu query heads per kv head exceeds shared memory",
+                       (unsigned long long)p.D, (unsigned long long)Gq);
+    uint64_t per_launch = (uint64_t)maxrows / Gq;
+    if (per_launch > (uint64_t)kivi::kMaxSessionsPerLaunch) per_launch = kivi::kMaxSessionsPerLaunch;
+    const uint64_t main_tokens = p.vq / p.cfg.group_size * p.cfg.group_size;
+    const int64_t NC = (int64_t)((main_tokens + kChunkTokens - 1) / kChunkTokens);
+    const int parts = (int)NC + 2;
+    const uint64_t rows_per_sess = p.B * Hq;
+    for (uint64_t s0 = 0; s0 < nsess; s0 += per_launch) {
+        const uint64_t ns = nsess - s0 < per_launch ? nsess - s0 : per_launch;
+        const uint64_t rows = ns * rows_per_sess;
+        const size_t ml_bytes = rows * parts * 2 * sizeof(float);
+        const size_t o_bytes = rows * parts * p.D * sizeof(float);
+        CUDA_TRY(scratch.ensure(ml_bytes + o_bytes), "attention scratch");
+        kivi::AttnArgs a{};
+        a.g = g;
+        a.st = p.st;
+        a.B = (int)p.B;
+        a.H = (int)p.H;
+        a.Hq = (int)Hq;
+        a.Gq = (int)Gq;
+        a.kq = (int64_t)p.kq;
+        a.vq = (int64_t)p.vq;
+        a.kres_len = (int)p.kres_len;
+        a.vres_len = (int)p.vres_len;
+        a.vhead = (int)p.vhead;
+        a.seq_p = (int64_t)p.seq;
+        a.main_tokens = (int64_t)main_tokens;
+        a.chunk_tokens = kChunkTokens;
+        a.NC = (int)NC;
+        a.parts = parts;
+        a.S = (int)ns;
+        a.session_base = (int)s0;
+        a.q = d_q;
+        a.scale = scale;
+        a.part_ml = scratch.as<float>();
+        a.part_o = scratch.as<float>(ml_bytes);
+        for (uint64_t i = 0; i < ns; ++i) {
+            a.suf[i].k = sv ? sv[s0 + i].k : nullptr;
+            a.suf[i].v = sv ? sv[s0 + i].v : nullptr;
+            a.suf[i].len = sv ? (int64_t)sv[s0 + i].len : 0;
+            a.suf[i].cap = sv ? (int64_t)sv[s0 + i].cap : 0;
+        }
+        CUDA_TRY(kivi::launch_attention_chunks(a, stream), "attention");
+        const uint64_t off = s0 * rows_per_sess;
+        CUDA_TRY(kivi::launch_merge(a.part_ml, a.part_o, (int64_t)rows, parts, (int)p.D, 0,
+                                    d_out + off * p.D, d_m ? d_m + off : nullptr,
+                                    d_l ? d_l + off : nullptr, d_m ? 1 : 0, stream),
+                 "attention merge");
+    }
+    return KIVI_OK;
+}
+
+int32_t check_query(const KvState &p, uint64_t Hq, uint64_t query_len, bool check_len,
+                    kivi_error *err) {
+    if (Hq == 0 || Hq % p.H != 0) return set_err(err, KIVI_ERR_QUERY_HEADS, Hq, p.H);
+    const uint64_t expected = p.B * Hq * p.D;
+    if (check_len && query_len != expected) return set_err(err, KIVI_ERR_SHAPE, expected, query_len);
+    return KIVI_OK;
+}
+
+} // namespace
+
+// ---------------------------------------------------------------- handles
+
+struct kivi_cache {
+    KvState s;
+    cudaStream_t stream = nullptr;   // own stream of the synchronous host-pointer calls
+    cudaEvent_t dev_done = nullptr;  // recorded after every `_dev` call on the caller's stream
+    Scratch stage;   // host-input staging (keys, values, query, out)
+    mutable Scratch part;
+    mutable std::mutex mu; // serialises host-pointer calls that share scratch
+};
+
+struct kivi_prefix {
+    std::atomic<int> refs{1};
+    KvState s;
+    uint64_t prefix_bytes = 0;
+    cudaStream_t stream = nullptr;
+};
+
+struct kivi_session {
+    kivi_prefix *prefix = nullptr;
+    float *k = nullptr;
+    float *v = nullptr;
+    uint64_t len = 0, cap = 0;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t dev_done = nullptr;
+    Scratch stage;
+    mutable Scratch part;
+    mutable std::mutex mu;
+};
+
+namespace {
+
+// `_dev` calls run on the caller's stream exactly as given (NULL = the legacy
+// default stream).  Each records dev_done there; the synchronous host-pointer
+// calls, which run on the handle's own stream, first wait for it, so the two
+// kinds of call can be mixed on one handle.
+cudaStream_t pick(void *user, cudaStream_t /*own*/) { return (cudaStream_t)user; }
+
+cudaError_t mark_dev(cudaEvent_t ev, cudaStream_t st) { return cudaEventRecord(ev, st); }
+
+cudaError_t wait_dev(cudaStream_t own, cudaEvent_t ev) { return cudaStreamWaitEvent(own, ev, 0); }
+
+int32_t init_state(KvState &s, const kivi_config *cfg, uint64_t B, uint64_t H, uint64_t D,
+                   int32_t device, kivi_error *err) {
+    int32_t rc = check_config(cfg, err);
+    if (rc) return rc;
+    // cache.rs:93-104
+    if (B == 0) return set_err(err, KIVI_ERR_ZERO_DIMENSION, 0, 0, "batch");
+    if (H == 0) return set_err(err, KIVI_ERR_ZERO_DIMENSION, 0, 0, "num_kv_heads");
+    if (D == 0 || D % cfg->group_size != 0)
+        return set_err(err, KIVI_ERR_HEAD_DIM, D, cfg->group_size);
+    if (cfg->group_size > kMaxGroup || D > kMaxHeadDim || B * H > 65535)
+        return set_msg(err, KIVI_ERR_UNSUPPORTED,
+                       "device kernels support group_size <= %llu, head_dim <= %llu and "
+                       "batch*num_kv_heads <= 65535",
+                       (unsigned long long)kMaxGroup, (unsigned long long)kMaxHeadDim);
+    s.cfg = *cfg;
+    s.g = kivi::make_geom((int)cfg->bits, (int)cfg->group_size, (int)cfg->residual_length, (int)D);
+    s.B = B;
+    s.H = H;
+    s.D = D;
+    s.device = device;
+    return KIVI_OK;
+}
+
+} // namespace
+
+extern "C" {
+
+int32_t kivi_abi_version(void) { return KIVI_GPU_ABI_VERSION; }
+
+const char *kivi_status_string(int32_t code) {
+    switch (code) {
+    case KIVI_OK: return "ok";
+    case KIVI_ERR_INVALID_BITS: return "InvalidBits";
+    case KIVI_ERR_MISALIGNED_GROUP: return "MisalignedGroup";
+    case KIVI_ERR_RESIDUAL_LENGTH: return "ResidualLength";
+    case KIVI_ERR_HEAD_DIM: return "HeadDim";
+    case KIVI_ERR_TOKEN_GROUP: return "TokenGroup";
+    case KIVI_ERR_ZERO_DIMENSION: return "ZeroDimension";
+    case KIVI_ERR_SHAPE: return "Shape";
+    case KIVI_ERR_QUERY_HEADS: return "QueryHeads";
+    case KIVI_ERR_EARLY_LAYERS: return "EarlyLayers";
+    case KIVI_ERR_CUDA: return "Cuda";
+    case KIVI_ERR_INVALID_ARGUMENT: return "InvalidArgument";
+    case KIVI_ERR_OUT_OF_MEMORY: return "OutOfMemory";
+    case KIVI_ERR_UNSUPPORTED: return "Unsupported";
+    default: return "Unknown";
+    }
+}
+
+uint64_t kivi_kernel_launches(void) { return kivi::launch_count(); }
+
+int32_t kivi_config_default(kivi_config *out) {
+    if (!out) return KIVI_ERR_INVALID_ARGUMENT;
+    out->bits = 2;
+    out->group_size = 32;
+    out->residual_length = 128;
+    return KIVI_OK;
+}
+
+int32_t kivi_config_try_new(uint32_t bits, uint64_t group_size, uint64_t residual_length,
+                            kivi_config *out, kivi_error *err) {
+    kivi_config c{bits, group_size, residual_length};
+    int32_t rc = check_config(&c, err);
+    if (rc) return rc;
+    if (out) *out = c;
+    return set_err(err, KIVI_OK);
+}
+
+// ---------------------------------------------------------------- KiviCache
+
+int32_t kivi_cache_new(const kivi_config *config, uint64_t batch, uint64_t num_kv_heads,
+                       uint64_t head_dim, int32_t device, kivi_cache **out, kivi_error *err) {
+    if (!out) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null output handle");
+    *out = nullptr;
+    KvState s;
+    int32_t rc = init_state(s, config, batch, num_kv_heads, head_dim, device, err);
+    if (rc) return rc;
+    DeviceGuard dg(device);
+    if (!dg.ok) return set_msg(err, KIVI_ERR_CUDA, "cannot select device %d", device);
+    kivi_cache *h = new kivi_cache();
+    h->s = s;
+    const size_t res = (size_t)s.n() * s.cfg.residual_length * s.D;
+    cudaError_t e;
+    if ((e = cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking)) != cudaSuccess ||
+        (e = cudaEventCreateWithFlags(&h->dev_done, cudaEventDisableTiming)) != cudaSuccess ||
+        (e = cudaEventRecord(h->dev_done, h->stream)) != cudaSuccess ||
+        (e = dalloc(&h->s.st.kres, res)) != cudaSuccess ||
+        (e = dalloc(&h->s.st.vres, res)) != cudaSuccess ||
+        (e = cudaMemsetAsync(h->s.st.kres, 0, res * 4, h->stream)) != cudaSuccess ||
+        (e = cudaMemsetAsync(h->s.st.vres, 0, res * 4, h->stream)) != cudaSuccess ||
+        (e = cudaStreamSynchronize(h->stream)) != cudaSuccess) {
+        free_store(h->s.st);
+        if (h->dev_done) cudaEventDestroy(h->dev_done);
+        if (h->stream) cudaStreamDestroy(h->stream);
+        delete h;
+        return cuda_fail(err, e, "kivi_cache_new");
+    }
+    *out = h;
+    return set_err(err, KIVI_OK);
+}
+
+void kivi_cache_free(kivi_cache *h) {
+    if (!h) return;
+    DeviceGuard dg(h->s.device);
+    if (h->dev_done) cudaEventSynchronize(h->dev_done);
+    if (h->stream) cudaStreamSynchronize(h->stream);
+    free_store(h->s.st);
+    h->stage.release();
+    h->part.release();
+    if (h->dev_done) cudaEventDestroy(h->dev_done);
+    if (h->stream) cudaStreamDestroy(h->stream);
+    delete h;
+}
+
+int32_t kivi_cache_reserve(kivi_cache *h, uint64_t tokens, kivi_error *err) {
+    if (!h) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null cache");
+    std::lock_guard<std::mutex> lk(h->mu);
+    DeviceGuard dg(h->s.device);
+    CUDA_TRY(wait_dev(h->stream, h->dev_done), "reserve");
+    int32_t rc = ensure_capacity(h->s, tokens, h->stream, err);
+    if (rc) return rc;
+    return set_err(err, KIVI_OK);
+}
+
+int32_t kivi_cache_append_dev(kivi_cache *h, const float *dk, const float *dv, uint64_t seq,
+                              void *stream, kivi_error *err) {
+    if (!h) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null cache");
+    if (seq > 0 && (!dk || !dv)) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null input");
+    DeviceGuard dg(h->s.device);
+    cudaStream_t st = pick(stream, h->stream);
+    int32_t rc = append_device(h->s, dk, dv, seq, st, err);
+    if (rc) return rc;
+    CUDA_TRY(mark_dev(h->dev_done, st), "append_dev");
+    return set_err(err, KIVI_OK);
+}
+
+int32_t kivi_cache_append(kivi_cache *h, const float *keys, uint64_t keys_len,
+                          const float *values, uint64_t values_len, uint64_t seq,
+                          kivi_error *err) {
+    if (!h) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null cache");
+    const uint64_t expected = h->s.n() * seq * h->s.D;
+    // cache.rs:192-204
+    if (keys_len != expected) return set_err(err, KIVI_ERR_SHAPE, expected, keys_len);
+    if (values_len != expected) return set_err(err, KIVI_ERR_SHAPE, expected, values_len);
+    if (seq == 0) return set_err(err, KIVI_OK);
+    if (!keys || !values) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null input");
+    std::lock_guard<std::mutex> lk(h->mu);
+    DeviceGuard dg(h->s.device);
+    const size_t bytes = expected * sizeof(float);
+    CUDA_TRY(wait_dev(h->stream, h->dev_done), "append");
+    CUDA_TRY(h->stage.ensure(2 * bytes), "append staging");
+    float *dk = h->stage.as<float>(), *dv = h->stage.as<float>(bytes);
+    CUDA_TRY(cudaMemcpyAsync(dk, keys, bytes, cudaMemcpyHostToDevice, h->stream), "append H2D");
+    CUDA_TRY(cudaMemcpyAsync(dv, values, bytes, cudaMemcpyHostToDevice, h->stream), "append H2D");
+    int32_t rc = append_device(h->s, dk, dv, seq, h->stream, err);
+    if (rc) return rc;
+    CUDA_TRY(cudaStreamSynchronize(h->stream), "append");
+    return set_err(err, KIVI_OK);
+}
+
+int32_t kivi_cache_attention_dev(const kivi_cache *h, const float *dq, uint64_t Hq, float scale,
+                                 float *dout, void *stream, kivi_error *err) {
+    if (!h) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null cache");
+    int32_t rc = check_query(h->s, Hq, 0, false, err);
+    if (rc) return rc;
+    DeviceGuard dg(h->s.device);
+    cudaStream_t st = pick(stream, h->stream);
+    const uint64_t out_n = h->s.B * Hq * h->s.D;
+    if (h->s.seq == 0) { // cache.rs:243-246: empty cache -> zeros
+        CUDA_TRY(cudaMemsetAsync(dout, 0, out_n * sizeof(float), st), "attention zeros");
+    } else {
+        rc = run_attention(h->s, nullptr, 1, dq, Hq, scale, dout, nullptr, nullptr, h->part, st, err);
+        if (rc) return rc;
+    }
+    CUDA_TRY(mark_dev(h->dev_done, st), "attention_dev");
+    return set_err(err, KIVI_OK);
+}
+
+int32_t kivi_cache_attention(const kivi_cache *h, const float *query, uint64_t query_len,
+                             uint64_t Hq, float scale, float *out, uint64_t out_len,
+                             kivi_error *err) {
+    if (!h) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null cache");
+    int32_t rc = check_query(h->s, Hq, query_len, true, err);
+    if (rc) return rc;
+    const uint64_t n = h->s.B * Hq * h->s.D;
+    if (out_len != n) return set_err(err, KIVI_ERR_SHAPE, n, out_len);
+    if (!query || !out) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null buffer");
+    kivi_cache *mh = const_cast<kivi_cache *>(h);
+    std::lock_guard<std::mutex> lk(mh->mu);
+    DeviceGuard dg(h->s.device);
+    CUDA_TRY(wait_dev(h->stream, h->dev_done), "attention");
+    CUDA_TRY(mh->stage.ensure(2 * n * sizeof(float)), "attention staging");
+    float *dq = mh->stage.as<float>(), *dout = mh->stage.as<float>(n * sizeof(float));
+    CUDA_TRY(cudaMemcpyAsync(dq, query, n * 4, cudaMemcpyHostToDevice, h->stream), "attention H2D");
+    rc = kivi_cache_attention_dev(h, dq, Hq, scale, dout, h->stream, err);
+    if (rc) return rc;
+    CUDA_TRY(cudaMemcpyAsync(out, dout, n * 4, cudaMemcpyDeviceToHost, h->stream), "attention D2H");
+    CUDA_TRY(cudaStreamSynchronize(h->stream), "attention");
+    return set_err(err, KIVI_OK);
+}
+
+int32_t kivi_cache_decode_dev(kivi_cache *h, const float *dk, const float *dv, const float *dq,
+                              uint64_t Hq, float scale, float *dout, void *stream,
+                              kivi_error *err) {
+    if (!h) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null cache");
+    int32_t rc = check_query(h->s, Hq, 0, false, err);
+    if (rc) return rc;
+    rc = kivi_cache_append_dev(h, dk, dv, 1, stream, err);
+    if (rc) return rc;
+    return kivi_cache_attention_dev(h, dq, Hq, scale, dout, stream, err);
+}
+
+int32_t kivi_cache_decode(kivi_cache *h, const float *key, uint64_t key_len, const float *value,
+                          uint64_t value_len, const float *query, uint64_t query_len, uint64_t Hq,
+                          float scale, float *out, uint64_t out_len, kivi_error *err) {
+    // runtime.rs:53-55: append(key, value, 1)? then attention(query)
+    int32_t rc = kivi_cache_append(h, key, key_len, value, value_len, 1, err);
+    if (rc) return rc;
+    return kivi_cache_attention(h, query, query_len, Hq, scale, out, out_len, err);
+}
+
+int32_t kivi_cache_attention_partial_dev(const kivi_cache *h, const float *dq, uint64_t Hq,
+                                         float scale, float *dm, float *dl, float *dout,
+                                         void *stream, kivi_error *err) {
+    if (!h) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null cache");
+    int32_t rc = check_query(h->s, Hq, 0, false, err);
+    if (rc) return rc;
+    if (!dm || !dl || !dout) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null output");
+    DeviceGuard dg(h->s.device);
+    cudaStream_t st = pick(stream, h->stream);
+    const uint64_t rows = h->s.B * Hq;
+    if (h->s.seq == 0) {
+        std::vector<float> ninf(rows, -INFINITY);
+        CUDA_TRY(cudaMemcpyAsync(dm, ninf.data(), rows * 4, cudaMemcpyHostToDevice, st), "partial");
+        CUDA_TRY(cudaMemsetAsync(dl, 0, rows * 4, st), "partial");
+        CUDA_TRY(cudaMemsetAsync(dout, 0, rows * h->s.D * 4, st), "partial");
+        CUDA_TRY(cudaStreamSynchronize(st), "partial");
+        return set_err(err, KIVI_OK);
+    }
+    rc = run_attention(h->s, nullptr, 1, dq, Hq, scale, dout, dm, dl, h->part, st, err);
+    if (rc) return rc;
+    CUDA_TRY(mark_dev(h->dev_done, st), "attention_partial_dev");
+    return set_err(err, KIVI_OK);
+}
+
+int32_t kivi_merge_partials_dev(uint64_t parts, uint64_t rows, uint64_t head_dim, const float *dm,
+                                const float *dl, const float *dout_parts, float *dout,
+                                void *stream, kivi_error *err) {
+    if (parts == 0 || !dm || !dl || !dout_parts || !dout)
+        return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "bad merge arguments");
+    CUDA_TRY(kivi::launch_merge_shards(dm, dl, dout_parts, (int64_t)parts, (int64_t)rows,
+                                       (int)head_dim, dout, (cudaStream_t)stream),
+             "merge partials");
+    return set_err(err, KIVI_OK);
+}
+
+int32_t kivi_cache_seal(kivi_cache *h, kivi_error *err) {
+    if (!h) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null cache");
+    KvState &s = h->s;
+    if (s.kres_len != 0)
+        return set_msg(err, KIVI_ERR_INVALID_ARGUMENT,
+                       "seal needs a flushed key residual (key_residual_len = %llu)",
+                       (unsigned long long)s.kres_len);
+    std::lock_guard<std::mutex> lk(h->mu);
+    DeviceGuard dg(s.device);
+    CUDA_TRY(wait_dev(h->stream, h->dev_done), "seal");
+    int32_t rc = ensure_capacity(s, s.vq + s.vres_len, h->stream, err);
+    if (rc) return rc;
+    CUDA_TRY(kivi::launch_value_tokens(s.g, s.st, (int)s.n(), (int)s.vres_len, (int)s.vhead,
+                                       nullptr, 0, 0, (int64_t)s.vres_len, (int64_t)s.vq, h->stream),
+             "seal");
+    CUDA_TRY(cudaStreamSynchronize(h->stream), "seal");
+    s.vq += s.vres_len;
+    s.vres_len = 0;
+    s.vhead = 0;
+    return set_err(err, KIVI_OK);
+}
+
+int32_t kivi_cache_dequantize(const kivi_cache *h, float *keys, float *values, uint64_t len,
+                              kivi_error *err) {
+    if (!h) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null cache");
+    const KvState &s = h->s;
+    const uint64_t n = s.n() * s.seq * s.D;
+    if (len != n) return set_err(err, KIVI_ERR_SHAPE, n, len);
+    if (n == 0) return set_err(err, KIVI_OK);
+    if (!keys || !values) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null buffer");
+    kivi_cache *mh = const_cast<kivi_cache *>(h);
+    std::lock_guard<std::mutex> lk(mh->mu);
+    DeviceGuard dg(s.device);
+    CUDA_TRY(wait_dev(h->stream, h->dev_done), "dequantize");
+    CUDA_TRY(mh->stage.ensure(2 * n * 4), "dequantize staging");
+    float *dk = mh->stage.as<float>(), *dv = mh->stage.as<float>(n * 4);
+    CUDA_TRY(kivi::launch_dequant_cache(s.g, s.st, (int)s.n(), (int64_t)s.seq, (int64_t)s.kq,
+                                        (int64_t)s.vq, (int)s.vhead, dk, dv, h->stream),
+             "dequantize");
+    CUDA_TRY(cudaMemcpyAsync(keys, dk, n * 4, cudaMemcpyDeviceToHost, h->stream), "dequantize D2H");
+    CUDA_TRY(cudaMemcpyAsync(values, dv, n * 4, cudaMemcpyDeviceToHost, h->stream), "dequantize D2H");
+    CUDA_TRY(cudaStreamSynchronize(h->stream), "dequantize");
+    return set_err(err, KIVI_OK);
+}
+
+int32_t kivi_cache_memory(const kivi_cache *h, kivi_memory_report *out) {
+    if (!h || !out) return KIVI_ERR_INVALID_ARGUMENT;
+    *out = memory_of(h->s);
+    return KIVI_OK;
+}
+
+int32_t kivi_cache_get_state(const kivi_cache *h, kivi_cache_state *out) {
+    if (!h || !out) return KIVI_ERR_INVALID_ARGUMENT;
+    fill_state(h->s, out);
+    return KIVI_OK;
+}
+
+int32_t kivi_cache_budget_snapshot(const kivi_cache *h, kivi_budget_snapshot *out) {
+    if (!h || !out) return KIVI_ERR_INVALID_ARGUMENT;
+    const KvState &s = h->s;
+    const kivi_memory_report r = memory_of(s);
+    const uint64_t R = s.cfg.residual_length;
+    out->tokens_until_key_flush = R > s.kres_len ? R - s.kres_len : 0; // cache.rs:328-330
+    out->key_residual_tokens = s.kres_len;
+    out->value_residual_tokens = s.vres_len;
+    out->sequence_tokens = s.seq;
+    out->current_layer_bytes = compressed_bytes(r);
+    out->marginal_bytes_per_token = kivi_marginal_bytes_per_layer(&s.cfg, s.H, s.D);
+    out->residual_capacity_bytes = r.residual_capacity_bytes;
+    return KIVI_OK;
+}
+
+static int32_t export_stream(const KvState &s, uint64_t idx, int32_t axis, uint32_t *codes,
+                             uint64_t *ncodes, float *params, uint64_t *nparams,
+                             cudaStream_t stream, kivi_error *err) {
+    if (idx >= s.n() || (axis != 0 && axis != 1))
+        return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "stream index or axis out of range");
+    const Geom &g = s.g;
+    const uint64_t toks = axis == 0 ? s.kq : s.vq;
+    const uint64_t nc = (uint64_t)kivi::code_stride(g, (int64_t)toks);
+    const uint64_t np = 2 * (axis == 0 ? (uint64_t)kivi::kparam_stride(g, (int64_t)toks)
+                                       : (uint64_t)kivi::vparam_stride(g, (int64_t)toks));
+    if (ncodes) *ncodes = nc;
+    if (nparams) *nparams = np;
+    if (!codes && !params) return set_err(err, KIVI_OK);
+    DeviceGuard dg(s.device);
+    const uint32_t *src_c = (axis == 0 ? s.st.kcodes : s.st.vcodes) +
+                            idx * (uint64_t)kivi::code_stride(g, s.st.cap);
+    const float2 *src_p =
+        axis == 0 ? s.st.kparams + idx * (uint64_t)kivi::kparam_stride(g, s.st.cap)
+                  : s.st.vparams + idx * (uint64_t)kivi::vparam_stride(g, s.st.cap);
+    if (codes && nc)
+        CUDA_TRY(cudaMemcpyAsync(codes, src_c, nc * 4, cudaMemcpyDeviceToHost, stream), "export");
+    if (params && np)
+        CUDA_TRY(cudaMemcpyAsync(params, src_p, np * 4, cudaMemcpyDeviceToHost, stream), "export");
+    CUDA_TRY(cudaStreamSynchronize(stream), "export");
+    return set_err(err, KIVI_OK);
+}
+
+int32_t kivi_cache_export_stream(const kivi_cache *h, uint64_t idx, int32_t axis, uint32_t *codes,
+                                 uint64_t *ncodes, float *params, uint64_t *nparams,
+                                 kivi_error *err) {
+    if (!h) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null cache");
+    std::lock_guard<std::mutex> lk(h->mu);
+    {
+        DeviceGuard dg(h->s.device);
+        CUDA_TRY(wait_dev(h->stream, h->dev_done), "export");
+    }
+    return export_stream(h->s, idx, axis, codes, ncodes, params, nparams, h->stream, err);
+}
+
+// ---------------------------------------------------------------- SharedPrefix
+
+int32_t kivi_cache_share_prefix(const kivi_cache *h, kivi_prefix **out, kivi_error *err) {
+    if (!h || !out) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null argument");
+    *out = nullptr;
+    kivi_cache *mh = const_cast<kivi_cache *>(h);
+    std::lock_guard<std::mutex> lk(mh->mu);
+    const KvState &c = h->s;
+    DeviceGuard dg(c.device);
+    kivi_prefix *p = new kivi_prefix();
+    p->s = c;
+    p->s.st = Store();
+    p->prefix_bytes = compressed_bytes(memory_of(c)); // prefix.rs:75, 89
+    const Geom &g = c.g;
+    const uint64_t n = c.n(), R = c.cfg.residual_length, D = c.D;
+    int64_t cap = (int64_t)(c.kq > c.vq ? c.kq : c.vq);
+    cap = (cap + (int64_t)R - 1) / (int64_t)R * (int64_t)R;
+    p->s.st.cap = cap;
+    cudaError_t e;
+    const size_t res = n * R * D;
+    if ((e = cudaStreamCreateWithFlags(&p->stream, cudaStreamNonBlocking)) != cudaSuccess ||
+        (e = dalloc(&p->s.st.kcodes, n * kivi::code_stride(g, cap))) != cudaSuccess ||
+        (e = dalloc(&p->s.st.kparams, n * kivi::kparam_stride(g, cap))) != cudaSuccess ||
+        (e = dalloc(&p->s.st.vcodes, n * kivi::code_stride(g, cap))) != cudaSuccess ||
+        (e = dalloc(&p->s.st.vparams, n * kivi::vparam_stride(g, cap))) != cudaSuccess ||
+        (e = dalloc(&p->s.st.kres, res)) != cudaSuccess ||
+        (e = dalloc(&p->s.st.vres, res)) != cudaSuccess) {
+        free_store(p->s.st);
+        if (p->stream) cudaStreamDestroy(p->stream);
+        delete p;
+        return cuda_fail(err, e, "share_prefix");
+    }
+    cudaStream_t st = h->stream;
+    CUDA_TRY(wait_dev(st, h->dev_done), "share_prefix");
+    auto copy2d = [&](void *dst, size_t dpitch, const void *src, size_t spitch, size_t width) {
+        if (width == 0 || n == 0) return cudaSuccess;
+        return cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, n, cudaMemcpyDeviceToDevice, st);
+    };
+    const int64_t oc = c.st.cap;
+    CUDA_TRY(copy2d(p->s.st.kcodes, kivi::code_stride(g, cap) * 4, c.st.kcodes,
+                    kivi::code_stride(g, oc) * 4, kivi::code_stride(g, c.kq) * 4), "share_prefix copy");
+    CUDA_TRY(copy2d(p->s.st.kparams, kivi::kparam_stride(g, cap) * 8, c.st.kparams,
+                    kivi::kparam_stride(g, oc) * 8, (c.kq / g.G) * g.D * 8), "share_prefix copy");
+    CUDA_TRY(copy2d(p->s.st.vcodes, kivi::code_stride(g, cap) * 4, c.st.vcodes,
+                    kivi::code_stride(g, oc) * 4, kivi::code_stride(g, c.vq) * 4), "share_prefix copy");
+    CUDA_TRY(copy2d(p->s.st.vparams, kivi::vparam_stride(g, cap) * 8, c.st.vparams,
+                    kivi::vparam_stride(g, oc) * 8, kivi::vparam_stride(g, c.vq) * 8), "share_prefix copy");
+    CUDA_TRY(cudaMemcpyAsync(p->s.st.kres, c.st.kres, res * 4, cudaMemcpyDeviceToDevice, st),
+             "share_prefix copy");
+    // Linearise the value ring so the frozen window starts at slot 0.
+    const uint64_t first = c.vres_len < R - c.vhead ? c.vres_len : R - c.vhead;
+    CUDA_TRY(copy2d(p->s.st.vres, R * D * 4, c.st.vres + c.vhead * D, R * D * 4, first * D * 4),
+             "share_prefix copy");
+    CUDA_TRY(copy2d(p->s.st.vres + first * D, R * D * 4, c.st.vres, R * D * 4,
+                    (c.vres_len - first) * D * 4), "share_prefix copy");
+    CUDA_TRY(cudaStreamSynchronize(st), "share_prefix");
+    p->s.vhead = 0;
+    *out = p;
+    return set_err(err, KIVI_OK);
+}
+
+kivi_prefix *kivi_prefix_retain(kivi_prefix *p) {
+    if (p) p->refs.fetch_add(1);
+    return p;
+}
+
+void kivi_prefix_release(kivi_prefix *p) {
+    if (!p) return;
+    if (p->refs.fetch_sub(1) != 1) return;
+    DeviceGuard dg(p->s.device);
+    if (p->stream) cudaStreamSynchronize(p->stream);
+    free_store(p->s.st);
+    if (p->stream) cudaStreamDestroy(p->stream);
+    delete p;
+}
+
+int32_t kivi_prefix_get_state(const kivi_prefix *p, kivi_cache_state *out) {
+    if (!p || !out) return KIVI_ERR_INVALID_ARGUMENT;
+    fill_state(p->s, out);
+    return KIVI_OK;
+}
+
+uint64_t kivi_prefix_bytes(const kivi_prefix *p) { return p ? p->prefix_bytes : 0; }
+
+int32_t kivi_prefix_shares_allocation_with(const kivi_prefix *a, const kivi_prefix *b) {
+    return (a && a == b) ? 1 : 0;
+}
+
+int32_t kivi_prefix_get_footprint(const kivi_prefix *p, uint64_t sessions, uint64_t question_tokens,
+                              kivi_prefix_footprint *out) {
+    if (!p || !out) return KIVI_ERR_INVALID_ARGUMENT;
+    // prefix.rs:136-152
+    const uint64_t elements = p->s.B * p->s.H * p->s.D;
+    const uint64_t question_bytes = sessions * question_tokens * elements * 2 * 4;
+    const uint64_t tokens = p->s.seq + question_tokens;
+    const uint64_t fp16_per_user = 2 * tokens * elements * 2;
+    out->prefix_tokens = p->s.seq;
+    out->question_tokens = question_tokens;
+    out->sessions = sessions;
+    out->prefix_bytes = p->prefix_bytes;
+    out->question_bytes = question_bytes;
+    out->shared_total_bytes = p->prefix_bytes + question_bytes;
+    out->fp16_per_user_bytes = fp16_per_user;
+    out->fp16_all_users_bytes = sessions * fp16_per_user;
+    return KIVI_OK;
+}
+
+// ---------------------------------------------------------------- RagSession
+
+int32_t kivi_session_new(kivi_prefix *p, kivi_session **out, kivi_error *err) {
+    if (!p || !out) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null argument");
+    DeviceGuard dg(p->s.device);
+    kivi_session *s = new kivi_session();
+    cudaError_t e = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->dev_done, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventRecord(s->dev_done, s->stream);
+    if (e != cudaSuccess) {
+        if (s->dev_done) cudaEventDestroy(s->dev_done);
+        if (s->stream) cudaStreamDestroy(s->stream);
+        delete s;
+        return cuda_fail(err, e, "session_new");
+    }
+    s->prefix = kivi_prefix_retain(p);
+    *out = s;
+    return set_err(err, KIVI_OK);
+}
+
+void kivi_session_free(kivi_session *s) {
+    if (!s) return;
+    {
+        DeviceGuard dg(s->prefix->s.device);
+        if (s->dev_done) cudaEventSynchronize(s->dev_done);
+        if (s->stream) cudaStreamSynchronize(s->stream);
+        dfree(s->k);
+        dfree(s->v);
+        s->stage.release();
+        s->part.release();
+        if (s->dev_done) cudaEventDestroy(s->dev_done);
+        if (s->stream) cudaStreamDestroy(s->stream);
+    }
+    kivi_prefix_release(s->prefix);
+    delete s;
+}
+
+kivi_prefix *kivi_session_prefix(const kivi_session *s) { return s ? s->prefix : nullptr; }
+
+uint64_t kivi_session_question_tokens(const kivi_session *s) { return s ? s->len : 0; }
+
+// Copies [n][seq][D] rows (host or device) after the session's suffix; grows
+// the preallocated suffix by doubling (replaces the per-append re-splice of
+// prefix.rs:196-221).
+static int32_t session_append(kivi_session *s, const float *k, const float *v, uint64_t seq,
+                              cudaMemcpyKind kind, cudaStream_t st, kivi_error *err) {
+    const KvState &p = s->prefix->s;
+    const uint64_t n = p.n(), D = p.D;
+    if (s->len + seq > s->cap) {
+        uint64_t cap = s->cap * 2;
+        if (cap < s->len + seq) cap = s->len + seq;
+        if (cap < 64) cap = 64;
+        float *nk = nullptr, *nv = nullptr;
+        cudaError_t e;
+        if ((e = dalloc(&nk, n * cap * D)) != cudaSuccess || (e = dalloc(&nv, n * cap * D)) != cudaSuccess) {
+            dfree(nk);
+            dfree(nv);
+            return cuda_fail(err, e, "session grow");
+        }
+        if (s->len) {
+            CUDA_TRY(cudaMemcpy2DAsync(nk, cap * D * 4, s->k, s->cap * D * 4, s->len * D * 4, n,
+                                       cudaMemcpyDeviceToDevice, st), "session grow copy");
+            CUDA_TRY(cudaMemcpy2DAsync(nv, cap * D * 4, s->v, s->cap * D * 4, s->len * D * 4, n,
+                                       cudaMemcpyDeviceToDevice, st), "session grow copy");
+            CUDA_TRY(cudaStreamSynchronize(st), "session grow");
+        }
+        dfree(s->k);
+        dfree(s->v);
+        s->k = nk;
+        s->v = nv;
+        s->cap = cap;
+    }
+    CUDA_TRY(cudaMemcpy2DAsync(s->k + s->len * D, s->cap * D * 4, k, seq * D * 4, seq * D * 4, n,
+                               kind, st), "session append");
+    CUDA_TRY(cudaMemcpy2DAsync(s->v + s->len * D, s->cap * D * 4, v, seq * D * 4, seq * D * 4, n,
+                               kind, st), "session append");
+    s->len += seq;
+    return KIVI_OK;
+}
+
+int32_t kivi_session_append(kivi_session *s, const float *keys, uint64_t keys_len,
+                            const float *values, uint64_t values_len, uint64_t seq,
+                            kivi_error *err) {
+    if (!s) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null session");
+    const KvState &p = s->prefix->s;
+    const uint64_t expected = p.n() * seq * p.D; // prefix.rs:180-192
+    if (keys_len != expected) return set_err(err, KIVI_ERR_SHAPE, expected, keys_len);
+    if (values_len != expected) return set_err(err, KIVI_ERR_SHAPE, expected, values_len);
+    if (seq == 0) return set_err(err, KIVI_OK);
+    if (!keys || !values) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null input");
+    std::lock_guard<std::mutex> lk(s->mu);
+    DeviceGuard dg(p.device);
+    CUDA_TRY(wait_dev(s->stream, s->dev_done), "session append");
+    int32_t rc = session_append(s, keys, values, seq, cudaMemcpyHostToDevice, s->stream, err);
+    if (rc) return rc;
+    CUDA_TRY(cudaStreamSynchronize(s->stream), "session append");
+    return set_err(err, KIVI_OK);
+}
+
+int32_t kivi_session_append_dev(kivi_session *s, const float *dk, const float *dv, uint64_t seq,
+                                void *stream, kivi_error *err) {
+    if (!s) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null session");
+    if (seq == 0) return set_err(err, KIVI_OK);
+    if (!dk || !dv) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null input");
+    DeviceGuard dg(s->prefix->s.device);
+    cudaStream_t st = pick(stream, s->stream);
+    int32_t rc = session_append(s, dk, dv, seq, cudaMemcpyDeviceToDevice, st, err);
+    if (rc) return rc;
+    CUDA_TRY(mark_dev(s->dev_done, st), "session append_dev");
+    return set_err(err, KIVI_OK);
+}
+
+static int32_t sessions_attention_dev(const kivi_session *const *ss, uint64_t n, const float *dq,
+                                      uint64_t Hq, float scale, float *dout, cudaStream_t st,
+                                      Scratch &part, kivi_error *err) {
+    const kivi_prefix *p = ss[0]->prefix;
+    for (uint64_t i = 0; i < n; ++i)
+        if (!ss[i] || ss[i]->prefix != p)
+            return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "sessions must share one prefix");
+    int32_t rc = check_query(p->s, Hq, 0, false, err);
+    if (rc) return rc;
+    std::vector<SessionView> views(n);
+    bool any = p->s.seq > 0;
+    for (uint64_t i = 0; i < n; ++i) {
+        views[i] = SessionView{ss[i]->k, ss[i]->v, ss[i]->len, ss[i]->cap};
+        any = any || ss[i]->len > 0;
+    }
+    const uint64_t out_n = n * p->s.B * Hq * p->s.D;
+    if (!any) { // prefix.rs:248-252: nothing to attend -> zeros
+        CUDA_TRY(cudaMemsetAsync(dout, 0, out_n * 4, st), "session zeros");
+        return KIVI_OK;
+    }
+    return run_attention(p->s, views.data(), n, dq, Hq, scale, dout, nullptr, nullptr, part, st, err);
+}
+
+int32_t kivi_session_attention_dev(const kivi_session *s, const float *dq, uint64_t Hq,
+                                   float scale, float *dout, void *stream, kivi_error *err) {
+    if (!s) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null session");
+    DeviceGuard dg(s->prefix->s.device);
+    const kivi_session *arr[1] = {s};
+    cudaStream_t st = pick(stream, s->stream);
+    int32_t rc = sessions_attention_dev(arr, 1, dq, Hq, scale, dout, st, s->part, err);
+    if (rc) return rc;
+    CUDA_TRY(mark_dev(s->dev_done, st), "session attention_dev");
+    return set_err(err, KIVI_OK);
+}
+
+int32_t kivi_session_attention(const kivi_session *s, const float *query, uint64_t query_len,
+                               uint64_t Hq, float scale, float *out, uint64_t out_len,
+                               kivi_error *err) {
+    if (!s) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null session");
+    const KvState &p = s->prefix->s;
+    int32_t rc = check_query(p, Hq, query_len, true, err); // prefix.rs:235-247
+    if (rc) return rc;
+    const uint64_t n = p.B * Hq * p.D;
+    if (out_len != n) return set_err(err, KIVI_ERR_SHAPE, n, out_len);
+    if (!query || !out) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null buffer");
+    kivi_session *ms = const_cast<kivi_session *>(s);
+    std::lock_guard<std::mutex> lk(ms->mu);
+    DeviceGuard dg(p.device);
+    CUDA_TRY(wait_dev(s->stream, s->dev_done), "session attention");
+    CUDA_TRY(ms->stage.ensure(2 * n * 4), "session staging");
+    float *dq = ms->stage.as<float>(), *dout = ms->stage.as<float>(n * 4);
+    CUDA_TRY(cudaMemcpyAsync(dq, query, n * 4, cudaMemcpyHostToDevice, s->stream), "session H2D");
+    const kivi_session *arr[1] = {s};
+    rc = sessions_attention_dev(arr, 1, dq, Hq, scale, dout, s->stream, ms->part, err);
+    if (rc) return rc;
+    CUDA_TRY(cudaMemcpyAsync(out, dout, n * 4, cudaMemcpyDeviceToHost, s->stream), "session D2H");
+    CUDA_TRY(cudaStreamSynchronize(s->stream), "session attention");
+    return set_err(err, KIVI_OK);
+}
+
+int32_t kivi_sessions_attention_batched_dev(const kivi_session *const *ss, uint64_t n,
+                                            const float *dq, uint64_t Hq, float scale,
+                                            float *dout, void *stream, kivi_error *err) {
+    if (!ss || n == 0 || !ss[0]) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "no sessions");
+    DeviceGuard dg(ss[0]->prefix->s.device);
+    kivi_session *lead = const_cast<kivi_session *>(ss[0]);
+    cudaStream_t st = pick(stream, lead->stream);
+    int32_t rc = sessions_attention_dev(ss, n, dq, Hq, scale, dout, st, lead->part, err);
+    if (rc) return rc;
+    CUDA_TRY(mark_dev(lead->dev_done, st), "batched attention_dev");
+    return set_err(err, KIVI_OK);
+}
+
+int32_t kivi_sessions_attention_batched(const kivi_session *const *ss, uint64_t n,
+                                        const float *queries, uint64_t queries_len, uint64_t Hq,
+                                        float scale, float *out, uint64_t out_len,
+                                        kivi_error *err) {
+    if (!ss || n == 0 || !ss[0]) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "no sessions");
+    const KvState &p = ss[0]->prefix->s;
+    int32_t rc = check_query(p, Hq, 0, false, err);
+    if (rc) return rc;
+    const uint64_t total = n * p.B * Hq * p.D;
+    if (queries_len != total) return set_err(err, KIVI_ERR_SHAPE, total, queries_len);
+    if (out_len != total) return set_err(err, KIVI_ERR_SHAPE, total, out_len);
+    kivi_session *lead = const_cast<kivi_session *>(ss[0]);
+    std::lock_guard<std::mutex> lk(lead->mu);
+    DeviceGuard dg(p.device);
+    for (uint64_t i = 0; i < n; ++i)
+        CUDA_TRY(wait_dev(lead->stream, ss[i]->dev_done), "batched attention");
+    CUDA_TRY(lead->stage.ensure(2 * total * 4), "batched staging");
+    float *dq = lead->stage.as<float>(), *dout = lead->stage.as<float>(total * 4);
+    CUDA_TRY(cudaMemcpyAsync(dq, queries, total * 4, cudaMemcpyHostToDevice, lead->stream), "batched H2D");
+    rc = sessions_attention_dev(ss, n, dq, Hq, scale, dout, lead->stream, lead->part, err);
+    if (rc) return rc;
+    CUDA_TRY(cudaMemcpyAsync(out, dout, total * 4, cudaMemcpyDeviceToHost, lead->stream), "batched D2H");
+    CUDA_TRY(cudaStreamSynchronize(lead->stream), "batched attention");
+    return set_err(err, KIVI_OK);
+}
+
+// ---------------------------------------------------------------- standalone codec
+
+static int32_t check_quant_args(int32_t axis, uint64_t data_len, uint64_t batch, uint64_t heads,
+                                uint64_t tokens, uint64_t head_dim, uint32_t bits, uint64_t group,
+                                bool check_len, kivi_error *err) {
+    // quant.rs:235-273
+    int32_t rc = check_bits_group(bits, group, err);
+    if (rc) return rc;
+    if (batch == 0) return set_err(err, KIVI_ERR_ZERO_DIMENSION, 0, 0, "batch");
+    if (heads == 0) return set_err(err, KIVI_ERR_ZERO_DIMENSION, 0, 0, "heads");
+    if (head_dim == 0) return set_err(err, KIVI_ERR_ZERO_DIMENSION, 0, 0, "head_dim");
+    if (axis == 0) {
+        if (tokens == 0 || tokens % group != 0) return set_err(err, KIVI_ERR_TOKEN_GROUP, tokens, group);
+    } else if (head_dim % group != 0) {
+        return set_err(err, KIVI_ERR_HEAD_DIM, head_dim, group);
+    }
+    const uint64_t expected = batch * heads * tokens * head_dim;
+    if (check_len && data_len != expected) return set_err(err, KIVI_ERR_SHAPE, expected, data_len);
+    if (group > kMaxGroup || head_dim > kMaxHeadDim || batch * heads > 65535)
+        return set_msg(err, KIVI_ERR_UNSUPPORTED, "shape beyond the device kernels' limits");
+    return KIVI_OK;
+}
+
+int32_t kivi_quantized_sizes(int32_t axis, uint64_t batch, uint64_t heads, uint64_t tokens,
+                             uint64_t head_dim, uint32_t bits, uint64_t group, uint64_t *ncodes,
+                             uint64_t *nparams, kivi_error *err) {
+    if (axis != 0 && axis != 1) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "axis must be 0 or 1");
+    int32_t rc = check_quant_args(axis, 0, batch, heads, tokens, head_dim, bits, group, false, err);
+    if (rc) return rc;
+    const uint64_t n = batch * heads;
+    if (ncodes) *ncodes = n * tokens * head_dim * bits / 32;
+    if (nparams)
+        *nparams = n * 2 * (axis == 0 ? (tokens / group) * head_dim : tokens * (head_dim / group));
+    return set_err(err, KIVI_OK);
+}
+
+int32_t kivi_quantize_dev(int32_t axis, const float *d_data, uint64_t batch, uint64_t heads,
+                          uint64_t tokens, uint64_t head_dim, uint32_t bits, uint64_t group,
+                          uint32_t *d_codes, float *d_params, void *stream, kivi_error *err) {
+    if (axis != 0 && axis != 1) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "axis must be 0 or 1");
+    int32_t rc = check_quant_args(axis, 0, batch, heads, tokens, head_dim, bits, group, false, err);
+    if (rc) return rc;
+    const Geom g = kivi::make_geom((int)bits, (int)group, (int)group, (int)head_dim);
+    CUDA_TRY(kivi::launch_quantize_tensor(g, axis, (int)(batch * heads), (int64_t)tokens, d_data,
+                                          d_codes, (float2 *)d_params, (cudaStream_t)stream),
+             "quantize");
+    return set_err(err, KIVI_OK);
+}
+
+static int32_t quantize_host(int32_t axis, const float *data, uint64_t data_len, uint64_t batch,
+                             uint64_t heads, uint64_t tokens, uint64_t head_dim, uint32_t bits,
+                             uint64_t group, uint32_t *codes, uint64_t ncodes, float *params,
+                             uint64_t nparams, int32_t device, kivi_error *err) {
+    int32_t rc = check_quant_args(axis, data_len, batch, heads, tokens, head_dim, bits, group, true, err);
+    if (rc) return rc;
+    uint64_t nc = 0, np = 0;
+    kivi_quantized_sizes(axis, batch, heads, tokens, head_dim, bits, group, &nc, &np, nullptr);
+    if (ncodes != nc) return set_err(err, KIVI_ERR_SHAPE, nc, ncodes);
+    if (nparams != np) return set_err(err, KIVI_ERR_SHAPE, np, nparams);
+    if (!data || !codes || !params) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null buffer");
+    DeviceGuard dg(device);
+    float *dd = nullptr, *dp = nullptr;
+    uint32_t *dc = nullptr;
+    cudaError_t e;
+    if ((e = dalloc(&dd, data_len)) != cudaSuccess || (e = dalloc(&dc, nc)) != cudaSuccess ||
+        (e = dalloc(&dp, np)) != cudaSuccess) {
+        dfree(dd);
+        dfree(dc);
+        dfree(dp);
+        return cuda_fail(err, e, "quantize alloc");
+    }
+    int32_t out = KIVI_OK;
+    cudaStream_t st = nullptr;
+    if ((e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking)) != cudaSuccess ||
+        (e = cudaMemcpyAsync(dd, data, data_len * 4, cudaMemcpyHostToDevice, st)) != cudaSuccess) {
+        out = cuda_fail(err, e, "quantize");
+    } else {
+        out = kivi_quantize_dev(axis, dd, batch, heads, tokens, head_dim, bits, group, dc, dp, st, err);
+        if (out == KIVI_OK) {
+            if ((e = cudaMemcpyAsync(codes, dc, nc * 4, cudaMemcpyDeviceToHost, st)) != cudaSuccess ||
+                (e = cudaMemcpyAsync(params, dp, np * 4, cudaMemcpyDeviceToHost, st)) != cudaSuccess ||
+                (e = cudaStreamSynchronize(st)) != cudaSuccess)
+                out = cuda_fail(err, e, "quantize D2H");
+        }
+    }
+    if (st) {
+        cudaStreamSynchronize(st);
+        cudaStreamDestroy(st);
+    }
+    dfree(dd);
+    dfree(dc);
+    dfree(dp);
+    if (out == KIVI_OK) set_err(err, KIVI_OK);
+    return out;
+}
+
+int32_t kivi_quantize_per_channel(const float *data, uint64_t data_len, uint64_t batch,
+                                  uint64_t heads, uint64_t tokens, uint64_t head_dim,
+                                  uint32_t bits, uint64_t group, uint32_t *codes, uint64_t ncodes,
+                                  float *params, uint64_t nparams, int32_t device,
+                                  kivi_error *err) {
+    return quantize_host(0, data, data_len, batch, heads, tokens, head_dim, bits, group, codes,
+                         ncodes, params, nparams, device, err);
+}
+
+int32_t kivi_quantize_per_token(const float *data, uint64_t data_len, uint64_t batch,
+                                uint64_t heads, uint64_t tokens, uint64_t head_dim, uint32_t bits,
+                                uint64_t group, uint32_t *codes, uint64_t ncodes, float *params,
+                                uint64_t nparams, int32_t device, kivi_error *err) {
+    return quantize_host(1, data, data_len, batch, heads, tokens, head_dim, bits, group, codes,
+                         ncodes, params, nparams, device, err);
+}
+
+int32_t kivi_dequantize_packed_dev(int32_t axis, const uint32_t *d_codes, const float *d_params,
+                                   uint64_t batch, uint64_t heads, uint64_t tokens,
+                                   uint64_t head_dim, uint32_t bits, uint64_t group, float *d_out,
+                                   void *stream, kivi_error *err) {
+    if (axis != 0 && axis != 1) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "axis must be 0 or 1");
+    int32_t rc = check_quant_args(axis, 0, batch, heads, tokens, head_dim, bits, group, false, err);
+    if (rc) return rc;
+    const Geom g = kivi::make_geom((int)bits, (int)group, (int)group, (int)head_dim);
+    CUDA_TRY(kivi::launch_dequant_tensor(g, axis, (int)(batch * heads), (int64_t)tokens, d_codes,
+                                         (const float2 *)d_params, d_out, (cudaStream_t)stream),
+             "dequantize");
+    return set_err(err, KIVI_OK);
+}
+
+int32_t kivi_dequantize_packed(int32_t axis, const uint32_t *codes, uint64_t ncodes,
+                               const float *params, uint64_t nparams, uint64_t batch,
+                               uint64_t heads, uint64_t tokens, uint64_t head_dim, uint32_t bits,
+                               uint64_t group, float *out, uint64_t out_len, int32_t device,
+                               kivi_error *err) {
+    uint64_t nc = 0, np = 0;
+    int32_t rc = kivi_quantized_sizes(axis, batch, heads, tokens, head_dim, bits, group, &nc, &np, err);
+    if (rc) return rc;
+    const uint64_t n = batch * heads * tokens * head_dim;
+    if (ncodes != nc) return set_err(err, KIVI_ERR_SHAPE, nc, ncodes);
+    if (nparams != np) return set_err(err, KIVI_ERR_SHAPE, np, nparams);
+    if (out_len != n) return set_err(err, KIVI_ERR_SHAPE, n, out_len);
+    if (!codes || !params || !out) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null buffer");
+    DeviceGuard dg(device);
+    uint32_t *dc = nullptr;
+    float *dp = nullptr, *dout = nullptr;
+    cudaError_t e;
+    if ((e = dalloc(&dc, nc)) != cudaSuccess || (e = dalloc(&dp, np)) != cudaSuccess ||
+        (e = dalloc(&dout, n)) != cudaSuccess) {
+        dfree(dc);
+        dfree(dp);
+        dfree(dout);
+        return cuda_fail(err, e, "dequantize alloc");
+    }
+    int32_t res = KIVI_OK;
+    cudaStream_t st = nullptr;
+    if ((e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking)) != cudaSuccess ||
+        (e = cudaMemcpyAsync(dc, codes, nc * 4, cudaMemcpyHostToDevice, st)) != cudaSuccess ||
+        (e = cudaMemcpyAsync(dp, params, np * 4, cudaMemcpyHostToDevice, st)) != cudaSuccess) {
+        res = cuda_fail(err, e, "dequantize");
+    } else {
+        res = kivi_dequantize_packed_dev(axis, dc, dp, batch, heads, tokens, head_dim, bits, group,
+                                         dout, st, err);
+        if (res == KIVI_OK &&
+            ((e = cudaMemcpyAsync(out, dout, n * 4, cudaMemcpyDeviceToHost, st)) != cudaSuccess ||
+             (e = cudaStreamSynchronize(st)) != cudaSuccess))
+            res = cuda_fail(err, e, "dequantize D2H");
+    }
+    if (st) {
+        cudaStreamSynchronize(st);
+        cudaStreamDestroy(st);
+    }
+    dfree(dc);
+    dfree(dp);
+    dfree(dout);
+    if (res == KIVI_OK) set_err(err, KIVI_OK);
+    return res;
+}
+
+int32_t kivi_pytorch_codes(int32_t axis, const uint32_t *codes, uint64_t ncodes, uint64_t batch,
+                           uint64_t heads, uint64_t tokens, uint64_t head_dim, uint32_t bits,
+                           uint64_t group, uint32_t *out, uint64_t out_len, kivi_error *err) {
+    uint64_t nc = 0;
+    int32_t rc = kivi_quantized_sizes(axis, batch, heads, tokens, head_dim, bits, group, &nc, nullptr, err);
+    if (rc) return rc;
+    if (ncodes != nc) return set_err(err, KIVI_ERR_SHAPE, nc, ncodes);
+    if (out_len != nc) return set_err(err, KIVI_ERR_SHAPE, nc, out_len);
+    if (!codes || !out) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null buffer");
+    // quant.rs:77-112: a word permutation of the PackedStream order.
+    const uint64_t feat = 32 / bits, per = tokens * head_dim * bits / 32;
+    const uint64_t ipg = group * bits / 32;
+    uint64_t o = 0;
+    for (uint64_t hi = 0; hi < batch * heads; ++hi) {
+        const uint32_t *sc = codes + hi * per;
+        if (axis == 0) {
+            for (uint64_t tp = 0; tp < tokens / feat; ++tp) {
+                const uint64_t g = tp / ipg, w = tp % ipg;
+                for (uint64_t d = 0; d < head_dim; ++d) out[o++] = sc[(g * head_dim + d) * ipg + w];
+            }
+        } else {
+            const uint64_t n_ch = head_dim / group, d_pack = head_dim / feat;
+            for (uint64_t t = 0; t < tokens; ++t)
+                for (uint64_t dp = 0; dp < d_pack; ++dp) {
+                    const uint64_t cg = dp / ipg, w = dp % ipg;
+                    out[o++] = sc[(t * n_ch + cg) * ipg + w];
+                }
+        }
+    }
+    return set_err(err, KIVI_OK);
+}
+
+// ---------------------------------------------------------------- budget.rs
+
+uint64_t kivi_layer_kv_bytes(const kivi_config *c, uint64_t h, uint64_t d, uint64_t tokens) {
+    if (!c || tokens == 0) return 0;
+    // budget.rs:317-347
+    const uint64_t r = c->residual_length, g = c->group_size, b = c->bits;
+    const uint64_t key_res = tokens % r, key_quant = tokens - key_res;
+    const uint64_t val_res = tokens < r ? tokens : r;
+    const uint64_t val_quant = tokens > r ? tokens - r : 0;
+    const uint64_t val_groups = (d + g - 1) / g;
+    return h * key_quant * d * b / 8 + h * (key_quant / g) * d * 8 + h * val_quant * d * b / 8 +
+           h * val_quant * val_groups * 8 + h * d * 4 * (key_res + val_res);
+}
+
+uint64_t kivi_marginal_bytes_per_layer(const kivi_config *c, uint64_t h, uint64_t d) {
+    if (!c) return 0;
+    // budget.rs:349-364
+    const uint64_t b = c->bits, g = c->group_size;
+    return (d * b / 8 + d * 8 / g + d * b / 8 + (d + g - 1) / g * 8) * h;
+}
+
+} // extern "C"

@@ -1,0 +1,151 @@
+// kivi_internal.cuh -- device layout of the packed KIVI store and the kernel
+// launchers shared by the translation units of libkivi_gpu.so.
+//
+// HBM layout (one allocation per array, `cap` packed tokens per stream,
+// stream = b * num_kv_heads + h):
+//   kcodes  u32    [stream][cap/G][D][ipc]    ipc = G*bits/32   (PackedStream keys,
+//                                                                quant.rs:275-328)
+//   kparams float2 [stream][cap/G][D]         (scale, zero) per (key group, channel)
+//   vcodes  u32    [stream][cap][D/G][ipg]    ipg = G*bits/32   (PackedStream values,
+//                                                                quant.rs:330-377)
+//   vparams float2 [stream][cap][D/G]         (scale, zero) per (token, channel group)
+//   kres    f32    [stream][R][D]             key residual, rows 0..key_res_len
+//   vres    f32    [stream][R][D]             value window as a ring: logical row j
+//                                             lives in slot (vhead + j) % R
+// Each stream's packed region is the reference's PackedStream word/param order,
+// so exporting a stream is a plain device-to-host copy.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace kivi {
+
+// Compile-time-free geometry of one cache (KiviConfig + head_dim).
+struct Geom {
+    int bits;      // 2, 4, 8
+    int G;         // group_size
+    int R;         // residual_length
+    int D;         // head_dim
+    int nch;       // D / G   (value channel groups per token)
+    int ipc;       // G * bits / 32 (key words per channel per group; == ipg)
+    int tpw;       // 32 / bits  (codes per word)
+    uint32_t mask; // (1 << bits) - 1
+    float levels;  // 2^bits - 1
+};
+
+Geom make_geom(int bits, int G, int R, int D);
+
+struct Store {
+    uint32_t *kcodes = nullptr;
+    float2 *kparams = nullptr;
+    uint32_t *vcodes = nullptr;
+    float2 *vparams = nullptr;
+    float *kres = nullptr;
+    float *vres = nullptr;
+    int64_t cap = 0; // packed tokens per stream (multiple of R)
+};
+
+// Per-stream strides (in elements of each array).
+__host__ __device__ inline int64_t code_stride(const Geom &g, int64_t cap) {
+    return cap * g.D * g.bits / 32;
+}
+__host__ __device__ inline int64_t kparam_stride(const Geom &g, int64_t cap) {
+    return cap / g.G * g.D;
+}
+__host__ __device__ inline int64_t vparam_stride(const Geom &g, int64_t cap) {
+    return cap * g.nch;
+}
+
+// One session's fp32 suffix: keys/values [stream][cap][D], rows 0..len.
+struct SuffixRef {
+    const float *k;
+    const float *v;
+    int64_t len;
+    int64_t cap;
+};
+
+constexpr int kMaxSessionsPerLaunch = 64;
+
+// Everything one attention launch needs.  Token order per stream is the
+// reference's logit order (attention.rs:43-46): packed prefix keys, prefix
+// key residual, session suffix.
+struct AttnArgs {
+    Geom g;
+    Store st;
+    int B, H, Hq, Gq;
+    int64_t kq, vq;           // quantized key / value tokens of the prefix
+    int kres_len, vres_len;   // fp32 key residual rows / value window rows
+    int vhead;                // ring head of the value window
+    int64_t seq_p;            // prefix tokens (kq + kres_len == vq + vres_len)
+    int64_t main_tokens;      // tokens [0, main_tokens) have packed K and V and
+                              // are processed in whole chunks
+    int64_t chunk_tokens;     // tokens per main chunk
+    int NC;                   // number of main chunks
+    int parts;                // partial slots per row = NC + 2 (prefix tail, suffix)
+    int S;                    // sessions in this launch
+    int session_base;         // index of the first session of this launch
+    const float *q;           // [S_total][B][Hq][D]
+    float scale;
+    float *part_ml;           // [rows][parts][2]  (m, l)
+    float *part_o;            // [rows][parts][D]
+    SuffixRef suf[kMaxSessionsPerLaunch];
+};
+
+// Counts this library's kernel launches (reported as gpu_launches).
+void count_launch(int n = 1);
+uint64_t launch_count();
+
+// ---------------------------------------------------------------- quantize
+// Decode-path append (seq < R): key residual copy (+ flush when it fills) and
+// value window eviction/insert for every stream, one CTA per stream.
+cudaError_t launch_append_small(const Geom &g, const Store &st, int n, const float *keys,
+                                const float *values, int seq, int kres_len, int64_t kq,
+                                int vres_len, int64_t vq, int vhead, cudaStream_t s);
+// Quantize `ngroups` key groups per stream from the combined timeline
+// [residual rows 0..nres) ++ [input rows 0..in_seq) into groups out_group0...
+cudaError_t launch_key_groups(const Geom &g, const Store &st, int n, const float *res, int nres,
+                              const float *in, int64_t in_seq, int64_t ngroups,
+                              int64_t out_group0, cudaStream_t s);
+// Quantize `ntok` value tokens per stream from [window rows 0..nwin (ring at
+// vhead)] ++ [input rows in_off..] into tokens out_tok0...
+cudaError_t launch_value_tokens(const Geom &g, const Store &st, int n, int nwin, int vhead,
+                                const float *in, int64_t in_seq, int64_t in_off, int64_t ntok,
+                                int64_t out_tok0, cudaStream_t s);
+// Copy input rows [src_off, src_off+count) of every stream into ring/linear rows:
+// dst slot = (dst_head + dst_off + i) % ring (ring = R for the value window, or
+// a huge number for a linear buffer).
+cudaError_t launch_copy_rows(float *dst, int64_t dst_stream_rows, int64_t dst_head,
+                             int64_t dst_off, int64_t ring, const float *src, int64_t src_seq,
+                             int64_t src_off, int64_t count, int n, int D, cudaStream_t s);
+// Dense reconstruction (cache.rs:282-325) into [n][seq][D].
+cudaError_t launch_dequant_cache(const Geom &g, const Store &st, int n, int64_t seq, int64_t kq,
+                                 int64_t vq, int vhead, float *keys, float *values,
+                                 cudaStream_t s);
+// Standalone codec (quant.rs:153-233) on a [n][tokens][D] tensor; codes/params
+// written densely per stream (cap = tokens).
+cudaError_t launch_quantize_tensor(const Geom &g, int axis, int n, int64_t tokens,
+                                   const float *data, uint32_t *codes, float2 *params,
+                                   cudaStream_t s);
+cudaError_t launch_dequant_tensor(const Geom &g, int axis, int n, int64_t tokens,
+                                  const uint32_t *codes, const float2 *params, float *out,
+                                  cudaStream_t s);
+// Value window -> packed values for all rows (kivi_cache_seal).
+// (uses launch_value_tokens with in == nullptr)
+
+// ---------------------------------------------------------------- attention
+// Partial-softmax chunks (any config).
+cudaError_t launch_attention_chunks(const AttnArgs &a, cudaStream_t s);
+// LSE merge of a.parts partials per row.  mode 0: normalised output rows;
+// mode 1: merged (m, l, o) rows.
+cudaError_t launch_merge(const float *part_ml, const float *part_o, int64_t rows, int parts, int D,
+                         int ml_stride_pairs, float *out, float *out_m, float *out_l, int mode,
+                         cudaStream_t s);
+// Cross-shard merge: m/l [parts][rows], o [parts][rows][D].
+cudaError_t launch_merge_shards(const float *m, const float *l, const float *o, int64_t parts,
+                                int64_t rows, int D, float *out, cudaStream_t s);
+// Dynamic shared memory the attention kernel needs for `rows` query rows.
+size_t attention_smem_bytes(int D, int rows);
+int attention_max_rows(int D);
+
+} // namespace kivi

@@ -1,0 +1,335 @@
+// kivi_quant.cu -- KIVI quantize-and-pack kernels for sm_100a.
+//
+// Bit-exactness with the reference codec (quant.rs:275-377, 453-485):
+//   * group min/max with fminf/fmaxf (Rust f32::min/max ignore a NaN operand
+//     the same way) -- exact, so reduction order is free;
+//   * scale = (max - min) / levels with IEEE division (__fdiv_rn), 0 when the
+//     span is 0 (quant.rs:453-459);
+//   * code = clamp(round_half_even((x - zero) / scale), 0, levels): the
+//     quotient is >= 0, and rintf (round-to-nearest-even) equals the
+//     reference's floor/frac/parity rounding (quant.rs:474-485) for every
+//     finite input; NaN -> 0 like Rust's saturating `as u32`;
+//   * codes packed first-element-in-low-bits (quant.rs:312-322);
+//   * dequantization is one fused multiply-add fma(code, scale, zero)
+//     (quant.rs:404-406).
+// No --use_fast_math anywhere in this library.
+#include <math.h>
+
+#include "kivi_internal.cuh"
+
+namespace kivi {
+
+Geom make_geom(int bits, int G, int R, int D) {
+    Geom g;
+    g.bits = bits;
+    g.G = G;
+    g.R = R;
+    g.D = D;
+    g.nch = D / G;
+    g.ipc = G * bits / 32;
+    g.tpw = 32 / bits;
+    g.mask = (1u << bits) - 1u;
+    g.levels = (float)((1u << bits) - 1u);
+    return g;
+}
+
+namespace {
+
+__device__ __forceinline__ float scale_of(float span, float levels) {
+    return span == 0.0f ? 0.0f : __fdiv_rn(span, levels);
+}
+
+__device__ __forceinline__ uint32_t quant_code(float x, float zero, float scale, float levels) {
+    if (scale == 0.0f) return 0u;
+    float r = rintf(__fdiv_rn(__fsub_rn(x, zero), scale));
+    if (!(r == r)) return 0u;
+    if (r < 0.0f) return 0u;
+    if (r > levels) r = levels;
+    return (uint32_t)r;
+}
+
+// Per-channel key quantization of one channel `d` of one group whose G rows
+// are rows[u * D] (u < G).  quant.rs:296-325.
+__device__ __forceinline__ void quant_key_channel(const Geom &g, const float *const *rows, int d,
+                                                  uint32_t *words, float2 *param) {
+    float mn = INFINITY, mx = -INFINITY;
+    for (int u = 0; u < g.G; ++u) {
+        float x = rows[u][d];
+        mn = fminf(mn, x);
+        mx = fmaxf(mx, x);
+    }
+    const float scale = scale_of(__fsub_rn(mx, mn), g.levels);
+    *param = make_float2(scale, mn);
+    for (int i = 0; i < g.ipc; ++i) {
+        uint32_t w = 0;
+        for (int k = 0; k < g.tpw; ++k)
+            w |= quant_code(rows[i * g.tpw + k][d], mn, scale, g.levels) << (k * g.bits);
+        words[i] = w;
+    }
+}
+
+// Per-token value quantization of channel group `cg` of one token row.
+// quant.rs:349-374.
+__device__ __forceinline__ void quant_value_group(const Geom &g, const float *row, int cg,
+                                                  uint32_t *words, float2 *param) {
+    const float *grp = row + cg * g.G;
+    float mn = INFINITY, mx = -INFINITY;
+    for (int i = 0; i < g.G; ++i) {
+        float x = grp[i];
+        mn = fminf(mn, x);
+        mx = fmaxf(mx, x);
+    }
+    const float scale = scale_of(__fsub_rn(mx, mn), g.levels);
+    *param = make_float2(scale, mn);
+    for (int w = 0; w < g.ipc; ++w) {
+        uint32_t word = 0;
+        for (int k = 0; k < g.tpw; ++k)
+            word |= quant_code(grp[w * g.tpw + k], mn, scale, g.levels) << (k * g.bits);
+        words[w] = word;
+    }
+}
+
+constexpr int kMaxG = 256; // largest group handled by the row-pointer tables below
+
+// ---------------------------------------------------------------- decode append
+// One CTA per stream.  Keys: copy rows into the residual; if it fills, flush R
+// tokens (cache.rs:382-430) and continue with the remaining rows.  Values:
+// quantize the `drop` oldest window rows, then write the new rows into the
+// ring slots they free (cache.rs:455-483 without the O(R*D) shift).
+__global__ void __launch_bounds__(256) append_small_kernel(Geom g, Store st, const float *keys,
+                                                           const float *values, int seq,
+                                                           int kres_len, int64_t kq, int vres_len,
+                                                           int64_t vq, int vhead) {
+    const int s = blockIdx.x;
+    const int D = g.D, R = g.R;
+    const float *kin = keys + (int64_t)s * seq * D;
+    const float *vin = values + (int64_t)s * seq * D;
+    float *kres = st.kres + (int64_t)s * R * D;
+    float *vres = st.vres + (int64_t)s * R * D;
+    __shared__ const float *rows[kMaxG];
+
+    const int take1 = min(seq, R - kres_len);
+    for (int e = threadIdx.x; e < take1 * D; e += blockDim.x) kres[(int64_t)kres_len * D + e] = kin[e];
+    if (kres_len + take1 == R) {
+        __syncthreads();
+        const int ngroups = R / g.G;
+        uint32_t *kc = st.kcodes + (int64_t)s * code_stride(g, st.cap);
+        float2 *kp = st.kparams + (int64_t)s * kparam_stride(g, st.cap);
+        const int64_t g0 = kq / g.G;
+        for (int gi = 0; gi < ngroups; ++gi) {
+            if (threadIdx.x < g.G) rows[threadIdx.x] = kres + ((int64_t)gi * g.G + threadIdx.x) * D;
+            __syncthreads();
+            for (int d = threadIdx.x; d < D; d += blockDim.x) {
+                const int64_t og = g0 + gi;
+                quant_key_channel(g, rows, d, kc + (og * D + d) * g.ipc, kp + og * D + d);
+            }
+            __syncthreads();
+        }
+        const int rest = seq - take1;
+        for (int e = threadIdx.x; e < rest * D; e += blockDim.x) kres[e] = kin[(int64_t)take1 * D + e];
+    }
+
+    const int drop = max(0, vres_len + seq - R);
+    uint32_t *vc = st.vcodes + (int64_t)s * code_stride(g, st.cap);
+    float2 *vp = st.vparams + (int64_t)s * vparam_stride(g, st.cap);
+    for (int p = threadIdx.x; p < drop * g.nch; p += blockDim.x) {
+        const int j = p / g.nch, cg = p % g.nch;
+        const int slot = (vhead + j) % R;
+        const int64_t t = vq + j;
+        quant_value_group(g, vres + (int64_t)slot * D, cg, vc + (t * g.nch + cg) * g.ipc,
+                          vp + t * g.nch + cg);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < seq * D; e += blockDim.x) {
+        const int i = e / D, d = e - i * D;
+        const int slot = (vhead + vres_len + i) % R;
+        vres[(int64_t)slot * D + d] = vin[e];
+    }
+}
+
+// ---------------------------------------------------------------- bulk keys
+// grid (ngroups, n): one CTA per (key group, stream), one thread per channel.
+__global__ void __launch_bounds__(128) key_groups_kernel(Geom g, Store st, const float *res,
+                                                         int nres, const float *in, int64_t in_seq,
+                                                         int64_t out_group0) {
+    const int64_t gi = blockIdx.x;
+    const int s = blockIdx.y;
+    const int D = g.D;
+    __shared__ const float *rows[kMaxG];
+    for (int u = threadIdx.x; u < g.G; u += blockDim.x) {
+        const int64_t c = gi * g.G + u;
+        rows[u] = c < nres ? res + ((int64_t)s * g.R + c) * D
+                           : in + ((int64_t)s * in_seq + (c - nres)) * D;
+    }
+    __syncthreads();
+    uint32_t *kc = st.kcodes + (int64_t)s * code_stride(g, st.cap);
+    float2 *kp = st.kparams + (int64_t)s * kparam_stride(g, st.cap);
+    const int64_t og = out_group0 + gi;
+    for (int d = threadIdx.x; d < D; d += blockDim.x)
+        quant_key_channel(g, rows, d, kc + (og * D + d) * g.ipc, kp + og * D + d);
+}
+
+// ---------------------------------------------------------------- bulk values
+// grid (ceil(ntok*nch/128), n): one thread per (token, channel group).
+__global__ void __launch_bounds__(128) value_tokens_kernel(Geom g, Store st, int nwin, int vhead,
+                                                           const float *in, int64_t in_seq,
+                                                           int64_t in_off, int64_t ntok,
+                                                           int64_t out_tok0) {
+    const int s = blockIdx.y;
+    const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (p >= ntok * g.nch) return;
+    const int64_t j = p / g.nch;
+    const int cg = (int)(p - j * g.nch);
+    const float *row = j < nwin ? st.vres + ((int64_t)s * g.R + (vhead + j) % g.R) * g.D
+                                : in + ((int64_t)s * in_seq + in_off + (j - nwin)) * g.D;
+    const int64_t t = out_tok0 + j;
+    uint32_t *vc = st.vcodes + (int64_t)s * code_stride(g, st.cap);
+    float2 *vp = st.vparams + (int64_t)s * vparam_stride(g, st.cap);
+    quant_value_group(g, row, cg, vc + (t * g.nch + cg) * g.ipc, vp + t * g.nch + cg);
+}
+
+// ---------------------------------------------------------------- row copies
+__global__ void copy_rows_kernel(float *dst, int64_t dst_stream_rows, int64_t dst_head,
+                                 int64_t dst_off, int64_t ring, const float *src, int64_t src_seq,
+                                 int64_t src_off, int64_t count, int D) {
+    const int s = blockIdx.y;
+    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= count * D) return;
+    const int64_t i = e / D, d = e - i * D;
+    const int64_t slot = (dst_head + dst_off + i) % ring;
+    dst[((int64_t)s * dst_stream_rows + slot) * D + d] = src[((int64_t)s * src_seq + src_off + i) * D + d];
+}
+
+// ---------------------------------------------------------------- dequantize
+__device__ __forceinline__ float dq_key(const Geom &g, const uint32_t *kc, const float2 *kp,
+                                        int64_t t, int d) {
+    const int64_t grp = t / g.G;
+    const int u = (int)(t - grp * g.G);
+    const uint32_t w = kc[(grp * g.D + d) * g.ipc + u / g.tpw];
+    const uint32_t code = (w >> ((u % g.tpw) * g.bits)) & g.mask;
+    const float2 p = kp[grp * g.D + d];
+    return __fmaf_rn((float)code, p.x, p.y);
+}
+
+__device__ __forceinline__ float dq_value(const Geom &g, const uint32_t *vc, const float2 *vp,
+                                          int64_t t, int d) {
+    const int cg = d / g.G, lc = d - cg * g.G;
+    const uint32_t w = vc[(t * g.nch + cg) * g.ipc + lc / g.tpw];
+    const uint32_t code = (w >> ((lc % g.tpw) * g.bits)) & g.mask;
+    const float2 p = vp[t * g.nch + cg];
+    return __fmaf_rn((float)code, p.x, p.y);
+}
+
+__global__ void dequant_cache_kernel(Geom g, Store st, int64_t seq, int64_t kq, int64_t vq,
+                                     int vhead, float *keys, float *values) {
+    const int s = blockIdx.y;
+    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= seq * g.D) return;
+    const int64_t t = e / g.D;
+    const int d = (int)(e - t * g.D);
+    const uint32_t *kc = st.kcodes + (int64_t)s * code_stride(g, st.cap);
+    const float2 *kp = st.kparams + (int64_t)s * kparam_stride(g, st.cap);
+    const uint32_t *vc = st.vcodes + (int64_t)s * code_stride(g, st.cap);
+    const float2 *vp = st.vparams + (int64_t)s * vparam_stride(g, st.cap);
+    const int64_t o = (int64_t)s * seq * g.D + e;
+    keys[o] = t < kq ? dq_key(g, kc, kp, t, d) : st.kres[((int64_t)s * g.R + (t - kq)) * g.D + d];
+    values[o] = t < vq ? dq_value(g, vc, vp, t, d)
+                       : st.vres[((int64_t)s * g.R + (vhead + (t - vq)) % g.R) * g.D + d];
+}
+
+__global__ void dequant_tensor_kernel(Geom g, int axis, int64_t tokens, const uint32_t *codes,
+                                      const float2 *params, float *out) {
+    const int s = blockIdx.y;
+    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= tokens * g.D) return;
+    const int64_t t = e / g.D;
+    const int d = (int)(e - t * g.D);
+    const uint32_t *c = codes + (int64_t)s * code_stride(g, tokens);
+    const int64_t o = (int64_t)s * tokens * g.D + e;
+    if (axis == 0)
+        out[o] = dq_key(g, c, params + (int64_t)s * kparam_stride(g, tokens), t, d);
+    else
+        out[o] = dq_value(g, c, params + (int64_t)s * vparam_stride(g, tokens), t, d);
+}
+
+inline unsigned blocks_for(int64_t n, int t) { return (unsigned)((n + t - 1) / t); }
+
+} // namespace
+
+cudaError_t launch_append_small(const Geom &g, const Store &st, int n, const float *keys,
+                                const float *values, int seq, int kres_len, int64_t kq,
+                                int vres_len, int64_t vq, int vhead, cudaStream_t s) {
+    if (n <= 0 || seq <= 0) return cudaSuccess;
+    append_small_kernel<<<n, 256, 0, s>>>(g, st, keys, values, seq, kres_len, kq, vres_len, vq,
+                                          vhead);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_key_groups(const Geom &g, const Store &st, int n, const float *res, int nres,
+                              const float *in, int64_t in_seq, int64_t ngroups,
+                              int64_t out_group0, cudaStream_t s) {
+    if (n <= 0 || ngroups <= 0) return cudaSuccess;
+    key_groups_kernel<<<dim3((unsigned)ngroups, n), 128, 0, s>>>(g, st, res, nres, in, in_seq,
+                                                                   out_group0);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_value_tokens(const Geom &g, const Store &st, int n, int nwin, int vhead,
+                                const float *in, int64_t in_seq, int64_t in_off, int64_t ntok,
+                                int64_t out_tok0, cudaStream_t s) {
+    if (n <= 0 || ntok <= 0) return cudaSuccess;
+    value_tokens_kernel<<<dim3(blocks_for(ntok * g.nch, 128), n), 128, 0, s>>>(
+        g, st, nwin, vhead, in, in_seq, in_off, ntok, out_tok0);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_copy_rows(float *dst, int64_t dst_stream_rows, int64_t dst_head,
+                             int64_t dst_off, int64_t ring, const float *src, int64_t src_seq,
+                             int64_t src_off, int64_t count, int n, int D, cudaStream_t s) {
+    if (n <= 0 || count <= 0) return cudaSuccess;
+    copy_rows_kernel<<<dim3(blocks_for(count * D, 256), n), 256, 0, s>>>(
+        dst, dst_stream_rows, dst_head, dst_off, ring, src, src_seq, src_off, count, D);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dequant_cache(const Geom &g, const Store &st, int n, int64_t seq, int64_t kq,
+                                 int64_t vq, int vhead, float *keys, float *values,
+                                 cudaStream_t s) {
+    if (n <= 0 || seq <= 0) return cudaSuccess;
+    dequant_cache_kernel<<<dim3(blocks_for(seq * g.D, 256), n), 256, 0, s>>>(g, st, seq, kq, vq,
+                                                                             vhead, keys, values);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_tensor(const Geom &g, int axis, int n, int64_t tokens,
+                                   const float *data, uint32_t *codes, float2 *params,
+                                   cudaStream_t s) {
+    if (n <= 0 || tokens <= 0) return cudaSuccess;
+    Store st;
+    st.cap = tokens;
+    if (axis == 0) {
+        st.kcodes = codes;
+        st.kparams = params;
+        return launch_key_groups(g, st, n, nullptr, 0, data, tokens, tokens / g.G, 0, s);
+    }
+    st.vcodes = codes;
+    st.vparams = params;
+    return launch_value_tokens(g, st, n, 0, 0, data, tokens, 0, tokens, 0, s);
+}
+
+cudaError_t launch_dequant_tensor(const Geom &g, int axis, int n, int64_t tokens,
+                                  const uint32_t *codes, const float2 *params, float *out,
+                                  cudaStream_t s) {
+    if (n <= 0 || tokens <= 0) return cudaSuccess;
+    dequant_tensor_kernel<<<dim3(blocks_for(tokens * g.D, 256), n), 256, 0, s>>>(
+        g, axis, tokens, codes, params, out);
+    count_launch();
+    return cudaGetLastError();
+}
+
+} // namespace kivi

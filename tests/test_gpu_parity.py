@@ -1,0 +1,620 @@
+"""GPU parity: the CUDA path (through the C ABI) against the CPU oracle.
+
+Bar: packed codes, scales and zeros bit-exact;
+attention max-abs <= 1e-4 and relative L2 <= 1e-5 against the reference's
+fp32 output; the reference's bitwise self-consistency properties
+(determinism, session == cache, runtime == cache, chunked == one-shot) hold
+bit for bit on the device.  Each reference test is cited by file:line.
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+from helpers import (
+    concat_head_major,
+    dense_attend,
+    document,
+    fill,
+    fill_wide,
+    golden_tensor,
+    max_abs,
+    packed_word,
+    rel_l2,
+    slice_tokens,
+    synthetic_kv,
+    token_mean,
+)
+
+pytestmark = pytest.mark.gpu
+
+ATOL = 1e-4   # max abs error vs the reference fp32 output
+RTOL_L2 = 1e-5  # relative L2 error vs the reference fp32 output
+
+
+@pytest.fixture(scope="module")
+def K():
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import kivi_cache
+
+    kivi_cache.lib()
+    return kivi_cache
+
+
+def pair(K, bits, group, residual, batch, heads, dim):
+    return (K.KiviCache(K.KiviConfig.try_new(bits, group, residual), batch, heads, dim),
+            O.KiviCache(O.KiviConfig.try_new(bits, group, residual), batch, heads, dim))
+
+
+def append_both(g, o, keys, values, seq):
+    g.append(keys, values, seq)
+    o.append(keys, values, seq)
+
+
+def assert_store_equal(g, o):
+    """Counters, every PackedStream (codes, params) and the dense reconstruction, bitwise."""
+    assert g.sequence_length() == o.sequence_length()
+    assert g.key_residual_len() == o.key_residual_len()
+    assert g.value_residual_len() == o.value_residual_len()
+    assert g.quantized_key_tokens() == o.quantized_key_tokens()
+    assert g.quantized_value_tokens() == o.quantized_value_tokens()
+    for hi in range(g.batch_size() * g.num_kv_heads()):
+        for axis in (0, 1):
+            gc, gp = g.export_stream(hi, axis)
+            oc, op = o.export_stream(hi, axis)
+            assert gc.shape == oc.shape and (gc == oc).all(), (hi, axis)
+            assert gp.view(np.uint32).shape == op.view(np.uint32).shape
+            assert (gp.view(np.uint32) == op.view(np.uint32)).all(), (hi, axis)
+    gk, gv = g.dequantize()
+    ok, ov = o.dequantize()
+    assert (gk.view(np.uint32) == ok.view(np.uint32)).all()
+    assert (gv.view(np.uint32) == ov.view(np.uint32)).all()
+    gm, om = g.memory(), o.memory()
+    for k, v in om.items():
+        assert getattr(gm, k) == v, k
+
+
+def assert_attention_close(got, ref):
+    assert got.shape == ref.shape
+    assert max_abs(got, ref) <= ATOL, max_abs(got, ref)
+    assert rel_l2(got, ref) <= RTOL_L2, rel_l2(got, ref)
+
+
+# ---------------------------------------------------------------- codec
+
+
+@pytest.mark.parametrize("bits,group", [(2, 16), (2, 32), (4, 8), (4, 32), (8, 4), (8, 32), (2, 64)])
+@pytest.mark.parametrize("axis", [0, 1])
+def test_codec_bit_exact(K, bits, group, axis):
+    """quant.rs:154-233 on seeded data with outlier channels: codes, scale, zero bitwise."""
+    batch, heads, tokens, dim = 2, 3, 4 * group if axis == 0 else 37, 2 * group if group >= 32 else 64
+    keys, _, _ = synthetic_kv(bits * 100 + group, batch, heads, tokens, dim)
+    fn = K.quantize_per_channel if axis == 0 else K.quantize_per_token
+    qt = fn(keys, batch, heads, tokens, dim, bits, group)
+    oc, op = O.quantize(axis == 0, keys, batch, heads, tokens, dim, bits, group)
+    assert (qt.codes == oc).all()
+    assert (qt.params.view(np.uint32) == op.view(np.uint32)).all()
+    deq = qt.dequantize()
+    odq = O.dequantize_packed(axis == 0, oc, op, batch, heads, tokens, dim, bits, group)
+    assert (deq.view(np.uint32) == odq.view(np.uint32)).all()
+    assert (qt.pytorch_codes() == O.pytorch_codes(axis == 0, oc, batch, heads, tokens, dim, bits, group)).all()
+
+
+def test_pytorch_golden_words(K):
+    """tests/quant.rs:13-41, examples/pytorch_golden.rs:16-67"""
+    dim, seq = 32, 64
+    data = golden_tensor(seq, dim)
+    keys = K.quantize_per_channel(data, 1, 1, seq, dim, 2, 32)
+    values = K.quantize_per_token(data, 1, 1, seq, dim, 2, 32)
+    kc, vc = keys.pytorch_codes(), values.pytorch_codes()
+    assert list(kc[:4]) == [0xE4E4E4E4, 0x39393939, 0x4E4E4E4E, 0x93939393]
+    assert list(vc[:3]) == [0xE4E4E4E4, 0xE4E4E4E4, 0x39393939]
+    assert (kc == np.array([packed_word(d % 4) for d in range(dim)] * (seq // 16), np.uint32)).all()
+    assert (vc == np.array([packed_word(t % 4) for t in range(seq) for _ in range(2)], np.uint32)).all()
+    assert (keys.scale_zero().reshape(-1, 2) == [1.0, 0.0]).all()
+    assert (values.scale_zero().reshape(-1, 2) == [1.0, 0.0]).all()
+    assert (keys.dequantize() == data).all() and (values.dequantize() == data).all()
+    cache = K.KiviCache(K.KiviConfig.try_new(2, 32, 32), 1, 1, dim)
+    cache.append(data, data, seq)
+    got = cache.attention(np.ones(dim, np.float32), 1, 1.0 / np.sqrt(np.float32(dim)))
+    assert (got == np.float32(1.5)).all()
+
+
+def test_half_even_ties_and_endpoints(K):
+    """tests/quant.rs:43-129"""
+    data = np.zeros(16, np.float32)
+    data[[0, 1, 2, 3, 4, 5, 6, 15]] = [0.0, 0.5, 1.5, 2.5, 3.5, 1.2, 1.6, 15.0]
+    out = K.quantize_per_token(data, 1, 1, 1, 16, 4, 16).dequantize()
+    assert list(out[[0, 1, 2, 3, 4, 5, 6, 15]]) == [0, 0, 2, 2, 4, 1, 2, 15]
+    pat = np.ones(16, np.float32)
+    pat[:5] = [0.0, 0.5, 1.5, 2.5, 3.0]
+    expect = [0.0, 0.0, 2.0, 2.0, 3.0] + [1.0] * 11
+    assert list(K.quantize_per_token(pat, 1, 1, 1, 16, 2, 16).dequantize()) == expect
+    grid = np.zeros((16, 16), np.float32)
+    grid[:, 0] = pat
+    out = K.quantize_per_channel(grid, 1, 1, 16, 16, 2, 16).dequantize().reshape(16, 16)
+    assert list(out[:, 0]) == expect and (out[:, 1:] == 0).all()
+    grid = np.zeros((16, 16), np.float32)
+    grid[:4, 0] = [-2.0, -1.0, 0.0, 1.0]
+    out = K.quantize_per_channel(grid, 1, 1, 16, 16, 2, 16).dequantize().reshape(16, 16)
+    assert list(out[:4, 0]) == [-2.0, -1.0, 0.0, 1.0] and (out[4:, 0] == 0).all()
+    const = np.full(2 * 3 * 32 * 16, 0.25, np.float32)
+    assert (K.quantize_per_channel(const, 2, 3, 32, 16, 4, 16).dequantize() == const).all()
+    assert (K.quantize_per_token(const, 2, 3, 32, 16, 4, 16).dequantize() == const).all()
+
+
+def test_reconstruction_error_bound_and_quiet_channels(K):
+    """tests/quant.rs:131-211"""
+    data = fill_wide(32 * 32)
+    out = K.quantize_per_channel(data, 1, 1, 32, 32, 2, 32).dequantize().reshape(32, 32)
+    x = data.reshape(32, 32)
+    mn, mx = x.min(0), x.max(0)
+    scale = np.where(mx == mn, 0, (mx - mn) / np.float32(3))
+    assert (np.abs(out - x) <= scale * 0.5 + 1e-4).all()
+    data = np.zeros((32, 32), np.float32)
+    data[:, 0] = 100.0
+    data[:, 1:] = (np.arange(1, 32, dtype=np.float32) / np.float32(32))[None, :]
+    pc = K.quantize_per_channel(data, 1, 1, 32, 32, 2, 32).dequantize().reshape(32, 32)
+    pt = K.quantize_per_token(data, 1, 1, 32, 32, 2, 32).dequantize().reshape(32, 32)
+    assert np.abs(pc[:, 1:] - data[:, 1:]).mean() < 1e-5
+    assert np.abs(pt[:, 1:] - data[:, 1:]).mean() > 0.2
+
+
+# ---------------------------------------------------------------- streaming state machine
+
+
+def _append_chunks(caches, keys, values, batch, heads, total, dim, chunks):
+    off = 0
+    for n in chunks:
+        k = slice_tokens(keys, batch, heads, total, dim, off, n)
+        v = slice_tokens(values, batch, heads, total, dim, off, n)
+        for c in caches:
+            c.append(k, v, n)
+        off += n
+
+
+@pytest.mark.parametrize("bits,group,residual", [(2, 16, 32), (2, 32, 128), (4, 32, 64), (8, 16, 32)])
+def test_streaming_store_bit_exact(K, bits, group, residual):
+    """cache.rs:186-214, 382-578 chunk by chunk, incl. seq >= R and seq < R branches
+    (tests/cache.rs:59-130)."""
+    batch, heads, dim = 2, 3, 64
+    chunks = [1, residual - 1, 2, 5 * residual + 3, 1, 1, residual, 7, 3 * residual // 2, 1]
+    total = sum(chunks)
+    n = batch * heads * total * dim
+    keys, values = fill(n, 7 + bits), fill(n, 9 + group)
+    g, o = pair(K, bits, group, residual, batch, heads, dim)
+    off = 0
+    for c in chunks:
+        k = slice_tokens(keys, batch, heads, total, dim, off, c)
+        v = slice_tokens(values, batch, heads, total, dim, off, c)
+        append_both(g, o, k, v, c)
+        off += c
+        assert_store_equal(g, o)
+
+
+def test_chunked_appends_match_token_by_token(K):
+    """tests/cache.rs:78-104 on the device (bitwise)."""
+    cfg = K.KiviConfig.try_new(2, 16, 32)
+    batch, heads, dim, total = 2, 3, 16, 70
+    n = batch * heads * total * dim
+    keys, values = fill(n, 7), fill(n, 9)
+    streamed, chunked, once = (K.KiviCache(cfg, batch, heads, dim) for _ in range(3))
+    _append_chunks([streamed], keys, values, batch, heads, total, dim, [1] * total)
+    _append_chunks([chunked], keys, values, batch, heads, total, dim, [1, 50, 7, 12])
+    once.append(keys, values, total)
+    sk, sv = streamed.dequantize()
+    for other in (chunked, once):
+        ok, ov = other.dequantize()
+        assert (sk == ok).all() and (sv == ov).all()
+
+
+def test_streaming_boundaries_and_getters(K):
+    """tests/cache.rs:59-76, tests/budget.rs:5-45"""
+    cfg = K.KiviConfig.try_new(2, 16, 32)
+    cache = K.KiviCache(cfg, 2, 3, 16)
+    steps = [10, 20, 5, 100]
+    total = sum(steps)
+    n = 2 * 3 * total * 16
+    _append_chunks([cache], fill(n, 1), fill(n, 2), 2, 3, total, 16, steps)
+    assert cache.sequence_length() == total
+    assert cache.key_residual_len() == total % 32
+    assert cache.value_residual_len() == 32
+    assert cache.quantized_key_tokens() == total - total % 32
+    assert cache.quantized_value_tokens() == total - 32
+    c2 = K.KiviCache(cfg, 1, 1, 16)
+    assert c2.tokens_until_key_flush() == 32 and c2.value_residual_slots_remaining() == 32
+    c2.append(np.zeros(160), np.zeros(160), 10)
+    assert c2.tokens_until_key_flush() == 22 and c2.value_residual_slots_remaining() == 22
+    c2.append(np.zeros(16 * 22), np.zeros(16 * 22), 22)
+    assert c2.key_residual_len() == 0 and c2.tokens_until_key_flush() == 32
+    big = K.KiviCache(K.KiviConfig(), 1, 8, 128)
+    big.append(np.full(8 * 128 * 200, 0.1, np.float32), np.full(8 * 128 * 200, 0.2, np.float32), 200)
+    snap = big.budget_snapshot()
+    assert snap.sequence_tokens == 200 and snap.marginal_bytes_per_token == 1024
+    assert snap.current_layer_bytes == big.memory().compressed_bytes()
+
+
+def test_planner_bytes_match_live_cache(K):
+    """tests/budget.rs:68-82"""
+    cfg = K.KiviConfig()
+    for seq in [1, 32, 127, 128, 129, 512, 2048]:
+        cache = K.KiviCache(cfg, 1, 8, 128)
+        n = 8 * seq * 128
+        cache.append(np.full(n, 0.1, np.float32), np.full(n, 0.1, np.float32), seq)
+        assert K.layer_kv_bytes(cfg, 8, 128, seq) == cache.memory().compressed_bytes()
+
+
+def test_empty_append_and_shape_errors(K):
+    """tests/cache.rs:132-145, tests/runtime.rs:54-65"""
+    cache = K.KiviCache(K.KiviConfig.try_new(2, 16, 32), 1, 1, 16)
+    cache.append(np.zeros(0), np.zeros(0), 0)
+    assert cache.sequence_length() == 0
+    with pytest.raises(K.KiviError) as e:
+        cache.append(np.zeros(4), np.zeros(16), 1)
+    assert (e.value.variant, e.value.a, e.value.b) == ("Shape", 16, 4)
+    assert cache.sequence_length() == 0
+    with pytest.raises(K.KiviError) as e:
+        cache.append(np.zeros(16), np.zeros(4), 1)
+    assert (e.value.variant, e.value.a, e.value.b) == ("Shape", 16, 4)
+    rt = K.RuntimeKv.try_new(K.KiviConfig.try_new(2, 32, 32), 1, 1, 32)
+    with pytest.raises(K.KiviError) as e:
+        rt.prefill(np.zeros(8), np.zeros(32), 1)
+    assert (e.value.variant, e.value.a, e.value.b) == ("Shape", 32, 8)
+
+
+def test_long_sequence_beats_fp16_footprint(K):
+    """tests/cache.rs:196-207"""
+    cache = K.KiviCache(K.KiviConfig.try_new(2, 32, 64), 1, 2, 64)
+    n = 2 * 512 * 64
+    cache.append(fill(n, 11), fill(n, 13), 512)
+    r = cache.memory()
+    assert r.compression_ratio_vs_fp16() > 2.0 and r.compressed_bytes() < r.fp16_baseline_bytes
+    assert r.key_residual_bytes == 0
+
+
+# ---------------------------------------------------------------- attention
+
+
+@pytest.mark.parametrize("bits,group,residual,dim,seq", [
+    (2, 16, 32, 16, 40), (4, 32, 64, 32, 70),      # tests/attention.rs:61-65
+    (2, 32, 64, 64, 100),                           # tests/attention.rs:67-70
+    (2, 32, 128, 128, 4097), (4, 32, 128, 128, 3000), (8, 16, 32, 48, 333),
+    (2, 32, 128, 96, 129), (2, 16, 32, 32, 1), (4, 8, 16, 24, 77),
+])
+def test_attention_matches_oracle(K, bits, group, residual, dim, seq):
+    g, o = pair(K, bits, group, residual, 1, 1, dim)
+    keys, values, _ = synthetic_kv(seq + dim, 1, 1, seq, dim)
+    append_both(g, o, keys, values, seq)
+    q = fill(dim, 23)
+    scale = float(np.float32(1.0) / np.sqrt(np.float32(dim)))
+    got = g.attention(q, 1, scale)
+    assert_attention_close(got, o.attention(q, 1, scale))
+    k_hat, v_hat = o.dequantize()
+    assert max_abs(got, dense_attend(k_hat, v_hat, q, 1, 1, 1, seq, dim, scale)) < 1e-4
+
+
+@pytest.mark.parametrize("batch,kv,qh", [(2, 2, 4), (1, 8, 8), (3, 2, 6), (2, 1, 8), (1, 4, 32)])
+def test_gqa_attention_matches_oracle(K, batch, kv, qh):
+    """tests/attention.rs:72-101 (kv head = qh / group) at several group sizes."""
+    dim, seq = 128, 1000
+    g, o = pair(K, 2, 32, 128, batch, kv, dim)
+    keys, values, _ = synthetic_kv(batch * 10 + qh, batch, kv, seq, dim)
+    append_both(g, o, keys, values, seq)
+    q = np.random.default_rng(qh).standard_normal(batch * qh * dim, dtype=np.float32)
+    scale = float(np.float32(1.0) / np.sqrt(np.float32(dim)))
+    assert_attention_close(g.attention(q, qh, scale), o.attention(q, qh, scale))
+
+
+def test_empty_cache_and_bad_heads(K):
+    """tests/attention.rs:103-114"""
+    cache = K.KiviCache(K.KiviConfig(), 1, 2, 128)
+    assert (cache.attention(np.full(256, 0.2, np.float32), 2, 1.0) == 0).all()
+    c2 = K.KiviCache(K.KiviConfig.try_new(2, 16, 32), 1, 2, 16)
+    with pytest.raises(K.KiviError) as e:
+        c2.attention(np.zeros(48, np.float32), 3, 1.0)
+    assert (e.value.variant, e.value.a, e.value.b) == ("QueryHeads", 3, 2)
+    with pytest.raises(K.KiviError) as e:
+        c2.attention(np.zeros(8, np.float32), 2, 1.0)
+    assert (e.value.variant, e.value.a, e.value.b) == ("Shape", 32, 8)
+
+
+def test_attention_is_deterministic_and_cache_rebuild_is_bitwise(K):
+    """tests/cache.rs:160-194 on the device."""
+    cfg = K.KiviConfig.try_new(2, 32, 32)
+    keys, values = fill(64 * 32, 4), fill(64 * 32, 5)
+    keys[3:6] = [0.5, 1.5, 2.5]
+    qa, qb = fill(32, 8), fill(32, 9)
+    first, second = K.KiviCache(cfg, 1, 1, 32), K.KiviCache(cfg, 1, 1, 32)
+    first.append(keys, values, 64)
+    second.append(keys, values, 64)
+    a, b = first.attention(qa, 1, 0.25), first.attention(qb, 1, 0.25)
+    assert (a == second.attention(qa, 1, 0.25)).all()
+    assert (b == second.attention(qb, 1, 0.25)).all()
+    assert (a == first.attention(qa, 1, 0.25)).all()
+    assert not (a == b).all()
+
+
+def test_runtime_decode_matches_direct_cache(K):
+    """tests/runtime.rs:13-52: RuntimeKv::decode == append + attention, bitwise."""
+    cfg = K.KiviConfig.try_new(2, 32, 32)
+    batch, kv, qh, dim, prompt = 1, 2, 4, 32, 40
+    scale = float(np.float32(1.0) / np.sqrt(np.float32(dim)))
+    keys, values = fill(batch * kv * prompt * dim, 3), fill(batch * kv * prompt * dim, 4)
+    rt = K.RuntimeKv.try_new(cfg, batch, kv, dim)
+    cache = K.KiviCache(cfg, batch, kv, dim)
+    ocache = O.KiviCache(O.KiviConfig.try_new(2, 32, 32), batch, kv, dim)
+    rt.prefill(keys, values, prompt)
+    cache.append(keys, values, prompt)
+    ocache.append(keys, values, prompt)
+    prev = None
+    for step in range(3):
+        k, v = fill(batch * kv * dim, 10 + step), fill(batch * kv * dim, 20 + step)
+        q = fill(batch * qh * dim, 30 + step)
+        got = rt.decode(k, v, q, qh, scale)
+        cache.append(k, v, 1)
+        ocache.append(k, v, 1)
+        assert (got == cache.attention(q, qh, scale)).all()
+        assert_attention_close(got, ocache.attention(q, qh, scale))
+        if prev is not None:
+            assert not (got == prev).all()
+        prev = got
+    assert rt.cache().sequence_length() == prompt + 3
+    assert rt.cache().memory().compressed_bytes() == cache.memory().compressed_bytes()
+
+
+def test_decode_steps_track_oracle_through_flushes(K):
+    """Config-0-shaped decode loop (append 1 + attend) across key flushes and
+    value evictions; store bitwise and outputs within tolerance every step."""
+    batch, kv, qh, dim, prompt = 1, 8, 8, 128, 250
+    g, o = pair(K, 2, 32, 128, batch, kv, dim)
+    keys, values, _ = synthetic_kv(0, batch, kv, prompt + 140, dim)
+    append_both(g, o, slice_tokens(keys, batch, kv, prompt + 140, dim, 0, prompt),
+                slice_tokens(values, batch, kv, prompt + 140, dim, 0, prompt), prompt)
+    rng = np.random.default_rng(5)
+    scale = float(np.float32(1.0) / np.sqrt(np.float32(dim)))
+    for t in range(prompt, prompt + 140):
+        k = slice_tokens(keys, batch, kv, prompt + 140, dim, t, 1)
+        v = slice_tokens(values, batch, kv, prompt + 140, dim, t, 1)
+        append_both(g, o, k, v, 1)
+        q = rng.standard_normal(batch * qh * dim, dtype=np.float32)
+        assert_attention_close(g.attention(q, qh, scale), o.attention(q, qh, scale))
+    assert_store_equal(g, o)
+
+
+# ---------------------------------------------------------------- prefix / RAG
+
+
+def _share(K, cfg, batch, heads, dim, seq):
+    keys, values = document(batch, heads, seq, dim)
+    cache = K.KiviCache(cfg, batch, heads, dim)
+    cache.append(keys, values, seq)
+    return cache, cache.share_prefix()
+
+
+def test_sessions_share_one_prefix_allocation(K):
+    """tests/prefix.rs:97-110"""
+    cache, prefix = _share(K, K.KiviConfig.try_new(2, 32, 64), 1, 2, 64, 160)
+    again = prefix.clone()
+    assert prefix.shares_allocation_with(again) and prefix.prefix_tokens() == 160
+    a, b = prefix.session(), prefix.session()
+    assert a.prefix().shares_allocation_with(b.prefix())
+    assert a.prefix().prefix_bytes() == prefix.prefix_bytes() == cache.memory().compressed_bytes()
+    other = cache.share_prefix()
+    assert not other.shares_allocation_with(prefix)
+
+
+def test_empty_question_matches_cache_attention_bitwise(K):
+    """tests/prefix.rs:112-124"""
+    for seq in (96, 300, 4097):
+        cache, prefix = _share(K, K.KiviConfig.try_new(2, 32, 64), 1, 2, 64, seq)
+        q = np.full(4 * 64, 0.3, np.float32)
+        scale = 1.0 / 8.0
+        assert (prefix.session().attention(q, 4, scale) == cache.attention(q, 4, scale)).all()
+
+
+def test_question_attention_matches_dense_and_oracle(K):
+    """tests/prefix.rs:126-160, 275-307, 309-340"""
+    for bits, group, residual, batch, kv, qh, dim, doc, qlen, scale in [
+        (2, 32, 64, 1, 2, 2, 64, 96, 4, 0.25),
+        (4, 32, 64, 1, 1, 1, 64, 90, 6, 0.125),
+        (2, 32, 32, 2, 2, 6, 32, 48, 3, 0.5),
+        (2, 32, 128, 1, 8, 32, 128, 5000, 64, 1.0 / np.sqrt(128.0)),
+    ]:
+        cfg = K.KiviConfig.try_new(bits, group, residual)
+        cache, prefix = _share(K, cfg, batch, kv, dim, doc)
+        ocache = O.KiviCache(O.KiviConfig.try_new(bits, group, residual), batch, kv, dim)
+        ocache.append(*document(batch, kv, doc, dim), doc)
+        dk, dv = ocache.dequantize()
+        s = prefix.session()
+        os_ = ocache.share_prefix().session()
+        qk, qv = document(batch, kv, qlen, dim)
+        s.append(qk, qv, qlen)
+        os_.append(qk, qv, qlen)
+        q = document(batch, qh, 1, dim)[0]
+        got = s.attention(q, qh, scale)
+        expect = dense_attend(concat_head_major(dk, qk, batch, kv, doc, qlen, dim),
+                              concat_head_major(dv, qv, batch, kv, doc, qlen, dim),
+                              q, batch, kv, qh, doc + qlen, dim, scale)
+        assert max_abs(got, expect) < 1e-4
+        assert_attention_close(got, os_.attention(q, qh, scale))
+
+
+def test_one_session_does_not_see_another_question(K):
+    """tests/prefix.rs:162-181"""
+    cache, prefix = _share(K, K.KiviConfig.try_new(2, 32, 64), 1, 1, 64, 80)
+    a, b = prefix.session(), prefix.session()
+    ak, av = document(1, 1, 3, 64)
+    a.append(ak, av, 3)
+    assert b.question_tokens() == 0 and b.sequence_length() == 80
+    q = np.full(64, 0.2, np.float32)
+    only = prefix.session().attention(q, 1, 1.0)
+    assert (only == b.attention(q, 1, 1.0)).all()
+    assert not (a.attention(q, 1, 1.0) == b.attention(q, 1, 1.0)).all()
+
+
+def test_footprint_matches_the_byte_formula(K):
+    """tests/prefix.rs:183-199, 403-439"""
+    batch, heads, dim, doc, sessions, question = 2, 2, 32, 70, 3, 5
+    cache, prefix = _share(K, K.KiviConfig.try_new(2, 32, 64), batch, heads, dim, doc)
+    foot = prefix.footprint(sessions, question)
+    elements = batch * heads * dim
+    fp16_per_user = 2 * (doc + question) * elements * 2
+    assert foot.prefix_tokens == doc and foot.question_tokens == question
+    assert foot.sessions == sessions
+    assert foot.prefix_bytes == cache.memory().compressed_bytes()
+    assert foot.question_bytes == sessions * question * elements * 2 * 4
+    assert foot.shared_total_bytes == foot.prefix_bytes + foot.question_bytes
+    assert foot.fp16_per_user_bytes == fp16_per_user
+    assert foot.fp16_all_users_bytes == sessions * fp16_per_user
+    assert abs(foot.savings_vs_fp16() - foot.fp16_all_users_bytes / foot.shared_total_bytes) < 1e-12
+    empty = K.KiviCache(K.KiviConfig.try_new(2, 32, 64), 1, 1, 64).share_prefix().footprint(4, 0)
+    assert empty.prefix_bytes == 0 and empty.shared_total_bytes == 0 and empty.savings_vs_fp16() == 1.0
+
+
+def test_constant_keys_make_suffix_attention_the_value_mean(K):
+    """tests/prefix.rs:243-273"""
+    batch, heads, dim, doc, qlen = 1, 2, 32, 96, 4
+    cfg = K.KiviConfig.try_new(2, 32, 64)
+    values = document(batch, heads, doc, dim)[1]
+    cache = K.KiviCache(cfg, batch, heads, dim)
+    cache.append(np.zeros(batch * heads * doc * dim, np.float32), values, doc)
+    assert cache.key_residual_len() == doc % 64 and cache.value_residual_len() == 64
+    s = cache.share_prefix().session()
+    qv = document(batch, heads, qlen, dim)[1]
+    s.append(np.zeros(batch * heads * qlen * dim, np.float32), qv, qlen)
+    dk, dv = cache.dequantize()
+    assert (dk == 0).all()
+    expect = token_mean(concat_head_major(dv, qv, batch, heads, doc, qlen, dim), batch, heads,
+                        doc + qlen, dim)
+    assert max_abs(s.attention(np.ones(batch * heads * dim, np.float32), heads, 3.5), expect) < 1e-5
+
+
+def test_chunked_question_append_matches_one_shot(K):
+    """tests/prefix.rs:342-366 (bitwise)"""
+    batch, heads, dim, doc = 2, 2, 32, 40
+    _, prefix = _share(K, K.KiviConfig.try_new(2, 32, 32), batch, heads, dim, doc)
+    qk, qv = document(batch, heads, 7, dim)
+    chunked = prefix.session()
+    chunked.append(slice_tokens(qk, batch, heads, 7, dim, 0, 2), slice_tokens(qv, batch, heads, 7, dim, 0, 2), 2)
+    chunked.append(slice_tokens(qk, batch, heads, 7, dim, 2, 5), slice_tokens(qv, batch, heads, 7, dim, 2, 5), 5)
+    once = prefix.session()
+    once.append(qk, qv, 7)
+    assert chunked.question_tokens() == 7 and chunked.sequence_length() == doc + 7
+    q = np.full(batch * heads * dim, 0.4, np.float32)
+    assert (chunked.attention(q, heads, 1.25) == once.attention(q, heads, 1.25)).all()
+
+
+def test_suffix_dominates_and_question_only_session(K):
+    """tests/prefix.rs:368-401"""
+    dim = 32
+    cache = K.KiviCache(K.KiviConfig.try_new(2, 32, 32), 1, 1, dim)
+    cache.append(np.full(40 * dim, 0.01, np.float32), np.zeros(40 * dim, np.float32), 40)
+    s = cache.share_prefix().session()
+    s.append(np.ones(dim, np.float32), np.full(dim, 5.0, np.float32), 1)
+    assert max_abs(s.attention(np.ones(dim, np.float32), 1, 20.0), np.full(dim, 5.0)) < 1e-3
+    empty = K.KiviCache(K.KiviConfig.try_new(2, 32, 64), 1, 2, 64)
+    prefix = empty.share_prefix()
+    s = prefix.session()
+    qk, qv = document(1, 2, 5, 64)
+    s.append(qk, qv, 5)
+    q = np.full(2 * 64, 0.2, np.float32)
+    assert max_abs(s.attention(q, 2, 0.7), dense_attend(qk, qv, q, 1, 2, 2, 5, 64, 0.7)) < 1e-5
+    assert prefix.prefix_tokens() == 0 and prefix.prefix_bytes() == 0
+
+
+def test_appending_a_question_leaves_the_prefix_unchanged(K):
+    """tests/prefix.rs:441-457"""
+    cache, prefix = _share(K, K.KiviConfig.try_new(2, 32, 64), 1, 1, 64, 80)
+    before_tokens, before_bytes = prefix.prefix_tokens(), prefix.prefix_bytes()
+    q = np.full(64, 0.25, np.float32)
+    before = prefix.session().attention(q, 1, 1.0)
+    s = prefix.session()
+    s.append(*document(1, 1, 4, 64), 4)
+    s.append(np.zeros(0), np.zeros(0), 0)
+    assert prefix.prefix_tokens() == before_tokens and prefix.prefix_bytes() == before_bytes
+    assert cache.sequence_length() == before_tokens
+    assert (before == prefix.session().attention(q, 1, 1.0)).all()
+    # mutating the source cache after share_prefix leaves the frozen copy alone
+    cache.append(*document(1, 1, 50, 64), 50)
+    assert (before == prefix.session().attention(q, 1, 1.0)).all()
+
+
+def test_session_errors(K):
+    """tests/prefix.rs:201-217, 459-479"""
+    _, prefix = _share(K, K.KiviConfig.try_new(2, 32, 64), 1, 1, 64, 1)
+    s = prefix.session()
+    with pytest.raises(K.KiviError) as e:
+        s.append(np.zeros(8), np.zeros(8), 1)
+    assert e.value.variant == "Shape"
+    with pytest.raises(K.KiviError) as e:
+        s.append(np.zeros(64), np.zeros(8), 1)
+    assert (e.value.variant, e.value.a, e.value.b) == ("Shape", 64, 8)
+    _, prefix = _share(K, K.KiviConfig.try_new(2, 32, 64), 1, 2, 64, 32)
+    s = prefix.session()
+    with pytest.raises(K.KiviError) as e:
+        s.attention(np.zeros(64), 3, 1.0)
+    assert (e.value.variant, e.value.a, e.value.b) == ("QueryHeads", 3, 2)
+    with pytest.raises(K.KiviError) as e:
+        s.attention(np.zeros(8), 2, 1.0)
+    assert (e.value.variant, e.value.a, e.value.b) == ("Shape", 128, 8)
+
+
+def test_batched_sessions_equal_individual_sessions_bitwise(K):
+    """One pass over the prefix for all sessions == each RagSession::attention."""
+    cfg = K.KiviConfig()
+    kv, qh, dim, doc = 4, 16, 128, 3000
+    keys, values, _ = synthetic_kv(3, 1, kv, doc, dim)
+    cache = K.KiviCache(cfg, 1, kv, dim)
+    cache.append(keys, values, doc)
+    prefix = cache.share_prefix()
+    rng = np.random.default_rng(1)
+    sessions = []
+    for i in range(5):
+        s = prefix.session()
+        ln = [0, 1, 17, 64, 3][i]
+        if ln:
+            s.append(rng.standard_normal(kv * ln * dim, dtype=np.float32),
+                     rng.standard_normal(kv * ln * dim, dtype=np.float32), ln)
+        sessions.append(s)
+    q = rng.standard_normal((5, 1, qh, dim), dtype=np.float32)
+    scale = 1.0 / np.sqrt(128.0)
+    batched = K.sessions_attention_batched(sessions, q, qh, scale).reshape(5, -1)
+    for i, s in enumerate(sessions):
+        assert (batched[i] == s.attention(q[i].reshape(-1), qh, scale)).all(), i
+
+
+# ---------------------------------------------------------------- sequence sharding
+
+
+def test_sequence_sharded_partials_merge_to_full_attention(K):
+    """Shards of R-aligned token ranges, interior shards sealed; the LSE merge of
+    the shards' partial states equals single-cache attention within tolerance."""
+    torch = pytest.importorskip("torch")
+    cfg = K.KiviConfig()
+    kv, qh, dim, total, shards = 8, 32, 128, 4 * 1024 + 77, 4
+    keys, values, _ = synthetic_kv(11, 1, kv, total, dim)
+    full = O.KiviCache(O.KiviConfig(), 1, kv, dim)
+    full.append(keys, values, total)
+    bounds = [0, 1024, 2048, 3072, total]
+    q = np.random.default_rng(2).standard_normal(qh * dim, dtype=np.float32)
+    dq = torch.from_numpy(q).cuda()
+    rows = qh
+    m = torch.empty(shards, rows, device="cuda")
+    l = torch.empty(shards, rows, device="cuda")
+    o = torch.empty(shards, rows, dim, device="cuda")
+    caches = []
+    for r in range(shards):
+        n = bounds[r + 1] - bounds[r]
+        c = K.KiviCache(cfg, 1, kv, dim)
+        c.append(slice_tokens(keys, 1, kv, total, dim, bounds[r], n),
+                 slice_tokens(values, 1, kv, total, dim, bounds[r], n), n)
+        if r < shards - 1:
+            c.seal()
+            assert c.quantized_value_tokens() == n and c.value_residual_len() == 0
+        caches.append(c)
+        c.attention_partial_dev(dq, qh, 1.0 / np.sqrt(128.0), m[r], l[r], o[r])
+    out = torch.empty(rows, dim, device="cuda")
+    K.merge_partials_dev(shards, rows, dim, m, l, o, out)
+    torch.cuda.synchronize()
+    assert_attention_close(out.cpu().numpy().reshape(-1), full.attention(q, qh, 1.0 / np.sqrt(128.0)))
