@@ -134,6 +134,13 @@ int32_t kivi_abi_version(void);
 const char *kivi_status_string(int32_t code);
 /* Number of this library's kernels launched so far in this process. */
 uint64_t kivi_kernel_launches(void);
+/* Per-kernel device timing (no counterpart in the reference): while enabled,
+ * every launch is bracketed by a CUDA event pair on its stream.
+ * kivi_profile_read waits for the recorded events and returns the launch count
+ * and summed duration of `kernel` (NULL = all kernels).  Off by default. */
+void kivi_profile_enable(int32_t on);
+int32_t kivi_profile_read(const char *kernel, uint64_t *launches, double *total_ms);
+void kivi_profile_reset(void);
 
 /* ---------------------------------------------------------------- config.rs */
 

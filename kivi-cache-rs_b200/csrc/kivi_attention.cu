@@ -289,6 +289,7 @@ cudaError_t launch_attention_chunks(const AttnArgs &a, cudaStream_t s) {
         configured[dev] = true;
     }
     dim3 grid((unsigned)(a.NC + 1 + a.S), (unsigned)(a.B * a.H));
+    ProfScope prof("attn_chunk", s);
     attn_chunk_kernel<<<grid, kThreads, smem, s>>>(a);
     count_launch();
     return cudaGetLastError();
@@ -298,6 +299,7 @@ cudaError_t launch_merge(const float *part_ml, const float *part_o, int64_t rows
                          int /*ml_stride_pairs*/, float *out, float *out_m, float *out_l, int mode,
                          cudaStream_t s) {
     if (rows <= 0) return cudaSuccess;
+    ProfScope prof("merge", s);
     merge_kernel<<<(unsigned)rows, 128, sizeof(float) * parts, s>>>(part_ml, part_o, parts, D, out,
                                                                     out_m, out_l, mode);
     count_launch();
@@ -307,6 +309,7 @@ cudaError_t launch_merge(const float *part_ml, const float *part_o, int64_t rows
 cudaError_t launch_merge_shards(const float *m, const float *l, const float *o, int64_t parts,
                                 int64_t rows, int D, float *out, cudaStream_t s) {
     if (rows <= 0) return cudaSuccess;
+    ProfScope prof("merge_shards", s);
     merge_shards_kernel<<<(unsigned)rows, 128, sizeof(float) * parts, s>>>(m, l, o, (int)parts,
                                                                            rows, D, out);
     count_launch();

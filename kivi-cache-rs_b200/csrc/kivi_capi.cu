@@ -12,6 +12,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <string>
 #include <vector>
 
 #include "../../include/kivi_gpu.h"
@@ -22,6 +23,68 @@ namespace kivi {
 static std::atomic<uint64_t> g_launches{0};
 void count_launch(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
 uint64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
+
+namespace {
+struct ProfRecord {
+    const char *name;
+    cudaEvent_t start, stop;
+};
+std::atomic<bool> g_prof_on{false};
+std::mutex g_prof_mu;
+std::vector<ProfRecord> g_prof_pending;
+struct ProfTotal {
+    std::string name;
+    uint64_t launches = 0;
+    double ms = 0.0;
+};
+std::vector<ProfTotal> g_prof_totals;
+
+void prof_drain_locked() {
+    for (ProfRecord &r : g_prof_pending) {
+        float ms = 0.0f;
+        if (cudaEventSynchronize(r.stop) == cudaSuccess &&
+            cudaEventElapsedTime(&ms, r.start, r.stop) == cudaSuccess) {
+            ProfTotal *t = nullptr;
+            for (ProfTotal &x : g_prof_totals)
+                if (x.name == r.name) t = &x;
+            if (!t) {
+                g_prof_totals.push_back(ProfTotal{r.name, 0, 0.0});
+                t = &g_prof_totals.back();
+            }
+            t->launches += 1;
+            t->ms += ms;
+        }
+        cudaEventDestroy(r.start);
+        cudaEventDestroy(r.stop);
+    }
+    g_prof_pending.clear();
+}
+} // namespace
+
+bool profiling_enabled() { return g_prof_on.load(std::memory_order_relaxed); }
+
+ProfScope::ProfScope(const char *kernel, cudaStream_t s) : name(kernel), stream(s) {
+    if (!profiling_enabled()) return;
+    ProfRecord *r = new ProfRecord{kernel, nullptr, nullptr};
+    if (cudaEventCreate(&r->start) != cudaSuccess || cudaEventCreate(&r->stop) != cudaSuccess ||
+        cudaEventRecord(r->start, s) != cudaSuccess) {
+        if (r->start) cudaEventDestroy(r->start);
+        if (r->stop) cudaEventDestroy(r->stop);
+        delete r;
+        cudaGetLastError();
+        return;
+    }
+    rec = r;
+}
+
+ProfScope::~ProfScope() {
+    if (!rec) return;
+    ProfRecord *r = (ProfRecord *)rec;
+    cudaEventRecord(r->stop, stream);
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    g_prof_pending.push_back(*r);
+    delete r;
+}
 
 } // namespace kivi
 
@@ -519,6 +582,29 @@ const char *kivi_status_string(int32_t code) {
 }
 
 uint64_t kivi_kernel_launches(void) { return kivi::launch_count(); }
+
+void kivi_profile_enable(int32_t on) { kivi::g_prof_on.store(on != 0); }
+
+int32_t kivi_profile_read(const char *kernel, uint64_t *launches, double *total_ms) {
+    std::lock_guard<std::mutex> lk(kivi::g_prof_mu);
+    kivi::prof_drain_locked();
+    uint64_t n = 0;
+    double ms = 0.0;
+    for (const auto &t : kivi::g_prof_totals)
+        if (!kernel || t.name == kernel) {
+            n += t.launches;
+            ms += t.ms;
+        }
+    if (launches) *launches = n;
+    if (total_ms) *total_ms = ms;
+    return KIVI_OK;
+}
+
+void kivi_profile_reset(void) {
+    std::lock_guard<std::mutex> lk(kivi::g_prof_mu);
+    kivi::prof_drain_locked();
+    kivi::g_prof_totals.clear();
+}
 
 int32_t kivi_config_default(kivi_config *out) {
     if (!out) return KIVI_ERR_INVALID_ARGUMENT;

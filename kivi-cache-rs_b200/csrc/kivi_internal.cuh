@@ -96,6 +96,18 @@ struct AttnArgs {
 void count_launch(int n = 1);
 uint64_t launch_count();
 
+// Optional per-kernel device timing: while profiling is enabled, a ProfScope
+// records a CUDA event pair around one launch on its stream; the host reads
+// the accumulated durations through kivi_profile_read (include/kivi_gpu.h).
+bool profiling_enabled();
+struct ProfScope {
+    const char *name;
+    cudaStream_t stream;
+    void *rec = nullptr;
+    ProfScope(const char *kernel, cudaStream_t s);
+    ~ProfScope();
+};
+
 // ---------------------------------------------------------------- quantize
 // Decode-path append (seq < R): key residual copy (+ flush when it fills) and
 // value window eviction/insert for every stream, one CTA per stream.

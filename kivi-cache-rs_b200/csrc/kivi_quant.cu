@@ -260,6 +260,7 @@ cudaError_t launch_append_small(const Geom &g, const Store &st, int n, const flo
                                 const float *values, int seq, int kres_len, int64_t kq,
                                 int vres_len, int64_t vq, int vhead, cudaStream_t s) {
     if (n <= 0 || seq <= 0) return cudaSuccess;
+    ProfScope prof("append_small", s);
     append_small_kernel<<<n, 256, 0, s>>>(g, st, keys, values, seq, kres_len, kq, vres_len, vq,
                                           vhead);
     count_launch();
@@ -270,6 +271,7 @@ cudaError_t launch_key_groups(const Geom &g, const Store &st, int n, const float
                               const float *in, int64_t in_seq, int64_t ngroups,
                               int64_t out_group0, cudaStream_t s) {
     if (n <= 0 || ngroups <= 0) return cudaSuccess;
+    ProfScope prof("key_groups", s);
     key_groups_kernel<<<dim3((unsigned)ngroups, n), 128, 0, s>>>(g, st, res, nres, in, in_seq,
                                                                    out_group0);
     count_launch();
@@ -280,6 +282,7 @@ cudaError_t launch_value_tokens(const Geom &g, const Store &st, int n, int nwin,
                                 const float *in, int64_t in_seq, int64_t in_off, int64_t ntok,
                                 int64_t out_tok0, cudaStream_t s) {
     if (n <= 0 || ntok <= 0) return cudaSuccess;
+    ProfScope prof("value_tokens", s);
     value_tokens_kernel<<<dim3(blocks_for(ntok * g.nch, 128), n), 128, 0, s>>>(
         g, st, nwin, vhead, in, in_seq, in_off, ntok, out_tok0);
     count_launch();
@@ -290,6 +293,7 @@ cudaError_t launch_copy_rows(float *dst, int64_t dst_stream_rows, int64_t dst_he
                              int64_t dst_off, int64_t ring, const float *src, int64_t src_seq,
                              int64_t src_off, int64_t count, int n, int D, cudaStream_t s) {
     if (n <= 0 || count <= 0) return cudaSuccess;
+    ProfScope prof("copy_rows", s);
     copy_rows_kernel<<<dim3(blocks_for(count * D, 256), n), 256, 0, s>>>(
         dst, dst_stream_rows, dst_head, dst_off, ring, src, src_seq, src_off, count, D);
     count_launch();
@@ -300,6 +304,7 @@ cudaError_t launch_dequant_cache(const Geom &g, const Store &st, int n, int64_t 
                                  int64_t vq, int vhead, float *keys, float *values,
                                  cudaStream_t s) {
     if (n <= 0 || seq <= 0) return cudaSuccess;
+    ProfScope prof("dequant_cache", s);
     dequant_cache_kernel<<<dim3(blocks_for(seq * g.D, 256), n), 256, 0, s>>>(g, st, seq, kq, vq,
                                                                              vhead, keys, values);
     count_launch();
@@ -326,6 +331,7 @@ cudaError_t launch_dequant_tensor(const Geom &g, int axis, int n, int64_t tokens
                                   const uint32_t *codes, const float2 *params, float *out,
                                   cudaStream_t s) {
     if (n <= 0 || tokens <= 0) return cudaSuccess;
+    ProfScope prof("dequant_tensor", s);
     dequant_tensor_kernel<<<dim3(blocks_for(tokens * g.D, 256), n), 256, 0, s>>>(
         g, axis, tokens, codes, params, out);
     count_launch();

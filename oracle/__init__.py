@@ -81,6 +81,7 @@ def lib():
         L.ko_cache_free.argtypes = [P]
         L.ko_cache_append.argtypes = [P, fp, sz, fp, sz, sz, e]
         L.ko_cache_attention.argtypes = [P, fp, sz, sz, C.c_float, fp, C.c_int, e]
+        L.ko_cache_attention_batch_range.argtypes = [P, fp, sz, C.c_float, fp, C.c_int, sz, sz]
         L.ko_cache_attention_f64.argtypes = [P, fp, sz, C.c_float, C.POINTER(C.c_double)]
         L.ko_cache_dequantize.argtypes = [P, fp, fp]
         L.ko_cache_memory.argtypes = [P, u64p]
@@ -186,6 +187,17 @@ class KiviCache:
             out.ctypes.data_as(C.POINTER(C.c_float)), threads, C.byref(err),
         )
         _check(rc, err)
+        return out
+
+    def attention_batch_range(self, query, num_q_heads, scale, b0, b1, threads=1):
+        """Attention rows of batch elements [b0, b1) (cache.rs:250-277 on a sample)."""
+        q, qp = _f32(query)
+        out = np.zeros((b1 - b0) * num_q_heads * self.head_dim, np.float32)
+        rc = lib().ko_cache_attention_batch_range(
+            self._h, qp, num_q_heads, C.c_float(scale), out.ctypes.data_as(C.POINTER(C.c_float)),
+            threads, b0, b1)
+        if rc:
+            raise OracleError(rc, 0, 0, None)
         return out
 
     def attention_f64(self, query, num_q_heads, scale):

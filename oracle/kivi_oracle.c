@@ -786,6 +786,27 @@ int ko_cache_attention(const ko_cache *c, const float *query, size_t query_len,
     return KO_OK;
 }
 
+/* Attention for batch elements [b0, b1) only (a bounded sample of
+ * cache.rs:250-277 for the timed CPU baseline); out holds rows of those
+ * batch elements: (b1 - b0) * num_q_heads * head_dim floats. */
+int ko_cache_attention_batch_range(const ko_cache *c, const float *query, size_t num_q_heads,
+                                   float scale, float *out, int threads, size_t b0, size_t b1) {
+    if (num_q_heads == 0 || num_q_heads % c->heads != 0 || b0 >= b1 || b1 > c->batch)
+        return KO_QUERY_HEADS;
+    size_t dim = c->head_dim;
+    memset(out, 0, (b1 - b0) * num_q_heads * dim * sizeof(float));
+    if (c->seq_len == 0) return KO_OK;
+    ko_cache sub = *c;
+    sub.batch = b1 - b0;
+    sub.key_streams = c->key_streams + b0 * c->heads;
+    sub.value_streams = c->value_streams + b0 * c->heads;
+    sub.key_residual = c->key_residual + b0 * c->heads * c->residual_length * dim;
+    sub.value_residual = c->value_residual + b0 * c->heads * c->residual_length * dim;
+    attention_pairs(&sub, NULL, NULL, 0, query + b0 * num_q_heads * dim, num_q_heads, scale, out,
+                    threads);
+    return KO_OK;
+}
+
 /* fp64 attention over the fp32-dequantized cache: logits, softmax and the
  * value mix in double.  Not a reference routine; used to attribute the
  * GPU-vs-reference difference to either side. */

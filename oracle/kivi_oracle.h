@@ -65,6 +65,9 @@ int ko_cache_append(ko_cache *c, const float *keys, size_t keys_len, const float
  * reference's own serial loop; results are bit-identical for any count). */
 int ko_cache_attention(const ko_cache *c, const float *query, size_t query_len,
                        size_t num_q_heads, float scale, float *out, int threads, ko_error *err);
+/* cache.rs:250-277 restricted to batch elements [b0, b1) (bounded CPU-baseline sample). */
+int ko_cache_attention_batch_range(const ko_cache *c, const float *query, size_t num_q_heads,
+                                   float scale, float *out, int threads, size_t b0, size_t b1);
 /* Same attention evaluated in fp64 over the fp32 dequantized cache (for error attribution). */
 int ko_cache_attention_f64(const ko_cache *c, const float *query, size_t num_q_heads,
                            float scale, double *out);
