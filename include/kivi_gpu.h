@@ -176,6 +176,24 @@ int32_t kivi_cache_attention_dev(const kivi_cache *cache, const float *d_query,
                                  uint64_t num_q_heads, float scale, float *d_out, void *stream,
                                  kivi_error *err);
 
+/* Allocation-free variant of kivi_cache_attention_dev.  No counterpart in the
+ * reference: it serves callers that cannot call cudaMalloc while decoding --
+ * serving engines that reserve nearly all device memory for their own pool at
+ * start-up, and decode loops that must not hit cudaMalloc/cudaFree, which can
+ * synchronise the device.  The attention's partial-softmax scratch comes from a
+ * fixed 16 MiB array in the library's device image (held by every GPU that
+ * loads the library until exit) instead of the handle's grown buffer; a call
+ * needing more than 16 MiB of scratch (batch*num_q_heads*(head_dim+2)*4 bytes
+ * per 256-token chunk, plus two chunks) fails with KIVI_ERR_UNSUPPORTED and a
+ * message giving both sizes.  The call allocates nothing.  Its first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress) with that
+ * device current; make that first call before any stream capture.  All calls
+ * share the one array: calls that overlap on the GPU (other streams, other
+ * handles on the same device) race, so order them on one stream. */
+int32_t kivi_cache_attention_noalloc_dev(const kivi_cache *cache, const float *d_query,
+                                         uint64_t num_q_heads, float scale, float *d_out,
+                                         void *stream, kivi_error *err);
+
 /* RuntimeKv::decode (runtime.rs:46-56): append one token, then attend. */
 int32_t kivi_cache_decode(kivi_cache *cache, const float *key, uint64_t key_len,
                           const float *value, uint64_t value_len, const float *query,

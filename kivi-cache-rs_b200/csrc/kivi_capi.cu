@@ -1470,3 +1470,109 @@ uint64_t kivi_marginal_bytes_per_layer(const kivi_config *c, uint64_t h, uint64_
 }
 
 } // extern "C"
+
+// ---------------------------------------------------------------- allocation-free attention
+//
+// kivi_cache_attention_noalloc_dev: the split-sequence attention of
+// kivi_cache_attention_dev with its partial-softmax scratch taken from a
+// fixed array that is part of this library's device image, so the call itself
+// allocates nothing.  It exists for callers that cannot call cudaMalloc at
+// decode time: serving engines that reserve nearly all device memory for their
+// own pool at start-up (a late cudaMalloc then fails), and latency-critical
+// decode loops that must not hit cudaMalloc/cudaFree, which can synchronise
+// the whole device.
+namespace {
+
+// Maximum scratch: 16 MiB of fp32 partial states.  Every GPU that loads this
+// library holds this array until the process exits.
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
+__device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+std::mutex g_noalloc_mu;
+constexpr int kNoAllocMaxDevices = 64;
+float *g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on `device` (which must be current).
+// In host code the symbol's name is only a host-side stand-in, never a device
+// address, so the address is looked up once per device and cached.
+int32_t noalloc_scratch(int device, float **out, kivi_error *err) {
+    if (device < 0 || device >= kNoAllocMaxDevices)
+        return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "device %d out of range", device);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[device]) {
+        void *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail(err, e, "noalloc scratch address");
+        g_noalloc_ptr[device] = (float *)p;
+    }
+    *out = g_noalloc_ptr[device];
+    return KIVI_OK;
+}
+
+} // namespace
+
+extern "C" int32_t kivi_cache_attention_noalloc_dev(const kivi_cache *h, const float *dq,
+                                                    uint64_t Hq, float scale, float *dout,
+                                                    void *stream, kivi_error *err) {
+    if (!h) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null cache");
+    int32_t rc = check_query(h->s, Hq, 0, false, err);
+    if (rc) return rc;
+    if (!dq || !dout) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null buffer");
+    const KvState &p = h->s;
+    DeviceGuard dg(p.device);
+    cudaStream_t st = (cudaStream_t)stream;
+    if (p.seq == 0) { // cache.rs:243-246: empty cache -> zeros
+        CUDA_TRY(cudaMemsetAsync(dout, 0, p.B * Hq * p.D * sizeof(float), st), "noalloc zeros");
+        CUDA_TRY(cudaEventRecord(h->dev_done, st), "noalloc attention");
+        return set_err(err, KIVI_OK);
+    }
+    const uint64_t Gq = Hq / p.H;
+    if ((int)Gq > kivi::attention_max_rows((int)p.D))
+        return set_msg(err, KIVI_ERR_UNSUPPORTED, "too many query heads per kv head");
+    // Same split plan as kivi_cache_attention_dev for one query set.
+    const uint64_t main_tokens = p.vq / p.cfg.group_size * p.cfg.group_size;
+    const int64_t NC = (int64_t)((main_tokens + kChunkTokens - 1) / kChunkTokens);
+    const int parts = (int)NC + 2;
+    const uint64_t rows = p.B * Hq;
+    const size_t ml_floats = rows * parts * 2;
+    const size_t need = (ml_floats + rows * parts * p.D) * sizeof(float);
+    if (need > kNoAllocScratchBytes)
+        return set_msg(err, KIVI_ERR_UNSUPPORTED,
+                       "attention needs %llu bytes of scratch; the allocation-free entry point "
+                       "has a static limit of %llu bytes",
+                       (unsigned long long)need, (unsigned long long)kNoAllocScratchBytes);
+    float *scratch = nullptr;
+    rc = noalloc_scratch(p.device, &scratch, err);
+    if (rc) return rc;
+    kivi::AttnArgs a{};
+    a.g = p.g;
+    a.st = p.st;
+    a.B = (int)p.B;
+    a.H = (int)p.H;
+    a.Hq = (int)Hq;
+    a.Gq = (int)Gq;
+    a.kq = (int64_t)p.kq;
+    a.vq = (int64_t)p.vq;
+    a.kres_len = (int)p.kres_len;
+    a.vres_len = (int)p.vres_len;
+    a.vhead = (int)p.vhead;
+    a.seq_p = (int64_t)p.seq;
+    a.main_tokens = (int64_t)main_tokens;
+    a.chunk_tokens = kChunkTokens;
+    a.NC = (int)NC;
+    a.parts = parts;
+    a.S = 1;
+    a.session_base = 0;
+    a.q = dq;
+    a.scale = scale;
+    // Every slot the merge reads is written by this call's chunk kernel first,
+    // so the shared array needs no clearing between calls.
+    a.part_ml = scratch;
+    a.part_o = scratch + ml_floats;
+    CUDA_TRY(kivi::launch_attention_chunks(a, st), "noalloc attention");
+    CUDA_TRY(kivi::launch_merge(a.part_ml, a.part_o, (int64_t)rows, parts, (int)p.D, 0, dout,
+                                nullptr, nullptr, 0, st),
+             "noalloc attention merge");
+    CUDA_TRY(cudaEventRecord(h->dev_done, st), "noalloc attention");
+    return set_err(err, KIVI_OK);
+}

@@ -118,6 +118,7 @@ def lib():
         "kivi_cache_append_dev": ([P, P, P, sz, P, e], i32),
         "kivi_cache_attention": ([P, fp, sz, sz, f32, fp, sz, e], i32),
         "kivi_cache_attention_dev": ([P, P, sz, f32, P, P, e], i32),
+        "kivi_cache_attention_noalloc_dev": ([P, P, sz, f32, P, P, e], i32),
         "kivi_cache_decode": ([P, fp, sz, fp, sz, fp, sz, sz, f32, fp, sz, e], i32),
         "kivi_cache_decode_dev": ([P, P, P, P, sz, f32, P, P, e], i32),
         "kivi_cache_attention_partial_dev": ([P, P, sz, f32, P, P, P, P, e], i32),
