@@ -165,6 +165,21 @@ def channel_scales(rng, H, D, outlier):
     return np.where(mask, np.float32(20.0), np.float32(1.0)).astype(np.float32)
 
 
+KERNELS = ("attn_tc", "attn_chunk", "merge", "append_small", "key_groups", "value_tokens",
+           "copy_rows")
+
+
+def main_region_bytes(cache, cfgd):
+    """Algorithmic bytes the tensor-core kernel reads per launch: every whole
+    32-token group whose keys and values are both packed (codes + (scale, zero)
+    of keys and values, budget.rs:337-342 per token) for every stream, plus the
+    query rows."""
+    B, H, Hq, D, bits, G = cfgd["B"], cfgd["H"], cfgd["Hq"], cfgd["D"], cfgd["bits"], cfgd["G"]
+    groups = cache.quantized_value_tokens() // G
+    per_group = D * G * bits // 8 + D * 8 + G * D * bits // 8 + G * (D // G) * 8
+    return B * H * groups * per_group + B * Hq * D * 4
+
+
 def step_bytes(K, cache, cfgd):
     """Algorithmic HBM bytes of one decode step on this rank: the packed cache
     and fp32 residual/window the attention reads (memory().compressed_bytes(),
@@ -237,7 +252,7 @@ def run_gpu(args, cfgd, rank, world, local_rank):
     stream.synchronize()
 
     bytes_step0, attn_bytes0 = step_bytes(K, cache, cfgd)
-    kernel = "attn_chunk"
+    main_bytes0 = main_region_bytes(cache, cfgd)
     K.lib().kivi_profile_reset()
     launches0 = K.kernel_launches()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -258,13 +273,22 @@ def run_gpu(args, cfgd, rank, world, local_rank):
     launches = K.kernel_launches() - launches0
     t_ms = ev0.elapsed_time(ev1)
     bytes_step1, attn_bytes1 = step_bytes(K, cache, cfgd)
+    main_bytes1 = main_region_bytes(cache, cfgd)
     import ctypes as C
 
-    nl, ms = C.c_uint64(), C.c_double()
-    K.lib().kivi_profile_read(kernel.encode(), C.byref(nl), C.byref(ms))
+    kernels = {}
+    for name in KERNELS:
+        nl_, ms_ = C.c_uint64(), C.c_double()
+        K.lib().kivi_profile_read(name.encode(), C.byref(nl_), C.byref(ms_))
+        if nl_.value:
+            kernels[name] = {"launches": int(nl_.value), "total_ms": ms_.value,
+                             "avg_ms": ms_.value / nl_.value}
     n_all, ms_all = C.c_uint64(), C.c_double()
     K.lib().kivi_profile_read(None, C.byref(n_all), C.byref(ms_all))
-    kern_avg_ms = ms.value / max(1, nl.value)
+    kernel = max(kernels, key=lambda k: kernels[k]["total_ms"])
+    nl = C.c_uint64(kernels[kernel]["launches"])
+    ms = C.c_double(kernels[kernel]["total_ms"])
+    kern_avg_ms = kernels[kernel]["avg_ms"]
 
     # e2e: the public host API (RuntimeKv::decode) with pinned host buffers,
     # H2D of K/V/Q and D2H of the output inside every step
@@ -308,7 +332,8 @@ def run_gpu(args, cfgd, rank, world, local_rank):
     avg_step_bytes = 0.5 * (bytes_step0 + bytes_step1)
     hbm_gbs = world * avg_step_bytes * S / (t_ms / 1e3) / 1e9
     attn_bytes = 0.5 * (attn_bytes0 + attn_bytes1)
-    achieved = attn_bytes / (kern_avg_ms / 1e3) / 1e9 if kern_avg_ms > 0 else None
+    kern_bytes = attn_bytes if kernel == "attn_chunk" else 0.5 * (main_bytes0 + main_bytes1)
+    achieved = kern_bytes / (kern_avg_ms / 1e3) / 1e9 if kern_avg_ms > 0 else None
     workload = cfgd["name"]
     result = {
         "metric": METRIC,
@@ -337,9 +362,10 @@ def run_gpu(args, cfgd, rank, world, local_rank):
             "peak_kind": peak_kind, "unit": "GB/s",
             "frac": (achieved / peak) if achieved else None,
             "traffic": load_traffic(kernel, workload),
-            "algorithmic_bytes_per_launch": attn_bytes,
+            "algorithmic_bytes_per_launch": kern_bytes,
             "avg_launch_ms": kern_avg_ms, "launches": int(nl.value),
             "share_of_timed_kernels": ms.value / ms_all.value if ms_all.value else None,
+            "kernels": kernels,
         },
         "e2e": {
             "value": world * E / e2e_s, "unit": "steps/s",

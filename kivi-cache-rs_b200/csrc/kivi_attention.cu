@@ -6,7 +6,8 @@
 //     row that reads this stream -- all GQA heads of the kv head and, for RAG,
 //     all sessions -- so the packed prefix is read from HBM once per launch;
 //   * prefix tail: tokens [main_tokens, seq_p) (partial group, fp32 value
-//     window, fp32 key residual), one CTA per stream, all sessions;
+//     window, fp32 key residual), one CTA per 32-token tile and stream, all
+//     sessions;
 //   * suffix: one CTA per (session, stream) over the session's fp32 question.
 // Each CTA writes a partial softmax state (m, l, o) per query row; a merge
 // kernel combines the slots in token order (main chunks, prefix tail,
@@ -84,11 +85,12 @@ __global__ void __launch_bounds__(kThreads) attn_chunk_kernel(const AttnArgs a) 
     extern __shared__ float sm[];
     const Geom &g = a.g;
     const int D = g.D, DP = D + 1;
-    const int c = blockIdx.x;
+    const int c = blockIdx.x + a.c0;
     const int s = blockIdx.y; // stream = b * H + kvh
     const int b = s / a.H, kvh = s - b * a.H;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
+    const int ntt = a.NTT > 0 ? a.NTT : 1;
     int slot, sess0, nsess;
     int64_t lo, hi;
     const SuffixRef *suf = nullptr;
@@ -98,15 +100,20 @@ __global__ void __launch_bounds__(kThreads) attn_chunk_kernel(const AttnArgs a) 
         nsess = a.S;
         lo = (int64_t)c * a.chunk_tokens;
         hi = min(lo + a.chunk_tokens, a.main_tokens);
-    } else if (c == a.NC) {
-        slot = a.NC;
+    } else if (c < a.NC + ntt) {
+        slot = c;
         sess0 = 0;
         nsess = a.S;
-        lo = a.main_tokens;
-        hi = a.seq_p;
+        if (a.NTT > 0) {
+            lo = min(a.main_tokens + (int64_t)(c - a.NC) * a.tail_tile, a.seq_p);
+            hi = min(lo + a.tail_tile, a.seq_p);
+        } else {
+            lo = a.main_tokens;
+            hi = a.seq_p;
+        }
     } else {
-        slot = a.NC + 1;
-        sess0 = c - a.NC - 1;
+        slot = a.NC + ntt;
+        sess0 = c - a.NC - ntt;
         nsess = 1;
         suf = &a.suf[sess0];
         lo = a.seq_p;
@@ -288,7 +295,8 @@ cudaError_t launch_attention_chunks(const AttnArgs &a, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         configured[dev] = true;
     }
-    dim3 grid((unsigned)(a.NC + 1 + a.S), (unsigned)(a.B * a.H));
+    const int ntt = a.NTT > 0 ? a.NTT : 1;
+    dim3 grid((unsigned)(a.NC + ntt + a.S - a.c0), (unsigned)(a.B * a.H));
     ProfScope prof("attn_chunk", s);
     attn_chunk_kernel<<<grid, kThreads, smem, s>>>(a);
     count_launch();

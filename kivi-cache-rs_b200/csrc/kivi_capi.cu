@@ -6,6 +6,7 @@
 // cache.rs:382-484, with the value window kept as a ring instead of being
 // shifted (cache.rs:559-578).  All tensor work happens in kernels on the
 // handle's device.
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdarg>
@@ -409,7 +410,9 @@ int32_t append_device(KvState &s, const float *dk, const float *dv, uint64_t seq
 
 // ---------------------------------------------------------------- attention plan
 
-constexpr int64_t kChunkTokens = 256;
+constexpr int64_t kChunkTokens = 256;   // generic kernel: tokens per main chunk
+constexpr int kTcChunkGroups = 32;      // tensor-core kernel: 32-token groups per CTA
+constexpr int64_t kTailTile = 32;       // prefix-tail tokens per CTA
 
 struct SessionView {
     const float *k;
@@ -425,6 +428,20 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
                       Scratch &scratch, cudaStream_t stream, kivi_error *err) {
     const Geom &g = p.g;
     const uint64_t Gq = Hq / p.H;
+    const bool tc = kivi::attention_tc_supported(g, (int)Gq);
+    if (tc && nsess > 1) {
+        // The tensor-core kernel evaluates one query set; run each session on
+        // its own so that every session's result is bit-identical to its
+        // single-session attention.
+        const uint64_t rows1 = p.B * Hq;
+        for (uint64_t i = 0; i < nsess; ++i) {
+            int32_t rc = run_attention(p, sv + i, 1, d_q + i * rows1 * p.D, Hq, scale,
+                                       d_out + i * rows1 * p.D, d_m ? d_m + i * rows1 : nullptr,
+                                       d_l ? d_l + i * rows1 : nullptr, scratch, stream, err);
+            if (rc) return rc;
+        }
+        return KIVI_OK;
+    }
     const int maxrows = kivi::attention_max_rows((int)p.D);
     if (maxrows < (int)Gq)
         return set_msg(err, KIVI_ERR_UNSUPPORTED, "head_dim %llu with %llu query heads per kv head exceeds shared memory",
@@ -432,8 +449,11 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
     uint64_t per_launch = (uint64_t)maxrows / Gq;
     if (per_launch > (uint64_t)kivi::kMaxSessionsPerLaunch) per_launch = kivi::kMaxSessionsPerLaunch;
     const uint64_t main_tokens = p.vq / p.cfg.group_size * p.cfg.group_size;
-    const int64_t NC = (int64_t)((main_tokens + kChunkTokens - 1) / kChunkTokens);
-    const int parts = (int)NC + 2;
+    const int64_t chunk_tokens = tc ? (int64_t)kTcChunkGroups * (int64_t)p.cfg.group_size : kChunkTokens;
+    const int64_t NC = (int64_t)((main_tokens + chunk_tokens - 1) / chunk_tokens);
+    const int64_t tail_tokens = (int64_t)(p.seq - main_tokens);
+    const int NTT = (int)std::max<int64_t>(1, (tail_tokens + kTailTile - 1) / kTailTile);
+    const int parts = (int)NC + NTT + 1;
     const uint64_t rows_per_sess = p.B * Hq;
     for (uint64_t s0 = 0; s0 < nsess; s0 += per_launch) {
         const uint64_t ns = nsess - s0 < per_launch ? nsess - s0 : per_launch;
@@ -455,8 +475,11 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
         a.vhead = (int)p.vhead;
         a.seq_p = (int64_t)p.seq;
         a.main_tokens = (int64_t)main_tokens;
-        a.chunk_tokens = kChunkTokens;
+        a.chunk_tokens = chunk_tokens;
         a.NC = (int)NC;
+        a.c0 = 0;
+        a.NTT = NTT;
+        a.tail_tile = (int)kTailTile;
         a.parts = parts;
         a.S = (int)ns;
         a.session_base = (int)s0;
@@ -464,6 +487,29 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
         a.scale = scale;
         a.part_ml = scratch.as<float>();
         a.part_o = scratch.as<float>(ml_bytes);
+        if (tc) {
+            kivi::TcArgs t{};
+            t.kcodes = p.st.kcodes;
+            t.kparams = p.st.kparams;
+            t.vcodes = p.st.vcodes;
+            t.vparams = p.st.vparams;
+            t.code_stride = kivi::code_stride(g, p.st.cap);
+            t.kp_stride = kivi::kparam_stride(g, p.st.cap);
+            t.vp_stride = kivi::vparam_stride(g, p.st.cap);
+            t.H = (int)p.H;
+            t.Hq = (int)Hq;
+            t.GQ = (int)Gq;
+            t.main_groups = (int64_t)(main_tokens / p.cfg.group_size);
+            t.chunk_groups = kTcChunkGroups;
+            t.q = d_q;
+            t.scale = scale;
+            t.part_ml = a.part_ml;
+            t.part_o = a.part_o;
+            t.parts = parts;
+            CUDA_TRY(kivi::launch_attention_tc(t, (int)p.cfg.bits, (int)(p.B * p.H), stream),
+                     "attention (tensor cores)");
+            a.c0 = (int)NC; // the generic kernel covers the prefix tail and suffix only
+        }
         for (uint64_t i = 0; i < ns; ++i) {
             a.suf[i].k = sv ? sv[s0 + i].k : nullptr;
             a.suf[i].v = sv ? sv[s0 + i].v : nullptr;
@@ -477,6 +523,18 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
                                     d_l ? d_l + off : nullptr, d_m ? 1 : 0, stream),
                  "attention merge");
     }
+    return KIVI_OK;
+}
+
+// A tensor-core kernel whose bounded wait gave up leaves a flag instead of
+// hanging; synchronous calls report it as a CUDA-class error.
+int32_t check_device_waits(kivi_error *err) {
+    unsigned int flag = 0;
+    cudaError_t e = kivi::take_tc_error(&flag);
+    if (e != cudaSuccess) return cuda_fail(err, e, "device wait flag");
+    if (flag)
+        return set_msg(err, KIVI_ERR_CUDA, "attention kernel gave up waiting for its copies (flag %u)",
+                       flag);
     return KIVI_OK;
 }
 
@@ -753,6 +811,8 @@ int32_t kivi_cache_attention(const kivi_cache *h, const float *query, uint64_t q
     if (rc) return rc;
     CUDA_TRY(cudaMemcpyAsync(out, dout, n * 4, cudaMemcpyDeviceToHost, h->stream), "attention D2H");
     CUDA_TRY(cudaStreamSynchronize(h->stream), "attention");
+    rc = check_device_waits(err);
+    if (rc) return rc;
     return set_err(err, KIVI_OK);
 }
 
@@ -1198,6 +1258,8 @@ int32_t kivi_session_attention(const kivi_session *s, const float *query, uint64
     if (rc) return rc;
     CUDA_TRY(cudaMemcpyAsync(out, dout, n * 4, cudaMemcpyDeviceToHost, s->stream), "session D2H");
     CUDA_TRY(cudaStreamSynchronize(s->stream), "session attention");
+    rc = check_device_waits(err);
+    if (rc) return rc;
     return set_err(err, KIVI_OK);
 }
 

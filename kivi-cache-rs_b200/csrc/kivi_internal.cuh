@@ -82,7 +82,12 @@ struct AttnArgs {
                               // are processed in whole chunks
     int64_t chunk_tokens;     // tokens per main chunk
     int NC;                   // number of main chunks
-    int parts;                // partial slots per row = NC + 2 (prefix tail, suffix)
+    int c0;                   // first chunk slot this launch evaluates (NC when the
+                              // main chunks run on the tensor-core kernel)
+    int NTT;                  // prefix-tail tiles of tail_tile tokens each (slots
+                              // NC .. NC+NTT-1); 0 = one slot for the whole tail
+    int tail_tile;
+    int parts;                // partial slots per row = NC + max(NTT,1) + 1 (suffix)
     int S;                    // sessions in this launch
     int session_base;         // index of the first session of this launch
     const float *q;           // [S_total][B][Hq][D]
@@ -156,6 +161,28 @@ cudaError_t launch_merge(const float *part_ml, const float *part_o, int64_t rows
 // Cross-shard merge: m/l [parts][rows], o [parts][rows][D].
 cudaError_t launch_merge_shards(const float *m, const float *l, const float *o, int64_t parts,
                                 int64_t rows, int D, float *out, cudaStream_t s);
+// Tensor-core attention over the packed main region (kivi_attention_tc.cu):
+// head_dim 128, group 32, 2/4-bit, <= 8 query heads per kv head, one query set.
+struct TcArgs {
+    const uint32_t *kcodes;
+    const float2 *kparams;
+    const uint32_t *vcodes;
+    const float2 *vparams;
+    int64_t code_stride, kp_stride, vp_stride; // per-stream strides (elements)
+    int H, Hq, GQ;
+    int64_t main_groups; // 32-token groups with packed K and V
+    int chunk_groups;    // groups per CTA (partial slot = chunk index)
+    const float *q;      // [B][Hq][128]
+    float scale;
+    float *part_ml;
+    float *part_o;
+    int parts;
+};
+bool attention_tc_supported(const Geom &g, int gq);
+cudaError_t launch_attention_tc(const TcArgs &a, int bits, int nstreams, cudaStream_t s);
+// Reads and clears the flag set when a tensor-core kernel's bounded wait gave up.
+cudaError_t take_tc_error(unsigned int *out);
+
 // Dynamic shared memory the attention kernel needs for `rows` query rows.
 size_t attention_smem_bytes(int D, int rows);
 int attention_max_rows(int D);

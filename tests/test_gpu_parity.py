@@ -75,10 +75,23 @@ def assert_store_equal(g, o):
         assert getattr(gm, k) == v, k
 
 
-def assert_attention_close(got, ref):
+def assert_attention_close(got, ref, ref64=None):
+    """max-abs <= 1e-4 against the reference's fp32 output, and rel-L2 <= 1e-5.
+
+    The reference itself rounds: over long contexts its sequential fp32 sums
+    drift from exact arithmetic by more than 1e-5 (1.6e-5 rel-L2 at 8269 tokens
+    with lognormal key channels, measured with the oracle's fp64 evaluation of
+    the same quantized cache).  When `ref64` is given, the rel-L2 bar is applied
+    against that exact evaluation, and the GPU-to-reference gap may not exceed
+    the reference's own error plus 1e-5."""
     assert got.shape == ref.shape
     assert max_abs(got, ref) <= ATOL, max_abs(got, ref)
-    assert rel_l2(got, ref) <= RTOL_L2, rel_l2(got, ref)
+    if ref64 is None:
+        assert rel_l2(got, ref) <= RTOL_L2, rel_l2(got, ref)
+        return
+    own = rel_l2(ref, ref64)
+    assert rel_l2(got, ref64) <= RTOL_L2, (rel_l2(got, ref64), own)
+    assert rel_l2(got, ref) <= own + RTOL_L2, (rel_l2(got, ref), own)
 
 
 # ---------------------------------------------------------------- codec
@@ -618,3 +631,45 @@ def test_sequence_sharded_partials_merge_to_full_attention(K):
     K.merge_partials_dev(shards, rows, dim, m, l, o, out)
     torch.cuda.synchronize()
     assert_attention_close(out.cpu().numpy().reshape(-1), full.attention(q, qh, 1.0 / np.sqrt(128.0)))
+
+
+# ---------------------------------------------------------------- tensor-core main region
+
+
+@pytest.mark.parametrize("bits,batch,kv,qh,seq,outlier", [
+    (2, 2, 8, 32, 8192 + 77, "lognormal"),   # config-1 shape, shorter context
+    (4, 1, 2, 16, 5000, "x20"),              # config-2 distribution, 8 q heads per kv head
+    (4, 2, 2, 8, 2100, "lognormal"),         # 4-bit, 4 q heads per kv head
+    (2, 1, 3, 15, 3333, "x20"),              # 5 q heads per kv head (padded head tile)
+    (2, 3, 2, 4, 700, "lognormal"),          # 2 q heads per kv head
+])
+def test_tensor_core_region_matches_oracle(K, bits, batch, kv, qh, seq, outlier):
+    g, o = pair(K, bits, 32, 128, batch, kv, 128)
+    keys, values, _ = synthetic_kv(seq * bits + qh, batch, kv, seq, 128, outlier=outlier)
+    append_both(g, o, keys, values, seq)
+    rng = np.random.default_rng(seq)
+    scale = float(np.float32(1.0) / np.sqrt(np.float32(128)))
+    for _ in range(2):
+        q = rng.standard_normal(batch * qh * 128, dtype=np.float32)
+        assert_attention_close(g.attention(q, qh, scale), o.attention(q, qh, scale, threads=8),
+                               o.attention_f64(q, qh, scale))
+        k, v, _ = synthetic_kv(int(rng.integers(1 << 30)), batch, kv, 1, 128, outlier=outlier)
+        append_both(g, o, k, v, 1)
+
+
+@pytest.mark.parametrize("mag", [1e-3, 3e3])
+def test_tensor_core_region_extreme_magnitudes(K, mag):
+    """Power-of-two operand scaling keeps both fp16 parts in range for tiny and
+    huge keys/values/queries."""
+    batch, kv, qh, seq = 1, 2, 8, 2000
+    g, o = pair(K, 2, 32, 128, batch, kv, 128)
+    keys, values, _ = synthetic_kv(9, batch, kv, seq, 128)
+    keys = keys * np.float32(mag)
+    values = values * np.float32(mag)
+    append_both(g, o, keys, values, seq)
+    q = np.random.default_rng(4).standard_normal(batch * qh * 128, dtype=np.float32) / np.float32(mag)
+    scale = float(np.float32(1.0) / np.sqrt(np.float32(128)))
+    ref = o.attention(q, qh, scale)
+    got = g.attention(q, qh, scale)
+    assert rel_l2(got, ref) <= RTOL_L2
+    assert max_abs(got, ref) <= ATOL * max(1.0, mag)
