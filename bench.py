@@ -165,8 +165,8 @@ def channel_scales(rng, H, D, outlier):
     return np.where(mask, np.float32(20.0), np.float32(1.0)).astype(np.float32)
 
 
-KERNELS = ("attn_tc", "attn_chunk", "merge", "append_small", "key_groups", "value_tokens",
-           "copy_rows")
+KERNELS = ("attn_tc", "attn_tail", "attn_chunk", "merge", "append_small", "key_groups",
+           "value_tokens", "copy_rows")
 
 
 def main_region_bytes(cache, cfgd):
@@ -252,28 +252,40 @@ def run_gpu(args, cfgd, rank, world, local_rank):
     stream.synchronize()
 
     bytes_step0, attn_bytes0 = step_bytes(K, cache, cfgd)
-    main_bytes0 = main_region_bytes(cache, cfgd)
-    K.lib().kivi_profile_reset()
     launches0 = K.kernel_launches()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
-    K.lib().kivi_profile_enable(1)
     with ClockSampler(local_rank) as clk:
         ev0.record(stream)
         for i in range(W, W + S):
             decode(i)
         ev1.record(stream)
         stream.synchronize()
-    K.lib().kivi_profile_enable(0)
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
     launches = K.kernel_launches() - launches0
     t_ms = ev0.elapsed_time(ev1)
     bytes_step1, attn_bytes1 = step_bytes(K, cache, cfgd)
-    main_bytes1 = main_region_bytes(cache, cfgd)
+
+    # Per-kernel durations: the same decode step again, each launch bracketed by
+    # CUDA events on its stream (kept out of the timed region above).
+    P = min(S, 64)
+    pk, pv = gen_tokens(rng, chs, B, H, P, D)
+    pk_dev = torch.from_numpy(np.ascontiguousarray(pk.transpose(2, 0, 1, 3))).cuda()
+    pv_dev = torch.from_numpy(np.ascontiguousarray(pv.transpose(2, 0, 1, 3))).cuda()
+    pq_dev = torch.from_numpy(rng.standard_normal((P, B, Hq, D), dtype=np.float32)).cuda()
+    torch.cuda.synchronize()
+    prof_bytes0 = (step_bytes(K, cache, cfgd)[1], main_region_bytes(cache, cfgd))
+    K.lib().kivi_profile_reset()
+    K.lib().kivi_profile_enable(1)
+    for i in range(P):
+        cache.decode_dev(pk_dev[i], pv_dev[i], pq_dev[i], Hq, scale, dout, stream=stream)
+    stream.synchronize()
+    K.lib().kivi_profile_enable(0)
+    prof_bytes1 = (step_bytes(K, cache, cfgd)[1], main_region_bytes(cache, cfgd))
     import ctypes as C
 
     kernels = {}
@@ -331,8 +343,9 @@ def run_gpu(args, cfgd, rank, world, local_rank):
     steps_per_s = world * S / (t_ms / 1e3)
     avg_step_bytes = 0.5 * (bytes_step0 + bytes_step1)
     hbm_gbs = world * avg_step_bytes * S / (t_ms / 1e3) / 1e9
+    kern_bytes = 0.5 * (prof_bytes0[0] + prof_bytes1[0]) if kernel == "attn_chunk" \
+        else 0.5 * (prof_bytes0[1] + prof_bytes1[1])
     attn_bytes = 0.5 * (attn_bytes0 + attn_bytes1)
-    kern_bytes = attn_bytes if kernel == "attn_chunk" else 0.5 * (main_bytes0 + main_bytes1)
     achieved = kern_bytes / (kern_avg_ms / 1e3) / 1e9 if kern_avg_ms > 0 else None
     workload = cfgd["name"]
     result = {

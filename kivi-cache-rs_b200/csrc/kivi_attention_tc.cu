@@ -41,9 +41,15 @@ __device__ unsigned int g_tc_error = 0; // set by bounded waits that give up
 
 namespace {
 
+#ifndef KIVI_TC_STAGES
+#define KIVI_TC_STAGES 8
+#endif
+#ifndef KIVI_TC_MINB1
+#define KIVI_TC_MINB1 3
+#endif
 constexpr int kConsumers = 4;
 constexpr int kTcThreads = (kConsumers + 1) * 32;
-constexpr int kStages = 8;
+constexpr int kStages = KIVI_TC_STAGES; // pipeline depth (groups in flight per CTA)
 constexpr int kD = 128;
 constexpr int kG = 32;
 constexpr long long kWaitCycles = 2000000000LL; // ~1 s at B200 clocks
@@ -209,7 +215,7 @@ template <int BITS> struct LaneCodes {
 };
 
 template <int BITS, int NT>
-__global__ void __launch_bounds__(kTcThreads, NT == 1 ? 3 : 2) attn_tc_kernel(const TcArgs a) {
+__global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_tc_kernel(const TcArgs a) {
     using TG = TcGeom<BITS>;
     extern __shared__ __align__(128) unsigned char smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * TG::STAGE);
@@ -667,6 +673,250 @@ cudaError_t take_tc_error(unsigned int *out) {
     cudaError_t e = cudaMemcpyFromSymbol(out, g_tc_error, sizeof(unsigned int));
     if (e == cudaSuccess && *out) e = cudaMemcpyToSymbol(g_tc_error, &zero, sizeof(unsigned int));
     return e;
+}
+
+} // namespace kivi
+
+// ---------------------------------------------------------------- dense tail
+//
+// Tokens [main_tokens, seq_p + suffix_len) of every stream, one CTA per
+// 32-token tile: the partial key group, the fp32 value window, the fp32 key
+// residual and a session's fp32 suffix (attention.rs:75-104).  Keys/values are
+// staged as fp32 rows (packed tokens dequantized with fma(code, scale, zero),
+// quant.rs:404-406), then every query head of the kv head scores the tile.
+namespace kivi {
+namespace {
+
+constexpr int kTailThreads = 128;
+constexpr int kTailTokens = 32;
+constexpr int kTailPitch = 129;
+
+// Four consecutive channels d..d+3 (d % 4 == 0) of token t, as fp32.
+template <int BITS>
+__device__ __forceinline__ float4 tail_key4(const TailArgs &a, const uint32_t *kc, const float2 *kp,
+                                            const float *kres, const float *sk, int64_t t, int d) {
+    constexpr int IPC = 32 * BITS / 32, TPW = 32 / BITS;
+    constexpr uint32_t MASK = (1u << BITS) - 1u;
+    if (t < a.kq) {
+        const int64_t grp = t >> 5;
+        const int u = (int)(t & 31);
+        const int sh = (u % TPW) * BITS;
+        const uint32_t *w = kc + (grp * 128 + d) * IPC + u / TPW;
+        const float4 p01 = *reinterpret_cast<const float4 *>(kp + grp * 128 + d);
+        const float4 p23 = *reinterpret_cast<const float4 *>(kp + grp * 128 + d + 2);
+        return make_float4(__fmaf_rn((float)((w[0] >> sh) & MASK), p01.x, p01.y),
+                           __fmaf_rn((float)((w[IPC] >> sh) & MASK), p01.z, p01.w),
+                           __fmaf_rn((float)((w[2 * IPC] >> sh) & MASK), p23.x, p23.y),
+                           __fmaf_rn((float)((w[3 * IPC] >> sh) & MASK), p23.z, p23.w));
+    }
+    if (t < a.seq_p) return *reinterpret_cast<const float4 *>(kres + (t - a.kq) * 128 + d);
+    return *reinterpret_cast<const float4 *>(sk + (t - a.seq_p) * 128 + d);
+}
+
+template <int BITS>
+__device__ __forceinline__ float4 tail_value4(const TailArgs &a, const uint32_t *vc, const float2 *vp,
+                                              const float *vres, const float *sv, int64_t t, int d) {
+    constexpr int IPC = 32 * BITS / 32, TPW = 32 / BITS;
+    constexpr uint32_t MASK = (1u << BITS) - 1u;
+    if (t < a.vq) {
+        const int cg = d >> 5, lc = d & 31;
+        const uint32_t w = vc[(t * 4 + cg) * IPC + lc / TPW];
+        const int sh = (lc % TPW) * BITS;
+        const float2 p = vp[t * 4 + cg];
+        return make_float4(__fmaf_rn((float)((w >> sh) & MASK), p.x, p.y),
+                           __fmaf_rn((float)((w >> (sh + BITS)) & MASK), p.x, p.y),
+                           __fmaf_rn((float)((w >> (sh + 2 * BITS)) & MASK), p.x, p.y),
+                           __fmaf_rn((float)((w >> (sh + 3 * BITS)) & MASK), p.x, p.y));
+    }
+    if (t < a.seq_p)
+        return *reinterpret_cast<const float4 *>(vres + ((a.vhead + (t - a.vq)) % a.g.R) * 128 + d);
+    return *reinterpret_cast<const float4 *>(sv + (t - a.seq_p) * 128 + d);
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(kTailThreads) attn_tail_kernel(const TailArgs a) {
+    __shared__ float Ks[kTailTokens * kTailPitch];
+    __shared__ float Vs[kTailTokens * kTailPitch];
+    __shared__ __align__(16) float Qs[8 * 128];
+    __shared__ float Ps[8 * kTailTokens];
+    const Geom &g = a.g;
+    const int tile = blockIdx.x, s = blockIdx.y;
+    const int b = s / a.H, kvh = s - b * a.H;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t t0 = a.main_tokens + (int64_t)tile * kTailTokens;
+    const int nt = (int)max((int64_t)0, min((int64_t)kTailTokens, a.end_tokens - t0));
+
+    const uint32_t *kc = a.st.kcodes + (int64_t)s * code_stride(g, a.st.cap);
+    const float2 *kp = a.st.kparams + (int64_t)s * kparam_stride(g, a.st.cap);
+    const uint32_t *vc = a.st.vcodes + (int64_t)s * code_stride(g, a.st.cap);
+    const float2 *vp = a.st.vparams + (int64_t)s * vparam_stride(g, a.st.cap);
+    const float *kres = a.st.kres + (int64_t)s * g.R * g.D;
+    const float *vres = a.st.vres + (int64_t)s * g.R * g.D;
+    const float *sk = a.suffix_k ? a.suffix_k + (int64_t)s * a.suffix_cap * g.D : nullptr;
+    const float *sv = a.suffix_v ? a.suffix_v + (int64_t)s * a.suffix_cap * g.D : nullptr;
+
+    for (int e = threadIdx.x; e < a.GQ * 128; e += kTailThreads)
+        Qs[e] = a.q[((int64_t)b * a.Hq + kvh * a.GQ) * 128 + e];
+    for (int e = threadIdx.x; e < nt * 32; e += kTailThreads) {
+        const int tt = e >> 5, d = (e & 31) * 4;
+        const int64_t t = t0 + tt;
+        const float4 k4 = tail_key4<BITS>(a, kc, kp, kres, sk, t, d);
+        const float4 v4 = tail_value4<BITS>(a, vc, vp, vres, sv, t, d);
+        float *kd = Ks + tt * kTailPitch + d;
+        float *vd = Vs + tt * kTailPitch + d;
+        kd[0] = k4.x;
+        kd[1] = k4.y;
+        kd[2] = k4.z;
+        kd[3] = k4.w;
+        vd[0] = v4.x;
+        vd[1] = v4.y;
+        vd[2] = v4.z;
+        vd[3] = v4.w;
+    }
+    __syncthreads();
+
+    float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+        const int h = warp + 4 * hh;
+        if (h >= a.GQ) continue;
+        float x = -INFINITY;
+        if (lane < nt) {
+            const float *kr = Ks + lane * kTailPitch;
+            const float4 *q4 = reinterpret_cast<const float4 *>(Qs + h * 128);
+            float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+#pragma unroll 8
+            for (int i = 0; i < 32; ++i) {
+                const float4 qq = q4[i];
+                d0 = fmaf(kr[4 * i + 0], qq.x, d0);
+                d1 = fmaf(kr[4 * i + 1], qq.y, d1);
+                d2 = fmaf(kr[4 * i + 2], qq.z, d2);
+                d3 = fmaf(kr[4 * i + 3], qq.w, d3);
+            }
+            x = ((d0 + d1) + (d2 + d3)) * a.scale;
+        }
+        float m = x;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        const float p = (lane < nt && m != -INFINITY) ? expf(x - m) : 0.0f;
+        float l = p;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        Ps[h * kTailTokens + lane] = p;
+        mrow[hh] = m;
+        lrow[hh] = l;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+        const int h = warp + 4 * hh;
+        if (h >= a.GQ) continue;
+        const int64_t row = (int64_t)b * a.Hq + kvh * a.GQ + h;
+        const int slot = a.slot0 + tile;
+        float o[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int tt = 0; tt < nt; ++tt) {
+            const float pt = Ps[h * kTailTokens + tt];
+            if (pt == 0.0f) continue;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) o[k] = fmaf(pt, Vs[tt * kTailPitch + lane + 32 * k], o[k]);
+        }
+        float *dst = a.part_o + (row * a.parts + slot) * 128;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) dst[lane + 32 * k] = o[k];
+        if (lane == 0) {
+            a.part_ml[(row * a.parts + slot) * 2 + 0] = mrow[hh];
+            a.part_ml[(row * a.parts + slot) * 2 + 1] = lrow[hh];
+        }
+    }
+}
+
+// One CTA per row (head_dim 128): log-sum-exp merge of the row's `parts`
+// slots.  Warp w sums slots w, w+4, ... (4 channels per lane); the four warp
+// partials and the normaliser are combined in a fixed order (deterministic).
+__global__ void __launch_bounds__(128) merge_rows_kernel(const float *part_ml, const float *part_o,
+                                                        int parts, int64_t rows, float *out,
+                                                        float *out_m, float *out_l) {
+    __shared__ float wsh[512];
+    __shared__ __align__(16) float osh[4][128];
+    __shared__ float lsh[4];
+    __shared__ float Msh;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t row = blockIdx.x;
+    const float *ml = part_ml + row * parts * 2;
+    if (warp == 0) {
+        float M = -INFINITY;
+        for (int c = lane; c < parts; c += 32)
+            if (ml[2 * c + 1] > 0.0f) M = fmaxf(M, ml[2 * c]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        if (lane == 0) Msh = M;
+    }
+    __syncthreads();
+    const float M = Msh;
+    float Lp = 0.0f;
+    for (int c = threadIdx.x; c < parts; c += 128) {
+        const float l = ml[2 * c + 1];
+        const float w = (l > 0.0f) ? expf(ml[2 * c] - M) : 0.0f;
+        if (c < 512) wsh[c] = w;
+        Lp = fmaf(l, w, Lp);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) Lp += __shfl_xor_sync(0xffffffffu, Lp, o);
+    if (lane == 0) lsh[warp] = Lp;
+    __syncthreads();
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 *po = reinterpret_cast<const float4 *>(part_o + row * parts * 128) + lane;
+#pragma unroll 4
+    for (int c = warp; c < parts; c += 4) {
+        float w;
+        if (c < 512) {
+            w = wsh[c];
+        } else {
+            const float l = ml[2 * c + 1];
+            w = (l > 0.0f) ? expf(ml[2 * c] - M) : 0.0f;
+        }
+        const float4 o = po[(int64_t)c * 32];
+        acc.x = fmaf(o.x, w, acc.x);
+        acc.y = fmaf(o.y, w, acc.y);
+        acc.z = fmaf(o.z, w, acc.z);
+        acc.w = fmaf(o.w, w, acc.w);
+    }
+    reinterpret_cast<float4 *>(osh[warp])[lane] = acc;
+    __syncthreads();
+    const int d = threadIdx.x;
+    const float o = ((osh[0][d] + osh[1][d]) + (osh[2][d] + osh[3][d]));
+    const float L = (lsh[0] + lsh[1]) + (lsh[2] + lsh[3]);
+    if (out_m) {
+        out[row * 128 + d] = o;
+        if (d == 0) {
+            out_m[row] = M;
+            out_l[row] = L;
+        }
+    } else {
+        out[row * 128 + d] = (L > 0.0f) ? o * (1.0f / L) : 0.0f;
+    }
+}
+
+} // namespace
+
+cudaError_t launch_attention_tail(const TailArgs &a, int ntiles, int nstreams, cudaStream_t s) {
+    if (ntiles <= 0) return cudaSuccess;
+    ProfScope prof("attn_tail", s);
+    if (a.g.bits == 2)
+        attn_tail_kernel<2><<<dim3((unsigned)ntiles, (unsigned)nstreams), kTailThreads, 0, s>>>(a);
+    else
+        attn_tail_kernel<4><<<dim3((unsigned)ntiles, (unsigned)nstreams), kTailThreads, 0, s>>>(a);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_merge_rows(const float *part_ml, const float *part_o, int parts, int64_t rows,
+                              float *out, float *out_m, float *out_l, cudaStream_t s) {
+    if (rows <= 0) return cudaSuccess;
+    ProfScope prof("merge", s);
+    merge_rows_kernel<<<(unsigned)rows, 128, 0, s>>>(part_ml, part_o, parts, rows, out, out_m, out_l);
+    count_launch();
+    return cudaGetLastError();
 }
 
 } // namespace kivi

@@ -411,7 +411,10 @@ int32_t append_device(KvState &s, const float *dk, const float *dv, uint64_t seq
 // ---------------------------------------------------------------- attention plan
 
 constexpr int64_t kChunkTokens = 256;   // generic kernel: tokens per main chunk
-constexpr int kTcChunkGroups = 32;      // tensor-core kernel: 32-token groups per CTA
+#ifndef KIVI_TC_CHUNK_GROUPS
+#define KIVI_TC_CHUNK_GROUPS 64
+#endif
+constexpr int kTcChunkGroups = KIVI_TC_CHUNK_GROUPS; // tensor-core kernel: 32-token groups per CTA
 constexpr int64_t kTailTile = 32;       // prefix-tail tokens per CTA
 
 struct SessionView {
@@ -442,6 +445,70 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
         }
         return KIVI_OK;
     }
+    if (tc) {
+        // Tensor-core main region + dense tail tiles + one-warp-per-row merge.
+        const uint64_t G = p.cfg.group_size;
+        const uint64_t main_tokens = p.vq / G * G;
+        const int64_t main_groups = (int64_t)(main_tokens / G);
+        const int64_t NC = (main_groups + kTcChunkGroups - 1) / kTcChunkGroups;
+        const int64_t slen = sv ? (int64_t)sv[0].len : 0;
+        const int64_t end = (int64_t)p.seq + slen;
+        const int64_t NTT = (end - (int64_t)main_tokens + kTailTile - 1) / kTailTile;
+        const int parts = (int)(NC + NTT);
+        const uint64_t rows = p.B * Hq;
+        // part_o is read as float4: keep its offset 256-byte aligned
+        const size_t ml_bytes = (rows * parts * 2 * sizeof(float) + 255) / 256 * 256;
+        const size_t o_bytes = rows * parts * p.D * sizeof(float);
+        CUDA_TRY(scratch.ensure(ml_bytes + o_bytes), "attention scratch");
+        float *part_ml = scratch.as<float>(), *part_o = scratch.as<float>(ml_bytes);
+        if (NC > 0) {
+            kivi::TcArgs t{};
+            t.kcodes = p.st.kcodes;
+            t.kparams = p.st.kparams;
+            t.vcodes = p.st.vcodes;
+            t.vparams = p.st.vparams;
+            t.code_stride = kivi::code_stride(g, p.st.cap);
+            t.kp_stride = kivi::kparam_stride(g, p.st.cap);
+            t.vp_stride = kivi::vparam_stride(g, p.st.cap);
+            t.H = (int)p.H;
+            t.Hq = (int)Hq;
+            t.GQ = (int)Gq;
+            t.main_groups = main_groups;
+            t.chunk_groups = kTcChunkGroups;
+            t.q = d_q;
+            t.scale = scale;
+            t.part_ml = part_ml;
+            t.part_o = part_o;
+            t.parts = parts;
+            CUDA_TRY(kivi::launch_attention_tc(t, (int)p.cfg.bits, (int)(p.B * p.H), stream),
+                     "attention (tensor cores)");
+        }
+        kivi::TailArgs ta{};
+        ta.g = g;
+        ta.st = p.st;
+        ta.H = (int)p.H;
+        ta.Hq = (int)Hq;
+        ta.GQ = (int)Gq;
+        ta.kq = (int64_t)p.kq;
+        ta.vq = (int64_t)p.vq;
+        ta.seq_p = (int64_t)p.seq;
+        ta.vhead = (int)p.vhead;
+        ta.main_tokens = (int64_t)main_tokens;
+        ta.end_tokens = end;
+        ta.suffix_k = sv ? sv[0].k : nullptr;
+        ta.suffix_v = sv ? sv[0].v : nullptr;
+        ta.suffix_cap = sv ? (int64_t)sv[0].cap : 0;
+        ta.q = d_q;
+        ta.scale = scale;
+        ta.part_ml = part_ml;
+        ta.part_o = part_o;
+        ta.parts = parts;
+        ta.slot0 = (int)NC;
+        CUDA_TRY(kivi::launch_attention_tail(ta, (int)NTT, (int)(p.B * p.H), stream), "attention tail");
+        CUDA_TRY(kivi::launch_merge_rows(part_ml, part_o, parts, (int64_t)rows, d_out, d_m, d_l, stream),
+                 "attention merge");
+        return KIVI_OK;
+    }
     const int maxrows = kivi::attention_max_rows((int)p.D);
     if (maxrows < (int)Gq)
         return set_msg(err, KIVI_ERR_UNSUPPORTED, "head_dim %llu with %llu query heads per kv head exceeds shared memory",
@@ -449,7 +516,7 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
     uint64_t per_launch = (uint64_t)maxrows / Gq;
     if (per_launch > (uint64_t)kivi::kMaxSessionsPerLaunch) per_launch = kivi::kMaxSessionsPerLaunch;
     const uint64_t main_tokens = p.vq / p.cfg.group_size * p.cfg.group_size;
-    const int64_t chunk_tokens = tc ? (int64_t)kTcChunkGroups * (int64_t)p.cfg.group_size : kChunkTokens;
+    const int64_t chunk_tokens = kChunkTokens;
     const int64_t NC = (int64_t)((main_tokens + chunk_tokens - 1) / chunk_tokens);
     const int64_t tail_tokens = (int64_t)(p.seq - main_tokens);
     const int NTT = (int)std::max<int64_t>(1, (tail_tokens + kTailTile - 1) / kTailTile);
@@ -487,29 +554,7 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
         a.scale = scale;
         a.part_ml = scratch.as<float>();
         a.part_o = scratch.as<float>(ml_bytes);
-        if (tc) {
-            kivi::TcArgs t{};
-            t.kcodes = p.st.kcodes;
-            t.kparams = p.st.kparams;
-            t.vcodes = p.st.vcodes;
-            t.vparams = p.st.vparams;
-            t.code_stride = kivi::code_stride(g, p.st.cap);
-            t.kp_stride = kivi::kparam_stride(g, p.st.cap);
-            t.vp_stride = kivi::vparam_stride(g, p.st.cap);
-            t.H = (int)p.H;
-            t.Hq = (int)Hq;
-            t.GQ = (int)Gq;
-            t.main_groups = (int64_t)(main_tokens / p.cfg.group_size);
-            t.chunk_groups = kTcChunkGroups;
-            t.q = d_q;
-            t.scale = scale;
-            t.part_ml = a.part_ml;
-            t.part_o = a.part_o;
-            t.parts = parts;
-            CUDA_TRY(kivi::launch_attention_tc(t, (int)p.cfg.bits, (int)(p.B * p.H), stream),
-                     "attention (tensor cores)");
-            a.c0 = (int)NC; // the generic kernel covers the prefix tail and suffix only
-        }
+
         for (uint64_t i = 0; i < ns; ++i) {
             a.suf[i].k = sv ? sv[s0 + i].k : nullptr;
             a.suf[i].v = sv ? sv[s0 + i].v : nullptr;

@@ -178,6 +178,28 @@ struct TcArgs {
     float *part_o;
     int parts;
 };
+// Dense tail of the tensor-core path: tokens [main_tokens, end_tokens) of each
+// stream (partial group, fp32 window/residual, one session's fp32 suffix),
+// 32 tokens per CTA, partial slots slot0 + tile.  head_dim 128, <= 8 q heads
+// per kv head.
+struct TailArgs {
+    Geom g;
+    Store st;
+    int H, Hq, GQ;
+    int64_t kq, vq, seq_p;
+    int vhead;
+    int64_t main_tokens, end_tokens;
+    const float *suffix_k, *suffix_v; // [stream][suffix_cap][128] or null
+    int64_t suffix_cap;
+    const float *q;
+    float scale;
+    float *part_ml, *part_o;
+    int parts, slot0;
+};
+cudaError_t launch_attention_tail(const TailArgs &a, int ntiles, int nstreams, cudaStream_t s);
+// One warp per row merge for head_dim 128 (mode: out_m == null -> normalised rows).
+cudaError_t launch_merge_rows(const float *part_ml, const float *part_o, int parts, int64_t rows,
+                              float *out, float *out_m, float *out_l, cudaStream_t s);
 bool attention_tc_supported(const Geom &g, int gq);
 cudaError_t launch_attention_tc(const TcArgs &a, int bits, int nstreams, cudaStream_t s);
 // Reads and clears the flag set when a tensor-core kernel's bounded wait gave up.

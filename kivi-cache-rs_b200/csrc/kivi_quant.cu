@@ -53,6 +53,7 @@ __device__ __forceinline__ uint32_t quant_code(float x, float zero, float scale,
 __device__ __forceinline__ void quant_key_channel(const Geom &g, const float *const *rows, int d,
                                                   uint32_t *words, float2 *param) {
     float mn = INFINITY, mx = -INFINITY;
+#pragma unroll 8
     for (int u = 0; u < g.G; ++u) {
         float x = rows[u][d];
         mn = fminf(mn, x);
@@ -74,6 +75,7 @@ __device__ __forceinline__ void quant_value_group(const Geom &g, const float *ro
                                                   uint32_t *words, float2 *param) {
     const float *grp = row + cg * g.G;
     float mn = INFINITY, mx = -INFINITY;
+#pragma unroll 8
     for (int i = 0; i < g.G; ++i) {
         float x = grp[i];
         mn = fminf(mn, x);
@@ -86,6 +88,36 @@ __device__ __forceinline__ void quant_value_group(const Geom &g, const float *ro
         for (int k = 0; k < g.tpw; ++k)
             word |= quant_code(grp[w * g.tpw + k], mn, scale, g.levels) << (k * g.bits);
         words[w] = word;
+    }
+}
+
+// Warp-cooperative per-token value quantization of channel group `cg` (the
+// decode-step eviction): lanes split the G channels, min/max by shuffle
+// reduction (exact, order-free), each lane codes its channels, and the packed
+// words are OR-reduced across the warp.  Same results as quant_value_group.
+__device__ __forceinline__ void quant_value_group_warp(const Geom &g, const float *row, int cg,
+                                                       uint32_t *words, float2 *param, int lane) {
+    const float *grp = row + cg * g.G;
+    float mn = INFINITY, mx = -INFINITY;
+    for (int i = lane; i < g.G; i += 32) {
+        const float x = grp[i];
+        mn = fminf(mn, x);
+        mx = fmaxf(mx, x);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    const float scale = scale_of(__fsub_rn(mx, mn), g.levels);
+    if (lane == 0) *param = make_float2(scale, mn);
+    for (int w = 0; w < g.ipc; ++w) {
+        uint32_t part = 0;
+        for (int i = lane; i < g.G; i += 32)
+            if (i / g.tpw == w) part |= quant_code(grp[i], mn, scale, g.levels) << ((i % g.tpw) * g.bits);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) part |= __shfl_xor_sync(0xffffffffu, part, o);
+        if (lane == 0) words[w] = part;
     }
 }
 
@@ -132,12 +164,13 @@ __global__ void __launch_bounds__(256) append_small_kernel(Geom g, Store st, con
     const int drop = max(0, vres_len + seq - R);
     uint32_t *vc = st.vcodes + (int64_t)s * code_stride(g, st.cap);
     float2 *vp = st.vparams + (int64_t)s * vparam_stride(g, st.cap);
-    for (int p = threadIdx.x; p < drop * g.nch; p += blockDim.x) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    for (int p = warp; p < drop * g.nch; p += nwarps) {
         const int j = p / g.nch, cg = p % g.nch;
         const int slot = (vhead + j) % R;
         const int64_t t = vq + j;
-        quant_value_group(g, vres + (int64_t)slot * D, cg, vc + (t * g.nch + cg) * g.ipc,
-                          vp + t * g.nch + cg);
+        quant_value_group_warp(g, vres + (int64_t)slot * D, cg, vc + (t * g.nch + cg) * g.ipc,
+                               vp + t * g.nch + cg, lane);
     }
     __syncthreads();
     for (int e = threadIdx.x; e < seq * D; e += blockDim.x) {
