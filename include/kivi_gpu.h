@@ -216,6 +216,19 @@ int32_t kivi_cache_attention_partial_dev(const kivi_cache *cache, const float *d
 int32_t kivi_merge_partials_dev(uint64_t parts, uint64_t rows, uint64_t head_dim,
                                 const float *d_m, const float *d_l, const float *d_o,
                                 float *d_out, void *stream, kivi_error *err);
+/* Packed form of the partial state above, for one collective per decode step:
+ * one buffer of kivi_packed_partials_floats(rows, head_dim) floats holding
+ * m [rows], l [rows], then o [rows, head_dim] starting at the first multiple of
+ * 4 floats after 2*rows.  Parts gathered back to back (an all-gather of every
+ * shard's buffer, in rank order) merge with kivi_merge_packed_partials_dev.
+ * d_packed must be 16-byte aligned.  No counterpart in the reference. */
+uint64_t kivi_packed_partials_floats(uint64_t rows, uint64_t head_dim);
+int32_t kivi_cache_attention_partial_packed_dev(const kivi_cache *cache, const float *d_query,
+                                                uint64_t num_q_heads, float scale,
+                                                float *d_packed, void *stream, kivi_error *err);
+int32_t kivi_merge_packed_partials_dev(uint64_t parts, uint64_t rows, uint64_t head_dim,
+                                       const float *d_packed, float *d_out, void *stream,
+                                       kivi_error *err);
 /* Quantize the fp32 value window into the packed store (no counterpart in the
  * reference).  Used for an interior sequence shard, whose tokens a single-device
  * cache would already have evicted: the packed values are bit-identical to

@@ -241,18 +241,20 @@ __global__ void merge_kernel(const float *part_ml, const float *part_o, int part
 
 // Cross-shard merge: m, l [parts][rows]; o [parts][rows][D]; out [rows][D].
 __global__ void merge_shards_kernel(const float *m, const float *l, const float *o, int parts,
-                                    int64_t rows, int D, float *out) {
+                                    int64_t rows, int D, int64_t ml_stride, int64_t o_stride,
+                                    float *out) {
+    // Part c's row r: m[c*ml_stride + r], l[c*ml_stride + r], o[c*o_stride + r*D + d].
     extern __shared__ float w[];
     __shared__ float sh_L;
     const int64_t row = blockIdx.x;
     if (threadIdx.x == 0) {
         float M = -INFINITY;
         for (int c = 0; c < parts; ++c)
-            if (l[c * rows + row] > 0.0f) M = fmaxf(M, m[c * rows + row]);
+            if (l[c * ml_stride + row] > 0.0f) M = fmaxf(M, m[c * ml_stride + row]);
         float L = 0.0f;
         for (int c = 0; c < parts; ++c) {
-            const float lc = l[c * rows + row];
-            const float e = (lc > 0.0f) ? expf(m[c * rows + row] - M) : 0.0f;
+            const float lc = l[c * ml_stride + row];
+            const float e = (lc > 0.0f) ? expf(m[c * ml_stride + row] - M) : 0.0f;
             w[c] = e;
             L = __fmaf_rn(lc, e, L);
         }
@@ -263,7 +265,7 @@ __global__ void merge_shards_kernel(const float *m, const float *l, const float 
     for (int d = threadIdx.x; d < D; d += blockDim.x) {
         float acc = 0.0f;
         for (int c = 0; c < parts; ++c)
-            if (w[c] != 0.0f) acc = __fmaf_rn(o[((int64_t)c * rows + row) * D + d], w[c], acc);
+            if (w[c] != 0.0f) acc = __fmaf_rn(o[(int64_t)c * o_stride + row * D + d], w[c], acc);
         out[row * D + d] = acc * inv;
     }
 }
@@ -315,11 +317,12 @@ cudaError_t launch_merge(const float *part_ml, const float *part_o, int64_t rows
 }
 
 cudaError_t launch_merge_shards(const float *m, const float *l, const float *o, int64_t parts,
-                                int64_t rows, int D, float *out, cudaStream_t s) {
+                                int64_t rows, int D, int64_t ml_stride, int64_t o_stride,
+                                float *out, cudaStream_t s) {
     if (rows <= 0) return cudaSuccess;
     ProfScope prof("merge_shards", s);
-    merge_shards_kernel<<<(unsigned)rows, 128, sizeof(float) * parts, s>>>(m, l, o, (int)parts,
-                                                                           rows, D, out);
+    merge_shards_kernel<<<(unsigned)rows, 128, sizeof(float) * parts, s>>>(
+        m, l, o, (int)parts, rows, D, ml_stride, o_stride, out);
     count_launch();
     return cudaGetLastError();
 }

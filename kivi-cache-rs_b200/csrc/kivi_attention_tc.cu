@@ -6,7 +6,8 @@
 // each 32-token key/value group (codes + (scale, zero) of keys and values, the
 // reference's PackedStream order, quant.rs:37-44) from HBM into a ring of
 // shared-memory stages with bulk async copies (cp.async.bulk + mbarrier
-// complete_tx; no multicast); four consumer warps each take whole groups.
+// complete_tx, each copy into this CTA only); four consumer warps each take
+// whole groups.
 //
 // Per group, with q' = q * s_k (per channel), w' = p * s_v (per token and
 // channel group) and mid = (2^bits - 1) / 2, the dequantize-and-dot of

@@ -911,8 +911,42 @@ int32_t kivi_merge_partials_dev(uint64_t parts, uint64_t rows, uint64_t head_dim
     if (parts == 0 || !dm || !dl || !dout_parts || !dout)
         return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "bad merge arguments");
     CUDA_TRY(kivi::launch_merge_shards(dm, dl, dout_parts, (int64_t)parts, (int64_t)rows,
-                                       (int)head_dim, dout, (cudaStream_t)stream),
+                                       (int)head_dim, (int64_t)rows, (int64_t)(rows * head_dim),
+                                       dout, (cudaStream_t)stream),
              "merge partials");
+    return set_err(err, KIVI_OK);
+}
+
+uint64_t kivi_packed_partials_floats(uint64_t rows, uint64_t head_dim) {
+    const uint64_t off_o = (2 * rows + 3) & ~uint64_t(3);
+    return (off_o + rows * head_dim + 3) & ~uint64_t(3);
+}
+
+int32_t kivi_cache_attention_partial_packed_dev(const kivi_cache *h, const float *dq, uint64_t Hq,
+                                                float scale, float *d_packed, void *stream,
+                                                kivi_error *err) {
+    if (!h) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null cache");
+    if (!d_packed) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null output");
+    if (((uintptr_t)d_packed) & 15u)
+        return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "packed partials must be 16-byte aligned");
+    const uint64_t rows = h->s.B * Hq;
+    const uint64_t off_o = (2 * rows + 3) & ~uint64_t(3);
+    return kivi_cache_attention_partial_dev(h, dq, Hq, scale, d_packed, d_packed + rows,
+                                            d_packed + off_o, stream, err);
+}
+
+int32_t kivi_merge_packed_partials_dev(uint64_t parts, uint64_t rows, uint64_t head_dim,
+                                       const float *d_packed, float *dout, void *stream,
+                                       kivi_error *err) {
+    if (parts == 0 || !d_packed || !dout)
+        return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "bad merge arguments");
+    const uint64_t off_o = (2 * rows + 3) & ~uint64_t(3);
+    const uint64_t stride = kivi_packed_partials_floats(rows, head_dim);
+    CUDA_TRY(kivi::launch_merge_shards(d_packed, d_packed + rows, d_packed + off_o,
+                                       (int64_t)parts, (int64_t)rows, (int)head_dim,
+                                       (int64_t)stride, (int64_t)stride, dout,
+                                       (cudaStream_t)stream),
+             "merge packed partials");
     return set_err(err, KIVI_OK);
 }
 

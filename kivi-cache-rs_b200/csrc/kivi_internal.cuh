@@ -158,9 +158,11 @@ cudaError_t launch_attention_chunks(const AttnArgs &a, cudaStream_t s);
 cudaError_t launch_merge(const float *part_ml, const float *part_o, int64_t rows, int parts, int D,
                          int ml_stride_pairs, float *out, float *out_m, float *out_l, int mode,
                          cudaStream_t s);
-// Cross-shard merge: m/l [parts][rows], o [parts][rows][D].
+// Cross-shard merge: part c's m/l rows start at c*ml_stride, its o rows at
+// c*o_stride (floats); merged in part order.
 cudaError_t launch_merge_shards(const float *m, const float *l, const float *o, int64_t parts,
-                                int64_t rows, int D, float *out, cudaStream_t s);
+                                int64_t rows, int D, int64_t ml_stride, int64_t o_stride,
+                                float *out, cudaStream_t s);
 // Tensor-core attention over the packed main region (kivi_attention_tc.cu):
 // head_dim 128, group 32, 2/4-bit, <= 8 query heads per kv head, one query set.
 struct TcArgs {

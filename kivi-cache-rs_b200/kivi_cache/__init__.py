@@ -124,6 +124,9 @@ def lib():
         "kivi_cache_attention_partial_dev": ([P, P, sz, f32, P, P, P, P, e], i32),
         "kivi_merge_partials_dev": ([sz, sz, sz, P, P, P, P, P, e], i32),
         "kivi_cache_seal": ([P, e], i32),
+        "kivi_packed_partials_floats": ([sz, sz], sz),
+        "kivi_cache_attention_partial_packed_dev": ([P, P, sz, f32, P, P, e], i32),
+        "kivi_merge_packed_partials_dev": ([sz, sz, sz, P, P, P, e], i32),
         "kivi_cache_dequantize": ([P, fp, fp, sz, e], i32),
         "kivi_cache_memory": ([P, C.POINTER(_Memory)], i32),
         "kivi_cache_get_state": ([P, C.POINTER(_State)], i32),
@@ -383,6 +386,14 @@ class KiviCache:
             self._h, _ptr(d_query), num_q_heads, C.c_float(scale), _ptr(d_m), _ptr(d_l),
             _ptr(d_o), _stream(stream), C.byref(err)), err)
 
+    def attention_partial_packed_dev(self, d_query, num_q_heads, scale, d_packed, stream=None):
+        """Partial (m, l, o) of this shard in one packed buffer of
+        packed_partials_floats(batch * num_q_heads, head_dim) floats."""
+        err = _Err()
+        _check(lib().kivi_cache_attention_partial_packed_dev(
+            self._h, _ptr(d_query), num_q_heads, C.c_float(scale), _ptr(d_packed),
+            _stream(stream), C.byref(err)), err)
+
     def seal(self):
         err = _Err()
         _check(lib().kivi_cache_seal(self._h, C.byref(err)), err)
@@ -502,6 +513,18 @@ class SharedPrefix:
     def prefix_bytes(self):
         return int(lib().kivi_prefix_bytes(self._h))
 
+    def key_residual_len(self):
+        return int(self._st.key_residual_len)
+
+    def value_residual_len(self):
+        return int(self._st.value_residual_len)
+
+    def quantized_key_tokens(self):
+        return int(self._st.quantized_key_tokens)
+
+    def quantized_value_tokens(self):
+        return int(self._st.quantized_value_tokens)
+
     def shares_allocation_with(self, other):
         return bool(lib().kivi_prefix_shares_allocation_with(self._h, other._h))
 
@@ -605,6 +628,18 @@ def merge_partials_dev(parts, rows, head_dim, d_m, d_l, d_o, d_out, stream=None)
     err = _Err()
     _check(lib().kivi_merge_partials_dev(parts, rows, head_dim, _ptr(d_m), _ptr(d_l), _ptr(d_o),
                                          _ptr(d_out), _stream(stream), C.byref(err)), err)
+
+
+def packed_partials_floats(rows, head_dim):
+    """Floats of one shard's packed partial state (m, l, o) for `rows` query rows."""
+    return int(lib().kivi_packed_partials_floats(rows, head_dim))
+
+
+def merge_packed_partials_dev(parts, rows, head_dim, d_packed, d_out, stream=None):
+    """Log-sum-exp merge of `parts` packed partial states stored back to back."""
+    err = _Err()
+    _check(lib().kivi_merge_packed_partials_dev(parts, rows, head_dim, _ptr(d_packed),
+                                                _ptr(d_out), _stream(stream), C.byref(err)), err)
 
 
 # ---------------------------------------------------------------- runtime.rs
