@@ -2,37 +2,50 @@
 // packed main region of a stream (sm_100a).
 //
 // Applies to head_dim 128, group 32, 2- or 4-bit codes, up to 8 query heads
-// per kv head.  One CTA = one (token chunk, stream): a producer warp streams
-// each 32-token key/value group (codes + (scale, zero) of keys and values, the
-// reference's PackedStream order, quant.rs:37-44) from HBM into a ring of
-// shared-memory stages with bulk async copies (cp.async.bulk + mbarrier
-// complete_tx, each copy into this CTA only); four consumer warps each take
-// whole groups.
+// per kv head.  Work split: the main regions of all streams form one flat
+// sequence of 32-token groups (stream-major); every CTA of a launch takes an
+// equal contiguous run of it (one wave of resident CTAs per query set), so a
+// CTA covers one stream or the end of one and the start of the next, and it
+// emits one partial (m, l, o) slot per stream it touches.
 //
-// Per group, with q' = q * s_k (per channel), w' = p * s_v (per token and
-// channel group) and mid = (2^bits - 1) / 2, the dequantize-and-dot of
-// attention.rs:143-269 becomes
-//     logit[t][h] = sum_d (code[t][d] - mid) q'[h][d] + sum_d q[h][d] (z_k[d] + mid s_k[d])
-//     o[h][d]    += sum_t (code[t][d] - mid) w'[t][h] + sum_t p[t][h] (z_v[t] + mid s_v[t])
-// The code sums run on the tensor cores as m16n8k16 f16 MMAs with fp32
-// accumulation:
-//   * A = codes, exact: a byte permute + one AND places a 2/4-bit code in the
-//     mantissa of an fp16 subnormal, and one packed fma turns it into the
-//     normal fp16 (code - mid) * 2^(bits*j - 10), where j is the code's
-//     position in its byte; the per-row factor 2^(10 - bits*j) is undone on
-//     the fp32 accumulator and mid * scale moves into the zero-point term;
-//   * B = q' or w' split into two fp16 parts (11 + 11 significant bits): the
-//     high part is the fp32 value truncated to 11 bits, the low part the exact
-//     remainder, each in its own N column; a power-of-two scale per group
-//     keeps both in fp16 range.  The tensor-core product therefore carries
-//     ~22 bits of the fp32 operand -- the same order as the reference's fp32
-//     arithmetic -- while each code costs about one integer op.
+// Inside a CTA a producer warp streams each group (codes + (scale, zero) of
+// keys and values, the reference's PackedStream order, quant.rs:37-44) from
+// HBM into a ring of shared-memory stages with bulk async copies
+// (cp.async.bulk + mbarrier complete_tx, each copy into this CTA only); four
+// consumer warps each take whole groups and first rewrite the group's
+// parameters in place (scaled scales, folded zero points).
+//
+// Per group, with mid = 2^(bits-1) (an integer, so every constant below is an
+// exact fp16), the dequantize-and-dot of attention.rs:143-269 is
+//     logit[t][h] = sum_d (code[t][d] - mid) s_k[d] q[h][d] + sum_d q[h][d] z'_k[d]
+//     o[h][d]    += sum_t (code[t][d] - mid) s_v[t] p[t][h] + sum_t p[t][h] z'_v[t]
+// with z' = z + mid * s (folded when the stage lands).  The code sums run on the
+// tensor cores as m16n8k16 f16 MMAs with fp32 accumulation:
+//   * A = codes, exact: one byte permute gathers the byte holding four
+//     (2-bit) or two (4-bit) codes of two K neighbours into the two fp16
+//     halves of a register; per code position one LOP3 ORs the code into the
+//     mantissa of 1024 (fp16 1024 + code * 2^(bits*j)) and one packed fma
+//     rescales and subtracts 1024 + mid, leaving code - mid exactly;
+//   * B = s_k q (keys) or s_v p (values) split into two fp16 parts (11 + 11
+//     significant bits): the fp32 value truncated to 11 bits and the exact
+//     remainder, each in its own N column, so the tensor-core product carries
+//     ~22 bits of the fp32 operand.  Power-of-two scales keep B in fp16
+//     range: 2^(14 - e_q) per query head (|q| < 2^e_q), 2^-e_s per key group
+//     (s_k < 2^e_s) and 2^(3 - e_v) per value group (s_v < 2^e_v, and
+//     p < 2^11 under the lazy softmax rescale below); each is undone exactly
+//     on the fp32 side.
 // The zero-point sums and the online softmax stay in fp32 on the CUDA cores.
-// Partial (m, l, o) per query row go to the same slots the generic chunk
-// kernel uses, and the same deterministic merge combines them.
+// The softmax reference point moves only when a logit exceeds it by more than
+// 2^11 (in exp2 units), which skips almost every rescale of the accumulators.
+// Row/column orders inside the MMAs are permuted so that each lane's codes sit
+// in one byte: key tile row m <-> token 4*(m&7) + 2*mt + (m>>3); value tile
+// row m of m-tile 2*cg + jm <-> channel 32*cg + 4*(m&7) + 2*jm + (m>>3); value
+// K position 2c (+1) <-> token c (c+4), 2c+8 (+9) <-> token 8+c (12+c).
 #include <cuda_fp16.h>
 #include <math.h>
 #include <stdint.h>
+
+#include <algorithm>
 
 #include "kivi_internal.cuh"
 
@@ -51,10 +64,14 @@ namespace {
 constexpr int kConsumers = 4;
 constexpr int kTcThreads = (kConsumers + 1) * 32;
 constexpr int kStages = KIVI_TC_STAGES; // pipeline depth (groups in flight per CTA)
+#ifndef KIVI_TC_WAVES
+#define KIVI_TC_WAVES 1
+#endif
 constexpr int kD = 128;
 constexpr int kG = 32;
 constexpr long long kWaitCycles = 2000000000LL; // ~1 s at B200 clocks
-constexpr int kPStride = 40; // floats per head in the per-warp softmax-weight buffer
+constexpr int kPStride = 50;  // floats per head in the per-warp softmax-weight buffer
+constexpr float kLazy = 11.0f; // log2 headroom of the lazy softmax reference point
 
 template <int BITS> struct TcGeom {
     static constexpr int IPC = kG * BITS / 32;          // words per channel per key group
@@ -123,6 +140,11 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         : "memory");
 }
 
+// Named barrier over the four consumer warps (the producer never joins it).
+__device__ __forceinline__ void consumers_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
+}
+
 __device__ __forceinline__ void mma16816(float4 &d, uint32_t a0, uint32_t a1, uint32_t a2,
                                          uint32_t a3, uint32_t b0, uint32_t b1) {
     asm volatile(
@@ -171,64 +193,133 @@ __device__ __forceinline__ void b_frag(float x0, float x1, int par, uint32_t &b0
     b23 = par ? lo : recv;
 }
 
-// Codes enter the MMAs centred, as (code - mid) with mid = (2^bits - 1) / 2,
-// and mid * scale is folded into the zero point (z + mid * s): the tensor-core
-// sums then stay small next to the fp32 zero-point sums instead of cancelling
-// against them, which keeps the MMA's fp32 accumulation error well below the
-// reference's own rounding.
-template <int BITS> struct LaneCodes {
-    static constexpr float kMid = BITS == 2 ? 1.5f : 7.5f;
-    uint32_t selA, selB, mask, shift;
-    int rowexp; // log2 of the per-row factor that undoes the code placement
-    __device__ __forceinline__ LaneCodes(int r) {
-        int j;
-        if (BITS == 2) {
-            const uint32_t qb = (uint32_t)(r >> 2);
-            selA = qb | (qb << 4) | ((qb + 4) << 8) | ((qb + 4) << 12);
-            const uint32_t q2 = qb + 2;
-            selB = q2 | (q2 << 4) | ((q2 + 4) << 8) | ((q2 + 4) << 12);
-            j = 2 * (r & 3);
-            mask = 0x00030003u << j;
-        } else {
-            const uint32_t qb = (uint32_t)(r >> 1);
-            selA = qb | (qb << 4) | ((qb + 4) << 8) | ((qb + 4) << 12);
-            selB = selA;
-            j = 4 * (r & 1);
-            mask = 0x000F000Fu << j;
-        }
-        rowexp = 10 - j;
-        // -mid * 2^(j - 10) in both halves: exact in fp16
-        const __half hm = __float2half_rn(-kMid * exp2i(j - 10));
-        const uint32_t hb = (uint32_t)(*reinterpret_cast<const unsigned short *>(&hm));
-        shift = hb | (hb << 16);
+// fp16 bit pattern of an exactly representable normal value (compile time).
+constexpr uint32_t fp16_bits(double v) {
+    uint32_t sign = 0;
+    if (v < 0) {
+        sign = 0x8000u;
+        v = -v;
     }
-    // Two codes (one fragment row, K pair from words wa and wb) as a packed
-    // fp16x2: the permute + AND leaves code * 2^j as an fp16 subnormal
-    // (code * 2^j * 2^-24); one packed fma, * 2^14 - mid * 2^(j-10), gives
-    // (code - mid) * 2^(j-10) exactly, a normal fp16 (the tensor cores keep
-    // only a few bits of products formed from deep subnormals).
-    __device__ __forceinline__ uint32_t pick(uint32_t wa, uint32_t wb, uint32_t sel) const {
-        const uint32_t sub = __byte_perm(wa, wb, sel) & mask;
-        uint32_t out;
-        asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(out) : "r"(sub), "r"(0x74007400u), "r"(shift));
-        return out;
+    int e = 0;
+    while (v >= 2048.0) {
+        v /= 2.0;
+        ++e;
+    }
+    while (v < 1024.0) {
+        v *= 2.0;
+        --e;
+    }
+    return sign | ((uint32_t)(e + 25) << 10) | (uint32_t)(v - 1024.0);
+}
+constexpr uint32_t half2_bits(double v) { return fp16_bits(v) * 0x10001u; }
+constexpr double pow2(int k) { return k >= 0 ? double(1ull << k) : 1.0 / double(1ull << -k); }
+
+// Code position j of a permuted register x (bits j*BITS of both halves) as the
+// fp16 pair (code - mid): LOP3 puts the code into the mantissa of 1024, the
+// packed fma scales by 2^(-BITS*j) and subtracts 1024*2^(-BITS*j) + mid.
+template <int BITS, int J> __device__ __forceinline__ uint32_t code_pair(uint32_t x) {
+    constexpr uint32_t kMask = ((1u << BITS) - 1u) * 0x10001u << (BITS * J);
+    constexpr double kScale = pow2(-BITS * J);
+    constexpr double kMid = BITS == 2 ? 2.0 : 8.0;
+    constexpr uint32_t kMul = half2_bits(kScale);
+    constexpr uint32_t kSub = half2_bits(-(1024.0 * kScale + kMid));
+    uint32_t v, out;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(v) : "r"(x), "n"(kMask), "n"(0x64006400));
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(out) : "r"(v), "r"(kMul), "r"(kSub));
+    return out;
+}
+
+// Eight A registers from four code words.  wa/wb: K neighbours 2c, 2c+1 (keys:
+// channels; values: tokens), wc/wd: K neighbours 2c+8, 2c+9.  out[0..3] come
+// from wa/wb, out[4..7] from wc/wd, in code-position order (2-bit: the four
+// codes of byte `sel`; 4-bit: the two codes of each of two bytes).
+template <int BITS> struct Perm {
+    uint32_t s0, s1; // byte-permute selectors
+    __device__ __forceinline__ explicit Perm(int r) {
+        if (BITS == 2) {
+            const uint32_t k = (uint32_t)(r & 3);
+            s0 = k | (k << 4) | ((k + 4) << 8) | ((k + 4) << 12);
+            s1 = s0;
+        } else {
+            const uint32_t k = 2u * (uint32_t)(r & 1);
+            s0 = k | (k << 4) | ((k + 4) << 8) | ((k + 4) << 12);
+            s1 = s0 + 0x1111u;
+        }
+    }
+    __device__ __forceinline__ void eight(uint32_t wa, uint32_t wb, uint32_t wc, uint32_t wd,
+                                          uint32_t out[8]) const {
+        if (BITS == 2) {
+            const uint32_t x = __byte_perm(wa, wb, s0), y = __byte_perm(wc, wd, s0);
+            out[0] = code_pair<2, 0>(x);
+            out[1] = code_pair<2, 1>(x);
+            out[2] = code_pair<2, 2>(x);
+            out[3] = code_pair<2, 3>(x);
+            out[4] = code_pair<2, 0>(y);
+            out[5] = code_pair<2, 1>(y);
+            out[6] = code_pair<2, 2>(y);
+            out[7] = code_pair<2, 3>(y);
+        } else {
+            const uint32_t x0 = __byte_perm(wa, wb, s0), x1 = __byte_perm(wa, wb, s1);
+            const uint32_t y0 = __byte_perm(wc, wd, s0), y1 = __byte_perm(wc, wd, s1);
+            out[0] = code_pair<4, 0>(x0);
+            out[1] = code_pair<4, 1>(x0);
+            out[2] = code_pair<4, 0>(x1);
+            out[3] = code_pair<4, 1>(x1);
+            out[4] = code_pair<4, 0>(y0);
+            out[5] = code_pair<4, 1>(y0);
+            out[6] = code_pair<4, 0>(y1);
+            out[7] = code_pair<4, 1>(y1);
+        }
     }
 };
+
+// Rewrite of one landed stage's parameters by the warp that consumes it (all
+// 32 lanes; the stage belongs to that warp alone): key (s, z)
+// -> (s * 2^-e_s, z + mid s), value (s, z) -> (s * 2^(3 - e_v), z + mid s);
+// exps = (e_s, e_v).
+template <int BITS>
+__device__ __forceinline__ void prep_stage(unsigned char *base, int2 *exps, int lane) {
+    using TG = TcGeom<BITS>;
+    constexpr float kMid = BITS == 2 ? 2.0f : 8.0f;
+    float4 *kp = reinterpret_cast<float4 *>(base + TG::KC_BYTES) + 2 * lane; // channels 4l..4l+3
+    float4 *vp = reinterpret_cast<float4 *>(base + TG::KC_BYTES + TG::KP_BYTES + TG::VC_BYTES) +
+                 2 * lane; // (token, cg) entries 4l..4l+3
+    float4 k0 = kp[0], k1 = kp[1], v0 = vp[0], v1 = vp[1];
+    float ks = fmaxf(fmaxf(fabsf(k0.x), fabsf(k0.z)), fmaxf(fabsf(k1.x), fabsf(k1.z)));
+    float vs = fmaxf(fmaxf(fabsf(v0.x), fabsf(v0.z)), fmaxf(fabsf(v1.x), fabsf(v1.z)));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        ks = fmaxf(ks, __shfl_xor_sync(0xffffffffu, ks, o));
+        vs = fmaxf(vs, __shfl_xor_sync(0xffffffffu, vs, o));
+    }
+    const int es = exp_ceil(ks), ev = exp_ceil(vs);
+    const float fk = exp2i(-es), fv = exp2i(3 - ev);
+    kp[0] = make_float4(k0.x * fk, fmaf(kMid, k0.x, k0.y), k0.z * fk, fmaf(kMid, k0.z, k0.w));
+    kp[1] = make_float4(k1.x * fk, fmaf(kMid, k1.x, k1.y), k1.z * fk, fmaf(kMid, k1.z, k1.w));
+    vp[0] = make_float4(v0.x * fv, fmaf(kMid, v0.x, v0.y), v0.z * fv, fmaf(kMid, v0.z, v0.w));
+    vp[1] = make_float4(v1.x * fv, fmaf(kMid, v1.x, v1.y), v1.z * fv, fmaf(kMid, v1.z, v1.w));
+    if (lane == 0) *exps = make_int2(es, ev);
+}
 
 template <int BITS, int NT>
 __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_tc_kernel(const TcArgs a) {
     using TG = TcGeom<BITS>;
+    constexpr int IPC = TG::IPC;
     extern __shared__ __align__(128) unsigned char smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * TG::STAGE);
     uint64_t *empty = full + kStages;
-    float *pbuf = reinterpret_cast<float *>(empty + kStages); // [warp][nt][4][kPStride]
+    int2 *gexp = reinterpret_cast<int2 *>(empty + kStages);               // [stage] (e_s, e_v)
+    float *pbuf = reinterpret_cast<float *>(gexp + kStages);              // [warp][NT*4][kPStride]
+    float *Ow = pbuf + kConsumers * NT * 4 * kPStride;                   // [warp][8][128]
+    float *Mw = Ow + kConsumers * 8 * kD;                                // [warp][8]
+    float *Lw = Mw + kConsumers * 8;                                     // [warp][8]
 
-    const int chunk = blockIdx.x;
-    const int s = blockIdx.y;
-    const int b = s / a.H, kvh = s - b * a.H;
+    const int64_t rbase = (int64_t)blockIdx.z * a.rows_per_set; // this query set's first row
+    const int64_t W = (int64_t)a.nstreams * a.main_groups;
+    const int64_t gb = (int64_t)blockIdx.x * a.per;
+    const int64_t ge = min(W, gb + a.per);
+    const int ng = (int)max((int64_t)0, ge - gb);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t g0 = (int64_t)chunk * a.chunk_groups;
-    const int ng = (int)min((int64_t)a.chunk_groups, a.main_groups - g0);
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kStages; ++i) {
@@ -239,318 +330,256 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_
     }
     __syncthreads();
 
-    // Per-warp results handed to the cross-warp merge.
-    float res_m[NT], res_l[NT];
-    float res_o[NT][8][2];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-        res_m[nt] = -INFINITY;
-        res_l[nt] = 0.0f;
-    }
-
     if (warp == kConsumers) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
-            const char *kc = reinterpret_cast<const char *>(a.kcodes + (int64_t)s * a.code_stride);
-            const char *kp = reinterpret_cast<const char *>(a.kparams + (int64_t)s * a.kp_stride);
-            const char *vc = reinterpret_cast<const char *>(a.vcodes + (int64_t)s * a.code_stride);
-            const char *vp = reinterpret_cast<const char *>(a.vparams + (int64_t)s * a.vp_stride);
+            // (stream, group) of the next group to issue, advanced without division
+            int64_t cur_s = gb / a.main_groups, cur_g = gb - cur_s * a.main_groups;
             int issued = 0;
             for (int i = 0; i < ng; ++i) {
                 const int st = i % kStages;
                 if (i >= kStages && !mbar_wait(&empty[st], ((i / kStages) - 1) & 1, 1u)) break;
+                const char *kc = reinterpret_cast<const char *>(a.kcodes + cur_s * a.code_stride);
+                const char *kp = reinterpret_cast<const char *>(a.kparams + cur_s * a.kp_stride);
+                const char *vc = reinterpret_cast<const char *>(a.vcodes + cur_s * a.code_stride);
+                const char *vp = reinterpret_cast<const char *>(a.vparams + cur_s * a.vp_stride);
                 unsigned char *dst = smem + st * TG::STAGE;
-                const int64_t g = g0 + i;
                 mbar_expect_tx(&full[st], TG::STAGE);
-                bulk_g2s(dst, kc + g * TG::KC_BYTES, TG::KC_BYTES, &full[st]);
-                bulk_g2s(dst + TG::KC_BYTES, kp + g * TG::KP_BYTES, TG::KP_BYTES, &full[st]);
-                bulk_g2s(dst + TG::KC_BYTES + TG::KP_BYTES, vc + g * TG::VC_BYTES, TG::VC_BYTES,
+                bulk_g2s(dst, kc + cur_g * TG::KC_BYTES, TG::KC_BYTES, &full[st]);
+                bulk_g2s(dst + TG::KC_BYTES, kp + cur_g * TG::KP_BYTES, TG::KP_BYTES, &full[st]);
+                bulk_g2s(dst + TG::KC_BYTES + TG::KP_BYTES, vc + cur_g * TG::VC_BYTES, TG::VC_BYTES,
                          &full[st]);
-                bulk_g2s(dst + TG::KC_BYTES + TG::KP_BYTES + TG::VC_BYTES, vp + g * TG::VP_BYTES,
+                bulk_g2s(dst + TG::KC_BYTES + TG::KP_BYTES + TG::VC_BYTES, vp + cur_g * TG::VP_BYTES,
                          TG::VP_BYTES, &full[st]);
                 issued = i + 1;
+                if (++cur_g == a.main_groups) {
+                    cur_g = 0;
+                    ++cur_s;
+                }
             }
             // No copy may still be in flight into this CTA's shared memory at
             // exit: wait (bounded) for the last phase of every stage used.
             for (int st = 0; st < kStages && st < issued; ++st) {
-                const int last = st + ((issued - 1 - st) / kStages) * kStages;
-                mbar_wait(&full[st], (last / kStages) & 1, 4u);
+                const int j = st + ((issued - 1 - st) / kStages) * kStages; // last group in stage st
+                mbar_wait(&full[st], (j / kStages) & 1, 4u);
             }
         }
-    } else {
-        // ------------------------------------------------------------ consumers
-        const int r = lane >> 2, c = lane & 3;
-        const int par = r & 1, hb = r >> 1;
-        const LaneCodes<BITS> lc(r);
+        return;
+    }
 
-        // query values for the B fragments of the key MMA: head nt*4 + hb,
-        // channels 16kt + 2c + 8par (+1)
+    // ---------------------------------------------------------------- consumers
+    const int r = lane >> 2, c = lane & 3;
+    const int par = r & 1, hb = r >> 1;
+    const Perm<BITS> perm(r);
+    // lane's code-word offsets inside a stage (words): keys channel 2c, word
+    // holding tokens 4r..4r+3; values token c, word holding channels 4r..4r+3
+    const int kw = 2 * c * IPC + (BITS == 2 ? (r >> 2) : (r >> 1));
+    const int vw = c * 4 * IPC + (BITS == 2 ? (r >> 2) : (r >> 1));
+    // K position (value tiles) of this lane's logit tokens 4r + j: 2j + koff
+    const int koff = 16 * (r >> 2) + ((r & 1) ? 1 : 0) + ((r & 2) ? 8 : 0);
+    float *pw = pbuf + warp * (NT * 4 * kPStride);
+    bool ok = true;
+
+    int i0 = 0; // CTA-local index of the segment's first group
+    for (int64_t f = gb; f < ge;) {
+        const int64_t s = f / a.main_groups;
+        const int64_t seg_end = min(ge, (s + 1) * a.main_groups);
+        const int n_seg = (int)(seg_end - f);
+        const int b = (int)(s / a.H), kvh = (int)(s - (int64_t)b * a.H);
+
+        // ---- query rows of this stream: q' = q * 2^(14 - e_q) per head
         float qv[NT][8][2];
+        float fh[NT]; // per lane head c: 2^(e_q - 14) * scale * log2(e)
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
             const int h = nt * 4 + hb;
-            const bool ok = h < a.GQ;
-            const float *qrow = a.q + ((int64_t)b * a.Hq + kvh * a.GQ + (ok ? h : 0)) * kD;
+            const bool okh = h < a.GQ;
+            const float *qrow = a.q + (rbase + (int64_t)b * a.Hq + kvh * a.GQ + (okh ? h : 0)) * kD;
+            float qm = 0.0f;
 #pragma unroll
             for (int kt = 0; kt < 8; ++kt) {
                 const float2 v = *reinterpret_cast<const float2 *>(qrow + 16 * kt + 2 * c + 8 * par);
-                qv[nt][kt][0] = ok ? v.x : 0.0f;
-                qv[nt][kt][1] = ok ? v.y : 0.0f;
+                qv[nt][kt][0] = okh ? v.x : 0.0f;
+                qv[nt][kt][1] = okh ? v.y : 0.0f;
+                qm = fmaxf(qm, fmaxf(fabsf(qv[nt][kt][0]), fabsf(qv[nt][kt][1])));
             }
+            qm = fmaxf(qm, __shfl_xor_sync(0xffffffffu, qm, 1));
+            qm = fmaxf(qm, __shfl_xor_sync(0xffffffffu, qm, 2));
+            qm = fmaxf(qm, __shfl_xor_sync(0xffffffffu, qm, 4));
+            const int eq = exp_ceil(qm);
+            const float sq = exp2i(14 - eq);
+#pragma unroll
+            for (int kt = 0; kt < 8; ++kt) {
+                qv[nt][kt][0] *= sq;
+                qv[nt][kt][1] *= sq;
+            }
+            const int eqc = __shfl_sync(0xffffffffu, eq, 8 * c); // head nt*4 + c
+            fh[nt] = exp2i(eqc - 14) * (a.scale * 1.4426950408889634f);
         }
 
-        float m[NT], l[NT];
+        float mref[NT], l[NT];
         float4 acc[NT][8];
         float zv[NT][4];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-            m[nt] = -INFINITY;
+            mref[nt] = -INFINITY;
             l[nt] = 0.0f;
 #pragma unroll
             for (int mt = 0; mt < 8; ++mt) acc[nt][mt] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
             for (int cg = 0; cg < 4; ++cg) zv[nt][cg] = 0.0f;
         }
-        int erun = -1000; // running value-scale exponent (warp-uniform)
-        float *pw = pbuf + warp * (NT * 4 * kPStride);
-        // Value K tiles use a token permutation: K pair c <-> tokens (c, c+4),
-        // K pair c+4 <-> tokens (8+e, 12+e), e = (c+2)&3.  It makes the value
-        // code loads bank-conflict free.  kpos*: K position of this lane's
-        // logit tokens r and r+8 within their 16-token tile.
-        const int kpos0 = (r < 4) ? 2 * r : 2 * (r - 4) + 1;
-        const int kpos1 = (r < 4) ? 8 + 2 * ((r + 2) & 3) : 9 + 2 * ((r + 2) & 3);
-        const int tA_own = par ? 8 + ((c + 2) & 3) : c; // own value K pair: tokens tA, tA+4
-        const int e_c = (c + 2) & 3;
 
-        for (int i = warp; i < ng; i += kConsumers) {
+        const int first = i0 + ((warp - i0) % kConsumers + kConsumers) % kConsumers;
+        for (int i = first; ok && i < i0 + n_seg; i += kConsumers) {
             const int st = i % kStages;
-            if (!mbar_wait(&full[st], (i / kStages) & 1, 2u)) break;
+            if (!mbar_wait(&full[st], (i / kStages) & 1, 2u)) {
+                ok = false;
+                break;
+            }
+            prep_stage<BITS>(smem + st * TG::STAGE, &gexp[st], lane);
+            __syncwarp();
             const unsigned char *base = smem + st * TG::STAGE;
             const uint32_t *KC = reinterpret_cast<const uint32_t *>(base);
             const float4 *KP4 = reinterpret_cast<const float4 *>(base + TG::KC_BYTES);
             const uint32_t *VC = reinterpret_cast<const uint32_t *>(base + TG::KC_BYTES + TG::KP_BYTES);
             const float4 *VP4 = reinterpret_cast<const float4 *>(base + TG::KC_BYTES + TG::KP_BYTES +
                                                                  TG::VC_BYTES);
+            const int2 ex = gexp[st];
 
-            // ---------------- keys: B = q' = q * s_k, split, per-group scale
-            float4 kpz[8];
-#pragma unroll
-            for (int kt = 0; kt < 8; ++kt) kpz[kt] = KP4[(16 * kt + 2 * c + 8 * par) >> 1];
+            // ---------------- keys: B = q' s' (split), zero term q' . z'
             uint32_t bk[NT][8][2];
-            int kexp[NT];
-            float kzero[NT];
+            float zc[NT];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) zc[nt] = 0.0f;
+#pragma unroll
+            for (int kt = 0; kt < 8; ++kt) {
+                const float4 kpz = KP4[8 * kt + c + 4 * par]; // channels 16kt + 2c + 8par (+1)
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    zc[nt] = fmaf(qv[nt][kt][0], kpz.y, zc[nt]);
+                    zc[nt] = fmaf(qv[nt][kt][1], kpz.w, zc[nt]);
+                    b_frag(qv[nt][kt][0] * kpz.x, qv[nt][kt][1] * kpz.z, par, bk[nt][kt][0],
+                           bk[nt][kt][1]);
+                }
+            }
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-                float amax = 0.0f, zc = 0.0f;
-                float v[8][2];
-#pragma unroll
-                for (int kt = 0; kt < 8; ++kt) {
-                    v[kt][0] = qv[nt][kt][0] * kpz[kt].x;
-                    v[kt][1] = qv[nt][kt][1] * kpz[kt].z;
-                    zc = fmaf(qv[nt][kt][0], fmaf(LaneCodes<BITS>::kMid, kpz[kt].x, kpz[kt].y), zc);
-                    zc = fmaf(qv[nt][kt][1], fmaf(LaneCodes<BITS>::kMid, kpz[kt].z, kpz[kt].w), zc);
-                    amax = fmaxf(amax, fmaxf(fabsf(v[kt][0]), fabsf(v[kt][1])));
-                }
-#pragma unroll
-                for (int o = 1; o <= 4; o <<= 1) {
-                    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-                    zc += __shfl_xor_sync(0xffffffffu, zc, o);
-                }
-                const int k = 14 - exp_ceil(amax);
-                const float sc = exp2i(k);
-#pragma unroll
-                for (int kt = 0; kt < 8; ++kt)
-                    b_frag(v[kt][0] * sc, v[kt][1] * sc, par, bk[nt][kt][0], bk[nt][kt][1]);
-                kexp[nt] = k;
-                kzero[nt] = zc;
+                zc[nt] += __shfl_xor_sync(0xffffffffu, zc[nt], 1);
+                zc[nt] += __shfl_xor_sync(0xffffffffu, zc[nt], 2);
+                zc[nt] += __shfl_xor_sync(0xffffffffu, zc[nt], 4);
             }
 
-            // ---------------- keys: A = codes, D = raw logits
+            // ---------------- keys: A = codes, D = code sums per (token, head part)
             float4 dk[NT][2];
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) dk[nt][0] = dk[nt][1] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
             for (int kt = 0; kt < 8; ++kt) {
-                if (BITS == 2) {
-                    const uint4 X = *reinterpret_cast<const uint4 *>(KC + (16 * kt + 2 * c) * 2);
-                    const uint4 Y = *reinterpret_cast<const uint4 *>(KC + (16 * kt + 2 * c + 8) * 2);
+                const uint32_t *w = KC + kw + 16 * kt * IPC;
+                uint32_t av[8];
+                perm.eight(w[0], w[IPC], w[8 * IPC], w[9 * IPC], av);
 #pragma unroll
-                    for (int im = 0; im < 2; ++im) {
-                        const uint32_t wa = im ? X.y : X.x, wb = im ? X.w : X.z;
-                        const uint32_t ya = im ? Y.y : Y.x, yb = im ? Y.w : Y.z;
-                        const uint32_t a0 = lc.pick(wa, wb, lc.selA), a1 = lc.pick(wa, wb, lc.selB);
-                        const uint32_t a2 = lc.pick(ya, yb, lc.selA), a3 = lc.pick(ya, yb, lc.selB);
-#pragma unroll
-                        for (int nt = 0; nt < NT; ++nt)
-                            mma16816(dk[nt][im], a0, a1, a2, a3, bk[nt][kt][0], bk[nt][kt][1]);
-                    }
-                } else {
-                    const uint4 X = *reinterpret_cast<const uint4 *>(KC + (16 * kt + 2 * c) * 4);
-                    const uint4 Z = *reinterpret_cast<const uint4 *>(KC + (16 * kt + 2 * c + 1) * 4);
-                    const uint4 Y = *reinterpret_cast<const uint4 *>(KC + (16 * kt + 2 * c + 8) * 4);
-                    const uint4 W = *reinterpret_cast<const uint4 *>(KC + (16 * kt + 2 * c + 9) * 4);
-#pragma unroll
-                    for (int im = 0; im < 2; ++im) {
-                        const uint32_t x0 = im ? X.z : X.x, x1 = im ? X.w : X.y;
-                        const uint32_t z0 = im ? Z.z : Z.x, z1 = im ? Z.w : Z.y;
-                        const uint32_t y0 = im ? Y.z : Y.x, y1 = im ? Y.w : Y.y;
-                        const uint32_t w0 = im ? W.z : W.x, w1 = im ? W.w : W.y;
-                        const uint32_t a0 = lc.pick(x0, z0, lc.selA), a1 = lc.pick(x1, z1, lc.selA);
-                        const uint32_t a2 = lc.pick(y0, w0, lc.selA), a3 = lc.pick(y1, w1, lc.selA);
-#pragma unroll
-                        for (int nt = 0; nt < NT; ++nt)
-                            mma16816(dk[nt][im], a0, a1, a2, a3, bk[nt][kt][0], bk[nt][kt][1]);
-                    }
+                for (int nt = 0; nt < NT; ++nt) {
+                    mma16816(dk[nt][0], av[0], av[1], av[4], av[5], bk[nt][kt][0], bk[nt][kt][1]);
+                    mma16816(dk[nt][1], av[2], av[3], av[6], av[7], bk[nt][kt][0], bk[nt][kt][1]);
                 }
             }
 
-            // ---------------- logits + online softmax (lane's head nt*4 + c)
+            // ---------------- logits (exp2 units) + lazy online softmax, lane head nt*4 + c
+            const float fs = exp2i(ex.x);
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-                const int kk = __shfl_sync(0xffffffffu, kexp[nt], 8 * c);
-                const float zz = __shfl_sync(0xffffffffu, kzero[nt], 8 * c);
-                const float fac = exp2i(lc.rowexp - kk);
+                const float zz = __shfl_sync(0xffffffffu, zc[nt], 8 * c);
                 float x[4];
-                x[0] = fmaf(dk[nt][0].x + dk[nt][0].y, fac, zz) * a.scale;
-                x[1] = fmaf(dk[nt][0].z + dk[nt][0].w, fac, zz) * a.scale;
-                x[2] = fmaf(dk[nt][1].x + dk[nt][1].y, fac, zz) * a.scale;
-                x[3] = fmaf(dk[nt][1].z + dk[nt][1].w, fac, zz) * a.scale;
+                x[0] = fmaf(dk[nt][0].x + dk[nt][0].y, fs, zz) * fh[nt]; // token 4r
+                x[1] = fmaf(dk[nt][0].z + dk[nt][0].w, fs, zz) * fh[nt]; // token 4r + 1
+                x[2] = fmaf(dk[nt][1].x + dk[nt][1].y, fs, zz) * fh[nt]; // token 4r + 2
+                x[3] = fmaf(dk[nt][1].z + dk[nt][1].w, fs, zz) * fh[nt]; // token 4r + 3
                 float gmax = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
                 gmax = fmaxf(gmax, __shfl_xor_sync(0xffffffffu, gmax, 4));
                 gmax = fmaxf(gmax, __shfl_xor_sync(0xffffffffu, gmax, 8));
                 gmax = fmaxf(gmax, __shfl_xor_sync(0xffffffffu, gmax, 16));
-                const float mnew = fmaxf(m[nt], gmax);
-                const float alpha = (m[nt] == -INFINITY) ? 0.0f : expf(m[nt] - mnew);
+                const bool need = gmax > mref[nt] + kLazy;
+                if (__any_sync(0xffffffffu, need)) {
+                    const float nref = need ? gmax : mref[nt];
+                    const float alpha = (mref[nt] == -INFINITY) ? 0.0f : exp2f(mref[nt] - nref);
+                    mref[nt] = nref;
+                    l[nt] *= alpha;
+#pragma unroll
+                    for (int mt = 0; mt < 8; ++mt) {
+                        acc[nt][mt].x *= alpha;
+                        acc[nt][mt].y *= alpha;
+                        acc[nt][mt].z *= alpha;
+                        acc[nt][mt].w *= alpha;
+                    }
+                    const float ab = __shfl_sync(0xffffffffu, alpha, hb);
+#pragma unroll
+                    for (int cg = 0; cg < 4; ++cg) zv[nt][cg] *= ab;
+                }
                 float p[4];
 #pragma unroll
-                for (int jj = 0; jj < 4; ++jj) p[jj] = expf(x[jj] - mnew);
-                l[nt] = fmaf(l[nt], alpha, (p[0] + p[1]) + (p[2] + p[3]));
-                m[nt] = mnew;
+                for (int jj = 0; jj < 4; ++jj) p[jj] = exp2f(x[jj] - mref[nt]);
+                l[nt] += (p[0] + p[1]) + (p[2] + p[3]);
+                float *ph = pw + (nt * 4 + c) * kPStride + koff;
 #pragma unroll
-                for (int mt = 0; mt < 8; ++mt) {
-                    acc[nt][mt].x *= alpha;
-                    acc[nt][mt].y *= alpha;
-                    acc[nt][mt].z *= alpha;
-                    acc[nt][mt].w *= alpha;
-                }
-                const float ab = __shfl_sync(0xffffffffu, alpha, hb);
-#pragma unroll
-                for (int cg = 0; cg < 4; ++cg) zv[nt][cg] *= ab;
-                // p of head c at tokens r + 8jj, stored at their value-tile K
-                // positions for the value B fragments
-#pragma unroll
-                for (int jj = 0; jj < 4; ++jj)
-                    pw[(nt * 4 + c) * kPStride + 16 * (jj >> 1) + ((jj & 1) ? kpos1 : kpos0)] = p[jj];
+                for (int jj = 0; jj < 4; ++jj) ph[2 * jj] = p[jj];
             }
             __syncwarp();
 
-            // ---------------- value scale exponent (max s_v over the group)
-            float4 vpz[2][2][2]; // [kk][own token tA / tA+4][cg pair] = (s,z,s,z)
-#pragma unroll
-            for (int kk = 0; kk < 2; ++kk) {
-#pragma unroll
-                for (int tt = 0; tt < 2; ++tt) {
-                    const int t = 16 * kk + tA_own + 4 * tt;
-                    vpz[kk][tt][0] = VP4[t * 2];
-                    vpz[kk][tt][1] = VP4[t * 2 + 1];
-                }
-            }
-            float smax = 0.0f;
-#pragma unroll
-            for (int kk = 0; kk < 2; ++kk)
-#pragma unroll
-                for (int tt = 0; tt < 2; ++tt)
-#pragma unroll
-                    for (int h2 = 0; h2 < 2; ++h2)
-                        smax = fmaxf(smax, fmaxf(fabsf(vpz[kk][tt][h2].x), fabsf(vpz[kk][tt][h2].z)));
-#pragma unroll
-            for (int o = 1; o <= 4; o <<= 1) smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, o));
-            const int eg = exp_ceil(smax);
-            if (eg > erun) {
-                if (erun > -1000) {
-                    const float f = exp2i(erun - eg);
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                        for (int mt = 0; mt < 8; ++mt) {
-                            acc[nt][mt].x *= f;
-                            acc[nt][mt].y *= f;
-                            acc[nt][mt].z *= f;
-                            acc[nt][mt].w *= f;
-                        }
-                }
-                erun = eg;
-            }
-            const float vsc = exp2i(14 - erun);
-
-            // ---------------- values: B = w' = p * s_v, A = codes
-            // Both 16-token K tiles of the group accumulate into a fresh
-            // fragment that is then added to the running fp32 sums with
-            // round-to-nearest: the MMA's own accumulation truncates, and
-            // over hundreds of tokens that bias would exceed the reference's
-            // rounding error.
+            // ---------------- values: B = p s'_v (split), zero term p . z'_v
             uint32_t bv[2][NT][4][2];
 #pragma unroll
             for (int kk = 0; kk < 2; ++kk) {
+                const int t0 = 16 * kk + 8 * par + c; // own K pair: tokens t0, t0 + 4
+                const float4 e00 = VP4[t0 * 2], e01 = VP4[t0 * 2 + 1];
+                const float4 e10 = VP4[(t0 + 4) * 2], e11 = VP4[(t0 + 4) * 2 + 1];
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                     const float2 pp = *reinterpret_cast<const float2 *>(
                         pw + (nt * 4 + hb) * kPStride + 16 * kk + 2 * c + 8 * par);
-                    const float p0 = pp.x * vsc, p1 = pp.y * vsc;
 #pragma unroll
                     for (int cg = 0; cg < 4; ++cg) {
-                        const float4 e0 = vpz[kk][0][cg >> 1], e1 = vpz[kk][1][cg >> 1];
-                        const float s0 = (cg & 1) ? e0.z : e0.x, z0 = (cg & 1) ? e0.w : e0.y;
-                        const float s1 = (cg & 1) ? e1.z : e1.x, z1 = (cg & 1) ? e1.w : e1.y;
-                        zv[nt][cg] = fmaf(pp.x, fmaf(LaneCodes<BITS>::kMid, s0, z0), zv[nt][cg]);
-                        zv[nt][cg] = fmaf(pp.y, fmaf(LaneCodes<BITS>::kMid, s1, z1), zv[nt][cg]);
-                        b_frag(p0 * s0, p1 * s1, par, bv[kk][nt][cg][0], bv[kk][nt][cg][1]);
+                        const float4 a0 = (cg < 2) ? e00 : e01, a1 = (cg < 2) ? e10 : e11;
+                        const float s0 = (cg & 1) ? a0.z : a0.x, z0 = (cg & 1) ? a0.w : a0.y;
+                        const float s1 = (cg & 1) ? a1.z : a1.x, z1 = (cg & 1) ? a1.w : a1.y;
+                        zv[nt][cg] = fmaf(pp.x, z0, zv[nt][cg]);
+                        zv[nt][cg] = fmaf(pp.y, z1, zv[nt][cg]);
+                        b_frag(pp.x * s0, pp.y * s1, par, bv[kk][nt][cg][0], bv[kk][nt][cg][1]);
                     }
                 }
             }
+
+            // ---------------- values: A = codes (channels x tokens), fresh sums per group
+            const float fvv = exp2i(ex.y - 3);
 #pragma unroll
             for (int cg = 0; cg < 4; ++cg) {
+                float4 t[NT][2];
 #pragma unroll
-                for (int im = 0; im < 2; ++im) {
-                    // A fragments of both K tiles: rows = channels 32cg + 16im + (r, r+8),
-                    // K pairs = tokens (c, c+4) and (8+e, 12+e) of each 16-token tile
-                    uint32_t af[2][4];
+                for (int nt = 0; nt < NT; ++nt) t[nt][0] = t[nt][1] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-                    for (int kk = 0; kk < 2; ++kk) {
-                        const int t0 = 16 * kk + c, t1 = t0 + 4;
-                        const int t2 = 16 * kk + 8 + e_c, t3 = t2 + 4;
-                        if constexpr (BITS == 2) {
-                            // one word per (token, cg, im); rows r and r+8 share it
-                            const uint32_t w0 = VC[t0 * 8 + cg * 2 + im], w1 = VC[t1 * 8 + cg * 2 + im];
-                            const uint32_t w2 = VC[t2 * 8 + cg * 2 + im], w3 = VC[t3 * 8 + cg * 2 + im];
-                            af[kk][0] = lc.pick(w0, w1, lc.selA);
-                            af[kk][1] = lc.pick(w0, w1, lc.selB);
-                            af[kk][2] = lc.pick(w2, w3, lc.selA);
-                            af[kk][3] = lc.pick(w2, w3, lc.selB);
-                        } else {
-                            // words 2im (rows r) and 2im+1 (rows r+8) of (token, cg)
-                            const uint2 q0 = *reinterpret_cast<const uint2 *>(VC + t0 * 16 + cg * 4 + 2 * im);
-                            const uint2 q1 = *reinterpret_cast<const uint2 *>(VC + t1 * 16 + cg * 4 + 2 * im);
-                            const uint2 q2 = *reinterpret_cast<const uint2 *>(VC + t2 * 16 + cg * 4 + 2 * im);
-                            const uint2 q3 = *reinterpret_cast<const uint2 *>(VC + t3 * 16 + cg * 4 + 2 * im);
-                            af[kk][0] = lc.pick(q0.x, q1.x, lc.selA);
-                            af[kk][1] = lc.pick(q0.y, q1.y, lc.selA);
-                            af[kk][2] = lc.pick(q2.x, q3.x, lc.selA);
-                            af[kk][3] = lc.pick(q2.y, q3.y, lc.selA);
-                        }
-                    }
+                for (int kk = 0; kk < 2; ++kk) {
+                    // tokens 16kk + c, +4, +8, +12 (K positions 2c, 2c+1, 2c+8, 2c+9)
+                    const uint32_t *w = VC + vw + (16 * kk) * 4 * IPC + cg * IPC;
+                    uint32_t av[8];
+                    perm.eight(w[0], w[16 * IPC], w[32 * IPC], w[48 * IPC], av);
 #pragma unroll
                     for (int nt = 0; nt < NT; ++nt) {
-                        float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
-                        mma16816(t, af[0][0], af[0][1], af[0][2], af[0][3], bv[0][nt][cg][0],
-                                 bv[0][nt][cg][1]);
-                        mma16816(t, af[1][0], af[1][1], af[1][2], af[1][3], bv[1][nt][cg][0],
-                                 bv[1][nt][cg][1]);
-                        float4 &r4 = acc[nt][2 * cg + im];
-                        r4.x += t.x;
-                        r4.y += t.y;
-                        r4.z += t.z;
-                        r4.w += t.w;
+                        mma16816(t[nt][0], av[0], av[1], av[4], av[5], bv[kk][nt][cg][0],
+                                 bv[kk][nt][cg][1]);
+                        mma16816(t[nt][1], av[2], av[3], av[6], av[7], bv[kk][nt][cg][0],
+                                 bv[kk][nt][cg][1]);
+                    }
+                }
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+                    for (int jm = 0; jm < 2; ++jm) {
+                        float4 &r4 = acc[nt][2 * cg + jm];
+                        r4.x = fmaf(t[nt][jm].x, fvv, r4.x);
+                        r4.y = fmaf(t[nt][jm].y, fvv, r4.y);
+                        r4.z = fmaf(t[nt][jm].z, fvv, r4.z);
+                        r4.w = fmaf(t[nt][jm].w, fvv, r4.w);
                     }
                 }
             }
@@ -558,100 +587,115 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_
             if (lane == 0) mbar_arrive(&empty[st]);
         }
 
-        // ---------------- per-warp results (lane's head nt*4 + c)
+        // ---------------- per-warp results of the segment (lane's head nt*4 + c)
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
             float ls = l[nt];
             ls += __shfl_xor_sync(0xffffffffu, ls, 4);
             ls += __shfl_xor_sync(0xffffffffu, ls, 8);
             ls += __shfl_xor_sync(0xffffffffu, ls, 16);
-            float zsum[4];
+            const int h = nt * 4 + c;
+            float *ow = Ow + (warp * 8 + h) * kD;
 #pragma unroll
             for (int cg = 0; cg < 4; ++cg) {
                 float zt = zv[nt][cg];
                 zt += __shfl_xor_sync(0xffffffffu, zt, 1);
                 zt += __shfl_xor_sync(0xffffffffu, zt, 2);
                 zt += __shfl_xor_sync(0xffffffffu, zt, 4);
-                zsum[cg] = __shfl_sync(0xffffffffu, zt, 8 * c);
+                const float zs = __shfl_sync(0xffffffffu, zt, 8 * c);
+                const float4 u0 = acc[nt][2 * cg], u1 = acc[nt][2 * cg + 1];
+                // channels 32cg + 4r + (0, 1, 2, 3)
+                *reinterpret_cast<float4 *>(ow + 32 * cg + 4 * r) =
+                    make_float4((u0.x + u0.y) + zs, (u0.z + u0.w) + zs, (u1.x + u1.y) + zs,
+                                (u1.z + u1.w) + zs);
             }
-            const float vf = exp2i(lc.rowexp + erun - 14);
-#pragma unroll
-            for (int mt = 0; mt < 8; ++mt) {
-                res_o[nt][mt][0] = fmaf(acc[nt][mt].x + acc[nt][mt].y, vf, zsum[mt >> 1]);
-                res_o[nt][mt][1] = fmaf(acc[nt][mt].z + acc[nt][mt].w, vf, zsum[mt >> 1]);
+            if (r == 0) {
+                Mw[warp * 8 + h] = mref[nt];
+                Lw[warp * 8 + h] = ls;
             }
-            res_m[nt] = m[nt];
-            res_l[nt] = ls;
         }
-    }
-
-    __syncthreads(); // every stage consumed (or given up): stage memory is free
-    float *Ow = reinterpret_cast<float *>(smem);             // [kConsumers][8][128]
-    float *Mw = Ow + kConsumers * 8 * kD;                    // [kConsumers][8]
-    float *Lw = Mw + kConsumers * 8;                         // [kConsumers][8]
-    if (warp < kConsumers) {
-        const int r = lane >> 2, c = lane & 3;
+        consumers_sync();
+        // ---------------- combine the four warps (fixed order), write the slot
+        const int64_t first_cta = (s * a.main_groups) / a.per;
+        const int slot = (int)(blockIdx.x - first_cta);
+        const bool last = seg_end == (s + 1) * a.main_groups; // this CTA ends stream s
+        const int nslot_s = slot + 1;
+        for (int e = threadIdx.x; e < a.GQ * kD; e += kConsumers * 32) {
+            const int h = e / kD, d = e - h * kD;
+            float M = -INFINITY;
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            const int h = nt * 4 + c;
-            if (h < a.GQ) {
+            for (int w = 0; w < kConsumers; ++w)
+                if (Lw[w * 8 + h] > 0.0f) M = fmaxf(M, Mw[w * 8 + h]);
+            float O = 0.0f, L = 0.0f;
 #pragma unroll
-                for (int mt = 0; mt < 8; ++mt) {
-                    Ow[(warp * 8 + h) * kD + 16 * mt + r] = res_o[nt][mt][0];
-                    Ow[(warp * 8 + h) * kD + 16 * mt + r + 8] = res_o[nt][mt][1];
+            for (int w = 0; w < kConsumers; ++w) {
+                const float lw = Lw[w * 8 + h];
+                if (lw > 0.0f) {
+                    const float fw = exp2f(Mw[w * 8 + h] - M);
+                    O = fmaf(Ow[(w * 8 + h) * kD + d], fw, O);
+                    L = fmaf(lw, fw, L);
                 }
-                if (r == 0) {
-                    Mw[warp * 8 + h] = res_m[nt];
-                    Lw[warp * 8 + h] = res_l[nt];
+            }
+            const int64_t row = rbase + (int64_t)b * a.Hq + kvh * a.GQ + h;
+            float *po = a.part_o + row * a.parts * kD;
+            float *pml = a.part_ml + row * a.parts * 2;
+            po[slot * kD + d] = O;
+            if (d == 0) {
+                // the merge works in natural-log units
+                pml[slot * 2 + 0] = M * 0.6931471805599453f;
+                pml[slot * 2 + 1] = L;
+            }
+            if (last) {
+                // slots no CTA writes for this stream hold empty states
+                for (int sl = nslot_s; sl < a.nslots; ++sl) {
+                    po[sl * kD + d] = 0.0f;
+                    if (d == 0) {
+                        pml[sl * 2 + 0] = -INFINITY;
+                        pml[sl * 2 + 1] = 0.0f;
+                    }
                 }
             }
         }
-    }
-    __syncthreads();
-    for (int e = threadIdx.x; e < a.GQ * kD; e += kTcThreads) {
-        const int h = e / kD, d = e - h * kD;
-        float M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < kConsumers; ++w)
-            if (Lw[w * 8 + h] > 0.0f) M = fmaxf(M, Mw[w * 8 + h]);
-        float O = 0.0f, L = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kConsumers; ++w) {
-            const float lw = Lw[w * 8 + h];
-            if (lw > 0.0f) {
-                const float f = expf(Mw[w * 8 + h] - M);
-                O = fmaf(Ow[(w * 8 + h) * kD + d], f, O);
-                L = fmaf(lw, f, L);
-            }
-        }
-        const int64_t row = (int64_t)b * a.Hq + kvh * a.GQ + h;
-        a.part_o[(row * a.parts + chunk) * kD + d] = O;
-        if (d == 0) {
-            a.part_ml[(row * a.parts + chunk) * 2 + 0] = M;
-            a.part_ml[(row * a.parts + chunk) * 2 + 1] = L;
-        }
+        consumers_sync();
+        i0 += n_seg;
+        f = seg_end;
     }
 }
 
 template <int BITS, int NT> size_t tc_smem() {
     return (size_t)kStages * TcGeom<BITS>::STAGE + 2 * kStages * sizeof(uint64_t) +
-           (size_t)kConsumers * NT * 4 * kPStride * sizeof(float);
+           kStages * sizeof(int2) + (size_t)kConsumers * NT * 4 * kPStride * sizeof(float) +
+           (size_t)kConsumers * 8 * (kD + 2) * sizeof(float);
 }
 
-template <int BITS, int NT> cudaError_t launch_tc(const TcArgs &a, int nstreams, cudaStream_t s) {
-    const size_t smem = tc_smem<BITS, NT>();
-    static bool configured[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<BITS, NT>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        configured[dev] = true;
+template <int BITS, int NT> struct TcKernelInfo {
+    static int resident(int dev) {
+        static int cached[64] = {0};
+        if (dev < 0 || dev >= 64) return 0;
+        if (!cached[dev]) {
+            const size_t smem = tc_smem<BITS, NT>();
+            if (cudaFuncSetAttribute(attn_tc_kernel<BITS, NT>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem) != cudaSuccess)
+                return 0;
+            int per_sm = 0, sms = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn_tc_kernel<BITS, NT>,
+                                                              kTcThreads, smem) != cudaSuccess ||
+                cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+                return 0;
+            cached[dev] = per_sm * sms;
+        }
+        return cached[dev];
     }
-    const int nchunks = (int)((a.main_groups + a.chunk_groups - 1) / a.chunk_groups);
+};
+
+template <int BITS, int NT>
+cudaError_t launch_tc(const TcArgs &a, int nsets, cudaStream_t s) {
+    const int64_t W = (int64_t)a.nstreams * a.main_groups;
+    const int nctas = (int)((W + a.per - 1) / a.per);
     ProfScope prof("attn_tc", s);
-    attn_tc_kernel<BITS, NT><<<dim3((unsigned)nchunks, (unsigned)nstreams), kTcThreads, smem, s>>>(a);
+    const dim3 grid((unsigned)nctas, 1u, (unsigned)nsets);
+    attn_tc_kernel<BITS, NT><<<grid, kTcThreads, tc_smem<BITS, NT>(), s>>>(a);
     count_launch();
     return cudaGetLastError();
 }
@@ -662,11 +706,40 @@ bool attention_tc_supported(const Geom &g, int gq) {
     return g.D == kD && g.G == kG && (g.bits == 2 || g.bits == 4) && gq >= 1 && gq <= 8;
 }
 
-cudaError_t launch_attention_tc(const TcArgs &a, int bits, int nstreams, cudaStream_t s) {
-    if (a.main_groups <= 0) return cudaSuccess;
+cudaError_t plan_attention_tc(int bits, int gq, int64_t nstreams, int64_t main_groups,
+                              int64_t *per, int *nslots) {
+    *per = 0;
+    *nslots = 0;
+    if (nstreams <= 0 || main_groups <= 0) return cudaSuccess;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const bool two = gq > 4;
+    const int res = bits == 2 ? (two ? TcKernelInfo<2, 2>::resident(dev) : TcKernelInfo<2, 1>::resident(dev))
+                              : (two ? TcKernelInfo<4, 2>::resident(dev) : TcKernelInfo<4, 1>::resident(dev));
+    if (res <= 0) return cudaErrorInvalidConfiguration;
+    const int64_t W = nstreams * main_groups;
+    // one wave of resident CTAs, at least kMinGroups groups each
+    constexpr int64_t kMinGroups = 8;
+    int64_t nctas = std::min<int64_t>((int64_t)res * KIVI_TC_WAVES, (W + kMinGroups - 1) / kMinGroups);
+    if (nctas < 1) nctas = 1;
+    const int64_t p = (W + nctas - 1) / nctas;
+    int ms = 0;
+    for (int64_t s = 0; s < nstreams; ++s) {
+        const int64_t f = (s * main_groups) / p, l = ((s + 1) * main_groups - 1) / p;
+        ms = std::max<int>(ms, (int)(l - f + 1));
+    }
+    *per = p;
+    *nslots = ms;
+    return cudaSuccess;
+}
+
+cudaError_t launch_attention_tc(const TcArgs &a, int bits, int nsets, cudaStream_t s) {
+    if (a.main_groups <= 0 || a.nstreams <= 0 || nsets <= 0 || a.per <= 0) return cudaSuccess;
+    if (nsets > 65535) return cudaErrorInvalidValue;
     const bool two = a.GQ > 4;
-    if (bits == 2) return two ? launch_tc<2, 2>(a, nstreams, s) : launch_tc<2, 1>(a, nstreams, s);
-    return two ? launch_tc<4, 2>(a, nstreams, s) : launch_tc<4, 1>(a, nstreams, s);
+    if (bits == 2) return two ? launch_tc<2, 2>(a, nsets, s) : launch_tc<2, 1>(a, nsets, s);
+    return two ? launch_tc<4, 2>(a, nsets, s) : launch_tc<4, 1>(a, nsets, s);
 }
 
 cudaError_t take_tc_error(unsigned int *out) {
@@ -741,11 +814,13 @@ __global__ void __launch_bounds__(kTailThreads) attn_tail_kernel(const TailArgs 
     __shared__ __align__(16) float Qs[8 * 128];
     __shared__ float Ps[8 * kTailTokens];
     const Geom &g = a.g;
-    const int tile = blockIdx.x, s = blockIdx.y;
+    const int tile = blockIdx.x, s = blockIdx.y, z = blockIdx.z;
     const int b = s / a.H, kvh = s - b * a.H;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t rbase = (int64_t)z * a.rows_per_set;
+    const SuffixRef suf = a.suf[z];
     const int64_t t0 = a.main_tokens + (int64_t)tile * kTailTokens;
-    const int nt = (int)max((int64_t)0, min((int64_t)kTailTokens, a.end_tokens - t0));
+    const int nt = (int)max((int64_t)0, min((int64_t)kTailTokens, a.seq_p + suf.len - t0));
 
     const uint32_t *kc = a.st.kcodes + (int64_t)s * code_stride(g, a.st.cap);
     const float2 *kp = a.st.kparams + (int64_t)s * kparam_stride(g, a.st.cap);
@@ -753,11 +828,11 @@ __global__ void __launch_bounds__(kTailThreads) attn_tail_kernel(const TailArgs 
     const float2 *vp = a.st.vparams + (int64_t)s * vparam_stride(g, a.st.cap);
     const float *kres = a.st.kres + (int64_t)s * g.R * g.D;
     const float *vres = a.st.vres + (int64_t)s * g.R * g.D;
-    const float *sk = a.suffix_k ? a.suffix_k + (int64_t)s * a.suffix_cap * g.D : nullptr;
-    const float *sv = a.suffix_v ? a.suffix_v + (int64_t)s * a.suffix_cap * g.D : nullptr;
+    const float *sk = suf.k ? suf.k + (int64_t)s * suf.cap * g.D : nullptr;
+    const float *sv = suf.v ? suf.v + (int64_t)s * suf.cap * g.D : nullptr;
 
     for (int e = threadIdx.x; e < a.GQ * 128; e += kTailThreads)
-        Qs[e] = a.q[((int64_t)b * a.Hq + kvh * a.GQ) * 128 + e];
+        Qs[e] = a.q[(rbase + (int64_t)b * a.Hq + kvh * a.GQ) * 128 + e];
     for (int e = threadIdx.x; e < nt * 32; e += kTailThreads) {
         const int tt = e >> 5, d = (e & 31) * 4;
         const int64_t t = t0 + tt;
@@ -812,7 +887,7 @@ __global__ void __launch_bounds__(kTailThreads) attn_tail_kernel(const TailArgs 
     for (int hh = 0; hh < 2; ++hh) {
         const int h = warp + 4 * hh;
         if (h >= a.GQ) continue;
-        const int64_t row = (int64_t)b * a.Hq + kvh * a.GQ + h;
+        const int64_t row = rbase + (int64_t)b * a.Hq + kvh * a.GQ + h;
         const int slot = a.slot0 + tile;
         float o[4] = {0.f, 0.f, 0.f, 0.f};
         for (int tt = 0; tt < nt; ++tt) {
@@ -900,13 +975,16 @@ __global__ void __launch_bounds__(128) merge_rows_kernel(const float *part_ml, c
 
 } // namespace
 
-cudaError_t launch_attention_tail(const TailArgs &a, int ntiles, int nstreams, cudaStream_t s) {
-    if (ntiles <= 0) return cudaSuccess;
+cudaError_t launch_attention_tail(const TailArgs &a, int ntiles, int nstreams, int nsets,
+                                  cudaStream_t s) {
+    if (ntiles <= 0 || nsets <= 0) return cudaSuccess;
+    if (nsets > kMaxSessionsPerLaunch) return cudaErrorInvalidValue;
     ProfScope prof("attn_tail", s);
+    const dim3 grid((unsigned)ntiles, (unsigned)nstreams, (unsigned)nsets);
     if (a.g.bits == 2)
-        attn_tail_kernel<2><<<dim3((unsigned)ntiles, (unsigned)nstreams), kTailThreads, 0, s>>>(a);
+        attn_tail_kernel<2><<<grid, kTailThreads, 0, s>>>(a);
     else
-        attn_tail_kernel<4><<<dim3((unsigned)ntiles, (unsigned)nstreams), kTailThreads, 0, s>>>(a);
+        attn_tail_kernel<4><<<grid, kTailThreads, 0, s>>>(a);
     count_launch();
     return cudaGetLastError();
 }

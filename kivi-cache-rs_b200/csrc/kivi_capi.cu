@@ -411,10 +411,6 @@ int32_t append_device(KvState &s, const float *dk, const float *dv, uint64_t seq
 // ---------------------------------------------------------------- attention plan
 
 constexpr int64_t kChunkTokens = 256;   // generic kernel: tokens per main chunk
-#ifndef KIVI_TC_CHUNK_GROUPS
-#define KIVI_TC_CHUNK_GROUPS 64
-#endif
-constexpr int kTcChunkGroups = KIVI_TC_CHUNK_GROUPS; // tensor-core kernel: 32-token groups per CTA
 constexpr int64_t kTailTile = 32;       // prefix-tail tokens per CTA
 
 struct SessionView {
@@ -432,81 +428,95 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
     const Geom &g = p.g;
     const uint64_t Gq = Hq / p.H;
     const bool tc = kivi::attention_tc_supported(g, (int)Gq);
-    if (tc && nsess > 1) {
-        // The tensor-core kernel evaluates one query set; run each session on
-        // its own so that every session's result is bit-identical to its
-        // single-session attention.
-        const uint64_t rows1 = p.B * Hq;
-        for (uint64_t i = 0; i < nsess; ++i) {
-            int32_t rc = run_attention(p, sv + i, 1, d_q + i * rows1 * p.D, Hq, scale,
-                                       d_out + i * rows1 * p.D, d_m ? d_m + i * rows1 : nullptr,
-                                       d_l ? d_l + i * rows1 : nullptr, scratch, stream, err);
-            if (rc) return rc;
-        }
-        return KIVI_OK;
-    }
     if (tc) {
-        // Tensor-core main region + dense tail tiles + one-warp-per-row merge.
+        // Tensor-core main region + dense tail tiles + per-row merge.  Up to
+        // kMaxSessionsPerLaunch query sets (sessions of one prefix) share each
+        // launch; every set runs exactly the kernels and partial-slot layout of
+        // a single-set call (tail tiles past a set's end hold empty states,
+        // which the merge skips), so batched results equal per-session ones
+        // bit for bit.
         const uint64_t G = p.cfg.group_size;
         const uint64_t main_tokens = p.vq / G * G;
         const int64_t main_groups = (int64_t)(main_tokens / G);
-        const int64_t NC = (main_groups + kTcChunkGroups - 1) / kTcChunkGroups;
-        const int64_t slen = sv ? (int64_t)sv[0].len : 0;
-        const int64_t end = (int64_t)p.seq + slen;
-        const int64_t NTT = (end - (int64_t)main_tokens + kTailTile - 1) / kTailTile;
-        const int parts = (int)(NC + NTT);
-        const uint64_t rows = p.B * Hq;
-        // part_o is read as float4: keep its offset 256-byte aligned
-        const size_t ml_bytes = (rows * parts * 2 * sizeof(float) + 255) / 256 * 256;
-        const size_t o_bytes = rows * parts * p.D * sizeof(float);
-        CUDA_TRY(scratch.ensure(ml_bytes + o_bytes), "attention scratch");
-        float *part_ml = scratch.as<float>(), *part_o = scratch.as<float>(ml_bytes);
-        if (NC > 0) {
-            kivi::TcArgs t{};
-            t.kcodes = p.st.kcodes;
-            t.kparams = p.st.kparams;
-            t.vcodes = p.st.vcodes;
-            t.vparams = p.st.vparams;
-            t.code_stride = kivi::code_stride(g, p.st.cap);
-            t.kp_stride = kivi::kparam_stride(g, p.st.cap);
-            t.vp_stride = kivi::vparam_stride(g, p.st.cap);
-            t.H = (int)p.H;
-            t.Hq = (int)Hq;
-            t.GQ = (int)Gq;
-            t.main_groups = main_groups;
-            t.chunk_groups = kTcChunkGroups;
-            t.q = d_q;
-            t.scale = scale;
-            t.part_ml = part_ml;
-            t.part_o = part_o;
-            t.parts = parts;
-            CUDA_TRY(kivi::launch_attention_tc(t, (int)p.cfg.bits, (int)(p.B * p.H), stream),
-                     "attention (tensor cores)");
+        int64_t per = 0;
+        int nslots = 0;
+        CUDA_TRY(kivi::plan_attention_tc((int)p.cfg.bits, (int)Gq, (int64_t)(p.B * p.H),
+                                         main_groups, &per, &nslots),
+                 "attention plan");
+        const int64_t NC = nslots;
+        const uint64_t rows1 = p.B * Hq;
+        for (uint64_t s0 = 0; s0 < nsess; s0 += kivi::kMaxSessionsPerLaunch) {
+            const uint64_t ns = std::min<uint64_t>(kivi::kMaxSessionsPerLaunch, nsess - s0);
+            int64_t slen_max = 0;
+            for (uint64_t i = 0; i < ns; ++i)
+                if (sv) slen_max = std::max<int64_t>(slen_max, (int64_t)sv[s0 + i].len);
+            const int64_t end = (int64_t)p.seq + slen_max;
+            const int64_t NTT = (end - (int64_t)main_tokens + kTailTile - 1) / kTailTile;
+            const int parts = (int)(NC + NTT);
+            const uint64_t rows = ns * rows1;
+            // part_o is read as float4: keep its offset 256-byte aligned
+            const size_t ml_bytes = (rows * parts * 2 * sizeof(float) + 255) / 256 * 256;
+            const size_t o_bytes = rows * parts * p.D * sizeof(float);
+            CUDA_TRY(scratch.ensure(ml_bytes + o_bytes), "attention scratch");
+            float *part_ml = scratch.as<float>(), *part_o = scratch.as<float>(ml_bytes);
+            const float *q = d_q + s0 * rows1 * p.D;
+            if (NC > 0) {
+                kivi::TcArgs t{};
+                t.kcodes = p.st.kcodes;
+                t.kparams = p.st.kparams;
+                t.vcodes = p.st.vcodes;
+                t.vparams = p.st.vparams;
+                t.code_stride = kivi::code_stride(g, p.st.cap);
+                t.kp_stride = kivi::kparam_stride(g, p.st.cap);
+                t.vp_stride = kivi::vparam_stride(g, p.st.cap);
+                t.H = (int)p.H;
+                t.Hq = (int)Hq;
+                t.GQ = (int)Gq;
+                t.nstreams = (int64_t)(p.B * p.H);
+                t.main_groups = main_groups;
+                t.per = per;
+                t.nslots = nslots;
+                t.q = q;
+                t.scale = scale;
+                t.part_ml = part_ml;
+                t.part_o = part_o;
+                t.parts = parts;
+                t.rows_per_set = (int64_t)rows1;
+                CUDA_TRY(kivi::launch_attention_tc(t, (int)p.cfg.bits, (int)ns, stream),
+                         "attention (tensor cores)");
+            }
+            kivi::TailArgs ta{};
+            ta.g = g;
+            ta.st = p.st;
+            ta.H = (int)p.H;
+            ta.Hq = (int)Hq;
+            ta.GQ = (int)Gq;
+            ta.kq = (int64_t)p.kq;
+            ta.vq = (int64_t)p.vq;
+            ta.seq_p = (int64_t)p.seq;
+            ta.vhead = (int)p.vhead;
+            ta.main_tokens = (int64_t)main_tokens;
+            ta.q = q;
+            ta.scale = scale;
+            ta.part_ml = part_ml;
+            ta.part_o = part_o;
+            ta.parts = parts;
+            ta.slot0 = (int)NC;
+            ta.rows_per_set = (int64_t)rows1;
+            for (uint64_t i = 0; i < ns; ++i) {
+                ta.suf[i].k = sv ? sv[s0 + i].k : nullptr;
+                ta.suf[i].v = sv ? sv[s0 + i].v : nullptr;
+                ta.suf[i].len = sv ? (int64_t)sv[s0 + i].len : 0;
+                ta.suf[i].cap = sv ? (int64_t)sv[s0 + i].cap : 0;
+            }
+            CUDA_TRY(kivi::launch_attention_tail(ta, (int)NTT, (int)(p.B * p.H), (int)ns, stream),
+                     "attention tail");
+            const uint64_t off = s0 * rows1;
+            CUDA_TRY(kivi::launch_merge_rows(part_ml, part_o, parts, (int64_t)rows,
+                                             d_out + off * p.D, d_m ? d_m + off : nullptr,
+                                             d_l ? d_l + off : nullptr, stream),
+                     "attention merge");
         }
-        kivi::TailArgs ta{};
-        ta.g = g;
-        ta.st = p.st;
-        ta.H = (int)p.H;
-        ta.Hq = (int)Hq;
-        ta.GQ = (int)Gq;
-        ta.kq = (int64_t)p.kq;
-        ta.vq = (int64_t)p.vq;
-        ta.seq_p = (int64_t)p.seq;
-        ta.vhead = (int)p.vhead;
-        ta.main_tokens = (int64_t)main_tokens;
-        ta.end_tokens = end;
-        ta.suffix_k = sv ? sv[0].k : nullptr;
-        ta.suffix_v = sv ? sv[0].v : nullptr;
-        ta.suffix_cap = sv ? (int64_t)sv[0].cap : 0;
-        ta.q = d_q;
-        ta.scale = scale;
-        ta.part_ml = part_ml;
-        ta.part_o = part_o;
-        ta.parts = parts;
-        ta.slot0 = (int)NC;
-        CUDA_TRY(kivi::launch_attention_tail(ta, (int)NTT, (int)(p.B * p.H), stream), "attention tail");
-        CUDA_TRY(kivi::launch_merge_rows(part_ml, part_o, parts, (int64_t)rows, d_out, d_m, d_l, stream),
-                 "attention merge");
         return KIVI_OK;
     }
     const int maxrows = kivi::attention_max_rows((int)p.D);

@@ -164,7 +164,14 @@ cudaError_t launch_merge_shards(const float *m, const float *l, const float *o, 
                                 int64_t rows, int D, int64_t ml_stride, int64_t o_stride,
                                 float *out, cudaStream_t s);
 // Tensor-core attention over the packed main region (kivi_attention_tc.cu):
-// head_dim 128, group 32, 2/4-bit, <= 8 query heads per kv head, one query set.
+// head_dim 128, group 32, 2/4-bit, <= 8 query heads per kv head.  The main
+// regions of all streams (main_groups 32-token groups each) form one flat
+// stream-major sequence; CTA i takes groups [i*per, (i+1)*per) and writes one
+// partial slot per stream it touches (slot i - first CTA of that stream);
+// slots 0..nslots-1 of every row are written (empty states where no CTA has
+// one).  Several query sets (sessions of one shared prefix) run in one
+// launch, one per blockIdx.z: set z's query rows and partial slots follow
+// set z-1's.
 struct TcArgs {
     const uint32_t *kcodes;
     const float2 *kparams;
@@ -172,38 +179,49 @@ struct TcArgs {
     const float2 *vparams;
     int64_t code_stride, kp_stride, vp_stride; // per-stream strides (elements)
     int H, Hq, GQ;
-    int64_t main_groups; // 32-token groups with packed K and V
-    int chunk_groups;    // groups per CTA (partial slot = chunk index)
-    const float *q;      // [B][Hq][128]
+    int64_t nstreams;     // B * H
+    int64_t main_groups;  // 32-token groups with packed K and V, per stream
+    int64_t per;          // groups per CTA (plan_attention_tc)
+    int nslots;           // partial slots per row taken by this kernel
+    const float *q;       // [sets][B][Hq][128]
     float scale;
-    float *part_ml;
-    float *part_o;
+    float *part_ml;       // [sets][B*Hq][parts][2]
+    float *part_o;        // [sets][B*Hq][parts][128]
     int parts;
+    int64_t rows_per_set; // B * Hq
 };
-// Dense tail of the tensor-core path: tokens [main_tokens, end_tokens) of each
-// stream (partial group, fp32 window/residual, one session's fp32 suffix),
-// 32 tokens per CTA, partial slots slot0 + tile.  head_dim 128, <= 8 q heads
-// per kv head.
+// Dense tail of the tensor-core path: tokens [main_tokens, seq_p + suf[z].len)
+// of each stream (partial group, fp32 window/residual, session z's fp32
+// suffix), 32 tokens per CTA, partial slots slot0 + tile; query set z =
+// blockIdx.z as in TcArgs.  Tiles past a set's end write empty states
+// (m = -inf, l = 0, o = 0).  head_dim 128, <= 8 q heads per kv head.
 struct TailArgs {
     Geom g;
     Store st;
     int H, Hq, GQ;
     int64_t kq, vq, seq_p;
     int vhead;
-    int64_t main_tokens, end_tokens;
-    const float *suffix_k, *suffix_v; // [stream][suffix_cap][128] or null
-    int64_t suffix_cap;
+    int64_t main_tokens;
     const float *q;
     float scale;
     float *part_ml, *part_o;
     int parts, slot0;
+    int64_t rows_per_set;
+    SuffixRef suf[kMaxSessionsPerLaunch]; // per set; k/v null and len 0 without suffix
 };
-cudaError_t launch_attention_tail(const TailArgs &a, int ntiles, int nstreams, cudaStream_t s);
+cudaError_t launch_attention_tail(const TailArgs &a, int ntiles, int nstreams, int nsets,
+                                  cudaStream_t s);
 // One warp per row merge for head_dim 128 (mode: out_m == null -> normalised rows).
 cudaError_t launch_merge_rows(const float *part_ml, const float *part_o, int parts, int64_t rows,
                               float *out, float *out_m, float *out_l, cudaStream_t s);
 bool attention_tc_supported(const Geom &g, int gq);
-cudaError_t launch_attention_tc(const TcArgs &a, int bits, int nstreams, cudaStream_t s);
+// Work split of the tensor-core kernel on the current device: one wave of
+// resident CTAs (fewer when the work is small); a function of the stream count
+// and length only, so every query set and every call on the same cache shape
+// splits identically.
+cudaError_t plan_attention_tc(int bits, int gq, int64_t nstreams, int64_t main_groups,
+                              int64_t *per, int *nslots);
+cudaError_t launch_attention_tc(const TcArgs &a, int bits, int nsets, cudaStream_t s);
 // Reads and clears the flag set when a tensor-core kernel's bounded wait gave up.
 cudaError_t take_tc_error(unsigned int *out);
 
