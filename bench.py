@@ -63,7 +63,7 @@ CONFIGS = {
 }
 
 KERNELS = ("attn_tc", "attn_tail", "attn_chunk", "merge", "merge_shards", "append_small",
-           "key_groups", "value_tokens", "copy_rows")
+           "key_groups", "value_tokens", "copy_rows", "suffix_append")
 
 
 # ---------------------------------------------------------------- helpers
@@ -338,8 +338,9 @@ class DecodeWorkload:
 
 
 class RagWorkload:
-    """Config 3: SharedPrefix + RagSessions (prefix.rs:155-290), all sessions
-    attended by one batched call per step."""
+    """Config 3: SharedPrefix + RagSessions (prefix.rs:155-290); a step appends
+    one token to every session (one batched append) and attends all sessions
+    (one batched attention call)."""
 
     def __init__(self, K, cfgd, rank, local_rank, nsteps, nprof, stream):
         import torch
@@ -380,8 +381,7 @@ class RagWorkload:
         torch.cuda.synchronize()
 
     def _step(self, ks, vs, q):
-        for j, s in enumerate(self.sessions):
-            s.append_dev(ks[j], vs[j], 1, stream=self.stream)
+        self.K.sessions_append_dev(self.sessions, ks, vs, 1, stream=self.stream)
         self.K.sessions_attention_batched_dev(self.sessions, q, self.Hq, self.scale, self.dout,
                                               stream=self.stream)
 
@@ -411,7 +411,7 @@ class RagWorkload:
         if rc:
             raise K.KiviError(err.code, err.a, err.b, None, err.message.decode())
 
-    e2e_api = ("kivi_session_append x sessions + kivi_sessions_attention_batched "
+    e2e_api = ("kivi_session_append per session + kivi_sessions_attention_batched "
                "(RagSession::append/attention), pinned host buffers")
 
     def io_bytes(self):
@@ -437,8 +437,8 @@ class RagWorkload:
         c = self.cfgd
         if kernel == "attn_chunk":
             return self.step_bytes()
-        # one tensor-core launch per session: the packed prefix + that session's queries
-        return main_region_bytes(self.prefix, c["B"] * c["H"], c["B"] * c["Hq"], c)
+        # one tensor-core launch for all sessions: the packed prefix once + every query
+        return main_region_bytes(self.prefix, c["B"] * c["H"], self.S * c["B"] * c["Hq"], c)
 
     def config_extra(self, world):
         c = self.cfgd

@@ -296,6 +296,14 @@ int32_t kivi_session_attention_dev(const kivi_session *session, const float *d_q
  * reads the packed prefix once for all of them (no reference counterpart; each
  * session's result equals its own RagSession::attention).
  * queries: [n][batch][num_q_heads][head_dim]; out: same shape. */
+/* RagSession::append (prefix.rs:173-211) of `n` sessions of one prefix in one
+ * launch: session i appends seq_len rows per stream from
+ * d_keys/d_values + i * batch*num_kv_heads*seq_len*head_dim (each block laid
+ * out [batch, num_kv_heads, seq_len, head_dim]).  No counterpart in the
+ * reference, which appends one session at a time. */
+int32_t kivi_sessions_append_dev(kivi_session *const *sessions, uint64_t n, const float *d_keys,
+                                 const float *d_values, uint64_t seq_len, void *stream,
+                                 kivi_error *err);
 int32_t kivi_sessions_attention_batched(const kivi_session *const *sessions, uint64_t n,
                                         const float *queries, uint64_t queries_len,
                                         uint64_t num_q_heads, float scale, float *out,

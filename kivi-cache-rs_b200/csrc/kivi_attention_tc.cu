@@ -8,12 +8,13 @@
 // CTA covers one stream or the end of one and the start of the next, and it
 // emits one partial (m, l, o) slot per stream it touches.
 //
-// Inside a CTA a producer warp streams each group (codes + (scale, zero) of
-// keys and values, the reference's PackedStream order, quant.rs:37-44) from
-// HBM into a ring of shared-memory stages with bulk async copies
-// (cp.async.bulk + mbarrier complete_tx, each copy into this CTA only); four
-// consumer warps each take whole groups and first rewrite the group's
-// parameters in place (scaled scales, folded zero points).
+// Inside a CTA four warps each take every fourth group of the run.  A warp
+// streams its groups (codes + (scale, zero) of keys and values, the
+// reference's PackedStream order, quant.rs:37-44) from HBM into its own
+// shared-memory stages with bulk async copies (cp.async.bulk + mbarrier
+// complete_tx, each copy into this CTA only), one group ahead of the one it
+// computes, and first rewrites each landed group's parameters in place
+// (scaled scales, folded zero points).
 //
 // Per group, with mid = 2^(bits-1) (an integer, so every constant below is an
 // exact fp16), the dequantize-and-dot of attention.rs:143-269 is
@@ -59,10 +60,10 @@ namespace {
 #define KIVI_TC_STAGES 8
 #endif
 #ifndef KIVI_TC_MINB1
-#define KIVI_TC_MINB1 3
+#define KIVI_TC_MINB1 4
 #endif
 constexpr int kConsumers = 4;
-constexpr int kTcThreads = (kConsumers + 1) * 32;
+constexpr int kTcThreads = kConsumers * 32;
 constexpr int kStages = KIVI_TC_STAGES; // pipeline depth (groups in flight per CTA)
 #ifndef KIVI_TC_WAVES
 #define KIVI_TC_WAVES 1
@@ -101,10 +102,6 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
                  : "memory");
 }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t done;
     asm volatile(
@@ -138,11 +135,6 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
             "r"(smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
-}
-
-// Named barrier over the four consumer warps (the producer never joins it).
-__device__ __forceinline__ void consumers_sync() {
-    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
 }
 
 __device__ __forceinline__ void mma16816(float4 &d, uint32_t a0, uint32_t a1, uint32_t a2,
@@ -274,17 +266,21 @@ template <int BITS> struct Perm {
 };
 
 // Rewrite of one landed stage's parameters by the warp that consumes it (all
-// 32 lanes; the stage belongs to that warp alone): key (s, z)
-// -> (s * 2^-e_s, z + mid s), value (s, z) -> (s * 2^(3 - e_v), z + mid s);
-// exps = (e_s, e_v).
+// 32 lanes; the stage belongs to that warp alone).  Keys (s, z) per channel ->
+// (s * 2^-e_s, z + mid s) in place.  Values: entry (token t, channel group g)
+// -> s' = s * 2^(3 - e_v), z' = z + mid s, stored per token as two float4
+// halves (s'0, s'1, z'0, z'1) and (s'2, s'3, z'2, z'3), the halves swapped for
+// tokens with bit 3 set so that the consumers' loads of eight tokens
+// (c + 8 par) hit distinct banks.  exps = (e_s, e_v).
 template <int BITS>
 __device__ __forceinline__ void prep_stage(unsigned char *base, int2 *exps, int lane) {
     using TG = TcGeom<BITS>;
     constexpr float kMid = BITS == 2 ? 2.0f : 8.0f;
-    float4 *kp = reinterpret_cast<float4 *>(base + TG::KC_BYTES) + 2 * lane; // channels 4l..4l+3
-    float4 *vp = reinterpret_cast<float4 *>(base + TG::KC_BYTES + TG::KP_BYTES + TG::VC_BYTES) +
-                 2 * lane; // (token, cg) entries 4l..4l+3
-    float4 k0 = kp[0], k1 = kp[1], v0 = vp[0], v1 = vp[1];
+    float4 *kp = reinterpret_cast<float4 *>(base + TG::KC_BYTES);
+    float4 *vp = reinterpret_cast<float4 *>(base + TG::KC_BYTES + TG::KP_BYTES + TG::VC_BYTES);
+    // float4 index l and l + 32 (conflict-free): keys channels 2l, 2l+1 and
+    // 64 + 2l, 65 + 2l; values token l/2 and 16 + l/2, channel groups 2(l&1), +1
+    const float4 k0 = kp[lane], k1 = kp[lane + 32], v0 = vp[lane], v1 = vp[lane + 32];
     float ks = fmaxf(fmaxf(fabsf(k0.x), fabsf(k0.z)), fmaxf(fabsf(k1.x), fabsf(k1.z)));
     float vs = fmaxf(fmaxf(fabsf(v0.x), fabsf(v0.z)), fmaxf(fabsf(v1.x), fabsf(v1.z)));
 #pragma unroll
@@ -294,25 +290,49 @@ __device__ __forceinline__ void prep_stage(unsigned char *base, int2 *exps, int 
     }
     const int es = exp_ceil(ks), ev = exp_ceil(vs);
     const float fk = exp2i(-es), fv = exp2i(3 - ev);
-    kp[0] = make_float4(k0.x * fk, fmaf(kMid, k0.x, k0.y), k0.z * fk, fmaf(kMid, k0.z, k0.w));
-    kp[1] = make_float4(k1.x * fk, fmaf(kMid, k1.x, k1.y), k1.z * fk, fmaf(kMid, k1.z, k1.w));
-    vp[0] = make_float4(v0.x * fv, fmaf(kMid, v0.x, v0.y), v0.z * fv, fmaf(kMid, v0.z, v0.w));
-    vp[1] = make_float4(v1.x * fv, fmaf(kMid, v1.x, v1.y), v1.z * fv, fmaf(kMid, v1.z, v1.w));
+    kp[lane] = make_float4(k0.x * fk, fmaf(kMid, k0.x, k0.y), k0.z * fk, fmaf(kMid, k0.z, k0.w));
+    kp[lane + 32] =
+        make_float4(k1.x * fk, fmaf(kMid, k1.x, k1.y), k1.z * fk, fmaf(kMid, k1.z, k1.w));
+    const int t0 = lane >> 1, h = lane & 1;     // token t0 (bit 3 of t0 and t0 + 16 agree)
+    const int slot = 2 * t0 + (h ^ ((t0 >> 3) & 1));
+    vp[slot] = make_float4(v0.x * fv, v0.z * fv, fmaf(kMid, v0.x, v0.y), fmaf(kMid, v0.z, v0.w));
+    vp[slot + 32] =
+        make_float4(v1.x * fv, v1.z * fv, fmaf(kMid, v1.x, v1.y), fmaf(kMid, v1.z, v1.w));
     if (lane == 0) *exps = make_int2(es, ev);
 }
 
+// Issues the four bulk copies of one group (stream s, group g) into stage dst.
+template <int BITS>
+__device__ __forceinline__ void issue_group(const TcArgs &a, int64_t s, int64_t g,
+                                            unsigned char *dst, uint64_t *bar) {
+    using TG = TcGeom<BITS>;
+    const char *kc = reinterpret_cast<const char *>(a.kcodes + s * a.code_stride);
+    const char *kp = reinterpret_cast<const char *>(a.kparams + s * a.kp_stride);
+    const char *vc = reinterpret_cast<const char *>(a.vcodes + s * a.code_stride);
+    const char *vp = reinterpret_cast<const char *>(a.vparams + s * a.vp_stride);
+    mbar_expect_tx(bar, TG::STAGE);
+    bulk_g2s(dst, kc + g * TG::KC_BYTES, TG::KC_BYTES, bar);
+    bulk_g2s(dst + TG::KC_BYTES, kp + g * TG::KP_BYTES, TG::KP_BYTES, bar);
+    bulk_g2s(dst + TG::KC_BYTES + TG::KP_BYTES, vc + g * TG::VC_BYTES, TG::VC_BYTES, bar);
+    bulk_g2s(dst + TG::KC_BYTES + TG::KP_BYTES + TG::VC_BYTES, vp + g * TG::VP_BYTES,
+             TG::VP_BYTES, bar);
+}
+
+// Four warps, no producer: warp w takes the CTA's groups i = w, w+4, ... and
+// keeps kStages/4 of them in flight in its own stages (i % kStages), issuing
+// the copy of group i + kStages as soon as it has finished group i.
 template <int BITS, int NT>
 __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_tc_kernel(const TcArgs a) {
     using TG = TcGeom<BITS>;
     constexpr int IPC = TG::IPC;
+    constexpr int kHeads = NT * 4;
     extern __shared__ __align__(128) unsigned char smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * TG::STAGE);
-    uint64_t *empty = full + kStages;
-    int2 *gexp = reinterpret_cast<int2 *>(empty + kStages);               // [stage] (e_s, e_v)
-    float *pbuf = reinterpret_cast<float *>(gexp + kStages);              // [warp][NT*4][kPStride]
-    float *Ow = pbuf + kConsumers * NT * 4 * kPStride;                   // [warp][8][128]
-    float *Mw = Ow + kConsumers * 8 * kD;                                // [warp][8]
-    float *Lw = Mw + kConsumers * 8;                                     // [warp][8]
+    int2 *gexp = reinterpret_cast<int2 *>(full + kStages);                // [stage] (e_s, e_v)
+    float *pbuf = reinterpret_cast<float *>(gexp + kStages);              // [warp][kHeads][kPStride]
+    float *Ow = pbuf + kConsumers * kHeads * kPStride;                   // [warp][kHeads][128]
+    float *Mw = Ow + kConsumers * kHeads * kD;                           // [warp][kHeads]
+    float *Lw = Mw + kConsumers * kHeads;                                // [warp][kHeads]
 
     const int64_t rbase = (int64_t)blockIdx.z * a.rows_per_set; // this query set's first row
     const int64_t W = (int64_t)a.nstreams * a.main_groups;
@@ -322,52 +342,29 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kStages; ++i) {
-            mbar_init(&full[i], 1);
-            mbar_init(&empty[i], 1);
-        }
+        for (int i = 0; i < kStages; ++i) mbar_init(&full[i], 1);
         fence_barrier_init();
     }
     __syncthreads();
 
-    if (warp == kConsumers) {
-        // ------------------------------------------------------------ producer
-        if (lane == 0) {
-            // (stream, group) of the next group to issue, advanced without division
-            int64_t cur_s = gb / a.main_groups, cur_g = gb - cur_s * a.main_groups;
-            int issued = 0;
-            for (int i = 0; i < ng; ++i) {
-                const int st = i % kStages;
-                if (i >= kStages && !mbar_wait(&empty[st], ((i / kStages) - 1) & 1, 1u)) break;
-                const char *kc = reinterpret_cast<const char *>(a.kcodes + cur_s * a.code_stride);
-                const char *kp = reinterpret_cast<const char *>(a.kparams + cur_s * a.kp_stride);
-                const char *vc = reinterpret_cast<const char *>(a.vcodes + cur_s * a.code_stride);
-                const char *vp = reinterpret_cast<const char *>(a.vparams + cur_s * a.vp_stride);
-                unsigned char *dst = smem + st * TG::STAGE;
-                mbar_expect_tx(&full[st], TG::STAGE);
-                bulk_g2s(dst, kc + cur_g * TG::KC_BYTES, TG::KC_BYTES, &full[st]);
-                bulk_g2s(dst + TG::KC_BYTES, kp + cur_g * TG::KP_BYTES, TG::KP_BYTES, &full[st]);
-                bulk_g2s(dst + TG::KC_BYTES + TG::KP_BYTES, vc + cur_g * TG::VC_BYTES, TG::VC_BYTES,
-                         &full[st]);
-                bulk_g2s(dst + TG::KC_BYTES + TG::KP_BYTES + TG::VC_BYTES, vp + cur_g * TG::VP_BYTES,
-                         TG::VP_BYTES, &full[st]);
-                issued = i + 1;
-                if (++cur_g == a.main_groups) {
-                    cur_g = 0;
-                    ++cur_s;
-                }
-            }
-            // No copy may still be in flight into this CTA's shared memory at
-            // exit: wait (bounded) for the last phase of every stage used.
-            for (int st = 0; st < kStages && st < issued; ++st) {
-                const int j = st + ((issued - 1 - st) / kStages) * kStages; // last group in stage st
-                mbar_wait(&full[st], (j / kStages) & 1, 4u);
-            }
+    // this warp's next group to issue: CTA-local index, stream and group
+    int nxt = warp;
+    int64_t nx_s = (gb + warp) / a.main_groups, nx_g = gb + warp - nx_s * a.main_groups;
+    auto issue_next = [&]() {
+        if (lane == 0 && nxt < ng) {
+            const int st = nxt % kStages;
+            issue_group<BITS>(a, nx_s, nx_g, smem + st * TG::STAGE, &full[st]);
         }
-        return;
-    }
+        nxt += kConsumers;
+        nx_g += kConsumers;
+        while (nx_g >= a.main_groups && nx_s + 1 < a.nstreams) {
+            nx_g -= a.main_groups;
+            ++nx_s;
+        }
+    };
+#pragma unroll
+    for (int k = 0; k < kStages / kConsumers; ++k) issue_next();
 
-    // ---------------------------------------------------------------- consumers
     const int r = lane >> 2, c = lane & 3;
     const int par = r & 1, hb = r >> 1;
     const Perm<BITS> perm(r);
@@ -377,7 +374,9 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_
     const int vw = c * 4 * IPC + (BITS == 2 ? (r >> 2) : (r >> 1));
     // K position (value tiles) of this lane's logit tokens 4r + j: 2j + koff
     const int koff = 16 * (r >> 2) + ((r & 1) ? 1 : 0) + ((r & 2) ? 8 : 0);
-    float *pw = pbuf + warp * (NT * 4 * kPStride);
+    // value parameter halves of this lane's tokens (see prep_stage)
+    const int vsw = par; // tokens 8par + c (+4) have bit 3 = par
+    float *pw = pbuf + warp * (kHeads * kPStride);
     bool ok = true;
 
     int i0 = 0; // CTA-local index of the segment's first group
@@ -532,8 +531,9 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_
 #pragma unroll
             for (int kk = 0; kk < 2; ++kk) {
                 const int t0 = 16 * kk + 8 * par + c; // own K pair: tokens t0, t0 + 4
-                const float4 e00 = VP4[t0 * 2], e01 = VP4[t0 * 2 + 1];
-                const float4 e10 = VP4[(t0 + 4) * 2], e11 = VP4[(t0 + 4) * 2 + 1];
+                // halves (s'0, s'1, z'0, z'1) and (s'2, s'3, z'2, z'3) of t0 and t0 + 4
+                const float4 e00 = VP4[2 * t0 + vsw], e01 = VP4[2 * t0 + (vsw ^ 1)];
+                const float4 e10 = VP4[2 * t0 + 8 + vsw], e11 = VP4[2 * t0 + 8 + (vsw ^ 1)];
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                     const float2 pp = *reinterpret_cast<const float2 *>(
@@ -541,8 +541,8 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_
 #pragma unroll
                     for (int cg = 0; cg < 4; ++cg) {
                         const float4 a0 = (cg < 2) ? e00 : e01, a1 = (cg < 2) ? e10 : e11;
-                        const float s0 = (cg & 1) ? a0.z : a0.x, z0 = (cg & 1) ? a0.w : a0.y;
-                        const float s1 = (cg & 1) ? a1.z : a1.x, z1 = (cg & 1) ? a1.w : a1.y;
+                        const float s0 = (cg & 1) ? a0.y : a0.x, z0 = (cg & 1) ? a0.w : a0.z;
+                        const float s1 = (cg & 1) ? a1.y : a1.x, z1 = (cg & 1) ? a1.w : a1.z;
                         zv[nt][cg] = fmaf(pp.x, z0, zv[nt][cg]);
                         zv[nt][cg] = fmaf(pp.y, z1, zv[nt][cg]);
                         b_frag(pp.x * s0, pp.y * s1, par, bv[kk][nt][cg][0], bv[kk][nt][cg][1]);
@@ -583,8 +583,11 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_
                     }
                 }
             }
+            // the stage is free: order this warp's reads and rewrites of it
+            // before the bulk copy of its group i + kStages
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[st]);
+            issue_next();
         }
 
         // ---------------- per-warp results of the segment (lane's head nt*4 + c)
@@ -595,7 +598,7 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_
             ls += __shfl_xor_sync(0xffffffffu, ls, 8);
             ls += __shfl_xor_sync(0xffffffffu, ls, 16);
             const int h = nt * 4 + c;
-            float *ow = Ow + (warp * 8 + h) * kD;
+            float *ow = Ow + (warp * kHeads + h) * kD;
 #pragma unroll
             for (int cg = 0; cg < 4; ++cg) {
                 float zt = zv[nt][cg];
@@ -610,29 +613,28 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_
                                 (u1.z + u1.w) + zs);
             }
             if (r == 0) {
-                Mw[warp * 8 + h] = mref[nt];
-                Lw[warp * 8 + h] = ls;
+                Mw[warp * kHeads + h] = mref[nt];
+                Lw[warp * kHeads + h] = ls;
             }
         }
-        consumers_sync();
+        __syncthreads();
         // ---------------- combine the four warps (fixed order), write the slot
         const int64_t first_cta = (s * a.main_groups) / a.per;
         const int slot = (int)(blockIdx.x - first_cta);
         const bool last = seg_end == (s + 1) * a.main_groups; // this CTA ends stream s
-        const int nslot_s = slot + 1;
-        for (int e = threadIdx.x; e < a.GQ * kD; e += kConsumers * 32) {
+        for (int e = threadIdx.x; e < a.GQ * kD; e += kTcThreads) {
             const int h = e / kD, d = e - h * kD;
             float M = -INFINITY;
 #pragma unroll
             for (int w = 0; w < kConsumers; ++w)
-                if (Lw[w * 8 + h] > 0.0f) M = fmaxf(M, Mw[w * 8 + h]);
+                if (Lw[w * kHeads + h] > 0.0f) M = fmaxf(M, Mw[w * kHeads + h]);
             float O = 0.0f, L = 0.0f;
 #pragma unroll
             for (int w = 0; w < kConsumers; ++w) {
-                const float lw = Lw[w * 8 + h];
+                const float lw = Lw[w * kHeads + h];
                 if (lw > 0.0f) {
-                    const float fw = exp2f(Mw[w * 8 + h] - M);
-                    O = fmaf(Ow[(w * 8 + h) * kD + d], fw, O);
+                    const float fw = exp2f(Mw[w * kHeads + h] - M);
+                    O = fmaf(Ow[(w * kHeads + h) * kD + d], fw, O);
                     L = fmaf(lw, fw, L);
                 }
             }
@@ -647,7 +649,7 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_
             }
             if (last) {
                 // slots no CTA writes for this stream hold empty states
-                for (int sl = nslot_s; sl < a.nslots; ++sl) {
+                for (int sl = slot + 1; sl < a.nslots; ++sl) {
                     po[sl * kD + d] = 0.0f;
                     if (d == 0) {
                         pml[sl * 2 + 0] = -INFINITY;
@@ -656,16 +658,25 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_
                 }
             }
         }
-        consumers_sync();
+        __syncthreads();
         i0 += n_seg;
         f = seg_end;
+    }
+
+    // No copy may still be in flight into this CTA's shared memory at exit:
+    // wait (bounded) for this warp's issued groups nobody has waited for
+    // (groups it never reached after a failed wait).
+    if (!ok) {
+        for (int i = warp; i < min(nxt, ng); i += kConsumers) {
+            // only the last kStages/4 issues of the warp can still be pending
+            if (i + kStages >= min(nxt, ng)) mbar_wait(&full[i % kStages], (i / kStages) & 1, 4u);
+        }
     }
 }
 
 template <int BITS, int NT> size_t tc_smem() {
-    return (size_t)kStages * TcGeom<BITS>::STAGE + 2 * kStages * sizeof(uint64_t) +
-           kStages * sizeof(int2) + (size_t)kConsumers * NT * 4 * kPStride * sizeof(float) +
-           (size_t)kConsumers * 8 * (kD + 2) * sizeof(float);
+    return (size_t)kStages * TcGeom<BITS>::STAGE + kStages * (sizeof(uint64_t) + sizeof(int2)) +
+           (size_t)kConsumers * NT * 4 * (kPStride + kD + 2) * sizeof(float);
 }
 
 template <int BITS, int NT> struct TcKernelInfo {

@@ -1222,40 +1222,98 @@ uint64_t kivi_session_question_tokens(const kivi_session *s) { return s ? s->len
 // Copies [n][seq][D] rows (host or device) after the session's suffix; grows
 // the preallocated suffix by doubling (replaces the per-append re-splice of
 // prefix.rs:196-221).
+// Grows a session's suffix buffers (doubling) to hold `extra` more rows.
+static int32_t session_reserve(kivi_session *s, uint64_t extra, cudaStream_t st, kivi_error *err) {
+    const KvState &p = s->prefix->s;
+    const uint64_t n = p.n(), D = p.D;
+    if (s->len + extra <= s->cap) return KIVI_OK;
+    uint64_t cap = s->cap * 2;
+    if (cap < s->len + extra) cap = s->len + extra;
+    if (cap < 64) cap = 64;
+    float *nk = nullptr, *nv = nullptr;
+    cudaError_t e;
+    if ((e = dalloc(&nk, n * cap * D)) != cudaSuccess || (e = dalloc(&nv, n * cap * D)) != cudaSuccess) {
+        dfree(nk);
+        dfree(nv);
+        return cuda_fail(err, e, "session grow");
+    }
+    if (s->len) {
+        CUDA_TRY(cudaMemcpy2DAsync(nk, cap * D * 4, s->k, s->cap * D * 4, s->len * D * 4, n,
+                                   cudaMemcpyDeviceToDevice, st), "session grow copy");
+        CUDA_TRY(cudaMemcpy2DAsync(nv, cap * D * 4, s->v, s->cap * D * 4, s->len * D * 4, n,
+                                   cudaMemcpyDeviceToDevice, st), "session grow copy");
+        CUDA_TRY(cudaStreamSynchronize(st), "session grow");
+    }
+    dfree(s->k);
+    dfree(s->v);
+    s->k = nk;
+    s->v = nv;
+    s->cap = cap;
+    return KIVI_OK;
+}
+
+// RagSession::append (prefix.rs:173-211): host rows by copy, device rows by
+// the suffix-append kernel.
 static int32_t session_append(kivi_session *s, const float *k, const float *v, uint64_t seq,
                               cudaMemcpyKind kind, cudaStream_t st, kivi_error *err) {
     const KvState &p = s->prefix->s;
     const uint64_t n = p.n(), D = p.D;
-    if (s->len + seq > s->cap) {
-        uint64_t cap = s->cap * 2;
-        if (cap < s->len + seq) cap = s->len + seq;
-        if (cap < 64) cap = 64;
-        float *nk = nullptr, *nv = nullptr;
-        cudaError_t e;
-        if ((e = dalloc(&nk, n * cap * D)) != cudaSuccess || (e = dalloc(&nv, n * cap * D)) != cudaSuccess) {
-            dfree(nk);
-            dfree(nv);
-            return cuda_fail(err, e, "session grow");
-        }
-        if (s->len) {
-            CUDA_TRY(cudaMemcpy2DAsync(nk, cap * D * 4, s->k, s->cap * D * 4, s->len * D * 4, n,
-                                       cudaMemcpyDeviceToDevice, st), "session grow copy");
-            CUDA_TRY(cudaMemcpy2DAsync(nv, cap * D * 4, s->v, s->cap * D * 4, s->len * D * 4, n,
-                                       cudaMemcpyDeviceToDevice, st), "session grow copy");
-            CUDA_TRY(cudaStreamSynchronize(st), "session grow");
-        }
-        dfree(s->k);
-        dfree(s->v);
-        s->k = nk;
-        s->v = nv;
-        s->cap = cap;
+    int32_t rc = session_reserve(s, seq, st, err);
+    if (rc) return rc;
+    if (kind == cudaMemcpyDeviceToDevice) {
+        kivi::SuffixAppend sa{};
+        sa.k[0] = s->k;
+        sa.v[0] = s->v;
+        sa.len[0] = (int64_t)s->len;
+        sa.cap[0] = (int64_t)s->cap;
+        CUDA_TRY(kivi::launch_suffix_append(sa, k, v, 1, (int)n, (int64_t)seq, (int)D, st),
+                 "session append");
+    } else {
+        CUDA_TRY(cudaMemcpy2DAsync(s->k + s->len * D, s->cap * D * 4, k, seq * D * 4, seq * D * 4,
+                                   n, kind, st), "session append");
+        CUDA_TRY(cudaMemcpy2DAsync(s->v + s->len * D, s->cap * D * 4, v, seq * D * 4, seq * D * 4,
+                                   n, kind, st), "session append");
     }
-    CUDA_TRY(cudaMemcpy2DAsync(s->k + s->len * D, s->cap * D * 4, k, seq * D * 4, seq * D * 4, n,
-                               kind, st), "session append");
-    CUDA_TRY(cudaMemcpy2DAsync(s->v + s->len * D, s->cap * D * 4, v, seq * D * 4, seq * D * 4, n,
-                               kind, st), "session append");
     s->len += seq;
     return KIVI_OK;
+}
+
+int32_t kivi_sessions_append_dev(kivi_session *const *ss, uint64_t nsess, const float *dk,
+                                 const float *dv, uint64_t seq, void *stream, kivi_error *err) {
+    if (!ss || nsess == 0 || !ss[0]) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "no sessions");
+    if (seq == 0) return set_err(err, KIVI_OK);
+    if (!dk || !dv) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null input");
+    const kivi_prefix *p = ss[0]->prefix;
+    for (uint64_t i = 0; i < nsess; ++i)
+        if (!ss[i] || ss[i]->prefix != p)
+            return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "sessions must share one prefix");
+    const uint64_t n = p->s.n(), D = p->s.D;
+    DeviceGuard dg(p->s.device);
+    cudaStream_t st = pick(stream, ss[0]->stream);
+    for (uint64_t i = 0; i < nsess; ++i) {
+        int32_t rc = session_reserve(ss[i], seq, st, err);
+        if (rc) return rc;
+    }
+    for (uint64_t s0 = 0; s0 < nsess; s0 += kivi::kMaxSessionsPerLaunch) {
+        const uint64_t ns = std::min<uint64_t>(kivi::kMaxSessionsPerLaunch, nsess - s0);
+        kivi::SuffixAppend sa{};
+        for (uint64_t i = 0; i < ns; ++i) {
+            kivi_session *s = ss[s0 + i];
+            sa.k[i] = s->k;
+            sa.v[i] = s->v;
+            sa.len[i] = (int64_t)s->len;
+            sa.cap[i] = (int64_t)s->cap;
+        }
+        const uint64_t off = s0 * n * seq * D;
+        CUDA_TRY(kivi::launch_suffix_append(sa, dk + off, dv + off, (int)ns, (int)n, (int64_t)seq,
+                                            (int)D, st),
+                 "sessions append");
+    }
+    for (uint64_t i = 0; i < nsess; ++i) {
+        ss[i]->len += seq;
+        CUDA_TRY(mark_dev(ss[i]->dev_done, st), "sessions append");
+    }
+    return set_err(err, KIVI_OK);
 }
 
 int32_t kivi_session_append(kivi_session *s, const float *keys, uint64_t keys_len,

@@ -132,6 +132,16 @@ cudaError_t launch_value_tokens(const Geom &g, const Store &st, int n, int nwin,
 // Copy input rows [src_off, src_off+count) of every stream into ring/linear rows:
 // dst slot = (dst_head + dst_off + i) % ring (ring = R for the value window, or
 // a huge number for a linear buffer).
+// Session suffix append: set z of the launch appends `seq` rows per stream from
+// src [sets][nstreams][seq][D] (keys and values) at row len of its buffers.
+struct SuffixAppend {
+    float *k[kMaxSessionsPerLaunch];
+    float *v[kMaxSessionsPerLaunch];
+    int64_t len[kMaxSessionsPerLaunch];
+    int64_t cap[kMaxSessionsPerLaunch];
+};
+cudaError_t launch_suffix_append(const SuffixAppend &a, const float *k, const float *v,
+                                 int nsets, int nstreams, int64_t seq, int D, cudaStream_t s);
 cudaError_t launch_copy_rows(float *dst, int64_t dst_stream_rows, int64_t dst_head,
                              int64_t dst_off, int64_t ring, const float *src, int64_t src_seq,
                              int64_t src_off, int64_t count, int n, int D, cudaStream_t s);

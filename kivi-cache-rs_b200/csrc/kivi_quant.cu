@@ -233,6 +233,17 @@ __global__ void copy_rows_kernel(float *dst, int64_t dst_stream_rows, int64_t ds
     dst[((int64_t)s * dst_stream_rows + slot) * D + d] = src[((int64_t)s * src_seq + src_off + i) * D + d];
 }
 
+__global__ void suffix_append_kernel(const SuffixAppend a, const float *k, const float *v,
+                                     int nstreams, int64_t seq, int D) {
+    const int z = blockIdx.z, s = blockIdx.y;
+    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= seq * D) return;
+    const int64_t src = (((int64_t)z * nstreams + s) * seq) * D + e;
+    const int64_t dst = ((int64_t)s * a.cap[z] + a.len[z]) * D + e;
+    a.k[z][dst] = k[src];
+    a.v[z][dst] = v[src];
+}
+
 // ---------------------------------------------------------------- dequantize
 __device__ __forceinline__ float dq_key(const Geom &g, const uint32_t *kc, const float2 *kp,
                                         int64_t t, int d) {
@@ -318,6 +329,17 @@ cudaError_t launch_value_tokens(const Geom &g, const Store &st, int n, int nwin,
     ProfScope prof("value_tokens", s);
     value_tokens_kernel<<<dim3(blocks_for(ntok * g.nch, 128), n), 128, 0, s>>>(
         g, st, nwin, vhead, in, in_seq, in_off, ntok, out_tok0);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_suffix_append(const SuffixAppend &a, const float *k, const float *v,
+                                 int nsets, int nstreams, int64_t seq, int D, cudaStream_t s) {
+    if (nsets <= 0 || seq <= 0) return cudaSuccess;
+    if (nsets > kMaxSessionsPerLaunch) return cudaErrorInvalidValue;
+    ProfScope prof("suffix_append", s);
+    suffix_append_kernel<<<dim3(blocks_for(seq * D, 256), nstreams, nsets), 256, 0, s>>>(
+        a, k, v, nstreams, seq, D);
     count_launch();
     return cudaGetLastError();
 }

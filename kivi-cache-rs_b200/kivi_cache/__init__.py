@@ -124,6 +124,7 @@ def lib():
         "kivi_cache_attention_partial_dev": ([P, P, sz, f32, P, P, P, P, e], i32),
         "kivi_merge_partials_dev": ([sz, sz, sz, P, P, P, P, P, e], i32),
         "kivi_cache_seal": ([P, e], i32),
+        "kivi_sessions_append_dev": ([P, sz, P, P, sz, P, e], i32),
         "kivi_packed_partials_floats": ([sz, sz], sz),
         "kivi_cache_attention_partial_packed_dev": ([P, P, sz, f32, P, P, e], i32),
         "kivi_merge_packed_partials_dev": ([sz, sz, sz, P, P, P, e], i32),
@@ -601,8 +602,10 @@ class RagSession:
 
 
 def sessions_attention_batched(sessions, queries, num_q_heads, scale):
-    """Attention of every session of one shared prefix in one pass over the
-    packed prefix.  queries: [n, batch, num_q_heads, head_dim] -> same shape."""
+    """Attention of every session of one shared prefix, all sessions in the
+    same kernel launches (up to 64 per launch); each session's result equals
+    its own RagSession.attention bit for bit.
+    queries: [n, batch, num_q_heads, head_dim] -> same shape."""
     n = len(sessions)
     arr = (C.c_void_p * n)(*[s._h for s in sessions])
     q, qp = _f32(queries)
@@ -612,6 +615,16 @@ def sessions_attention_batched(sessions, queries, num_q_heads, scale):
                                                  out.ctypes.data_as(C.POINTER(C.c_float)), q.size,
                                                  C.byref(err)), err)
     return out
+
+
+def sessions_append_dev(sessions, d_keys, d_values, seq_len, stream=None):
+    """RagSession::append of every session in one launch: d_keys/d_values
+    [n, batch, num_kv_heads, seq_len, head_dim] on the device."""
+    n = len(sessions)
+    arr = (C.c_void_p * n)(*[s._h for s in sessions])
+    err = _Err()
+    _check(lib().kivi_sessions_append_dev(arr, n, _ptr(d_keys), _ptr(d_values), seq_len,
+                                          _stream(stream), C.byref(err)), err)
 
 
 def sessions_attention_batched_dev(sessions, d_queries, num_q_heads, scale, d_out, stream=None):
@@ -842,5 +855,5 @@ __all__ = [
     "SharedPrefix", "SharedPrefixFootprint", "RagSession", "RuntimeKv", "QuantAxis",
     "QuantizedTensor", "quantize_per_channel", "quantize_per_token", "layer_kv_bytes",
     "marginal_bytes_per_layer", "AgentMemoryBudget", "sessions_attention_batched",
-    "sessions_attention_batched_dev", "merge_partials_dev", "kernel_launches", "lib", "LIB_PATH",
+    "sessions_attention_batched_dev", "sessions_append_dev", "merge_partials_dev", "kernel_launches", "lib", "LIB_PATH",
 ]

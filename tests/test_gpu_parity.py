@@ -597,6 +597,39 @@ def test_batched_sessions_equal_individual_sessions_bitwise(K):
         assert (batched[i] == s.attention(q[i].reshape(-1), qh, scale)).all(), i
 
 
+def test_batched_session_append_equals_per_session_append(K):
+    """kivi_sessions_append_dev (one launch for all sessions) leaves every
+    session exactly as RagSession::append would (prefix.rs:173-211): same
+    suffix length, bitwise-equal attention afterwards, and the tensor-core
+    batched attention matches the oracle's RagSession::attention."""
+    torch = pytest.importorskip("torch")
+    kv, qh, dim, doc, n = 4, 16, 128, 2100, 6
+    keys, values, _ = synthetic_kv(5, 1, kv, doc, dim)
+    cache, ocache = pair(K, 2, 32, 128, 1, kv, dim)
+    append_both(cache, ocache, keys, values, doc)
+    prefix, oprefix = cache.share_prefix(), ocache.share_prefix()
+    rng = np.random.default_rng(9)
+    batched = [prefix.session() for _ in range(n)]
+    single = [prefix.session() for _ in range(n)]
+    oracle = [oprefix.session() for _ in range(n)]
+    for step, ln in enumerate([3, 1, 1, 40, 1]):
+        k = rng.standard_normal((n, 1, kv, ln, dim), dtype=np.float32)
+        v = rng.standard_normal((n, 1, kv, ln, dim), dtype=np.float32)
+        K.sessions_append_dev(batched, torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda(), ln)
+        torch.cuda.synchronize()
+        for i in range(n):
+            single[i].append(k[i].reshape(-1), v[i].reshape(-1), ln)
+            oracle[i].append(k[i].reshape(-1), v[i].reshape(-1), ln)
+    q = rng.standard_normal((n, 1, qh, dim), dtype=np.float32)
+    scale = np.float32(1.0) / np.sqrt(np.float32(dim))
+    out = K.sessions_attention_batched(batched, q, qh, scale).reshape(n, -1)
+    for i in range(n):
+        assert batched[i].question_tokens() == single[i].question_tokens() == 46
+        assert (out[i] == single[i].attention(q[i].reshape(-1), qh, scale)).all(), i
+        ref = oracle[i].attention(q[i].reshape(-1), qh, scale)
+        assert max_abs(out[i], ref) <= ATOL and rel_l2(out[i], ref) <= RTOL_L2, i
+
+
 # ---------------------------------------------------------------- sequence sharding
 
 
