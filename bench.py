@@ -236,19 +236,28 @@ class DevGen:
         return torch.randn(shape, generator=self.g, device="cuda")
 
 
+PREFILL_MS = [0.0, 0]  # device time of the prefill appends, tokens appended (per process)
+
+
 def prefill(cache, gen, cfgd, n_tokens, stream):
-    """Chunked device appends (appends are chunk-invariant, tests/cache.rs:78-104)."""
+    """Chunked device appends (appends are chunk-invariant, tests/cache.rs:78-104);
+    the appends alone are timed with CUDA events (bulk-append throughput)."""
     import torch
 
     B, H, D = cfgd["B"], cfgd["H"], cfgd["D"]
     chunk = max(cfgd["R"], min(n_tokens, (1 << 25) // (B * H * D)))
     done = 0
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     while done < n_tokens:
         n = min(chunk, n_tokens - done)
         dk, dv = gen.tokens(B, H, n, D)
         torch.cuda.synchronize()
+        e0.record(stream)
         cache.append_dev(dk, dv, n, stream=stream)
+        e1.record(stream)
         stream.synchronize()
+        PREFILL_MS[0] += e0.elapsed_time(e1)
+        PREFILL_MS[1] += n * B * H
         done += n
         del dk, dv
 
@@ -687,6 +696,13 @@ def run_gpu(args, cfgd, rank, world, local_rank):
         "gpu_launches": int(launches),
         "clocks": clk.summary(),
     }
+    if PREFILL_MS[0] > 0:
+        # bulk append (prefill) of this rank: stream-tokens/s and fp32 K+V input GB/s
+        result["prefill"] = {
+            "stream_tokens_per_s": PREFILL_MS[1] / (PREFILL_MS[0] / 1e3),
+            "input_gbs": PREFILL_MS[1] * cfgd["D"] * 8 / (PREFILL_MS[0] / 1e3) / 1e9,
+            "ms": PREFILL_MS[0], "chunk_kernel": "key_groups + value_tokens + copy_rows",
+        }
     if mode == "rag":
         c = cfgd
         flops = 4 * c["sessions"] * c["B"] * c["Hq"] * (c["ctx"] + c["suffix"]) * c["D"]

@@ -427,7 +427,8 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
                       Scratch &scratch, cudaStream_t stream, kivi_error *err) {
     const Geom &g = p.g;
     const uint64_t Gq = Hq / p.H;
-    const bool tc = kivi::attention_tc_supported(g, (int)Gq);
+    // the tensor-core kernel reads query rows as float2
+    const bool tc = kivi::attention_tc_supported(g, (int)Gq) && (((uintptr_t)d_q) & 7u) == 0;
     if (tc) {
         // Tensor-core main region + dense tail tiles + per-row merge.  Up to
         // kMaxSessionsPerLaunch query sets (sessions of one prefix) share each

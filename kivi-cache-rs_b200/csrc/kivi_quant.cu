@@ -14,6 +14,7 @@
 //     (quant.rs:404-406).
 // No --use_fast_math anywhere in this library.
 #include <math.h>
+#include <stdint.h>
 
 #include "kivi_internal.cuh"
 
@@ -69,10 +70,49 @@ __device__ __forceinline__ void quant_key_channel(const Geom &g, const float *co
     }
 }
 
+// Per-token value quantization of one 32-channel group (BITS known at
+// compile time): the group is read as eight float4 (callers check the row is
+// 16-byte aligned), same arithmetic as the generic loop below.
+template <int BITS>
+__device__ __forceinline__ void quant_value_g32(const float *grp, uint32_t *words, float2 *param) {
+    constexpr int TPW = 32 / BITS, IPC = BITS;
+    constexpr float kLevels = (float)((1u << BITS) - 1u);
+    const float4 *grp4 = reinterpret_cast<const float4 *>(grp);
+    float x[32];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 v = grp4[i];
+        x[4 * i] = v.x;
+        x[4 * i + 1] = v.y;
+        x[4 * i + 2] = v.z;
+        x[4 * i + 3] = v.w;
+    }
+    float mn = INFINITY, mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        mn = fminf(mn, x[i]);
+        mx = fmaxf(mx, x[i]);
+    }
+    const float scale = scale_of(__fsub_rn(mx, mn), kLevels);
+    *param = make_float2(scale, mn);
+#pragma unroll
+    for (int w = 0; w < IPC; ++w) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int k = 0; k < TPW; ++k) word |= quant_code(x[w * TPW + k], mn, scale, kLevels) << (k * BITS);
+        words[w] = word;
+    }
+}
+
 // Per-token value quantization of channel group `cg` of one token row.
 // quant.rs:349-374.
 __device__ __forceinline__ void quant_value_group(const Geom &g, const float *row, int cg,
                                                   uint32_t *words, float2 *param) {
+    if (g.G == 32 && (reinterpret_cast<uintptr_t>(row) & 15u) == 0) {
+        if (g.bits == 2) return quant_value_g32<2>(row + cg * 32, words, param);
+        if (g.bits == 4) return quant_value_g32<4>(row + cg * 32, words, param);
+        if (g.bits == 8) return quant_value_g32<8>(row + cg * 32, words, param);
+    }
     const float *grp = row + cg * g.G;
     float mn = INFINITY, mx = -INFINITY;
 #pragma unroll 8

@@ -630,6 +630,41 @@ def test_batched_session_append_equals_per_session_append(K):
         assert max_abs(out[i], ref) <= ATOL and rel_l2(out[i], ref) <= RTOL_L2, i
 
 
+def test_unaligned_device_inputs(K):
+    """Device inputs at 4-byte (not 16-byte) offsets take the scalar paths and
+    give the same bits as aligned ones (append) and the same attention."""
+    torch = pytest.importorskip("torch")
+    kv, qh, dim, n = 2, 8, 128, 300
+    keys, values, _ = synthetic_kv(21, 1, kv, n, dim)
+    q = np.random.default_rng(4).standard_normal(qh * dim, dtype=np.float32)
+    scale = float(np.float32(1.0) / np.sqrt(np.float32(dim)))
+    outs = []
+    caches = []
+    for off in (0, 1):
+        bk = torch.zeros(keys.size + 4, device="cuda")
+        bv = torch.zeros(values.size + 4, device="cuda")
+        bq = torch.zeros(q.size + 4, device="cuda")
+        bk[off:off + keys.size] = torch.from_numpy(keys).cuda()
+        bv[off:off + values.size] = torch.from_numpy(values).cuda()
+        bq[off:off + q.size] = torch.from_numpy(q).cuda()
+        c = K.KiviCache(K.KiviConfig(), 1, kv, dim)
+        c.append_dev(bk[off:], bv[off:], n)
+        out = torch.zeros(qh * dim, device="cuda")
+        c.attention_dev(bq[off:], qh, scale, out)
+        torch.cuda.synchronize()
+        outs.append(out.cpu().numpy())
+        caches.append(c)
+    for h in range(kv):
+        for axis in (0, 1):
+            a, b = caches[0].export_stream(h, axis), caches[1].export_stream(h, axis)
+            assert all((x == y).all() for x, y in zip(a, b))
+    o = O.KiviCache(O.KiviConfig(), 1, kv, dim)
+    o.append(keys, values, n)
+    ref = o.attention(q, qh, np.float32(scale))
+    for got in outs:
+        assert max_abs(got, ref) <= ATOL and rel_l2(got, ref) <= RTOL_L2
+
+
 # ---------------------------------------------------------------- sequence sharding
 
 
