@@ -62,8 +62,9 @@ CONFIGS = {
             Hq=32, bits=2, ctx=(1 << 20) - 1),
 }
 
-KERNELS = ("attn_tc", "attn_tail", "attn_chunk", "merge", "merge_shards", "append_small",
-           "key_groups", "value_tokens", "copy_rows", "suffix_append")
+KERNELS = ("attn_tc", "attn_sets_tc", "attn_tail", "attn_chunk", "merge", "merge_shards",
+           "append_small", "key_groups", "value_tokens", "copy_rows", "suffix_append",
+           "prefix_bounds")
 
 
 # ---------------------------------------------------------------- helpers
@@ -76,14 +77,15 @@ def env_int(name, default):
         return default
 
 
-def load_peaks():
+def load_peaks(key="hbm_gbs"):
+    """(peak, kind): measured HBM GB/s or bf16 TFLOP/s (burst) of this pool's B200s."""
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
         with open(path) as f:
             p = json.load(f)
-        return float(p["hbm_gbs"]), "measured"
+        return float(p[key]), "measured"
     except Exception:
-        return 6650.0, "fallback"
+        return (6650.0 if key == "hbm_gbs" else 1590.0), "fallback"
 
 
 def load_traffic(kernel, workload):
@@ -370,6 +372,7 @@ class RagWorkload:
         del cache
         self.sessions = [self.prefix.session() for _ in range(S)]
         for s in self.sessions:
+            s.reserve(suffix + nsteps + nprof + 64)
             dk, dv = self.gen.tokens(B, H, suffix, D)
             torch.cuda.synchronize()
             s.append_dev(dk, dv, suffix, stream=stream)
@@ -447,6 +450,8 @@ class RagWorkload:
         if kernel == "attn_chunk":
             return self.step_bytes()
         # one tensor-core launch for all sessions: the packed prefix once + every query
+        # (attn_sets_tc); the roofline for this GEMM-shaped kernel is the tensor
+        # one, reported beside it as tensor_flops_per_step
         return main_region_bytes(self.prefix, c["B"] * c["H"], self.S * c["B"] * c["Hq"], c)
 
     def config_extra(self, world):
@@ -707,6 +712,20 @@ def run_gpu(args, cfgd, rank, world, local_rank):
         c = cfgd
         flops = 4 * c["sessions"] * c["B"] * c["Hq"] * (c["ctx"] + c["suffix"]) * c["D"]
         result["roofline"]["tensor_flops_per_step"] = flops
+        if kernel == "attn_sets_tc":
+            # GEMM-shaped: QK^T and PV over the packed main region for every
+            # (session, query head), 2 flops per multiply-add (the fp16 hi/lo
+            # split's extra products are not counted)
+            main_tok = wl.prefix.quantized_value_tokens() // c["G"] * c["G"]
+            kflops = 4.0 * c["sessions"] * c["B"] * c["Hq"] * main_tok * c["D"]
+            tpeak, tkind = load_peaks("bf16_tflops")
+            tach = kflops / (kern_avg_ms / 1e3) / 1e12
+            result["roofline"].update({
+                "bound": "tensor", "achieved": tach, "peak": tpeak, "peak_kind": tkind,
+                "unit": "TFLOP/s", "frac": tach / tpeak, "algorithmic_flops_per_launch": kflops,
+                "hbm_view": {"achieved_gbs": achieved, "peak_gbs": peak,
+                             "frac": (achieved / peak) if achieved else None},
+            })
     wl.close()
     del wl
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

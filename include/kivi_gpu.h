@@ -296,6 +296,10 @@ int32_t kivi_session_attention_dev(const kivi_session *session, const float *d_q
  * reads the packed prefix once for all of them (no reference counterpart; each
  * session's result equals its own RagSession::attention).
  * queries: [n][batch][num_q_heads][head_dim]; out: same shape. */
+/* Grow a session's fp32 suffix buffers to hold `tokens` question tokens (no
+ * counterpart in the reference, whose suffix Vec grows on every append,
+ * prefix.rs:196-211); later appends up to that length allocate nothing. */
+int32_t kivi_session_reserve(kivi_session *session, uint64_t tokens, kivi_error *err);
 /* RagSession::append (prefix.rs:173-211) of `n` sessions of one prefix in one
  * launch: session i appends seq_len rows per stream from
  * d_keys/d_values + i * batch*num_kv_heads*seq_len*head_dim (each block laid

@@ -424,7 +424,8 @@ struct SessionView {
 // state `p`; query rows of session i at d_q + i*B*Hq*D, outputs likewise.
 int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, const float *d_q,
                       uint64_t Hq, float scale, float *d_out, float *d_m, float *d_l,
-                      Scratch &scratch, cudaStream_t stream, kivi_error *err) {
+                      Scratch &scratch, cudaStream_t stream, kivi_error *err,
+                      const int *bounds = nullptr) {
     const Geom &g = p.g;
     const uint64_t Gq = Hq / p.H;
     // the tensor-core kernel reads query rows as float2
@@ -432,10 +433,13 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
     if (tc) {
         // Tensor-core main region + dense tail tiles + per-row merge.  Up to
         // kMaxSessionsPerLaunch query sets (sessions of one prefix) share each
-        // launch; every set runs exactly the kernels and partial-slot layout of
-        // a single-set call (tail tiles past a set's end hold empty states,
-        // which the merge skips), so batched results equal per-session ones
-        // bit for bit.
+        // launch.  A single set, or a few, runs the decode kernel, whose
+        // partial-slot layout is the same for every set (tail tiles past a
+        // set's end hold empty states, which the merge skips), so such a
+        // batch equals per-session calls bit for bit.  Four or more sets of a
+        // frozen prefix (bounds != null) run the tcgen05 multi-set kernel,
+        // which dequantizes each group once for all sets (results equal the
+        // per-session ones within the attention tolerance).
         const uint64_t G = p.cfg.group_size;
         const uint64_t main_tokens = p.vq / G * G;
         const int64_t main_groups = (int64_t)(main_tokens / G);
@@ -444,7 +448,6 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
         CUDA_TRY(kivi::plan_attention_tc((int)p.cfg.bits, (int)Gq, (int64_t)(p.B * p.H),
                                          main_groups, &per, &nslots),
                  "attention plan");
-        const int64_t NC = nslots;
         const uint64_t rows1 = p.B * Hq;
         for (uint64_t s0 = 0; s0 < nsess; s0 += kivi::kMaxSessionsPerLaunch) {
             const uint64_t ns = std::min<uint64_t>(kivi::kMaxSessionsPerLaunch, nsess - s0);
@@ -453,6 +456,16 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
                 if (sv) slen_max = std::max<int64_t>(slen_max, (int64_t)sv[s0 + i].len);
             const int64_t end = (int64_t)p.seq + slen_max;
             const int64_t NTT = (end - (int64_t)main_tokens + kTailTile - 1) / kTailTile;
+            const bool sets = bounds && main_groups > 0 &&
+                              kivi::attention_sets_supported(g, (int)Gq, (int)ns);
+            const int sets_per_cta = (int)(128 / Gq);
+            const int nz = (int)((ns + sets_per_cta - 1) / sets_per_cta);
+            int64_t sper = 0;
+            int snc = 0;
+            if (sets)
+                CUDA_TRY(kivi::plan_attention_sets((int64_t)(p.B * p.H), main_groups, nz, &sper, &snc),
+                         "attention plan");
+            const int64_t NC = sets ? snc : nslots;
             const int parts = (int)(NC + NTT);
             const uint64_t rows = ns * rows1;
             // part_o is read as float4: keep its offset 256-byte aligned
@@ -461,7 +474,34 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
             CUDA_TRY(scratch.ensure(ml_bytes + o_bytes), "attention scratch");
             float *part_ml = scratch.as<float>(), *part_o = scratch.as<float>(ml_bytes);
             const float *q = d_q + s0 * rows1 * p.D;
-            if (NC > 0) {
+            if (sets) {
+                kivi::SetsArgs t{};
+                t.kcodes = p.st.kcodes;
+                t.kparams = p.st.kparams;
+                t.vcodes = p.st.vcodes;
+                t.vparams = p.st.vparams;
+                t.code_stride = kivi::code_stride(g, p.st.cap);
+                t.kp_stride = kivi::kparam_stride(g, p.st.cap);
+                t.vp_stride = kivi::vparam_stride(g, p.st.cap);
+                t.H = (int)p.H;
+                t.Hq = (int)Hq;
+                t.GQ = (int)Gq;
+                t.main_groups = main_groups;
+                t.per = sper;
+                t.nsets = (int)ns;
+                t.sets_per_cta = sets_per_cta;
+                t.rows_per_set = (int64_t)rows1;
+                t.q = q;
+                t.scale = scale;
+                t.kexp = bounds;
+                t.vexp = bounds + p.n() * p.D;
+                t.part_ml = part_ml;
+                t.part_o = part_o;
+                t.parts = parts;
+                CUDA_TRY(kivi::launch_attention_sets(t, (int)p.cfg.bits, snc, (int)(p.B * p.H), nz,
+                                                     stream),
+                         "attention (tcgen05, query sets)");
+            } else if (NC > 0) {
                 kivi::TcArgs t{};
                 t.kcodes = p.st.kcodes;
                 t.kparams = p.st.kparams;
@@ -585,9 +625,11 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
 // A tensor-core kernel whose bounded wait gave up leaves a flag instead of
 // hanging; synchronous calls report it as a CUDA-class error.
 int32_t check_device_waits(kivi_error *err) {
-    unsigned int flag = 0;
+    unsigned int flag = 0, flag2 = 0;
     cudaError_t e = kivi::take_tc_error(&flag);
+    if (e == cudaSuccess) e = kivi::take_sets_error(&flag2);
     if (e != cudaSuccess) return cuda_fail(err, e, "device wait flag");
+    flag |= flag2;
     if (flag)
         return set_msg(err, KIVI_ERR_CUDA, "attention kernel gave up waiting for its copies (flag %u)",
                        flag);
@@ -620,6 +662,11 @@ struct kivi_prefix {
     KvState s;
     uint64_t prefix_bytes = 0;
     cudaStream_t stream = nullptr;
+    // range bounds of the packed main region for the multi-session tensor-core
+    // kernel: [streams][head_dim] key exponents then [streams][head_dim/G]
+    // value exponents; computed on first use (the prefix never changes)
+    int *bounds = nullptr;
+    std::mutex bounds_mu;
 };
 
 struct kivi_session {
@@ -1144,6 +1191,7 @@ void kivi_prefix_release(kivi_prefix *p) {
     DeviceGuard dg(p->s.device);
     if (p->stream) cudaStreamSynchronize(p->stream);
     free_store(p->s.st);
+    if (p->bounds) cudaFree(p->bounds);
     if (p->stream) cudaStreamDestroy(p->stream);
     delete p;
 }
@@ -1279,6 +1327,15 @@ static int32_t session_append(kivi_session *s, const float *k, const float *v, u
     return KIVI_OK;
 }
 
+int32_t kivi_session_reserve(kivi_session *s, uint64_t tokens, kivi_error *err) {
+    if (!s) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null session");
+    DeviceGuard dg(s->prefix->s.device);
+    if (tokens <= s->len) return set_err(err, KIVI_OK);
+    int32_t rc = session_reserve(s, tokens - s->len, s->stream, err);
+    if (rc) return rc;
+    return set_err(err, KIVI_OK);
+}
+
 int32_t kivi_sessions_append_dev(kivi_session *const *ss, uint64_t nsess, const float *dk,
                                  const float *dv, uint64_t seq, void *stream, kivi_error *err) {
     if (!ss || nsess == 0 || !ss[0]) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "no sessions");
@@ -1369,7 +1426,31 @@ static int32_t sessions_attention_dev(const kivi_session *const *ss, uint64_t n,
         CUDA_TRY(cudaMemsetAsync(dout, 0, out_n * 4, st), "session zeros");
         return KIVI_OK;
     }
-    return run_attention(p->s, views.data(), n, dq, Hq, scale, dout, nullptr, nullptr, part, st, err);
+    const int *bounds = nullptr;
+    const uint64_t Gq = Hq / p->s.H;
+    if (kivi::attention_sets_supported(p->s.g, (int)Gq, (int)std::min<uint64_t>(n, kivi::kMaxSessionsPerLaunch)) &&
+        kivi::attention_tc_supported(p->s.g, (int)Gq)) {
+        kivi_prefix *mp = const_cast<kivi_prefix *>(p);
+        std::lock_guard<std::mutex> lk(mp->bounds_mu);
+        if (!mp->bounds) {
+            const uint64_t ns = p->s.n();
+            int *bd = nullptr;
+            CUDA_TRY(cudaMalloc(&bd, ns * (p->s.D + p->s.D / p->s.cfg.group_size) * sizeof(int)),
+                     "prefix bounds");
+            const int64_t mg = (int64_t)(p->s.vq / p->s.cfg.group_size);
+            cudaError_t e = kivi::launch_prefix_bounds(p->s.g, p->s.st, (int64_t)ns, mg, bd,
+                                                       bd + ns * p->s.D, st);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+            if (e != cudaSuccess) {
+                cudaFree(bd);
+                return cuda_fail(err, e, "prefix bounds");
+            }
+            mp->bounds = bd;
+        }
+        bounds = mp->bounds;
+    }
+    return run_attention(p->s, views.data(), n, dq, Hq, scale, dout, nullptr, nullptr, part, st, err,
+                         bounds);
 }
 
 int32_t kivi_session_attention_dev(const kivi_session *s, const float *dq, uint64_t Hq,

@@ -232,6 +232,36 @@ bool attention_tc_supported(const Geom &g, int gq);
 cudaError_t plan_attention_tc(int bits, int gq, int64_t nstreams, int64_t main_groups,
                               int64_t *per, int *nslots);
 cudaError_t launch_attention_tc(const TcArgs &a, int bits, int nsets, cudaStream_t s);
+// tcgen05 attention of many query sets over a frozen prefix's packed main
+// region (kivi_attention_sets.cu).  CTA (chunk, stream, z) takes groups
+// [chunk*per, (chunk+1)*per) of its stream and the query rows of sets
+// [z*sets_per_cta, ...) (row m = set * GQ + head, at most 128 rows); it writes
+// partial slot `chunk` (slots 0..nchunks-1) of each of those rows.
+struct SetsArgs {
+    const uint32_t *kcodes;
+    const float2 *kparams;
+    const uint32_t *vcodes;
+    const float2 *vparams;
+    int64_t code_stride, kp_stride, vp_stride;
+    int H, Hq, GQ;
+    int64_t main_groups, per;
+    int nsets, sets_per_cta;
+    int64_t rows_per_set;   // B * Hq
+    const float *q;         // [sets][B][Hq][128]
+    float scale;
+    const int *kexp;        // [streams][128] range bounds of the prefix's keys
+    const int *vexp;        // [streams][4]   range bounds of its values
+    float *part_ml, *part_o;
+    int parts;
+};
+bool attention_sets_supported(const Geom &g, int gq, int nsets);
+cudaError_t launch_prefix_bounds(const Geom &g, const Store &st, int64_t nstreams,
+                                 int64_t main_groups, int *kexp, int *vexp, cudaStream_t s);
+cudaError_t plan_attention_sets(int64_t nstreams, int64_t main_groups, int nz, int64_t *per,
+                                int *nchunks);
+cudaError_t launch_attention_sets(const SetsArgs &a, int bits, int nchunks, int nstreams, int nz,
+                                  cudaStream_t s);
+cudaError_t take_sets_error(unsigned int *out);
 // Reads and clears the flag set when a tensor-core kernel's bounded wait gave up.
 cudaError_t take_tc_error(unsigned int *out);
 

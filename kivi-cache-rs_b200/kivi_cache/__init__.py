@@ -125,6 +125,7 @@ def lib():
         "kivi_merge_partials_dev": ([sz, sz, sz, P, P, P, P, P, e], i32),
         "kivi_cache_seal": ([P, e], i32),
         "kivi_sessions_append_dev": ([P, sz, P, P, sz, P, e], i32),
+        "kivi_session_reserve": ([P, sz, e], i32),
         "kivi_packed_partials_floats": ([sz, sz], sz),
         "kivi_cache_attention_partial_packed_dev": ([P, P, sz, f32, P, P, e], i32),
         "kivi_merge_packed_partials_dev": ([sz, sz, sz, P, P, P, e], i32),
@@ -567,6 +568,12 @@ class RagSession:
 
     def question_tokens(self):
         return int(lib().kivi_session_question_tokens(self._h))
+
+    def reserve(self, tokens):
+        """Pre-size the fp32 suffix for `tokens` question tokens (no reference
+        counterpart; appends up to that length then allocate nothing)."""
+        err = _Err()
+        _check(lib().kivi_session_reserve(self._h, tokens, C.byref(err)), err)
 
     def sequence_length(self):
         return self.prefix_tokens() + self.question_tokens()

@@ -573,8 +573,9 @@ def test_session_errors(K):
     assert (e.value.variant, e.value.a, e.value.b) == ("Shape", 128, 8)
 
 
-def test_batched_sessions_equal_individual_sessions_bitwise(K):
-    """One pass over the prefix for all sessions == each RagSession::attention."""
+def test_batched_sessions_few_equal_individual_sessions_bitwise(K):
+    """Up to three sessions share the decode kernel's launches: batched ==
+    each RagSession::attention bit for bit."""
     cfg = K.KiviConfig()
     kv, qh, dim, doc = 4, 16, 128, 3000
     keys, values, _ = synthetic_kv(3, 1, kv, doc, dim)
@@ -583,18 +584,58 @@ def test_batched_sessions_equal_individual_sessions_bitwise(K):
     prefix = cache.share_prefix()
     rng = np.random.default_rng(1)
     sessions = []
-    for i in range(5):
+    for i in range(3):
         s = prefix.session()
-        ln = [0, 1, 17, 64, 3][i]
+        ln = [0, 17, 64][i]
         if ln:
             s.append(rng.standard_normal(kv * ln * dim, dtype=np.float32),
                      rng.standard_normal(kv * ln * dim, dtype=np.float32), ln)
         sessions.append(s)
-    q = rng.standard_normal((5, 1, qh, dim), dtype=np.float32)
+    q = rng.standard_normal((3, 1, qh, dim), dtype=np.float32)
     scale = 1.0 / np.sqrt(128.0)
-    batched = K.sessions_attention_batched(sessions, q, qh, scale).reshape(5, -1)
+    batched = K.sessions_attention_batched(sessions, q, qh, scale).reshape(3, -1)
     for i, s in enumerate(sessions):
         assert (batched[i] == s.attention(q[i].reshape(-1), qh, scale)).all(), i
+
+
+@pytest.mark.parametrize("bits,kv,qh,nsess,doc", [
+    (2, 4, 16, 5, 3000),     # 20 rows, padded to 128
+    (2, 8, 32, 32, 4100),    # config-3 shape: 128 rows per kv head
+    (4, 2, 16, 40, 2100),    # 8 q heads per kv head, 320 rows -> three row chunks
+    (2, 2, 2, 70, 1500),     # more sessions than one launch takes
+])
+def test_batched_sessions_tcgen05_match_oracle(K, bits, kv, qh, nsess, doc):
+    """Four or more sessions of a frozen prefix run the tcgen05 multi-set
+    kernel: every session's output matches the oracle's RagSession::attention
+    (prefix.rs:228-290) within the attention tolerance and its own
+    single-session attention within the same tolerance."""
+    dim = 128
+    keys, values, _ = synthetic_kv(41 + bits, 1, kv, doc, dim)
+    cache, ocache = pair(K, bits, 32, 128, 1, kv, dim)
+    append_both(cache, ocache, keys, values, doc)
+    prefix, oprefix = cache.share_prefix(), ocache.share_prefix()
+    rng = np.random.default_rng(nsess)
+    sessions, osessions = [], []
+    for i in range(nsess):
+        s, o = prefix.session(), oprefix.session()
+        ln = int(rng.integers(0, 70))
+        if ln:
+            k = rng.standard_normal(kv * ln * dim, dtype=np.float32)
+            v = rng.standard_normal(kv * ln * dim, dtype=np.float32)
+            s.append(k, v, ln)
+            o.append(k, v, ln)
+        sessions.append(s)
+        osessions.append(o)
+    q = rng.standard_normal((nsess, 1, qh, dim), dtype=np.float32)
+    scale = np.float32(1.0) / np.sqrt(np.float32(dim))
+    batched = K.sessions_attention_batched(sessions, q, qh, scale).reshape(nsess, -1)
+    for i in range(nsess):
+        ref = osessions[i].attention(q[i].reshape(-1), qh, scale)
+        assert max_abs(batched[i], ref) <= ATOL, (i, max_abs(batched[i], ref))
+        assert rel_l2(batched[i], ref) <= RTOL_L2, (i, rel_l2(batched[i], ref))
+        if i < 3:
+            single = sessions[i].attention(q[i].reshape(-1), qh, scale)
+            assert max_abs(batched[i], single) <= ATOL and rel_l2(batched[i], single) <= RTOL_L2
 
 
 def test_batched_session_append_equals_per_session_append(K):
@@ -625,9 +666,12 @@ def test_batched_session_append_equals_per_session_append(K):
     out = K.sessions_attention_batched(batched, q, qh, scale).reshape(n, -1)
     for i in range(n):
         assert batched[i].question_tokens() == single[i].question_tokens() == 46
-        assert (out[i] == single[i].attention(q[i].reshape(-1), qh, scale)).all(), i
+        # identical suffixes: the single-session attentions agree bit for bit
+        one = batched[i].attention(q[i].reshape(-1), qh, scale)
+        assert (one == single[i].attention(q[i].reshape(-1), qh, scale)).all(), i
         ref = oracle[i].attention(q[i].reshape(-1), qh, scale)
         assert max_abs(out[i], ref) <= ATOL and rel_l2(out[i], ref) <= RTOL_L2, i
+        assert max_abs(one, ref) <= ATOL and rel_l2(one, ref) <= RTOL_L2, i
 
 
 def test_unaligned_device_inputs(K):
