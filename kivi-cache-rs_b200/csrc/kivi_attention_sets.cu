@@ -9,7 +9,7 @@
 //   per CTA: one stream (kv head), one run of its 32-token groups, all query
 //   rows of up to 128/GQ sets (row m = set * GQ + head, padded to 128);
 //   S = Q K^T   tcgen05.mma kind::f16, M = 128 rows, N = 32 tokens, K = 128,
-//               D in tensor memory;
+//               D in tensor memory (three S buffers in flight);
 //   softmax     one thread per row reads its S row from tensor memory;
 //   O += P V    tcgen05.mma kind::f16, M = 128, N = 128 channels, K = 32 tokens,
 //               O accumulated in tensor memory across all the CTA's groups.
@@ -60,17 +60,18 @@ constexpr int kNS = 4;                             // packed-group stages
 constexpr int kD = 128;
 constexpr int kTok = 32;                           // tokens per group = per S tile
 constexpr long long kWait = 2000000000LL;          // ~1 s at B200 clocks
-// tensor-memory columns: S_hh[b] 32b, S_lh[b] 64 + 32b, O_hh 128.., O_lh 256..
+constexpr int kKV = 3; // key/value tiles and S accumulators in flight
+// tensor-memory columns: S_hh[b] 32b, S_lh[b] 96 + 32b, O_hh 192.., O_lh 320..
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kSlh = 64, kOhh = 128, kOlh = 256;
+constexpr uint32_t kSlh = 96, kOhh = 192, kOlh = 320;
 constexpr float kLoScale = 2048.0f, kLoUnscale = 1.0f / 2048.0f;
 constexpr float kLazy2 = 2.0f;                     // log2 headroom of the softmax reference
 
 // shared-memory map (bytes)
 constexpr int kQhi = 0, kQlo = 32768;               // 128 x 128 fp16 each
-constexpr int kKbuf = 65536;                        // [2] x (hi 8 KB, lo 8 KB): 32 tokens x 128
-constexpr int kVbuf = kKbuf + 2 * 16384;            // [2] x (hi, lo): 32 tokens x 128, MN-major
-constexpr int kPbuf = kVbuf + 2 * 16384;            // [2] x (hi, lo): 128 rows x 32 tokens
+constexpr int kKbuf = 65536;                        // [kKV] x (hi 8 KB, lo 8 KB): 128 x 32, MN-major
+constexpr int kVbuf = kKbuf + kKV * 16384;          // [kKV] x (hi, lo): 32 tokens x 128, MN-major
+constexpr int kPbuf = kVbuf + kKV * 16384;          // [2] x (hi, lo): 128 rows x 32 tokens
 constexpr int kStages = kPbuf + 2 * 16384;          // packed groups
 
 template <int BITS> struct SetGeom {
@@ -248,12 +249,13 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
     unsigned char *misc = sm + SG::MISC;
     uint64_t *full = reinterpret_cast<uint64_t *>(misc);       // [kNS]
     uint64_t *empty = full + kNS;                               // [kNS]
-    uint64_t *kv_ready = empty + kNS;                           // [2]
-    uint64_t *s_full = kv_ready + 2;                            // [2]
-    uint64_t *s_free = s_full + 2;                              // [2]
-    uint64_t *p_ready = s_free + 2;                             // [2]
-    uint64_t *pv_done = p_ready + 2;                            // [2]
-    uint64_t *drain = pv_done + 2;                              // [1]
+    uint64_t *kv_ready = empty + kNS;                           // [kKV] tiles written
+    uint64_t *s_full = kv_ready + kKV;                          // [kKV] S computed
+    uint64_t *s_free = s_full + kKV;                            // [kKV] S read
+    uint64_t *pv_kv = s_free + kKV;                             // [kKV] tiles read by PV
+    uint64_t *p_ready = pv_kv + kKV;                            // [2]   P written
+    uint64_t *pv_p = p_ready + 2;                               // [2]   PV done (P free, O current)
+    uint64_t *drain = pv_p + 2;                                 // [1]
     uint64_t *pscaled = drain + 1;                              // [kNS]
     uint32_t *tslot = reinterpret_cast<uint32_t *>(pscaled + kNS);
     int *kexp = reinterpret_cast<int *>(tslot + 1);             // [128]
@@ -276,12 +278,15 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
             bar_init(&empty[i], kConvWarps);
             bar_init(&pscaled[i], kConvWarps);
         }
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < kKV; ++i) {
             bar_init(&kv_ready[i], kConvWarps);
             bar_init(&s_full[i], 1);
             bar_init(&s_free[i], kSoftWarps);
+            bar_init(&pv_kv[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
             bar_init(&p_ready[i], kSoftWarps);
-            bar_init(&pv_done[i], 1);
+            bar_init(&pv_p[i], 1);
         }
         bar_init(drain, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -360,7 +365,7 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
     } else if (warp == kMmaWarp) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            constexpr uint32_t id_qk = idesc_f16(128, kTok, 0);
+            constexpr uint32_t id_qk = idesc_f16(128, kTok, 1);
             constexpr uint32_t id_pv = idesc_f16(128, kD, 1);
             const uint32_t qhi = su32(sm + kQhi), qlo = su32(sm + kQlo);
             bool ok = true;
@@ -369,7 +374,7 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
                 if (!bar_wait(&p_ready[bj], (j >> 1) & 1, 32u)) return false;
                 tc_fence_after();
                 const uint32_t phi = su32(sm + kPbuf + bj * 16384), plo = phi + 8192;
-                const uint32_t vhi = su32(sm + kVbuf + bj * 16384), vlo = vhi + 8192;
+                const uint32_t vhi = su32(sm + kVbuf + (j % kKV) * 16384), vlo = vhi + 8192;
                 const uint32_t pa[3] = {phi, plo, phi}, vb[3] = {vhi, vhi, vlo};
 #pragma unroll
                 for (int pass = 0; pass < 3; ++pass)
@@ -378,13 +383,14 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
                         umma(tbase + (pass == 0 ? kOhh : kOlh), sdesc(pa[pass] + ks * 256, 128, 512),
                              sdesc(vb[pass] + ks * 256, 128, 512), id_pv,
                              (j > 0 || pass == 2 || ks > 0) ? 1u : 0u);
-                umma_commit(&pv_done[bj]);
+                umma_commit(&pv_kv[j % kKV]);
+                umma_commit(&pv_p[bj]);
                 return true;
             };
             for (int g = 0; ok && g < ng; ++g) {
-                const int bg = g & 1;
-                if (!bar_wait(&kv_ready[bg], (g >> 1) & 1, 32u) ||
-                    (g >= 2 && !bar_wait(&s_free[bg], ((g - 2) >> 1) & 1, 32u))) {
+                const int bg = g % kKV;
+                if (!bar_wait(&kv_ready[bg], (g / kKV) & 1, 32u) ||
+                    (g >= kKV && !bar_wait(&s_free[bg], ((g - kKV) / kKV) & 1, 32u))) {
                     ok = false;
                     break;
                 }
@@ -412,9 +418,9 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
         const int ct = threadIdx.x - kSoftWarps * 32; // 0..255
         bool ok = true;
         for (int g = 0; ok && g < ng; ++g) {
-            const int st = g % kNS, bg = g & 1;
+            const int st = g % kNS, bg = g % kKV;
             if (!warp_wait(&full[st], (g / kNS) & 1, 64u) ||
-                (g >= 2 && !warp_wait(&pv_done[bg], ((g - 2) >> 1) & 1, 64u))) {
+                (g >= kKV && !warp_wait(&pv_kv[bg], ((g - kKV) / kKV) & 1, 64u))) {
                 ok = false;
                 break;
             }
@@ -445,21 +451,23 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
             unsigned char *vhi = sm + kVbuf + bg * 16384, *vlo = vhi + 8192;
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
-                // task: token t, 8-channel chunk j (8 tokens x 4 chunks per warp instruction)
                 const int tau = ct + 256 * r;
+                float x[8];
+                {
+                    // keys, MN-major: channel kd, tokens 8 tb .. 8 tb + 7 (one
+                    // word, one (scale, zero)); 8 channels x 4 blocks per warp
+                    const int kd = 8 * (tau >> 5) + (tau & 7), tb = (tau >> 3) & 3;
+                    const int bit0 = 8 * tb * BITS;
+                    const uint32_t w = KC[kd * SG::IPC + (bit0 >> 5)];
+                    const float2 p = KP[kd];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) x[k] = fmaf(code_f(w, (bit0 & 31) + k * BITS, kMask), p.x, p.y);
+                    const int koff = tb * 2048 + (kd >> 3) * 128 + (kd & 7) * 16;
+                    store_split8(x, khi + koff, klo + koff);
+                }
+                // task: token t, 8-channel chunk j (8 tokens x 4 chunks per warp instruction)
                 const int t = (tau & 7) + 8 * ((tau >> 5) & 3);
                 const int j = ((tau >> 3) & 3) + 4 * (tau >> 7);
-                float x[8];
-                // keys: channel words (d, t*BITS/32), code at (t % (32/BITS)) * BITS
-                const int wi = (t * BITS) >> 5, sh = (t % (32 / BITS)) * BITS;
-#pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    const int d = 8 * j + k;
-                    const float2 p = KP[d];
-                    x[k] = fmaf(code_f(KC[d * SG::IPC + wi], sh, kMask), p.x, p.y);
-                }
-                const int koff = (t >> 3) * 2048 + j * 128 + (t & 7) * 16;
-                store_split8(x, khi + koff, klo + koff);
                 // values: word (t, cg, i) holds 32/BITS channels of group cg
                 const int cg = j >> 2;
                 const int cin = (j & 3) * 8;                   // first channel within the group
@@ -485,8 +493,8 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
         float mref = -INFINITY, l = 0.0f;
         bool ok = true;
         for (int g = 0; ok && g < ng; ++g) {
-            const int bg = g & 1;
-            if (!warp_wait(&s_full[bg], (g >> 1) & 1, 128u)) {
+            const int bg = g % kKV, bp = g & 1;
+            if (!warp_wait(&s_full[bg], (g / kKV) & 1, 128u)) {
                 ok = false;
                 break;
             }
@@ -516,7 +524,7 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
                 l *= alpha;
                 if (g >= 1) {
                     // O holds groups < g: wait for PV(g-1), rescale this warp's rows
-                    if (!warp_wait(&pv_done[(g - 1) & 1], ((g - 1) >> 1) & 1, 128u)) {
+                    if (!warp_wait(&pv_p[(g - 1) & 1], ((g - 1) >> 1) & 1, 128u)) {
                         ok = false;
                     } else {
                         tc_fence_after();
@@ -544,11 +552,11 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
             }
             l += psum;
             // P[bg] is free once PV(g-2) has completed
-            if (g >= 2 && !warp_wait(&pv_done[bg], ((g - 2) >> 1) & 1, 128u)) {
+            if (g >= 2 && !warp_wait(&pv_p[bp], ((g - 2) >> 1) & 1, 128u)) {
                 ok = false;
                 break;
             }
-            unsigned char *phi = sm + kPbuf + bg * 16384, *plo = phi + 8192;
+            unsigned char *phi = sm + kPbuf + bp * 16384, *plo = phi + 8192;
 #pragma unroll
             for (int c8 = 0; c8 < 4; ++c8) {
                 const int off = (m >> 3) * 512 + c8 * 128 + (m & 7) * 16;
@@ -557,11 +565,11 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
             proxy_fence();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) bar_arrive(&p_ready[bg]);
+            if (lane == 0) bar_arrive(&p_ready[bp]);
         }
         // ---- epilogue: partial (m, l, o) of this row for slot `chunk`
         bool have = ok && ng > 0;
-        if (have && !warp_wait(&pv_done[(ng - 1) & 1], ((ng - 1) >> 1) & 1, 128u)) have = false;
+        if (have && !warp_wait(&pv_p[(ng - 1) & 1], ((ng - 1) >> 1) & 1, 128u)) have = false;
         tc_fence_after();
         float o[kD];
         if (have) {
