@@ -23,8 +23,9 @@
 // fma(code, scale, zero) (quant.rs:404-406), with (scale, zero) pre-multiplied
 // by 2^-E_d, E_d bounding channel d's |key| over the whole prefix; the query
 // carries 2^(E_d - e_row), e_row bounding its row; values likewise with one
-// bound per channel group; softmax weights enter as p/4 with the reference
-// point moved only when a logit exceeds it by 2 (exp2 units).  All bounds are
+// bound per channel group; softmax weights enter as p * 2^9 <= 2^15 (fp16
+// normal down to p = 2^-23) with the reference point moved only when a logit
+// exceeds it by 6 (exp2 units).  All bounds are
 // powers of two, undone exactly in fp32.
 //
 // Warp roles (448 threads): warps 0-3 softmax and epilogue (thread = row,
@@ -60,12 +61,24 @@ constexpr int kNS = 4;                             // packed-group stages
 constexpr int kD = 128;
 constexpr int kTok = 32;                           // tokens per group = per S tile
 constexpr long long kWait = 2000000000LL;          // ~1 s at B200 clocks
-constexpr int kKV = 3; // key/value tiles and S accumulators in flight
-// tensor-memory columns: S_hh[b] 32b, S_lh[b] 96 + 32b, O_hh 192.., O_lh 320..
+constexpr int kKV = 3; // key/value tiles in flight
+constexpr int kS = 2;  // S accumulators in flight
+#ifndef KIVI_SETS_FLUSH
+#define KIVI_SETS_FLUSH 4
+#endif
+#ifndef KIVI_SETS_LAZY
+#define KIVI_SETS_LAZY 6
+#endif
+constexpr int kFlush = KIVI_SETS_FLUSH; // groups accumulated in O_hh before it is folded into O_tot
+// tensor-memory columns: S_hh[b] 32b, S_lh[b] 64 + 32b, O_hh 128.., O_lh 256..,
+// O_tot 384.. (the MMA's fp32 accumulation truncates; O_hh restarts every
+// kFlush groups and is added to O_tot with round-to-nearest on the CUDA cores)
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kSlh = 96, kOhh = 192, kOlh = 320;
+constexpr uint32_t kSlh = 64, kOhh = 128, kOlh = 256, kOtot = 384;
 constexpr float kLoScale = 2048.0f, kLoUnscale = 1.0f / 2048.0f;
-constexpr float kLazy2 = 2.0f;                     // log2 headroom of the softmax reference
+constexpr int kLazyBits = KIVI_SETS_LAZY;          // log2 headroom of the softmax reference
+constexpr float kLazy2 = (float)kLazyBits;
+constexpr float kPScale = (float)(1 << (15 - kLazyBits)); // p * kPScale <= 2^15
 
 // shared-memory map (bytes)
 constexpr int kQhi = 0, kQlo = 32768;               // 128 x 128 fp16 each
@@ -250,9 +263,9 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
     uint64_t *full = reinterpret_cast<uint64_t *>(misc);       // [kNS]
     uint64_t *empty = full + kNS;                               // [kNS]
     uint64_t *kv_ready = empty + kNS;                           // [kKV] tiles written
-    uint64_t *s_full = kv_ready + kKV;                          // [kKV] S computed
-    uint64_t *s_free = s_full + kKV;                            // [kKV] S read
-    uint64_t *pv_kv = s_free + kKV;                             // [kKV] tiles read by PV
+    uint64_t *s_full = kv_ready + kKV;                          // [kS]  S computed
+    uint64_t *s_free = s_full + kS;                             // [kS]  S read
+    uint64_t *pv_kv = s_free + kS;                              // [kKV] tiles read by PV
     uint64_t *p_ready = pv_kv + kKV;                            // [2]   P written
     uint64_t *pv_p = p_ready + 2;                               // [2]   PV done (P free, O current)
     uint64_t *drain = pv_p + 2;                                 // [1]
@@ -280,9 +293,11 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
         }
         for (int i = 0; i < kKV; ++i) {
             bar_init(&kv_ready[i], kConvWarps);
+            bar_init(&pv_kv[i], 1);
+        }
+        for (int i = 0; i < kS; ++i) {
             bar_init(&s_full[i], 1);
             bar_init(&s_free[i], kSoftWarps);
-            bar_init(&pv_kv[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
             bar_init(&p_ready[i], kSoftWarps);
@@ -333,6 +348,15 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *tslot;
+    if (warp < kSoftWarps) {
+        float z[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) z[i] = 0.0f;
+        const uint32_t lb = tbase + ((uint32_t)(32 * warp) << 16);
+#pragma unroll 1
+        for (int c4 = 0; c4 < 4; ++c4) tmem_st32(lb + kOtot + 32 * c4, z);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+    }
 
     if (warp == kProdWarp) {
         // ------------------------------------------------------------ producer
@@ -382,15 +406,15 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
                     for (int ks = 0; ks < 2; ++ks)
                         umma(tbase + (pass == 0 ? kOhh : kOlh), sdesc(pa[pass] + ks * 256, 128, 512),
                              sdesc(vb[pass] + ks * 256, 128, 512), id_pv,
-                             (j > 0 || pass == 2 || ks > 0) ? 1u : 0u);
+                             (ks > 0 || pass == 2 || (pass == 0 ? j % kFlush != 0 : j > 0)) ? 1u : 0u);
                 umma_commit(&pv_kv[j % kKV]);
                 umma_commit(&pv_p[bj]);
                 return true;
             };
             for (int g = 0; ok && g < ng; ++g) {
-                const int bg = g % kKV;
+                const int bg = g % kKV, bs = g % kS;
                 if (!bar_wait(&kv_ready[bg], (g / kKV) & 1, 32u) ||
-                    (g >= kKV && !bar_wait(&s_free[bg], ((g - kKV) / kKV) & 1, 32u))) {
+                    (g >= kS && !bar_wait(&s_free[bs], ((g - kS) / kS) & 1, 32u))) {
                     ok = false;
                     break;
                 }
@@ -401,11 +425,11 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
                 for (int pass = 0; pass < 3; ++pass)
 #pragma unroll
                     for (int ks = 0; ks < 8; ++ks)
-                        umma(tbase + (pass == 0 ? 0u : kSlh) + 32 * bg,
+                        umma(tbase + (pass == 0 ? 0u : kSlh) + 32 * bs,
                              sdesc(qa[pass] + ks * 256, 128, 2048),
                              sdesc(kb[pass] + ks * 256, 128, 2048), id_qk,
                              (pass == 2 || ks > 0) ? 1u : 0u);
-                umma_commit(&s_full[bg]);
+                umma_commit(&s_full[bs]);
                 if (g >= 1 && !pv(g - 1)) ok = false;
             }
             if (ok && ng >= 1) pv(ng - 1);
@@ -493,8 +517,8 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
         float mref = -INFINITY, l = 0.0f;
         bool ok = true;
         for (int g = 0; ok && g < ng; ++g) {
-            const int bg = g % kKV, bp = g & 1;
-            if (!warp_wait(&s_full[bg], (g / kKV) & 1, 128u)) {
+            const int bg = g % kS, bp = g & 1;
+            if (!warp_wait(&s_full[bg], (g / kS) & 1, 128u)) {
                 ok = false;
                 break;
             }
@@ -517,29 +541,46 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
                 mx = fmaxf(mx, x[i]);
             }
             const bool need = mx > mref + kLazy2;
-            if (__any_sync(0xffffffffu, need)) {
+            const bool flush = g >= 1 && g % kFlush == 0; // PV(g) restarts O_hh
+            const bool rescale = __any_sync(0xffffffffu, need);
+            float alpha = 1.0f;
+            if (rescale) {
                 const float nref = need ? mx : mref;
-                const float alpha = (mref == -INFINITY) ? 0.0f : exp2f(mref - nref);
+                alpha = (mref == -INFINITY) ? 0.0f : exp2f(mref - nref);
                 mref = nref;
                 l *= alpha;
-                if (g >= 1) {
-                    // O holds groups < g: wait for PV(g-1), rescale this warp's rows
-                    if (!warp_wait(&pv_p[(g - 1) & 1], ((g - 1) >> 1) & 1, 128u)) {
-                        ok = false;
-                    } else {
-                        tc_fence_after();
+            }
+            if (g >= 1 && (rescale || flush)) {
+                // O holds groups < g: wait for PV(g-1), then scale and/or fold
+                if (!warp_wait(&pv_p[(g - 1) & 1], ((g - 1) >> 1) & 1, 128u)) {
+                    ok = false;
+                } else {
+                    tc_fence_after();
 #pragma unroll 1
-                        for (int c8 = 0; c8 < 8; ++c8) {
-                            // O_hh then O_lh, 32 columns at a time
-                            const uint32_t col = (c8 < 4 ? kOhh : kOlh) + 32 * (c8 & 3);
-                            float o[32];
-                            tmem_ld32(lane_base + col, o);
+                    for (int c4 = 0; c4 < 4; ++c4) {
+                        float a[32], t[32];
+                        tmem_ld32(lane_base + kOtot + 32 * c4, t);
+                        tmem_ld32(lane_base + kOhh + 32 * c4, a);
+                        if (flush) {
 #pragma unroll
-                            for (int i = 0; i < 32; ++i) o[i] *= alpha;
-                            tmem_st32(lane_base + col, o);
+                            for (int i = 0; i < 32; ++i) t[i] = (t[i] + a[i]) * alpha;
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) {
+                                t[i] *= alpha;
+                                a[i] *= alpha;
+                            }
+                            tmem_st32(lane_base + kOhh + 32 * c4, a);
                         }
-                        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                        tmem_st32(lane_base + kOtot + 32 * c4, t);
+                        if (rescale) {
+                            tmem_ld32(lane_base + kOlh + 32 * c4, a);
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) a[i] *= alpha;
+                            tmem_st32(lane_base + kOlh + 32 * c4, a);
+                        }
                     }
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                 }
             }
             if (!ok) break;
@@ -548,7 +589,7 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
             for (int i = 0; i < 32; ++i) {
                 x[i] = exp2f(x[i] - mref);
                 psum += x[i];
-                x[i] *= 0.25f;
+                x[i] *= kPScale; // <= 2^15, fp16 normal down to p = 2^(kLazyBits - 29)
             }
             l += psum;
             // P[bg] is free once PV(g-2) has completed
@@ -575,11 +616,13 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
         if (have) {
 #pragma unroll
             for (int c4 = 0; c4 < 4; ++c4) {
-                float y[32];
+                float y[32], t[32];
                 tmem_ld32(lane_base + kOhh + 32 * c4, o + 32 * c4);
                 tmem_ld32(lane_base + kOlh + 32 * c4, y);
+                tmem_ld32(lane_base + kOtot + 32 * c4, t);
 #pragma unroll
-                for (int i = 0; i < 32; ++i) o[32 * c4 + i] = fmaf(y[i], kLoUnscale, o[32 * c4 + i]);
+                for (int i = 0; i < 32; ++i)
+                    o[32 * c4 + i] = fmaf(y[i], kLoUnscale, t[i] + o[32 * c4 + i]);
             }
         }
         if (m < rows_valid) {
@@ -588,7 +631,7 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
             float *po = a.part_o + (row * a.parts + chunk) * kD;
             float *pml = a.part_ml + (row * a.parts + chunk) * 2;
             if (have) {
-                for (int d = 0; d < kD; ++d) po[d] = o[d] * exp2i_(2 + vexp[d >> 5]);
+                for (int d = 0; d < kD; ++d) po[d] = o[d] * exp2i_(vexp[d >> 5] - (15 - kLazyBits));
                 pml[0] = mref * 0.6931471805599453f;
                 pml[1] = l;
             } else {

@@ -614,28 +614,33 @@ def test_batched_sessions_tcgen05_match_oracle(K, bits, kv, qh, nsess, doc):
     cache, ocache = pair(K, bits, 32, 128, 1, kv, dim)
     append_both(cache, ocache, keys, values, doc)
     prefix, oprefix = cache.share_prefix(), ocache.share_prefix()
+    pk, pv = ocache.dequantize()  # the prefix exactly as the reference attends it
     rng = np.random.default_rng(nsess)
-    sessions, osessions = [], []
+    sessions, osessions, suffixes = [], [], []
     for i in range(nsess):
         s, o = prefix.session(), oprefix.session()
         ln = int(rng.integers(0, 70))
+        k = rng.standard_normal(kv * ln * dim, dtype=np.float32)
+        v = rng.standard_normal(kv * ln * dim, dtype=np.float32)
         if ln:
-            k = rng.standard_normal(kv * ln * dim, dtype=np.float32)
-            v = rng.standard_normal(kv * ln * dim, dtype=np.float32)
             s.append(k, v, ln)
             o.append(k, v, ln)
         sessions.append(s)
         osessions.append(o)
+        suffixes.append((k, v, ln))
     q = rng.standard_normal((nsess, 1, qh, dim), dtype=np.float32)
     scale = np.float32(1.0) / np.sqrt(np.float32(dim))
     batched = K.sessions_attention_batched(sessions, q, qh, scale).reshape(nsess, -1)
     for i in range(nsess):
+        k, v, ln = suffixes[i]
         ref = osessions[i].attention(q[i].reshape(-1), qh, scale)
-        assert max_abs(batched[i], ref) <= ATOL, (i, max_abs(batched[i], ref))
-        assert rel_l2(batched[i], ref) <= RTOL_L2, (i, rel_l2(batched[i], ref))
+        ref64 = dense_attend(concat_head_major(pk, k, 1, kv, doc, ln, dim),
+                             concat_head_major(pv, v, 1, kv, doc, ln, dim),
+                             q[i].reshape(-1), 1, kv, qh, doc + ln, dim, scale)
+        assert_attention_close(batched[i], ref, ref64)
         if i < 3:
             single = sessions[i].attention(q[i].reshape(-1), qh, scale)
-            assert max_abs(batched[i], single) <= ATOL and rel_l2(batched[i], single) <= RTOL_L2
+            assert_attention_close(single, ref, ref64)
 
 
 def test_batched_session_append_equals_per_session_append(K):
