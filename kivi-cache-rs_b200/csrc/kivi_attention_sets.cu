@@ -57,45 +57,44 @@ constexpr int kConvWarps = 8;
 constexpr int kProdWarp = kSoftWarps + kConvWarps; // 12
 constexpr int kMmaWarp = kProdWarp + 1;            // 13
 constexpr int kSetThreads = (kMmaWarp + 1) * 32;   // 448
-constexpr int kNS = 4;                             // packed-group stages
+#ifndef KIVI_SETS_STAGES2
+#define KIVI_SETS_STAGES2 8
+#endif
 constexpr int kD = 128;
 constexpr int kTok = 32;                           // tokens per group = per S tile
 constexpr long long kWait = 2000000000LL;          // ~1 s at B200 clocks
-constexpr int kKV = 3; // key/value tiles in flight
-constexpr int kS = 2;  // S accumulators in flight
-#ifndef KIVI_SETS_FLUSH
-#define KIVI_SETS_FLUSH 4
-#endif
+constexpr int kTile = 64;   // tokens per S tile (two groups): QK^T runs at N = 64
+constexpr int kKV = 2;      // key/value tiles in flight
+constexpr int kS = 2;       // S / P tensor-memory buffers
 #ifndef KIVI_SETS_LAZY
 #define KIVI_SETS_LAZY 6
 #endif
-constexpr int kFlush = KIVI_SETS_FLUSH; // groups accumulated in O_hh before it is folded into O_tot
-// tensor-memory columns: S_hh[b] 32b, S_lh[b] 64 + 32b, O_hh 128.., O_lh 256..,
-// O_tot 384.. (the MMA's fp32 accumulation truncates; O_hh restarts every
-// kFlush groups and is added to O_tot with round-to-nearest on the CUDA cores)
-constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kSlh = 64, kOhh = 128, kOlh = 256, kOtot = 384;
-constexpr float kLoScale = 2048.0f, kLoUnscale = 1.0f / 2048.0f;
 constexpr int kLazyBits = KIVI_SETS_LAZY;          // log2 headroom of the softmax reference
 constexpr float kLazy2 = (float)kLazyBits;
 constexpr float kPScale = (float)(1 << (15 - kLazyBits)); // p * kPScale <= 2^15
+// tensor-memory columns (fp32 words; fp16 operands two per column):
+// S[b] 64b .. 64b + 63, P[b] 128 + 64b: hi (32 columns) then lo (32), Q_hi 256..319,
+// Q_lo 320..383, O 384..511
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kSc = 0, kP = 128, kQH = 256, kQL = 320, kO = 384;
 
-// shared-memory map (bytes)
-constexpr int kQhi = 0, kQlo = 32768;               // 128 x 128 fp16 each
-constexpr int kKbuf = 65536;                        // [kKV] x (hi 8 KB, lo 8 KB): 128 x 32, MN-major
-constexpr int kVbuf = kKbuf + kKV * 16384;          // [kKV] x (hi, lo): 32 tokens x 128, MN-major
-constexpr int kPbuf = kVbuf + kKV * 16384;          // [2] x (hi, lo): 128 rows x 32 tokens
-constexpr int kStages = kPbuf + 2 * 16384;          // packed groups
+// shared-memory map (bytes): per key/value tile hi and lo parts of 16 KB each
+constexpr int kKbuf = 0;                            // [kKV] x (hi, lo): 128 channels x 64 tokens
+constexpr int kVbuf = kKbuf + kKV * 32768;          // [kKV] x (hi, lo): 64 tokens x 128 channels
+constexpr int kStages = kVbuf + kKV * 32768;        // packed groups
 
 template <int BITS> struct SetGeom {
+    // packed-group stages in flight: as many as shared memory leaves room for
+    static constexpr int NS = KIVI_SETS_STAGES2;
     static constexpr int IPC = BITS;                 // words per channel per key group
     static constexpr int KC = kD * IPC * 4;
     static constexpr int KP = kD * 8;
     static constexpr int VC = kTok * 4 * IPC * 4;
     static constexpr int VP = kTok * 4 * 8;
     static constexpr int STAGE = KC + KP + VC + VP;
-    static constexpr int MISC = kStages + kNS * STAGE;
+    static constexpr int MISC = kStages + NS * STAGE;
     static constexpr int SMEM = MISC + 1024;
+    static_assert(SMEM <= 232448, "shared memory per block");
 };
 
 __device__ __forceinline__ uint32_t su32(const void *p) {
@@ -161,14 +160,6 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int b_mn_major) {
            ((uint32_t)(M >> 4) << 24);
 }
 
-__device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t id,
-                                     uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a), "l"(b), "r"(id), "r"(acc));
-}
-
 __device__ __forceinline__ void umma_commit(uint64_t *b) {
     asm volatile(
         "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(b))
@@ -230,23 +221,43 @@ __device__ __forceinline__ int exp_ceil_(float x) {
     return e == 0 ? -126 : e - 126;
 }
 
-// hi/lo fp16 split of 8 consecutive values -> two 16-byte stores: hi = x
-// truncated to 11 significant bits, lo = (x - hi) * 2^11 (exact, and in the
-// same binade range as hi, so it stays a normal fp16 wherever hi does).
+// hi/lo fp16 split of a pair: hi = x truncated to 11 significant bits,
+// lo = x - hi (exact); packed as fp16x2 (first value in the low half).
+__device__ __forceinline__ void split_pair(float a, float b, uint32_t &hi, uint32_t &lo) {
+    const float ta = __uint_as_float(__float_as_uint(a) & 0xFFFFE000u);
+    const float tb = __uint_as_float(__float_as_uint(b) & 0xFFFFE000u);
+    const __half2 hh = __floats2half2_rn(ta, tb);
+    const __half2 ll = __floats2half2_rn(a - ta, b - tb);
+    hi = *reinterpret_cast<const uint32_t *>(&hh);
+    lo = *reinterpret_cast<const uint32_t *>(&ll);
+}
+
+// 8 consecutive values -> hi and lo 16-byte stores (shared memory).
 __device__ __forceinline__ void store_split8(const float *x, unsigned char *hi, unsigned char *lo) {
     uint32_t h[4], l[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float a = x[2 * i], b = x[2 * i + 1];
-        const float ta = __uint_as_float(__float_as_uint(a) & 0xFFFFE000u);
-        const float tb = __uint_as_float(__float_as_uint(b) & 0xFFFFE000u);
-        const __half2 hh = __floats2half2_rn(ta, tb);
-        const __half2 ll = __floats2half2_rn((a - ta) * kLoScale, (b - tb) * kLoScale);
-        h[i] = *reinterpret_cast<const uint32_t *>(&hh);
-        l[i] = *reinterpret_cast<const uint32_t *>(&ll);
-    }
+    for (int i = 0; i < 4; ++i) split_pair(x[2 * i], x[2 * i + 1], h[i], l[i]);
     *reinterpret_cast<uint4 *>(hi) = make_uint4(h[0], h[1], h[2], h[3]);
     *reinterpret_cast<uint4 *>(lo) = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// 16 consecutive 32-bit columns of this thread's tensor-memory lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+        "%14,%15,%16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
+// MMA with A in tensor memory (lane = row, column j = fp16 pair (2j, 2j+1)).
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t id,
+                                        uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b), "r"(id), "r"(acc));
 }
 
 // code (0..2^BITS-1) as an exact float: mantissa of 2^23, minus 2^23
@@ -257,20 +268,19 @@ __device__ __forceinline__ float code_f(uint32_t w, int shift, uint32_t mask) {
 template <int BITS>
 __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArgs a) {
     using SG = SetGeom<BITS>;
+    constexpr int NS = SG::NS;
     constexpr uint32_t kMask = (1u << BITS) - 1u;
     extern __shared__ __align__(1024) unsigned char sm[];
     unsigned char *misc = sm + SG::MISC;
-    uint64_t *full = reinterpret_cast<uint64_t *>(misc);       // [kNS]
-    uint64_t *empty = full + kNS;                               // [kNS]
-    uint64_t *kv_ready = empty + kNS;                           // [kKV] tiles written
+    uint64_t *full = reinterpret_cast<uint64_t *>(misc);        // [NS]  packed group landed
+    uint64_t *empty = full + NS;                                // [NS]  packed group consumed
+    uint64_t *kv_ready = empty + NS;                            // [kKV] tile written
     uint64_t *s_full = kv_ready + kKV;                          // [kS]  S computed
-    uint64_t *s_free = s_full + kS;                             // [kS]  S read
-    uint64_t *pv_kv = s_free + kS;                              // [kKV] tiles read by PV
-    uint64_t *p_ready = pv_kv + kKV;                            // [2]   P written
-    uint64_t *pv_p = p_ready + 2;                               // [2]   PV done (P free, O current)
-    uint64_t *drain = pv_p + 2;                                 // [1]
-    uint64_t *pscaled = drain + 1;                              // [kNS]
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(pscaled + kNS);
+    uint64_t *p_ready = s_full + kS;                            // [kS]  S read, P written
+    uint64_t *pv_done = p_ready + kS;                           // [kS]  PV done: tile, S, P free
+    uint64_t *drain = pv_done + kS;                             // [1]
+    uint64_t *pscaled = drain + 1;                              // [NS]
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(pscaled + NS);
     int *kexp = reinterpret_cast<int *>(tslot + 1);             // [128]
     int *vexp = kexp + kD;                                      // [4]
 
@@ -280,28 +290,23 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
     const int b = (int)(s / a.H), kvh = (int)(s - (int64_t)b * a.H);
     const int64_t gb = (int64_t)chunk * a.per;
     const int64_t ge = min(a.main_groups, gb + a.per);
-    const int ng = (int)max((int64_t)0, ge - gb);
+    const int ng = (int)max((int64_t)0, ge - gb);   // groups of this CTA
+    const int nt = (ng + 1) / 2;                    // 64-token tiles (the last may hold one group)
     const int z0 = blockIdx.z * a.sets_per_cta;
     const int zn = min(a.nsets, z0 + a.sets_per_cta) - z0; // sets in this CTA
     const int rows_valid = zn * a.GQ;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kNS; ++i) {
+        for (int i = 0; i < NS; ++i) {
             bar_init(&full[i], 1);
             bar_init(&empty[i], kConvWarps);
             bar_init(&pscaled[i], kConvWarps);
         }
-        for (int i = 0; i < kKV; ++i) {
-            bar_init(&kv_ready[i], kConvWarps);
-            bar_init(&pv_kv[i], 1);
-        }
+        for (int i = 0; i < kKV; ++i) bar_init(&kv_ready[i], kConvWarps);
         for (int i = 0; i < kS; ++i) {
             bar_init(&s_full[i], 1);
-            bar_init(&s_free[i], kSoftWarps);
-        }
-        for (int i = 0; i < 2; ++i) {
             bar_init(&p_ready[i], kSoftWarps);
-            bar_init(&pv_p[i], 1);
+            bar_init(&pv_done[i], 1);
         }
         bar_init(drain, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -315,12 +320,17 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
     }
     if (threadIdx.x < kD) kexp[threadIdx.x] = a.kexp[s * kD + threadIdx.x];
     if (threadIdx.x < 4) vexp[threadIdx.x] = a.vexp[s * 4 + threadIdx.x];
+    tc_fence_before();
     __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tslot;
 
-    // ---- query tile: Q'' = q * 2^(E_d - e_row), hi/lo, K-major (SBO 2048)
-    float rowfac = 0.0f; // 2^e_row * scale * log2(e), softmax threads only
+    // ---- query rows into tensor memory: Q'' = q 2^(E_d - e_row + 14) < 2^14,
+    // hi/lo, lane = row
+    float rowfac = 0.0f; // 2^(e_row - 28) * scale * log2(e), softmax threads only
     if (warp < kSoftWarps) {
         const int m = threadIdx.x;
+        const uint32_t lane_base = tbase + ((uint32_t)(32 * warp) << 16);
         const bool valid = m < rows_valid;
         const int z = z0 + (valid ? m / a.GQ : 0), h = valid ? m % a.GQ : 0;
         const float *qrow = a.q + ((int64_t)z * a.rows_per_set + (int64_t)b * a.Hq + kvh * a.GQ + h) * kD;
@@ -330,33 +340,25 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
             qm = fmaxf(qm, fabsf(t));
         }
         const int er = exp_ceil_(qm);
-        const float sc = exp2i_(-er);
-        rowfac = exp2i_(er) * (a.scale * 1.4426950408889634f);
-        for (int j = 0; j < kD / 8; ++j) {
-            float x[8];
+        rowfac = exp2i_(er - 28) * (a.scale * 1.4426950408889634f);
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) { // 32 channels -> 16 columns of hi and of lo
+            uint32_t hi[16], lo[16];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const int d = 8 * j + k;
-                x[k] = valid ? (qrow[d] * exp2i_(kexp[d])) * sc : 0.0f;
+            for (int j = 0; j < 16; ++j) {
+                const int d = 32 * c + 2 * j;
+                const float x0 = valid ? (qrow[d] * exp2i_(kexp[d] + 14 - er)) : 0.0f;
+                const float x1 = valid ? (qrow[d + 1] * exp2i_(kexp[d + 1] + 14 - er)) : 0.0f;
+                split_pair(x0, x1, hi[j], lo[j]);
             }
-            const int off = (m >> 3) * 2048 + j * 128 + (m & 7) * 16;
-            store_split8(x, sm + kQhi + off, sm + kQlo + off);
+            tmem_st16(lane_base + kQH + 16 * c, hi);
+            tmem_st16(lane_base + kQL + 16 * c, lo);
         }
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
     }
-    proxy_fence();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tbase = *tslot;
-    if (warp < kSoftWarps) {
-        float z[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) z[i] = 0.0f;
-        const uint32_t lb = tbase + ((uint32_t)(32 * warp) << 16);
-#pragma unroll 1
-        for (int c4 = 0; c4 < 4; ++c4) tmem_st32(lb + kOtot + 32 * c4, z);
-        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-    }
 
     if (warp == kProdWarp) {
         // ------------------------------------------------------------ producer
@@ -367,8 +369,8 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
             const char *vp = reinterpret_cast<const char *>(a.vparams + s * a.vp_stride);
             int issued = 0;
             for (int i = 0; i < ng; ++i) {
-                const int st = i % kNS;
-                if (i >= kNS && !bar_wait(&empty[st], ((i / kNS) - 1) & 1, 16u)) break;
+                const int st = i % NS;
+                if (i >= NS && !bar_wait(&empty[st], ((i / NS) - 1) & 1, 16u)) break;
                 const int64_t g = gb + i;
                 unsigned char *dst = sm + kStages + st * SG::STAGE;
                 asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
@@ -381,58 +383,66 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
                 bulk_load(dst + SG::KC + SG::KP + SG::VC, vp + g * SG::VP, SG::VP, &full[st]);
                 issued = i + 1;
             }
-            for (int st = 0; st < kNS && st < issued; ++st) {
-                const int j = st + ((issued - 1 - st) / kNS) * kNS;
-                bar_wait(&full[st], (j / kNS) & 1, 16u);
+            for (int st = 0; st < NS && st < issued; ++st) {
+                const int j = st + ((issued - 1 - st) / NS) * NS;
+                bar_wait(&full[st], (j / NS) & 1, 16u);
             }
         }
     } else if (warp == kMmaWarp) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            constexpr uint32_t id_qk = idesc_f16(128, kTok, 1);
+            constexpr uint32_t id_qk = idesc_f16(128, kTile, 1);
             constexpr uint32_t id_pv = idesc_f16(128, kD, 1);
-            const uint32_t qhi = su32(sm + kQhi), qlo = su32(sm + kQlo);
+            // descriptors of the shared-memory tiles, computed once; a K step of
+            // 16 elements is +256 bytes = +16 in the start-address field
+            uint64_t dk_hi[kKV], dk_lo[kKV], dv_hi[kKV], dv_lo[kKV];
+#pragma unroll
+            for (int i = 0; i < kKV; ++i) {
+                dk_hi[i] = sdesc(su32(sm + kKbuf + i * 32768), 128, 2048);
+                dk_lo[i] = sdesc(su32(sm + kKbuf + i * 32768 + 16384), 128, 2048);
+                dv_hi[i] = sdesc(su32(sm + kVbuf + i * 32768), 128, 1024);
+                dv_lo[i] = sdesc(su32(sm + kVbuf + i * 32768 + 16384), 128, 1024);
+            }
             bool ok = true;
             auto pv = [&](int j) {
-                const int bj = j & 1;
-                if (!bar_wait(&p_ready[bj], (j >> 1) & 1, 32u)) return false;
+                // O += P V over tile j (K = 32 tokens per group present)
+                const int bj = j % kS, bk = j % kKV;
+                if (!bar_wait(&p_ready[bj], (j / kS) & 1, 32u)) return false;
                 tc_fence_after();
-                const uint32_t phi = su32(sm + kPbuf + bj * 16384), plo = phi + 8192;
-                const uint32_t vhi = su32(sm + kVbuf + (j % kKV) * 16384), vlo = vhi + 8192;
-                const uint32_t pa[3] = {phi, plo, phi}, vb[3] = {vhi, vhi, vlo};
-#pragma unroll
-                for (int pass = 0; pass < 3; ++pass)
-#pragma unroll
-                    for (int ks = 0; ks < 2; ++ks)
-                        umma(tbase + (pass == 0 ? kOhh : kOlh), sdesc(pa[pass] + ks * 256, 128, 512),
-                             sdesc(vb[pass] + ks * 256, 128, 512), id_pv,
-                             (ks > 0 || pass == 2 || (pass == 0 ? j % kFlush != 0 : j > 0)) ? 1u : 0u);
-                umma_commit(&pv_kv[j % kKV]);
-                umma_commit(&pv_p[bj]);
+                const int ksteps = (2 * j + 1 < ng) ? 4 : 2;
+                const uint32_t ph = tbase + kP + 64 * bj, pl = ph + 32;
+                const uint64_t vh = dv_hi[bk], vl = dv_lo[bk];
+#pragma unroll 1
+                for (int ks = 0; ks < ksteps; ++ks) {
+                    umma_ts(tbase + kO, ph + 8 * ks, vh + 16 * ks, id_pv, (j > 0 || ks > 0) ? 1u : 0u);
+                    umma_ts(tbase + kO, pl + 8 * ks, vh + 16 * ks, id_pv, 1u);
+                    umma_ts(tbase + kO, ph + 8 * ks, vl + 16 * ks, id_pv, 1u);
+                }
+                umma_commit(&pv_done[bj]);
                 return true;
             };
-            for (int g = 0; ok && g < ng; ++g) {
-                const int bg = g % kKV, bs = g % kS;
-                if (!bar_wait(&kv_ready[bg], (g / kKV) & 1, 32u) ||
-                    (g >= kS && !bar_wait(&s_free[bs], ((g - kS) / kS) & 1, 32u))) {
+            for (int j = 0; ok && j < nt; ++j) {
+                const int bk = j % kKV, bs = j % kS;
+                // tile bk converted; S/P buffer bs free once PV(j - kS) is done
+                if (!bar_wait(&kv_ready[bk], (j / kKV) & 1, 32u) ||
+                    (j >= kS && !bar_wait(&pv_done[bs], ((j - kS) / kS) & 1, 32u))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t khi = su32(sm + kKbuf + bg * 16384), klo = khi + 8192;
-                const uint32_t qa[3] = {qhi, qlo, qhi}, kb[3] = {khi, khi, klo};
+                const uint32_t sacc = tbase + kSc + 64 * bs;
+                const uint64_t kh = dk_hi[bk], kl = dk_lo[bk];
 #pragma unroll
-                for (int pass = 0; pass < 3; ++pass)
+                for (int ks = 0; ks < 8; ++ks)
+                    umma_ts(sacc, tbase + kQH + 8 * ks, kh + 16 * ks, id_qk, ks > 0 ? 1u : 0u);
 #pragma unroll
-                    for (int ks = 0; ks < 8; ++ks)
-                        umma(tbase + (pass == 0 ? 0u : kSlh) + 32 * bs,
-                             sdesc(qa[pass] + ks * 256, 128, 2048),
-                             sdesc(kb[pass] + ks * 256, 128, 2048), id_qk,
-                             (pass == 2 || ks > 0) ? 1u : 0u);
+                for (int ks = 0; ks < 8; ++ks) umma_ts(sacc, tbase + kQL + 8 * ks, kh + 16 * ks, id_qk, 1u);
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks) umma_ts(sacc, tbase + kQH + 8 * ks, kl + 16 * ks, id_qk, 1u);
                 umma_commit(&s_full[bs]);
-                if (g >= 1 && !pv(g - 1)) ok = false;
+                if (j >= 1 && !pv(j - 1)) ok = false;
             }
-            if (ok && ng >= 1) pv(ng - 1);
+            if (ok && nt >= 1) pv(nt - 1);
             // every MMA of this CTA complete before tensor memory is released
             umma_commit(drain);
             bar_wait(drain, 0, 32u);
@@ -442,9 +452,10 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
         const int ct = threadIdx.x - kSoftWarps * 32; // 0..255
         bool ok = true;
         for (int g = 0; ok && g < ng; ++g) {
-            const int st = g % kNS, bg = g % kKV;
-            if (!warp_wait(&full[st], (g / kNS) & 1, 64u) ||
-                (g >= kKV && !warp_wait(&pv_kv[bg], ((g - kKV) / kKV) & 1, 64u))) {
+            const int st = g % NS, j = g >> 1, bk = j % kKV, half = g & 1;
+            // the tile's buffers are free once PV(j - kKV) is done (first group of a tile)
+            if (!warp_wait(&full[st], (g / NS) & 1, 64u) ||
+                (half == 0 && j >= kKV && !warp_wait(&pv_done[(j - kKV) % kS], ((j - kKV) / kS) & 1, 64u))) {
                 ok = false;
                 break;
             }
@@ -453,60 +464,62 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
             float2 *KP = reinterpret_cast<float2 *>(base + SG::KC);
             const uint32_t *VC = reinterpret_cast<const uint32_t *>(base + SG::KC + SG::KP);
             float2 *VP = reinterpret_cast<float2 *>(base + SG::KC + SG::KP + SG::VC);
-            // parameters pre-multiplied by the power-of-two range bounds
+            // parameters pre-multiplied by the power-of-two range factors
+            // (keys 2^(14 - E_d), values 2^(14 - F_cg): dequantized values < 2^13)
             if (ct < kD) {
-                const float f = exp2i_(-kexp[ct]);
+                const float f = exp2i_(14 - kexp[ct]);
                 const float2 p = KP[ct];
                 KP[ct] = make_float2(p.x * f, p.y * f);
             } else {
                 const int e = ct - kD; // (token e/4, channel group e%4)
-                const float f = exp2i_(-vexp[e & 3]);
+                const float f = exp2i_(14 - vexp[e & 3]);
                 const float2 p = VP[e];
                 VP[e] = make_float2(p.x * f, p.y * f);
             }
             // all eight warps' rewrites done (bounded, unlike a named barrier)
             __syncwarp();
             if (lane == 0) bar_arrive(&pscaled[st]);
-            if (!warp_wait(&pscaled[st], (g / kNS) & 1, 64u)) {
+            if (!warp_wait(&pscaled[st], (g / NS) & 1, 64u)) {
                 ok = false;
                 break;
             }
-            unsigned char *khi = sm + kKbuf + bg * 16384, *klo = khi + 8192;
-            unsigned char *vhi = sm + kVbuf + bg * 16384, *vlo = vhi + 8192;
+            unsigned char *khi = sm + kKbuf + bk * 32768, *klo = khi + 16384;
+            unsigned char *vhi = sm + kVbuf + bk * 32768, *vlo = vhi + 16384;
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
                 const int tau = ct + 256 * r;
                 float x[8];
                 {
-                    // keys, MN-major: channel kd, tokens 8 tb .. 8 tb + 7 (one
-                    // word, one (scale, zero)); 8 channels x 4 blocks per warp
+                    // keys, MN-major (n = token, SBO 2048): channel kd, tokens
+                    // 8 tb .. 8 tb + 7 of this group (one word, one (scale, zero))
                     const int kd = 8 * (tau >> 5) + (tau & 7), tb = (tau >> 3) & 3;
                     const int bit0 = 8 * tb * BITS;
                     const uint32_t w = KC[kd * SG::IPC + (bit0 >> 5)];
                     const float2 p = KP[kd];
 #pragma unroll
                     for (int k = 0; k < 8; ++k) x[k] = fmaf(code_f(w, (bit0 & 31) + k * BITS, kMask), p.x, p.y);
-                    const int koff = tb * 2048 + (kd >> 3) * 128 + (kd & 7) * 16;
+                    const int koff = (4 * half + tb) * 2048 + (kd >> 3) * 128 + (kd & 7) * 16;
                     store_split8(x, khi + koff, klo + koff);
                 }
-                // task: token t, 8-channel chunk j (8 tokens x 4 chunks per warp instruction)
+                // values, MN-major (k = token, SBO 1024): token t, channels 8j .. 8j+7
                 const int t = (tau & 7) + 8 * ((tau >> 5) & 3);
-                const int j = ((tau >> 3) & 3) + 4 * (tau >> 7);
-                // values: word (t, cg, i) holds 32/BITS channels of group cg
-                const int cg = j >> 2;
-                const int cin = (j & 3) * 8;                   // first channel within the group
+                const int jj = ((tau >> 3) & 3) + 4 * (tau >> 7);
+                const int cg = jj >> 2;
+                const int cin = (jj & 3) * 8;                   // first channel within the group
                 const int vwi = (cin * BITS) >> 5, vsh = (cin % (32 / BITS)) * BITS;
                 const uint32_t w = VC[(t * 4 + cg) * SG::IPC + vwi];
                 const float2 p = VP[t * 4 + cg];
 #pragma unroll
                 for (int k = 0; k < 8; ++k) x[k] = fmaf(code_f(w, vsh + k * BITS, kMask), p.x, p.y);
-                const int voff = j * 512 + (t >> 3) * 128 + (t & 7) * 16;
+                const int tt = 32 * half + t;
+                const int voff = jj * 1024 + (tt >> 3) * 128 + (tt & 7) * 16;
                 store_split8(x, vhi + voff, vlo + voff);
             }
             proxy_fence();
             __syncwarp();
             if (lane == 0) {
-                bar_arrive(&kv_ready[bg]);
+                // a tile is ready after its last group (one group in the CTA's last odd tile)
+                if (half == 1 || g == ng - 1) bar_arrive(&kv_ready[bk]);
                 bar_arrive(&empty[st]);
             }
         }
@@ -516,114 +529,79 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
         const uint32_t lane_base = tbase + ((uint32_t)(32 * warp) << 16);
         float mref = -INFINITY, l = 0.0f;
         bool ok = true;
-        for (int g = 0; ok && g < ng; ++g) {
-            const int bg = g % kS, bp = g & 1;
-            if (!warp_wait(&s_full[bg], (g / kS) & 1, 128u)) {
+        for (int j = 0; ok && j < nt; ++j) {
+            const int bs = j % kS;
+            const bool two = 2 * j + 1 < ng; // tile holds 64 tokens (else 32)
+            if (!warp_wait(&s_full[bs], (j / kS) & 1, 128u)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            float x[32];
-            {
-                float y[32];
-                tmem_ld32(lane_base + 32 * bg, x);
-                tmem_ld32(lane_base + kSlh + 32 * bg, y);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) x[i] = fmaf(y[i], kLoUnscale, x[i]);
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) bar_arrive(&s_free[bg]);
+            float x[64];
+            tmem_ld32(lane_base + kSc + 64 * bs, x);
+            tmem_ld32(lane_base + kSc + 64 * bs + 32, x + 32);
             float mx = -INFINITY;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                x[i] *= rowfac;
+            for (int i = 0; i < 64; ++i) {
+                x[i] = (i < 32 || two) ? x[i] * rowfac : -INFINITY;
                 mx = fmaxf(mx, x[i]);
             }
             const bool need = mx > mref + kLazy2;
-            const bool flush = g >= 1 && g % kFlush == 0; // PV(g) restarts O_hh
-            const bool rescale = __any_sync(0xffffffffu, need);
-            float alpha = 1.0f;
-            if (rescale) {
+            if (__any_sync(0xffffffffu, need)) {
                 const float nref = need ? mx : mref;
-                alpha = (mref == -INFINITY) ? 0.0f : exp2f(mref - nref);
+                const float alpha = (mref == -INFINITY) ? 0.0f : exp2f(mref - nref);
                 mref = nref;
                 l *= alpha;
-            }
-            if (g >= 1 && (rescale || flush)) {
-                // O holds groups < g: wait for PV(g-1), then scale and/or fold
-                if (!warp_wait(&pv_p[(g - 1) & 1], ((g - 1) >> 1) & 1, 128u)) {
-                    ok = false;
-                } else {
-                    tc_fence_after();
+                if (j >= 1) {
+                    // O holds tiles < j: wait for PV(j-1), rescale this warp's rows
+                    if (!warp_wait(&pv_done[(j - 1) % kS], ((j - 1) / kS) & 1, 128u)) {
+                        ok = false;
+                    } else {
+                        tc_fence_after();
 #pragma unroll 1
-                    for (int c4 = 0; c4 < 4; ++c4) {
-                        float a[32], t[32];
-                        tmem_ld32(lane_base + kOtot + 32 * c4, t);
-                        tmem_ld32(lane_base + kOhh + 32 * c4, a);
-                        if (flush) {
+                        for (int c4 = 0; c4 < 4; ++c4) {
+                            float o[32];
+                            tmem_ld32(lane_base + kO + 32 * c4, o);
 #pragma unroll
-                            for (int i = 0; i < 32; ++i) t[i] = (t[i] + a[i]) * alpha;
-                        } else {
-#pragma unroll
-                            for (int i = 0; i < 32; ++i) {
-                                t[i] *= alpha;
-                                a[i] *= alpha;
-                            }
-                            tmem_st32(lane_base + kOhh + 32 * c4, a);
+                            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+                            tmem_st32(lane_base + kO + 32 * c4, o);
                         }
-                        tmem_st32(lane_base + kOtot + 32 * c4, t);
-                        if (rescale) {
-                            tmem_ld32(lane_base + kOlh + 32 * c4, a);
-#pragma unroll
-                            for (int i = 0; i < 32; ++i) a[i] *= alpha;
-                            tmem_st32(lane_base + kOlh + 32 * c4, a);
-                        }
+                        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                     }
-                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                 }
             }
             if (!ok) break;
             float psum = 0.0f;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
+            for (int i = 0; i < 64; ++i) {
                 x[i] = exp2f(x[i] - mref);
                 psum += x[i];
                 x[i] *= kPScale; // <= 2^15, fp16 normal down to p = 2^(kLazyBits - 29)
             }
             l += psum;
-            // P[bg] is free once PV(g-2) has completed
-            if (g >= 2 && !warp_wait(&pv_p[bp], ((g - 2) >> 1) & 1, 128u)) {
-                ok = false;
-                break;
-            }
-            unsigned char *phi = sm + kPbuf + bp * 16384, *plo = phi + 8192;
+            // P[bs] shares its buffer's life with S[bs]: free (PV(j - kS) done) since
+            // the MMA issued QK(j) into S[bs]
+            uint32_t hi[16], lo[16];
 #pragma unroll
-            for (int c8 = 0; c8 < 4; ++c8) {
-                const int off = (m >> 3) * 512 + c8 * 128 + (m & 7) * 16;
-                store_split8(x + 8 * c8, phi + off, plo + off);
+            for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+                for (int q = 0; q < 16; ++q) split_pair(x[32 * hh + 2 * q], x[32 * hh + 2 * q + 1], hi[q], lo[q]);
+                tmem_st16(lane_base + kP + 64 * bs + 16 * hh, hi);
+                tmem_st16(lane_base + kP + 64 * bs + 32 + 16 * hh, lo);
             }
-            proxy_fence();
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) bar_arrive(&p_ready[bp]);
+            if (lane == 0) bar_arrive(&p_ready[bs]);
         }
         // ---- epilogue: partial (m, l, o) of this row for slot `chunk`
-        bool have = ok && ng > 0;
-        if (have && !warp_wait(&pv_p[(ng - 1) & 1], ((ng - 1) >> 1) & 1, 128u)) have = false;
+        bool have = ok && nt > 0;
+        if (have && !warp_wait(&pv_done[(nt - 1) % kS], ((nt - 1) / kS) & 1, 128u)) have = false;
         tc_fence_after();
         float o[kD];
         if (have) {
 #pragma unroll
-            for (int c4 = 0; c4 < 4; ++c4) {
-                float y[32], t[32];
-                tmem_ld32(lane_base + kOhh + 32 * c4, o + 32 * c4);
-                tmem_ld32(lane_base + kOlh + 32 * c4, y);
-                tmem_ld32(lane_base + kOtot + 32 * c4, t);
-#pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    o[32 * c4 + i] = fmaf(y[i], kLoUnscale, t[i] + o[32 * c4 + i]);
-            }
+            for (int c4 = 0; c4 < 4; ++c4) tmem_ld32(lane_base + kO + 32 * c4, o + 32 * c4);
         }
         if (m < rows_valid) {
             const int z = z0 + m / a.GQ, h = m % a.GQ;
@@ -631,7 +609,8 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
             float *po = a.part_o + (row * a.parts + chunk) * kD;
             float *pml = a.part_ml + (row * a.parts + chunk) * 2;
             if (have) {
-                for (int d = 0; d < kD; ++d) po[d] = o[d] * exp2i_(vexp[d >> 5] - (15 - kLazyBits));
+                // O = sum p v = O' 2^(F_cg - 14) 2^-(15 - kLazyBits)
+                for (int d = 0; d < kD; ++d) po[d] = o[d] * exp2i_(vexp[d >> 5] - 29 + kLazyBits);
                 pml[0] = mref * 0.6931471805599453f;
                 pml[1] = l;
             } else {
