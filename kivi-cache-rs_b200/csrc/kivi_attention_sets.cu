@@ -8,36 +8,42 @@
 //
 //   per CTA: one stream (kv head), one run of its 32-token groups, all query
 //   rows of up to 128/GQ sets (row m = set * GQ + head, padded to 128);
-//   S = Q K^T   tcgen05.mma kind::f16, M = 128 rows, N = 32 tokens, K = 128,
-//               D in tensor memory (three S buffers in flight);
-//   softmax     one thread per row reads its S row from tensor memory;
-//   O += P V    tcgen05.mma kind::f16, M = 128, N = 128 channels, K = 32 tokens,
-//               O accumulated in tensor memory across all the CTA's groups.
+//   S = Q K^T   tcgen05.mma kind::f16, M = 128 rows, N = 64 tokens (two
+//               groups), K = 128; Q is the A operand in tensor memory, the
+//               key tile the B operand in shared memory, S in tensor memory
+//               (two S buffers);
+//   softmax     one thread per row reads its S row from tensor memory and
+//               writes P (fp16 hi/lo) back to tensor memory;
+//   O += P V    tcgen05.mma kind::f16, M = 128, N = 128 channels, K = 64
+//               tokens, P from tensor memory, O accumulated in tensor memory
+//               across all the CTA's groups.
 //
 // fp32 accuracy from fp16 operands: every operand x is split into
-// hi = x truncated to 11 significant bits and lo = (x - hi) * 2^11 (exact),
-// and each product is formed as hi*hi + 2^-11 (lo*hi + hi*lo): hi*hi and the
-// two cross terms accumulate in separate tensor-memory accumulators that are
-// combined in fp32 (~22 significant bits; the dropped lo*lo is below 2^-22).
-// Range: keys are dequantized exactly as the reference does,
+// hi = x truncated to 11 significant bits and lo = x - hi (exact), and each
+// product is formed as hi*hi + lo*hi + hi*lo in the fp32 accumulator (~22
+// significant bits; the dropped lo*lo is below 2^-22 relative).  Both parts
+// must be fp16 normals, so every operand is scaled into the upper fp16 range
+// by powers of two: keys are dequantized exactly as the reference does,
 // fma(code, scale, zero) (quant.rs:404-406), with (scale, zero) pre-multiplied
-// by 2^-E_d, E_d bounding channel d's |key| over the whole prefix; the query
-// carries 2^(E_d - e_row), e_row bounding its row; values likewise with one
-// bound per channel group; softmax weights enter as p * 2^9 <= 2^15 (fp16
-// normal down to p = 2^-23) with the reference point moved only when a logit
-// exceeds it by 6 (exp2 units).  All bounds are
-// powers of two, undone exactly in fp32.
+// by 2^(14 - E_d), E_d bounding channel d's |key| over the whole prefix; the
+// query row carries 2^(E_d - e_row + 14), e_row bounding the row; values
+// likewise with one bound per channel group; softmax weights enter as
+// p * 2^(15 - T) with the reference point moved only when a logit exceeds it
+// by T = 6 (exp2 units).  All factors are powers of two, undone exactly in fp32.
 //
 // Warp roles (448 threads): warps 0-3 softmax and epilogue (thread = row,
-// tensor-memory lanes 0..127), warps 4-11 dequantize each landed group into
-// the fp16 hi/lo operand tiles, warp 12 lane 0 streams the packed groups in
-// with bulk async copies (cp.async.bulk, into this CTA only), warp 13 lane 0
-// issues the MMAs.  Operand tiles use the canonical no-swizzle layouts:
-// K-major addr(r, k) = (r/8)*SBO + (k/8)*128 + (r%8)*16 + (k%8)*2, MN-major
-// addr(k, n) = (n/8)*SBO + (k/8)*128 + (k%8)*16 + (n%8)*2.  Every mbarrier
-// wait is bounded (~1 s); a wait that gives up sets a device error flag
-// (read by the host after synchronous calls) and the CTA winds down without
-// hanging.
+// tensor-memory lanes 0..127); warps 4-7 dequantize each landed group into
+// the fp16 hi/lo key tile, warps 8-11 into the value tile; warp 12 lane 0
+// streams the packed groups in with bulk async copies (cp.async.bulk, into
+// this CTA only); warp 13 issues the MMAs (the whole warp runs the loop, one
+// elected lane issues) in the order QK(0), QK(1), PV(0), QK(2), PV(1), ...  Key tiles (two in flight) are released when their
+// QK^T completes, value tiles (three in flight) when their PV completes, so the
+// converters run ahead of the tensor pipe.  Operand tiles use the canonical
+// no-swizzle layouts: K-major addr(r, k) = (r/8)*SBO + (k/8)*128 + (r%8)*16 +
+// (k%8)*2, MN-major addr(k, n) = (n/8)*SBO + (k/8)*128 + (k%8)*16 + (n%8)*2.
+// Every mbarrier wait is bounded (~1 s); a wait that gives up sets a device
+// error flag (read by the host after synchronous calls) and the CTA winds
+// down without hanging.
 #include <cuda_fp16.h>
 #include <math.h>
 #include <stdint.h>
@@ -53,7 +59,8 @@ __device__ unsigned int g_sets_error = 0; // set by bounded waits that give up
 namespace {
 
 constexpr int kSoftWarps = 4;
-constexpr int kConvWarps = 8;
+constexpr int kConvWarps = 8;                      // 4 key converters, then 4 value converters
+constexpr int kConvHalf = kConvWarps / 2;
 constexpr int kProdWarp = kSoftWarps + kConvWarps; // 12
 constexpr int kMmaWarp = kProdWarp + 1;            // 13
 constexpr int kSetThreads = (kMmaWarp + 1) * 32;   // 448
@@ -64,8 +71,12 @@ constexpr int kD = 128;
 constexpr int kTok = 32;                           // tokens per group = per S tile
 constexpr long long kWait = 2000000000LL;          // ~1 s at B200 clocks
 constexpr int kTile = 64;   // tokens per S tile (two groups): QK^T runs at N = 64
-constexpr int kKV = 2;      // key/value tiles in flight
-constexpr int kS = 2;       // S / P tensor-memory buffers
+#ifndef KIVI_SETS_KBUF
+#define KIVI_SETS_KBUF 2
+#endif
+constexpr int kK = KIVI_SETS_KBUF; // key operand tiles in flight (free once QK^T is done)
+constexpr int kV = 3;              // value operand tiles in flight (free once PV is done)
+constexpr int kS = 2;              // S / P tensor-memory buffers
 #ifndef KIVI_SETS_LAZY
 #define KIVI_SETS_LAZY 6
 #endif
@@ -79,21 +90,22 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSc = 0, kP = 128, kQH = 256, kQL = 320, kO = 384;
 
 // shared-memory map (bytes): per key/value tile hi and lo parts of 16 KB each
-constexpr int kKbuf = 0;                            // [kKV] x (hi, lo): 128 channels x 64 tokens
-constexpr int kVbuf = kKbuf + kKV * 32768;          // [kKV] x (hi, lo): 64 tokens x 128 channels
-constexpr int kStages = kVbuf + kKV * 32768;        // packed groups
+constexpr int kKbuf = 0;                            // [kK] x (hi, lo): 128 channels x 64 tokens
+constexpr int kVbuf = kKbuf + kK * 32768;           // [kV] x (hi, lo): 64 tokens x 128 channels
+constexpr int kStages = kVbuf + kV * 32768;         // packed groups
 
 template <int BITS> struct SetGeom {
-    // packed-group stages in flight: as many as shared memory leaves room for
-    static constexpr int NS = KIVI_SETS_STAGES2;
     static constexpr int IPC = BITS;                 // words per channel per key group
     static constexpr int KC = kD * IPC * 4;
     static constexpr int KP = kD * 8;
     static constexpr int VC = kTok * 4 * IPC * 4;
     static constexpr int VP = kTok * 4 * 8;
     static constexpr int STAGE = KC + KP + VC + VP;
+    // packed-group stages in flight: as many as shared memory leaves room for, up to 8
+    static constexpr int NS = std::min(KIVI_SETS_STAGES2, (232448 - 1024 - kStages) / STAGE);
     static constexpr int MISC = kStages + NS * STAGE;
     static constexpr int SMEM = MISC + 1024;
+    static_assert(NS >= 2, "packed-group stages");
     static_assert(SMEM <= 232448, "shared memory per block");
 };
 
@@ -158,12 +170,6 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t 
 __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int b_mn_major) {
     return (1u << 4) | ((uint32_t)b_mn_major << 16) | ((uint32_t)(N >> 3) << 17) |
            ((uint32_t)(M >> 4) << 24);
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t *b) {
-    asm volatile(
-        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(b))
-        : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -251,13 +257,25 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *r) {
         : "memory");
 }
 
-// MMA with A in tensor memory (lane = row, column j = fp16 pair (2j, 2j+1)).
+// MMA with A in tensor memory (lane = row, column j = fp16 pair (2j, 2j+1)),
+// issued by one elected lane of a converged warp.  The whole warp runs the
+// issue loop: a single-lane loop inside a divergent branch issues several
+// times slower once the other warps of its sub-partition keep the issue
+// slots busy.
 __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t id,
                                         uint32_t acc) {
     asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
         "r"(a_tmem), "l"(b), "r"(id), "r"(acc));
+}
+
+// tcgen05.commit by the same elected lane (elect.sync picks the same leader for a full mask)
+__device__ __forceinline__ void umma_commit_e(uint64_t *b) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(su32(b))
+        : "memory");
 }
 
 // code (0..2^BITS-1) as an exact float: mantissa of 2^23, minus 2^23
@@ -274,13 +292,15 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
     unsigned char *misc = sm + SG::MISC;
     uint64_t *full = reinterpret_cast<uint64_t *>(misc);        // [NS]  packed group landed
     uint64_t *empty = full + NS;                                // [NS]  packed group consumed
-    uint64_t *kv_ready = empty + NS;                            // [kKV] tile written
-    uint64_t *s_full = kv_ready + kKV;                          // [kS]  S computed
+    uint64_t *k_ready = empty + NS;                             // [kK]  key tile written
+    uint64_t *k_free = k_ready + kK;                            // [kK]  QK^T over it done
+    uint64_t *v_ready = k_free + kK;                            // [kV]  value tile written
+    uint64_t *v_free = v_ready + kV;                            // [kV]  PV over it done
+    uint64_t *s_full = v_free + kV;                             // [kS]  S computed
     uint64_t *p_ready = s_full + kS;                            // [kS]  S read, P written
-    uint64_t *pv_done = p_ready + kS;                           // [kS]  PV done: tile, S, P free
+    uint64_t *pv_done = p_ready + kS;                           // [kS]  PV of the tile done
     uint64_t *drain = pv_done + kS;                             // [1]
-    uint64_t *pscaled = drain + 1;                              // [NS]
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(pscaled + NS);
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(drain + 1);
     int *kexp = reinterpret_cast<int *>(tslot + 1);             // [128]
     int *vexp = kexp + kD;                                      // [4]
 
@@ -299,10 +319,16 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
     if (threadIdx.x == 0) {
         for (int i = 0; i < NS; ++i) {
             bar_init(&full[i], 1);
-            bar_init(&empty[i], kConvWarps);
-            bar_init(&pscaled[i], kConvWarps);
+            bar_init(&empty[i], 2 * kConvHalf);
         }
-        for (int i = 0; i < kKV; ++i) bar_init(&kv_ready[i], kConvWarps);
+        for (int i = 0; i < kK; ++i) {
+            bar_init(&k_ready[i], kConvHalf);
+            bar_init(&k_free[i], 1);
+        }
+        for (int i = 0; i < kV; ++i) {
+            bar_init(&v_ready[i], kConvHalf);
+            bar_init(&v_free[i], 1);
+        }
         for (int i = 0; i < kS; ++i) {
             bar_init(&s_full[i], 1);
             bar_init(&p_ready[i], kSoftWarps);
@@ -326,30 +352,58 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
     const uint32_t tbase = *tslot;
 
     // ---- query rows into tensor memory: Q'' = q 2^(E_d - e_row + 14) < 2^14,
-    // hi/lo, lane = row
+    // hi/lo, lane = row.  All warps stage the rows through shared memory (the
+    // value-tile buffers, unused until the roles start): warp w takes rows
+    // w, w + 14, ..., each lane two float2 of a row (coalesced), the row bound
+    // e_row comes from a warp max; the row's owner thread then moves its hi/lo
+    // words into tensor memory.  Staged row r: hi words at r * kQRow, lo words
+    // 256 bytes later; the 16-byte pad keeps the owners' 16-byte reads
+    // conflict-free.
+    constexpr int kQRow = 528;
+    uint32_t *qstage = reinterpret_cast<uint32_t *>(sm + kVbuf);
+    int *rowexp = reinterpret_cast<int *>(sm + kVbuf + 128 * kQRow); // [128]
+    static_assert(128 * kQRow + 512 <= kV * 32768, "query staging fits the value tiles");
+    for (int r = warp; r < 128; r += kSetThreads / 32) {
+        const bool valid = r < rows_valid;
+        float2 v0 = make_float2(0.0f, 0.0f), v1 = v0;
+        if (valid) {
+            const int z = z0 + r / a.GQ, h = r % a.GQ;
+            const float2 *qrow = reinterpret_cast<const float2 *>(
+                a.q + ((int64_t)z * a.rows_per_set + (int64_t)b * a.Hq + kvh * a.GQ + h) * kD);
+            v0 = qrow[lane];      // channels 2 lane, 2 lane + 1
+            v1 = qrow[32 + lane]; // channels 64 + 2 lane, 64 + 2 lane + 1
+        }
+        const int d0 = 2 * lane, d1 = 64 + 2 * lane;
+        float qm = fmaxf(fmaxf(fabsf(v0.x * exp2i_(kexp[d0])), fabsf(v0.y * exp2i_(kexp[d0 + 1]))),
+                         fmaxf(fabsf(v1.x * exp2i_(kexp[d1])), fabsf(v1.y * exp2i_(kexp[d1 + 1]))));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) qm = fmaxf(qm, __shfl_xor_sync(0xffffffffu, qm, o));
+        const int er = exp_ceil_(qm);
+        uint32_t h0, l0, h1, l1;
+        split_pair(v0.x * exp2i_(kexp[d0] + 14 - er), v0.y * exp2i_(kexp[d0 + 1] + 14 - er), h0, l0);
+        split_pair(v1.x * exp2i_(kexp[d1] + 14 - er), v1.y * exp2i_(kexp[d1 + 1] + 14 - er), h1, l1);
+        uint32_t *row = qstage + r * (kQRow / 4);
+        row[lane] = h0;
+        row[32 + lane] = h1;
+        row[64 + lane] = l0;
+        row[96 + lane] = l1;
+        if (lane == 0) rowexp[r] = er;
+    }
+    __syncthreads();
     float rowfac = 0.0f; // 2^(e_row - 28) * scale * log2(e), softmax threads only
     if (warp < kSoftWarps) {
         const int m = threadIdx.x;
         const uint32_t lane_base = tbase + ((uint32_t)(32 * warp) << 16);
-        const bool valid = m < rows_valid;
-        const int z = z0 + (valid ? m / a.GQ : 0), h = valid ? m % a.GQ : 0;
-        const float *qrow = a.q + ((int64_t)z * a.rows_per_set + (int64_t)b * a.Hq + kvh * a.GQ + h) * kD;
-        float qm = 0.0f;
-        for (int d = 0; d < kD; ++d) {
-            const float t = valid ? qrow[d] * exp2i_(kexp[d]) : 0.0f;
-            qm = fmaxf(qm, fabsf(t));
-        }
-        const int er = exp_ceil_(qm);
-        rowfac = exp2i_(er - 28) * (a.scale * 1.4426950408889634f);
+        rowfac = exp2i_(rowexp[m] - 28) * (a.scale * 1.4426950408889634f);
+        const uint4 *row = reinterpret_cast<const uint4 *>(qstage + m * (kQRow / 4));
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) { // 32 channels -> 16 columns of hi and of lo
             uint32_t hi[16], lo[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int d = 32 * c + 2 * j;
-                const float x0 = valid ? (qrow[d] * exp2i_(kexp[d] + 14 - er)) : 0.0f;
-                const float x1 = valid ? (qrow[d + 1] * exp2i_(kexp[d + 1] + 14 - er)) : 0.0f;
-                split_pair(x0, x1, hi[j], lo[j]);
+            for (int i = 0; i < 4; ++i) {
+                const uint4 x = row[4 * c + i], y = row[16 + 4 * c + i];
+                hi[4 * i] = x.x, hi[4 * i + 1] = x.y, hi[4 * i + 2] = x.z, hi[4 * i + 3] = x.w;
+                lo[4 * i] = y.x, lo[4 * i + 1] = y.y, lo[4 * i + 2] = y.z, lo[4 * i + 3] = y.w;
             }
             tmem_st16(lane_base + kQH + 16 * c, hi);
             tmem_st16(lane_base + kQL + 16 * c, lo);
@@ -389,49 +443,50 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
             }
         }
     } else if (warp == kMmaWarp) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
+        // ------------------------------------------------------------ MMA issuer (whole warp)
+        {
             constexpr uint32_t id_qk = idesc_f16(128, kTile, 1);
             constexpr uint32_t id_pv = idesc_f16(128, kD, 1);
-            // descriptors of the shared-memory tiles, computed once; a K step of
-            // 16 elements is +256 bytes = +16 in the start-address field
-            uint64_t dk_hi[kKV], dk_lo[kKV], dv_hi[kKV], dv_lo[kKV];
-#pragma unroll
-            for (int i = 0; i < kKV; ++i) {
-                dk_hi[i] = sdesc(su32(sm + kKbuf + i * 32768), 128, 2048);
-                dk_lo[i] = sdesc(su32(sm + kKbuf + i * 32768 + 16384), 128, 2048);
-                dv_hi[i] = sdesc(su32(sm + kVbuf + i * 32768), 128, 1024);
-                dv_lo[i] = sdesc(su32(sm + kVbuf + i * 32768 + 16384), 128, 1024);
-            }
+            // descriptors of the shared-memory tiles: the start-address field holds
+            // address / 16, so a K step of 16 elements (256 bytes) is +16 and buffer
+            // i of a ring is the first one's + i * 32768 / 16
+            const uint64_t dk0 = sdesc(su32(sm + kKbuf), 128, 2048);
+            const uint64_t dv0 = sdesc(su32(sm + kVbuf), 128, 1024);
             bool ok = true;
             auto pv = [&](int j) {
                 // O += P V over tile j (K = 32 tokens per group present)
-                const int bj = j % kS, bk = j % kKV;
-                if (!bar_wait(&p_ready[bj], (j / kS) & 1, 32u)) return false;
+                const int bj = j % kS, bv = j % kV;
+                if (!warp_wait(&p_ready[bj], (j / kS) & 1, 32u) ||
+                    !warp_wait(&v_ready[bv], (j / kV) & 1, 32u))
+                    return false;
                 tc_fence_after();
                 const int ksteps = (2 * j + 1 < ng) ? 4 : 2;
                 const uint32_t ph = tbase + kP + 64 * bj, pl = ph + 32;
-                const uint64_t vh = dv_hi[bk], vl = dv_lo[bk];
+                const uint64_t vh = dv0 + (uint64_t)bv * 2048u, vl = vh + 1024u;
 #pragma unroll 1
                 for (int ks = 0; ks < ksteps; ++ks) {
                     umma_ts(tbase + kO, ph + 8 * ks, vh + 16 * ks, id_pv, (j > 0 || ks > 0) ? 1u : 0u);
                     umma_ts(tbase + kO, pl + 8 * ks, vh + 16 * ks, id_pv, 1u);
                     umma_ts(tbase + kO, ph + 8 * ks, vl + 16 * ks, id_pv, 1u);
                 }
-                umma_commit(&pv_done[bj]);
+                umma_commit_e(&pv_done[bj]);
+                umma_commit_e(&v_free[bv]);
                 return true;
             };
+            // Issue order QK(0), QK(1), PV(0), QK(2), PV(1), ...: softmax of tile j
+            // overlaps PV(j - 1) and QK(j + 1).  S[bs] / P[bs] are free for tile j:
+            // softmax(j - kS) read S before p_ready(j - kS), which PV(j - kS) (issued
+            // earlier) waited for, and P[bs] is rewritten only after QK(j) completes,
+            // which in issue order follows PV(j - kS).
             for (int j = 0; ok && j < nt; ++j) {
-                const int bk = j % kKV, bs = j % kS;
-                // tile bk converted; S/P buffer bs free once PV(j - kS) is done
-                if (!bar_wait(&kv_ready[bk], (j / kKV) & 1, 32u) ||
-                    (j >= kS && !bar_wait(&pv_done[bs], ((j - kS) / kS) & 1, 32u))) {
+                const int bk = j % kK, bs = j % kS;
+                if (!warp_wait(&k_ready[bk], (j / kK) & 1, 32u)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t sacc = tbase + kSc + 64 * bs;
-                const uint64_t kh = dk_hi[bk], kl = dk_lo[bk];
+                const uint64_t kh = dk0 + (uint64_t)bk * 2048u, kl = kh + 1024u;
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks)
                     umma_ts(sacc, tbase + kQH + 8 * ks, kh + 16 * ks, id_qk, ks > 0 ? 1u : 0u);
@@ -439,87 +494,95 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
                 for (int ks = 0; ks < 8; ++ks) umma_ts(sacc, tbase + kQL + 8 * ks, kh + 16 * ks, id_qk, 1u);
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks) umma_ts(sacc, tbase + kQH + 8 * ks, kl + 16 * ks, id_qk, 1u);
-                umma_commit(&s_full[bs]);
+                umma_commit_e(&s_full[bs]);
+                umma_commit_e(&k_free[bk]);
                 if (j >= 1 && !pv(j - 1)) ok = false;
             }
             if (ok && nt >= 1) pv(nt - 1);
             // every MMA of this CTA complete before tensor memory is released
-            umma_commit(drain);
-            bar_wait(drain, 0, 32u);
+            umma_commit_e(drain);
+            warp_wait(drain, 0, 32u);
         }
     } else if (warp >= kSoftWarps) {
         // ------------------------------------------------------------ converters
-        const int ct = threadIdx.x - kSoftWarps * 32; // 0..255
+        // Warps 4-7 write key tiles, warps 8-11 value tiles; each half runs at its
+        // own pace (keys free once QK^T is done, values once PV is done).  Thread ct
+        // handles four units of 8 elements per group; a unit's channel (keys) or
+        // channel group (values) is fixed, so its range factor is computed once.
+        const bool keys = warp < kSoftWarps + kConvHalf;
+        const int ct = threadIdx.x - (keys ? kSoftWarps : kSoftWarps + kConvHalf) * 32; // 0..127
+        float fac[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int u = ct + 128 * r;
+            // keys: channel 8 (u / 32) + u % 8, factor 2^(14 - E_d); values: channel
+            // group u / 128 = r, factor 2^(14 - F_cg) (dequantized values < 2^13)
+            fac[r] = keys ? exp2i_(14 - kexp[8 * (u >> 5) + (u & 7)]) : exp2i_(14 - vexp[r]);
+        }
+        uint64_t *ready = keys ? k_ready : v_ready;
+        uint64_t *freed = keys ? k_free : v_free;
+        const int nbuf = keys ? kK : kV;
         bool ok = true;
         for (int g = 0; ok && g < ng; ++g) {
-            const int st = g % NS, j = g >> 1, bk = j % kKV, half = g & 1;
-            // the tile's buffers are free once PV(j - kKV) is done (first group of a tile)
+            const int st = g % NS, j = g >> 1, half = g & 1, bb = j % nbuf;
+            // the tile's buffer is free once QK^T (keys) or PV (values) of tile
+            // j - nbuf is done (checked at the tile's first group)
             if (!warp_wait(&full[st], (g / NS) & 1, 64u) ||
-                (half == 0 && j >= kKV && !warp_wait(&pv_done[(j - kKV) % kS], ((j - kKV) / kS) & 1, 64u))) {
+                (half == 0 && j >= nbuf && !warp_wait(&freed[bb], ((j - nbuf) / nbuf) & 1, 64u))) {
                 ok = false;
                 break;
             }
-            unsigned char *base = sm + kStages + st * SG::STAGE;
-            const uint32_t *KC = reinterpret_cast<const uint32_t *>(base);
-            float2 *KP = reinterpret_cast<float2 *>(base + SG::KC);
-            const uint32_t *VC = reinterpret_cast<const uint32_t *>(base + SG::KC + SG::KP);
-            float2 *VP = reinterpret_cast<float2 *>(base + SG::KC + SG::KP + SG::VC);
-            // parameters pre-multiplied by the power-of-two range factors
-            // (keys 2^(14 - E_d), values 2^(14 - F_cg): dequantized values < 2^13)
-            if (ct < kD) {
-                const float f = exp2i_(14 - kexp[ct]);
-                const float2 p = KP[ct];
-                KP[ct] = make_float2(p.x * f, p.y * f);
-            } else {
-                const int e = ct - kD; // (token e/4, channel group e%4)
-                const float f = exp2i_(14 - vexp[e & 3]);
-                const float2 p = VP[e];
-                VP[e] = make_float2(p.x * f, p.y * f);
-            }
-            // all eight warps' rewrites done (bounded, unlike a named barrier)
-            __syncwarp();
-            if (lane == 0) bar_arrive(&pscaled[st]);
-            if (!warp_wait(&pscaled[st], (g / NS) & 1, 64u)) {
-                ok = false;
-                break;
-            }
-            unsigned char *khi = sm + kKbuf + bk * 32768, *klo = khi + 16384;
-            unsigned char *vhi = sm + kVbuf + bk * 32768, *vlo = vhi + 16384;
+            const unsigned char *base = sm + kStages + st * SG::STAGE;
+            if (keys) {
+                const uint32_t *KC = reinterpret_cast<const uint32_t *>(base);
+                const float2 *KP = reinterpret_cast<const float2 *>(base + SG::KC);
+                unsigned char *khi = sm + kKbuf + bb * 32768, *klo = khi + 16384;
 #pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                const int tau = ct + 256 * r;
-                float x[8];
-                {
-                    // keys, MN-major (n = token, SBO 2048): channel kd, tokens
-                    // 8 tb .. 8 tb + 7 of this group (one word, one (scale, zero))
-                    const int kd = 8 * (tau >> 5) + (tau & 7), tb = (tau >> 3) & 3;
+                for (int r = 0; r < 4; ++r) {
+                    // MN-major (n = token, SBO 2048): channel kd, tokens 8 tb .. 8 tb + 7
+                    // of this group (one code word, one (scale, zero))
+                    const int u = ct + 128 * r;
+                    const int kd = 8 * (u >> 5) + (u & 7), tb = (u >> 3) & 3;
                     const int bit0 = 8 * tb * BITS;
                     const uint32_t w = KC[kd * SG::IPC + (bit0 >> 5)];
                     const float2 p = KP[kd];
+                    const float sc = p.x * fac[r], zc = p.y * fac[r];
+                    float x[8];
 #pragma unroll
-                    for (int k = 0; k < 8; ++k) x[k] = fmaf(code_f(w, (bit0 & 31) + k * BITS, kMask), p.x, p.y);
+                    for (int k = 0; k < 8; ++k) x[k] = fmaf(code_f(w, (bit0 & 31) + k * BITS, kMask), sc, zc);
                     const int koff = (4 * half + tb) * 2048 + (kd >> 3) * 128 + (kd & 7) * 16;
                     store_split8(x, khi + koff, klo + koff);
                 }
-                // values, MN-major (k = token, SBO 1024): token t, channels 8j .. 8j+7
-                const int t = (tau & 7) + 8 * ((tau >> 5) & 3);
-                const int jj = ((tau >> 3) & 3) + 4 * (tau >> 7);
-                const int cg = jj >> 2;
-                const int cin = (jj & 3) * 8;                   // first channel within the group
-                const int vwi = (cin * BITS) >> 5, vsh = (cin % (32 / BITS)) * BITS;
-                const uint32_t w = VC[(t * 4 + cg) * SG::IPC + vwi];
-                const float2 p = VP[t * 4 + cg];
+            } else {
+                const uint32_t *VC = reinterpret_cast<const uint32_t *>(base + SG::KC + SG::KP);
+                const float2 *VP = reinterpret_cast<const float2 *>(base + SG::KC + SG::KP + SG::VC);
+                unsigned char *vhi = sm + kVbuf + bb * 32768, *vlo = vhi + 16384;
 #pragma unroll
-                for (int k = 0; k < 8; ++k) x[k] = fmaf(code_f(w, vsh + k * BITS, kMask), p.x, p.y);
-                const int tt = 32 * half + t;
-                const int voff = jj * 1024 + (tt >> 3) * 128 + (tt & 7) * 16;
-                store_split8(x, vhi + voff, vlo + voff);
+                for (int r = 0; r < 4; ++r) {
+                    // MN-major (k = token, SBO 1024): token t, channels 8 jj .. 8 jj + 7
+                    const int u = ct + 128 * r;
+                    const int t = (u & 7) + 8 * ((u >> 5) & 3);
+                    const int jj = ((u >> 3) & 3) + 4 * r;  // channel group r
+                    const int cin = (jj & 3) * 8;            // first channel within the group
+                    const int vwi = (cin * BITS) >> 5, vsh = (cin % (32 / BITS)) * BITS;
+                    const uint32_t w = VC[(t * 4 + r) * SG::IPC + vwi];
+                    const float2 p = VP[t * 4 + r];
+                    const float sc = p.x * fac[r], zc = p.y * fac[r];
+                    float x[8];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) x[k] = fmaf(code_f(w, vsh + k * BITS, kMask), sc, zc);
+                    const int tt = 32 * half + t;
+                    const int voff = jj * 1024 + (tt >> 3) * 128 + (tt & 7) * 16;
+                    store_split8(x, vhi + voff, vlo + voff);
+                }
             }
-            proxy_fence();
+            // a tile is ready after its last group (one group in the CTA's last odd
+            // tile); the proxy fence there orders both groups' writes before the MMAs
+            const bool last = half == 1 || g == ng - 1;
+            if (last) proxy_fence();
             __syncwarp();
             if (lane == 0) {
-                // a tile is ready after its last group (one group in the CTA's last odd tile)
-                if (half == 1 || g == ng - 1) bar_arrive(&kv_ready[bk]);
+                if (last) bar_arrive(&ready[bb]);
                 bar_arrive(&empty[st]);
             }
         }
@@ -598,26 +661,31 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
         bool have = ok && nt > 0;
         if (have && !warp_wait(&pv_done[(nt - 1) % kS], ((nt - 1) / kS) & 1, 128u)) have = false;
         tc_fence_after();
-        float o[kD];
-        if (have) {
-#pragma unroll
-            for (int c4 = 0; c4 < 4; ++c4) tmem_ld32(lane_base + kO + 32 * c4, o + 32 * c4);
-        }
-        if (m < rows_valid) {
+        const bool mine = m < rows_valid;
+        float *po = nullptr, *pml = nullptr;
+        if (mine) {
             const int z = z0 + m / a.GQ, h = m % a.GQ;
             const int64_t row = (int64_t)z * a.rows_per_set + (int64_t)b * a.Hq + kvh * a.GQ + h;
-            float *po = a.part_o + (row * a.parts + chunk) * kD;
-            float *pml = a.part_ml + (row * a.parts + chunk) * 2;
-            if (have) {
-                // O = sum p v = O' 2^(F_cg - 14) 2^-(15 - kLazyBits)
-                for (int d = 0; d < kD; ++d) po[d] = o[d] * exp2i_(vexp[d >> 5] - 29 + kLazyBits);
-                pml[0] = mref * 0.6931471805599453f;
-                pml[1] = l;
-            } else {
-                for (int d = 0; d < kD; ++d) po[d] = 0.0f;
-                pml[0] = -INFINITY;
-                pml[1] = 0.0f;
+            po = a.part_o + (row * a.parts + chunk) * kD;
+            pml = a.part_ml + (row * a.parts + chunk) * 2;
+        }
+#pragma unroll 1
+        for (int c4 = 0; c4 < 4; ++c4) {
+            // channel group c4: O = sum p v = O' 2^(F_cg - 14) 2^-(15 - kLazyBits)
+            float o[32];
+            if (have) tmem_ld32(lane_base + kO + 32 * c4, o); // warp-collective
+            const float f = exp2i_(vexp[c4] - 29 + kLazyBits);
+            if (mine) {
+                float4 *dst = reinterpret_cast<float4 *>(po + 32 * c4);
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    dst[i] = have ? make_float4(o[4 * i] * f, o[4 * i + 1] * f, o[4 * i + 2] * f, o[4 * i + 3] * f)
+                                  : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             }
+        }
+        if (mine) {
+            pml[0] = have ? mref * 0.6931471805599453f : -INFINITY;
+            pml[1] = have ? l : 0.0f;
         }
     }
     tc_fence_before();
