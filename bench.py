@@ -606,9 +606,13 @@ def run_gpu(args, cfgd, rank, world, local_rank):
 
     # Per-kernel durations: P more steps, each launch bracketed by CUDA events
     # on its stream (kept out of the timed region above).
+    # Each profiled step starts behind a short device-side hold, so the host has
+    # enqueued the step's launches before the device reaches them and every
+    # event pair brackets its own kernel (not host launch gaps).
     K.lib().kivi_profile_reset()
     K.lib().kivi_profile_enable(1)
     for i in range(P):
+        K.lib().kivi_profile_hold(2000, ctypes.c_void_p(stream.cuda_stream))
         wl.prof_step(i)
     stream.synchronize()
     K.lib().kivi_profile_enable(0)

@@ -141,6 +141,11 @@ uint64_t kivi_kernel_launches(void);
 void kivi_profile_enable(int32_t on);
 int32_t kivi_profile_read(const char *kernel, uint64_t *launches, double *total_ms);
 void kivi_profile_reset(void);
+/* Profiling aid (no counterpart in the reference): one kernel on `stream`
+ * that spins for `microseconds` (at most 100000) of device time, so that the
+ * host can enqueue the launches that follow before the device reaches them
+ * and each event pair brackets its kernel alone. */
+int32_t kivi_profile_hold(uint64_t microseconds, void *stream);
 
 /* ---------------------------------------------------------------- config.rs */
 

@@ -8,20 +8,23 @@
 //
 //   per CTA: one stream (kv head), one run of its 32-token groups, all query
 //   rows of up to 128/GQ sets (row m = set * GQ + head, padded to 128);
-//   S = Q K^T   tcgen05.mma kind::f16, M = 128 rows, N = 64 tokens (two
-//               groups), K = 128; Q is the A operand in tensor memory, the
-//               key tile the B operand in shared memory, S in tensor memory
-//               (two S buffers);
+//   S = Q K^T   tcgen05.mma kind::f16, M = 128 rows, K = 128, over a tile of
+//               64 tokens (two groups); Q is the A operand in tensor memory,
+//               the key tile the B operand in shared memory, S in tensor
+//               memory (two S buffers);
 //   softmax     one thread per row reads its S row from tensor memory and
-//               writes P (fp16 hi/lo) back to tensor memory;
+//               writes P (fp16 hi/lo) back over it;
 //   O += P V    tcgen05.mma kind::f16, M = 128, N = 128 channels, K = 64
 //               tokens, P from tensor memory, O accumulated in tensor memory
 //               across all the CTA's groups.
 //
 // fp32 accuracy from fp16 operands: every operand x is split into
 // hi = x truncated to 11 significant bits and lo = x - hi (exact), and each
-// product is formed as hi*hi + lo*hi + hi*lo in the fp32 accumulator (~22
-// significant bits; the dropped lo*lo is below 2^-22 relative).  Both parts
+// product is formed as hi*hi + lo*hi + hi*lo in fp32 accumulators (~22
+// significant bits; the dropped lo*lo is below 2^-22 relative).  The key tile
+// stores its lo half after its hi half in the token direction, so
+// Q_hi [K_hi | K_lo] is one N = 128 MMA per K step and Q_lo K_hi one N = 64
+// MMA into the first half; softmax adds the two halves.  Both parts
 // must be fp16 normals, so every operand is scaled into the upper fp16 range
 // by powers of two: keys are dequantized exactly as the reference does,
 // fma(code, scale, zero) (quant.rs:404-406), with (scale, zero) pre-multiplied
@@ -84,10 +87,11 @@ constexpr int kLazyBits = KIVI_SETS_LAZY;          // log2 headroom of the softm
 constexpr float kLazy2 = (float)kLazyBits;
 constexpr float kPScale = (float)(1 << (15 - kLazyBits)); // p * kPScale <= 2^15
 // tensor-memory columns (fp32 words; fp16 operands two per column):
-// S[b] 64b .. 64b + 63, P[b] 128 + 64b: hi (32 columns) then lo (32), Q_hi 256..319,
-// Q_lo 320..383, O 384..511
+// S[b] 128b .. 128b + 127 (Q_hi K_hi + Q_lo K_hi in the first 64, Q_hi K_lo in
+// the second 64; P[b] overwrites the first 64 once softmax has read them: hi 32
+// columns, then lo 32), Q_hi 256..319, Q_lo 320..383, O 384..511
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kSc = 0, kP = 128, kQH = 256, kQL = 320, kO = 384;
+constexpr uint32_t kSc = 0, kQH = 256, kQL = 320, kO = 384;
 
 // shared-memory map (bytes): per key/value tile hi and lo parts of 16 KB each
 constexpr int kKbuf = 0;                            // [kK] x (hi, lo): 128 channels x 64 tokens
@@ -217,6 +221,14 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float *v) {
         : "memory");
 }
 
+// 2^x by the MUFU approximation (relative error ~2^-22; -inf -> 0, results
+// below 2^-126 flush to 0)
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __device__ __forceinline__ float exp2i_(int k) {
     k = max(-126, min(127, k));
     return __uint_as_float((uint32_t)(k + 127) << 23);
@@ -276,6 +288,40 @@ __device__ __forceinline__ void umma_commit_e(uint64_t *b) {
         "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
         "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(su32(b))
         : "memory");
+}
+
+// Byte permute: bytes of {a, b} (a = bytes 0-3) chosen by the four selector nibbles.
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+// 2-bit codes: the four dequantized values fma(c, s, z), c = 0..3 (the
+// reference's dequantization, quant.rs:404-406), as fp16 hi parts (th0 = c 0,1;
+// th1 = c 2,3) and lo parts.
+__device__ __forceinline__ void table2(float s, float z, uint32_t &th0, uint32_t &th1, uint32_t &tl0,
+                                       uint32_t &tl1) {
+    split_pair(fmaf(0.0f, s, z), fmaf(1.0f, s, z), th0, tl0);
+    split_pair(fmaf(2.0f, s, z), fmaf(3.0f, s, z), th1, tl1);
+}
+
+// Eight consecutive 2-bit codes (low 16 bits of w, first code lowest) -> the
+// eight fp16 hi values (16 bytes) and lo values, by table lookup: a pair of
+// codes (c0, c1) = nibble n selects bytes 2 c0, 2 c0 + 1, 2 c1, 2 c1 + 1 of the
+// 8-byte table, selector 0x1010 + 0x22 c0 + 0x2200 c1.
+__device__ __forceinline__ void lookup8(uint32_t w, uint32_t th0, uint32_t th1, uint32_t tl0, uint32_t tl1,
+                                        unsigned char *hi, unsigned char *lo) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const uint32_t n = w >> (4 * q);
+        const uint32_t sel = 0x1010u + 0x22u * (n & 3u) + 0x880u * (n & 0xCu);
+        h[q] = prmt(th0, th1, sel);
+        l[q] = prmt(tl0, tl1, sel);
+    }
+    *reinterpret_cast<uint4 *>(hi) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4 *>(lo) = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
 // code (0..2^BITS-1) as an exact float: mantissa of 2^23, minus 2^23
@@ -445,7 +491,8 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
     } else if (warp == kMmaWarp) {
         // ------------------------------------------------------------ MMA issuer (whole warp)
         {
-            constexpr uint32_t id_qk = idesc_f16(128, kTile, 1);
+            constexpr uint32_t id_qk2 = idesc_f16(128, 2 * kTile, 1); // B = [K_hi | K_lo]
+            constexpr uint32_t id_qk = idesc_f16(128, kTile, 1);      // B = K_hi
             constexpr uint32_t id_pv = idesc_f16(128, kD, 1);
             // descriptors of the shared-memory tiles: the start-address field holds
             // address / 16, so a K step of 16 elements (256 bytes) is +16 and buffer
@@ -461,7 +508,7 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
                     return false;
                 tc_fence_after();
                 const int ksteps = (2 * j + 1 < ng) ? 4 : 2;
-                const uint32_t ph = tbase + kP + 64 * bj, pl = ph + 32;
+                const uint32_t ph = tbase + kSc + 128 * bj, pl = ph + 32;
                 const uint64_t vh = dv0 + (uint64_t)bv * 2048u, vl = vh + 1024u;
 #pragma unroll 1
                 for (int ks = 0; ks < ksteps; ++ks) {
@@ -485,15 +532,15 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
                     break;
                 }
                 tc_fence_after();
-                const uint32_t sacc = tbase + kSc + 64 * bs;
-                const uint64_t kh = dk0 + (uint64_t)bk * 2048u, kl = kh + 1024u;
+                // the key tile's lo half follows its hi half in the token (N)
+                // direction, so one N = 128 MMA forms Q_hi K_hi and Q_hi K_lo
+                const uint32_t sacc = tbase + kSc + 128 * bs;
+                const uint64_t kh = dk0 + (uint64_t)bk * 2048u;
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks)
-                    umma_ts(sacc, tbase + kQH + 8 * ks, kh + 16 * ks, id_qk, ks > 0 ? 1u : 0u);
+                    umma_ts(sacc, tbase + kQH + 8 * ks, kh + 16 * ks, id_qk2, ks > 0 ? 1u : 0u);
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks) umma_ts(sacc, tbase + kQL + 8 * ks, kh + 16 * ks, id_qk, 1u);
-#pragma unroll
-                for (int ks = 0; ks < 8; ++ks) umma_ts(sacc, tbase + kQH + 8 * ks, kl + 16 * ks, id_qk, 1u);
                 umma_commit_e(&s_full[bs]);
                 umma_commit_e(&k_free[bk]);
                 if (j >= 1 && !pv(j - 1)) ok = false;
@@ -506,18 +553,26 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
     } else if (warp >= kSoftWarps) {
         // ------------------------------------------------------------ converters
         // Warps 4-7 write key tiles, warps 8-11 value tiles; each half runs at its
-        // own pace (keys free once QK^T is done, values once PV is done).  Thread ct
-        // handles four units of 8 elements per group; a unit's channel (keys) or
-        // channel group (values) is fixed, so its range factor is computed once.
+        // own pace (keys free once QK^T is done, values once PV is done).
+        // 2-bit: key thread ct owns channel ct (32 tokens per group), value thread
+        // ct owns token ct % 32 of channel group ct / 32 (32 channels): one
+        // (scale, zero), so one four-entry table per group, and each 8-element
+        // unit is eight byte permutes.  Each 8-lane phase of a 16-byte store
+        // then covers 128 contiguous bytes (no bank conflicts).  4-bit: thread ct handles four units of 8 elements
+        // (keys: channel 8 (u / 32) + u % 8, tokens 8 ((u / 8) % 4) ..; values:
+        // token (u % 8) + 8 ((u / 32) % 4), channel group u / 128), dequantized
+        // with fma(code, scale, zero).
         const bool keys = warp < kSoftWarps + kConvHalf;
         const int ct = threadIdx.x - (keys ? kSoftWarps : kSoftWarps + kConvHalf) * 32; // 0..127
         float fac[4];
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
             const int u = ct + 128 * r;
-            // keys: channel 8 (u / 32) + u % 8, factor 2^(14 - E_d); values: channel
-            // group u / 128 = r, factor 2^(14 - F_cg) (dequantized values < 2^13)
-            fac[r] = keys ? exp2i_(14 - kexp[8 * (u >> 5) + (u & 7)]) : exp2i_(14 - vexp[r]);
+            // range factors: keys 2^(14 - E_d), values 2^(14 - F_cg) (dequantized values < 2^13)
+            if (BITS == 2)
+                fac[r] = keys ? exp2i_(14 - kexp[ct]) : exp2i_(14 - vexp[ct >> 5]);
+            else
+                fac[r] = keys ? exp2i_(14 - kexp[8 * (u >> 5) + (u & 7)]) : exp2i_(14 - vexp[r]);
         }
         uint64_t *ready = keys ? k_ready : v_ready;
         uint64_t *freed = keys ? k_free : v_free;
@@ -533,7 +588,38 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
                 break;
             }
             const unsigned char *base = sm + kStages + st * SG::STAGE;
-            if (keys) {
+            if (BITS == 2 && keys) {
+                // channel kd = ct: tokens 0-15 in word 0, 16-31 in word 1; MN-major
+                // (n = token, SBO 2048), 8 tokens of one channel per 16 bytes
+                const uint2 w2 = reinterpret_cast<const uint2 *>(base)[ct];
+                const float2 p = reinterpret_cast<const float2 *>(base + SG::KC)[ct];
+                uint32_t th0, th1, tl0, tl1;
+                table2(p.x * fac[0], p.y * fac[0], th0, th1, tl0, tl1);
+                unsigned char *khi = sm + kKbuf + bb * 32768, *klo = khi + 16384;
+                const int koff = 4 * half * 2048 + (ct >> 3) * 128 + (ct & 7) * 16;
+#pragma unroll
+                for (int tb = 0; tb < 4; ++tb) {
+                    const uint32_t w = (tb < 2 ? w2.x : w2.y) >> (16 * (tb & 1));
+                    lookup8(w, th0, th1, tl0, tl1, khi + koff + tb * 2048, klo + koff + tb * 2048);
+                }
+            } else if (BITS == 2) {
+                // token t = ct % 32, channel group cg = ct / 32: channels 0-15 of the
+                // group in word 0, 16-31 in word 1; MN-major (k = token, SBO 1024),
+                // 8 channels of one token per 16 bytes
+                const int t = ct & 31, cg = ct >> 5;
+                const uint2 w2 = reinterpret_cast<const uint2 *>(base + SG::KC + SG::KP)[t * 4 + cg];
+                const float2 p = reinterpret_cast<const float2 *>(base + SG::KC + SG::KP + SG::VC)[t * 4 + cg];
+                uint32_t th0, th1, tl0, tl1;
+                table2(p.x * fac[0], p.y * fac[0], th0, th1, tl0, tl1);
+                unsigned char *vhi = sm + kVbuf + bb * 32768, *vlo = vhi + 16384;
+                const int tt = 32 * half + t;
+                const int voff = 4 * cg * 1024 + (tt >> 3) * 128 + (tt & 7) * 16;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const uint32_t w = (u < 2 ? w2.x : w2.y) >> (16 * (u & 1));
+                    lookup8(w, th0, th1, tl0, tl1, vhi + voff + u * 1024, vlo + voff + u * 1024);
+                }
+            } else if (keys) {
                 const uint32_t *KC = reinterpret_cast<const uint32_t *>(base);
                 const float2 *KP = reinterpret_cast<const float2 *>(base + SG::KC);
                 unsigned char *khi = sm + kKbuf + bb * 32768, *klo = khi + 16384;
@@ -600,15 +686,26 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
                 break;
             }
             tc_fence_after();
+            // S = (Q_hi K_hi + Q_lo K_hi) + Q_hi K_lo: columns i and 64 + i
             float x[64];
-            tmem_ld32(lane_base + kSc + 64 * bs, x);
-            tmem_ld32(lane_base + kSc + 64 * bs + 32, x + 32);
+            const uint32_t srow = lane_base + kSc + 128 * bs;
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                float t[32];
+                tmem_ld32(srow + 32 * hh, x + 32 * hh);
+                tmem_ld32(srow + 64 + 32 * hh, t);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) x[32 * hh + i] += t[i];
+            }
+            // logits are x rowfac (exp2 units); the max is taken on the raw scores
+            // (rowfac > 0 and rounding is monotone, so max(x) rowfac = max(x rowfac))
             float mx = -INFINITY;
 #pragma unroll
             for (int i = 0; i < 64; ++i) {
-                x[i] = (i < 32 || two) ? x[i] * rowfac : -INFINITY;
+                if (i >= 32 && !two) x[i] = -INFINITY;
                 mx = fmaxf(mx, x[i]);
             }
+            mx *= rowfac;
             const bool need = mx > mref + kLazy2;
             if (__any_sync(0xffffffffu, need)) {
                 const float nref = need ? mx : mref;
@@ -634,23 +731,25 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
                 }
             }
             if (!ok) break;
+            // P' = p kPScale = 2^(x rowfac - mref + 15 - kLazyBits) <= 2^15, fp16
+            // normal down to p = 2^(kLazyBits - 29); l accumulates p = P' / kPScale
+            const float off = (float)(15 - kLazyBits) - mref;
             float psum = 0.0f;
 #pragma unroll
             for (int i = 0; i < 64; ++i) {
-                x[i] = exp2f(x[i] - mref);
+                x[i] = ex2_approx(fmaf(x[i], rowfac, off));
                 psum += x[i];
-                x[i] *= kPScale; // <= 2^15, fp16 normal down to p = 2^(kLazyBits - 29)
             }
-            l += psum;
-            // P[bs] shares its buffer's life with S[bs]: free (PV(j - kS) done) since
-            // the MMA issued QK(j) into S[bs]
+            l += psum * (1.0f / kPScale);
+            // P(j) overwrites the first half of S[bs] (read above); QK(j + kS)
+            // rewrites S[bs] only after PV(j) in issue order
             uint32_t hi[16], lo[16];
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
 #pragma unroll
                 for (int q = 0; q < 16; ++q) split_pair(x[32 * hh + 2 * q], x[32 * hh + 2 * q + 1], hi[q], lo[q]);
-                tmem_st16(lane_base + kP + 64 * bs + 16 * hh, hi);
-                tmem_st16(lane_base + kP + 64 * bs + 32 + 16 * hh, lo);
+                tmem_st16(srow + 16 * hh, hi);
+                tmem_st16(srow + 32 + 16 * hh, lo);
             }
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tc_fence_before();

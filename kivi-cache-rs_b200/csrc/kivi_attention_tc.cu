@@ -844,21 +844,36 @@ __global__ void __launch_bounds__(kTailThreads) attn_tail_kernel(const TailArgs 
 
     for (int e = threadIdx.x; e < a.GQ * 128; e += kTailThreads)
         Qs[e] = a.q[(rbase + (int64_t)b * a.Hq + kvh * a.GQ) * 128 + e];
-    for (int e = threadIdx.x; e < nt * 32; e += kTailThreads) {
+    // Each thread stages 8 (token, 4 channels) units of K and V: every load is
+    // issued before the first shared-memory store, so one memory latency covers
+    // the tile (a warp's 32 lanes share one token: the source branch is uniform).
+    constexpr int kUnits = kTailTokens * 32 / kTailThreads;
+    float4 k4[kUnits], v4[kUnits];
+#pragma unroll
+    for (int i = 0; i < kUnits; ++i) {
+        const int e = threadIdx.x + i * kTailThreads;
         const int tt = e >> 5, d = (e & 31) * 4;
-        const int64_t t = t0 + tt;
-        const float4 k4 = tail_key4<BITS>(a, kc, kp, kres, sk, t, d);
-        const float4 v4 = tail_value4<BITS>(a, vc, vp, vres, sv, t, d);
-        float *kd = Ks + tt * kTailPitch + d;
-        float *vd = Vs + tt * kTailPitch + d;
-        kd[0] = k4.x;
-        kd[1] = k4.y;
-        kd[2] = k4.z;
-        kd[3] = k4.w;
-        vd[0] = v4.x;
-        vd[1] = v4.y;
-        vd[2] = v4.z;
-        vd[3] = v4.w;
+        if (tt < nt) {
+            k4[i] = tail_key4<BITS>(a, kc, kp, kres, sk, t0 + tt, d);
+            v4[i] = tail_value4<BITS>(a, vc, vp, vres, sv, t0 + tt, d);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < kUnits; ++i) {
+        const int e = threadIdx.x + i * kTailThreads;
+        const int tt = e >> 5, d = (e & 31) * 4;
+        if (tt < nt) {
+            float *kd = Ks + tt * kTailPitch + d;
+            float *vd = Vs + tt * kTailPitch + d;
+            kd[0] = k4[i].x;
+            kd[1] = k4[i].y;
+            kd[2] = k4[i].z;
+            kd[3] = k4[i].w;
+            vd[0] = v4[i].x;
+            vd[1] = v4[i].y;
+            vd[2] = v4[i].z;
+            vd[3] = v4[i].w;
+        }
     }
     __syncthreads();
 

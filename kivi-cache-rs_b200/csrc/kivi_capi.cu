@@ -78,6 +78,23 @@ ProfScope::ProfScope(const char *kernel, cudaStream_t s) : name(kernel), stream(
     rec = r;
 }
 
+namespace {
+// bounded device-time spin (globaltimer, ns); one thread
+__global__ void profile_hold_kernel(uint64_t ns) {
+    uint64_t t0, t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    do {
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    } while (t - t0 < ns);
+}
+} // namespace
+
+cudaError_t launch_profile_hold(uint64_t us, cudaStream_t s) {
+    if (us > 100000) us = 100000;
+    profile_hold_kernel<<<1, 1, 0, s>>>(us * 1000ull);
+    return cudaGetLastError();
+}
+
 ProfScope::~ProfScope() {
     if (!rec) return;
     ProfRecord *r = (ProfRecord *)rec;
@@ -667,6 +684,10 @@ struct kivi_prefix {
     // value exponents; computed on first use (the prefix never changes)
     int *bounds = nullptr;
     std::mutex bounds_mu;
+    // recorded once by each batched `_dev` call over sessions of this prefix
+    // (instead of one record per session); the sessions' synchronous calls wait
+    // for it as well as for their own dev_done
+    cudaEvent_t batch_done = nullptr;
 };
 
 struct kivi_session {
@@ -692,6 +713,13 @@ cudaStream_t pick(void *user, cudaStream_t /*own*/) { return (cudaStream_t)user;
 cudaError_t mark_dev(cudaEvent_t ev, cudaStream_t st) { return cudaEventRecord(ev, st); }
 
 cudaError_t wait_dev(cudaStream_t own, cudaEvent_t ev) { return cudaStreamWaitEvent(own, ev, 0); }
+
+// a session's last device work: its own `_dev` calls and its prefix's batched ones
+cudaError_t wait_session(cudaStream_t own, const kivi_session *s) {
+    cudaError_t e = cudaStreamWaitEvent(own, s->dev_done, 0);
+    if (e == cudaSuccess && s->prefix->batch_done) e = cudaStreamWaitEvent(own, s->prefix->batch_done, 0);
+    return e;
+}
 
 int32_t init_state(KvState &s, const kivi_config *cfg, uint64_t B, uint64_t H, uint64_t D,
                    int32_t device, kivi_error *err) {
@@ -759,6 +787,11 @@ int32_t kivi_profile_read(const char *kernel, uint64_t *launches, double *total_
     if (launches) *launches = n;
     if (total_ms) *total_ms = ms;
     return KIVI_OK;
+}
+
+int32_t kivi_profile_hold(uint64_t microseconds, void *stream) {
+    return kivi::launch_profile_hold(microseconds, (cudaStream_t)stream) == cudaSuccess ? KIVI_OK
+                                                                                          : KIVI_ERR_CUDA;
 }
 
 void kivi_profile_reset(void) {
@@ -1140,6 +1173,7 @@ int32_t kivi_cache_share_prefix(const kivi_cache *h, kivi_prefix **out, kivi_err
     cudaError_t e;
     const size_t res = n * R * D;
     if ((e = cudaStreamCreateWithFlags(&p->stream, cudaStreamNonBlocking)) != cudaSuccess ||
+        (e = cudaEventCreateWithFlags(&p->batch_done, cudaEventDisableTiming)) != cudaSuccess ||
         (e = dalloc(&p->s.st.kcodes, n * kivi::code_stride(g, cap))) != cudaSuccess ||
         (e = dalloc(&p->s.st.kparams, n * kivi::kparam_stride(g, cap))) != cudaSuccess ||
         (e = dalloc(&p->s.st.vcodes, n * kivi::code_stride(g, cap))) != cudaSuccess ||
@@ -1148,6 +1182,7 @@ int32_t kivi_cache_share_prefix(const kivi_cache *h, kivi_prefix **out, kivi_err
         (e = dalloc(&p->s.st.vres, res)) != cudaSuccess) {
         free_store(p->s.st);
         if (p->stream) cudaStreamDestroy(p->stream);
+        if (p->batch_done) cudaEventDestroy(p->batch_done);
         delete p;
         return cuda_fail(err, e, "share_prefix");
     }
@@ -1193,6 +1228,7 @@ void kivi_prefix_release(kivi_prefix *p) {
     free_store(p->s.st);
     if (p->bounds) cudaFree(p->bounds);
     if (p->stream) cudaStreamDestroy(p->stream);
+    if (p->batch_done) cudaEventDestroy(p->batch_done);
     delete p;
 }
 
@@ -1252,6 +1288,7 @@ void kivi_session_free(kivi_session *s) {
     {
         DeviceGuard dg(s->prefix->s.device);
         if (s->dev_done) cudaEventSynchronize(s->dev_done);
+        if (s->prefix->batch_done) cudaEventSynchronize(s->prefix->batch_done);
         if (s->stream) cudaStreamSynchronize(s->stream);
         dfree(s->k);
         dfree(s->v);
@@ -1331,6 +1368,7 @@ int32_t kivi_session_reserve(kivi_session *s, uint64_t tokens, kivi_error *err) 
     if (!s) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null session");
     DeviceGuard dg(s->prefix->s.device);
     if (tokens <= s->len) return set_err(err, KIVI_OK);
+    CUDA_TRY(wait_session(s->stream, s), "session reserve");
     int32_t rc = session_reserve(s, tokens - s->len, s->stream, err);
     if (rc) return rc;
     return set_err(err, KIVI_OK);
@@ -1367,10 +1405,8 @@ int32_t kivi_sessions_append_dev(kivi_session *const *ss, uint64_t nsess, const 
                                             (int)D, st),
                  "sessions append");
     }
-    for (uint64_t i = 0; i < nsess; ++i) {
-        ss[i]->len += seq;
-        CUDA_TRY(mark_dev(ss[i]->dev_done, st), "sessions append");
-    }
+    for (uint64_t i = 0; i < nsess; ++i) ss[i]->len += seq;
+    CUDA_TRY(mark_dev(p->batch_done, st), "sessions append");
     return set_err(err, KIVI_OK);
 }
 
@@ -1386,7 +1422,7 @@ int32_t kivi_session_append(kivi_session *s, const float *keys, uint64_t keys_le
     if (!keys || !values) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null input");
     std::lock_guard<std::mutex> lk(s->mu);
     DeviceGuard dg(p.device);
-    CUDA_TRY(wait_dev(s->stream, s->dev_done), "session append");
+    CUDA_TRY(wait_session(s->stream, s), "session append");
     int32_t rc = session_append(s, keys, values, seq, cudaMemcpyHostToDevice, s->stream, err);
     if (rc) return rc;
     CUDA_TRY(cudaStreamSynchronize(s->stream), "session append");
@@ -1478,7 +1514,7 @@ int32_t kivi_session_attention(const kivi_session *s, const float *query, uint64
     kivi_session *ms = const_cast<kivi_session *>(s);
     std::lock_guard<std::mutex> lk(ms->mu);
     DeviceGuard dg(p.device);
-    CUDA_TRY(wait_dev(s->stream, s->dev_done), "session attention");
+    CUDA_TRY(wait_session(s->stream, s), "session attention");
     CUDA_TRY(ms->stage.ensure(2 * n * 4), "session staging");
     float *dq = ms->stage.as<float>(), *dout = ms->stage.as<float>(n * 4);
     CUDA_TRY(cudaMemcpyAsync(dq, query, n * 4, cudaMemcpyHostToDevice, s->stream), "session H2D");
@@ -1501,7 +1537,7 @@ int32_t kivi_sessions_attention_batched_dev(const kivi_session *const *ss, uint6
     cudaStream_t st = pick(stream, lead->stream);
     int32_t rc = sessions_attention_dev(ss, n, dq, Hq, scale, dout, st, lead->part, err);
     if (rc) return rc;
-    CUDA_TRY(mark_dev(lead->dev_done, st), "batched attention_dev");
+    CUDA_TRY(mark_dev(lead->prefix->batch_done, st), "batched attention_dev");
     return set_err(err, KIVI_OK);
 }
 
@@ -1521,6 +1557,8 @@ int32_t kivi_sessions_attention_batched(const kivi_session *const *ss, uint64_t 
     DeviceGuard dg(p.device);
     for (uint64_t i = 0; i < n; ++i)
         CUDA_TRY(wait_dev(lead->stream, ss[i]->dev_done), "batched attention");
+    if (lead->prefix->batch_done)
+        CUDA_TRY(wait_dev(lead->stream, lead->prefix->batch_done), "batched attention");
     CUDA_TRY(lead->stage.ensure(2 * total * 4), "batched staging");
     float *dq = lead->stage.as<float>(), *dout = lead->stage.as<float>(total * 4);
     CUDA_TRY(cudaMemcpyAsync(dq, queries, total * 4, cudaMemcpyHostToDevice, lead->stream), "batched H2D");

@@ -109,6 +109,7 @@ def lib():
         "kivi_profile_enable": ([i32], None),
         "kivi_profile_read": ([C.c_char_p, u64p, C.POINTER(C.c_double)], i32),
         "kivi_profile_reset": ([], None),
+        "kivi_profile_hold": ([sz, P], i32),
         "kivi_config_default": ([C.POINTER(_Config)], i32),
         "kivi_config_try_new": ([C.c_uint32, sz, sz, C.POINTER(_Config), e], i32),
         "kivi_cache_new": ([C.POINTER(_Config), sz, sz, sz, i32, C.POINTER(P), e], i32),
