@@ -100,7 +100,12 @@ def load_traffic(kernel, workload):
 
 
 class ClockSampler:
-    """Samples SM clock and clock-event reasons through NVML while running."""
+    """SM clock and clock-event reasons sampled by a separate `nvidia-smi -lms`
+    process: NVML calls made from a thread of this process stalled its kernel
+    launches for milliseconds at a time, which a short timed region cannot
+    absorb.  The sampler starts before the warm-up (its first sample marks
+    NVML ready), writes to a file, and the samples inside the timed window are
+    kept (the nearest ones when the window is shorter than the period)."""
 
     REASONS = {
         0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
@@ -108,65 +113,105 @@ class ClockSampler:
         0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
         0x100: "display_clock_setting",
     }
+    FIELDS = "timestamp,clocks.sm,clocks.max.sm,clocks_event_reasons.active"
 
-    def __init__(self, device_index, period_s=0.01):
-        self.samples = []
-        self.reasons = 0
-        self.max_mhz = None
-        self._stop = threading.Event()
-        self._h = None
-        self.period = period_s
-        try:
-            import pynvml
+    def __init__(self, device_index, period_ms=20):
+        import tempfile
 
-            pynvml.nvmlInit()
-            self._nv = pynvml
-            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
-        except Exception:
-            self._h = None
-        self._t = threading.Thread(target=self._run, daemon=True)
+        self.idx = device_index
+        self.period_ms = period_ms
+        fd, self.path = tempfile.mkstemp(prefix="kivi_clocks_", suffix=".csv")
+        os.close(fd)
+        self.proc = None
+        self.t0 = self.t1 = None
 
-    def _sample(self):
-        nv = self._nv
-        mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
-        try:
-            r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
-        except Exception:
-            r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
-        self.samples.append(mhz)
-        self.reasons |= int(r) & ~0x1
+    def start(self):
+        import shutil
+        import subprocess
 
-    def _run(self):
-        while not self._stop.is_set():
-            try:
-                self._sample()
-            except Exception:
-                return
-            self._stop.wait(self.period)
-
-    def __enter__(self):
-        if self._h is not None:
-            self._t.start()
+        if not shutil.which("nvidia-smi"):
+            return self
+        env = dict(os.environ)
+        env.pop("CUDA_VISIBLE_DEVICES", None)  # -i takes the physical index
+        phys = self.idx
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if vis:
+            ids = [v.strip() for v in vis.split(",") if v.strip()]
+            if self.idx < len(ids) and ids[self.idx].isdigit():
+                phys = int(ids[self.idx])
+        self._f = open(self.path, "w")
+        self.proc = subprocess.Popen(
+            ["nvidia-smi", "-i", str(phys), f"--query-gpu={self.FIELDS}",
+             "--format=csv,noheader,nounits", "-lms", str(self.period_ms)],
+            stdout=self._f, stderr=subprocess.DEVNULL, env=env)
+        deadline = time.time() + 5.0
+        while time.time() < deadline:
+            if os.path.getsize(self.path) > 0:
+                break
+            time.sleep(0.01)
         return self
 
-    def __exit__(self, *a):
-        self._stop.set()
-        if self._h is not None:
-            self._t.join()
+    def mark_start(self):
+        import datetime
+
+        self.t0 = datetime.datetime.now()
+
+    def mark_end(self):
+        import datetime
+
+        self.t1 = datetime.datetime.now()
+
+    def stop(self):
+        if self.proc is None:
+            return
+        time.sleep(2 * self.period_ms / 1000.0)  # one sample past the window
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self._f.close()
+
+    def _rows(self):
+        import datetime
+
+        rows = []
+        try:
+            lines = open(self.path).read().splitlines()
+        except OSError:
+            return rows
+        for line in lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) != 4:
+                continue
             try:
-                self._sample()
-            except Exception:
-                pass
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f")
+                rows.append((ts, float(parts[1]), float(parts[2]), int(parts[3], 16)))
+            except ValueError:
+                continue
+        return rows
 
     def summary(self):
-        if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        rows = self._rows()
+        try:
+            os.unlink(self.path)
+        except OSError:
+            pass
+        if not rows or self.t0 is None or self.t1 is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        inside = [r for r in rows if self.t0 <= r[0] <= self.t1]
+        if not inside:  # window shorter than the period: the samples around it
+            before = [r for r in rows if r[0] < self.t0]
+            after = [r for r in rows if r[0] > self.t1]
+            inside = before[-1:] + after[:1]
+        reasons = 0
+        for r in inside:
+            reasons |= r[3] & ~0x1
         return {
-            "sm_mhz": float(np.median(self.samples)),
-            "sm_max_mhz": self.max_mhz,
-            "reasons": [n for b, n in self.REASONS.items() if self.reasons & b],
-            "samples": len(self.samples),
+            "sm_mhz": float(np.median([r[1] for r in inside])),
+            "sm_max_mhz": int(inside[0][2]),
+            "reasons": [n for b, n in self.REASONS.items() if reasons & b],
+            "samples": len(inside),
         }
 
 
@@ -580,6 +625,7 @@ def run_gpu(args, cfgd, rank, world, local_rank):
     else:
         wl = SeqShardWorkload(K, cfgd, rank, local_rank, W + S, P, stream, world)
 
+    clk = ClockSampler(local_rank).start()
     for i in range(W):
         wl.step(i)
     stream.synchronize()
@@ -591,13 +637,15 @@ def run_gpu(args, cfgd, rank, world, local_rank):
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local_rank) as clk:
-        ev0.record(stream)
-        for i in range(W, W + S):
-            wl.step(i)
-        ev1.record(stream)
-        stream.synchronize()
+    clk.mark_start()
+    ev0.record(stream)
+    for i in range(W, W + S):
+        wl.step(i)
+    ev1.record(stream)
+    stream.synchronize()
+    clk.mark_end()
     torch.cuda.synchronize()
+    clk.stop()
     if dist:
         dist.barrier()
     launches = K.kernel_launches() - launches0

@@ -34,14 +34,15 @@
 // p * 2^(15 - T) with the reference point moved only when a logit exceeds it
 // by T = 6 (exp2 units).  All factors are powers of two, undone exactly in fp32.
 //
-// Warp roles (448 threads): warps 0-3 softmax and epilogue (thread = row,
-// tensor-memory lanes 0..127); warps 4-7 dequantize each landed group into
-// the fp16 hi/lo key tile, warps 8-11 into the value tile; warp 12 lane 0
-// streams the packed groups in with bulk async copies (cp.async.bulk, into
-// this CTA only); warp 13 issues the MMAs (the whole warp runs the loop, one
-// elected lane issues) in the order QK(0), QK(1), PV(0), QK(2), PV(1), ...  Key tiles (two in flight) are released when their
-// QK^T completes, value tiles (three in flight) when their PV completes, so the
-// converters run ahead of the tensor pipe.  Operand tiles use the canonical
+// Warp roles (480 threads): warps 0-3 softmax and epilogue (thread = row,
+// tensor-memory lanes 0..127); eight converter warps dequantize each landed
+// tile into the fp16 hi/lo key tile (warps 4, 6, 7, 12) or value tile (8, 10,
+// 11, 14); warp 9 lane 0 streams the packed tiles in with bulk async copies
+// (cp.async.bulk, into this CTA only); warp 5 issues the MMAs (the whole warp
+// runs the loop, one elected lane issues) in the order QK(0), QK(1), PV(0),
+// QK(2), PV(1), ...; warp 13 idles.  Key tiles (three in flight) are released
+// when their QK^T completes, value tiles (three in flight) when their PV
+// completes, so the converters run ahead of the tensor pipe.  Operand tiles use the canonical
 // no-swizzle layouts: K-major addr(r, k) = (r/8)*SBO + (k/8)*128 + (r%8)*16 +
 // (k%8)*2, MN-major addr(k, n) = (n/8)*SBO + (k/8)*128 + (k%8)*16 + (n%8)*2.
 // Every mbarrier wait is bounded (~1 s); a wait that gives up sets a device
@@ -62,11 +63,21 @@ __device__ unsigned int g_sets_error = 0; // set by bounded waits that give up
 namespace {
 
 constexpr int kSoftWarps = 4;
-constexpr int kConvWarps = 8;                      // 4 key converters, then 4 value converters
+// Warp w runs on sub-partition w % 4.  Softmax warp w serves tensor-memory
+// lanes 32 (w % 4) ..; the MMA issuer shares its sub-partition only with
+// softmax warp 1, the producer and an idle warp, so the ALU-bound converters
+// (three, three and two on the other sub-partitions) do not take its issue slots.
+constexpr int kConvWarps = 8;  // 4 key converters, 4 value converters
 constexpr int kConvHalf = kConvWarps / 2;
-constexpr int kProdWarp = kSoftWarps + kConvWarps; // 12
-constexpr int kMmaWarp = kProdWarp + 1;            // 13
-constexpr int kSetThreads = (kMmaWarp + 1) * 32;   // 448
+constexpr int kMmaWarp = 5;
+constexpr int kProdWarp = 9;
+constexpr int kSetThreads = 15 * 32; // warp 13 idles
+// converter role of warp w: 0..3 key converter index, 4..7 value converter
+// index + 4, -1 for the other roles
+__host__ __device__ constexpr int conv_role(int w) {
+    return w == 4 ? 0 : w == 6 ? 1 : w == 7 ? 2 : w == 12 ? 3
+         : w == 8 ? 4 : w == 10 ? 5 : w == 11 ? 6 : w == 14 ? 7 : -1;
+}
 #ifndef KIVI_SETS_STAGES2
 #define KIVI_SETS_STAGES2 8
 #endif
@@ -75,7 +86,7 @@ constexpr int kTok = 32;                           // tokens per group = per S t
 constexpr long long kWait = 2000000000LL;          // ~1 s at B200 clocks
 constexpr int kTile = 64;   // tokens per S tile (two groups): QK^T runs at N = 64
 #ifndef KIVI_SETS_KBUF
-#define KIVI_SETS_KBUF 2
+#define KIVI_SETS_KBUF 3
 #endif
 constexpr int kK = KIVI_SETS_KBUF; // key operand tiles in flight (free once QK^T is done)
 constexpr int kV = 3;              // value operand tiles in flight (free once PV is done)
@@ -104,8 +115,12 @@ template <int BITS> struct SetGeom {
     static constexpr int KP = kD * 8;
     static constexpr int VC = kTok * 4 * IPC * 4;
     static constexpr int VP = kTok * 4 * 8;
-    static constexpr int STAGE = KC + KP + VC + VP;
-    // packed-group stages in flight: as many as shared memory leaves room for, up to 8
+    // one stage holds a tile's two consecutive groups, each array's two groups
+    // back to back (they are contiguous in the packed store): [KC KC][KP KP][VC VC][VP VP]
+    static constexpr int GROUP = KC + KP + VC + VP;
+    static constexpr int STAGE = 2 * GROUP;
+    static constexpr int OKP = 2 * KC, OVC = OKP + 2 * KP, OVP = OVC + 2 * VC;
+    // packed-tile stages in flight: as many as shared memory leaves room for, up to 8
     static constexpr int NS = std::min(KIVI_SETS_STAGES2, (232448 - 1024 - kStages) / STAGE);
     static constexpr int MISC = kStages + NS * STAGE;
     static constexpr int SMEM = MISC + 1024;
@@ -203,6 +218,22 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *v) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 16 consecutive fp32 columns (no wait: the caller issues tcgen05.wait::ld).
+__device__ __forceinline__ void tmem_ld16_nw(uint32_t taddr, float *v) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+        "%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float *v) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
@@ -248,6 +279,26 @@ __device__ __forceinline__ void split_pair(float a, float b, uint32_t &hi, uint3
     const __half2 ll = __floats2half2_rn(a - ta, b - tb);
     hi = *reinterpret_cast<const uint32_t *>(&hh);
     lo = *reinterpret_cast<const uint32_t *>(&ll);
+}
+
+// Packed fp32 pair arithmetic (sm_100 f32x2 forms): one instruction per pair.
+__device__ __forceinline__ void add2(float &a0, float &a1, float b0, float b1) {
+    asm("{\n\t.reg .b64 ra, rb;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %3};\n\t"
+        "add.rn.f32x2 ra, ra, rb;\n\tmov.b64 {%0, %1}, ra;\n\t}"
+        : "+f"(a0), "+f"(a1)
+        : "f"(b0), "f"(b1));
+}
+// (a0, a1) = (a0, a1) * m + c
+__device__ __forceinline__ void fma2s(float &a0, float &a1, float m, float c) {
+    asm("{\n\t.reg .b64 ra, rm, rc;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rm, {%2, %2};\n\t"
+        "mov.b64 rc, {%3, %3};\n\tfma.rn.f32x2 ra, ra, rm, rc;\n\tmov.b64 {%0, %1}, ra;\n\t}"
+        : "+f"(a0), "+f"(a1)
+        : "f"(m), "f"(c));
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
 }
 
 // 8 consecutive values -> hi and lo 16-byte stores (shared memory).
@@ -468,19 +519,21 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
             const char *vc = reinterpret_cast<const char *>(a.vcodes + s * a.code_stride);
             const char *vp = reinterpret_cast<const char *>(a.vparams + s * a.vp_stride);
             int issued = 0;
-            for (int i = 0; i < ng; ++i) {
+            for (int i = 0; i < nt; ++i) {
+                // tile i: groups 2i and 2i + 1 (one group in the CTA's last odd tile)
                 const int st = i % NS;
                 if (i >= NS && !bar_wait(&empty[st], ((i / NS) - 1) & 1, 16u)) break;
-                const int64_t g = gb + i;
+                const int64_t g = gb + 2 * i;
+                const uint32_t cnt = (uint32_t)min(2, ng - 2 * i);
                 unsigned char *dst = sm + kStages + st * SG::STAGE;
                 asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
                                  su32(&full[st])),
-                             "r"((uint32_t)SG::STAGE)
+                             "r"(cnt * (uint32_t)SG::GROUP)
                              : "memory");
-                bulk_load(dst, kc + g * SG::KC, SG::KC, &full[st]);
-                bulk_load(dst + SG::KC, kp + g * SG::KP, SG::KP, &full[st]);
-                bulk_load(dst + SG::KC + SG::KP, vc + g * SG::VC, SG::VC, &full[st]);
-                bulk_load(dst + SG::KC + SG::KP + SG::VC, vp + g * SG::VP, SG::VP, &full[st]);
+                bulk_load(dst, kc + g * SG::KC, cnt * SG::KC, &full[st]);
+                bulk_load(dst + SG::OKP, kp + g * SG::KP, cnt * SG::KP, &full[st]);
+                bulk_load(dst + SG::OVC, vc + g * SG::VC, cnt * SG::VC, &full[st]);
+                bulk_load(dst + SG::OVP, vp + g * SG::VP, cnt * SG::VP, &full[st]);
                 issued = i + 1;
             }
             for (int st = 0; st < NS && st < issued; ++st) {
@@ -550,7 +603,7 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
             umma_commit_e(drain);
             warp_wait(drain, 0, 32u);
         }
-    } else if (warp >= kSoftWarps) {
+    } else if (conv_role(warp) >= 0) {
         // ------------------------------------------------------------ converters
         // Warps 4-7 write key tiles, warps 8-11 value tiles; each half runs at its
         // own pace (keys free once QK^T is done, values once PV is done).
@@ -562,8 +615,9 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
         // (keys: channel 8 (u / 32) + u % 8, tokens 8 ((u / 8) % 4) ..; values:
         // token (u % 8) + 8 ((u / 32) % 4), channel group u / 128), dequantized
         // with fma(code, scale, zero).
-        const bool keys = warp < kSoftWarps + kConvHalf;
-        const int ct = threadIdx.x - (keys ? kSoftWarps : kSoftWarps + kConvHalf) * 32; // 0..127
+        const int role = conv_role(warp);
+        const bool keys = role < kConvHalf;
+        const int ct = (role & (kConvHalf - 1)) * 32 + lane; // 0..127
         float fac[4];
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
@@ -578,101 +632,106 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
         uint64_t *freed = keys ? k_free : v_free;
         const int nbuf = keys ? kK : kV;
         bool ok = true;
-        for (int g = 0; ok && g < ng; ++g) {
-            const int st = g % NS, j = g >> 1, half = g & 1, bb = j % nbuf;
+        for (int j = 0; ok && j < nt; ++j) {
+            const int st = j % NS, bb = j % nbuf;
+            const bool two = 2 * j + 1 < ng;
             // the tile's buffer is free once QK^T (keys) or PV (values) of tile
-            // j - nbuf is done (checked at the tile's first group)
-            if (!warp_wait(&full[st], (g / NS) & 1, 64u) ||
-                (half == 0 && j >= nbuf && !warp_wait(&freed[bb], ((j - nbuf) / nbuf) & 1, 64u))) {
+            // j - nbuf is done
+            if (!warp_wait(&full[st], (j / NS) & 1, 64u) ||
+                (j >= nbuf && !warp_wait(&freed[bb], ((j - nbuf) / nbuf) & 1, 64u))) {
                 ok = false;
                 break;
             }
-            const unsigned char *base = sm + kStages + st * SG::STAGE;
-            if (BITS == 2 && keys) {
-                // channel kd = ct: tokens 0-15 in word 0, 16-31 in word 1; MN-major
-                // (n = token, SBO 2048), 8 tokens of one channel per 16 bytes
-                const uint2 w2 = reinterpret_cast<const uint2 *>(base)[ct];
-                const float2 p = reinterpret_cast<const float2 *>(base + SG::KC)[ct];
-                uint32_t th0, th1, tl0, tl1;
-                table2(p.x * fac[0], p.y * fac[0], th0, th1, tl0, tl1);
-                unsigned char *khi = sm + kKbuf + bb * 32768, *klo = khi + 16384;
-                const int koff = 4 * half * 2048 + (ct >> 3) * 128 + (ct & 7) * 16;
+            const unsigned char *sbase = sm + kStages + st * SG::STAGE;
 #pragma unroll
-                for (int tb = 0; tb < 4; ++tb) {
-                    const uint32_t w = (tb < 2 ? w2.x : w2.y) >> (16 * (tb & 1));
-                    lookup8(w, th0, th1, tl0, tl1, khi + koff + tb * 2048, klo + koff + tb * 2048);
-                }
-            } else if (BITS == 2) {
-                // token t = ct % 32, channel group cg = ct / 32: channels 0-15 of the
-                // group in word 0, 16-31 in word 1; MN-major (k = token, SBO 1024),
-                // 8 channels of one token per 16 bytes
-                const int t = ct & 31, cg = ct >> 5;
-                const uint2 w2 = reinterpret_cast<const uint2 *>(base + SG::KC + SG::KP)[t * 4 + cg];
-                const float2 p = reinterpret_cast<const float2 *>(base + SG::KC + SG::KP + SG::VC)[t * 4 + cg];
-                uint32_t th0, th1, tl0, tl1;
-                table2(p.x * fac[0], p.y * fac[0], th0, th1, tl0, tl1);
-                unsigned char *vhi = sm + kVbuf + bb * 32768, *vlo = vhi + 16384;
-                const int tt = 32 * half + t;
-                const int voff = 4 * cg * 1024 + (tt >> 3) * 128 + (tt & 7) * 16;
+            for (int half = 0; half < 2; ++half) {
+                if (half == 1 && !two) break;
+                const unsigned char *kcb = sbase + half * SG::KC, *kpb = sbase + SG::OKP + half * SG::KP;
+                const unsigned char *vcb = sbase + SG::OVC + half * SG::VC, *vpb = sbase + SG::OVP + half * SG::VP;
+                if (BITS == 2 && keys) {
+                    // channel kd = ct: tokens 0-15 in word 0, 16-31 in word 1; MN-major
+                    // (n = token, SBO 2048), 8 tokens of one channel per 16 bytes
+                    const uint2 w2 = reinterpret_cast<const uint2 *>(kcb)[ct];
+                    const float2 p = reinterpret_cast<const float2 *>(kpb)[ct];
+                    uint32_t th0, th1, tl0, tl1;
+                    table2(p.x * fac[0], p.y * fac[0], th0, th1, tl0, tl1);
+                    unsigned char *khi = sm + kKbuf + bb * 32768, *klo = khi + 16384;
+                    const int koff = 4 * half * 2048 + (ct >> 3) * 128 + (ct & 7) * 16;
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const uint32_t w = (u < 2 ? w2.x : w2.y) >> (16 * (u & 1));
-                    lookup8(w, th0, th1, tl0, tl1, vhi + voff + u * 1024, vlo + voff + u * 1024);
-                }
-            } else if (keys) {
-                const uint32_t *KC = reinterpret_cast<const uint32_t *>(base);
-                const float2 *KP = reinterpret_cast<const float2 *>(base + SG::KC);
-                unsigned char *khi = sm + kKbuf + bb * 32768, *klo = khi + 16384;
-#pragma unroll
-                for (int r = 0; r < 4; ++r) {
-                    // MN-major (n = token, SBO 2048): channel kd, tokens 8 tb .. 8 tb + 7
-                    // of this group (one code word, one (scale, zero))
-                    const int u = ct + 128 * r;
-                    const int kd = 8 * (u >> 5) + (u & 7), tb = (u >> 3) & 3;
-                    const int bit0 = 8 * tb * BITS;
-                    const uint32_t w = KC[kd * SG::IPC + (bit0 >> 5)];
-                    const float2 p = KP[kd];
-                    const float sc = p.x * fac[r], zc = p.y * fac[r];
-                    float x[8];
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) x[k] = fmaf(code_f(w, (bit0 & 31) + k * BITS, kMask), sc, zc);
-                    const int koff = (4 * half + tb) * 2048 + (kd >> 3) * 128 + (kd & 7) * 16;
-                    store_split8(x, khi + koff, klo + koff);
-                }
-            } else {
-                const uint32_t *VC = reinterpret_cast<const uint32_t *>(base + SG::KC + SG::KP);
-                const float2 *VP = reinterpret_cast<const float2 *>(base + SG::KC + SG::KP + SG::VC);
-                unsigned char *vhi = sm + kVbuf + bb * 32768, *vlo = vhi + 16384;
-#pragma unroll
-                for (int r = 0; r < 4; ++r) {
-                    // MN-major (k = token, SBO 1024): token t, channels 8 jj .. 8 jj + 7
-                    const int u = ct + 128 * r;
-                    const int t = (u & 7) + 8 * ((u >> 5) & 3);
-                    const int jj = ((u >> 3) & 3) + 4 * r;  // channel group r
-                    const int cin = (jj & 3) * 8;            // first channel within the group
-                    const int vwi = (cin * BITS) >> 5, vsh = (cin % (32 / BITS)) * BITS;
-                    const uint32_t w = VC[(t * 4 + r) * SG::IPC + vwi];
-                    const float2 p = VP[t * 4 + r];
-                    const float sc = p.x * fac[r], zc = p.y * fac[r];
-                    float x[8];
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) x[k] = fmaf(code_f(w, vsh + k * BITS, kMask), sc, zc);
+                    for (int tb = 0; tb < 4; ++tb) {
+                        const uint32_t w = (tb < 2 ? w2.x : w2.y) >> (16 * (tb & 1));
+                        lookup8(w, th0, th1, tl0, tl1, khi + koff + tb * 2048, klo + koff + tb * 2048);
+                    }
+                } else if (BITS == 2) {
+                    // token t = ct % 32, channel group cg = ct / 32: channels 0-15 of the
+                    // group in word 0, 16-31 in word 1; MN-major (k = token, SBO 1024),
+                    // 8 channels of one token per 16 bytes
+                    const int t = ct & 31, cg = ct >> 5;
+                    const uint2 w2 = reinterpret_cast<const uint2 *>(vcb)[t * 4 + cg];
+                    const float2 p = reinterpret_cast<const float2 *>(vpb)[t * 4 + cg];
+                    uint32_t th0, th1, tl0, tl1;
+                    table2(p.x * fac[0], p.y * fac[0], th0, th1, tl0, tl1);
+                    unsigned char *vhi = sm + kVbuf + bb * 32768, *vlo = vhi + 16384;
                     const int tt = 32 * half + t;
-                    const int voff = jj * 1024 + (tt >> 3) * 128 + (tt & 7) * 16;
-                    store_split8(x, vhi + voff, vlo + voff);
+                    const int voff = 4 * cg * 1024 + (tt >> 3) * 128 + (tt & 7) * 16;
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const uint32_t w = (u < 2 ? w2.x : w2.y) >> (16 * (u & 1));
+                        lookup8(w, th0, th1, tl0, tl1, vhi + voff + u * 1024, vlo + voff + u * 1024);
+                    }
+                } else if (keys) {
+                    const uint32_t *KC = reinterpret_cast<const uint32_t *>(kcb);
+                    const float2 *KP = reinterpret_cast<const float2 *>(kpb);
+                    unsigned char *khi = sm + kKbuf + bb * 32768, *klo = khi + 16384;
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        // MN-major (n = token, SBO 2048): channel kd, tokens 8 tb .. 8 tb + 7
+                        // of this group (one code word, one (scale, zero))
+                        const int u = ct + 128 * r;
+                        const int kd = 8 * (u >> 5) + (u & 7), tb = (u >> 3) & 3;
+                        const int bit0 = 8 * tb * BITS;
+                        const uint32_t w = KC[kd * SG::IPC + (bit0 >> 5)];
+                        const float2 p = KP[kd];
+                        const float sc = p.x * fac[r], zc = p.y * fac[r];
+                        float x[8];
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) x[k] = fmaf(code_f(w, (bit0 & 31) + k * BITS, kMask), sc, zc);
+                        const int koff = (4 * half + tb) * 2048 + (kd >> 3) * 128 + (kd & 7) * 16;
+                        store_split8(x, khi + koff, klo + koff);
+                    }
+                } else {
+                    const uint32_t *VC = reinterpret_cast<const uint32_t *>(vcb);
+                    const float2 *VP = reinterpret_cast<const float2 *>(vpb);
+                    unsigned char *vhi = sm + kVbuf + bb * 32768, *vlo = vhi + 16384;
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        // MN-major (k = token, SBO 1024): token t, channels 8 jj .. 8 jj + 7
+                        const int u = ct + 128 * r;
+                        const int t = (u & 7) + 8 * ((u >> 5) & 3);
+                        const int jj = ((u >> 3) & 3) + 4 * r;  // channel group r
+                        const int cin = (jj & 3) * 8;            // first channel within the group
+                        const int vwi = (cin * BITS) >> 5, vsh = (cin % (32 / BITS)) * BITS;
+                        const uint32_t w = VC[(t * 4 + r) * SG::IPC + vwi];
+                        const float2 p = VP[t * 4 + r];
+                        const float sc = p.x * fac[r], zc = p.y * fac[r];
+                        float x[8];
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) x[k] = fmaf(code_f(w, vsh + k * BITS, kMask), sc, zc);
+                        const int tt = 32 * half + t;
+                        const int voff = jj * 1024 + (tt >> 3) * 128 + (tt & 7) * 16;
+                        store_split8(x, vhi + voff, vlo + voff);
+                    }
                 }
             }
-            // a tile is ready after its last group (one group in the CTA's last odd
-            // tile); the proxy fence there orders both groups' writes before the MMAs
-            const bool last = half == 1 || g == ng - 1;
-            if (last) proxy_fence();
+            // the proxy fence orders the tile's shared-memory writes before the MMAs
+            proxy_fence();
             __syncwarp();
             if (lane == 0) {
-                if (last) bar_arrive(&ready[bb]);
+                bar_arrive(&ready[bb]);
                 bar_arrive(&empty[st]);
             }
         }
-    } else {
+    } else if (warp < kSoftWarps) {
         // ------------------------------------------------------------ softmax (thread = row)
         const int m = threadIdx.x;
         const uint32_t lane_base = tbase + ((uint32_t)(32 * warp) << 16);
@@ -690,22 +749,29 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
             float x[64];
             const uint32_t srow = lane_base + kSc + 128 * bs;
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                float t[32];
-                tmem_ld32(srow + 32 * hh, x + 32 * hh);
-                tmem_ld32(srow + 64 + 32 * hh, t);
+            for (int c = 0; c < 4; ++c) {
+                float t[16];
+                tmem_ld16_nw(srow + 16 * c, x + 16 * c);
+                tmem_ld16_nw(srow + 64 + 16 * c, t);
+                tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 32; ++i) x[32 * hh + i] += t[i];
+                for (int i = 0; i < 16; i += 2) add2(x[16 * c + i], x[16 * c + i + 1], t[i], t[i + 1]);
+            }
+            if (!two) { // the CTA's last odd tile holds one group
+#pragma unroll
+                for (int i = 32; i < 64; ++i) x[i] = -INFINITY;
             }
             // logits are x rowfac (exp2 units); the max is taken on the raw scores
             // (rowfac > 0 and rounding is monotone, so max(x) rowfac = max(x rowfac))
-            float mx = -INFINITY;
+            float m4[4] = {x[0], x[1], x[2], x[3]};
 #pragma unroll
-            for (int i = 0; i < 64; ++i) {
-                if (i >= 32 && !two) x[i] = -INFINITY;
-                mx = fmaxf(mx, x[i]);
+            for (int i = 4; i < 64; i += 8) {
+                m4[0] = max3(m4[0], x[i], x[i + 1]);
+                m4[1] = max3(m4[1], x[i + 2], x[i + 3]);
+                m4[2] = max3(m4[2], x[i + 4], x[i + 5]);
+                m4[3] = max3(m4[3], x[i + 6], x[i + 7]);
             }
-            mx *= rowfac;
+            float mx = fmaxf(max3(m4[0], m4[1], m4[2]), m4[3]) * rowfac;
             const bool need = mx > mref + kLazy2;
             if (__any_sync(0xffffffffu, need)) {
                 const float nref = need ? mx : mref;
@@ -734,13 +800,19 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
             // P' = p kPScale = 2^(x rowfac - mref + 15 - kLazyBits) <= 2^15, fp16
             // normal down to p = 2^(kLazyBits - 29); l accumulates p = P' / kPScale
             const float off = (float)(15 - kLazyBits) - mref;
-            float psum = 0.0f;
+            float ps0 = 0.0f, ps1 = 0.0f, ps2 = 0.0f, ps3 = 0.0f;
 #pragma unroll
-            for (int i = 0; i < 64; ++i) {
-                x[i] = ex2_approx(fmaf(x[i], rowfac, off));
-                psum += x[i];
+            for (int i = 0; i < 64; i += 4) {
+                fma2s(x[i], x[i + 1], rowfac, off);
+                fma2s(x[i + 2], x[i + 3], rowfac, off);
+                x[i] = ex2_approx(x[i]);
+                x[i + 1] = ex2_approx(x[i + 1]);
+                x[i + 2] = ex2_approx(x[i + 2]);
+                x[i + 3] = ex2_approx(x[i + 3]);
+                add2(ps0, ps1, x[i], x[i + 1]);
+                add2(ps2, ps3, x[i + 2], x[i + 3]);
             }
-            l += psum * (1.0f / kPScale);
+            l += ((ps0 + ps1) + (ps2 + ps3)) * (1.0f / kPScale);
             // P(j) overwrites the first half of S[bs] (read above); QK(j + kS)
             // rewrites S[bs] only after PV(j) in issue order
             uint32_t hi[16], lo[16];
