@@ -123,9 +123,29 @@ typedef struct kivi_prefix_footprint {
     uint64_t fp16_all_users_bytes;
 } kivi_prefix_footprint;
 
+/* QualityGuard (guard.rs:14-36): policy, one upgrade, one flush check. */
+#define KIVI_POLICY_RAISE_BITS 0
+#define KIVI_POLICY_LENGTHEN_RESIDUAL 1
+#define KIVI_UPGRADE_BITS 0
+#define KIVI_UPGRADE_RESIDUAL 1
+#define KIVI_MAX_UPGRADES 64
+typedef struct kivi_quality_upgrade {
+    int32_t kind; /* KIVI_UPGRADE_BITS or KIVI_UPGRADE_RESIDUAL */
+    uint64_t from;
+    uint64_t to;
+} kivi_quality_upgrade;
+typedef struct kivi_flush_check {
+    uint64_t sequence_tokens;
+    float cosine_before;
+    float cosine;
+    uint32_t num_upgrades;
+    kivi_quality_upgrade upgrades[KIVI_MAX_UPGRADES];
+} kivi_flush_check;
+
 typedef struct kivi_cache kivi_cache;     /* KiviCache (cache.rs:71-83) */
 typedef struct kivi_prefix kivi_prefix;   /* SharedPrefix (prefix.rs:32-35), refcounted */
 typedef struct kivi_session kivi_session; /* RagSession (prefix.rs:41-46) */
+typedef struct kivi_guard kivi_guard;     /* QualityGuard (guard.rs:38-47) */
 
 /* ---------------------------------------------------------------- library */
 
@@ -367,6 +387,33 @@ uint64_t kivi_layer_kv_bytes(const kivi_config *config, uint64_t num_kv_heads,
 /* marginal_bytes_per_layer (budget.rs:349-364). */
 uint64_t kivi_marginal_bytes_per_layer(const kivi_config *config, uint64_t num_kv_heads,
                                        uint64_t head_dim);
+
+/* ---------------------------------------------------------------- guard.rs */
+
+/* QualityGuard::try_new (guard.rs:50-71): a KiviCache on `device` plus the fp32
+ * tape of every appended token, also on the device. */
+int32_t kivi_guard_new(const kivi_config *config, uint64_t batch, uint64_t num_kv_heads,
+                       uint64_t head_dim, float threshold, int32_t policy, uint32_t max_bits,
+                       uint64_t max_residual, int32_t device, kivi_guard **out, kivi_error *err);
+void kivi_guard_free(kivi_guard *guard);
+/* QualityGuard::append (guard.rs:93-152): appends keys/values [batch, heads,
+ * seq_len, head_dim] flush by flush; after every key flush scores the cache's
+ * attention against dense fp32 attention over the tape (cosine of the
+ * [batch, num_q_heads, head_dim] outputs) and upgrades the cache under the
+ * policy while the cosine misses the threshold (guard.rs:154-225).  One
+ * kivi_flush_check per flush; `checks` must hold seq_len / group_size + 1
+ * entries (checked before any mutation). */
+int32_t kivi_guard_append(kivi_guard *guard, const float *keys, uint64_t keys_len,
+                          const float *values, uint64_t values_len, uint64_t seq_len,
+                          const float *query, uint64_t query_len, uint64_t num_q_heads, float scale,
+                          kivi_flush_check *checks, uint64_t checks_capacity, uint64_t *num_checks,
+                          kivi_error *err);
+/* QualityGuard::cache / policy / sequence_length (guard.rs:73-91); the
+ * config is kivi_cache_get_state(kivi_guard_cache(g)).config.  The cache
+ * pointer changes when an upgrade rebuilds the cache. */
+const kivi_cache *kivi_guard_cache(const kivi_guard *guard);
+int32_t kivi_guard_policy(const kivi_guard *guard);
+uint64_t kivi_guard_sequence_length(const kivi_guard *guard);
 
 #ifdef __cplusplus
 }

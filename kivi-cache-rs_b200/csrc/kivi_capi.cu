@@ -1905,3 +1905,297 @@ extern "C" int32_t kivi_cache_attention_noalloc_dev(const kivi_cache *h, const f
     CUDA_TRY(cudaEventRecord(h->dev_done, st), "noalloc attention");
     return set_err(err, KIVI_OK);
 }
+
+// ---------------------------------------------------------------- guard.rs
+
+// QualityGuard (guard.rs:38-47): the resident cache, the fp32 tape of every
+// appended token on the device ([stream][cap][D], grown by doubling) and the
+// guard's settings.  Host calls are synchronous, like the reference's.
+struct kivi_guard {
+    kivi_cache *cache = nullptr;
+    uint64_t B = 0, H = 0, D = 0;
+    int device = 0;
+    float threshold = 0.0f;
+    int32_t policy = KIVI_POLICY_RAISE_BITS;
+    uint32_t max_bits = 8;
+    uint64_t max_residual = 0;
+    cudaStream_t stream = nullptr;
+    float *tk = nullptr, *tv = nullptr;
+    uint64_t seq = 0, cap = 0;
+    Scratch work; // token span, query, the two attention outputs, cosine sums, logits
+    Scratch dense; // contiguous tape copy for a rebuild
+    std::mutex mu;
+};
+
+namespace {
+
+// byte offsets inside kivi_guard::work for a span of `take` tokens and Hq heads
+struct GuardLayout {
+    size_t q, got, expect, sums, span_k, span_v, logits, total;
+    GuardLayout(const kivi_guard *g, uint64_t Hq, uint64_t take, uint64_t seq_after) {
+        auto up = [](size_t x) { return (x + 255) / 256 * 256; };
+        const size_t rows = g->B * Hq;
+        q = 0;
+        got = up(q + rows * g->D * 4);
+        expect = up(got + rows * g->D * 4);
+        sums = up(expect + rows * g->D * 4);
+        span_k = up(sums + 16);
+        span_v = up(span_k + g->B * g->H * take * g->D * 4);
+        logits = up(span_v + g->B * g->H * take * g->D * 4);
+        total = logits + rows * (seq_after ? seq_after : 1) * 4;
+    }
+};
+
+int32_t guard_grow_tape(kivi_guard *g, uint64_t need, kivi_error *err) {
+    if (need <= g->cap) return KIVI_OK;
+    uint64_t cap = g->cap * 2;
+    if (cap < need) cap = need;
+    if (cap < 64) cap = 64;
+    const size_t row = g->D * 4, n = g->B * g->H;
+    float *nk = nullptr, *nv = nullptr;
+    cudaError_t e = cudaMalloc(&nk, n * cap * row);
+    if (e == cudaSuccess) e = cudaMalloc(&nv, n * cap * row);
+    if (e != cudaSuccess) {
+        if (nk) cudaFree(nk);
+        if (nv) cudaFree(nv);
+        return cuda_fail(err, e, "guard tape");
+    }
+    if (g->seq) {
+        CUDA_TRY(cudaMemcpy2DAsync(nk, cap * row, g->tk, g->cap * row, g->seq * row, n,
+                                   cudaMemcpyDeviceToDevice, g->stream), "guard tape");
+        CUDA_TRY(cudaMemcpy2DAsync(nv, cap * row, g->tv, g->cap * row, g->seq * row, n,
+                                   cudaMemcpyDeviceToDevice, g->stream), "guard tape");
+        CUDA_TRY(cudaStreamSynchronize(g->stream), "guard tape");
+    }
+    if (g->tk) cudaFree(g->tk);
+    if (g->tv) cudaFree(g->tv);
+    g->tk = nk;
+    g->tv = nv;
+    g->cap = cap;
+    return KIVI_OK;
+}
+
+// guard.rs:237-250: cosine of the cache's attention against dense fp32
+// attention over the tape, for the query already staged at layout.q
+int32_t guard_cosine(kivi_guard *g, const GuardLayout &L, uint64_t Hq, float scale, float *cos,
+                     kivi_error *err) {
+    float *q = g->work.as<float>(L.q), *got = g->work.as<float>(L.got);
+    float *expect = g->work.as<float>(L.expect), *sums = g->work.as<float>(L.sums);
+    int32_t rc = kivi_cache_attention_dev(g->cache, q, Hq, scale, got, g->stream, err);
+    if (rc) return rc;
+    CUDA_TRY(kivi::launch_guard_attention(q, g->tk, g->tv, (int64_t)g->cap, (int)g->B, (int)g->H,
+                                          (int)Hq, (int)g->D, (int64_t)g->seq, scale,
+                                          g->work.as<float>(L.logits), expect, g->stream),
+             "guard reference attention");
+    CUDA_TRY(kivi::launch_guard_cosine(got, expect, (int64_t)(g->B * Hq * g->D), sums, g->stream),
+             "guard cosine");
+    float h[3];
+    CUDA_TRY(cudaMemcpyAsync(h, sums, sizeof(h), cudaMemcpyDeviceToHost, g->stream), "guard cosine");
+    CUDA_TRY(cudaStreamSynchronize(g->stream), "guard cosine");
+    rc = check_device_waits(err);
+    if (rc) return rc;
+    const float denom = sqrtf(h[1]) * sqrtf(h[2]); // guard.rs:343-359
+    *cos = denom == 0.0f ? 1.0f : h[0] / denom;
+    return KIVI_OK;
+}
+
+// guard.rs:175-197, 252-284: the policy's next configuration (false = none)
+bool guard_propose(const kivi_guard *g, kivi_quality_upgrade *u) {
+    const kivi_config &c = g->cache->s.cfg;
+    if (g->policy == KIVI_POLICY_RAISE_BITS) {
+        const uint32_t next = c.bits == 2 ? 4u : c.bits == 4 ? 8u : 0u;
+        if (next == 0 || next > g->max_bits) return false;
+        *u = kivi_quality_upgrade{KIVI_UPGRADE_BITS, c.bits, next};
+        return true;
+    }
+    const uint64_t cur = c.residual_length;
+    if (cur >= g->max_residual) return false;
+    const uint64_t doubled = cur > UINT64_MAX / 2 ? UINT64_MAX : cur * 2;
+    const uint64_t next = doubled <= g->max_residual ? doubled : g->max_residual;
+    if (!(next > cur && next % c.group_size == 0)) return false;
+    *u = kivi_quality_upgrade{KIVI_UPGRADE_RESIDUAL, cur, next};
+    return true;
+}
+
+// guard.rs:199-225: a new cache with the upgraded config, rebuilt by one
+// append of the whole tape
+int32_t guard_apply(kivi_guard *g, const kivi_quality_upgrade &u, kivi_error *err) {
+    const kivi_config cur = g->cache->s.cfg;
+    kivi_config cfg{};
+    int32_t rc = kivi_config_try_new(u.kind == KIVI_UPGRADE_BITS ? (uint32_t)u.to : cur.bits,
+                                     cur.group_size,
+                                     u.kind == KIVI_UPGRADE_RESIDUAL ? u.to : cur.residual_length,
+                                     &cfg, err);
+    if (rc) return rc;
+    kivi_cache *nc = nullptr;
+    rc = kivi_cache_new(&cfg, g->B, g->H, g->D, g->device, &nc, err);
+    if (rc) return rc;
+    if (g->seq > 0) {
+        const float *k = g->tk, *v = g->tv;
+        if (g->cap != g->seq) { // the append takes [batch, heads, seq, D] contiguous
+            const size_t row = g->D * 4, n = g->B * g->H, bytes = n * g->seq * row;
+            cudaError_t e = g->dense.ensure(2 * bytes);
+            if (e == cudaSuccess)
+                e = cudaMemcpy2DAsync(g->dense.as<char>(), g->seq * row, g->tk, g->cap * row,
+                                      g->seq * row, n, cudaMemcpyDeviceToDevice, g->stream);
+            if (e == cudaSuccess)
+                e = cudaMemcpy2DAsync(g->dense.as<char>(bytes), g->seq * row, g->tv, g->cap * row,
+                                      g->seq * row, n, cudaMemcpyDeviceToDevice, g->stream);
+            if (e != cudaSuccess) {
+                kivi_cache_free(nc);
+                return cuda_fail(err, e, "guard rebuild");
+            }
+            k = g->dense.as<float>();
+            v = g->dense.as<float>(bytes);
+        }
+        rc = kivi_cache_append_dev(nc, k, v, g->seq, g->stream, err);
+        if (rc == KIVI_OK) {
+            cudaError_t e = cudaStreamSynchronize(g->stream);
+            if (e != cudaSuccess) rc = cuda_fail(err, e, "guard rebuild");
+        }
+        if (rc) {
+            kivi_cache_free(nc);
+            return rc;
+        }
+    }
+    kivi_cache_free(g->cache);
+    g->cache = nc;
+    return KIVI_OK;
+}
+
+// guard.rs:154-173
+int32_t guard_check(kivi_guard *g, const GuardLayout &L, uint64_t Hq, float scale,
+                    kivi_flush_check *out, kivi_error *err) {
+    memset(out, 0, sizeof(*out));
+    float cos = 0.0f;
+    int32_t rc = guard_cosine(g, L, Hq, scale, &cos, err);
+    if (rc) return rc;
+    out->cosine_before = cos;
+    while (cos < g->threshold) {
+        kivi_quality_upgrade u{};
+        if (!guard_propose(g, &u)) break;
+        if ((rc = guard_apply(g, u, err))) return rc;
+        if (out->num_upgrades < KIVI_MAX_UPGRADES) out->upgrades[out->num_upgrades++] = u;
+        if ((rc = guard_cosine(g, L, Hq, scale, &cos, err))) return rc;
+    }
+    out->cosine = cos;
+    out->sequence_tokens = g->seq;
+    return KIVI_OK;
+}
+
+} // namespace
+
+int32_t kivi_guard_new(const kivi_config *config, uint64_t batch, uint64_t num_kv_heads,
+                       uint64_t head_dim, float threshold, int32_t policy, uint32_t max_bits,
+                       uint64_t max_residual, int32_t device, kivi_guard **out, kivi_error *err) {
+    if (!out) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null output");
+    *out = nullptr;
+    if (policy != KIVI_POLICY_RAISE_BITS && policy != KIVI_POLICY_LENGTHEN_RESIDUAL)
+        return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "unknown quality policy %d", policy);
+    kivi_cache *c = nullptr;
+    int32_t rc = kivi_cache_new(config, batch, num_kv_heads, head_dim, device, &c, err);
+    if (rc) return rc;
+    DeviceGuard dg(device);
+    kivi_guard *g = new kivi_guard();
+    g->cache = c;
+    g->B = batch;
+    g->H = num_kv_heads;
+    g->D = head_dim;
+    g->device = device;
+    g->threshold = threshold;
+    g->policy = policy;
+    g->max_bits = max_bits;
+    g->max_residual = max_residual;
+    cudaError_t e = cudaStreamCreateWithFlags(&g->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        kivi_cache_free(c);
+        delete g;
+        return cuda_fail(err, e, "guard stream");
+    }
+    *out = g;
+    return set_err(err, KIVI_OK);
+}
+
+void kivi_guard_free(kivi_guard *g) {
+    if (!g) return;
+    DeviceGuard dg(g->device);
+    if (g->stream) cudaStreamSynchronize(g->stream);
+    kivi_cache_free(g->cache);
+    if (g->tk) cudaFree(g->tk);
+    if (g->tv) cudaFree(g->tv);
+    g->work.release();
+    g->dense.release();
+    if (g->stream) cudaStreamDestroy(g->stream);
+    delete g;
+}
+
+const kivi_cache *kivi_guard_cache(const kivi_guard *g) { return g ? g->cache : nullptr; }
+int32_t kivi_guard_policy(const kivi_guard *g) { return g ? g->policy : -1; }
+uint64_t kivi_guard_sequence_length(const kivi_guard *g) { return g ? g->seq : 0; }
+
+int32_t kivi_guard_append(kivi_guard *g, const float *keys, uint64_t keys_len, const float *values,
+                          uint64_t values_len, uint64_t seq_len, const float *query,
+                          uint64_t query_len, uint64_t Hq, float scale, kivi_flush_check *checks,
+                          uint64_t checks_capacity, uint64_t *num_checks, kivi_error *err) {
+    if (!g || !num_checks) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null argument");
+    *num_checks = 0;
+    // guard.rs:103-127, in the reference's order
+    const uint64_t expected = g->B * g->H * seq_len * g->D;
+    if (keys_len != expected) return set_err(err, KIVI_ERR_SHAPE, expected, keys_len);
+    if (values_len != expected) return set_err(err, KIVI_ERR_SHAPE, expected, values_len);
+    const uint64_t query_elems = g->B * Hq * g->D;
+    if (Hq == 0 || Hq % g->H != 0) return set_err(err, KIVI_ERR_QUERY_HEADS, Hq, g->H);
+    if (query_len != query_elems) return set_err(err, KIVI_ERR_SHAPE, query_elems, query_len);
+    const uint64_t G = g->cache->s.cfg.group_size;
+    if (!checks || checks_capacity < seq_len / G + 1)
+        return set_msg(err, KIVI_ERR_INVALID_ARGUMENT,
+                       "checks must hold seq_len / group_size + 1 = %llu entries",
+                       (unsigned long long)(seq_len / G + 1));
+    if (seq_len > 0 && (!keys || !values || !query))
+        return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null buffer");
+    std::lock_guard<std::mutex> lk(g->mu);
+    DeviceGuard dg(g->device);
+    const size_t row = g->D * 4;
+    uint64_t offset = 0;
+    bool staged_query = false;
+    while (offset < seq_len) {
+        const KvState &s = g->cache->s;
+        const uint64_t R = s.cfg.residual_length;
+        const uint64_t room = R > s.kres_len ? R - s.kres_len : 0; // cache.rs:328-330
+        const uint64_t take = std::min<uint64_t>(room, seq_len - offset);
+        const GuardLayout L(g, Hq, take, g->seq + take);
+        const void *prev = g->work.p;
+        CUDA_TRY(g->work.ensure(L.total), "guard scratch");
+        if (g->work.p != prev) staged_query = false;
+        if (!staged_query) {
+            CUDA_TRY(cudaMemcpyAsync(g->work.as<float>(L.q), query, query_elems * 4,
+                                     cudaMemcpyHostToDevice, g->stream), "guard query");
+            staged_query = true;
+        }
+        // guard.rs:248-265: this flush's token span of every stream
+        float *sk = g->work.as<float>(L.span_k), *sv = g->work.as<float>(L.span_v);
+        const uint64_t n = g->B * g->H;
+        CUDA_TRY(cudaMemcpy2DAsync(sk, take * row, keys + offset * g->D, seq_len * row, take * row, n,
+                                   cudaMemcpyHostToDevice, g->stream), "guard keys");
+        CUDA_TRY(cudaMemcpy2DAsync(sv, take * row, values + offset * g->D, seq_len * row, take * row,
+                                   n, cudaMemcpyHostToDevice, g->stream), "guard values");
+        int32_t rc = kivi_cache_append_dev(g->cache, sk, sv, take, g->stream, err);
+        if (rc) return rc;
+        // guard.rs:267-292: the tape
+        rc = guard_grow_tape(g, g->seq + take, err);
+        if (rc) return rc;
+        CUDA_TRY(cudaMemcpy2DAsync(g->tk + g->seq * g->D, g->cap * row, sk, take * row, take * row,
+                                   n, cudaMemcpyDeviceToDevice, g->stream), "guard tape");
+        CUDA_TRY(cudaMemcpy2DAsync(g->tv + g->seq * g->D, g->cap * row, sv, take * row, take * row,
+                                   n, cudaMemcpyDeviceToDevice, g->stream), "guard tape");
+        g->seq += take;
+        if (g->cache->s.kres_len == 0) {
+            rc = guard_check(g, L, Hq, scale, &checks[*num_checks], err);
+            if (rc) return rc;
+            ++*num_checks;
+        }
+        offset += take;
+    }
+    CUDA_TRY(cudaStreamSynchronize(g->stream), "guard append");
+    return set_err(err, KIVI_OK);
+}

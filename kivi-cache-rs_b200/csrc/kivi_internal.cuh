@@ -262,6 +262,15 @@ cudaError_t plan_attention_sets(int64_t nstreams, int64_t main_groups, int nz, i
 cudaError_t launch_attention_sets(const SetsArgs &a, int bits, int nchunks, int nstreams, int nz,
                                   cudaStream_t s);
 cudaError_t take_sets_error(unsigned int *out);
+
+// QualityGuard's reference score (kivi_guard.cu): dense fp32 attention over a
+// token tape [B*H][cap][D] (logits scratch: B*Hq*seq floats) and the cosine
+// sums (a.b, a.a, b.b) of two vectors.
+cudaError_t launch_guard_attention(const float *q, const float *k, const float *v, int64_t cap,
+                                   int B, int H, int Hq, int D, int64_t seq, float scale,
+                                   float *logits, float *out, cudaStream_t s);
+cudaError_t launch_guard_cosine(const float *a, const float *b, int64_t n, float *out3,
+                                cudaStream_t s);
 // Reads and clears the flag set when a tensor-core kernel's bounded wait gave up.
 cudaError_t take_tc_error(unsigned int *out);
 

@@ -58,6 +58,15 @@ class _Config(C.Structure):
     _fields_ = [("bits", C.c_uint32), ("group_size", C.c_uint64), ("residual_length", C.c_uint64)]
 
 
+class _Upgrade(C.Structure):
+    _fields_ = [("kind", C.c_int32), ("frm", C.c_uint64), ("to", C.c_uint64)]
+
+
+class _FlushCheck(C.Structure):
+    _fields_ = [("sequence_tokens", C.c_uint64), ("cosine_before", C.c_float),
+                ("cosine", C.c_float), ("num_upgrades", C.c_uint32), ("upgrades", _Upgrade * 64)]
+
+
 class _Memory(C.Structure):
     _fields_ = [(n, C.c_uint64) for n in (
         "tokens", "key_code_bytes", "key_metadata_bytes", "value_code_bytes",
@@ -110,6 +119,14 @@ def lib():
         "kivi_profile_read": ([C.c_char_p, u64p, C.POINTER(C.c_double)], i32),
         "kivi_profile_reset": ([], None),
         "kivi_profile_hold": ([sz, P], i32),
+        "kivi_guard_new": ([C.POINTER(_Config), sz, sz, sz, f32, i32, C.c_uint32, sz, i32,
+                            C.POINTER(P), e], i32),
+        "kivi_guard_free": ([P], None),
+        "kivi_guard_append": ([P, fp, sz, fp, sz, sz, fp, sz, sz, f32, C.POINTER(_FlushCheck), sz,
+                               u64p, e], i32),
+        "kivi_guard_cache": ([P], P),
+        "kivi_guard_policy": ([P], i32),
+        "kivi_guard_sequence_length": ([P], sz),
         "kivi_config_default": ([C.POINTER(_Config)], i32),
         "kivi_config_try_new": ([C.c_uint32, sz, sz, C.POINTER(_Config), e], i32),
         "kivi_cache_new": ([C.POINTER(_Config), sz, sz, sz, i32, C.POINTER(P), e], i32),
@@ -864,4 +881,146 @@ __all__ = [
     "QuantizedTensor", "quantize_per_channel", "quantize_per_token", "layer_kv_bytes",
     "marginal_bytes_per_layer", "AgentMemoryBudget", "sessions_attention_batched",
     "sessions_attention_batched_dev", "sessions_append_dev", "merge_partials_dev", "kernel_launches", "lib", "LIB_PATH",
+    "QualityGuard", "QualityPolicy", "QualityUpgrade", "FlushCheck",
 ]
+
+
+# ---------------------------------------------------------------- guard.rs
+
+
+class QualityPolicy:
+    """guard.rs:14-20: what a missed cosine threshold changes."""
+
+    RaiseBits = 0          # 2-bit -> 4-bit -> 8-bit, up to max_bits
+    LengthenResidual = 1   # residual length doubles, up to max_residual
+
+
+class QualityUpgrade(tuple):
+    """guard.rs:23-27: ("Bits" | "Residual", from, to); QualityUpgrade.Bits(2, 4) ..."""
+
+    def __new__(cls, kind, from_, to):
+        return super().__new__(cls, (kind, int(from_), int(to)))
+
+    @classmethod
+    def Bits(cls, from_, to):
+        return cls("Bits", from_, to)
+
+    @classmethod
+    def Residual(cls, from_, to):
+        return cls("Residual", from_, to)
+
+    @property
+    def kind(self):
+        return self[0]
+
+    @property
+    def from_(self):
+        return self[1]
+
+    @property
+    def to(self):
+        return self[2]
+
+
+@dataclass
+class FlushCheck:
+    """guard.rs:30-36: the cosine of the probe query just after a key flush."""
+
+    sequence_tokens: int
+    cosine_before: float
+    cosine: float
+    upgrades: list
+
+
+class _GuardCache(KiviCache):
+    """QualityGuard::cache (guard.rs:77-79): the guard's resident cache, borrowed
+    (valid until the guard's next append, which may rebuild it)."""
+
+    def __init__(self, h, owner, config, batch, heads, dim, device):
+        self._h = h
+        self._owner = owner
+        self._config = config
+        self._batch = batch
+        self._heads = heads
+        self._dim = dim
+        self.device = device
+
+    def close(self):
+        self._h = None  # owned by the guard
+
+
+class QualityGuard:
+    """QualityGuard (guard.rs:38-246): a device-resident KiviCache plus the fp32
+    tape of every appended token; after each key flush the cache's attention
+    for a probe query is scored against dense fp32 attention over the tape
+    (cosine) and the cache is rebuilt with wider codes or a longer residual
+    while the cosine misses the threshold."""
+
+    def __init__(self, config, batch, num_kv_heads, head_dim, threshold, policy, max_bits,
+                 max_residual, device=0):
+        err = _Err()
+        h = C.c_void_p()
+        _check(lib().kivi_guard_new(C.byref(config._c()), batch, num_kv_heads, head_dim,
+                                    C.c_float(threshold), int(policy), max_bits, max_residual,
+                                    device, C.byref(h), C.byref(err)), err)
+        self._h = h.value
+        self._batch = batch
+        self._heads = num_kv_heads
+        self._dim = head_dim
+        self.device = device
+
+    @classmethod
+    def try_new(cls, config, batch, num_kv_heads, head_dim, threshold, policy, max_bits,
+                max_residual, device=0):
+        return cls(config, batch, num_kv_heads, head_dim, threshold, policy, max_bits,
+                   max_residual, device)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().kivi_guard_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _cache_handle(self):
+        return lib().kivi_guard_cache(self._h)
+
+    def config(self):
+        st = _State()
+        lib().kivi_cache_get_state(self._cache_handle(), C.byref(st))
+        return KiviConfig(int(st.config.bits), int(st.config.group_size),
+                          int(st.config.residual_length))
+
+    def cache(self):
+        return _GuardCache(self._cache_handle(), self, self.config(), self._batch, self._heads,
+                           self._dim, self.device)
+
+    def policy(self):
+        return int(lib().kivi_guard_policy(self._h))
+
+    def sequence_length(self):
+        return int(lib().kivi_guard_sequence_length(self._h))
+
+    def append(self, keys, values, seq_len, query, num_q_heads, scale):
+        """guard.rs:93-152: one FlushCheck per key flush inside this append."""
+        k, kp = _f32(keys)
+        v, vp = _f32(values)
+        q, qp = _f32(query)
+        cap = seq_len // max(1, self.config().group_size) + 1
+        checks = (_FlushCheck * cap)()
+        n = C.c_uint64(0)
+        err = _Err()
+        _check(lib().kivi_guard_append(self._h, kp, k.size, vp, v.size, seq_len, qp, q.size,
+                                       num_q_heads, C.c_float(scale), checks, cap, C.byref(n),
+                                       C.byref(err)), err)
+        out = []
+        for c in checks[: n.value]:
+            ups = [QualityUpgrade("Bits" if u.kind == 0 else "Residual", u.frm, u.to)
+                   for u in c.upgrades[: c.num_upgrades]]
+            out.append(FlushCheck(int(c.sequence_tokens), float(c.cosine_before), float(c.cosine),
+                                  ups))
+        return out

@@ -106,8 +106,30 @@ def lib():
         L.ko_marginal_bytes_per_layer.restype = C.c_uint64
         L.ko_round_half_even.argtypes = [C.c_float]
         L.ko_round_half_even.restype = C.c_float
+        L.ko_guard_new.argtypes = [C.c_uint8, sz, sz, sz, sz, sz, C.c_float, C.c_int, C.c_uint8, sz, e]
+        L.ko_guard_new.restype = P
+        L.ko_guard_free.argtypes = [P]
+        L.ko_guard_append.argtypes = [P, fp, sz, fp, sz, sz, fp, sz, sz, C.c_float,
+                                      C.POINTER(_FlushCheck), sz, szp, e]
+        L.ko_guard_cache.argtypes = [P]
+        L.ko_guard_cache.restype = P
+        L.ko_guard_config.argtypes = [P, u64p]
+        L.ko_guard_sequence_length.argtypes = [P]
+        L.ko_guard_sequence_length.restype = sz
+        L.ko_fp32_attention.argtypes = [fp, fp, fp, sz, sz, sz, sz, sz, C.c_float, fp]
+        L.ko_cosine_sim.argtypes = [fp, fp, sz]
+        L.ko_cosine_sim.restype = C.c_float
         _lib = L
     return _lib
+
+
+class _Upgrade(C.Structure):
+    _fields_ = [("kind", C.c_int32), ("frm", C.c_uint64), ("to", C.c_uint64)]
+
+
+class _FlushCheck(C.Structure):
+    _fields_ = [("sequence_tokens", C.c_uint64), ("cosine_before", C.c_float),
+                ("cosine", C.c_float), ("num_upgrades", C.c_uint32), ("upgrades", _Upgrade * 64)]
 
 
 def _f32(a):
@@ -368,3 +390,135 @@ def marginal_bytes_per_layer(config, num_kv_heads, head_dim):
 
 def round_half_even(x):
     return float(lib().ko_round_half_even(C.c_float(x)))
+
+
+# ---------------------------------------------------------------- guard.rs
+
+
+class QualityPolicy:
+    """guard.rs:14-20"""
+
+    RaiseBits = 0
+    LengthenResidual = 1
+
+
+class QualityUpgrade(tuple):
+    """guard.rs:23-27: ("Bits" | "Residual", from, to)."""
+
+    def __new__(cls, kind, from_, to):
+        return super().__new__(cls, (kind, int(from_), int(to)))
+
+    @classmethod
+    def Bits(cls, from_, to):
+        return cls("Bits", from_, to)
+
+    @classmethod
+    def Residual(cls, from_, to):
+        return cls("Residual", from_, to)
+
+
+class FlushCheck:
+    """guard.rs:30-36"""
+
+    def __init__(self, sequence_tokens, cosine_before, cosine, upgrades):
+        self.sequence_tokens = sequence_tokens
+        self.cosine_before = cosine_before
+        self.cosine = cosine
+        self.upgrades = upgrades
+
+    def __repr__(self):
+        return (f"FlushCheck(sequence_tokens={self.sequence_tokens}, cosine_before={self.cosine_before}, "
+                f"cosine={self.cosine}, upgrades={self.upgrades})")
+
+
+class _BorrowedCache(KiviCache):
+    """The guard's resident cache (guard.rs:77-79), owned by the guard."""
+
+    def __init__(self, h, owner, config, batch, heads, head_dim):
+        self._h = h
+        self._owner = owner
+        self.config = config
+        self.batch = batch
+        self.heads = heads
+        self.head_dim = head_dim
+
+    def __del__(self):
+        pass
+
+
+class QualityGuard:
+    """guard.rs:38-246 restated in C (cache + fp32 tape + cosine checks)."""
+
+    def __init__(self, h, batch, num_kv_heads, head_dim, policy):
+        self._h = h
+        self.batch = batch
+        self.heads = num_kv_heads
+        self.head_dim = head_dim
+        self._policy = policy
+
+    @classmethod
+    def try_new(cls, config, batch, num_kv_heads, head_dim, threshold, policy, max_bits,
+                max_residual):
+        err = _Err()
+        h = lib().ko_guard_new(config.bits, config.group_size, config.residual_length, batch,
+                               num_kv_heads, head_dim, C.c_float(threshold), policy, max_bits,
+                               max_residual, C.byref(err))
+        if not h:
+            _check(err.code or 1, err)
+        return cls(h, batch, num_kv_heads, head_dim, policy)
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().ko_guard_free(self._h)
+            self._h = None
+
+    def config(self):
+        out = (C.c_uint64 * 3)()
+        lib().ko_guard_config(self._h, out)
+        return KiviConfig(int(out[0]), int(out[1]), int(out[2]))
+
+    def cache(self):
+        return _BorrowedCache(lib().ko_guard_cache(self._h), self, self.config(), self.batch,
+                              self.heads, self.head_dim)
+
+    def policy(self):
+        return self._policy
+
+    def sequence_length(self):
+        return int(lib().ko_guard_sequence_length(self._h))
+
+    def append(self, keys, values, seq_len, query, num_q_heads, scale):
+        k, kp = _f32(keys)
+        v, vp = _f32(values)
+        q, qp = _f32(query)
+        cap = seq_len // max(1, self.config().group_size) + 1
+        checks = (_FlushCheck * cap)()
+        n = C.c_size_t(0)
+        err = _Err()
+        rc = lib().ko_guard_append(self._h, kp, k.size, vp, v.size, seq_len, qp, q.size, num_q_heads,
+                                   C.c_float(scale), checks, cap, C.byref(n), C.byref(err))
+        _check(rc, err)
+        out = []
+        for c in checks[: n.value]:
+            ups = [QualityUpgrade("Bits" if u.kind == 0 else "Residual", u.frm, u.to)
+                   for u in c.upgrades[: c.num_upgrades]]
+            out.append(FlushCheck(int(c.sequence_tokens), float(c.cosine_before), float(c.cosine), ups))
+        return out
+
+
+def fp32_attention(query, keys, values, batch, kv_heads, q_heads, seq, dim, scale):
+    """guard.rs:294-341"""
+    q, qp = _f32(query)
+    k, kp = _f32(keys)
+    v, vp = _f32(values)
+    out = np.zeros(batch * q_heads * dim, np.float32)
+    lib().ko_fp32_attention(qp, kp, vp, batch, kv_heads, q_heads, seq, dim, C.c_float(scale),
+                            out.ctypes.data_as(C.POINTER(C.c_float)))
+    return out
+
+
+def cosine_sim(a, b):
+    """guard.rs:343-359"""
+    x, xp = _f32(a)
+    y, yp = _f32(b)
+    return float(lib().ko_cosine_sim(xp, yp, x.size))

@@ -1066,3 +1066,253 @@ uint64_t ko_marginal_bytes_per_layer(uint8_t bits, size_t group_size, size_t num
     size_t per_head = d * b / 8 + d * 8 / g + d * b / 8 + val_groups_per_token(d, g) * 8;
     return per_head * num_kv_heads;
 }
+
+/* ------------------------------------------------------------------ guard.rs */
+
+/* guard.rs:38-47 */
+struct ko_guard {
+    ko_cache *cache;
+    float *keys, *values; /* fp32 tape [batch, heads, seq, dim] */
+    size_t seq;
+    float threshold;
+    uint8_t max_bits;
+    size_t max_residual;
+    int policy;
+};
+
+ko_guard *ko_guard_new(uint8_t bits, size_t group_size, size_t residual_length, size_t batch,
+                       size_t heads, size_t head_dim, float threshold, int policy,
+                       uint8_t max_bits, size_t max_residual, ko_error *err) {
+    ko_cache *c = ko_cache_new(bits, group_size, residual_length, batch, heads, head_dim, err);
+    if (!c) return NULL;
+    ko_guard *g = (ko_guard *)calloc(1, sizeof(ko_guard));
+    g->cache = c;
+    g->threshold = threshold;
+    g->policy = policy;
+    g->max_bits = max_bits;
+    g->max_residual = max_residual;
+    return g;
+}
+
+void ko_guard_free(ko_guard *g) {
+    if (!g) return;
+    ko_cache_free(g->cache);
+    free(g->keys);
+    free(g->values);
+    free(g);
+}
+
+const ko_cache *ko_guard_cache(const ko_guard *g) { return g->cache; }
+
+void ko_guard_config(const ko_guard *g, uint64_t out[3]) {
+    out[0] = g->cache->bits;
+    out[1] = g->cache->group_size;
+    out[2] = g->cache->residual_length;
+}
+
+size_t ko_guard_sequence_length(const ko_guard *g) { return g->seq; }
+
+/* guard.rs:294-341 (Rust's `a += b * c` is a separate multiply and add) */
+void ko_fp32_attention(const float *query, const float *keys, const float *values, size_t batch,
+                       size_t kv_heads, size_t q_heads, size_t seq, size_t dim, float scale,
+                       float *out) {
+    const size_t group = q_heads / kv_heads;
+    float *logits = (float *)malloc((seq ? seq : 1) * sizeof(float));
+    for (size_t b = 0; b < batch; ++b) {
+        for (size_t qh = 0; qh < q_heads; ++qh) {
+            const size_t kvh = qh / group;
+            const float *q = query + (b * q_heads + qh) * dim;
+            const size_t base = (b * kv_heads + kvh) * seq * dim;
+            for (size_t t = 0; t < seq; ++t) {
+                float dot = 0.0f;
+                for (size_t d = 0; d < dim; ++d) dot += q[d] * keys[base + t * dim + d];
+                logits[t] = dot * scale;
+            }
+            float mx = -INFINITY;
+            for (size_t t = 0; t < seq; ++t) mx = fmaxf(mx, logits[t]);
+            float sum = 0.0f;
+            for (size_t t = 0; t < seq; ++t) {
+                logits[t] = expf(logits[t] - mx);
+                sum += logits[t];
+            }
+            float *y = out + (b * q_heads + qh) * dim;
+            for (size_t d = 0; d < dim; ++d) y[d] = 0.0f;
+            for (size_t t = 0; t < seq; ++t) {
+                const float w = logits[t] / sum;
+                for (size_t d = 0; d < dim; ++d) y[d] += w * values[base + t * dim + d];
+            }
+        }
+    }
+    free(logits);
+}
+
+/* guard.rs:343-359 */
+float ko_cosine_sim(const float *a, const float *b, size_t n) {
+    float dot = 0.0f, na = 0.0f, nb = 0.0f;
+    for (size_t i = 0; i < n; ++i) {
+        dot += a[i] * b[i];
+        na += a[i] * a[i];
+        nb += b[i] * b[i];
+    }
+    const float denom = sqrtf(na) * sqrtf(nb);
+    return denom == 0.0f ? 1.0f : dot / denom;
+}
+
+/* guard.rs:267-292: the tape grows by concatenation per stream */
+static void guard_push(ko_guard *g, const float *keys, const float *values, size_t len) {
+    const ko_cache *c = g->cache;
+    const size_t hs = c->batch * c->heads, dim = c->head_dim, total = g->seq + len;
+    float *nk = (float *)malloc(hs * total * dim * sizeof(float) + 1);
+    float *nv = (float *)malloc(hs * total * dim * sizeof(float) + 1);
+    for (size_t hi = 0; hi < hs; ++hi) {
+        if (g->seq) {
+            memcpy(nk + hi * total * dim, g->keys + hi * g->seq * dim, g->seq * dim * sizeof(float));
+            memcpy(nv + hi * total * dim, g->values + hi * g->seq * dim, g->seq * dim * sizeof(float));
+        }
+        memcpy(nk + hi * total * dim + g->seq * dim, keys + hi * len * dim, len * dim * sizeof(float));
+        memcpy(nv + hi * total * dim + g->seq * dim, values + hi * len * dim, len * dim * sizeof(float));
+    }
+    free(g->keys);
+    free(g->values);
+    g->keys = nk;
+    g->values = nv;
+    g->seq = total;
+}
+
+/* guard.rs:237-250 */
+static int guard_cosine(ko_guard *g, const float *query, size_t query_len, size_t num_q_heads,
+                        float scale, float *out, ko_error *err) {
+    const ko_cache *c = g->cache;
+    const size_t n = c->batch * num_q_heads * c->head_dim;
+    float *got = (float *)malloc(n * sizeof(float));
+    float *expect = (float *)malloc(n * sizeof(float));
+    int rc = ko_cache_attention(c, query, query_len, num_q_heads, scale, got, 1, err);
+    if (rc == KO_OK) {
+        ko_fp32_attention(query, g->keys, g->values, c->batch, c->heads, num_q_heads, g->seq,
+                          c->head_dim, scale, expect);
+        *out = ko_cosine_sim(got, expect, n);
+    }
+    free(got);
+    free(expect);
+    return rc;
+}
+
+/* guard.rs:175-197, 252-284: next configuration under the policy (0 = none) */
+static int guard_propose(const ko_guard *g, ko_upgrade *u) {
+    const ko_cache *c = g->cache;
+    if (g->policy == KO_POLICY_RAISE_BITS) {
+        const unsigned next = c->bits == 2 ? 4u : c->bits == 4 ? 8u : 0u;
+        if (next == 0 || next > g->max_bits) return 0;
+        u->kind = KO_UPGRADE_BITS;
+        u->from = c->bits;
+        u->to = next;
+        return 1;
+    }
+    const size_t cur = c->residual_length;
+    if (cur >= g->max_residual) return 0;
+    const size_t doubled = cur > SIZE_MAX / 2 ? SIZE_MAX : cur * 2;
+    const size_t next = doubled <= g->max_residual ? doubled : g->max_residual;
+    if (!(next > cur && next % c->group_size == 0)) return 0;
+    u->kind = KO_UPGRADE_RESIDUAL;
+    u->from = cur;
+    u->to = next;
+    return 1;
+}
+
+/* guard.rs:199-225: rebuild the resident cache from the tape */
+static int guard_apply(ko_guard *g, const ko_upgrade *u, ko_error *err) {
+    const ko_cache *c = g->cache;
+    const uint8_t bits = u->kind == KO_UPGRADE_BITS ? (uint8_t)u->to : c->bits;
+    const size_t residual = u->kind == KO_UPGRADE_RESIDUAL ? (size_t)u->to : c->residual_length;
+    if (ko_config_check(bits, c->group_size, residual, err)) return err ? err->code : 1;
+    ko_cache *nc = ko_cache_new(bits, c->group_size, residual, c->batch, c->heads, c->head_dim, err);
+    if (!nc) return err ? err->code : 1;
+    if (g->seq > 0) {
+        const size_t n = c->batch * c->heads * g->seq * c->head_dim;
+        const int rc = ko_cache_append(nc, g->keys, n, g->values, n, g->seq, err);
+        if (rc) {
+            ko_cache_free(nc);
+            return rc;
+        }
+    }
+    ko_cache_free(g->cache);
+    g->cache = nc;
+    return KO_OK;
+}
+
+/* guard.rs:154-173 */
+static int guard_check(ko_guard *g, const float *query, size_t query_len, size_t num_q_heads,
+                       float scale, ko_flush_check *out, ko_error *err) {
+    memset(out, 0, sizeof(*out));
+    float cos = 0.0f;
+    int rc = guard_cosine(g, query, query_len, num_q_heads, scale, &cos, err);
+    if (rc) return rc;
+    out->cosine_before = cos;
+    while (cos < g->threshold) {
+        ko_upgrade u;
+        if (!guard_propose(g, &u)) break;
+        if ((rc = guard_apply(g, &u, err))) return rc;
+        if (out->num_upgrades < KO_MAX_UPGRADES) out->upgrades[out->num_upgrades++] = u;
+        if ((rc = guard_cosine(g, query, query_len, num_q_heads, scale, &cos, err))) return rc;
+    }
+    out->cosine = cos;
+    out->sequence_tokens = g->seq;
+    return KO_OK;
+}
+
+/* guard.rs:93-152 */
+int ko_guard_append(ko_guard *g, const float *keys, size_t keys_len, const float *values,
+                    size_t values_len, size_t seq, const float *query, size_t query_len,
+                    size_t num_q_heads, float scale, ko_flush_check *checks,
+                    size_t checks_capacity, size_t *num_checks, ko_error *err) {
+    const ko_cache *c = g->cache;
+    const size_t batch = c->batch, heads = c->heads, dim = c->head_dim;
+    *num_checks = 0;
+    const size_t expected = batch * heads * seq * dim;
+    if (keys_len != expected) {
+        set_err(err, KO_SHAPE, expected, keys_len, NULL);
+        return KO_SHAPE;
+    }
+    if (values_len != expected) {
+        set_err(err, KO_SHAPE, expected, values_len, NULL);
+        return KO_SHAPE;
+    }
+    const size_t query_elems = batch * num_q_heads * dim;
+    if (num_q_heads == 0 || num_q_heads % heads != 0) {
+        set_err(err, KO_QUERY_HEADS, num_q_heads, heads, NULL);
+        return KO_QUERY_HEADS;
+    }
+    if (query_len != query_elems) {
+        set_err(err, KO_SHAPE, query_elems, query_len, NULL);
+        return KO_SHAPE;
+    }
+    size_t offset = 0;
+    while (offset < seq) {
+        c = g->cache;
+        const size_t room = c->residual_length > c->key_res_len ? c->residual_length - c->key_res_len : 0;
+        const size_t take = room < seq - offset ? room : seq - offset;
+        const size_t hs = batch * heads;
+        float *ks = (float *)malloc(hs * take * dim * sizeof(float) + 1);
+        float *vs = (float *)malloc(hs * take * dim * sizeof(float) + 1);
+        for (size_t hi = 0; hi < hs; ++hi) { /* guard.rs:248-265 slice_tokens */
+            memcpy(ks + hi * take * dim, keys + hi * seq * dim + offset * dim, take * dim * sizeof(float));
+            memcpy(vs + hi * take * dim, values + hi * seq * dim + offset * dim, take * dim * sizeof(float));
+        }
+        int rc = ko_cache_append(g->cache, ks, hs * take * dim, vs, hs * take * dim, take, err);
+        if (rc == KO_OK) guard_push(g, ks, vs, take);
+        free(ks);
+        free(vs);
+        if (rc) return rc;
+        if (g->cache->key_res_len == 0) {
+            if (*num_checks >= checks_capacity) {
+                set_err(err, KO_SHAPE, *num_checks + 1, checks_capacity, "checks");
+                return KO_SHAPE;
+            }
+            rc = guard_check(g, query, query_len, num_q_heads, scale, &checks[*num_checks], err);
+            if (rc) return rc;
+            ++*num_checks;
+        }
+        offset += take;
+    }
+    return KO_OK;
+}

@@ -118,6 +118,42 @@ uint64_t ko_marginal_bytes_per_layer(uint8_t bits, size_t group_size, size_t num
 /* quant.rs:474-485 */
 float ko_round_half_even(float x);
 
+/* guard.rs: QualityGuard (one KIVI layer plus its fp32 reference tape). */
+enum { KO_POLICY_RAISE_BITS = 0, KO_POLICY_LENGTHEN_RESIDUAL = 1 }; /* guard.rs:14-20 */
+enum { KO_UPGRADE_BITS = 0, KO_UPGRADE_RESIDUAL = 1 };             /* guard.rs:23-27 */
+#define KO_MAX_UPGRADES 64
+typedef struct ko_upgrade {
+    int32_t kind;
+    uint64_t from, to;
+} ko_upgrade;
+typedef struct ko_flush_check { /* guard.rs:30-36 */
+    uint64_t sequence_tokens;
+    float cosine_before, cosine;
+    uint32_t num_upgrades;
+    ko_upgrade upgrades[KO_MAX_UPGRADES];
+} ko_flush_check;
+typedef struct ko_guard ko_guard;
+/* guard.rs:50-71 */
+ko_guard *ko_guard_new(uint8_t bits, size_t group_size, size_t residual_length, size_t batch,
+                       size_t heads, size_t head_dim, float threshold, int policy,
+                       uint8_t max_bits, size_t max_residual, ko_error *err);
+void ko_guard_free(ko_guard *g);
+/* guard.rs:93-152; checks must hold seq / group_size + 1 entries */
+int ko_guard_append(ko_guard *g, const float *keys, size_t keys_len, const float *values,
+                    size_t values_len, size_t seq, const float *query, size_t query_len,
+                    size_t num_q_heads, float scale, ko_flush_check *checks,
+                    size_t checks_capacity, size_t *num_checks, ko_error *err);
+const ko_cache *ko_guard_cache(const ko_guard *g);
+/* out[3] = bits, group_size, residual_length of the resident cache */
+void ko_guard_config(const ko_guard *g, uint64_t out[3]);
+size_t ko_guard_sequence_length(const ko_guard *g);
+/* guard.rs:294-341: dense fp32 attention over [batch, kv_heads, seq, dim] K/V */
+void ko_fp32_attention(const float *query, const float *keys, const float *values, size_t batch,
+                       size_t kv_heads, size_t q_heads, size_t seq, size_t dim, float scale,
+                       float *out);
+/* guard.rs:343-359 */
+float ko_cosine_sim(const float *a, const float *b, size_t n);
+
 #ifdef __cplusplus
 }
 #endif
