@@ -65,6 +65,10 @@ namespace {
 constexpr int kConsumers = 4;
 constexpr int kTcThreads = kConsumers * 32;
 constexpr int kStages = KIVI_TC_STAGES; // pipeline depth (groups in flight per CTA)
+// warp w owns the stages i % kStages of its groups i = w, w + kConsumers, ...:
+// a stage (and its mbarrier) must belong to one warp only
+static_assert(kStages % kConsumers == 0 && kStages >= kConsumers,
+              "stages must be a positive multiple of the consumer warps");
 #ifndef KIVI_TC_WAVES
 #define KIVI_TC_WAVES 1
 #endif
