@@ -760,6 +760,8 @@ def run_gpu(args, cfgd, rank, world, local_rank):
             "input_gbs": PREFILL_MS[1] * cfgd["D"] * 8 / (PREFILL_MS[0] / 1e3) / 1e9,
             "ms": PREFILL_MS[0], "chunk_kernel": "key_groups + value_tokens + copy_rows",
         }
+    if mode == "seqshard" and rank == 0:
+        result["key_flush"] = key_flush_microbench(K, cfgd, stream)
     if mode == "rag":
         c = cfgd
         flops = 4 * c["sessions"] * c["B"] * c["Hq"] * (c["ctx"] + c["suffix"]) * c["D"]
@@ -875,32 +877,88 @@ def time_oracle_rag_steps(state, rng, chs, cfgd, steps, threads, budget_s):
     return (t_append + t_attn * S / ns) / steps, ns
 
 
-def cpu_time(cfgd, steps, threads, budget_s, warm=0):
+def cpu_time(cfgd, steps, threads, budget_s, warm=0, also_single=False):
+    """Per-step seconds of the oracle on `threads` host threads (and, with
+    also_single, on one thread over the same state, after the first run)."""
     if cfgd["mode"] == "rag":
         state, rng, chs = build_oracle_rag(cfgd)
-        if warm:
-            time_oracle_rag_steps(state, rng, chs, cfgd, warm, threads, budget_s / 10)
-        per_step, n = time_oracle_rag_steps(state, rng, chs, cfgd, steps, threads, budget_s)
-        what = f"attention on {n} of {cfgd['sessions']} sessions per step, scaled"
+        run = lambda n_steps, th, b: time_oracle_rag_steps(state, rng, chs, cfgd, n_steps, th, b)
+        label = lambda n: f"attention on {n} of {cfgd['sessions']} sessions per step, scaled"
     else:
         c, rng, chs = build_oracle_cache(cfgd)
-        if warm:
-            time_oracle_steps(c, rng, chs, cfgd, warm, threads, budget_s / 10)
-        per_step, n = time_oracle_steps(c, rng, chs, cfgd, steps, threads, budget_s)
-        what = (f"append timed on all {cfgd['B']} sequences, attention on {n} of "
-                f"{cfgd['B']} and scaled")
-    return per_step, what
+        run = lambda n_steps, th, b: time_oracle_steps(c, rng, chs, cfgd, n_steps, th, b)
+        label = lambda n: (f"append timed on all {cfgd['B']} sequences, attention on {n} of "
+                           f"{cfgd['B']} and scaled")
+    if warm:
+        run(warm, threads, budget_s / 10)
+    per_step, n = run(steps, threads, budget_s)
+    if not also_single:
+        return per_step, label(n)
+    per_step1, n1 = run(2, 1, budget_s / 2)
+    return per_step, label(n), per_step1, label(n1)
+
+
+def key_flush_microbench(K, cfgd, stream, reps=12):
+    """Forced key flush (cache.rs:382-430): a 1-token append that completes the
+    R-token fp32 key residual of every stream (B x H streams) and quantizes it
+    into R / G packed groups, timed with CUDA events on the launching stream
+    (median of `reps`); beside it a 1-token append that does not flush."""
+    import torch
+
+    B, H, D, R = cfgd["B"], cfgd["H"], cfgd["D"], cfgd["R"]
+    cfg = K.KiviConfig.try_new(cfgd["bits"], cfgd["G"], R)
+    c = K.KiviCache(cfg, B, H, D, device=torch.cuda.current_device())
+    c.reserve((reps + 4) * R)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(77)
+    fill_k = torch.randn((B, H, R - 2, D), generator=g, device="cuda")
+    fill_v = torch.randn((B, H, R - 2, D), generator=g, device="cuda")
+    one_k = torch.randn((B, H, 1, D), generator=g, device="cuda")
+    one_v = torch.randn((B, H, 1, D), generator=g, device="cuda")
+    flush, plain = [], []
+    for _ in range(reps + 2):
+        c.append_dev(fill_k, fill_v, R - 2, stream=stream)  # residual at R - 2
+        for dst in (plain, flush):  # R - 1 (no flush), then R (flush)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            c.append_dev(one_k, one_v, 1, stream=stream)
+            e1.record(stream)
+            stream.synchronize()
+            dst.append(e0.elapsed_time(e1) * 1e3)
+    c.close()
+    return {"flush_append_us": float(np.median(flush[2:])), "plain_append_us": float(np.median(plain[2:])),
+            "tokens_flushed_per_stream": R, "streams": B * H, "reps": reps,
+            "what": "1-token append_dev completing the key residual (quantizes R tokens per stream) "
+                    "vs one that does not"}
+
+
+def host_info():
+    """CPU model and logical core count of this host."""
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"cpu_model": model, "nproc": os.cpu_count()}
 
 
 def cpu_baseline(cfgd, budget_s=20.0):
     threads = os.cpu_count() or 1
     steps = 4
-    per_step, what = cpu_time(cfgd, steps, threads, budget_s)
+    # also the same sample on one core: the reference itself is single-threaded
+    per_step, what, per_step1, what1 = cpu_time(cfgd, steps, threads, budget_s, also_single=True)
     return {
         "value": 1.0 / per_step, "unit": "steps/s", "cores": threads, "kind": "port",
         "sample": (f"{steps} decode steps of {cfgd['name']} on the C restatement of the reference "
                    f"(oracle/, gcc -O3 -ffp-contract=off, {threads} threads over (batch, q-head) "
                    f"pairs); {what}"),
+        "single_core": {"value": 1.0 / per_step1, "unit": "steps/s", "cores": 1,
+                        "sample": f"2 decode steps, 1 thread (the reference's own loop); {what1}"},
+        "host": host_info(),
     }
 
 
@@ -923,6 +981,7 @@ def run_reference(args, cfgd, rank, world):
             "value": v, "unit": "steps/s", "cores": threads, "kind": "port",
             "sample": (f"reference algorithm restated in C (oracle/, no cargo on this image), "
                        f"{threads} threads; {what}"),
+            "host": host_info(),
         },
         "e2e": {"value": v, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
