@@ -875,13 +875,111 @@ class AgentMemoryBudget:
         return 1.0 if kivi == 0 else self.fp16_bytes_for_agents(agents, context_tokens) / kivi
 
 
+_USIZE_MAX = (1 << 64) - 1
+
+
+class MixedPrecisionBudget:
+    """MixedPrecisionBudget (budget.rs:157-314): one bit width per layer, the
+    group size, residual length and head shape shared; every byte count is
+    layer_kv_bytes (the live cache's memory().compressed_bytes())."""
+
+    def __init__(self, layers, num_kv_heads, head_dim):
+        self._layers = list(layers)
+        self._heads = num_kv_heads
+        self._dim = head_dim
+
+    @classmethod
+    def try_from_bits(cls, bits_per_layer, group_size, residual_length, num_kv_heads, head_dim):
+        """budget.rs:171-201"""
+        bits_per_layer = list(bits_per_layer)
+        if not bits_per_layer:
+            raise KiviError(6, name="num_layers", message="num_layers must be greater than zero")
+        if num_kv_heads == 0:
+            raise KiviError(6, name="num_kv_heads", message="num_kv_heads must be greater than zero")
+        layers = []
+        for bits in bits_per_layer:
+            cfg = KiviConfig.try_new(bits, group_size, residual_length)
+            if head_dim == 0 or head_dim % cfg.group_size != 0:
+                raise KiviError(4, head_dim, cfg.group_size,
+                                message=f"head_dim {head_dim} must be a positive multiple of "
+                                        f"group_size {cfg.group_size}")
+            layers.append(cfg)
+        return cls(layers, num_kv_heads, head_dim)
+
+    @classmethod
+    def early_wide(cls, num_layers, early_layers, early_bits, late_bits, group_size,
+                   residual_length, num_kv_heads, head_dim):
+        """budget.rs:203-226: the first early_layers at early_bits, the rest at late_bits."""
+        if num_layers == 0:
+            raise KiviError(6, name="num_layers", message="num_layers must be greater than zero")
+        if early_layers > num_layers:
+            raise KiviError(9, early_layers, num_layers,
+                            message=f"early_layers {early_layers} exceeds num_layers {num_layers}")
+        bits = [early_bits] * early_layers + [late_bits] * (num_layers - early_layers)
+        return cls.try_from_bits(bits, group_size, residual_length, num_kv_heads, head_dim)
+
+    def num_layers(self):
+        return len(self._layers)
+
+    def num_kv_heads(self):
+        return self._heads
+
+    def head_dim(self):
+        return self._dim
+
+    def group_size(self):
+        return self._layers[0].group_size
+
+    def residual_length(self):
+        return self._layers[0].residual_length
+
+    def layer_bits(self, layer):
+        return self._layers[layer].bits if 0 <= layer < len(self._layers) else None
+
+    def layer_config(self, layer):
+        return self._layers[layer] if 0 <= layer < len(self._layers) else None
+
+    def bytes_for_layer(self, layer, context_tokens):
+        if not 0 <= layer < len(self._layers):
+            return None
+        return layer_kv_bytes(self._layers[layer], self._heads, self._dim, context_tokens)
+
+    def bytes_for_context(self, context_tokens):
+        return sum(layer_kv_bytes(c, self._heads, self._dim, context_tokens) for c in self._layers)
+
+    def bytes_for_agents(self, agents, context_tokens):
+        return agents * self.bytes_for_context(context_tokens)
+
+    def marginal_bytes_per_token(self):
+        return sum(marginal_bytes_per_layer(c, self._heads, self._dim) for c in self._layers)
+
+    def next_token_bytes(self, current_tokens):
+        return self.bytes_for_context(current_tokens + 1) - self.bytes_for_context(current_tokens)
+
+    def max_agents(self, budget_bytes, context_tokens):
+        per = self.bytes_for_context(context_tokens)
+        return _USIZE_MAX if per == 0 else budget_bytes // per
+
+    def fits(self, budget_bytes, agents, context_tokens):
+        return self.bytes_for_agents(agents, context_tokens) <= budget_bytes
+
+    def fp16_bytes_for_agents(self, agents, context_tokens):
+        return 2 * agents * self.num_layers() * context_tokens * self._heads * self._dim * 2
+
+    def compression_ratio_vs_fp16(self, agents, context_tokens):
+        kivi = self.bytes_for_agents(agents, context_tokens)
+        return 1.0 if kivi == 0 else self.fp16_bytes_for_agents(agents, context_tokens) / kivi
+
+
 __all__ = [
     "KiviError", "KiviConfig", "KiviCache", "MemoryReport", "MemoryBudgetSnapshot",
     "SharedPrefix", "SharedPrefixFootprint", "RagSession", "RuntimeKv", "QuantAxis",
     "QuantizedTensor", "quantize_per_channel", "quantize_per_token", "layer_kv_bytes",
     "marginal_bytes_per_layer", "AgentMemoryBudget", "sessions_attention_batched",
     "sessions_attention_batched_dev", "sessions_append_dev", "merge_partials_dev", "kernel_launches", "lib", "LIB_PATH",
-    "QualityGuard", "QualityPolicy", "QualityUpgrade", "FlushCheck",
+    "QualityGuard", "QualityPolicy", "QualityUpgrade", "FlushCheck", "MixedPrecisionBudget",
+    "ModelPreset", "EconInputs", "EconReport", "PretrainEstimate", "compute_report",
+    "estimate_pretrain", "gpus_for_kv", "kv_budget_bytes", "parse_context_tokens",
 ]
 
 
@@ -1024,3 +1122,18 @@ class QualityGuard:
             out.append(FlushCheck(int(c.sequence_tokens), float(c.cosine_before), float(c.cosine),
                                   ups))
         return out
+
+
+# ---------------------------------------------------------------- econ.rs (host arithmetic)
+
+from .econ import (  # noqa: E402  (re-exported at the top level, as lib.rs does)
+    EconInputs,
+    EconReport,
+    ModelPreset,
+    PretrainEstimate,
+    compute_report,
+    estimate_pretrain,
+    gpus_for_kv,
+    kv_budget_bytes,
+    parse_context_tokens,
+)
