@@ -8,7 +8,9 @@
 //   * code = clamp(round_half_even((x - zero) / scale), 0, levels): the
 //     quotient is >= 0, and rintf (round-to-nearest-even) equals the
 //     reference's floor/frac/parity rounding (quant.rs:474-485) for every
-//     finite input; NaN -> 0 like Rust's saturating `as u32`;
+//     finite input; NaN -> 0 like Rust's saturating `as u32`.  The quotient
+//     comes from a reciprocal multiply, redone with IEEE division whenever it
+//     lies close enough to a rounding boundary to matter (Quantizer below);
 //   * codes packed first-element-in-low-bits (quant.rs:312-322);
 //   * dequantization is one fused multiply-add fma(code, scale, zero)
 //     (quant.rs:404-406).
@@ -40,14 +42,41 @@ __device__ __forceinline__ float scale_of(float span, float levels) {
     return span == 0.0f ? 0.0f : __fdiv_rn(span, levels);
 }
 
-__device__ __forceinline__ uint32_t quant_code(float x, float zero, float scale, float levels) {
-    if (scale == 0.0f) return 0u;
-    float r = rintf(__fdiv_rn(__fsub_rn(x, zero), scale));
-    if (!(r == r)) return 0u;
-    if (r < 0.0f) return 0u;
-    if (r > levels) r = levels;
-    return (uint32_t)r;
-}
+// One group's quantizer (quant.rs:461-472): code = clamp(round_half_even(
+// (x - zero) / scale), 0, levels), 0 when scale == 0.  The quotient is formed as
+// (x - zero) * (1 / scale): that product and the correctly rounded quotient
+// differ by at most 1.8e-7 * q (two roundings of 2^-24 each, plus the
+// quotient's own), i.e. 4.6e-5 for q <= 256, so their nearest integers agree
+// unless q lies within that distance of a half-integer; quotients within 2^-12
+// of one are redone with IEEE division, so every code is the reference's.
+// The reciprocal path is taken only for a normal scale with a normal
+// reciprocal.  NaN quotients give 0 and +-inf clamp as in the reference
+// (fmaxf drops a NaN operand); codes come out of the mantissa of r + 2^23.
+struct Quantizer {
+    float zero, scale, rcp, levels;
+    bool fast;
+    __device__ __forceinline__ Quantizer(float mn, float s, float lv)
+        : zero(mn), scale(s), rcp(0.0f), levels(lv), fast(false) {
+        if (s >= 0x1p-125f && s <= 0x1p125f) {
+            rcp = __frcp_rn(s);
+            fast = true;
+        }
+    }
+    __device__ __forceinline__ uint32_t code(float x) const {
+        if (scale == 0.0f) return 0u;
+        const float d = __fsub_rn(x, zero);
+        float r;
+        if (fast) {
+            const float q = __fmul_rn(d, rcp);
+            r = rintf(q);
+            if (fabsf(__fsub_rn(q, r)) > 0.5f - 0x1p-12f) r = rintf(__fdiv_rn(d, scale));
+        } else {
+            r = rintf(__fdiv_rn(d, scale));
+        }
+        r = fminf(fmaxf(r, 0.0f), levels);
+        return __float_as_uint(__fadd_rn(r, 8388608.0f)) & 0xFFFFu;
+    }
+};
 
 // Per-channel key quantization of one channel `d` of one group whose G rows
 // are rows[u * D] (u < G).  quant.rs:296-325.
@@ -62,10 +91,10 @@ __device__ __forceinline__ void quant_key_channel(const Geom &g, const float *co
     }
     const float scale = scale_of(__fsub_rn(mx, mn), g.levels);
     *param = make_float2(scale, mn);
+    const Quantizer qz(mn, scale, g.levels);
     for (int i = 0; i < g.ipc; ++i) {
         uint32_t w = 0;
-        for (int k = 0; k < g.tpw; ++k)
-            w |= quant_code(rows[i * g.tpw + k][d], mn, scale, g.levels) << (k * g.bits);
+        for (int k = 0; k < g.tpw; ++k) w |= qz.code(rows[i * g.tpw + k][d]) << (k * g.bits);
         words[i] = w;
     }
 }
@@ -95,11 +124,12 @@ __device__ __forceinline__ void quant_value_g32(const float *grp, uint32_t *word
     }
     const float scale = scale_of(__fsub_rn(mx, mn), kLevels);
     *param = make_float2(scale, mn);
+    const Quantizer qz(mn, scale, kLevels);
 #pragma unroll
     for (int w = 0; w < IPC; ++w) {
         uint32_t word = 0;
 #pragma unroll
-        for (int k = 0; k < TPW; ++k) word |= quant_code(x[w * TPW + k], mn, scale, kLevels) << (k * BITS);
+        for (int k = 0; k < TPW; ++k) word |= qz.code(x[w * TPW + k]) << (k * BITS);
         words[w] = word;
     }
 }
@@ -123,10 +153,10 @@ __device__ __forceinline__ void quant_value_group(const Geom &g, const float *ro
     }
     const float scale = scale_of(__fsub_rn(mx, mn), g.levels);
     *param = make_float2(scale, mn);
+    const Quantizer qz(mn, scale, g.levels);
     for (int w = 0; w < g.ipc; ++w) {
         uint32_t word = 0;
-        for (int k = 0; k < g.tpw; ++k)
-            word |= quant_code(grp[w * g.tpw + k], mn, scale, g.levels) << (k * g.bits);
+        for (int k = 0; k < g.tpw; ++k) word |= qz.code(grp[w * g.tpw + k]) << (k * g.bits);
         words[w] = word;
     }
 }
@@ -151,10 +181,11 @@ __device__ __forceinline__ void quant_value_group_warp(const Geom &g, const floa
     }
     const float scale = scale_of(__fsub_rn(mx, mn), g.levels);
     if (lane == 0) *param = make_float2(scale, mn);
+    const Quantizer qz(mn, scale, g.levels);
     for (int w = 0; w < g.ipc; ++w) {
         uint32_t part = 0;
         for (int i = lane; i < g.G; i += 32)
-            if (i / g.tpw == w) part |= quant_code(grp[i], mn, scale, g.levels) << ((i % g.tpw) * g.bits);
+            if (i / g.tpw == w) part |= qz.code(grp[i]) << ((i % g.tpw) * g.bits);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) part |= __shfl_xor_sync(0xffffffffu, part, o);
         if (lane == 0) words[w] = part;

@@ -114,6 +114,52 @@ def test_codec_bit_exact(K, bits, group, axis):
     assert (qt.pytorch_codes() == O.pytorch_codes(axis == 0, oc, batch, heads, tokens, dim, bits, group)).all()
 
 
+def near_tie_groups(rng, bits, group, count):
+    """`count` groups of `group` fp32 values whose quotients (x - min) / scale
+    land on and within a few ulps of half-integers (the rounding boundaries),
+    with scales that are not powers of two."""
+    levels = (1 << bits) - 1
+    out = np.empty((count, group), np.float32)
+    for i in range(count):
+        mn = np.float32(rng.uniform(-3.0, 3.0))
+        mx = np.float32(mn + np.float32(rng.uniform(0.01, 10.0)))
+        scale = np.float32(np.float32(mx - mn) / np.float32(levels))
+        vals = [mn, mx]
+        while len(vals) < group:
+            k = int(rng.integers(0, levels))
+            x = np.float32(mn + np.float32(np.float32(k + 0.5) * scale))
+            for _ in range(abs(int(rng.integers(-4, 5)))):
+                x = np.nextafter(x, np.float32(np.inf if rng.random() < 0.5 else -np.inf), dtype=np.float32)
+            vals.append(np.float32(min(max(x, mn), mx)))
+        vals = np.array(vals, np.float32)
+        rng.shuffle(vals)
+        out[i] = vals
+    return out
+
+
+@pytest.mark.parametrize("bits,group", [(2, 32), (4, 32), (8, 32), (2, 16), (4, 64)])
+@pytest.mark.parametrize("axis", [0, 1])
+def test_codec_near_ties_bit_exact(K, bits, group, axis):
+    """Codes whose quotients sit on or next to a rounding boundary (where a
+    reciprocal-multiply quotient could round differently from the reference's
+    IEEE division) equal the oracle's bit for bit."""
+    rng = np.random.default_rng(bits * 1000 + group * 10 + axis)
+    batch, heads, dim = 1, 2, max(64, group)
+    tokens = 4 * group if axis == 0 else 40
+    data = np.empty((batch, heads, tokens, dim), np.float32)
+    if axis == 0:  # groups of `group` tokens of one channel
+        g = near_tie_groups(rng, bits, group, batch * heads * (tokens // group) * dim)
+        data[:] = g.reshape(batch, heads, tokens // group, dim, group).transpose(0, 1, 2, 4, 3).reshape(data.shape)
+    else:  # groups of `group` channels of one token
+        g = near_tie_groups(rng, bits, group, batch * heads * tokens * (dim // group))
+        data[:] = g.reshape(data.shape)
+    fn = K.quantize_per_channel if axis == 0 else K.quantize_per_token
+    qt = fn(data, batch, heads, tokens, dim, bits, group)
+    oc, op = O.quantize(axis == 0, data, batch, heads, tokens, dim, bits, group)
+    assert (qt.params.view(np.uint32) == op.view(np.uint32)).all()
+    assert (qt.codes == oc).all()
+
+
 def test_pytorch_golden_words(K):
     """tests/quant.rs:13-41, examples/pytorch_golden.rs:16-67"""
     dim, seq = 32, 64
