@@ -758,7 +758,7 @@ def run_gpu(args, cfgd, rank, world, local_rank):
         result["prefill"] = {
             "stream_tokens_per_s": PREFILL_MS[1] / (PREFILL_MS[0] / 1e3),
             "input_gbs": PREFILL_MS[1] * cfgd["D"] * 8 / (PREFILL_MS[0] / 1e3) / 1e9,
-            "ms": PREFILL_MS[0], "chunk_kernel": "key_groups + value_tokens + copy_rows",
+            "ms": PREFILL_MS[0], "chunk_kernel": "key_groups + value_tokens + copy_rows2",
         }
     if mode == "seqshard" and rank == 0:
         result["key_flush"] = key_flush_microbench(K, cfgd, stream)

@@ -397,24 +397,37 @@ int32_t append_device(KvState &s, const float *dk, const float *dv, uint64_t seq
                                            (int)s.vhead, stream),
                  "append");
     } else {
-        // Keys: flush every complete R-block of [residual ++ input], then keep
-        // the tail in the residual (cache.rs:382-405).
+        // Keys: flush every complete R-block of [residual ++ input]
+        // (cache.rs:382-405).  Values, seq >= R: quantize the window and
+        // input[0, seq-R) (cache.rs:434-454).  (One fused launch of both ran
+        // slower than the two: each already fills the SMs.)
         CUDA_TRY(kivi::launch_key_groups(g, s.st, n, s.st.kres, (int)s.kres_len, dk, (int64_t)seq,
                                          (int64_t)(nblk * R / G), (int64_t)(s.kq / G), stream),
                  "append keys");
-        const uint64_t tail = ktotal % R;
-        CUDA_TRY(kivi::launch_copy_rows(s.st.kres, (int64_t)R, 0, 0, (int64_t)R, dk, (int64_t)seq,
-                                        (int64_t)(seq - tail), (int64_t)tail, n, (int)s.D, stream),
-                 "append keys tail");
-        // Values, seq >= R: quantize the window and input[0, seq-R), keep the
-        // last R input rows (cache.rs:434-454).
         CUDA_TRY(kivi::launch_value_tokens(g, s.st, n, (int)s.vres_len, (int)s.vhead, dv,
                                            (int64_t)seq, 0, (int64_t)(s.vres_len + seq - R),
                                            (int64_t)s.vq, stream),
                  "append values");
-        CUDA_TRY(kivi::launch_copy_rows(s.st.vres, (int64_t)R, 0, 0, (int64_t)R, dv, (int64_t)seq,
-                                        (int64_t)(seq - R), (int64_t)R, n, (int)s.D, stream),
-                 "append window");
+        // Then the key tail into the residual and the last R input rows into
+        // the window (after the quantization read the old ones).
+        const uint64_t tail = ktotal % R;
+        const kivi::RowCopy kc{s.st.kres, (int64_t)R, 0, 0, (int64_t)R, dk, (int64_t)seq,
+                               (int64_t)(seq - tail), (int64_t)tail};
+        const kivi::RowCopy vc{s.st.vres, (int64_t)R, 0, 0, (int64_t)R, dv, (int64_t)seq,
+                               (int64_t)(seq - R), (int64_t)R};
+        const bool vec = s.D % 4 == 0 && ((uintptr_t)dk & 15u) == 0 && ((uintptr_t)dv & 15u) == 0;
+        if (vec) {
+            CUDA_TRY(kivi::launch_copy_rows2(kc, vc, n, (int)s.D, stream), "append tails");
+        } else {
+            CUDA_TRY(kivi::launch_copy_rows(kc.dst, kc.dst_stream_rows, kc.dst_head, kc.dst_off,
+                                            kc.ring, kc.src, kc.src_seq, kc.src_off, kc.count, n,
+                                            (int)s.D, stream),
+                     "append keys tail");
+            CUDA_TRY(kivi::launch_copy_rows(vc.dst, vc.dst_stream_rows, vc.dst_head, vc.dst_off,
+                                            vc.ring, vc.src, vc.src_seq, vc.src_off, vc.count, n,
+                                            (int)s.D, stream),
+                     "append window");
+        }
     }
     s.kq = kq_new;
     s.kres_len = ktotal % R;

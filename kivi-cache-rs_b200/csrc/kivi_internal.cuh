@@ -129,6 +129,16 @@ cudaError_t launch_key_groups(const Geom &g, const Store &st, int n, const float
 cudaError_t launch_value_tokens(const Geom &g, const Store &st, int n, int nwin, int vhead,
                                 const float *in, int64_t in_seq, int64_t in_off, int64_t ntok,
                                 int64_t out_tok0, cudaStream_t s);
+// One row copy: input rows [src_off, src_off+count) of every stream into
+// dst slot (dst_head + dst_off + i) % ring.
+struct RowCopy {
+    float *dst;
+    int64_t dst_stream_rows, dst_head, dst_off, ring;
+    const float *src;
+    int64_t src_seq, src_off, count;
+};
+// Two row copies in one launch (rows of D floats, D % 4 == 0, 16-byte aligned).
+cudaError_t launch_copy_rows2(const RowCopy &j0, const RowCopy &j1, int n, int D, cudaStream_t s);
 // Copy input rows [src_off, src_off+count) of every stream into ring/linear rows:
 // dst slot = (dst_head + dst_off + i) % ring (ring = R for the value window, or
 // a huge number for a linear buffer).

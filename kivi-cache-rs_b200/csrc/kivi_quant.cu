@@ -304,6 +304,20 @@ __global__ void copy_rows_kernel(float *dst, int64_t dst_stream_rows, int64_t ds
     dst[((int64_t)s * dst_stream_rows + slot) * D + d] = src[((int64_t)s * src_seq + src_off + i) * D + d];
 }
 
+// Two row copies in one launch (grid.z = job), float4 at a time (rows of D
+// floats, D % 4 == 0, 16-byte aligned buffers).
+__global__ void copy_rows2_kernel(RowCopy j0, RowCopy j1, int D) {
+    const RowCopy &j = blockIdx.z ? j1 : j0;
+    const int s = blockIdx.y;
+    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; // float4 index
+    const int D4 = D / 4;
+    if (e >= j.count * D4) return;
+    const int64_t i = e / D4, d4 = e - i * D4;
+    const int64_t slot = (j.dst_head + j.dst_off + i) % j.ring;
+    reinterpret_cast<float4 *>(j.dst)[((int64_t)s * j.dst_stream_rows + slot) * D4 + d4] =
+        reinterpret_cast<const float4 *>(j.src)[((int64_t)s * j.src_seq + j.src_off + i) * D4 + d4];
+}
+
 __global__ void suffix_append_kernel(const SuffixAppend a, const float *k, const float *v,
                                      int nstreams, int64_t seq, int D) {
     const int z = blockIdx.z, s = blockIdx.y;
@@ -400,6 +414,15 @@ cudaError_t launch_value_tokens(const Geom &g, const Store &st, int n, int nwin,
     ProfScope prof("value_tokens", s);
     value_tokens_kernel<<<dim3(blocks_for(ntok * g.nch, 128), n), 128, 0, s>>>(
         g, st, nwin, vhead, in, in_seq, in_off, ntok, out_tok0);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_copy_rows2(const RowCopy &j0, const RowCopy &j1, int n, int D, cudaStream_t s) {
+    const int64_t cnt = j0.count > j1.count ? j0.count : j1.count;
+    if (n <= 0 || cnt <= 0) return cudaSuccess;
+    ProfScope prof("copy_rows", s);
+    copy_rows2_kernel<<<dim3(blocks_for(cnt * (D / 4), 256), n, 2), 256, 0, s>>>(j0, j1, D);
     count_launch();
     return cudaGetLastError();
 }
