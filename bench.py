@@ -417,7 +417,7 @@ class RagWorkload:
         del cache
         self.sessions = [self.prefix.session() for _ in range(S)]
         for s in self.sessions:
-            s.reserve(suffix + nsteps + nprof + 64)
+            s.reserve(suffix + nsteps + nprof + 256)  # + e2e warm-up and timed steps
             dk, dv = self.gen.tokens(B, H, suffix, D)
             torch.cuda.synchronize()
             s.append_dev(dk, dv, suffix, stream=stream)
