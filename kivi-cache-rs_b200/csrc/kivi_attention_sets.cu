@@ -34,14 +34,16 @@
 // p * 2^(15 - T) with the reference point moved only when a logit exceeds it
 // by T = 6 (exp2 units).  All factors are powers of two, undone exactly in fp32.
 //
-// Warp roles (480 threads): warps 0-3 softmax and epilogue (thread = row,
-// tensor-memory lanes 0..127); eight converter warps dequantize each landed
-// tile into the fp16 hi/lo key tile (warps 4, 6, 7, 12) or value tile (8, 10,
-// 11, 14); warp 9 lane 0 streams the packed tiles in with bulk async copies
-// (cp.async.bulk, into this CTA only); warp 5 issues the MMAs (the whole warp
-// runs the loop, one elected lane issues) in the order QK(0), QK(1), PV(0),
-// QK(2), PV(1), ...; warp 13 idles.  Key tiles (three in flight) are released
-// when their QK^T completes, value tiles (three in flight) when their PV
+// Warp roles (608 threads): warps 0-3 and 15-18 softmax and epilogue (thread =
+// row, tensor-memory lanes 32 (w % 4) ..; warps 0-3 take tokens 0-31 of each
+// tile, warps 15-18 tokens 32-63, a pair sharing its row maxima); eight
+// converter warps dequantize each landed tile into the fp16 hi/lo key tile
+// (warps 4, 6, 7, 12) or value tile (8, 10, 11, 14); warp 9 lane 0 streams the
+// packed tiles in with bulk async copies (cp.async.bulk, into this CTA only);
+// warp 5 issues the MMAs (the whole warp runs the loop, one elected lane
+// issues) in the order QK(0), QK(1), PV(0), QK(2), PV(1), ...; warp 13 idles.
+// Key tiles (three in flight) are released when their QK^T completes, value
+// tiles (three in flight) when their PV
 // completes, so the converters run ahead of the tensor pipe.  Operand tiles use the canonical
 // no-swizzle layouts: K-major addr(r, k) = (r/8)*SBO + (k/8)*128 + (r%8)*16 +
 // (k%8)*2, MN-major addr(k, n) = (n/8)*SBO + (k/8)*128 + (k%8)*16 + (n%8)*2.
@@ -71,7 +73,12 @@ constexpr int kConvWarps = 8;  // 4 key converters, 4 value converters
 constexpr int kConvHalf = kConvWarps / 2;
 constexpr int kMmaWarp = 5;
 constexpr int kProdWarp = 9;
-constexpr int kSetThreads = 15 * 32; // warp 13 idles
+// Softmax runs on two warps per tensor-memory lane quarter: warps 0-3 take
+// tokens 0-31 of each 64-token tile, warps 15-18 (lane quarter w % 4) tokens
+// 32-63; a pair exchanges its partial row maxima through shared memory.
+constexpr int kSoftB0 = 15;
+constexpr int kSetThreads = 19 * 32; // warp 13 idles
+constexpr int kMiscBytes = 4096;     // barriers, bounds, the softmax exchange
 // converter role of warp w: 0..3 key converter index, 4..7 value converter
 // index + 4, -1 for the other roles
 __host__ __device__ constexpr int conv_role(int w) {
@@ -121,9 +128,9 @@ template <int BITS> struct SetGeom {
     static constexpr int STAGE = 2 * GROUP;
     static constexpr int OKP = 2 * KC, OVC = OKP + 2 * KP, OVP = OVC + 2 * VC;
     // packed-tile stages in flight: as many as shared memory leaves room for, up to 8
-    static constexpr int NS = std::min(KIVI_SETS_STAGES2, (232448 - 1024 - kStages) / STAGE);
+    static constexpr int NS = std::min(KIVI_SETS_STAGES2, (232448 - kMiscBytes - kStages) / STAGE);
     static constexpr int MISC = kStages + NS * STAGE;
-    static constexpr int SMEM = MISC + 1024;
+    static constexpr int SMEM = MISC + kMiscBytes;
     static_assert(NS >= 2, "packed-group stages");
     static_assert(SMEM <= 232448, "shared memory per block");
 };
@@ -397,9 +404,13 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
     uint64_t *p_ready = s_full + kS;                            // [kS]  S read, P written
     uint64_t *pv_done = p_ready + kS;                           // [kS]  PV of the tile done
     uint64_t *drain = pv_done + kS;                             // [1]
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(drain + 1);
+    uint64_t *pair = drain + 1;                                 // [4]  softmax pair exchange
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(pair + 4);
     int *kexp = reinterpret_cast<int *>(tslot + 1);             // [128]
     int *vexp = kexp + kD;                                      // [4]
+    float *xmax = reinterpret_cast<float *>(vexp + 4);          // [2 tiles][2 halves][128]
+    float *lsum = xmax + 2 * 2 * 128;                           // [128]
+    static_assert(8 * 32 + 4 + 4 * 132 + 4 * (4 * 128 + 128) <= kMiscBytes, "misc");
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t s = blockIdx.y;
@@ -428,10 +439,11 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
         }
         for (int i = 0; i < kS; ++i) {
             bar_init(&s_full[i], 1);
-            bar_init(&p_ready[i], kSoftWarps);
+            bar_init(&p_ready[i], 2 * kSoftWarps);
             bar_init(&pv_done[i], 1);
         }
         bar_init(drain, 1);
+        for (int i = 0; i < 4; ++i) bar_init(&pair[i], 2);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
@@ -487,11 +499,14 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
         if (lane == 0) rowexp[r] = er;
     }
     __syncthreads();
-    float rowfac = 0.0f; // 2^(e_row - 28) * scale * log2(e), softmax threads only
+    // 2^(e_row - 28) * scale * log2(e) of this softmax thread's row (read here:
+    // the staging area belongs to the value converters once the roles start)
+    float rowfac = 0.0f;
+    if (warp < kSoftWarps || warp >= kSoftB0)
+        rowfac = exp2i_(rowexp[32 * (warp & 3) + lane] - 28) * (a.scale * 1.4426950408889634f);
     if (warp < kSoftWarps) {
         const int m = threadIdx.x;
         const uint32_t lane_base = tbase + ((uint32_t)(32 * warp) << 16);
-        rowfac = exp2i_(rowexp[m] - 28) * (a.scale * 1.4426950408889634f);
         const uint4 *row = reinterpret_cast<const uint4 *>(qstage + m * (kQRow / 4));
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) { // 32 channels -> 16 columns of hi and of lo
@@ -731,10 +746,17 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
                 bar_arrive(&empty[st]);
             }
         }
-    } else if (warp < kSoftWarps) {
+    } else if (warp < kSoftWarps || warp >= kSoftB0) {
         // ------------------------------------------------------------ softmax (thread = row)
-        const int m = threadIdx.x;
-        const uint32_t lane_base = tbase + ((uint32_t)(32 * warp) << 16);
+        // Half h of the tile's 64 tokens: S columns 32h.. and 64 + 32h..; the
+        // pair (warp q, warp kSoftB0 + ...) of lane quarter q shares the row max
+        // through xmax (double-buffered by tile) and the pair mbarrier (one
+        // phase per tile, one more for the row sums), and each warp rescales and
+        // writes out its half of O's columns.
+        const int h = warp < kSoftWarps ? 0 : 1;
+        const int q = warp & 3;
+        const int m = 32 * q + lane;
+        const uint32_t lane_base = tbase + ((uint32_t)(32 * q) << 16);
         float mref = -INFINITY, l = 0.0f;
         bool ok = true;
         for (int j = 0; ok && j < nt; ++j) {
@@ -746,32 +768,44 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
             }
             tc_fence_after();
             // S = (Q_hi K_hi + Q_lo K_hi) + Q_hi K_lo: columns i and 64 + i
-            float x[64];
+            float x[32];
             const uint32_t srow = lane_base + kSc + 128 * bs;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 2; ++c) {
                 float t[16];
-                tmem_ld16_nw(srow + 16 * c, x + 16 * c);
-                tmem_ld16_nw(srow + 64 + 16 * c, t);
+                tmem_ld16_nw(srow + 32 * h + 16 * c, x + 16 * c);
+                tmem_ld16_nw(srow + 64 + 32 * h + 16 * c, t);
                 tmem_wait_ld();
 #pragma unroll
                 for (int i = 0; i < 16; i += 2) add2(x[16 * c + i], x[16 * c + i + 1], t[i], t[i + 1]);
             }
-            if (!two) { // the CTA's last odd tile holds one group
+            if (h == 1 && !two) { // the CTA's last odd tile holds one group
 #pragma unroll
-                for (int i = 32; i < 64; ++i) x[i] = -INFINITY;
+                for (int i = 0; i < 32; ++i) x[i] = -INFINITY;
             }
             // logits are x rowfac (exp2 units); the max is taken on the raw scores
             // (rowfac > 0 and rounding is monotone, so max(x) rowfac = max(x rowfac))
             float m4[4] = {x[0], x[1], x[2], x[3]};
 #pragma unroll
-            for (int i = 4; i < 64; i += 8) {
+            for (int i = 4; i < 32; i += 8) {
                 m4[0] = max3(m4[0], x[i], x[i + 1]);
                 m4[1] = max3(m4[1], x[i + 2], x[i + 3]);
                 m4[2] = max3(m4[2], x[i + 4], x[i + 5]);
                 m4[3] = max3(m4[3], x[i + 6], x[i + 7]);
             }
-            float mx = fmaxf(max3(m4[0], m4[1], m4[2]), m4[3]) * rowfac;
+            float* xm = xmax + (j & 1) * 256;
+            xm[h * 128 + m] = fmaxf(max3(m4[0], m4[1], m4[2]), m4[3]);
+            // both halves' S reads and maxima are done after this phase (the
+            // P writes below overwrite S columns 0..63 of both halves)
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) bar_arrive(&pair[q]);
+            if (!warp_wait(&pair[q], j & 1, 128u)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float mx = fmaxf(xm[m], xm[128 + m]) * rowfac; // same order in both halves
             const bool need = mx > mref + kLazy2;
             if (__any_sync(0xffffffffu, need)) {
                 const float nref = need ? mx : mref;
@@ -779,18 +813,18 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
                 mref = nref;
                 l *= alpha;
                 if (j >= 1) {
-                    // O holds tiles < j: wait for PV(j-1), rescale this warp's rows
+                    // O holds tiles < j: wait for PV(j-1), rescale this half's columns
                     if (!warp_wait(&pv_done[(j - 1) % kS], ((j - 1) / kS) & 1, 128u)) {
                         ok = false;
                     } else {
                         tc_fence_after();
 #pragma unroll 1
-                        for (int c4 = 0; c4 < 4; ++c4) {
+                        for (int c4 = 0; c4 < 2; ++c4) {
                             float o[32];
-                            tmem_ld32(lane_base + kO + 32 * c4, o);
+                            tmem_ld32(lane_base + kO + 64 * h + 32 * c4, o);
 #pragma unroll
                             for (int i = 0; i < 32; ++i) o[i] *= alpha;
-                            tmem_st32(lane_base + kO + 32 * c4, o);
+                            tmem_st32(lane_base + kO + 64 * h + 32 * c4, o);
                         }
                         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                     }
@@ -802,7 +836,7 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
             const float off = (float)(15 - kLazyBits) - mref;
             float ps0 = 0.0f, ps1 = 0.0f, ps2 = 0.0f, ps3 = 0.0f;
 #pragma unroll
-            for (int i = 0; i < 64; i += 4) {
+            for (int i = 0; i < 32; i += 4) {
                 fma2s(x[i], x[i + 1], rowfac, off);
                 fma2s(x[i + 2], x[i + 3], rowfac, off);
                 x[i] = ex2_approx(x[i]);
@@ -813,16 +847,14 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
                 add2(ps2, ps3, x[i + 2], x[i + 3]);
             }
             l += ((ps0 + ps1) + (ps2 + ps3)) * (1.0f / kPScale);
-            // P(j) overwrites the first half of S[bs] (read above); QK(j + kS)
-            // rewrites S[bs] only after PV(j) in issue order
+            // P(j) overwrites the first half of S[bs] (both halves have read it,
+            // see the pair phase above): tokens 32h.. -> hi columns 16h.., lo 32 + 16h..
+            // QK(j + kS) rewrites S[bs] only after PV(j) in issue order
             uint32_t hi[16], lo[16];
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-#pragma unroll
-                for (int q = 0; q < 16; ++q) split_pair(x[32 * hh + 2 * q], x[32 * hh + 2 * q + 1], hi[q], lo[q]);
-                tmem_st16(srow + 16 * hh, hi);
-                tmem_st16(srow + 32 + 16 * hh, lo);
-            }
+            for (int qq = 0; qq < 16; ++qq) split_pair(x[2 * qq], x[2 * qq + 1], hi[qq], lo[qq]);
+            tmem_st16(srow + 16 * h, hi);
+            tmem_st16(srow + 32 + 16 * h, lo);
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tc_fence_before();
             __syncwarp();
@@ -832,16 +864,21 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
         bool have = ok && nt > 0;
         if (have && !warp_wait(&pv_done[(nt - 1) % kS], ((nt - 1) / kS) & 1, 128u)) have = false;
         tc_fence_after();
+        // row sums: half 1 hands its l to half 0 (one more pair phase)
+        if (h == 1) lsum[m] = l;
+        __syncwarp();
+        if (lane == 0) bar_arrive(&pair[q]);
+        const bool lpair = warp_wait(&pair[q], nt & 1, 128u);
         const bool mine = m < rows_valid;
         float *po = nullptr, *pml = nullptr;
         if (mine) {
-            const int z = z0 + m / a.GQ, h = m % a.GQ;
-            const int64_t row = (int64_t)z * a.rows_per_set + (int64_t)b * a.Hq + kvh * a.GQ + h;
+            const int z = z0 + m / a.GQ, hq = m % a.GQ;
+            const int64_t row = (int64_t)z * a.rows_per_set + (int64_t)b * a.Hq + kvh * a.GQ + hq;
             po = a.part_o + (row * a.parts + chunk) * kD;
             pml = a.part_ml + (row * a.parts + chunk) * 2;
         }
 #pragma unroll 1
-        for (int c4 = 0; c4 < 4; ++c4) {
+        for (int c4 = 2 * h; c4 < 2 * h + 2; ++c4) {
             // channel group c4: O = sum p v = O' 2^(F_cg - 14) 2^-(15 - kLazyBits)
             float o[32];
             if (have) tmem_ld32(lane_base + kO + 32 * c4, o); // warp-collective
@@ -854,9 +891,10 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
                                   : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             }
         }
-        if (mine) {
-            pml[0] = have ? mref * 0.6931471805599453f : -INFINITY;
-            pml[1] = have ? l : 0.0f;
+        if (mine && h == 0) {
+            const bool all = have && lpair;
+            pml[0] = all ? mref * 0.6931471805599453f : -INFINITY;
+            pml[1] = all ? l + lsum[m] : 0.0f;
         }
     }
     tc_fence_before();
