@@ -67,8 +67,9 @@ namespace {
 constexpr int kSoftWarps = 4;
 // Warp w runs on sub-partition w % 4.  Softmax warp w serves tensor-memory
 // lanes 32 (w % 4) ..; the MMA issuer shares its sub-partition only with
-// softmax warp 1, the producer and an idle warp, so the ALU-bound converters
-// (three, three and two on the other sub-partitions) do not take its issue slots.
+// softmax warps 1 and 17, the producer and an idle warp, so the ALU-bound
+// converters (three, three and two on the other sub-partitions) do not take
+// its issue slots.
 constexpr int kConvWarps = 8;  // 4 key converters, 4 value converters
 constexpr int kConvHalf = kConvWarps / 2;
 constexpr int kMmaWarp = 5;
@@ -92,12 +93,14 @@ constexpr int kD = 128;
 constexpr int kTok = 32;                           // tokens per group = per S tile
 constexpr long long kWait = 2000000000LL;          // ~1 s at B200 clocks
 constexpr int kTile = 64;   // tokens per S tile (two groups): QK^T runs at N = 64
-#ifndef KIVI_SETS_KBUF
-#define KIVI_SETS_KBUF 3
-#endif
-constexpr int kK = KIVI_SETS_KBUF; // key operand tiles in flight (free once QK^T is done)
-constexpr int kV = 3;              // value operand tiles in flight (free once PV is done)
-constexpr int kS = 2;              // S / P tensor-memory buffers
+// Tile j uses slot j % 3 of the key-operand ring, the value-operand ring and
+// the S / P buffers alike, so one commit after QK^T(j) both publishes S(j)
+// and frees key slot j % 3, and one commit after PV(j) both marks O current
+// and frees value slot j % 3 (two commits per tile rather than four).
+constexpr int kK = 3; // key operand tiles in flight (free once QK^T is done)
+constexpr int kV = 3; // value operand tiles in flight (free once PV is done)
+constexpr int kS = 3; // S / P tensor-memory buffers
+static_assert(kK == kS && kV == kS, "the free signals share s_full / pv_done");
 #ifndef KIVI_SETS_LAZY
 #define KIVI_SETS_LAZY 6
 #endif
@@ -105,11 +108,10 @@ constexpr int kLazyBits = KIVI_SETS_LAZY;          // log2 headroom of the softm
 constexpr float kLazy2 = (float)kLazyBits;
 constexpr float kPScale = (float)(1 << (15 - kLazyBits)); // p * kPScale <= 2^15
 // tensor-memory columns (fp32 words; fp16 operands two per column):
-// S[b] 128b .. 128b + 127 (Q_hi K_hi + Q_lo K_hi in the first 64, Q_hi K_lo in
-// the second 64; P[b] overwrites the first 64 once softmax has read them: hi 32
-// columns, then lo 32), Q_hi 256..319, Q_lo 320..383, O 384..511
+// S[b] 64b .. 64b + 63 (P[b] overwrites it once softmax has read it: hi 32
+// columns, then lo 32), Q_hi 192..255, Q_lo 256..319, O 320..447
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kSc = 0, kQH = 256, kQL = 320, kO = 384;
+constexpr uint32_t kSc = 0, kQH = 192, kQL = 256, kO = 320;
 
 // shared-memory map (bytes): per key/value tile hi and lo parts of 16 KB each
 constexpr int kKbuf = 0;                            // [kK] x (hi, lo): 128 channels x 64 tokens
@@ -225,22 +227,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *v) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// 16 consecutive fp32 columns (no wait: the caller issues tcgen05.wait::ld).
-__device__ __forceinline__ void tmem_ld16_nw(uint32_t taddr, float *v) {
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-        "%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-          "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float *v) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
@@ -327,18 +313,37 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *r) {
         : "memory");
 }
 
-// MMA with A in tensor memory (lane = row, column j = fp16 pair (2j, 2j+1)),
-// issued by one elected lane of a converged warp.  The whole warp runs the
-// issue loop: a single-lane loop inside a divergent branch issues several
-// times slower once the other warps of its sub-partition keep the issue
-// slots busy.
-__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t id,
-                                        uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(b), "r"(id), "r"(acc));
+// One K sweep of MMAs with A in tensor memory (lane = row, column j = fp16
+// pair (2j, 2j+1)): MMA i reads A columns a0 + 8 i and the B descriptor
+// b0 + 16 i (16 K elements further in both), the first one accumulating iff
+// acc0 != 0.  The whole warp runs it and one elected lane issues: one
+// elect.sync per sweep in a single asm block keeps tcgen05.mma at the tensor
+// pipe's rate even while the other warps of the sub-partition keep its issue
+// slots busy (one elect per MMA, or a single-lane loop in a divergent branch,
+// issues a third to four times slower then).
+#define KIVI_SWEEP_HEAD                                                                              \
+    "{\n\t.reg .pred p, e, t;\n\t.reg .b32 a;\n\t.reg .b64 b;\n\telect.sync _|e, 0xffffffff;\n\t"   \
+    "setp.ne.b32 p, %4, 0;\n\tsetp.ne.b32 t, %5, 0;\n\tmov.b32 a, %1;\n\tmov.b64 b, %2;\n\t"        \
+    "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, p;\n\t"
+#define KIVI_SWEEP_STEP                                                                              \
+    "add.u32 a, a, 8;\n\tadd.u64 b, b, 16;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, t;\n\t"
+template <int N>
+__device__ __forceinline__ void umma_sweep(uint32_t d_tmem, uint32_t a0, uint64_t b0, uint32_t id,
+                                           uint32_t acc0) {
+    static_assert(N == 2 || N == 4 || N == 8, "sweep length");
+    if constexpr (N == 8)
+        asm volatile(KIVI_SWEEP_HEAD KIVI_SWEEP_STEP KIVI_SWEEP_STEP KIVI_SWEEP_STEP KIVI_SWEEP_STEP
+                         KIVI_SWEEP_STEP KIVI_SWEEP_STEP KIVI_SWEEP_STEP "}" ::"r"(d_tmem),
+                     "r"(a0), "l"(b0), "r"(id), "r"(acc0), "r"(1u));
+    else if constexpr (N == 4)
+        asm volatile(KIVI_SWEEP_HEAD KIVI_SWEEP_STEP KIVI_SWEEP_STEP KIVI_SWEEP_STEP "}" ::"r"(d_tmem),
+                     "r"(a0), "l"(b0), "r"(id), "r"(acc0), "r"(1u));
+    else
+        asm volatile(KIVI_SWEEP_HEAD KIVI_SWEEP_STEP "}" ::"r"(d_tmem), "r"(a0), "l"(b0), "r"(id),
+                     "r"(acc0), "r"(1u));
 }
+#undef KIVI_SWEEP_HEAD
+#undef KIVI_SWEEP_STEP
 
 // tcgen05.commit by the same elected lane (elect.sync picks the same leader for a full mask)
 __device__ __forceinline__ void umma_commit_e(uint64_t *b) {
@@ -397,12 +402,10 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
     uint64_t *full = reinterpret_cast<uint64_t *>(misc);        // [NS]  packed group landed
     uint64_t *empty = full + NS;                                // [NS]  packed group consumed
     uint64_t *k_ready = empty + NS;                             // [kK]  key tile written
-    uint64_t *k_free = k_ready + kK;                            // [kK]  QK^T over it done
-    uint64_t *v_ready = k_free + kK;                            // [kV]  value tile written
-    uint64_t *v_free = v_ready + kV;                            // [kV]  PV over it done
-    uint64_t *s_full = v_free + kV;                             // [kS]  S computed
+    uint64_t *v_ready = k_ready + kK;                           // [kV]  value tile written
+    uint64_t *s_full = v_ready + kV;                            // [kS]  S computed, key slot free
     uint64_t *p_ready = s_full + kS;                            // [kS]  S read, P written
-    uint64_t *pv_done = p_ready + kS;                           // [kS]  PV of the tile done
+    uint64_t *pv_done = p_ready + kS;                           // [kS]  PV done, value slot free
     uint64_t *drain = pv_done + kS;                             // [1]
     uint64_t *pair = drain + 1;                                 // [4]  softmax pair exchange
     uint32_t *tslot = reinterpret_cast<uint32_t *>(pair + 4);
@@ -429,14 +432,8 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
             bar_init(&full[i], 1);
             bar_init(&empty[i], 2 * kConvHalf);
         }
-        for (int i = 0; i < kK; ++i) {
-            bar_init(&k_ready[i], kConvHalf);
-            bar_init(&k_free[i], 1);
-        }
-        for (int i = 0; i < kV; ++i) {
-            bar_init(&v_ready[i], kConvHalf);
-            bar_init(&v_free[i], 1);
-        }
+        for (int i = 0; i < kK; ++i) bar_init(&k_ready[i], kConvHalf);
+        for (int i = 0; i < kV; ++i) bar_init(&v_ready[i], kConvHalf);
         for (int i = 0; i < kS; ++i) {
             bar_init(&s_full[i], 1);
             bar_init(&p_ready[i], 2 * kSoftWarps);
@@ -558,66 +555,67 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
         }
     } else if (warp == kMmaWarp) {
         // ------------------------------------------------------------ MMA issuer (whole warp)
-        {
-            constexpr uint32_t id_qk2 = idesc_f16(128, 2 * kTile, 1); // B = [K_hi | K_lo]
-            constexpr uint32_t id_qk = idesc_f16(128, kTile, 1);      // B = K_hi
-            constexpr uint32_t id_pv = idesc_f16(128, kD, 1);
-            // descriptors of the shared-memory tiles: the start-address field holds
-            // address / 16, so a K step of 16 elements (256 bytes) is +16 and buffer
-            // i of a ring is the first one's + i * 32768 / 16
-            const uint64_t dk0 = sdesc(su32(sm + kKbuf), 128, 2048);
-            const uint64_t dv0 = sdesc(su32(sm + kVbuf), 128, 1024);
-            bool ok = true;
-            auto pv = [&](int j) {
-                // O += P V over tile j (K = 32 tokens per group present)
-                const int bj = j % kS, bv = j % kV;
-                if (!warp_wait(&p_ready[bj], (j / kS) & 1, 32u) ||
-                    !warp_wait(&v_ready[bv], (j / kV) & 1, 32u))
-                    return false;
-                tc_fence_after();
-                const int ksteps = (2 * j + 1 < ng) ? 4 : 2;
-                const uint32_t ph = tbase + kSc + 128 * bj, pl = ph + 32;
-                const uint64_t vh = dv0 + (uint64_t)bv * 2048u, vl = vh + 1024u;
-#pragma unroll 1
-                for (int ks = 0; ks < ksteps; ++ks) {
-                    umma_ts(tbase + kO, ph + 8 * ks, vh + 16 * ks, id_pv, (j > 0 || ks > 0) ? 1u : 0u);
-                    umma_ts(tbase + kO, pl + 8 * ks, vh + 16 * ks, id_pv, 1u);
-                    umma_ts(tbase + kO, ph + 8 * ks, vl + 16 * ks, id_pv, 1u);
-                }
-                umma_commit_e(&pv_done[bj]);
-                umma_commit_e(&v_free[bv]);
-                return true;
-            };
-            // Issue order QK(0), QK(1), PV(0), QK(2), PV(1), ...: softmax of tile j
-            // overlaps PV(j - 1) and QK(j + 1).  S[bs] / P[bs] are free for tile j:
-            // softmax(j - kS) read S before p_ready(j - kS), which PV(j - kS) (issued
-            // earlier) waited for, and P[bs] is rewritten only after QK(j) completes,
-            // which in issue order follows PV(j - kS).
-            for (int j = 0; ok && j < nt; ++j) {
-                const int bk = j % kK, bs = j % kS;
-                if (!warp_wait(&k_ready[bk], (j / kK) & 1, 32u)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                // the key tile's lo half follows its hi half in the token (N)
-                // direction, so one N = 128 MMA forms Q_hi K_hi and Q_hi K_lo
-                const uint32_t sacc = tbase + kSc + 128 * bs;
-                const uint64_t kh = dk0 + (uint64_t)bk * 2048u;
-#pragma unroll
-                for (int ks = 0; ks < 8; ++ks)
-                    umma_ts(sacc, tbase + kQH + 8 * ks, kh + 16 * ks, id_qk2, ks > 0 ? 1u : 0u);
-#pragma unroll
-                for (int ks = 0; ks < 8; ++ks) umma_ts(sacc, tbase + kQL + 8 * ks, kh + 16 * ks, id_qk, 1u);
-                umma_commit_e(&s_full[bs]);
-                umma_commit_e(&k_free[bk]);
-                if (j >= 1 && !pv(j - 1)) ok = false;
+        constexpr uint32_t id_qk = idesc_f16(128, kTile, 1);
+        constexpr uint32_t id_pv = idesc_f16(128, kD, 1);
+        // descriptors of the shared-memory tiles: the start-address field holds
+        // address / 16, so a K step of 16 elements (256 bytes) is +16 and buffer
+        // i of a ring is the first one's + i * 32768 / 16
+        const uint64_t dk0 = sdesc(su32(sm + kKbuf), 128, 2048);
+        const uint64_t dv0 = sdesc(su32(sm + kVbuf), 128, 1024);
+        bool ok = true;
+        auto pv = [&](int j) {
+            // O += P V over tile j, once softmax has written P(j) and the value
+            // tile is in place
+            const int bj = j % kS, bv = j % kV;
+            if (!warp_wait(&p_ready[bj], (j / kS) & 1, 32u) ||
+                !warp_wait(&v_ready[bv], (j / kV) & 1, 32u))
+                return false;
+            tc_fence_after();
+            // O += P_hi V_hi + P_lo V_hi + P_hi V_lo, one sweep over the
+            // tile's tokens each (4 K steps, 2 for a one-group tile)
+            const uint32_t ph = tbase + kSc + 64 * bj, pl = ph + 32;
+            const uint64_t vh = dv0 + (uint64_t)bv * 2048u, vl = vh + 1024u;
+            const uint32_t o = tbase + kO;
+            if (2 * j + 1 < ng) {
+                umma_sweep<4>(o, ph, vh, id_pv, j > 0 ? 1u : 0u);
+                umma_sweep<4>(o, pl, vh, id_pv, 1u);
+                umma_sweep<4>(o, ph, vl, id_pv, 1u);
+            } else {
+                umma_sweep<2>(o, ph, vh, id_pv, j > 0 ? 1u : 0u);
+                umma_sweep<2>(o, pl, vh, id_pv, 1u);
+                umma_sweep<2>(o, ph, vl, id_pv, 1u);
             }
-            if (ok && nt >= 1) pv(nt - 1);
-            // every MMA of this CTA complete before tensor memory is released
-            umma_commit_e(drain);
-            warp_wait(drain, 0, 32u);
+            umma_commit_e(&pv_done[bj]); // also frees value slot bv == bj
+            return true;
+        };
+        // Issue order QK(0), QK(1), QK(2), PV(0), QK(3), PV(1), ...: softmax
+        // of tile j finds S(j) computed (QK(j) went out two tiles earlier)
+        // and overlaps the MMAs of its neighbours.  S[bs] / P[bs] are free
+        // for tile j: softmax(j - kS) read S before p_ready(j - kS), which
+        // PV(j - kS) (issued earlier) waited for, and P[bs] is rewritten only
+        // after QK(j) completes, which in issue order follows PV(j - kS).
+        for (int j = 0; ok && j < nt; ++j) {
+            const int bk = j % kK, bs = j % kS;
+            if (!warp_wait(&k_ready[bk], (j / kK) & 1, 32u)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            // S = Q_hi K_hi + Q_lo K_hi + Q_hi K_lo, N = 64 tokens; the key
+            // tile's lo half starts 16 KB after its hi half
+            const uint32_t sacc = tbase + kSc + 64 * bs;
+            const uint64_t kh = dk0 + (uint64_t)bk * 2048u, kl = kh + 1024u;
+            umma_sweep<8>(sacc, tbase + kQH, kh, id_qk, 0u);
+            umma_sweep<8>(sacc, tbase + kQL, kh, id_qk, 1u);
+            umma_sweep<8>(sacc, tbase + kQH, kl, id_qk, 1u);
+            umma_commit_e(&s_full[bs]); // also frees key slot bk == bs
+            if (j >= 2 && !pv(j - 2)) ok = false;
         }
+        if (ok && nt >= 2) ok = pv(nt - 2);
+        if (ok && nt >= 1) pv(nt - 1);
+        // every MMA of this CTA complete before tensor memory is released
+        umma_commit_e(drain);
+        warp_wait(drain, 0, 32u);
     } else if (conv_role(warp) >= 0) {
         // ------------------------------------------------------------ converters
         // Warps 4-7 write key tiles, warps 8-11 value tiles; each half runs at its
@@ -644,7 +642,7 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
                 fac[r] = keys ? exp2i_(14 - kexp[8 * (u >> 5) + (u & 7)]) : exp2i_(14 - vexp[r]);
         }
         uint64_t *ready = keys ? k_ready : v_ready;
-        uint64_t *freed = keys ? k_free : v_free;
+        uint64_t *freed = keys ? s_full : pv_done; // QK^T / PV of the slot's last tile done
         const int nbuf = keys ? kK : kV;
         bool ok = true;
         for (int j = 0; ok && j < nt; ++j) {
@@ -748,7 +746,7 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
         }
     } else if (warp < kSoftWarps || warp >= kSoftB0) {
         // ------------------------------------------------------------ softmax (thread = row)
-        // Half h of the tile's 64 tokens: S columns 32h.. and 64 + 32h..; the
+        // Half h of the tile's 64 tokens: S columns 32h .. 32h + 31; the
         // pair (warp q, warp kSoftB0 + ...) of lane quarter q shares the row max
         // through xmax (double-buffered by tile) and the pair mbarrier (one
         // phase per tile, one more for the row sums), and each warp rescales and
@@ -767,18 +765,10 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
                 break;
             }
             tc_fence_after();
-            // S = (Q_hi K_hi + Q_lo K_hi) + Q_hi K_lo: columns i and 64 + i
+            // this half's 32 tokens of S[bs]
             float x[32];
-            const uint32_t srow = lane_base + kSc + 128 * bs;
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                float t[16];
-                tmem_ld16_nw(srow + 32 * h + 16 * c, x + 16 * c);
-                tmem_ld16_nw(srow + 64 + 32 * h + 16 * c, t);
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 16; i += 2) add2(x[16 * c + i], x[16 * c + i + 1], t[i], t[i + 1]);
-            }
+            const uint32_t srow = lane_base + kSc + 64 * bs;
+            tmem_ld32(srow + 32 * h, x);
             if (h == 1 && !two) { // the CTA's last odd tile holds one group
 #pragma unroll
                 for (int i = 0; i < 32; ++i) x[i] = -INFINITY;
@@ -847,8 +837,8 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
                 add2(ps2, ps3, x[i + 2], x[i + 3]);
             }
             l += ((ps0 + ps1) + (ps2 + ps3)) * (1.0f / kPScale);
-            // P(j) overwrites the first half of S[bs] (both halves have read it,
-            // see the pair phase above): tokens 32h.. -> hi columns 16h.., lo 32 + 16h..
+            // P(j) overwrites S[bs] (both halves have read it, see the pair phase
+            // above): tokens 32h.. -> hi columns 16h.., lo 32 + 16h..
             // QK(j + kS) rewrites S[bs] only after PV(j) in issue order
             uint32_t hi[16], lo[16];
 #pragma unroll
