@@ -103,9 +103,14 @@ class ClockSampler:
     """SM clock and clock-event reasons sampled by a separate `nvidia-smi -lms`
     process: NVML calls made from a thread of this process stalled its kernel
     launches for milliseconds at a time, which a short timed region cannot
-    absorb.  The sampler starts before the warm-up (its first sample marks
-    NVML ready), writes to a file, and the samples inside the timed window are
-    kept (the nearest ones when the window is shorter than the period)."""
+    absorb.  The sampler starts before the warm-up and is let settle: the
+    process still initialises after its first sample, and launches made then
+    stalled for tens of milliseconds (one 35 ms stall in a 40 ms timed region),
+    so start() returns once SETTLE_SAMPLES samples are on file.  Samples inside
+    the timed window are kept (the nearest ones when the window is shorter than
+    the period)."""
+
+    SETTLE_SAMPLES = 5
 
     REASONS = {
         0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
@@ -144,10 +149,14 @@ class ClockSampler:
             ["nvidia-smi", "-i", str(phys), f"--query-gpu={self.FIELDS}",
              "--format=csv,noheader,nounits", "-lms", str(self.period_ms)],
             stdout=self._f, stderr=subprocess.DEVNULL, env=env)
-        deadline = time.time() + 5.0
+        deadline = time.time() + 10.0
         while time.time() < deadline:
-            if os.path.getsize(self.path) > 0:
-                break
+            try:
+                with open(self.path) as f:
+                    if sum(1 for _ in f) >= self.SETTLE_SAMPLES:
+                        break
+            except OSError:
+                pass
             time.sleep(0.01)
         return self
 
