@@ -777,6 +777,7 @@ namespace kivi {
 namespace {
 
 constexpr int kTailThreads = 128;
+static_assert(kTailThreads == 128, "packed key tiles are staged one thread per channel (head_dim 128)");
 constexpr int kTailTokens = 32;
 constexpr int kTailPitch = 129;
 
@@ -846,11 +847,33 @@ __global__ void __launch_bounds__(kTailThreads) attn_tail_kernel(const TailArgs 
     const float *sk = suf.k ? suf.k + (int64_t)s * suf.cap * g.D : nullptr;
     const float *sv = suf.v ? suf.v + (int64_t)s * suf.cap * g.D : nullptr;
 
-    for (int e = threadIdx.x; e < a.GQ * 128; e += kTailThreads)
-        Qs[e] = a.q[(rbase + (int64_t)b * a.Hq + kvh * a.GQ) * 128 + e];
-    // Each thread stages 8 (token, 4 channels) units of K and V: every load is
-    // issued before the first shared-memory store, so one memory latency covers
-    // the tile (a warp's 32 lanes share one token: the source branch is uniform).
+    // Every global load of the tile (query rows, K, V) is issued before the
+    // first shared-memory store, so one memory latency covers the tile.
+    constexpr int kQPer = 8 * 128 / kTailThreads; // up to 8 query heads
+    float qreg[kQPer];
+#pragma unroll
+    for (int i = 0; i < kQPer; ++i) {
+        const int e = threadIdx.x + i * kTailThreads;
+        if (e < a.GQ * 128) qreg[i] = a.q[(rbase + (int64_t)b * a.Hq + kvh * a.GQ) * 128 + e];
+    }
+    // Keys: tiles start on group boundaries and the packed key region ends on
+    // one (kq is a multiple of the group), so a tile is either one whole packed
+    // key group or all fp32.  A packed group is read channel-major, one thread
+    // per channel: its code words and (scale, zero) are contiguous across the
+    // warp (four wavefronts per warp instead of eight per load per token).
+    constexpr int IPC = 32 * BITS / 32, TPW = 32 / BITS;
+    constexpr uint32_t MASK = (1u << BITS) - 1u;
+    const bool kpacked = nt == kTailTokens && t0 + kTailTokens <= a.kq && (t0 & 31) == 0;
+    uint32_t kwd[IPC];
+    float2 kpd = make_float2(0.f, 0.f);
+    if (kpacked) {
+        const int64_t gi = (t0 >> 5) * 128 + threadIdx.x; // (group, channel) of this thread
+#pragma unroll
+        for (int i = 0; i < IPC; ++i) kwd[i] = kc[gi * IPC + i];
+        kpd = kp[gi];
+    }
+    // Values (and fp32 keys): each thread stages 8 (token, 4 channels) units (a
+    // warp's 32 lanes share one token: the source branch is uniform).
     constexpr int kUnits = kTailTokens * 32 / kTailThreads;
     float4 k4[kUnits], v4[kUnits];
 #pragma unroll
@@ -858,8 +881,22 @@ __global__ void __launch_bounds__(kTailThreads) attn_tail_kernel(const TailArgs 
         const int e = threadIdx.x + i * kTailThreads;
         const int tt = e >> 5, d = (e & 31) * 4;
         if (tt < nt) {
-            k4[i] = tail_key4<BITS>(a, kc, kp, kres, sk, t0 + tt, d);
+            if (!kpacked) k4[i] = tail_key4<BITS>(a, kc, kp, kres, sk, t0 + tt, d);
             v4[i] = tail_value4<BITS>(a, vc, vp, vres, sv, t0 + tt, d);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < kQPer; ++i) {
+        const int e = threadIdx.x + i * kTailThreads;
+        if (e < a.GQ * 128) Qs[e] = qreg[i];
+    }
+    if (kpacked) {
+        // fma(code, scale, zero) as the packed path (quant.rs:404-406)
+        const int d = threadIdx.x;
+#pragma unroll
+        for (int u = 0; u < kTailTokens; ++u) {
+            const float x = (float)((kwd[u / TPW] >> ((u % TPW) * BITS)) & MASK);
+            Ks[u * kTailPitch + d] = __fmaf_rn(x, kpd.x, kpd.y);
         }
     }
 #pragma unroll
@@ -867,12 +904,14 @@ __global__ void __launch_bounds__(kTailThreads) attn_tail_kernel(const TailArgs 
         const int e = threadIdx.x + i * kTailThreads;
         const int tt = e >> 5, d = (e & 31) * 4;
         if (tt < nt) {
-            float *kd = Ks + tt * kTailPitch + d;
+            if (!kpacked) {
+                float *kd = Ks + tt * kTailPitch + d;
+                kd[0] = k4[i].x;
+                kd[1] = k4[i].y;
+                kd[2] = k4[i].z;
+                kd[3] = k4[i].w;
+            }
             float *vd = Vs + tt * kTailPitch + d;
-            kd[0] = k4[i].x;
-            kd[1] = k4[i].y;
-            kd[2] = k4[i].z;
-            kd[3] = k4[i].w;
             vd[0] = v4[i].x;
             vd[1] = v4[i].y;
             vd[2] = v4[i].z;
