@@ -437,9 +437,10 @@ class RagWorkload:
         self.pk, self.pv = self.gen.steps(nprof * S, B, H, D)
         self.pq = self.gen.queries((nprof, S, B, Hq, D))
         self.dout = torch.empty((S, B, Hq, D), device="cuda")
-        hk, hv = gen_tokens(rng, chs, B, H, 1, D)
-        self.hk = torch.from_numpy(hk.reshape(-1)).pin_memory()
-        self.hv = torch.from_numpy(hv.reshape(-1)).pin_memory()
+        # one new token per session, [S, B, H, 1, D] back to back
+        hk, hv = gen_tokens(rng, chs, B, H, S, D)
+        self.hk = torch.from_numpy(np.ascontiguousarray(hk.transpose(2, 0, 1, 3)).reshape(-1)).pin_memory()
+        self.hv = torch.from_numpy(np.ascontiguousarray(hv.transpose(2, 0, 1, 3)).reshape(-1)).pin_memory()
         self.hq = torch.from_numpy(
             rng.standard_normal(S * B * Hq * D, dtype=np.float32)).pin_memory()
         self.hout = torch.empty(S * B * Hq * D, dtype=torch.float32).pin_memory()
@@ -464,12 +465,11 @@ class RagWorkload:
         L = K.lib()
         fp = ctypes.POINTER(ctypes.c_float)
         err = K._Err()
-        kp, vp = ctypes.cast(self.hk.data_ptr(), fp), ctypes.cast(self.hv.data_ptr(), fp)
-        for s in self.sessions:
-            rc = L.kivi_session_append(s._h, kp, self.hk.numel(), vp, self.hv.numel(), 1,
-                                       ctypes.byref(err))
-            if rc:
-                raise K.KiviError(err.code, err.a, err.b, None, err.message.decode())
+        rc = L.kivi_sessions_append(
+            self._arr, self.S, ctypes.cast(self.hk.data_ptr(), fp), self.hk.numel(),
+            ctypes.cast(self.hv.data_ptr(), fp), self.hv.numel(), 1, ctypes.byref(err))
+        if rc:
+            raise K.KiviError(err.code, err.a, err.b, None, err.message.decode())
         rc = L.kivi_sessions_attention_batched(
             self._arr, self.S, ctypes.cast(self.hq.data_ptr(), fp), self.hq.numel(), self.Hq,
             ctypes.c_float(self.scale), ctypes.cast(self.hout.data_ptr(), fp), self.hout.numel(),
@@ -477,13 +477,12 @@ class RagWorkload:
         if rc:
             raise K.KiviError(err.code, err.a, err.b, None, err.message.decode())
 
-    e2e_api = ("kivi_session_append per session + kivi_sessions_attention_batched "
-               "(RagSession::append/attention), pinned host buffers")
+    e2e_api = ("kivi_sessions_append + kivi_sessions_attention_batched (RagSession::append and "
+               "::attention of every session, one upload and one synchronisation each), pinned "
+               "host buffers")
 
     def io_bytes(self):
-        S = self.S
-        return (S * (self.hk.numel() + self.hv.numel()) + self.hq.numel()) * 4, \
-            self.hout.numel() * 4
+        return (self.hk.numel() + self.hv.numel() + self.hq.numel()) * 4, self.hout.numel() * 4
 
     def _suffix_bytes(self):
         c = self.cfgd

@@ -219,7 +219,9 @@ int32_t kivi_cache_attention_noalloc_dev(const kivi_cache *cache, const float *d
                                          uint64_t num_q_heads, float scale, float *d_out,
                                          void *stream, kivi_error *err);
 
-/* RuntimeKv::decode (runtime.rs:46-56): append one token, then attend. */
+/* RuntimeKv::decode (runtime.rs:46-56): append one token, then attend.  One
+ * upload of key, value and query, one synchronisation; a rejected query
+ * (QueryHeads, Shape) is reported after the append, as in the reference. */
 int32_t kivi_cache_decode(kivi_cache *cache, const float *key, uint64_t key_len,
                           const float *value, uint64_t value_len, const float *query,
                           uint64_t query_len, uint64_t num_q_heads, float scale, float *out,
@@ -333,6 +335,13 @@ int32_t kivi_session_reserve(kivi_session *session, uint64_t tokens, kivi_error 
 int32_t kivi_sessions_append_dev(kivi_session *const *sessions, uint64_t n, const float *d_keys,
                                  const float *d_values, uint64_t seq_len, void *stream,
                                  kivi_error *err);
+/* The same from host memory (keys/values of all n sessions back to back,
+ * keys_len == values_len == n*batch*num_kv_heads*seq_len*head_dim, else
+ * Shape): one upload, one synchronisation.  Equal to n kivi_session_append
+ * calls. */
+int32_t kivi_sessions_append(kivi_session *const *sessions, uint64_t n, const float *keys,
+                             uint64_t keys_len, const float *values, uint64_t values_len,
+                             uint64_t seq_len, kivi_error *err);
 int32_t kivi_sessions_attention_batched(const kivi_session *const *sessions, uint64_t n,
                                         const float *queries, uint64_t queries_len,
                                         uint64_t num_q_heads, float scale, float *out,

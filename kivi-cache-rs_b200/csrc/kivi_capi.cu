@@ -980,9 +980,43 @@ int32_t kivi_cache_decode(kivi_cache *h, const float *key, uint64_t key_len, con
                           uint64_t value_len, const float *query, uint64_t query_len, uint64_t Hq,
                           float scale, float *out, uint64_t out_len, kivi_error *err) {
     // runtime.rs:53-55: append(key, value, 1)? then attention(query)
-    int32_t rc = kivi_cache_append(h, key, key_len, value, value_len, 1, err);
+    if (!h) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null cache");
+    const uint64_t kv = h->s.n() * h->s.D;
+    if (key_len != kv || value_len != kv || !key || !value)
+        return kivi_cache_append(h, key, key_len, value, value_len, 1, err); // its error
+    // a query the attention would reject: the append still happens first
+    kivi_error qerr{};
+    int32_t qrc = check_query(h->s, Hq, query_len, true, &qerr);
+    const uint64_t n = h->s.B * Hq * h->s.D;
+    if (!qrc && out_len != n) qrc = set_err(&qerr, KIVI_ERR_SHAPE, n, out_len);
+    if (!qrc && (!query || !out)) qrc = set_msg(&qerr, KIVI_ERR_INVALID_ARGUMENT, "null buffer");
+    if (qrc) {
+        int32_t rc = kivi_cache_append(h, key, key_len, value, value_len, 1, err);
+        if (rc) return rc;
+        if (err) *err = qerr;
+        return qrc;
+    }
+    // one upload of key, value and query, both launches, one synchronisation
+    std::lock_guard<std::mutex> lk(h->mu);
+    DeviceGuard dg(h->s.device);
+    const size_t kb = kv * sizeof(float), qb = n * sizeof(float);
+    CUDA_TRY(wait_dev(h->stream, h->dev_done), "decode");
+    CUDA_TRY(h->stage.ensure(2 * kb + 2 * qb), "decode staging");
+    float *dk = h->stage.as<float>(), *dv = h->stage.as<float>(kb);
+    float *dq = h->stage.as<float>(2 * kb), *dout = h->stage.as<float>(2 * kb + qb);
+    CUDA_TRY(cudaMemcpyAsync(dk, key, kb, cudaMemcpyHostToDevice, h->stream), "decode H2D");
+    CUDA_TRY(cudaMemcpyAsync(dv, value, kb, cudaMemcpyHostToDevice, h->stream), "decode H2D");
+    CUDA_TRY(cudaMemcpyAsync(dq, query, qb, cudaMemcpyHostToDevice, h->stream), "decode H2D");
+    int32_t rc = append_device(h->s, dk, dv, 1, h->stream, err);
     if (rc) return rc;
-    return kivi_cache_attention(h, query, query_len, Hq, scale, out, out_len, err);
+    rc = run_attention(h->s, nullptr, 1, dq, Hq, scale, dout, nullptr, nullptr, h->part, h->stream,
+                       err);
+    if (rc) return rc;
+    CUDA_TRY(cudaMemcpyAsync(out, dout, qb, cudaMemcpyDeviceToHost, h->stream), "decode D2H");
+    CUDA_TRY(cudaStreamSynchronize(h->stream), "decode");
+    rc = check_device_waits(err);
+    if (rc) return rc;
+    return set_err(err, KIVI_OK);
 }
 
 int32_t kivi_cache_attention_partial_dev(const kivi_cache *h, const float *dq, uint64_t Hq,
@@ -1420,6 +1454,34 @@ int32_t kivi_sessions_append_dev(kivi_session *const *ss, uint64_t nsess, const 
     }
     for (uint64_t i = 0; i < nsess; ++i) ss[i]->len += seq;
     CUDA_TRY(mark_dev(p->batch_done, st), "sessions append");
+    return set_err(err, KIVI_OK);
+}
+
+int32_t kivi_sessions_append(kivi_session *const *ss, uint64_t nsess, const float *keys,
+                             uint64_t keys_len, const float *values, uint64_t values_len,
+                             uint64_t seq, kivi_error *err) {
+    if (!ss || nsess == 0 || !ss[0]) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "no sessions");
+    const KvState &p = ss[0]->prefix->s;
+    const uint64_t expected = nsess * p.n() * seq * p.D; // prefix.rs:180-192 per session
+    if (keys_len != expected) return set_err(err, KIVI_ERR_SHAPE, expected, keys_len);
+    if (values_len != expected) return set_err(err, KIVI_ERR_SHAPE, expected, values_len);
+    if (seq == 0) return set_err(err, KIVI_OK);
+    if (!keys || !values) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null input");
+    for (uint64_t i = 0; i < nsess; ++i)
+        if (!ss[i] || ss[i]->prefix != ss[0]->prefix)
+            return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "sessions must share one prefix");
+    kivi_session *lead = ss[0];
+    std::lock_guard<std::mutex> lk(lead->mu);
+    DeviceGuard dg(p.device);
+    for (uint64_t i = 0; i < nsess; ++i) CUDA_TRY(wait_session(lead->stream, ss[i]), "sessions append");
+    const size_t bytes = expected * sizeof(float);
+    CUDA_TRY(lead->stage.ensure(2 * bytes), "sessions append staging");
+    float *dk = lead->stage.as<float>(), *dv = lead->stage.as<float>(bytes);
+    CUDA_TRY(cudaMemcpyAsync(dk, keys, bytes, cudaMemcpyHostToDevice, lead->stream), "sessions append H2D");
+    CUDA_TRY(cudaMemcpyAsync(dv, values, bytes, cudaMemcpyHostToDevice, lead->stream), "sessions append H2D");
+    int32_t rc = kivi_sessions_append_dev(ss, nsess, dk, dv, seq, lead->stream, err);
+    if (rc) return rc;
+    CUDA_TRY(cudaStreamSynchronize(lead->stream), "sessions append");
     return set_err(err, KIVI_OK);
 }
 

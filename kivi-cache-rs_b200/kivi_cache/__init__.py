@@ -143,6 +143,7 @@ def lib():
         "kivi_merge_partials_dev": ([sz, sz, sz, P, P, P, P, P, e], i32),
         "kivi_cache_seal": ([P, e], i32),
         "kivi_sessions_append_dev": ([P, sz, P, P, sz, P, e], i32),
+        "kivi_sessions_append": ([P, sz, fp, sz, fp, sz, sz, e], i32),
         "kivi_session_reserve": ([P, sz, e], i32),
         "kivi_packed_partials_floats": ([sz, sz], sz),
         "kivi_cache_attention_partial_packed_dev": ([P, P, sz, f32, P, P, e], i32),
@@ -642,6 +643,18 @@ def sessions_attention_batched(sessions, queries, num_q_heads, scale):
     return out
 
 
+def sessions_append(sessions, keys, values, seq_len):
+    """RagSession::append of every session of one prefix from host memory in
+    one upload and one launch: keys/values [n, batch, num_kv_heads, seq_len,
+    head_dim]; equal to appending session by session."""
+    n = len(sessions)
+    arr = (C.c_void_p * n)(*[s._h for s in sessions])
+    k, kp = _f32(keys)
+    v, vp = _f32(values)
+    err = _Err()
+    _check(lib().kivi_sessions_append(arr, n, kp, k.size, vp, v.size, seq_len, C.byref(err)), err)
+
+
 def sessions_append_dev(sessions, d_keys, d_values, seq_len, stream=None):
     """RagSession::append of every session in one launch: d_keys/d_values
     [n, batch, num_kv_heads, seq_len, head_dim] on the device."""
@@ -976,7 +989,7 @@ __all__ = [
     "SharedPrefix", "SharedPrefixFootprint", "RagSession", "RuntimeKv", "QuantAxis",
     "QuantizedTensor", "quantize_per_channel", "quantize_per_token", "layer_kv_bytes",
     "marginal_bytes_per_layer", "AgentMemoryBudget", "sessions_attention_batched",
-    "sessions_attention_batched_dev", "sessions_append_dev", "merge_partials_dev", "kernel_launches", "lib", "LIB_PATH",
+    "sessions_attention_batched_dev", "sessions_append", "sessions_append_dev", "merge_partials_dev", "kernel_launches", "lib", "LIB_PATH",
     "QualityGuard", "QualityPolicy", "QualityUpgrade", "FlushCheck", "MixedPrecisionBudget",
     "ModelPreset", "EconInputs", "EconReport", "PretrainEstimate", "compute_report",
     "estimate_pretrain", "gpus_for_kv", "kv_budget_bytes", "parse_context_tokens",

@@ -690,10 +690,11 @@ def test_batched_sessions_tcgen05_match_oracle(K, bits, kv, qh, nsess, doc):
 
 
 def test_batched_session_append_equals_per_session_append(K):
-    """kivi_sessions_append_dev (one launch for all sessions) leaves every
-    session exactly as RagSession::append would (prefix.rs:173-211): same
-    suffix length, bitwise-equal attention afterwards, and the tensor-core
-    batched attention matches the oracle's RagSession::attention."""
+    """kivi_sessions_append_dev (one launch for all sessions) and
+    kivi_sessions_append (the same from host memory) leave every session
+    exactly as RagSession::append would (prefix.rs:173-211): same suffix
+    length, bitwise-equal attention afterwards, and the tensor-core batched
+    attention matches the oracle's RagSession::attention."""
     torch = pytest.importorskip("torch")
     kv, qh, dim, doc, n = 4, 16, 128, 2100, 6
     keys, values, _ = synthetic_kv(5, 1, kv, doc, dim)
@@ -702,6 +703,7 @@ def test_batched_session_append_equals_per_session_append(K):
     prefix, oprefix = cache.share_prefix(), ocache.share_prefix()
     rng = np.random.default_rng(9)
     batched = [prefix.session() for _ in range(n)]
+    hostb = [prefix.session() for _ in range(n)]
     single = [prefix.session() for _ in range(n)]
     oracle = [oprefix.session() for _ in range(n)]
     for step, ln in enumerate([3, 1, 1, 40, 1]):
@@ -709,6 +711,7 @@ def test_batched_session_append_equals_per_session_append(K):
         v = rng.standard_normal((n, 1, kv, ln, dim), dtype=np.float32)
         K.sessions_append_dev(batched, torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda(), ln)
         torch.cuda.synchronize()
+        K.sessions_append(hostb, k, v, ln)
         for i in range(n):
             single[i].append(k[i].reshape(-1), v[i].reshape(-1), ln)
             oracle[i].append(k[i].reshape(-1), v[i].reshape(-1), ln)
@@ -720,9 +723,53 @@ def test_batched_session_append_equals_per_session_append(K):
         # identical suffixes: the single-session attentions agree bit for bit
         one = batched[i].attention(q[i].reshape(-1), qh, scale)
         assert (one == single[i].attention(q[i].reshape(-1), qh, scale)).all(), i
+        assert hostb[i].question_tokens() == 46
+        assert (hostb[i].attention(q[i].reshape(-1), qh, scale) == one).all(), i
         ref = oracle[i].attention(q[i].reshape(-1), qh, scale)
         assert max_abs(out[i], ref) <= ATOL and rel_l2(out[i], ref) <= RTOL_L2, i
         assert max_abs(one, ref) <= ATOL and rel_l2(one, ref) <= RTOL_L2, i
+
+
+def test_batched_host_session_append_checks_shapes(K):
+    """kivi_sessions_append: Shape{n*B*H*seq*D, len} before any mutation."""
+    cache = K.KiviCache(K.KiviConfig.try_new(2, 32, 128), 1, 2, 128)
+    x = np.ones(2 * 64 * 128, np.float32)
+    cache.append(x, x, 64)
+    prefix = cache.share_prefix()
+    ss = [prefix.session() for _ in range(3)]
+    good = np.ones(3 * 2 * 2 * 128, np.float32)
+    with pytest.raises(K.KiviError) as e:
+        K.sessions_append(ss, good[:-1], good, 2)
+    assert (e.value.variant, e.value.a, e.value.b) == ("Shape", good.size, good.size - 1)
+    with pytest.raises(K.KiviError) as e:
+        K.sessions_append(ss, good, good[:-1], 2)
+    assert e.value.variant == "Shape"
+    assert all(s.question_tokens() == 0 for s in ss)
+    K.sessions_append(ss, good, good, 2)
+    assert all(s.question_tokens() == 2 for s in ss)
+
+
+def test_decode_rejected_query_still_appends(K):
+    """runtime.rs:53-55: append(key, value, 1)? then attention(query)?: a query
+    the attention rejects (QueryHeads, Shape) is reported after the append,
+    and a good one returns what append + attention return."""
+    cfg = K.KiviConfig.try_new(2, 32, 128)
+    rt = K.RuntimeKv.try_new(cfg, 1, 2, 128)
+    cache = K.KiviCache(cfg, 1, 2, 128)
+    x = fill(2 * 40 * 128, 3)
+    rt.prefill(x, x, 40)
+    cache.append(x, x, 40)
+    k, v = fill(2 * 128, 5), fill(2 * 128, 6)
+    with pytest.raises(K.KiviError) as e:
+        rt.decode(k, v, fill(3 * 128, 7), 3, 0.1)
+    assert e.value.variant == "QueryHeads"
+    assert rt.cache().sequence_length() == 41
+    cache.append(k, v, 1)
+    q = fill(4 * 128, 8)
+    got = rt.decode(k, v, q, 4, 0.1)
+    cache.append(k, v, 1)
+    assert rt.cache().sequence_length() == 42
+    assert (got == cache.attention(q, 4, 0.1)).all()
 
 
 def test_unaligned_device_inputs(K):
