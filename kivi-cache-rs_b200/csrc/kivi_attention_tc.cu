@@ -988,6 +988,16 @@ __global__ void __launch_bounds__(128) merge_rows_kernel(const float *part_ml, c
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t row = blockIdx.x;
     const float *ml = part_ml + row * parts * 2;
+    // this warp's first kPre slots of o are loaded before the maximum and the
+    // weights are known, so their memory latency overlaps those two phases
+    constexpr int kPre = 8;
+    const float4 *po = reinterpret_cast<const float4 *>(part_o + row * parts * 128) + lane;
+    float4 pre[kPre];
+#pragma unroll
+    for (int i = 0; i < kPre; ++i) {
+        const int c = warp + 4 * i;
+        if (c < parts) pre[i] = po[(int64_t)c * 32];
+    }
     if (warp == 0) {
         float M = -INFINITY;
         for (int c = lane; c < parts; c += 32)
@@ -1010,9 +1020,20 @@ __global__ void __launch_bounds__(128) merge_rows_kernel(const float *part_ml, c
     if (lane == 0) lsh[warp] = Lp;
     __syncthreads();
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    const float4 *po = reinterpret_cast<const float4 *>(part_o + row * parts * 128) + lane;
+    // slots in increasing order per warp (the prefetched ones first)
+#pragma unroll
+    for (int i = 0; i < kPre; ++i) {
+        const int c = warp + 4 * i;
+        if (c < parts) {
+            const float w = wsh[c]; // c < 4 kPre <= 512
+            acc.x = fmaf(pre[i].x, w, acc.x);
+            acc.y = fmaf(pre[i].y, w, acc.y);
+            acc.z = fmaf(pre[i].z, w, acc.z);
+            acc.w = fmaf(pre[i].w, w, acc.w);
+        }
+    }
 #pragma unroll 4
-    for (int c = warp; c < parts; c += 4) {
+    for (int c = warp + 4 * kPre; c < parts; c += 4) {
         float w;
         if (c < 512) {
             w = wsh[c];
