@@ -898,6 +898,52 @@ int32_t kivi_cache_append_dev(kivi_cache *h, const float *dk, const float *dv, u
     return set_err(err, KIVI_OK);
 }
 
+// ---- host buffers of the synchronous calls
+// Mapped pinned host memory (cudaHostAlloc / cudaHostRegister under unified
+// addressing) is read and written by the kernels in place: a copy-engine
+// transfer costs ~20 us of fixed latency, more than a decode step's bytes
+// take over PCIe.  Pageable memory goes through the staging buffers.
+
+// The address at which the current device reads host pointer p, or null.
+static const float *mapped_host(const void *p) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return nullptr;
+    }
+    return a.type == cudaMemoryTypeHost ? static_cast<const float *>(a.devicePointer) : nullptr;
+}
+
+// An input read once in order (appended rows): in place when mapped.
+static cudaError_t input_once(const float *host, float *stage, size_t n, cudaStream_t st,
+                              const float **dev) {
+    if (const float *m = mapped_host(host)) {
+        *dev = m;
+        return cudaSuccess;
+    }
+    *dev = stage;
+    return cudaMemcpyAsync(stage, host, n * sizeof(float), cudaMemcpyHostToDevice, st);
+}
+
+// An input the kernels read many times (queries): brought into `stage`, by a
+// copy kernel when mapped.
+static cudaError_t input_staged(const float *host, float *stage, size_t n, cudaStream_t st) {
+    if (const float *m = mapped_host(host)) return kivi::launch_copy_f32(stage, m, (int64_t)n, st);
+    return cudaMemcpyAsync(stage, host, n * sizeof(float), cudaMemcpyHostToDevice, st);
+}
+
+// Where the kernels write an output: the host buffer itself when mapped (and
+// kernels compute it: `kernels`), else `stage`, copied back by output_done.
+static float *output_target(float *host, float *stage, bool kernels) {
+    float *m = kernels ? const_cast<float *>(mapped_host(host)) : nullptr;
+    return m ? m : stage;
+}
+static cudaError_t output_done(float *host, const float *dev, const float *stage, size_t n,
+                               cudaStream_t st) {
+    if (dev != stage) return cudaSuccess;
+    return cudaMemcpyAsync(host, stage, n * sizeof(float), cudaMemcpyDeviceToHost, st);
+}
+
 int32_t kivi_cache_append(kivi_cache *h, const float *keys, uint64_t keys_len,
                           const float *values, uint64_t values_len, uint64_t seq,
                           kivi_error *err) {
@@ -913,9 +959,17 @@ int32_t kivi_cache_append(kivi_cache *h, const float *keys, uint64_t keys_len,
     const size_t bytes = expected * sizeof(float);
     CUDA_TRY(wait_dev(h->stream, h->dev_done), "append");
     CUDA_TRY(h->stage.ensure(2 * bytes), "append staging");
-    float *dk = h->stage.as<float>(), *dv = h->stage.as<float>(bytes);
-    CUDA_TRY(cudaMemcpyAsync(dk, keys, bytes, cudaMemcpyHostToDevice, h->stream), "append H2D");
-    CUDA_TRY(cudaMemcpyAsync(dv, values, bytes, cudaMemcpyHostToDevice, h->stream), "append H2D");
+    const float *dk = h->stage.as<float>(), *dv = h->stage.as<float>(bytes);
+    if (seq < h->s.cfg.residual_length) {
+        // decode-sized appends read their rows in order: mapped inputs in place
+        CUDA_TRY(input_once(keys, h->stage.as<float>(), expected, h->stream, &dk), "append H2D");
+        CUDA_TRY(input_once(values, h->stage.as<float>(bytes), expected, h->stream, &dv), "append H2D");
+    } else {
+        CUDA_TRY(cudaMemcpyAsync(h->stage.as<float>(), keys, bytes, cudaMemcpyHostToDevice,
+                                 h->stream), "append H2D");
+        CUDA_TRY(cudaMemcpyAsync(h->stage.as<float>(bytes), values, bytes, cudaMemcpyHostToDevice,
+                                 h->stream), "append H2D");
+    }
     int32_t rc = append_device(h->s, dk, dv, seq, h->stream, err);
     if (rc) return rc;
     CUDA_TRY(cudaStreamSynchronize(h->stream), "append");
@@ -954,11 +1008,12 @@ int32_t kivi_cache_attention(const kivi_cache *h, const float *query, uint64_t q
     DeviceGuard dg(h->s.device);
     CUDA_TRY(wait_dev(h->stream, h->dev_done), "attention");
     CUDA_TRY(mh->stage.ensure(2 * n * sizeof(float)), "attention staging");
-    float *dq = mh->stage.as<float>(), *dout = mh->stage.as<float>(n * sizeof(float));
-    CUDA_TRY(cudaMemcpyAsync(dq, query, n * 4, cudaMemcpyHostToDevice, h->stream), "attention H2D");
+    float *dq = mh->stage.as<float>(), *stage_out = mh->stage.as<float>(n * sizeof(float));
+    CUDA_TRY(input_staged(query, dq, n, h->stream), "attention H2D");
+    float *dout = output_target(out, stage_out, h->s.seq > 0);
     rc = kivi_cache_attention_dev(h, dq, Hq, scale, dout, h->stream, err);
     if (rc) return rc;
-    CUDA_TRY(cudaMemcpyAsync(out, dout, n * 4, cudaMemcpyDeviceToHost, h->stream), "attention D2H");
+    CUDA_TRY(output_done(out, dout, stage_out, n, h->stream), "attention D2H");
     CUDA_TRY(cudaStreamSynchronize(h->stream), "attention");
     rc = check_device_waits(err);
     if (rc) return rc;
@@ -996,23 +1051,28 @@ int32_t kivi_cache_decode(kivi_cache *h, const float *key, uint64_t key_len, con
         if (err) *err = qerr;
         return qrc;
     }
-    // one upload of key, value and query, both launches, one synchronisation
+    // one upload of key, value and query, both launches, one synchronisation.
+    // Mapped pinned buffers skip the copy engine (each copy costs ~20 us of
+    // fixed latency): the append kernel reads key and value from host memory,
+    // a copy kernel brings the query into device memory (the attention kernels
+    // read it many times), and the merge writes the output into host memory.
     std::lock_guard<std::mutex> lk(h->mu);
     DeviceGuard dg(h->s.device);
     const size_t kb = kv * sizeof(float), qb = n * sizeof(float);
     CUDA_TRY(wait_dev(h->stream, h->dev_done), "decode");
     CUDA_TRY(h->stage.ensure(2 * kb + 2 * qb), "decode staging");
-    float *dk = h->stage.as<float>(), *dv = h->stage.as<float>(kb);
-    float *dq = h->stage.as<float>(2 * kb), *dout = h->stage.as<float>(2 * kb + qb);
-    CUDA_TRY(cudaMemcpyAsync(dk, key, kb, cudaMemcpyHostToDevice, h->stream), "decode H2D");
-    CUDA_TRY(cudaMemcpyAsync(dv, value, kb, cudaMemcpyHostToDevice, h->stream), "decode H2D");
-    CUDA_TRY(cudaMemcpyAsync(dq, query, qb, cudaMemcpyHostToDevice, h->stream), "decode H2D");
+    float *dq = h->stage.as<float>(2 * kb), *stage_out = h->stage.as<float>(2 * kb + qb);
+    const float *dk = nullptr, *dv = nullptr;
+    CUDA_TRY(input_once(key, h->stage.as<float>(), kv, h->stream, &dk), "decode H2D");
+    CUDA_TRY(input_once(value, h->stage.as<float>(kb), kv, h->stream, &dv), "decode H2D");
+    CUDA_TRY(input_staged(query, dq, n, h->stream), "decode H2D");
+    float *dout = output_target(out, stage_out, true);
     int32_t rc = append_device(h->s, dk, dv, 1, h->stream, err);
     if (rc) return rc;
     rc = run_attention(h->s, nullptr, 1, dq, Hq, scale, dout, nullptr, nullptr, h->part, h->stream,
                        err);
     if (rc) return rc;
-    CUDA_TRY(cudaMemcpyAsync(out, dout, qb, cudaMemcpyDeviceToHost, h->stream), "decode D2H");
+    CUDA_TRY(output_done(out, dout, stage_out, n, h->stream), "decode D2H");
     CUDA_TRY(cudaStreamSynchronize(h->stream), "decode");
     rc = check_device_waits(err);
     if (rc) return rc;
@@ -1476,9 +1536,10 @@ int32_t kivi_sessions_append(kivi_session *const *ss, uint64_t nsess, const floa
     for (uint64_t i = 0; i < nsess; ++i) CUDA_TRY(wait_session(lead->stream, ss[i]), "sessions append");
     const size_t bytes = expected * sizeof(float);
     CUDA_TRY(lead->stage.ensure(2 * bytes), "sessions append staging");
-    float *dk = lead->stage.as<float>(), *dv = lead->stage.as<float>(bytes);
-    CUDA_TRY(cudaMemcpyAsync(dk, keys, bytes, cudaMemcpyHostToDevice, lead->stream), "sessions append H2D");
-    CUDA_TRY(cudaMemcpyAsync(dv, values, bytes, cudaMemcpyHostToDevice, lead->stream), "sessions append H2D");
+    const float *dk = nullptr, *dv = nullptr;
+    CUDA_TRY(input_once(keys, lead->stage.as<float>(), expected, lead->stream, &dk), "sessions append H2D");
+    CUDA_TRY(input_once(values, lead->stage.as<float>(bytes), expected, lead->stream, &dv),
+             "sessions append H2D");
     int32_t rc = kivi_sessions_append_dev(ss, nsess, dk, dv, seq, lead->stream, err);
     if (rc) return rc;
     CUDA_TRY(cudaStreamSynchronize(lead->stream), "sessions append");
@@ -1498,7 +1559,10 @@ int32_t kivi_session_append(kivi_session *s, const float *keys, uint64_t keys_le
     std::lock_guard<std::mutex> lk(s->mu);
     DeviceGuard dg(p.device);
     CUDA_TRY(wait_session(s->stream, s), "session append");
-    int32_t rc = session_append(s, keys, values, seq, cudaMemcpyHostToDevice, s->stream, err);
+    // mapped inputs: the suffix-append kernel reads the rows in place
+    const float *mk = mapped_host(keys), *mv = mapped_host(values);
+    int32_t rc = mk && mv ? session_append(s, mk, mv, seq, cudaMemcpyDeviceToDevice, s->stream, err)
+                          : session_append(s, keys, values, seq, cudaMemcpyHostToDevice, s->stream, err);
     if (rc) return rc;
     CUDA_TRY(cudaStreamSynchronize(s->stream), "session append");
     return set_err(err, KIVI_OK);
@@ -1591,12 +1655,13 @@ int32_t kivi_session_attention(const kivi_session *s, const float *query, uint64
     DeviceGuard dg(p.device);
     CUDA_TRY(wait_session(s->stream, s), "session attention");
     CUDA_TRY(ms->stage.ensure(2 * n * 4), "session staging");
-    float *dq = ms->stage.as<float>(), *dout = ms->stage.as<float>(n * 4);
-    CUDA_TRY(cudaMemcpyAsync(dq, query, n * 4, cudaMemcpyHostToDevice, s->stream), "session H2D");
+    float *dq = ms->stage.as<float>(), *stage_out = ms->stage.as<float>(n * 4);
+    CUDA_TRY(input_staged(query, dq, n, s->stream), "session H2D");
+    float *dout = output_target(out, stage_out, p.seq > 0 || s->len > 0);
     const kivi_session *arr[1] = {s};
     rc = sessions_attention_dev(arr, 1, dq, Hq, scale, dout, s->stream, ms->part, err);
     if (rc) return rc;
-    CUDA_TRY(cudaMemcpyAsync(out, dout, n * 4, cudaMemcpyDeviceToHost, s->stream), "session D2H");
+    CUDA_TRY(output_done(out, dout, stage_out, n, s->stream), "session D2H");
     CUDA_TRY(cudaStreamSynchronize(s->stream), "session attention");
     rc = check_device_waits(err);
     if (rc) return rc;
@@ -1635,11 +1700,14 @@ int32_t kivi_sessions_attention_batched(const kivi_session *const *ss, uint64_t 
     if (lead->prefix->batch_done)
         CUDA_TRY(wait_dev(lead->stream, lead->prefix->batch_done), "batched attention");
     CUDA_TRY(lead->stage.ensure(2 * total * 4), "batched staging");
-    float *dq = lead->stage.as<float>(), *dout = lead->stage.as<float>(total * 4);
-    CUDA_TRY(cudaMemcpyAsync(dq, queries, total * 4, cudaMemcpyHostToDevice, lead->stream), "batched H2D");
+    float *dq = lead->stage.as<float>(), *stage_out = lead->stage.as<float>(total * 4);
+    CUDA_TRY(input_staged(queries, dq, total, lead->stream), "batched H2D");
+    bool any = p.seq > 0;
+    for (uint64_t i = 0; i < n; ++i) any = any || ss[i]->len > 0;
+    float *dout = output_target(out, stage_out, any);
     rc = sessions_attention_dev(ss, n, dq, Hq, scale, dout, lead->stream, lead->part, err);
     if (rc) return rc;
-    CUDA_TRY(cudaMemcpyAsync(out, dout, total * 4, cudaMemcpyDeviceToHost, lead->stream), "batched D2H");
+    CUDA_TRY(output_done(out, dout, stage_out, total, lead->stream), "batched D2H");
     CUDA_TRY(cudaStreamSynchronize(lead->stream), "batched attention");
     return set_err(err, KIVI_OK);
 }

@@ -139,6 +139,9 @@ struct RowCopy {
 };
 // Two row copies in one launch (rows of D floats, D % 4 == 0, 16-byte aligned).
 cudaError_t launch_copy_rows2(const RowCopy &j0, const RowCopy &j1, int n, int D, cudaStream_t s);
+// n floats src -> dst by a kernel (src may be mapped pinned host memory: the
+// read crosses PCIe without a copy-engine transfer and its fixed latency).
+cudaError_t launch_copy_f32(float *dst, const float *src, int64_t n, cudaStream_t s);
 // Copy input rows [src_off, src_off+count) of every stream into ring/linear rows:
 // dst slot = (dst_head + dst_off + i) % ring (ring = R for the value window, or
 // a huge number for a linear buffer).

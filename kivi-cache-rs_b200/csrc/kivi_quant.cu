@@ -18,6 +18,8 @@
 #include <math.h>
 #include <stdint.h>
 
+#include <algorithm>
+
 #include "kivi_internal.cuh"
 
 namespace kivi {
@@ -423,6 +425,31 @@ cudaError_t launch_copy_rows2(const RowCopy &j0, const RowCopy &j1, int n, int D
     if (n <= 0 || cnt <= 0) return cudaSuccess;
     ProfScope prof("copy_rows", s);
     copy_rows2_kernel<<<dim3(blocks_for(cnt * (D / 4), 256), n, 2), 256, 0, s>>>(j0, j1, D);
+    count_launch();
+    return cudaGetLastError();
+}
+
+__global__ void __launch_bounds__(256) copy_f32_kernel(float *dst, const float *src, int64_t n,
+                                                       bool vec) {
+    const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    if (vec) {
+        const int64_t n4 = n / 4;
+        for (int64_t i = i0; i < n4; i += step)
+            reinterpret_cast<float4 *>(dst)[i] = reinterpret_cast<const float4 *>(src)[i];
+        for (int64_t i = 4 * n4 + i0; i < n; i += step) dst[i] = src[i];
+    } else {
+        for (int64_t i = i0; i < n; i += step) dst[i] = src[i];
+    }
+}
+
+cudaError_t launch_copy_f32(float *dst, const float *src, int64_t n, cudaStream_t s) {
+    if (n <= 0) return cudaSuccess;
+    ProfScope prof("copy_in", s);
+    const bool vec = ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15u) == 0;
+    const int64_t units = vec ? (n + 3) / 4 : n;
+    const unsigned blocks = (unsigned)std::min<int64_t>((units + 255) / 256, 1184);
+    copy_f32_kernel<<<blocks, 256, 0, s>>>(dst, src, n, vec);
     count_launch();
     return cudaGetLastError();
 }

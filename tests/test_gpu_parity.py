@@ -772,6 +772,100 @@ def test_decode_rejected_query_still_appends(K):
     assert (got == cache.attention(q, 4, 0.1)).all()
 
 
+def test_decode_pinned_buffers_match_pageable(K):
+    """kivi_cache_decode reads mapped pinned host buffers in place (key, value,
+    query) and writes the output into them; the result and the cache equal
+    those of pageable buffers bit for bit, across key flushes."""
+    torch = pytest.importorskip("torch")
+    import ctypes as C
+
+    cfg = K.KiviConfig.try_new(2, 32, 128)
+    batch, kv, qh, dim = 2, 2, 8, 128
+    scale = float(np.float32(1.0) / np.sqrt(np.float32(dim)))
+    a, b = K.RuntimeKv.try_new(cfg, batch, kv, dim), K.RuntimeKv.try_new(cfg, batch, kv, dim)
+    x = fill(batch * kv * 250 * dim, 3)
+    a.prefill(x, x, 250)
+    b.prefill(x, x, 250)
+    fp = C.POINTER(C.c_float)
+    for step in range(40):  # crosses the key flush at 256
+        k, v = fill(batch * kv * dim, 10 + step), fill(batch * kv * dim, 60 + step)
+        q = fill(batch * qh * dim, 110 + step)
+        want = a.decode(k, v, q, qh, scale)
+        pk, pv, pq = (torch.from_numpy(t).pin_memory() for t in (k, v, q))
+        po = torch.full((want.size,), float("nan")).pin_memory()
+        err = K._Err()
+        rc = K.lib().kivi_cache_decode(b.cache()._h, C.cast(pk.data_ptr(), fp), k.size,
+                                       C.cast(pv.data_ptr(), fp), v.size, C.cast(pq.data_ptr(), fp),
+                                       q.size, qh, C.c_float(scale), C.cast(po.data_ptr(), fp),
+                                       want.size, C.byref(err))
+        assert rc == 0, err.message
+        assert (po.numpy() == want).all(), step
+    assert a.cache().sequence_length() == b.cache().sequence_length() == 290
+    ka, va = a.cache().dequantize()
+    kb, vb = b.cache().dequantize()
+    assert (ka == kb).all() and (va == vb).all()
+
+
+def test_host_calls_pinned_buffers_match_pageable(K):
+    """The host-pointer cache and session calls read mapped pinned inputs in
+    place and write mapped outputs directly; every result equals the one from
+    pageable buffers bit for bit (empty-cache zeros included)."""
+    torch = pytest.importorskip("torch")
+    import ctypes as C
+
+    fp = C.POINTER(C.c_float)
+
+    held = []  # pinned tensors stay alive until the test ends (the caching host
+    # allocator would otherwise hand a freed buffer to the next pin())
+
+    def pin(a):
+        t = torch.from_numpy(np.ascontiguousarray(a, np.float32)).pin_memory()
+        held.append(t)
+        return t
+
+    def ptr(t):
+        return C.cast(t.data_ptr(), fp)
+
+    def call(fn, *args):
+        err = K._Err()
+        assert fn(*args, C.byref(err)) == 0, err.message
+
+    L = K.lib()
+    cfg = K.KiviConfig.try_new(2, 32, 128)
+    batch, kv, qh, dim = 1, 2, 8, 128
+    scale = C.c_float(0.088)
+    a, b = K.KiviCache(cfg, batch, kv, dim), K.KiviCache(cfg, batch, kv, dim)
+    q = fill(batch * qh * dim, 1)
+    po = pin(np.full(q.size, np.nan, np.float32))
+    call(L.kivi_cache_attention, b._h, ptr(pin(q)), q.size, qh, scale, ptr(po), q.size)
+    assert (po.numpy() == a.attention(q, qh, 0.088)).all() and (po.numpy() == 0).all()
+    for n in (200, 1, 1, 70, 1):  # bulk (staged) and decode-sized (in place) appends
+        x, y = fill(batch * kv * n * dim, n), fill(batch * kv * n * dim, n + 7)
+        a.append(x, y, n)
+        call(L.kivi_cache_append, b._h, ptr(pin(x)), x.size, ptr(pin(y)), y.size, n)
+        call(L.kivi_cache_attention, b._h, ptr(pin(q)), q.size, qh, scale, ptr(po), q.size)
+        assert (po.numpy() == a.attention(q, qh, 0.088)).all(), n
+    pa, pb = a.share_prefix(), b.share_prefix()
+    sa = [pa.session() for _ in range(5)]
+    sb = [pb.session() for _ in range(5)]
+    k5 = fill(5 * batch * kv * 3 * dim, 40)
+    v5 = fill(5 * batch * kv * 3 * dim, 41)
+    K.sessions_append(sa, k5, v5, 3)
+    arr = (C.c_void_p * 5)(*[s._h for s in sb])
+    call(L.kivi_sessions_append, arr, 5, ptr(pin(k5)), k5.size, ptr(pin(v5)), v5.size, 3)
+    x1, y1 = fill(batch * kv * dim, 50), fill(batch * kv * dim, 51)
+    sa[0].append(x1, y1, 1)
+    call(L.kivi_session_append, sb[0]._h, ptr(pin(x1)), x1.size, ptr(pin(y1)), y1.size, 1)
+    q5 = fill(5 * batch * qh * dim, 60)
+    want = K.sessions_attention_batched(sa, q5, qh, 0.088)
+    po5 = pin(np.full(q5.size, np.nan, np.float32))
+    call(L.kivi_sessions_attention_batched, arr, 5, ptr(pin(q5)), q5.size, qh, scale, ptr(po5),
+         q5.size)
+    assert (po5.numpy() == want).all()
+    call(L.kivi_session_attention, sb[0]._h, ptr(pin(q)), q.size, qh, scale, ptr(po), q.size)
+    assert (po.numpy() == sa[0].attention(q, qh, 0.088)).all()
+
+
 def test_unaligned_device_inputs(K):
     """Device inputs at 4-byte (not 16-byte) offsets take the scalar paths and
     give the same bits as aligned ones (append) and the same attention."""
