@@ -211,6 +211,42 @@ __global__ void __launch_bounds__(256) append_small_kernel(Geom g, Store st, con
     const float *vin = values + (int64_t)s * seq * D;
     float *kres = st.kres + (int64_t)s * R * D;
     float *vres = st.vres + (int64_t)s * R * D;
+    if (seq == 1 && g.G == 32 && kres_len + 1 < R && D % 32 == 0 && D <= (int)blockDim.x) {
+        // One decode row, no key flush: thread = channel.  Every load of the
+        // step (key row, value row, the evicted window row) is issued first;
+        // the warp of a channel group quantizes the evicted row from registers
+        // (the arithmetic of quant_value_group_warp), and each thread then
+        // overwrites only the entries it read, so no barrier is needed.
+        const int d = threadIdx.x;
+        if (d >= D) return; // whole warps (D % 32 == 0)
+        const bool drop = vres_len == R;
+        const float kx = kin[d], vx = vin[d];
+        const float ex = drop ? vres[(int64_t)vhead * D + d] : 0.0f;
+        kres[(int64_t)kres_len * D + d] = kx;
+        if (drop) {
+            const int lane = d & 31, cg = d >> 5;
+            float mn = fminf(INFINITY, ex), mx = fmaxf(-INFINITY, ex);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            }
+            const float scale = scale_of(__fsub_rn(mx, mn), g.levels);
+            uint32_t *vc = st.vcodes + (int64_t)s * code_stride(g, st.cap) + (vq * g.nch + cg) * g.ipc;
+            float2 *vp = st.vparams + (int64_t)s * vparam_stride(g, st.cap);
+            if (lane == 0) vp[vq * g.nch + cg] = make_float2(scale, mn);
+            const Quantizer qz(mn, scale, g.levels);
+            const uint32_t code = qz.code(ex);
+            for (int w = 0; w < g.ipc; ++w) {
+                uint32_t part = lane / g.tpw == w ? code << ((lane % g.tpw) * g.bits) : 0u;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) part |= __shfl_xor_sync(0xffffffffu, part, o);
+                if (lane == 0) vc[w] = part;
+            }
+        }
+        vres[(int64_t)((vhead + vres_len) % R) * D + d] = vx;
+        return;
+    }
     __shared__ const float *rows[kMaxG];
 
     const int take1 = min(seq, R - kres_len);
