@@ -465,17 +465,18 @@ cudaError_t launch_copy_rows2(const RowCopy &j0, const RowCopy &j1, int n, int D
     return cudaGetLastError();
 }
 
-__global__ void __launch_bounds__(256) copy_f32_kernel(float *dst, const float *src, int64_t n,
+// One element (or float4) per thread, so every read of a source in mapped host
+// memory is in flight at once (a grid-stride loop would serialise its PCIe
+// round trips).
+__global__ void __launch_bounds__(256) copy_f32_kernel(float *__restrict__ dst,
+                                                       const float *__restrict__ src, int64_t n,
                                                        bool vec) {
-    const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (vec) {
-        const int64_t n4 = n / 4;
-        for (int64_t i = i0; i < n4; i += step)
-            reinterpret_cast<float4 *>(dst)[i] = reinterpret_cast<const float4 *>(src)[i];
-        for (int64_t i = 4 * n4 + i0; i < n; i += step) dst[i] = src[i];
-    } else {
-        for (int64_t i = i0; i < n; i += step) dst[i] = src[i];
+        if (i < n / 4) reinterpret_cast<float4 *>(dst)[i] = reinterpret_cast<const float4 *>(src)[i];
+        if (i < n % 4) dst[n - n % 4 + i] = src[n - n % 4 + i];
+    } else if (i < n) {
+        dst[i] = src[i];
     }
 }
 
@@ -483,9 +484,10 @@ cudaError_t launch_copy_f32(float *dst, const float *src, int64_t n, cudaStream_
     if (n <= 0) return cudaSuccess;
     ProfScope prof("copy_in", s);
     const bool vec = ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15u) == 0;
-    const int64_t units = vec ? (n + 3) / 4 : n;
-    const unsigned blocks = (unsigned)std::min<int64_t>((units + 255) / 256, 1184);
-    copy_f32_kernel<<<blocks, 256, 0, s>>>(dst, src, n, vec);
+    const int64_t units = vec ? std::max<int64_t>(n / 4, n % 4) : n;
+    const int64_t blocks = (units + 255) / 256;
+    if (blocks > 0x7fffffff) return cudaErrorInvalidValue;
+    copy_f32_kernel<<<(unsigned)blocks, 256, 0, s>>>(dst, src, n, vec);
     count_launch();
     return cudaGetLastError();
 }
