@@ -93,14 +93,22 @@ constexpr int kD = 128;
 constexpr int kTok = 32;                           // tokens per group = per S tile
 constexpr long long kWait = 2000000000LL;          // ~1 s at B200 clocks
 constexpr int kTile = 64;   // tokens per S tile (two groups): QK^T runs at N = 64
-// Tile j uses slot j % 3 of the key-operand ring, the value-operand ring and
-// the S / P buffers alike, so one commit after QK^T(j) both publishes S(j)
-// and frees key slot j % 3, and one commit after PV(j) both marks O current
-// and frees value slot j % 3 (two commits per tile rather than four).
-constexpr int kK = 3; // key operand tiles in flight (free once QK^T is done)
-constexpr int kV = 3; // value operand tiles in flight (free once PV is done)
-constexpr int kS = 3; // S / P tensor-memory buffers
-static_assert(kK == kS && kV == kS, "the free signals share s_full / pv_done");
+// One commit after QK^T(j) publishes S(j) in S buffer j % kS, one after PV(j)
+// marks O current; the same two barriers tell the converters when an operand
+// slot is free again: key slot j % kK once QK^T(j - kK) is done (s_full of
+// tile j - kK), value slot j % kV once PV(j - kV) is done (pv_done of tile
+// j - kV).  Both barriers complete tile by tile, so a converter at tile j
+// waiting for tile j - kK (<= kS) sees the right phase.
+#ifndef KIVI_SETS_KRING
+#define KIVI_SETS_KRING 3
+#endif
+#ifndef KIVI_SETS_VRING
+#define KIVI_SETS_VRING 3
+#endif
+constexpr int kK = KIVI_SETS_KRING; // key operand tiles in flight
+constexpr int kV = KIVI_SETS_VRING; // value operand tiles in flight
+constexpr int kS = 3;               // S / P tensor-memory buffers
+static_assert(kK >= 1 && kK <= kS && kV >= 1 && kV <= kS, "operand rings within the S ring");
 #ifndef KIVI_SETS_LAZY
 #define KIVI_SETS_LAZY 6
 #endif
@@ -459,16 +467,16 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
 
     // ---- query rows into tensor memory: Q'' = q 2^(E_d - e_row + 14) < 2^14,
     // hi/lo, lane = row.  All warps stage the rows through shared memory (the
-    // value-tile buffers, unused until the roles start): warp w takes rows
-    // w, w + 14, ..., each lane two float2 of a row (coalesced), the row bound
+    // operand rings, unused until the roles start): warp w takes rows w, w + 19,
+    // ..., each lane two float2 of a row (coalesced), the row bound
     // e_row comes from a warp max; the row's owner thread then moves its hi/lo
     // words into tensor memory.  Staged row r: hi words at r * kQRow, lo words
     // 256 bytes later; the 16-byte pad keeps the owners' 16-byte reads
     // conflict-free.
     constexpr int kQRow = 528;
-    uint32_t *qstage = reinterpret_cast<uint32_t *>(sm + kVbuf);
-    int *rowexp = reinterpret_cast<int *>(sm + kVbuf + 128 * kQRow); // [128]
-    static_assert(128 * kQRow + 512 <= kV * 32768, "query staging fits the value tiles");
+    uint32_t *qstage = reinterpret_cast<uint32_t *>(sm + kKbuf);
+    int *rowexp = reinterpret_cast<int *>(sm + kKbuf + 128 * kQRow); // [128]
+    static_assert(128 * kQRow + 512 <= (kK + kV) * 32768, "query staging fits the operand rings");
     for (int r = warp; r < 128; r += kSetThreads / 32) {
         const bool valid = r < rows_valid;
         float2 v0 = make_float2(0.0f, 0.0f), v1 = v0;
@@ -585,7 +593,7 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
                 umma_sweep<2>(o, pl, vh, id_pv, 1u);
                 umma_sweep<2>(o, ph, vl, id_pv, 1u);
             }
-            umma_commit_e(&pv_done[bj]); // also frees value slot bv == bj
+            umma_commit_e(&pv_done[bj]); // also frees value slot bv for tile j + kV
             return true;
         };
         // Issue order QK(0), QK(1), QK(2), PV(0), QK(3), PV(1), ...: softmax
@@ -608,7 +616,7 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
             umma_sweep<8>(sacc, tbase + kQH, kh, id_qk, 0u);
             umma_sweep<8>(sacc, tbase + kQL, kh, id_qk, 1u);
             umma_sweep<8>(sacc, tbase + kQH, kl, id_qk, 1u);
-            umma_commit_e(&s_full[bs]); // also frees key slot bk == bs
+            umma_commit_e(&s_full[bs]); // also frees key slot bk for tile j + kK
             if (j >= 2 && !pv(j - 2)) ok = false;
         }
         if (ok && nt >= 2) ok = pv(nt - 2);
@@ -642,7 +650,7 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
                 fac[r] = keys ? exp2i_(14 - kexp[8 * (u >> 5) + (u & 7)]) : exp2i_(14 - vexp[r]);
         }
         uint64_t *ready = keys ? k_ready : v_ready;
-        uint64_t *freed = keys ? s_full : pv_done; // QK^T / PV of the slot's last tile done
+        uint64_t *freed = keys ? s_full : pv_done; // QK^T / PV of tile j - nbuf done
         const int nbuf = keys ? kK : kV;
         bool ok = true;
         for (int j = 0; ok && j < nt; ++j) {
@@ -651,7 +659,7 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
             // the tile's buffer is free once QK^T (keys) or PV (values) of tile
             // j - nbuf is done
             if (!warp_wait(&full[st], (j / NS) & 1, 64u) ||
-                (j >= nbuf && !warp_wait(&freed[bb], ((j - nbuf) / nbuf) & 1, 64u))) {
+                (j >= nbuf && !warp_wait(&freed[(j - nbuf) % kS], ((j - nbuf) / kS) & 1, 64u))) {
                 ok = false;
                 break;
             }
