@@ -3,9 +3,9 @@
  *
  * This is the drop-in boundary for the public Rust API of kivi-cache v0.6.0
  * (bieli/kivi-cache-rs, exports at src/lib.rs:49-65).  A `kivi-cache-sys`
- * crate binds these symbols one-to-one and the safe
+ * crate binds these symbols one-to-one in an extern "C" block and the safe
  * crate keeps the reference signatures (KiviConfig, KiviCache, SharedPrefix,
- * RagSession, RuntimeKv, MemoryReport, budget math).
+ * RagSession, RuntimeKv, MemoryReport, budget math) on top of it.
  *
  * Conventions
  *  - Every fallible call returns int32_t: 0 (KIVI_OK) or a kivi_status code,
