@@ -103,11 +103,11 @@ def test_budget_byte_math_matches_oracle(bits, group, residual):
         for tokens in [0, 1, group, residual - 1, residual, residual + 1, 5 * residual + 7, 200_000]:
             assert K.layer_kv_bytes(cfg, heads, dim, tokens) == O.layer_kv_bytes(ocfg, heads, dim, tokens)
         assert K.marginal_bytes_per_layer(cfg, heads, dim) == O.marginal_bytes_per_layer(ocfg, heads, dim)
-    assert K.marginal_bytes_per_layer(K.KiviConfig(), 8, 128) == 1024  # README.md:176
+    assert K.marginal_bytes_per_layer(K.KiviConfig(), 8, 128) == 1024  # the reference README.md:176
 
 
 def test_agent_budget_planner_matches_readme():
-    """README.md:176-186 figures, tests/budget.rs:47-66"""
+    """the reference README.md:176-186 figures, tests/budget.rs:47-66"""
     import kivi_cache as K
 
     plan = K.AgentMemoryBudget.try_new(K.KiviConfig(), 32, 8, 128)

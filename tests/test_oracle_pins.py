@@ -519,7 +519,7 @@ def test_planner_bytes_match_live_cache():
 
 
 def test_marginal_rate_matches_one_key_flush_cycle():
-    """tests/budget.rs:84-91, budget.rs:349-364 (1024 B for 8 heads at d=128, README.md:176)"""
+    """tests/budget.rs:84-91, budget.rs:349-364 (1024 B for 8 heads at d=128, the reference README.md:176)"""
     cfg = O.KiviConfig()
     start = 128 * 40
     delta = O.layer_kv_bytes(cfg, 8, 128, start + 128) - O.layer_kv_bytes(cfg, 8, 128, start)
