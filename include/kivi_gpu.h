@@ -166,6 +166,13 @@ void kivi_profile_reset(void);
  * host can enqueue the launches that follow before the device reaches them
  * and each event pair brackets its kernel alone. */
 int32_t kivi_profile_hold(uint64_t microseconds, void *stream);
+/* Self-test of the bounded device waits (no counterpart in the reference):
+ * one warp waits, through the kernels' own bounded-wait path, on an mbarrier
+ * that nothing arrives at for about `microseconds` (1..100000) of device time,
+ * then gives up and records its flag.  Returns KIVI_ERR_CUDA with the flag
+ * (0x40000000) in the message when the give-up path works; the flag is then
+ * cleared and the device stays usable. */
+int32_t kivi_selftest_bounded_wait(uint64_t microseconds, kivi_error *err);
 
 /* ---------------------------------------------------------------- config.rs */
 

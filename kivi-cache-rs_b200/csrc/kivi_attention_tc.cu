@@ -118,13 +118,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return done != 0;
 }
 
-// Waits for the phase with the given parity; gives up after ~1 s, records the
-// failure in g_tc_error and returns false.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsigned code) {
+// Waits for the phase with the given parity; gives up after `limit` cycles
+// (~1 s by default), records the failure in g_tc_error and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsigned code,
+                                          long long limit = kWaitCycles) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try_wait(bar, parity)) {
-        if (clock64() - t0 > kWaitCycles) {
+        if (clock64() - t0 > limit) {
             atomicOr(&g_tc_error, code);
             return false;
         }
@@ -755,6 +756,27 @@ cudaError_t launch_attention_tc(const TcArgs &a, int bits, int nsets, cudaStream
     const bool two = a.GQ > 4;
     if (bits == 2) return two ? launch_tc<2, 2>(a, nsets, s) : launch_tc<2, 1>(a, nsets, s);
     return two ? launch_tc<4, 2>(a, nsets, s) : launch_tc<4, 1>(a, nsets, s);
+}
+
+namespace {
+// Self-test of the give-up path: one warp waits, with the kernels' own bounded
+// wait, on an mbarrier nothing arrives at; the wait runs out after `limit`
+// cycles and records kWaitProbeCode.  No copy or other thread is involved.
+__global__ void wait_probe_kernel(long long limit) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+    }
+    __syncwarp();
+    mbar_wait(&bar, 0, kWaitProbeCode, limit);
+}
+} // namespace
+
+cudaError_t launch_wait_probe(long long limit_cycles, cudaStream_t s) {
+    wait_probe_kernel<<<1, 32, 0, s>>>(limit_cycles);
+    count_launch();
+    return cudaGetLastError();
 }
 
 cudaError_t take_tc_error(unsigned int *out) {

@@ -807,6 +807,15 @@ int32_t kivi_profile_hold(uint64_t microseconds, void *stream) {
                                                                                           : KIVI_ERR_CUDA;
 }
 
+int32_t kivi_selftest_bounded_wait(uint64_t microseconds, kivi_error *err) {
+    if (microseconds == 0 || microseconds > 100000)
+        return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "bound must be 1..100000 us");
+    // clock64 counts SM cycles (at most ~2 GHz): 2000 per microsecond
+    CUDA_TRY(kivi::launch_wait_probe((long long)microseconds * 2000, nullptr), "wait self-test");
+    CUDA_TRY(cudaStreamSynchronize(nullptr), "wait self-test");
+    return check_device_waits(err);
+}
+
 void kivi_profile_reset(void) {
     std::lock_guard<std::mutex> lk(kivi::g_prof_mu);
     kivi::prof_drain_locked();

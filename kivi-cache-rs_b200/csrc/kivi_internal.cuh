@@ -245,6 +245,11 @@ bool attention_tc_supported(const Geom &g, int gq);
 cudaError_t plan_attention_tc(int bits, int gq, int64_t nstreams, int64_t main_groups,
                               int64_t *per, int *nslots);
 cudaError_t launch_attention_tc(const TcArgs &a, int bits, int nsets, cudaStream_t s);
+// Flag a bounded device wait records when it gives up in the self-test.
+constexpr unsigned kWaitProbeCode = 0x40000000u;
+// One warp waits on an mbarrier nothing arrives at for limit_cycles, then gives
+// up through the kernels' bounded-wait path (sets kWaitProbeCode).
+cudaError_t launch_wait_probe(long long limit_cycles, cudaStream_t s);
 // tcgen05 attention of many query sets over a frozen prefix's packed main
 // region (kivi_attention_sets.cu).  CTA (chunk, stream, z) takes groups
 // [chunk*per, (chunk+1)*per) of its stream and the query rows of sets

@@ -144,6 +144,7 @@ def lib():
         "kivi_cache_seal": ([P, e], i32),
         "kivi_sessions_append_dev": ([P, sz, P, P, sz, P, e], i32),
         "kivi_sessions_append": ([P, sz, fp, sz, fp, sz, sz, e], i32),
+        "kivi_selftest_bounded_wait": ([sz, e], i32),
         "kivi_session_reserve": ([P, sz, e], i32),
         "kivi_packed_partials_floats": ([sz, sz], sz),
         "kivi_cache_attention_partial_packed_dev": ([P, P, sz, f32, P, P, e], i32),

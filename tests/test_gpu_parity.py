@@ -866,6 +866,27 @@ def test_host_calls_pinned_buffers_match_pageable(K):
     assert (po.numpy() == sa[0].attention(q, qh, 0.088)).all()
 
 
+def test_bounded_wait_gives_up_and_the_device_stays_usable(K):
+    """A bounded device wait that nothing satisfies (an mbarrier without
+    arrivals, ~2 ms bound) gives up, records its flag and returns: the call
+    reports KIVI_ERR_CUDA with that flag, the flag is cleared, and attention
+    afterwards still matches the oracle."""
+    import ctypes as C
+
+    err = K._Err()
+    rc = K.lib().kivi_selftest_bounded_wait(2000, C.byref(err))
+    assert rc != 0 and "gave up waiting" in err.message.decode()
+    assert str(0x40000000) in err.message.decode()
+    err2 = K._Err()
+    assert K.lib().kivi_selftest_bounded_wait(0, C.byref(err2)) != 0  # bound checked first
+    assert "bound" in err2.message.decode()
+    cache, ocache = pair(K, 2, 32, 128, 1, 2, 128)
+    keys, values, _ = synthetic_kv(3, 1, 2, 300, 128)
+    append_both(cache, ocache, keys, values, 300)
+    q = fill(4 * 128, 9)
+    assert_attention_close(cache.attention(q, 4, 0.088), ocache.attention(q, 4, 0.088))
+
+
 def test_unaligned_device_inputs(K):
     """Device inputs at 4-byte (not 16-byte) offsets take the scalar paths and
     give the same bits as aligned ones (append) and the same attention."""
