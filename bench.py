@@ -467,21 +467,17 @@ class RagWorkload:
         L = K.lib()
         fp = ctypes.POINTER(ctypes.c_float)
         err = K._Err()
-        rc = L.kivi_sessions_append(
+        rc = L.kivi_sessions_decode_batched(
             self._arr, self.S, ctypes.cast(self.hk.data_ptr(), fp), self.hk.numel(),
-            ctypes.cast(self.hv.data_ptr(), fp), self.hv.numel(), 1, ctypes.byref(err))
-        if rc:
-            raise K.KiviError(err.code, err.a, err.b, None, err.message.decode())
-        rc = L.kivi_sessions_attention_batched(
-            self._arr, self.S, ctypes.cast(self.hq.data_ptr(), fp), self.hq.numel(), self.Hq,
+            ctypes.cast(self.hv.data_ptr(), fp), self.hv.numel(),
+            ctypes.cast(self.hq.data_ptr(), fp), self.hq.numel(), self.Hq,
             ctypes.c_float(self.scale), ctypes.cast(self.hout.data_ptr(), fp), self.hout.numel(),
             ctypes.byref(err))
         if rc:
             raise K.KiviError(err.code, err.a, err.b, None, err.message.decode())
 
-    e2e_api = ("kivi_sessions_append + kivi_sessions_attention_batched (RagSession::append and "
-               "::attention of every session, one upload and one synchronisation each), pinned "
-               "host buffers")
+    e2e_api = ("kivi_sessions_decode_batched (RagSession::append then ::attention of every "
+               "session, one upload and one synchronisation), pinned host buffers")
 
     def io_bytes(self):
         return (self.hk.numel() + self.hv.numel() + self.hq.numel()) * 4, self.hout.numel() * 4

@@ -357,6 +357,19 @@ int32_t kivi_sessions_attention_batched_dev(const kivi_session *const *sessions,
                                             const float *d_queries, uint64_t num_q_heads,
                                             float scale, float *d_out, void *stream,
                                             kivi_error *err);
+/* One decode step of n sessions of one prefix: every session appends one
+ * token (keys/values as kivi_sessions_append with seq_len 1), then attends
+ * (queries/out as kivi_sessions_attention_batched).  Equal to those two calls,
+ * with one upload and one synchronisation.  Errors follow
+ * RuntimeKv::decode's order (runtime.rs:53-55) per session: an append error
+ * returns before anything changes; a query error returns after the appends.
+ * No counterpart in the reference, whose RagSession appends and attends one
+ * session at a time (prefix.rs:173-226, prefix.rs:228-289). */
+int32_t kivi_sessions_decode_batched(kivi_session *const *sessions, uint64_t n,
+                                     const float *keys, uint64_t keys_len, const float *values,
+                                     uint64_t values_len, const float *queries,
+                                     uint64_t queries_len, uint64_t num_q_heads, float scale,
+                                     float *out, uint64_t out_len, kivi_error *err);
 
 /* ---------------------------------------------------------------- quant.rs */
 

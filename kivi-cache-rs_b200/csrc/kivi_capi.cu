@@ -366,9 +366,12 @@ int32_t ensure_capacity(KvState &s, uint64_t tokens, cudaStream_t stream, kivi_e
     return KIVI_OK;
 }
 
-// Appends [n][seq][D] device rows (cache.rs:186-214, 382-484).
+// Appends [n][seq][D] device rows (cache.rs:186-214, 382-484); `qc` is a
+// query copy that rides in the append kernel (a launch of its own when the
+// append is a flush-sized one).
 int32_t append_device(KvState &s, const float *dk, const float *dv, uint64_t seq,
-                      cudaStream_t stream, kivi_error *err) {
+                      cudaStream_t stream, kivi_error *err,
+                      const kivi::QueryCopy &qc = kivi::QueryCopy{}) {
     if (seq == 0) return KIVI_OK;
     const uint64_t R = s.cfg.residual_length, G = s.cfg.group_size;
     const int n = (int)s.n();
@@ -394,9 +397,12 @@ int32_t append_device(KvState &s, const float *dk, const float *dv, uint64_t seq
     if (seq < R) {
         CUDA_TRY(kivi::launch_append_small(g, s.st, n, dk, dv, (int)seq, (int)s.kres_len,
                                            (int64_t)s.kq, (int)s.vres_len, (int64_t)s.vq,
-                                           (int)s.vhead, stream),
+                                           (int)s.vhead, stream, qc),
                  "append");
     } else {
+        if (qc.per)
+            CUDA_TRY(kivi::launch_copy_f32(qc.dst, qc.src, (int64_t)n * qc.per, stream),
+                     "query copy");
         // Keys: flush every complete R-block of [residual ++ input]
         // (cache.rs:382-405).  Values, seq >= R: quantize the window and
         // input[0, seq-R) (cache.rs:434-454).  (One fused launch of both ran
@@ -1062,8 +1068,8 @@ int32_t kivi_cache_decode(kivi_cache *h, const float *key, uint64_t key_len, con
     }
     // one upload of key, value and query, both launches, one synchronisation.
     // Mapped pinned buffers skip the copy engine (each copy costs ~20 us of
-    // fixed latency): the append kernel reads key and value from host memory,
-    // a copy kernel brings the query into device memory (the attention kernels
+    // fixed latency): the append kernel reads key and value from host memory
+    // and also brings the query into device memory (the attention kernels
     // read it many times), and the merge writes the output into host memory.
     std::lock_guard<std::mutex> lk(h->mu);
     DeviceGuard dg(h->s.device);
@@ -1074,9 +1080,15 @@ int32_t kivi_cache_decode(kivi_cache *h, const float *key, uint64_t key_len, con
     const float *dk = nullptr, *dv = nullptr;
     CUDA_TRY(input_once(key, h->stage.as<float>(), kv, h->stream, &dk), "decode H2D");
     CUDA_TRY(input_once(value, h->stage.as<float>(kb), kv, h->stream, &dv), "decode H2D");
-    CUDA_TRY(input_staged(query, dq, n, h->stream), "decode H2D");
+    kivi::QueryCopy qc;
+    const float *mq = mapped_host(query);
+    const int64_t per = (int64_t)(Hq / h->s.H * h->s.D);
+    if (mq && kivi::append_query_fusable(dq, mq, per))
+        qc = kivi::QueryCopy{dq, mq, (int)per};
+    else
+        CUDA_TRY(input_staged(query, dq, n, h->stream), "decode H2D");
     float *dout = output_target(out, stage_out, true);
-    int32_t rc = append_device(h->s, dk, dv, 1, h->stream, err);
+    int32_t rc = append_device(h->s, dk, dv, 1, h->stream, err, qc);
     if (rc) return rc;
     rc = run_attention(h->s, nullptr, 1, dq, Hq, scale, dout, nullptr, nullptr, h->part, h->stream,
                        err);
@@ -1490,18 +1502,14 @@ int32_t kivi_session_reserve(kivi_session *s, uint64_t tokens, kivi_error *err) 
     return set_err(err, KIVI_OK);
 }
 
-int32_t kivi_sessions_append_dev(kivi_session *const *ss, uint64_t nsess, const float *dk,
-                                 const float *dv, uint64_t seq, void *stream, kivi_error *err) {
-    if (!ss || nsess == 0 || !ss[0]) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "no sessions");
-    if (seq == 0) return set_err(err, KIVI_OK);
-    if (!dk || !dv) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null input");
+// Appends seq device rows to each of nsess sessions of one prefix on `st`
+// (prefix.rs:173-226 per session); `qc` (per floats per (session, stream))
+// copies the sessions' query rows in the same launches.
+static int32_t sessions_append_launch(kivi_session *const *ss, uint64_t nsess, const float *dk,
+                                      const float *dv, uint64_t seq, cudaStream_t st,
+                                      kivi_error *err, const kivi::QueryCopy &qc = kivi::QueryCopy{}) {
     const kivi_prefix *p = ss[0]->prefix;
-    for (uint64_t i = 0; i < nsess; ++i)
-        if (!ss[i] || ss[i]->prefix != p)
-            return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "sessions must share one prefix");
     const uint64_t n = p->s.n(), D = p->s.D;
-    DeviceGuard dg(p->s.device);
-    cudaStream_t st = pick(stream, ss[0]->stream);
     for (uint64_t i = 0; i < nsess; ++i) {
         int32_t rc = session_reserve(ss[i], seq, st, err);
         if (rc) return rc;
@@ -1517,11 +1525,32 @@ int32_t kivi_sessions_append_dev(kivi_session *const *ss, uint64_t nsess, const 
             sa.cap[i] = (int64_t)s->cap;
         }
         const uint64_t off = s0 * n * seq * D;
+        kivi::QueryCopy q = qc;
+        if (q.per) {
+            q.dst += s0 * n * q.per;
+            q.src += s0 * n * q.per;
+        }
         CUDA_TRY(kivi::launch_suffix_append(sa, dk + off, dv + off, (int)ns, (int)n, (int64_t)seq,
-                                            (int)D, st),
+                                            (int)D, st, q),
                  "sessions append");
     }
     for (uint64_t i = 0; i < nsess; ++i) ss[i]->len += seq;
+    return KIVI_OK;
+}
+
+int32_t kivi_sessions_append_dev(kivi_session *const *ss, uint64_t nsess, const float *dk,
+                                 const float *dv, uint64_t seq, void *stream, kivi_error *err) {
+    if (!ss || nsess == 0 || !ss[0]) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "no sessions");
+    if (seq == 0) return set_err(err, KIVI_OK);
+    if (!dk || !dv) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null input");
+    const kivi_prefix *p = ss[0]->prefix;
+    for (uint64_t i = 0; i < nsess; ++i)
+        if (!ss[i] || ss[i]->prefix != p)
+            return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "sessions must share one prefix");
+    DeviceGuard dg(p->s.device);
+    cudaStream_t st = pick(stream, ss[0]->stream);
+    int32_t rc = sessions_append_launch(ss, nsess, dk, dv, seq, st, err);
+    if (rc) return rc;
     CUDA_TRY(mark_dev(p->batch_done, st), "sessions append");
     return set_err(err, KIVI_OK);
 }
@@ -1718,6 +1747,67 @@ int32_t kivi_sessions_attention_batched(const kivi_session *const *ss, uint64_t 
     if (rc) return rc;
     CUDA_TRY(output_done(out, dout, stage_out, total, lead->stream), "batched D2H");
     CUDA_TRY(cudaStreamSynchronize(lead->stream), "batched attention");
+    return set_err(err, KIVI_OK);
+}
+
+int32_t kivi_sessions_decode_batched(kivi_session *const *ss, uint64_t nsess, const float *keys,
+                                     uint64_t keys_len, const float *values, uint64_t values_len,
+                                     const float *queries, uint64_t queries_len, uint64_t Hq,
+                                     float scale, float *out, uint64_t out_len, kivi_error *err) {
+    // Per session, runtime.rs:53-55's order: append(key, value, 1)? then
+    // attention(query); a query the attention rejects leaves the appends done.
+    if (!ss || nsess == 0 || !ss[0]) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "no sessions");
+    const KvState &p = ss[0]->prefix->s;
+    const uint64_t kv = nsess * p.n() * p.D;
+    if (keys_len != kv || values_len != kv || !keys || !values)
+        return kivi_sessions_append(ss, nsess, keys, keys_len, values, values_len, 1, err);
+    for (uint64_t i = 0; i < nsess; ++i)
+        if (!ss[i] || ss[i]->prefix != ss[0]->prefix)
+            return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "sessions must share one prefix");
+    kivi_error qerr{};
+    int32_t qrc = check_query(p, Hq, 0, false, &qerr);
+    const uint64_t total = nsess * p.B * Hq * p.D;
+    if (!qrc && queries_len != total) qrc = set_err(&qerr, KIVI_ERR_SHAPE, total, queries_len);
+    if (!qrc && out_len != total) qrc = set_err(&qerr, KIVI_ERR_SHAPE, total, out_len);
+    if (!qrc && (!queries || !out)) qrc = set_msg(&qerr, KIVI_ERR_INVALID_ARGUMENT, "null buffer");
+    if (qrc) {
+        int32_t rc = kivi_sessions_append(ss, nsess, keys, keys_len, values, values_len, 1, err);
+        if (rc) return rc;
+        if (err) *err = qerr;
+        return qrc;
+    }
+    // One upload of keys, values and queries, the append and attention
+    // launches, one synchronisation; mapped pinned buffers as in
+    // kivi_cache_decode (the suffix-append kernel also brings the queries in).
+    kivi_session *lead = ss[0];
+    std::lock_guard<std::mutex> lk(lead->mu);
+    DeviceGuard dg(p.device);
+    for (uint64_t i = 0; i < nsess; ++i) CUDA_TRY(wait_session(lead->stream, ss[i]), "sessions decode");
+    if (lead->prefix->batch_done)
+        CUDA_TRY(wait_dev(lead->stream, lead->prefix->batch_done), "sessions decode");
+    const size_t kb = kv * sizeof(float), qb = total * sizeof(float);
+    CUDA_TRY(lead->stage.ensure(2 * kb + 2 * qb), "sessions decode staging");
+    float *dq = lead->stage.as<float>(2 * kb), *stage_out = lead->stage.as<float>(2 * kb + qb);
+    const float *dk = nullptr, *dv = nullptr;
+    CUDA_TRY(input_once(keys, lead->stage.as<float>(), kv, lead->stream, &dk), "sessions decode H2D");
+    CUDA_TRY(input_once(values, lead->stage.as<float>(kb), kv, lead->stream, &dv),
+             "sessions decode H2D");
+    kivi::QueryCopy qc;
+    const float *mq = mapped_host(queries);
+    const int64_t per = (int64_t)(Hq / p.H * p.D);
+    if (mq && kivi::append_query_fusable(dq, mq, per))
+        qc = kivi::QueryCopy{dq, mq, (int)per};
+    else
+        CUDA_TRY(input_staged(queries, dq, total, lead->stream), "sessions decode H2D");
+    float *dout = output_target(out, stage_out, true);
+    int32_t rc = sessions_append_launch(ss, nsess, dk, dv, 1, lead->stream, err, qc);
+    if (rc) return rc;
+    rc = sessions_attention_dev(ss, nsess, dq, Hq, scale, dout, lead->stream, lead->part, err);
+    if (rc) return rc;
+    CUDA_TRY(output_done(out, dout, stage_out, total, lead->stream), "sessions decode D2H");
+    CUDA_TRY(cudaStreamSynchronize(lead->stream), "sessions decode");
+    rc = check_device_waits(err);
+    if (rc) return rc;
     return set_err(err, KIVI_OK);
 }
 

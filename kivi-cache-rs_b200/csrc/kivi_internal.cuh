@@ -114,11 +114,23 @@ struct ProfScope {
 };
 
 // ---------------------------------------------------------------- quantize
+// A step's query rows copied by the append kernel: CTA (stream) s copies the
+// `per` floats at src + s*per (its GQA group of query heads, contiguous in
+// [B][Hq][D]) to dst + s*per.  per % 4 == 0, per / 4 <= 256 and both pointers
+// 16-byte aligned (append_query_fusable); per == 0 copies nothing.
+struct QueryCopy {
+    float *dst = nullptr;
+    const float *src = nullptr;
+    int per = 0;
+};
+bool append_query_fusable(const float *dst, const float *src, int64_t per);
 // Decode-path append (seq < R): key residual copy (+ flush when it fills) and
-// value window eviction/insert for every stream, one CTA per stream.
+// value window eviction/insert for every stream, one CTA per stream, plus the
+// optional query copy `qc`.
 cudaError_t launch_append_small(const Geom &g, const Store &st, int n, const float *keys,
                                 const float *values, int seq, int kres_len, int64_t kq,
-                                int vres_len, int64_t vq, int vhead, cudaStream_t s);
+                                int vres_len, int64_t vq, int vhead, cudaStream_t s,
+                                const QueryCopy &qc = QueryCopy{});
 // Quantize `ngroups` key groups per stream from the combined timeline
 // [residual rows 0..nres) ++ [input rows 0..in_seq) into groups out_group0...
 cudaError_t launch_key_groups(const Geom &g, const Store &st, int n, const float *res, int nres,
@@ -153,8 +165,11 @@ struct SuffixAppend {
     int64_t len[kMaxSessionsPerLaunch];
     int64_t cap[kMaxSessionsPerLaunch];
 };
+// Appends seq rows of every (set, stream) to the sessions' fp32 suffixes;
+// `qc` copies each (set, stream)'s query rows at ((set * nstreams + stream) * per).
 cudaError_t launch_suffix_append(const SuffixAppend &a, const float *k, const float *v,
-                                 int nsets, int nstreams, int64_t seq, int D, cudaStream_t s);
+                                 int nsets, int nstreams, int64_t seq, int D, cudaStream_t s,
+                                 const QueryCopy &qc = QueryCopy{});
 cudaError_t launch_copy_rows(float *dst, int64_t dst_stream_rows, int64_t dst_head,
                              int64_t dst_off, int64_t ring, const float *src, int64_t src_seq,
                              int64_t src_off, int64_t count, int n, int D, cudaStream_t s);

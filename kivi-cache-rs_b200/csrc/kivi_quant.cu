@@ -204,13 +204,21 @@ constexpr int kMaxG = 256; // largest group handled by the row-pointer tables be
 __global__ void __launch_bounds__(256) append_small_kernel(Geom g, Store st, const float *keys,
                                                            const float *values, int seq,
                                                            int kres_len, int64_t kq, int vres_len,
-                                                           int64_t vq, int vhead) {
+                                                           int64_t vq, int vhead, QueryCopy qc) {
     const int s = blockIdx.x;
     const int D = g.D, R = g.R;
     const float *kin = keys + (int64_t)s * seq * D;
     const float *vin = values + (int64_t)s * seq * D;
     float *kres = st.kres + (int64_t)s * R * D;
     float *vres = st.vres + (int64_t)s * R * D;
+    // The query copy's load is issued with the step's other loads and its
+    // store made last, so that a query in mapped host memory costs no PCIe
+    // round trip of its own.
+    const bool qon = (int)threadIdx.x < qc.per / 4;
+    float4 qv = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (qon) qv = reinterpret_cast<const float4 *>(qc.src + (int64_t)s * qc.per)[threadIdx.x];
+    float4 *qdst = qon ? reinterpret_cast<float4 *>(qc.dst + (int64_t)s * qc.per) + threadIdx.x
+                       : nullptr;
     if (seq == 1 && g.G == 32 && kres_len + 1 < R && D % 32 == 0 && D <= (int)blockDim.x) {
         // One decode row, no key flush: thread = channel.  Every load of the
         // step (key row, value row, the evicted window row) is issued first;
@@ -218,7 +226,10 @@ __global__ void __launch_bounds__(256) append_small_kernel(Geom g, Store st, con
         // (the arithmetic of quant_value_group_warp), and each thread then
         // overwrites only the entries it read, so no barrier is needed.
         const int d = threadIdx.x;
-        if (d >= D) return; // whole warps (D % 32 == 0)
+        if (d >= D) { // whole warps (D % 32 == 0)
+            if (qon) *qdst = qv;
+            return;
+        }
         const bool drop = vres_len == R;
         const float kx = kin[d], vx = vin[d];
         const float ex = drop ? vres[(int64_t)vhead * D + d] : 0.0f;
@@ -245,8 +256,10 @@ __global__ void __launch_bounds__(256) append_small_kernel(Geom g, Store st, con
             }
         }
         vres[(int64_t)((vhead + vres_len) % R) * D + d] = vx;
+        if (qon) *qdst = qv;
         return;
     }
+    if (qon) *qdst = qv;
     __shared__ const float *rows[kMaxG];
 
     const int take1 = min(seq, R - kres_len);
@@ -357,14 +370,22 @@ __global__ void copy_rows2_kernel(RowCopy j0, RowCopy j1, int D) {
 }
 
 __global__ void suffix_append_kernel(const SuffixAppend a, const float *k, const float *v,
-                                     int nstreams, int64_t seq, int D) {
+                                     int nstreams, int64_t seq, int D, QueryCopy qc) {
     const int z = blockIdx.z, s = blockIdx.y;
     const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (e >= seq * D) return;
-    const int64_t src = (((int64_t)z * nstreams + s) * seq) * D + e;
-    const int64_t dst = ((int64_t)s * a.cap[z] + a.len[z]) * D + e;
-    a.k[z][dst] = k[src];
-    a.v[z][dst] = v[src];
+    // Block 0 of each (set, stream) also copies that stream's query rows, the
+    // load issued with the row loads and the store made last.
+    const bool qon = blockIdx.x == 0 && (int)threadIdx.x < qc.per / 4;
+    const int64_t qo = ((int64_t)z * nstreams + s) * (qc.per / 4) + threadIdx.x;
+    float4 qv = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (qon) qv = reinterpret_cast<const float4 *>(qc.src)[qo];
+    if (e < seq * D) {
+        const int64_t src = (((int64_t)z * nstreams + s) * seq) * D + e;
+        const int64_t dst = ((int64_t)s * a.cap[z] + a.len[z]) * D + e;
+        a.k[z][dst] = k[src];
+        a.v[z][dst] = v[src];
+    }
+    if (qon) reinterpret_cast<float4 *>(qc.dst)[qo] = qv;
 }
 
 // ---------------------------------------------------------------- dequantize
@@ -425,13 +446,20 @@ inline unsigned blocks_for(int64_t n, int t) { return (unsigned)((n + t - 1) / t
 
 cudaError_t launch_append_small(const Geom &g, const Store &st, int n, const float *keys,
                                 const float *values, int seq, int kres_len, int64_t kq,
-                                int vres_len, int64_t vq, int vhead, cudaStream_t s) {
+                                int vres_len, int64_t vq, int vhead, cudaStream_t s,
+                                const QueryCopy &qc) {
     if (n <= 0 || seq <= 0) return cudaSuccess;
+    if (qc.per != 0 && !append_query_fusable(qc.dst, qc.src, qc.per)) return cudaErrorInvalidValue;
     ProfScope prof("append_small", s);
     append_small_kernel<<<n, 256, 0, s>>>(g, st, keys, values, seq, kres_len, kq, vres_len, vq,
-                                          vhead);
+                                          vhead, qc);
     count_launch();
     return cudaGetLastError();
+}
+
+bool append_query_fusable(const float *dst, const float *src, int64_t per) {
+    return dst && src && per > 0 && per % 4 == 0 && per / 4 <= 256 &&
+           ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15u) == 0;
 }
 
 cudaError_t launch_key_groups(const Geom &g, const Store &st, int n, const float *res, int nres,
@@ -493,12 +521,14 @@ cudaError_t launch_copy_f32(float *dst, const float *src, int64_t n, cudaStream_
 }
 
 cudaError_t launch_suffix_append(const SuffixAppend &a, const float *k, const float *v,
-                                 int nsets, int nstreams, int64_t seq, int D, cudaStream_t s) {
+                                 int nsets, int nstreams, int64_t seq, int D, cudaStream_t s,
+                                 const QueryCopy &qc) {
     if (nsets <= 0 || seq <= 0) return cudaSuccess;
     if (nsets > kMaxSessionsPerLaunch) return cudaErrorInvalidValue;
     ProfScope prof("suffix_append", s);
+    if (qc.per != 0 && !append_query_fusable(qc.dst, qc.src, qc.per)) return cudaErrorInvalidValue;
     suffix_append_kernel<<<dim3(blocks_for(seq * D, 256), nstreams, nsets), 256, 0, s>>>(
-        a, k, v, nstreams, seq, D);
+        a, k, v, nstreams, seq, D, qc);
     count_launch();
     return cudaGetLastError();
 }

@@ -144,6 +144,7 @@ def lib():
         "kivi_cache_seal": ([P, e], i32),
         "kivi_sessions_append_dev": ([P, sz, P, P, sz, P, e], i32),
         "kivi_sessions_append": ([P, sz, fp, sz, fp, sz, sz, e], i32),
+        "kivi_sessions_decode_batched": ([P, sz, fp, sz, fp, sz, fp, sz, sz, f32, fp, sz, e], i32),
         "kivi_selftest_bounded_wait": ([sz, e], i32),
         "kivi_session_reserve": ([P, sz, e], i32),
         "kivi_packed_partials_floats": ([sz, sz], sz),
@@ -654,6 +655,26 @@ def sessions_append(sessions, keys, values, seq_len):
     v, vp = _f32(values)
     err = _Err()
     _check(lib().kivi_sessions_append(arr, n, kp, k.size, vp, v.size, seq_len, C.byref(err)), err)
+
+
+def sessions_decode_batched(sessions, keys, values, queries, num_q_heads, scale):
+    """One decode step of every session of one prefix from host memory: each
+    appends one token (keys/values [n, batch, num_kv_heads, 1, head_dim]) and
+    then attends (queries [n, batch, num_q_heads, head_dim]); equal to
+    sessions_append(..., 1) followed by sessions_attention_batched, with one
+    synchronisation.  Returns the outputs, shaped like the queries."""
+    n = len(sessions)
+    arr = (C.c_void_p * n)(*[s._h for s in sessions])
+    k, kp = _f32(keys)
+    v, vp = _f32(values)
+    q, qp = _f32(queries)
+    out = np.empty(q.size, np.float32)
+    err = _Err()
+    _check(lib().kivi_sessions_decode_batched(arr, n, kp, k.size, vp, v.size, qp, q.size,
+                                              num_q_heads, C.c_float(scale),
+                                              out.ctypes.data_as(C.POINTER(C.c_float)), out.size,
+                                              C.byref(err)), err)
+    return out
 
 
 def sessions_append_dev(sessions, d_keys, d_values, seq_len, stream=None):

@@ -730,6 +730,92 @@ def test_batched_session_append_equals_per_session_append(K):
         assert max_abs(one, ref) <= ATOL and rel_l2(one, ref) <= RTOL_L2, i
 
 
+@pytest.mark.parametrize("n", [2, 6])
+def test_batched_session_decode_equals_append_then_attention(K, n):
+    """kivi_sessions_decode_batched equals kivi_sessions_append(seq 1) followed
+    by kivi_sessions_attention_batched bit for bit, step after step, from
+    pageable and from mapped pinned buffers (aligned queries ride in the
+    suffix-append kernel, a misaligned one takes the copy kernel), for the
+    decode kernel (2 sessions) and the tcgen05 multi-set kernel (6); the
+    outputs match the oracle's RagSession::attention."""
+    torch = pytest.importorskip("torch")
+    import ctypes as C
+
+    kv, qh, dim, doc = 4, 16, 128, 2100
+    keys, values, _ = synthetic_kv(7, 1, kv, doc, dim)
+    cache, ocache = pair(K, 2, 32, 128, 1, kv, dim)
+    append_both(cache, ocache, keys, values, doc)
+    prefix, oprefix = cache.share_prefix(), ocache.share_prefix()
+    rng = np.random.default_rng(11)
+    two = [prefix.session() for _ in range(n)]
+    one = [prefix.session() for _ in range(n)]
+    pinned = [prefix.session() for _ in range(n)]
+    oracle = [oprefix.session() for _ in range(n)]
+    x = rng.standard_normal((n, 1, kv, 5, dim), dtype=np.float32)
+    for group in (two, one, pinned):
+        K.sessions_append(group, x, x, 5)
+    for i in range(n):
+        oracle[i].append(x[i].reshape(-1), x[i].reshape(-1), 5)
+    scale = np.float32(1.0) / np.sqrt(np.float32(dim))
+    fp = C.POINTER(C.c_float)
+    arr = (C.c_void_p * n)(*[s._h for s in pinned])
+    for step in range(4):
+        k = rng.standard_normal((n, 1, kv, 1, dim), dtype=np.float32)
+        v = rng.standard_normal((n, 1, kv, 1, dim), dtype=np.float32)
+        q = rng.standard_normal((n, 1, qh, dim), dtype=np.float32)
+        K.sessions_append(two, k, v, 1)
+        want = K.sessions_attention_batched(two, q, qh, scale)
+        got = K.sessions_decode_batched(one, k, v, q, qh, scale)
+        assert (got == want).all(), step
+        pk, pv = (torch.from_numpy(np.ascontiguousarray(t).reshape(-1)).pin_memory() for t in (k, v))
+        off = step % 2  # odd steps: a query 4 bytes past a 16-byte boundary
+        qbuf = torch.full((q.size + off,), float("nan")).pin_memory()
+        qbuf[off:] = torch.from_numpy(q.reshape(-1))
+        po = torch.full((q.size,), float("nan")).pin_memory()
+        err = K._Err()
+        rc = K.lib().kivi_sessions_decode_batched(
+            arr, n, C.cast(pk.data_ptr(), fp), k.size, C.cast(pv.data_ptr(), fp), v.size,
+            C.cast(qbuf[off:].data_ptr(), fp), q.size, qh, C.c_float(scale),
+            C.cast(po.data_ptr(), fp), q.size, C.byref(err))
+        assert rc == 0, err.message
+        assert (po.numpy() == want).all(), step
+        for i in range(n):
+            oracle[i].append(k[i].reshape(-1), v[i].reshape(-1), 1)
+    want = want.reshape(n, -1)
+    for i in range(n):
+        assert one[i].question_tokens() == pinned[i].question_tokens() == 9
+        ref = oracle[i].attention(q[i].reshape(-1), qh, scale)
+        assert max_abs(want[i], ref) <= ATOL and rel_l2(want[i], ref) <= RTOL_L2, i
+
+
+def test_batched_session_decode_error_order(K):
+    """kivi_sessions_decode_batched: a bad key/value length is the append's
+    Shape error with nothing appended; a query the attention rejects
+    (QueryHeads, Shape) is reported after every session appended its token."""
+    cache = K.KiviCache(K.KiviConfig.try_new(2, 32, 128), 1, 2, 128)
+    x = np.ones(2 * 64 * 128, np.float32)
+    cache.append(x, x, 64)
+    prefix = cache.share_prefix()
+    ss = [prefix.session() for _ in range(3)]
+    kv = np.ones(3 * 2 * 128, np.float32)
+    q = np.ones(3 * 4 * 128, np.float32)
+    with pytest.raises(K.KiviError) as e:
+        K.sessions_decode_batched(ss, kv[:-1], kv, q, 4, 0.1)
+    assert (e.value.variant, e.value.a, e.value.b) == ("Shape", kv.size, kv.size - 1)
+    assert all(s.question_tokens() == 0 for s in ss)
+    with pytest.raises(K.KiviError) as e:
+        K.sessions_decode_batched(ss, kv, kv, np.ones(3 * 3 * 128, np.float32), 3, 0.1)
+    assert e.value.variant == "QueryHeads"
+    assert all(s.question_tokens() == 1 for s in ss)
+    with pytest.raises(K.KiviError) as e:
+        K.sessions_decode_batched(ss, kv, kv, q[:-1], 4, 0.1)
+    assert (e.value.variant, e.value.a, e.value.b) == ("Shape", q.size, q.size - 1)
+    assert all(s.question_tokens() == 2 for s in ss)
+    out = K.sessions_decode_batched(ss, kv, kv, q, 4, 0.1)
+    assert all(s.question_tokens() == 3 for s in ss)
+    assert np.isfinite(out).all()
+
+
 def test_batched_host_session_append_checks_shapes(K):
     """kivi_sessions_append: Shape{n*B*H*seq*D, len} before any mutation."""
     cache = K.KiviCache(K.KiviConfig.try_new(2, 32, 128), 1, 2, 128)
@@ -791,7 +877,13 @@ def test_decode_pinned_buffers_match_pageable(K):
         k, v = fill(batch * kv * dim, 10 + step), fill(batch * kv * dim, 60 + step)
         q = fill(batch * qh * dim, 110 + step)
         want = a.decode(k, v, q, qh, scale)
-        pk, pv, pq = (torch.from_numpy(t).pin_memory() for t in (k, v, q))
+        pk, pv = (torch.from_numpy(t).pin_memory() for t in (k, v))
+        # odd steps: a query 4 bytes past a 16-byte boundary, which the append
+        # kernel does not copy (the separate copy kernel does)
+        off = step % 2
+        qbuf = torch.full((q.size + off,), float("nan")).pin_memory()
+        qbuf[off:] = torch.from_numpy(q)
+        pq = qbuf[off:]
         po = torch.full((want.size,), float("nan")).pin_memory()
         err = K._Err()
         rc = K.lib().kivi_cache_decode(b.cache()._h, C.cast(pk.data_ptr(), fp), k.size,
@@ -804,6 +896,36 @@ def test_decode_pinned_buffers_match_pageable(K):
     ka, va = a.cache().dequantize()
     kb, vb = b.cache().dequantize()
     assert (ka == kb).all() and (va == vb).all()
+
+
+def test_decode_pinned_wide_query_group(K):
+    """A GQA group wider than one append CTA copies (16 query heads per kv
+    head x 128 channels) decodes from mapped pinned buffers equal to the
+    pageable call."""
+    torch = pytest.importorskip("torch")
+    import ctypes as C
+
+    cfg = K.KiviConfig.try_new(4, 32, 128)
+    batch, kv, qh, dim = 1, 2, 32, 128
+    scale = 0.125
+    a, b = K.RuntimeKv.try_new(cfg, batch, kv, dim), K.RuntimeKv.try_new(cfg, batch, kv, dim)
+    x = fill(batch * kv * 300 * dim, 4)
+    a.prefill(x, x, 300)
+    b.prefill(x, x, 300)
+    fp = C.POINTER(C.c_float)
+    for step in range(3):
+        k, v = fill(batch * kv * dim, 20 + step), fill(batch * kv * dim, 30 + step)
+        q = fill(batch * qh * dim, 40 + step)
+        want = a.decode(k, v, q, qh, scale)
+        pk, pv, pq = (torch.from_numpy(t).pin_memory() for t in (k, v, q))
+        po = torch.full((want.size,), float("nan")).pin_memory()
+        err = K._Err()
+        rc = K.lib().kivi_cache_decode(b.cache()._h, C.cast(pk.data_ptr(), fp), k.size,
+                                       C.cast(pv.data_ptr(), fp), v.size, C.cast(pq.data_ptr(), fp),
+                                       q.size, qh, C.c_float(scale), C.cast(po.data_ptr(), fp),
+                                       want.size, C.byref(err))
+        assert rc == 0, err.message
+        assert (po.numpy() == want).all(), step
 
 
 def test_host_calls_pinned_buffers_match_pageable(K):
