@@ -358,16 +358,20 @@ class DecodeWorkload:
                               stream=self.stream)
 
     def host_step(self):
+        # the C call a host-side caller makes; its ctypes arguments built once
         K = self.K
-        fp = ctypes.POINTER(ctypes.c_float)
-        err = K._Err()
-        rc = K.lib().kivi_cache_decode(
-            self.cache._h, ctypes.cast(self.hk.data_ptr(), fp), self.hk.numel(),
-            ctypes.cast(self.hv.data_ptr(), fp), self.hv.numel(),
-            ctypes.cast(self.hq.data_ptr(), fp), self.hq.numel(), self.Hq,
-            ctypes.c_float(self.scale), ctypes.cast(self.hout.data_ptr(), fp), self.hout.numel(),
-            ctypes.byref(err))
+        if getattr(self, "_hargs", None) is None:
+            fp = ctypes.POINTER(ctypes.c_float)
+            self._herr = K._Err()
+            self._hargs = (
+                self.cache._h, ctypes.cast(self.hk.data_ptr(), fp), self.hk.numel(),
+                ctypes.cast(self.hv.data_ptr(), fp), self.hv.numel(),
+                ctypes.cast(self.hq.data_ptr(), fp), self.hq.numel(), self.Hq,
+                ctypes.c_float(self.scale), ctypes.cast(self.hout.data_ptr(), fp),
+                self.hout.numel(), ctypes.byref(self._herr))
+        rc = K.lib().kivi_cache_decode(*self._hargs)
         if rc:
+            err = self._herr
             raise K.KiviError(err.code, err.a, err.b, None, err.message.decode())
 
     e2e_api = "kivi_cache_decode (RuntimeKv::decode), pinned host buffers"
@@ -463,17 +467,20 @@ class RagWorkload:
         self._step(self.pk[i * S:(i + 1) * S], self.pv[i * S:(i + 1) * S], self.pq[i])
 
     def host_step(self):
+        # the C call a host-side caller makes; its ctypes arguments built once
         K = self.K
-        L = K.lib()
-        fp = ctypes.POINTER(ctypes.c_float)
-        err = K._Err()
-        rc = L.kivi_sessions_decode_batched(
-            self._arr, self.S, ctypes.cast(self.hk.data_ptr(), fp), self.hk.numel(),
-            ctypes.cast(self.hv.data_ptr(), fp), self.hv.numel(),
-            ctypes.cast(self.hq.data_ptr(), fp), self.hq.numel(), self.Hq,
-            ctypes.c_float(self.scale), ctypes.cast(self.hout.data_ptr(), fp), self.hout.numel(),
-            ctypes.byref(err))
+        if getattr(self, "_hargs", None) is None:
+            fp = ctypes.POINTER(ctypes.c_float)
+            self._herr = K._Err()
+            self._hargs = (
+                self._arr, self.S, ctypes.cast(self.hk.data_ptr(), fp), self.hk.numel(),
+                ctypes.cast(self.hv.data_ptr(), fp), self.hv.numel(),
+                ctypes.cast(self.hq.data_ptr(), fp), self.hq.numel(), self.Hq,
+                ctypes.c_float(self.scale), ctypes.cast(self.hout.data_ptr(), fp),
+                self.hout.numel(), ctypes.byref(self._herr))
+        rc = K.lib().kivi_sessions_decode_batched(*self._hargs)
         if rc:
+            err = self._herr
             raise K.KiviError(err.code, err.a, err.b, None, err.message.decode())
 
     e2e_api = ("kivi_sessions_decode_batched (RagSession::append then ::attention of every "

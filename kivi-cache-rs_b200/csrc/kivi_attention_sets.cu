@@ -61,6 +61,8 @@
 namespace kivi {
 
 __device__ unsigned int g_sets_error = 0; // set by bounded waits that give up
+// This device's word of a mapped pinned host array, or null (as g_tc_hint).
+__device__ unsigned int *g_sets_hint = nullptr;
 
 namespace {
 
@@ -176,6 +178,7 @@ __device__ __forceinline__ bool bar_wait(uint64_t *b, uint32_t par, unsigned cod
     while (!bar_try(b, par)) {
         if (clock64() - t0 > kWait) {
             atomicOr(&g_sets_error, code);
+            if (g_sets_hint) *reinterpret_cast<volatile unsigned int *>(g_sets_hint) = 1u;
             return false;
         }
     }
@@ -985,6 +988,10 @@ cudaError_t plan_attention_sets(int64_t nstreams, int64_t main_groups, int nz, i
     *per = p;
     *nchunks = (int)((main_groups + p - 1) / p);
     return cudaSuccess;
+}
+
+cudaError_t set_sets_wait_hint(unsigned int *hint) {
+    return cudaMemcpyToSymbol(g_sets_hint, &hint, sizeof(hint));
 }
 
 cudaError_t take_sets_error(unsigned int *out) {

@@ -53,6 +53,9 @@
 namespace kivi {
 
 __device__ unsigned int g_tc_error = 0; // set by bounded waits that give up
+// This device's word of a mapped pinned host array, or null: a wait that gives
+// up also stores 1 there, so the host learns of it without reading g_tc_error.
+__device__ unsigned int *g_tc_hint = nullptr;
 
 namespace {
 
@@ -119,7 +122,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity; gives up after `limit` cycles
-// (~1 s by default), records the failure in g_tc_error and returns false.
+// (~1 s by default), records the failure in g_tc_error (and the host hint)
+// and returns false.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsigned code,
                                           long long limit = kWaitCycles) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -127,6 +131,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsign
     while (!mbar_try_wait(bar, parity)) {
         if (clock64() - t0 > limit) {
             atomicOr(&g_tc_error, code);
+            if (g_tc_hint) *reinterpret_cast<volatile unsigned int *>(g_tc_hint) = 1u;
             return false;
         }
     }
@@ -777,6 +782,10 @@ cudaError_t launch_wait_probe(long long limit_cycles, cudaStream_t s) {
     wait_probe_kernel<<<1, 32, 0, s>>>(limit_cycles);
     count_launch();
     return cudaGetLastError();
+}
+
+cudaError_t set_tc_wait_hint(unsigned int *hint) {
+    return cudaMemcpyToSymbol(g_tc_hint, &hint, sizeof(hint));
 }
 
 cudaError_t take_tc_error(unsigned int *out) {

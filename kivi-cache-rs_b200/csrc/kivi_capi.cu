@@ -660,7 +660,59 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
 
 // A tensor-core kernel whose bounded wait gave up leaves a flag instead of
 // hanging; synchronous calls report it as a CUDA-class error.
+// ---- give-up hints of the bounded device waits
+// A wait that gives up sets a device flag (read and cleared by two symbol
+// copies, each a synchronous copy-engine transfer) and stores 1 into its
+// device's word of this mapped pinned array, so that a synchronous call whose
+// device has the hint installed reads one host word after its stream
+// synchronisation and copies the flags only when the word is set.
+constexpr int kMaxHintDevices = 64;
+std::mutex g_hint_mu;
+volatile unsigned int *g_hint = nullptr;
+std::atomic<bool> g_hint_on[kMaxHintDevices];
+
+// Installs the current device's hint word (before that device's first attention
+// launch); best effort: without it the flags are copied on every check.
+void install_wait_hint() {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxHintDevices) {
+        (void)cudaGetLastError();
+        return;
+    }
+    std::lock_guard<std::mutex> lk(g_hint_mu);
+    if (g_hint_on[dev].load()) return;
+    if (!g_hint) {
+        void *p = nullptr;
+        if (cudaHostAlloc(&p, kMaxHintDevices * sizeof(unsigned int),
+                          cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess) {
+            (void)cudaGetLastError();
+            return;
+        }
+        std::memset(p, 0, kMaxHintDevices * sizeof(unsigned int));
+        g_hint = static_cast<volatile unsigned int *>(p);
+    }
+    void *dp = nullptr;
+    if (cudaHostGetDevicePointer(&dp, const_cast<unsigned int *>(g_hint), 0) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return;
+    }
+    unsigned int *word = static_cast<unsigned int *>(dp) + dev;
+    if (kivi::set_tc_wait_hint(word) != cudaSuccess || kivi::set_sets_wait_hint(word) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return;
+    }
+    g_hint_on[dev].store(true);
+}
+
 int32_t check_device_waits(kivi_error *err) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxHintDevices &&
+        g_hint_on[dev].load()) {
+        if (g_hint[dev] == 0) return KIVI_OK;
+        // cleared before the flags are taken: a give-up after this sets it again
+        g_hint[dev] = 0;
+        std::atomic_thread_fence(std::memory_order_seq_cst);
+    }
     unsigned int flag = 0, flag2 = 0;
     cudaError_t e = kivi::take_tc_error(&flag);
     if (e == cudaSuccess) e = kivi::take_sets_error(&flag2);
@@ -816,6 +868,7 @@ int32_t kivi_profile_hold(uint64_t microseconds, void *stream) {
 int32_t kivi_selftest_bounded_wait(uint64_t microseconds, kivi_error *err) {
     if (microseconds == 0 || microseconds > 100000)
         return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "bound must be 1..100000 us");
+    install_wait_hint();
     // clock64 counts SM cycles (at most ~2 GHz): 2000 per microsecond
     CUDA_TRY(kivi::launch_wait_probe((long long)microseconds * 2000, nullptr), "wait self-test");
     CUDA_TRY(cudaStreamSynchronize(nullptr), "wait self-test");
@@ -856,6 +909,7 @@ int32_t kivi_cache_new(const kivi_config *config, uint64_t batch, uint64_t num_k
     if (rc) return rc;
     DeviceGuard dg(device);
     if (!dg.ok) return set_msg(err, KIVI_ERR_CUDA, "cannot select device %d", device);
+    install_wait_hint();
     kivi_cache *h = new kivi_cache();
     h->s = s;
     const size_t res = (size_t)s.n() * s.cfg.residual_length * s.D;

@@ -295,6 +295,8 @@ cudaError_t plan_attention_sets(int64_t nstreams, int64_t main_groups, int nz, i
 cudaError_t launch_attention_sets(const SetsArgs &a, int bits, int nchunks, int nstreams, int nz,
                                   cudaStream_t s);
 cudaError_t take_sets_error(unsigned int *out);
+// Points the multi-set kernel's give-up hint at `hint` (current device).
+cudaError_t set_sets_wait_hint(unsigned int *hint);
 
 // QualityGuard's reference score (kivi_guard.cu): dense fp32 attention over a
 // token tape [B*H][cap][D] (logits scratch: B*Hq*seq floats) and the cosine
@@ -306,6 +308,9 @@ cudaError_t launch_guard_cosine(const float *a, const float *b, int64_t n, float
                                 cudaStream_t s);
 // Reads and clears the flag set when a tensor-core kernel's bounded wait gave up.
 cudaError_t take_tc_error(unsigned int *out);
+// Points the decode kernels' give-up hint at `hint`, a device address of
+// mapped pinned host memory (current device).
+cudaError_t set_tc_wait_hint(unsigned int *hint);
 
 // Dynamic shared memory the attention kernel needs for `rows` query rows.
 size_t attention_smem_bytes(int D, int rows);
