@@ -759,6 +759,7 @@ struct kivi_prefix {
     // (instead of one record per session); the sessions' synchronous calls wait
     // for it as well as for their own dev_done
     cudaEvent_t batch_done = nullptr;
+    mutable std::atomic<bool> batch_used{false}; // batch_done recorded by a `_dev` call
 };
 
 struct kivi_session {
@@ -768,6 +769,7 @@ struct kivi_session {
     uint64_t len = 0, cap = 0;
     cudaStream_t stream = nullptr;
     cudaEvent_t dev_done = nullptr;
+    mutable std::atomic<bool> dev_used{false}; // dev_done recorded by a `_dev` call
     Scratch stage;
     mutable Scratch part;
     mutable std::mutex mu;
@@ -789,6 +791,19 @@ cudaError_t wait_dev(cudaStream_t own, cudaEvent_t ev) { return cudaStreamWaitEv
 cudaError_t wait_session(cudaStream_t own, const kivi_session *s) {
     cudaError_t e = cudaStreamWaitEvent(own, s->dev_done, 0);
     if (e == cudaSuccess && s->prefix->batch_done) e = cudaStreamWaitEvent(own, s->prefix->batch_done, 0);
+    return e;
+}
+
+// The same for n sessions of one prefix, with one wait per event a `_dev`
+// call has recorded: a session's dev_done is otherwise only its creation's
+// record on an empty stream, and the synchronous calls finish their own work.
+cudaError_t wait_sessions(cudaStream_t own, const kivi_session *const *ss, uint64_t n) {
+    cudaError_t e = cudaSuccess;
+    for (uint64_t i = 0; i < n && e == cudaSuccess; ++i)
+        if (ss[i]->dev_used.load()) e = cudaStreamWaitEvent(own, ss[i]->dev_done, 0);
+    const kivi_prefix *p = ss[0]->prefix;
+    if (e == cudaSuccess && p->batch_done && p->batch_used.load())
+        e = cudaStreamWaitEvent(own, p->batch_done, 0);
     return e;
 }
 
@@ -1606,6 +1621,7 @@ int32_t kivi_sessions_append_dev(kivi_session *const *ss, uint64_t nsess, const 
     int32_t rc = sessions_append_launch(ss, nsess, dk, dv, seq, st, err);
     if (rc) return rc;
     CUDA_TRY(mark_dev(p->batch_done, st), "sessions append");
+    p->batch_used.store(true);
     return set_err(err, KIVI_OK);
 }
 
@@ -1625,7 +1641,7 @@ int32_t kivi_sessions_append(kivi_session *const *ss, uint64_t nsess, const floa
     kivi_session *lead = ss[0];
     std::lock_guard<std::mutex> lk(lead->mu);
     DeviceGuard dg(p.device);
-    for (uint64_t i = 0; i < nsess; ++i) CUDA_TRY(wait_session(lead->stream, ss[i]), "sessions append");
+    CUDA_TRY(wait_sessions(lead->stream, ss, nsess), "sessions append");
     const size_t bytes = expected * sizeof(float);
     CUDA_TRY(lead->stage.ensure(2 * bytes), "sessions append staging");
     const float *dk = nullptr, *dv = nullptr;
@@ -1670,6 +1686,7 @@ int32_t kivi_session_append_dev(kivi_session *s, const float *dk, const float *d
     int32_t rc = session_append(s, dk, dv, seq, cudaMemcpyDeviceToDevice, st, err);
     if (rc) return rc;
     CUDA_TRY(mark_dev(s->dev_done, st), "session append_dev");
+    s->dev_used.store(true);
     return set_err(err, KIVI_OK);
 }
 
@@ -1729,6 +1746,7 @@ int32_t kivi_session_attention_dev(const kivi_session *s, const float *dq, uint6
     int32_t rc = sessions_attention_dev(arr, 1, dq, Hq, scale, dout, st, s->part, err);
     if (rc) return rc;
     CUDA_TRY(mark_dev(s->dev_done, st), "session attention_dev");
+    s->dev_used.store(true);
     return set_err(err, KIVI_OK);
 }
 
@@ -1770,6 +1788,7 @@ int32_t kivi_sessions_attention_batched_dev(const kivi_session *const *ss, uint6
     int32_t rc = sessions_attention_dev(ss, n, dq, Hq, scale, dout, st, lead->part, err);
     if (rc) return rc;
     CUDA_TRY(mark_dev(lead->prefix->batch_done, st), "batched attention_dev");
+    lead->prefix->batch_used.store(true);
     return set_err(err, KIVI_OK);
 }
 
@@ -1787,10 +1806,7 @@ int32_t kivi_sessions_attention_batched(const kivi_session *const *ss, uint64_t 
     kivi_session *lead = const_cast<kivi_session *>(ss[0]);
     std::lock_guard<std::mutex> lk(lead->mu);
     DeviceGuard dg(p.device);
-    for (uint64_t i = 0; i < n; ++i)
-        CUDA_TRY(wait_dev(lead->stream, ss[i]->dev_done), "batched attention");
-    if (lead->prefix->batch_done)
-        CUDA_TRY(wait_dev(lead->stream, lead->prefix->batch_done), "batched attention");
+    CUDA_TRY(wait_sessions(lead->stream, ss, n), "batched attention");
     CUDA_TRY(lead->stage.ensure(2 * total * 4), "batched staging");
     float *dq = lead->stage.as<float>(), *stage_out = lead->stage.as<float>(total * 4);
     CUDA_TRY(input_staged(queries, dq, total, lead->stream), "batched H2D");
@@ -1836,9 +1852,7 @@ int32_t kivi_sessions_decode_batched(kivi_session *const *ss, uint64_t nsess, co
     kivi_session *lead = ss[0];
     std::lock_guard<std::mutex> lk(lead->mu);
     DeviceGuard dg(p.device);
-    for (uint64_t i = 0; i < nsess; ++i) CUDA_TRY(wait_session(lead->stream, ss[i]), "sessions decode");
-    if (lead->prefix->batch_done)
-        CUDA_TRY(wait_dev(lead->stream, lead->prefix->batch_done), "sessions decode");
+    CUDA_TRY(wait_sessions(lead->stream, ss, nsess), "sessions decode");
     const size_t kb = kv * sizeof(float), qb = total * sizeof(float);
     CUDA_TRY(lead->stage.ensure(2 * kb + 2 * qb), "sessions decode staging");
     float *dq = lead->stage.as<float>(2 * kb), *stage_out = lead->stage.as<float>(2 * kb + qb);
