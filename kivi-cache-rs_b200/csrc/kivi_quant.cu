@@ -80,6 +80,81 @@ struct Quantizer {
     }
 };
 
+// Sum over the code positions k of a word of 2^23's bit pattern times
+// 2^(BITS*k), modulo 2^32 (what pack32_fast's multiply-adds add on top of the
+// codes).
+__host__ __device__ constexpr uint32_t magic_word(int bits) {
+    uint64_t acc = 0;
+    for (int k = 0; k < 32 / bits; ++k) acc += (uint64_t)0x4B000000u << (bits * k);
+    return (uint32_t)acc;
+}
+
+// The 32 codes of one group packed into BITS words (LSB-first, quant.rs:
+// 296-325 / 349-374) without a branch per value: with q = (x - zero) * (1 /
+// scale), q + 2^23 rounds q to the nearest integer (ties to even) into the low
+// mantissa bits, and each word is accumulated as acc * 2^BITS + bits(q + 2^23)
+// from its last code down, the 2^23 patterns removed at the end.  q >= 0 up
+// to a NaN (x >= zero, the group's minimum), which fmaxf turns into code 0 as
+// the reference's clamp does, and q < levels + 1/2 (x <= the maximum), so no
+// upper clamp is needed.  Returns false, writing nothing, when the group needs
+// Quantizer::code's exact path: no normal reciprocal (scale 0 included), or a
+// quotient within 2^-12 of a half-integer.
+template <int BITS>
+__device__ __forceinline__ bool pack32_fast(const float (&x)[32], const Quantizer &qz,
+                                            uint32_t *words) {
+    constexpr int TPW = 32 / BITS;
+    if (!qz.fast) return false;
+    float dev = 0.0f;
+    uint32_t w[BITS];
+#pragma unroll
+    for (int wi = 0; wi < BITS; ++wi) {
+        uint32_t acc = 0;
+#pragma unroll
+        for (int k = TPW - 1; k >= 0; --k) {
+            const float q = __fmul_rn(__fsub_rn(x[wi * TPW + k], qz.zero), qz.rcp);
+            const float rm = __fadd_rn(fmaxf(q, 0.0f), 8388608.0f);
+            dev = fmaxf(dev, fabsf(__fsub_rn(q, __fsub_rn(rm, 8388608.0f))));
+            acc = acc * (1u << BITS) + __float_as_uint(rm);
+        }
+        constexpr uint32_t kMagic = magic_word(BITS);
+        w[wi] = acc - kMagic;
+    }
+    if (dev > 0.5f - 0x1p-12f) return false;
+#pragma unroll
+    for (int wi = 0; wi < BITS; ++wi) words[wi] = w[wi];
+    return true;
+}
+
+// Per-channel key quantization of channel `d` of one 32-row group whose rows
+// are base + u * stride (BITS known at compile time): the 32 values held in
+// registers, packed by pack32_fast unless the group needs the exact path.
+// Same results as quant_key_channel.
+template <int BITS>
+__device__ __forceinline__ void quant_key_channel_g32(const float *base, int stride, int d,
+                                                      uint32_t *words, float2 *param) {
+    constexpr float kLevels = (float)((1u << BITS) - 1u);
+    float x[32];
+#pragma unroll
+    for (int u = 0; u < 32; ++u) x[u] = base[(int64_t)u * stride + d];
+    float mn = INFINITY, mx = -INFINITY;
+#pragma unroll
+    for (int u = 0; u < 32; ++u) {
+        mn = fminf(mn, x[u]);
+        mx = fmaxf(mx, x[u]);
+    }
+    const float scale = scale_of(__fsub_rn(mx, mn), kLevels);
+    *param = make_float2(scale, mn);
+    const Quantizer qz(mn, scale, kLevels);
+    if (pack32_fast<BITS>(x, qz, words)) return;
+#pragma unroll
+    for (int w = 0; w < BITS; ++w) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int k = 0; k < 32 / BITS; ++k) word |= qz.code(x[w * (32 / BITS) + k]) << (k * BITS);
+        words[w] = word;
+    }
+}
+
 // Per-channel key quantization of one channel `d` of one group whose G rows
 // are rows[u * D] (u < G).  quant.rs:296-325.
 __device__ __forceinline__ void quant_key_channel(const Geom &g, const float *const *rows, int d,
@@ -106,7 +181,6 @@ __device__ __forceinline__ void quant_key_channel(const Geom &g, const float *co
 // 16-byte aligned), same arithmetic as the generic loop below.
 template <int BITS>
 __device__ __forceinline__ void quant_value_g32(const float *grp, uint32_t *words, float2 *param) {
-    constexpr int TPW = 32 / BITS, IPC = BITS;
     constexpr float kLevels = (float)((1u << BITS) - 1u);
     const float4 *grp4 = reinterpret_cast<const float4 *>(grp);
     float x[32];
@@ -127,11 +201,12 @@ __device__ __forceinline__ void quant_value_g32(const float *grp, uint32_t *word
     const float scale = scale_of(__fsub_rn(mx, mn), kLevels);
     *param = make_float2(scale, mn);
     const Quantizer qz(mn, scale, kLevels);
+    if (pack32_fast<BITS>(x, qz, words)) return;
 #pragma unroll
-    for (int w = 0; w < IPC; ++w) {
+    for (int w = 0; w < BITS; ++w) {
         uint32_t word = 0;
 #pragma unroll
-        for (int k = 0; k < TPW; ++k) word |= qz.code(x[w * TPW + k]) << (k * BITS);
+        for (int k = 0; k < 32 / BITS; ++k) word |= qz.code(x[w * (32 / BITS) + k]) << (k * BITS);
         words[w] = word;
     }
 }
@@ -304,22 +379,39 @@ __global__ void __launch_bounds__(256) append_small_kernel(Geom g, Store st, con
 
 // ---------------------------------------------------------------- bulk keys
 // grid (ngroups, n): one CTA per (key group, stream), one thread per channel.
-__global__ void __launch_bounds__(128) key_groups_kernel(Geom g, Store st, const float *res,
-                                                         int nres, const float *in, int64_t in_seq,
-                                                         int64_t out_group0) {
+// A 32-row group whose rows all come from the input (one contiguous span) is
+// quantized from registers by quant_key_channel_g32 (32 independent loads per
+// thread; 64 registers keep 8 CTAs per SM); other groups (rows from the
+// residual, other group sizes) go through the row table.
+__global__ void __launch_bounds__(128, 8) key_groups_kernel(Geom g, Store st, const float *res,
+                                                            int nres, const float *in,
+                                                            int64_t in_seq, int64_t out_group0) {
     const int64_t gi = blockIdx.x;
     const int s = blockIdx.y;
     const int D = g.D;
+    const int64_t c0 = gi * g.G;
+    uint32_t *kc = st.kcodes + (int64_t)s * code_stride(g, st.cap);
+    float2 *kp = st.kparams + (int64_t)s * kparam_stride(g, st.cap);
+    const int64_t og = out_group0 + gi;
+    if (g.G == 32 && c0 >= nres) {
+        // every row from the input: one contiguous span
+        const float *base = in + ((int64_t)s * in_seq + (c0 - nres)) * D;
+        for (int d = threadIdx.x; d < D; d += blockDim.x) {
+            uint32_t *words = kc + (og * D + d) * g.ipc;
+            float2 *param = kp + og * D + d;
+            if (g.bits == 2) quant_key_channel_g32<2>(base, D, d, words, param);
+            else if (g.bits == 4) quant_key_channel_g32<4>(base, D, d, words, param);
+            else quant_key_channel_g32<8>(base, D, d, words, param);
+        }
+        return;
+    }
     __shared__ const float *rows[kMaxG];
     for (int u = threadIdx.x; u < g.G; u += blockDim.x) {
-        const int64_t c = gi * g.G + u;
+        const int64_t c = c0 + u;
         rows[u] = c < nres ? res + ((int64_t)s * g.R + c) * D
                            : in + ((int64_t)s * in_seq + (c - nres)) * D;
     }
     __syncthreads();
-    uint32_t *kc = st.kcodes + (int64_t)s * code_stride(g, st.cap);
-    float2 *kp = st.kparams + (int64_t)s * kparam_stride(g, st.cap);
-    const int64_t og = out_group0 + gi;
     for (int d = threadIdx.x; d < D; d += blockDim.x)
         quant_key_channel(g, rows, d, kc + (og * D + d) * g.ipc, kp + og * D + d);
 }

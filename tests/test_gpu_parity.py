@@ -252,6 +252,27 @@ def test_streaming_store_bit_exact(K, bits, group, residual):
         assert_store_equal(g, o)
 
 
+@pytest.mark.parametrize("bits", [2, 4, 8])
+def test_streaming_store_bit_exact_head_dim_128(K, bits):
+    """The bulk-append kernels at head_dim 128, group 32 (their shared-memory
+    staged form: key groups and 32-token value blocks wholly from the input,
+    next to groups that take residual rows and blocks that take window rows or
+    end the input) match the reference store bit for bit."""
+    batch, heads, dim, residual = 1, 2, 128, 128
+    chunks = [300, 1, 2053, 129, 64, 1]
+    total = sum(chunks)
+    n = batch * heads * total * dim
+    keys, values = fill(n, 17 + bits), fill(n, 19 + bits)
+    g, o = pair(K, bits, 32, residual, batch, heads, dim)
+    off = 0
+    for c in chunks:
+        k = slice_tokens(keys, batch, heads, total, dim, off, c)
+        v = slice_tokens(values, batch, heads, total, dim, off, c)
+        append_both(g, o, k, v, c)
+        off += c
+        assert_store_equal(g, o)
+
+
 def test_chunked_appends_match_token_by_token(K):
     """tests/cache.rs:78-104 on the device (bitwise)."""
     cfg = K.KiviConfig.try_new(2, 16, 32)
