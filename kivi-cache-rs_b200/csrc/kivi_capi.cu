@@ -665,7 +665,8 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
 // copies, each a synchronous copy-engine transfer) and stores 1 into its
 // device's word of this mapped pinned array, so that a synchronous call whose
 // device has the hint installed reads one host word after its stream
-// synchronisation and copies the flags only when the word is set.
+// synchronisation and copies the flags only when the word is set.  The array
+// (one word per device) is allocated once and kept for the process's lifetime.
 constexpr int kMaxHintDevices = 64;
 std::mutex g_hint_mu;
 volatile unsigned int *g_hint = nullptr;
