@@ -91,14 +91,19 @@ def load_peaks(key="hbm_gbs"):
 
 
 def load_traffic(kernel, workload):
-    """Per-launch DRAM bytes of `kernel` on `workload` from a committed ncu summary."""
+    """(bytes, note): per-launch DRAM read + write bytes of `kernel` on
+    `workload` from the committed ncu summaries (profiles/traffic.json), or
+    (None, why) when no capture of that kernel on that workload exists."""
     path = os.path.join(ROOT, "profiles", "traffic.json")
     try:
         with open(path) as f:
             t = json.load(f)
-        return t.get(kernel, {}).get(workload)
     except Exception:
-        return None
+        return None, "no ncu traffic summary on file"
+    e = t.get(kernel, {}).get(workload)
+    if e is None:
+        return None, f"no ncu capture of {kernel} on this workload on file"
+    return int(e["bytes"]), e["source"]
 
 
 class ClockSampler:
@@ -257,6 +262,33 @@ def main_region_bytes(cache_like, streams, rows, cfgd):
     return streams * groups * per_group_bytes(cfgd) + rows * cfgd["D"] * 4
 
 
+def base_config(cfgd, world):
+    """The workload description both arms print (the GPU arm and --impl
+    reference), so the two lines name the same configuration."""
+    c = cfgd
+    cfg = {
+        "workload": c["name"], "num_kv_heads": c["H"], "num_q_heads": c["Hq"], "head_dim": c["D"],
+        "kivi": {"bits": c["bits"], "group_size": c["G"], "residual_length": c["R"]},
+        "batch_per_gpu": c["B"], "context_start": c["ctx"],
+    }
+    if c["mode"] == "decode":
+        cfg.update(global_batch=c["B"] * world, parallelism=f"batch x kv-head sharding, dp{world}")
+    elif c["mode"] == "rag":
+        cfg.update(global_batch=c["B"] * world, sessions=c["sessions"],
+                   question_tokens_start=c["suffix"],
+                   parallelism=f"independent documents per rank, dp{world}")
+    else:
+        cfg.update(global_batch=c["B"],
+                   parallelism=f"sequence sharding over {world} ranks, NCCL all-gather of "
+                               f"packed (m, l, o) + rank-ordered merge")
+    return cfg
+
+
+def data_desc(cfgd):
+    return ("synthetic (seeded N(0,1) K/V/Q, "
+            + ("x20 outlier" if cfgd["outlier"] == "x20" else "lognormal") + " key channel scales)")
+
+
 # ---------------------------------------------------------------- GPU workloads
 
 
@@ -398,12 +430,6 @@ class DecodeWorkload:
     def cache_bytes(self):
         return self.cache.memory().compressed_bytes()
 
-    def config_extra(self, world):
-        c = self.cfgd
-        return {"batch_per_gpu": c["B"], "global_batch": c["B"] * world,
-                "context_start": c["ctx"],
-                "parallelism": f"batch x kv-head sharding, dp{world}"}
-
     def close(self):
         pass
 
@@ -512,13 +538,6 @@ class RagWorkload:
         # one, reported beside it as tensor_flops_per_step
         return main_region_bytes(self.prefix, c["B"] * c["H"], self.S * c["B"] * c["Hq"], c)
 
-    def config_extra(self, world):
-        c = self.cfgd
-        return {"batch_per_gpu": c["B"], "global_batch": c["B"] * world,
-                "sessions": self.S, "question_tokens_start": c["suffix"],
-                "context_start": c["ctx"],
-                "parallelism": f"independent documents per rank, dp{world}"}
-
     def close(self):
         self.sessions = []
 
@@ -597,13 +616,6 @@ class SeqShardWorkload:
         if kernel == "attn_chunk":
             return self.cache_bytes() + c["B"] * c["Hq"] * c["D"] * 4
         return main_region_bytes(self.sc.cache, c["B"] * c["H"], c["B"] * c["Hq"], c)
-
-    def config_extra(self, world):
-        c = self.cfgd
-        return {"batch_per_gpu": c["B"], "global_batch": c["B"], "context_start": c["ctx"],
-                "shard_tokens_rank0": self.sc.plan.tokens if self.sc.rank == 0 else None,
-                "parallelism": f"sequence sharding over {world} ranks, NCCL all-gather of "
-                               f"packed (m, l, o) + rank-ordered merge"}
 
     def close(self):
         pass
@@ -738,16 +750,12 @@ def run_gpu(args, cfgd, rank, world, local_rank):
     achieved = kern_bytes / (kern_avg_ms / 1e3) / 1e9 if kern_avg_ms > 0 else None
     workload = cfgd["name"]
     h2d, d2h = wl.io_bytes()
-    config = {
-        "workload": workload, "num_kv_heads": cfgd["H"], "num_q_heads": cfgd["Hq"],
-        "head_dim": cfgd["D"],
-        "kivi": {"bits": cfgd["bits"], "group_size": cfgd["G"], "residual_length": cfgd["R"]},
-        "l2": (f"cache {job_cache_bytes / world / 1e6:.0f} MB per rank (< 126 MB L2): "
+    config = base_config(cfgd, world)
+    traffic, traffic_note = load_traffic(kernel, workload)
+    l2_note = (f"cache {job_cache_bytes / world / 1e6:.0f} MB per rank (< 126 MB L2): "
                f"L2 flushed between steps ({FLUSH_BYTES >> 20} MB write), each step timed by "
                f"its own CUDA events" if flush_l2 else
-               f"cache {job_cache_bytes / world / 1e6:.0f} MB per rank (> 126 MB L2)"),
-    }
-    config.update(wl.config_extra(world))
+               f"cache {job_cache_bytes / world / 1e6:.0f} MB per rank (> 126 MB L2)")
     result = {
         "metric": METRIC,
         "value": steps_per_s,
@@ -760,17 +768,16 @@ def run_gpu(args, cfgd, rank, world, local_rank):
         "scaling": "strong" if strong else "weak",
         "vs_baseline": None,
         "dtype": f"u32-packed {cfgd['bits']}-bit codes, fp32 arithmetic",
-        "data": "synthetic (seeded N(0,1) K/V/Q, "
-                + ("x20 outlier" if cfgd["outlier"] == "x20" else "lognormal")
-                + " key channel scales)",
+        "data": data_desc(cfgd),
         "config": config,
+        "l2": l2_note,
         "hbm_gbs": hbm_gbs,
         "hbm_frac": hbm_gbs / (peak * world),
         "roofline": {
             "kernel": kernel, "bound": "hbm", "achieved": achieved, "peak": peak,
             "peak_kind": peak_kind, "unit": "GB/s",
             "frac": (achieved / peak) if achieved else None,
-            "traffic": load_traffic(kernel, workload),
+            "traffic": traffic, "traffic_source": traffic_note,
             "algorithmic_bytes_per_launch": kern_bytes,
             "avg_launch_ms": kern_avg_ms, "launches": kernels[kernel]["launches"],
             "share_of_timed_kernels": kernels[kernel]["total_ms"] / ms_all if ms_all else None,
@@ -792,6 +799,7 @@ def run_gpu(args, cfgd, rank, world, local_rank):
             "ms": PREFILL_MS[0], "chunk_kernel": "key_groups + value_tokens + copy_rows2",
         }
     if mode == "seqshard" and rank == 0:
+        result["shard_tokens_rank0"] = wl.sc.plan.tokens
         result["key_flush"] = key_flush_microbench(K, cfgd, stream)
     if mode == "rag":
         c = cfgd
@@ -1005,8 +1013,8 @@ def run_reference(args, cfgd, rank, world):
         "metric": METRIC, "value": v, "unit": "steps/s", "n_gpus": world, "steps": S, "warmup": W,
         "ms_per_step": per_step * 1e3, "higher_is_better": True,
         "scaling": "strong" if cfgd["mode"] == "seqshard" else "weak",
-        "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded N(0,1))",
-        "config": {"workload": cfgd["name"], "batch_per_gpu": cfgd["B"]},
+        "vs_baseline": None, "dtype": "fp32", "data": data_desc(cfgd),
+        "config": base_config(cfgd, world),
         "impl": "reference",
         "cpu_baseline": {
             "value": v, "unit": "steps/s", "cores": threads, "kind": "port",

@@ -173,6 +173,21 @@ int32_t kivi_profile_hold(uint64_t microseconds, void *stream);
  * (0x40000000) in the message when the give-up path works; the flag is then
  * cleared and the device stays usable. */
 int32_t kivi_selftest_bounded_wait(uint64_t microseconds, kivi_error *err);
+/* Stream-ordered form of the self-test: enqueues the waiting warp on `stream`
+ * (as a *_dev call would) and returns without reading the flag, which the next
+ * kivi_device_wait_status or synchronous host call on the device reports. */
+int32_t kivi_selftest_bounded_wait_dev(uint64_t microseconds, void *stream, kivi_error *err);
+/* Bounded-wait status of `device` (no counterpart in the reference; the
+ * reference runs no device code).  An attention kernel whose wait on its own
+ * copies runs out (about a second) stops, records a flag on its device and
+ * leaves its output incomplete.  The synchronous host calls read that flag
+ * after their own synchronisation and report KIVI_ERR_CUDA.  The stream-ordered
+ * *_dev calls cannot: after synchronising its own stream, a caller of them
+ * calls this to learn whether any such wait on `device` gave up since the last
+ * report.  Returns KIVI_OK, or KIVI_ERR_CUDA with the flag in the message; the
+ * flag is cleared when reported, so each give-up is reported once, to whichever
+ * call (this one or a synchronous host call on that device) reads it first. */
+int32_t kivi_device_wait_status(int32_t device, kivi_error *err);
 
 /* ---------------------------------------------------------------- config.rs */
 
@@ -212,16 +227,20 @@ int32_t kivi_cache_attention_dev(const kivi_cache *cache, const float *d_query,
  * reference: it serves callers that cannot call cudaMalloc while decoding --
  * serving engines that reserve nearly all device memory for their own pool at
  * start-up, and decode loops that must not hit cudaMalloc/cudaFree, which can
- * synchronise the device.  The attention's partial-softmax scratch comes from a
- * fixed 16 MiB array in the library's device image (held by every GPU that
- * loads the library until exit) instead of the handle's grown buffer; a call
- * needing more than 16 MiB of scratch (batch*num_q_heads*(head_dim+2)*4 bytes
- * per 256-token chunk, plus two chunks) fails with KIVI_ERR_UNSUPPORTED and a
- * message giving both sizes.  The call allocates nothing.  Its first call on a
- * device looks up the array's device address (cudaGetSymbolAddress) with that
- * device current; make that first call before any stream capture.  All calls
- * share the one array: calls that overlap on the GPU (other streams, other
- * handles on the same device) race, so order them on one stream. */
+ * synchronise the device.  It runs the same plan and kernels as
+ * kivi_cache_attention_dev (the tensor-core split where the geometry allows
+ * it, so it runs at the same speed and gives the same bits), but its
+ * partial-softmax scratch comes from a fixed 16 MiB array in the library's
+ * device image (held by every GPU that loads the library until exit) instead
+ * of the handle's grown buffer.  The scratch is batch*num_q_heads*slots*
+ * (head_dim+2)*4 bytes, where slots is a handful of partial states per row
+ * (about 11 for a 32k-token cache of 128 streams on a B200); a call needing
+ * more than 16 MiB fails with KIVI_ERR_UNSUPPORTED and a message giving both
+ * sizes, before anything is launched.  The call allocates nothing.  Its first
+ * call on a device looks up the array's device address (cudaGetSymbolAddress)
+ * with that device current; make that first call before any stream capture.
+ * All calls share the one array: calls that overlap on the GPU (other streams,
+ * other handles on the same device) race, so order them on one stream. */
 int32_t kivi_cache_attention_noalloc_dev(const kivi_cache *cache, const float *d_query,
                                          uint64_t num_q_heads, float scale, float *d_out,
                                          void *stream, kivi_error *err);

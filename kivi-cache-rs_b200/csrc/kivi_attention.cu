@@ -305,10 +305,25 @@ cudaError_t launch_attention_chunks(const AttnArgs &a, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+// The merge keeps one weight per slot in dynamic shared memory.
+constexpr size_t kMergeSmemLimit = 200 * 1024;
+
+int merge_max_parts() { return (int)(kMergeSmemLimit / sizeof(float)); }
+
 cudaError_t launch_merge(const float *part_ml, const float *part_o, int64_t rows, int parts, int D,
                          int /*ml_stride_pairs*/, float *out, float *out_m, float *out_l, int mode,
                          cudaStream_t s) {
     if (rows <= 0) return cudaSuccess;
+    if (parts > merge_max_parts()) return cudaErrorInvalidValue;
+    static bool configured[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (sizeof(float) * parts > 48 * 1024 && dev >= 0 && dev < 64 && !configured[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)kMergeSmemLimit);
+        if (e != cudaSuccess) return e;
+        configured[dev] = true;
+    }
     ProfScope prof("merge", s);
     merge_kernel<<<(unsigned)rows, 128, sizeof(float) * parts, s>>>(part_ml, part_o, parts, D, out,
                                                                     out_m, out_l, mode);

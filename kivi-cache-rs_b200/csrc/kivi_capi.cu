@@ -237,8 +237,16 @@ void free_store(Store &st) {
 struct Scratch {
     void *p = nullptr;
     size_t bytes = 0;
+    // A fixed scratch is a view of memory it does not own: ensure() never
+    // allocates and fails for a request beyond `bytes` (recorded in `wanted`).
+    bool fixed = false;
+    size_t wanted = 0;
     cudaError_t ensure(size_t need) {
         if (need <= bytes) return cudaSuccess;
+        if (fixed) {
+            wanted = need;
+            return cudaErrorMemoryAllocation;
+        }
         const size_t n = need < 2 * bytes ? 2 * bytes : need;
         if (p) cudaFree(p);
         p = nullptr;
@@ -608,6 +616,10 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
     const int64_t tail_tokens = (int64_t)(p.seq - main_tokens);
     const int NTT = (int)std::max<int64_t>(1, (tail_tokens + kTailTile - 1) / kTailTile);
     const int parts = (int)NC + NTT + 1;
+    if (parts > kivi::merge_max_parts())
+        return set_msg(err, KIVI_ERR_UNSUPPORTED,
+                       "%llu tokens need %d partial slots per row; the merge takes at most %d",
+                       (unsigned long long)p.seq, parts, kivi::merge_max_parts());
     const uint64_t rows_per_sess = p.B * Hq;
     for (uint64_t s0 = 0; s0 < nsess; s0 += per_launch) {
         const uint64_t ns = nsess - s0 < per_launch ? nsess - s0 : per_launch;
@@ -889,6 +901,26 @@ int32_t kivi_selftest_bounded_wait(uint64_t microseconds, kivi_error *err) {
     CUDA_TRY(kivi::launch_wait_probe((long long)microseconds * 2000, nullptr), "wait self-test");
     CUDA_TRY(cudaStreamSynchronize(nullptr), "wait self-test");
     return check_device_waits(err);
+}
+
+int32_t kivi_selftest_bounded_wait_dev(uint64_t microseconds, void *stream, kivi_error *err) {
+    if (microseconds == 0 || microseconds > 100000)
+        return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "bound must be 1..100000 us");
+    install_wait_hint();
+    CUDA_TRY(kivi::launch_wait_probe((long long)microseconds * 2000, (cudaStream_t)stream),
+             "wait self-test");
+    return set_err(err, KIVI_OK);
+}
+
+int32_t kivi_device_wait_status(int32_t device, kivi_error *err) {
+    int count = 0;
+    CUDA_TRY(cudaGetDeviceCount(&count), "device count");
+    if (device < 0 || device >= count)
+        return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "no device %d", (int)device);
+    DeviceGuard dg(device);
+    int32_t rc = check_device_waits(err);
+    if (rc) return rc;
+    return set_err(err, KIVI_OK);
 }
 
 void kivi_profile_reset(void) {
@@ -1818,6 +1850,8 @@ int32_t kivi_sessions_attention_batched(const kivi_session *const *ss, uint64_t 
     if (rc) return rc;
     CUDA_TRY(output_done(out, dout, stage_out, total, lead->stream), "batched D2H");
     CUDA_TRY(cudaStreamSynchronize(lead->stream), "batched attention");
+    rc = check_device_waits(err);
+    if (rc) return rc;
     return set_err(err, KIVI_OK);
 }
 
@@ -2166,53 +2200,26 @@ extern "C" int32_t kivi_cache_attention_noalloc_dev(const kivi_cache *h, const f
         CUDA_TRY(cudaEventRecord(h->dev_done, st), "noalloc attention");
         return set_err(err, KIVI_OK);
     }
-    const uint64_t Gq = Hq / p.H;
-    if ((int)Gq > kivi::attention_max_rows((int)p.D))
-        return set_msg(err, KIVI_ERR_UNSUPPORTED, "too many query heads per kv head");
-    // Same split plan as kivi_cache_attention_dev for one query set.
-    const uint64_t main_tokens = p.vq / p.cfg.group_size * p.cfg.group_size;
-    const int64_t NC = (int64_t)((main_tokens + kChunkTokens - 1) / kChunkTokens);
-    const int parts = (int)NC + 2;
-    const uint64_t rows = p.B * Hq;
-    const size_t ml_floats = rows * parts * 2;
-    const size_t need = (ml_floats + rows * parts * p.D) * sizeof(float);
-    if (need > kNoAllocScratchBytes)
-        return set_msg(err, KIVI_ERR_UNSUPPORTED,
-                       "attention needs %llu bytes of scratch; the allocation-free entry point "
-                       "has a static limit of %llu bytes",
-                       (unsigned long long)need, (unsigned long long)kNoAllocScratchBytes);
     float *scratch = nullptr;
     rc = noalloc_scratch(p.device, &scratch, err);
     if (rc) return rc;
-    kivi::AttnArgs a{};
-    a.g = p.g;
-    a.st = p.st;
-    a.B = (int)p.B;
-    a.H = (int)p.H;
-    a.Hq = (int)Hq;
-    a.Gq = (int)Gq;
-    a.kq = (int64_t)p.kq;
-    a.vq = (int64_t)p.vq;
-    a.kres_len = (int)p.kres_len;
-    a.vres_len = (int)p.vres_len;
-    a.vhead = (int)p.vhead;
-    a.seq_p = (int64_t)p.seq;
-    a.main_tokens = (int64_t)main_tokens;
-    a.chunk_tokens = kChunkTokens;
-    a.NC = (int)NC;
-    a.parts = parts;
-    a.S = 1;
-    a.session_base = 0;
-    a.q = dq;
-    a.scale = scale;
-    // Every slot the merge reads is written by this call's chunk kernel first,
-    // so the shared array needs no clearing between calls.
-    a.part_ml = scratch;
-    a.part_o = scratch + ml_floats;
-    CUDA_TRY(kivi::launch_attention_chunks(a, st), "noalloc attention");
-    CUDA_TRY(kivi::launch_merge(a.part_ml, a.part_o, (int64_t)rows, parts, (int)p.D, 0, dout,
-                                nullptr, nullptr, 0, st),
-             "noalloc attention merge");
+    // The same plan and kernels as kivi_cache_attention_dev (the tensor-core
+    // split where the geometry allows it), over a view of the static array
+    // that never grows.  Every partial slot the merge reads is written by this
+    // call's kernels first, so the array needs no clearing between calls.
+    Scratch fixed;
+    fixed.p = scratch;
+    fixed.bytes = kNoAllocScratchBytes;
+    fixed.fixed = true;
+    rc = run_attention(p, nullptr, 1, dq, Hq, scale, dout, nullptr, nullptr, fixed, st, err);
+    if (rc) {
+        if (fixed.wanted > fixed.bytes)
+            return set_msg(err, KIVI_ERR_UNSUPPORTED,
+                           "attention needs %llu bytes of scratch; the allocation-free entry point "
+                           "has a static limit of %llu bytes",
+                           (unsigned long long)fixed.wanted, (unsigned long long)fixed.bytes);
+        return rc;
+    }
     CUDA_TRY(cudaEventRecord(h->dev_done, st), "noalloc attention");
     return set_err(err, KIVI_OK);
 }

@@ -196,6 +196,8 @@ cudaError_t launch_attention_chunks(const AttnArgs &a, cudaStream_t s);
 cudaError_t launch_merge(const float *part_ml, const float *part_o, int64_t rows, int parts, int D,
                          int ml_stride_pairs, float *out, float *out_m, float *out_l, int mode,
                          cudaStream_t s);
+// Most slots launch_merge takes (one float of dynamic shared memory each).
+int merge_max_parts();
 // Cross-shard merge: part c's m/l rows start at c*ml_stride, its o rows at
 // c*o_stride (floats); merged in part order.
 cudaError_t launch_merge_shards(const float *m, const float *l, const float *o, int64_t parts,

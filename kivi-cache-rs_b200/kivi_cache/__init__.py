@@ -146,6 +146,8 @@ def lib():
         "kivi_sessions_append": ([P, sz, fp, sz, fp, sz, sz, e], i32),
         "kivi_sessions_decode_batched": ([P, sz, fp, sz, fp, sz, fp, sz, sz, f32, fp, sz, e], i32),
         "kivi_selftest_bounded_wait": ([sz, e], i32),
+        "kivi_selftest_bounded_wait_dev": ([sz, P, e], i32),
+        "kivi_device_wait_status": ([i32, e], i32),
         "kivi_session_reserve": ([P, sz, e], i32),
         "kivi_packed_partials_floats": ([sz, sz], sz),
         "kivi_cache_attention_partial_packed_dev": ([P, P, sz, f32, P, P, e], i32),
@@ -221,6 +223,15 @@ def _stream(s):
 def kernel_launches():
     """Number of this library's kernels launched so far in this process."""
     return int(lib().kivi_kernel_launches())
+
+
+def device_wait_status(device=0):
+    """Raises KiviError (Cuda) if a bounded device wait on `device` gave up
+    since the last report.  Callers of the stream-ordered ``*_dev`` methods
+    call this after synchronising their stream; the synchronous host calls
+    check it themselves."""
+    err = _Err()
+    _check(lib().kivi_device_wait_status(int(device), C.byref(err)), err)
 
 
 # ---------------------------------------------------------------- config.rs

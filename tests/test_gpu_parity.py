@@ -1030,6 +1030,40 @@ def test_bounded_wait_gives_up_and_the_device_stays_usable(K):
     assert_attention_close(cache.attention(q, 4, 0.088), ocache.attention(q, 4, 0.088))
 
 
+def test_stream_ordered_wait_give_up_is_reported_once(K):
+    """A give-up recorded by stream-ordered work is reported by
+    kivi_device_wait_status (once, then cleared), and by the batched session
+    host call when that call is the first to look."""
+    import ctypes as C
+
+    torch = pytest.importorskip("torch")
+    L = K.lib()
+    err = K._Err()
+    assert L.kivi_selftest_bounded_wait_dev(2000, None, C.byref(err)) == 0
+    torch.cuda.synchronize()
+    err = K._Err()
+    rc = L.kivi_device_wait_status(0, C.byref(err))
+    assert rc == 100 and str(0x40000000) in err.message.decode()  # KIVI_ERR_CUDA
+    K.device_wait_status(0)  # cleared: nothing more to report
+    err = K._Err()
+    assert L.kivi_device_wait_status(-1, C.byref(err)) != 0
+
+    cache, ocache = pair(K, 2, 32, 128, 1, 2, 128)
+    keys, values, _ = synthetic_kv(5, 1, 2, 200, 128)
+    append_both(cache, ocache, keys, values, 200)
+    prefix, oprefix = cache.share_prefix(), ocache.share_prefix()
+    sessions = [prefix.session() for _ in range(4)]
+    q = fill(4 * 4 * 128, 11)
+    want = K.sessions_attention_batched(sessions, q, 4, 0.088)
+    assert L.kivi_selftest_bounded_wait_dev(2000, None, C.byref(err)) == 0
+    torch.cuda.synchronize()
+    with pytest.raises(K.KiviError) as e:
+        K.sessions_attention_batched(sessions, q, 4, 0.088)
+    assert str(0x40000000) in str(e.value)
+    assert (K.sessions_attention_batched(sessions, q, 4, 0.088) == want).all()
+    K.device_wait_status(0)
+
+
 def test_unaligned_device_inputs(K):
     """Device inputs at 4-byte (not 16-byte) offsets take the scalar paths and
     give the same bits as aligned ones (append) and the same attention."""
