@@ -19,9 +19,15 @@
 //               across all the CTA's groups.
 //
 // fp32 accuracy from fp16 operands: every operand x is split into
-// hi = x truncated to 11 significant bits and lo = x - hi (exact), and each
-// product is formed as hi*hi + lo*hi + hi*lo in fp32 accumulators (~22
-// significant bits; the dropped lo*lo is below 2^-22 relative).  The key tile
+// hi = x rounded to fp16 (11 significant bits) and lo = x - hi (exact), and each
+// product is formed as hi*hi + lo*hi + hi*lo in fp32 accumulators (~23
+// significant bits; the dropped lo*lo is below 2^-24 relative).  The tensor
+// cores' fp32 accumulation loses a little at every MMA step, relative to the
+// accumulator's magnitude, so S takes its two small sweeps first (into a
+// small accumulator) and the large hi*hi sweep last, and no CTA accumulates O
+// over more than about 28 tiles: at 64k tokens x 32 sessions the error against
+// an exact evaluation was 1.4e-5 rel-L2 with ~57 tiles per CTA and truncated
+// splits, 4.3e-6 with these three changes (plan_attention_sets).  The key tile
 // stores its lo half after its hi half in the token direction, so
 // Q_hi [K_hi | K_lo] is one N = 128 MMA per K step and Q_lo K_hi one N = 64
 // MMA into the first half; softmax adds the two halves.  Both parts
@@ -274,13 +280,13 @@ __device__ __forceinline__ int exp_ceil_(float x) {
     return e == 0 ? -126 : e - 126;
 }
 
-// hi/lo fp16 split of a pair: hi = x truncated to 11 significant bits,
-// lo = x - hi (exact); packed as fp16x2 (first value in the low half).
+// hi/lo fp16 split of a pair: hi = x rounded to fp16, lo = x - hi (exact in
+// fp32, |lo| <= 2^-12 |x|, then rounded to fp16); packed as fp16x2 (first
+// value in the low half).
 __device__ __forceinline__ void split_pair(float a, float b, uint32_t &hi, uint32_t &lo) {
-    const float ta = __uint_as_float(__float_as_uint(a) & 0xFFFFE000u);
-    const float tb = __uint_as_float(__float_as_uint(b) & 0xFFFFE000u);
-    const __half2 hh = __floats2half2_rn(ta, tb);
-    const __half2 ll = __floats2half2_rn(a - ta, b - tb);
+    const __half2 hh = __floats2half2_rn(a, b);
+    const float2 hf = __half22float2(hh);
+    const __half2 ll = __floats2half2_rn(a - hf.x, b - hf.y);
     hi = *reinterpret_cast<const uint32_t *>(&hh);
     lo = *reinterpret_cast<const uint32_t *>(&ll);
 }
@@ -616,9 +622,9 @@ __global__ void __launch_bounds__(kSetThreads, 1) attn_sets_kernel(const SetsArg
             // tile's lo half starts 16 KB after its hi half
             const uint32_t sacc = tbase + kSc + 64 * bs;
             const uint64_t kh = dk0 + (uint64_t)bk * 2048u, kl = kh + 1024u;
-            umma_sweep<8>(sacc, tbase + kQH, kh, id_qk, 0u);
-            umma_sweep<8>(sacc, tbase + kQL, kh, id_qk, 1u);
+            umma_sweep<8>(sacc, tbase + kQL, kh, id_qk, 0u);
             umma_sweep<8>(sacc, tbase + kQH, kl, id_qk, 1u);
+            umma_sweep<8>(sacc, tbase + kQH, kh, id_qk, 1u);
             umma_commit_e(&s_full[bs]); // also frees key slot bk for tile j + kK
             if (j >= 2 && !pv(j - 2)) ok = false;
         }
@@ -981,8 +987,11 @@ cudaError_t plan_attention_sets(int64_t nstreams, int64_t main_groups, int nz, i
     if (e != cudaSuccess) return e;
     if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
         return e;
-    // one CTA per SM: chunks per stream so that streams x chunks x row-chunks ~ #SMs
-    int64_t nc = std::max<int64_t>(1, sms / std::max<int64_t>(1, nstreams * nz));
+    // one CTA per SM, two waves: chunks per stream so that streams x chunks x
+    // row-chunks ~ 2 x #SMs (shorter runs per CTA bound the error of the
+    // tensor cores' O accumulation; one wave with twice the tiles per CTA
+    // exceeded 1e-5 rel-L2 at 64k tokens)
+    int64_t nc = std::max<int64_t>(1, 2 * sms / std::max<int64_t>(1, nstreams * nz));
     nc = std::min<int64_t>(nc, main_groups);
     const int64_t p = (main_groups + nc - 1) / nc;
     *per = p;

@@ -83,6 +83,11 @@ def lib():
         L.ko_cache_attention.argtypes = [P, fp, sz, sz, C.c_float, fp, C.c_int, e]
         L.ko_cache_attention_batch_range.argtypes = [P, fp, sz, C.c_float, fp, C.c_int, sz, sz]
         L.ko_cache_attention_f64.argtypes = [P, fp, sz, C.c_float, C.POINTER(C.c_double)]
+        L.ko_cache_attention_f64_threads.argtypes = [P, fp, sz, C.c_float, C.POINTER(C.c_double),
+                                                     C.c_int]
+        L.ko_session_attention_f64.argtypes = [P, fp, sz, C.c_float, C.POINTER(C.c_double), C.c_int]
+        L.ko_set_append_threads.argtypes = [C.c_int]
+        L.ko_set_append_threads.restype = None
         L.ko_cache_dequantize.argtypes = [P, fp, fp]
         L.ko_cache_memory.argtypes = [P, u64p]
         L.ko_cache_state.argtypes = [P, u64p]
@@ -222,12 +227,17 @@ class KiviCache:
             raise OracleError(rc, 0, 0, None)
         return out
 
-    def attention_f64(self, query, num_q_heads, scale):
+    def attention_f64(self, query, num_q_heads, scale, threads=1):
+        """fp64 evaluation of the same attention over the dequantized cache
+        (error attribution; not a reference routine).  Streamed over token
+        blocks and threaded over streams: memory stays small at full size."""
         q, qp = _f32(query)
         out = np.zeros(self.batch * num_q_heads * self.head_dim, np.float64)
-        lib().ko_cache_attention_f64(
-            self._h, qp, num_q_heads, C.c_float(scale), out.ctypes.data_as(C.POINTER(C.c_double))
-        )
+        rc = lib().ko_cache_attention_f64_threads(
+            self._h, qp, num_q_heads, C.c_float(scale), out.ctypes.data_as(C.POINTER(C.c_double)),
+            threads)
+        if rc:
+            raise OracleError(rc, num_q_heads, self.heads, None)
         return out
 
     def state(self):
@@ -320,6 +330,18 @@ class RagSession:
     def question_tokens(self):
         return int(lib().ko_session_question_tokens(self._h))
 
+    def attention_f64(self, query, num_q_heads, scale, threads=1):
+        """fp64 evaluation over prefix + suffix (error attribution)."""
+        p = self._prefix
+        q, qp = _f32(query)
+        out = np.zeros(p.batch * num_q_heads * p.head_dim, np.float64)
+        rc = lib().ko_session_attention_f64(
+            self._h, qp, num_q_heads, C.c_float(scale), out.ctypes.data_as(C.POINTER(C.c_double)),
+            threads)
+        if rc:
+            raise OracleError(rc, num_q_heads, p.heads, None)
+        return out
+
     def attention(self, query, num_q_heads, scale, threads=1):
         p = self._prefix
         q, qp = _f32(query)
@@ -331,6 +353,12 @@ class RagSession:
         )
         _check(rc, err)
         return out
+
+
+def set_append_threads(threads):
+    """Worker threads for the oracle's per-stream append loops (default 1, the
+    reference's serial loop); results are bit-identical for any count."""
+    lib().ko_set_append_threads(int(threads))
 
 
 def quantize(per_channel, data, batch, heads, tokens, head_dim, bits, group_size):

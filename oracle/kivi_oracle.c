@@ -618,12 +618,79 @@ static void shift_residual(float *residual, size_t cap, size_t from, size_t keep
         }
 }
 
+/* Worker threads for the per-stream loops of the append path (1 = the
+ * reference's serial loop).  Streams are independent (each PackedStream and
+ * residual slice belongs to one (b, h)), so the count changes no result bit;
+ * it only lets the parity tests fill full-size caches in seconds. */
+static int g_append_threads = 1;
+
+void ko_set_append_threads(int threads) { g_append_threads = threads < 1 ? 1 : threads; }
+
+typedef void (*stream_fn)(void *ctx, size_t hi);
+typedef struct {
+    stream_fn fn;
+    void *ctx;
+    size_t begin, end;
+} stream_job;
+
+static void *stream_worker(void *arg) {
+    const stream_job *j = (const stream_job *)arg;
+    for (size_t hi = j->begin; hi < j->end; hi++) j->fn(j->ctx, hi);
+    return NULL;
+}
+
+static void for_streams(size_t n, stream_fn fn, void *ctx) {
+    size_t threads = (size_t)g_append_threads;
+    if (threads > n) threads = n;
+    if (threads <= 1) {
+        for (size_t hi = 0; hi < n; hi++) fn(ctx, hi);
+        return;
+    }
+    stream_job *jobs = (stream_job *)calloc(threads, sizeof(stream_job));
+    pthread_t *tids = (pthread_t *)calloc(threads, sizeof(pthread_t));
+    for (size_t t = 0; t < threads; t++) {
+        stream_job j = {fn, ctx, n * t / threads, n * (t + 1) / threads};
+        jobs[t] = j;
+        pthread_create(&tids[t], NULL, stream_worker, &jobs[t]);
+    }
+    for (size_t t = 0; t < threads; t++) pthread_join(tids[t], NULL);
+    free(jobs);
+    free(tids);
+}
+
+typedef struct {
+    ko_cache *c;
+    const float *src;
+    size_t src_seq, offset, count;
+} quant_ctx;
+
+static void flush_one(void *ctx, size_t hi) {
+    ko_cache *c = ((quant_ctx *)ctx)->c;
+    size_t r = c->residual_length;
+    append_key_block(&c->key_streams[hi], c->key_residual + hi * r * c->head_dim, r, c->head_dim,
+                     c->bits, c->group_size);
+}
+
+static void value_prefix_one(void *ctx, size_t hi) {
+    const quant_ctx *q = (const quant_ctx *)ctx;
+    ko_cache *c = q->c;
+    size_t cap = c->residual_length;
+    append_value_block(&c->value_streams[hi], c->value_residual + hi * cap * c->head_dim, q->count,
+                       c->head_dim, c->bits, c->group_size);
+}
+
+static void value_input_one(void *ctx, size_t hi) {
+    const quant_ctx *q = (const quant_ctx *)ctx;
+    ko_cache *c = q->c;
+    append_value_block(&c->value_streams[hi],
+                       q->src + hi * q->src_seq * c->head_dim + q->offset * c->head_dim, q->count,
+                       c->head_dim, c->bits, c->group_size);
+}
+
 /* cache.rs:407-430 */
 static void flush_keys(ko_cache *c) {
-    size_t r = c->residual_length;
-    for (size_t hi = 0; hi < c->batch * c->heads; hi++)
-        append_key_block(&c->key_streams[hi], c->key_residual + hi * r * c->head_dim, r,
-                         c->head_dim, c->bits, c->group_size);
+    quant_ctx q = {c, NULL, 0, 0, 0};
+    for_streams(c->batch * c->heads, flush_one, &q);
     c->key_res_len = 0;
 }
 
@@ -644,18 +711,15 @@ static void append_keys(ko_cache *c, const float *keys, size_t seq) {
 /* cache.rs:486-510 */
 static void quantize_value_residual_prefix(ko_cache *c, size_t n) {
     if (n == 0) return;
-    size_t cap = c->residual_length;
-    for (size_t hi = 0; hi < c->batch * c->heads; hi++)
-        append_value_block(&c->value_streams[hi], c->value_residual + hi * cap * c->head_dim, n,
-                           c->head_dim, c->bits, c->group_size);
+    quant_ctx q = {c, NULL, 0, 0, n};
+    for_streams(c->batch * c->heads, value_prefix_one, &q);
 }
 
 /* cache.rs:512-530 */
 static void quantize_value_input(ko_cache *c, const float *values, size_t seq, size_t offset,
                                  size_t count) {
-    for (size_t hi = 0; hi < c->batch * c->heads; hi++)
-        append_value_block(&c->value_streams[hi], values + hi * seq * c->head_dim + offset * c->head_dim,
-                           count, c->head_dim, c->bits, c->group_size);
+    quant_ctx q = {c, values, seq, offset, count};
+    for_streams(c->batch * c->heads, value_input_one, &q);
 }
 
 /* cache.rs:432-484 */
@@ -847,6 +911,163 @@ int ko_cache_attention_f64(const ko_cache *c, const float *query, size_t num_q_h
     return KO_OK;
 }
 
+/* fp64 evaluation of the same attention, streamed: token blocks of one
+ * stream are dequantized exactly as ko_cache_dequantize does (fmaf(code,
+ * scale, zero); residual and suffix rows as stored), then logits, softmax and
+ * the value mix run in double in the same order as ko_cache_attention_f64, so
+ * the result equals it bit for bit.  Worker threads take whole streams (every
+ * query head of a kv head), so memory stays at one token block plus the
+ * logits of one stream per thread.  Not a reference routine: it attributes the
+ * device-vs-reference difference at sizes where the whole dequantized cache
+ * would not fit in host memory. */
+enum { F64_BLOCK = 512 };
+
+/* Rows [t0, t1) of stream hi (keys: axis 0, values: axis 1) over the packed
+ * region, the residual / value window and then the session suffix. */
+static void dequant_rows(const ko_cache *c, const float *local, size_t local_len, size_t hi,
+                         int axis, size_t t0, size_t t1, float *out) {
+    size_t dim = c->head_dim, G = c->group_size, bits = c->bits;
+    size_t cap = c->residual_length;
+    const ko_stream *st = axis == 0 ? &c->key_streams[hi] : &c->value_streams[hi];
+    size_t q = st->tokens;
+    size_t res_len = axis == 0 ? c->key_res_len : c->value_res_len;
+    const float *res = (axis == 0 ? c->key_residual : c->value_residual) + hi * cap * dim;
+    uint32_t mask = (1u << bits) - 1u;
+    size_t per_word = 32 / bits;
+    for (size_t t = t0; t < t1; t++) {
+        float *row = out + (t - t0) * dim;
+        if (t < q) {
+            if (axis == 0) {
+                size_t g = t / G, pos = t % G, ipc = G * bits / 32;
+                for (size_t d = 0; d < dim; d++) {
+                    size_t meta = 2 * (g * dim + d);
+                    uint32_t w = st->codes[(g * dim + d) * ipc + pos / per_word];
+                    float code = (float)((w >> ((pos % per_word) * bits)) & mask);
+                    row[d] = fmaf(code, st->params[meta], st->params[meta + 1]);
+                }
+            } else {
+                size_t n_ch = dim / G, ipg = G * bits / 32;
+                for (size_t cg = 0; cg < n_ch; cg++) {
+                    size_t meta = 2 * (t * n_ch + cg);
+                    for (size_t i = 0; i < G; i++) {
+                        uint32_t w = st->codes[(t * n_ch + cg) * ipg + i / per_word];
+                        float code = (float)((w >> ((i % per_word) * bits)) & mask);
+                        row[cg * G + i] = fmaf(code, st->params[meta], st->params[meta + 1]);
+                    }
+                }
+            }
+        } else if (t < q + res_len) {
+            memcpy(row, res + (t - q) * dim, dim * sizeof(float));
+        } else {
+            memcpy(row, local + (hi * local_len + (t - q - res_len)) * dim, dim * sizeof(float));
+        }
+    }
+}
+
+typedef struct {
+    const ko_cache *c;
+    const float *lk, *lv;
+    size_t llen;
+    const float *query;
+    size_t num_q_heads;
+    float scale;
+    double *out;
+    size_t begin, end; /* streams */
+} f64_job;
+
+static void run_f64_streams(const f64_job *j) {
+    const ko_cache *c = j->c;
+    size_t dim = c->head_dim, group = j->num_q_heads / c->heads;
+    size_t total = c->seq_len + j->llen;
+    float *buf = (float *)malloc((size_t)F64_BLOCK * dim * sizeof(float));
+    double *lg = (double *)malloc((total ? total : 1) * group * sizeof(double));
+    double *mx = (double *)malloc(group * sizeof(double));
+    double *sum = (double *)malloc(group * sizeof(double));
+    for (size_t hi = j->begin; hi < j->end; hi++) {
+        size_t b = hi / c->heads, kvh = hi % c->heads;
+        const float *q0 = j->query + (b * j->num_q_heads + kvh * group) * dim;
+        double *y0 = j->out + (b * j->num_q_heads + kvh * group) * dim;
+        for (size_t h = 0; h < group; h++) {
+            mx[h] = -INFINITY;
+            sum[h] = 0.0;
+        }
+        for (size_t t0 = 0; t0 < total; t0 += F64_BLOCK) {
+            size_t t1 = t0 + F64_BLOCK < total ? t0 + F64_BLOCK : total;
+            dequant_rows(c, j->lk, j->llen, hi, 0, t0, t1, buf);
+            for (size_t h = 0; h < group; h++) {
+                const float *q = q0 + h * dim;
+                for (size_t t = t0; t < t1; t++) {
+                    const float *k = buf + (t - t0) * dim;
+                    double dot = 0.0;
+                    for (size_t d = 0; d < dim; d++) dot += (double)q[d] * (double)k[d];
+                    double l = dot * (double)j->scale;
+                    lg[h * total + t] = l;
+                    if (l > mx[h]) mx[h] = l;
+                }
+            }
+        }
+        for (size_t h = 0; h < group; h++)
+            for (size_t t = 0; t < total; t++) {
+                lg[h * total + t] = exp(lg[h * total + t] - mx[h]);
+                sum[h] += lg[h * total + t];
+            }
+        for (size_t i = 0; i < group * dim; i++) y0[i] = 0.0;
+        for (size_t t0 = 0; t0 < total; t0 += F64_BLOCK) {
+            size_t t1 = t0 + F64_BLOCK < total ? t0 + F64_BLOCK : total;
+            dequant_rows(c, j->lv, j->llen, hi, 1, t0, t1, buf);
+            for (size_t h = 0; h < group; h++) {
+                double *y = y0 + h * dim;
+                for (size_t t = t0; t < t1; t++) {
+                    double w = lg[h * total + t] / sum[h];
+                    const float *v = buf + (t - t0) * dim;
+                    for (size_t d = 0; d < dim; d++) y[d] += w * (double)v[d];
+                }
+            }
+        }
+    }
+    free(buf);
+    free(lg);
+    free(mx);
+    free(sum);
+}
+
+static void *f64_thread(void *arg) {
+    run_f64_streams((const f64_job *)arg);
+    return NULL;
+}
+
+static void attention_f64_streams(const ko_cache *c, const float *lk, const float *lv, size_t llen,
+                                  const float *query, size_t num_q_heads, float scale, double *out,
+                                  int threads) {
+    size_t n = c->batch * c->heads;
+    for (size_t i = 0; i < c->batch * num_q_heads * c->head_dim; i++) out[i] = 0.0;
+    if (c->seq_len + llen == 0) return;
+    if (threads < 1) threads = 1;
+    if ((size_t)threads > n) threads = (int)n;
+    f64_job *jobs = (f64_job *)calloc((size_t)threads, sizeof(f64_job));
+    pthread_t *tids = (pthread_t *)calloc((size_t)threads, sizeof(pthread_t));
+    for (int t = 0; t < threads; t++) {
+        f64_job j = {c, lk, lv, llen, query, num_q_heads, scale, out, n * (size_t)t / (size_t)threads,
+                     n * (size_t)(t + 1) / (size_t)threads};
+        jobs[t] = j;
+    }
+    if (threads == 1) {
+        run_f64_streams(&jobs[0]);
+    } else {
+        for (int t = 0; t < threads; t++) pthread_create(&tids[t], NULL, f64_thread, &jobs[t]);
+        for (int t = 0; t < threads; t++) pthread_join(tids[t], NULL);
+    }
+    free(jobs);
+    free(tids);
+}
+
+int ko_cache_attention_f64_threads(const ko_cache *c, const float *query, size_t num_q_heads,
+                                   float scale, double *out, int threads) {
+    if (num_q_heads == 0 || num_q_heads % c->heads != 0) return KO_QUERY_HEADS;
+    attention_f64_streams(c, NULL, NULL, 0, query, num_q_heads, scale, out, threads);
+    return KO_OK;
+}
+
 /* cache.rs:282-325 */
 void ko_cache_dequantize(const ko_cache *c, float *keys, float *values) {
     size_t dim = c->head_dim, seq = c->seq_len, cap = c->residual_length;
@@ -1029,6 +1250,18 @@ int ko_session_attention(const ko_session *s, const float *query, size_t query_l
     if (st->seq_len + s->local_len == 0) return KO_OK;
     attention_pairs(st, s->local_keys, s->local_values, s->local_len, query, num_q_heads, scale, out,
                     threads);
+    return KO_OK;
+}
+
+/* fp64 evaluation of a session's attention over prefix + suffix (the same
+ * streamed evaluation as ko_cache_attention_f64_threads; not a reference
+ * routine, used to attribute differences at full size). */
+int ko_session_attention_f64(const ko_session *s, const float *query, size_t num_q_heads,
+                             float scale, double *out, int threads) {
+    const ko_cache *st = &s->prefix->state;
+    if (num_q_heads == 0 || num_q_heads % st->heads != 0) return KO_QUERY_HEADS;
+    attention_f64_streams(st, s->local_keys, s->local_values, s->local_len, query, num_q_heads,
+                          scale, out, threads);
     return KO_OK;
 }
 

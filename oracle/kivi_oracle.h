@@ -71,6 +71,13 @@ int ko_cache_attention_batch_range(const ko_cache *c, const float *query, size_t
 /* Same attention evaluated in fp64 over the fp32 dequantized cache (for error attribution). */
 int ko_cache_attention_f64(const ko_cache *c, const float *query, size_t num_q_heads,
                            float scale, double *out);
+/* The same fp64 evaluation streamed over token blocks, worker threads over
+ * streams; bit-identical to ko_cache_attention_f64 for any thread count. */
+int ko_cache_attention_f64_threads(const ko_cache *c, const float *query, size_t num_q_heads,
+                                   float scale, double *out, int threads);
+/* Worker threads for the per-stream loops of the append path (default 1);
+ * results are bit-identical for any count. */
+void ko_set_append_threads(int threads);
 /* cache.rs:282-325 ; keys/values sized batch*heads*seq*head_dim */
 void ko_cache_dequantize(const ko_cache *c, float *keys, float *values);
 /* cache.rs:362-380 ; out[10] = tokens, key_code, key_meta, value_code, value_meta,
@@ -94,6 +101,10 @@ int ko_session_append(ko_session *s, const float *keys, size_t keys_len, const f
 int ko_session_attention(const ko_session *s, const float *query, size_t query_len,
                          size_t num_q_heads, float scale, float *out, int threads, ko_error *err);
 size_t ko_session_question_tokens(const ko_session *s);
+/* fp64 evaluation of a session's attention over prefix + suffix (not a
+ * reference routine; error attribution at full size). */
+int ko_session_attention_f64(const ko_session *s, const float *query, size_t num_q_heads,
+                             float scale, double *out, int threads);
 
 /* quant.rs:154-233: codes/params concatenated over the batch*heads streams, in
  * PackedStream order. Pass NULL outputs to query sizes. */

@@ -1,0 +1,228 @@
+"""Parity at BASELINE.json's full configuration sizes, one decode step each.
+
+Every case fills the device cache and the CPU oracle with the same seeded
+inputs (generated on the GPU, copied to the host for the oracle), runs one
+decode step of the reference's hot path -- append one token (the key residual
+completes and flushes in that step, one value token is evicted and
+quantized), then attend -- and checks:
+
+* exported PackedStreams (codes, scale, zero) word for word on a sample of
+  streams, after the flush (quant.rs:275-377 / cache.rs:382-484);
+* memory() field for field (cache.rs:362-380);
+* attention (cache.rs:224-279, prefix.rs:228-290): max-abs <= 1e-4 and rel-L2
+  <= 1e-5 against the oracle's fp64 evaluation of the same quantized cache, and
+  the gap to the oracle's fp32 output no larger than the reference's own fp32
+  error plus those bars (its sequential fp32 sums, attention.rs:302-333, drift
+  from exact arithmetic over long contexts).
+
+Sizes: config 1 (batch 16, 8 kv / 32 q heads, 2-bit, 32768 tokens), config 2
+(batch 8, 8 kv / 64 q heads, 4-bit, 131072 tokens, 1% of key channels x20),
+config 3 (a 65536-token shared prefix, 32 sessions with 64-token suffixes) and
+config 4 (batch 1, 8 kv / 32 q heads, 1048576 tokens, on one GPU).
+Set KIVI_PARITY_LOG to a file path to record the measured errors (one JSON
+line per case).
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+from helpers import max_abs, rel_l2
+
+pytestmark = [pytest.mark.gpu, pytest.mark.slow]
+
+ATOL = 1e-4
+RTOL_L2 = 1e-5
+HOST_THREADS = os.cpu_count() or 1
+
+
+@pytest.fixture(scope="module")
+def env():
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import kivi_cache as K
+
+    K.lib()
+    O.set_append_threads(HOST_THREADS)
+    yield torch, K
+    O.set_append_threads(1)
+
+
+def _log(case, **fields):
+    path = os.environ.get("KIVI_PARITY_LOG")
+    if path:
+        with open(path, "a") as f:
+            f.write(json.dumps(dict(case=case, **fields)) + "\n")
+
+
+def channel_scales(seed, heads, dim, outlier):
+    rng = np.random.default_rng(seed)
+    if outlier == "x20":
+        mask = rng.random((heads, dim)) < 0.01
+        return np.where(mask, np.float32(20.0), np.float32(1.0)).astype(np.float32)
+    return np.exp(rng.standard_normal((heads, dim))).astype(np.float32)
+
+
+class Source:
+    """Seeded N(0,1) K/V (keys times per-channel scales) and queries, drawn on
+    the GPU; the oracle gets host copies of the same bits."""
+
+    def __init__(self, torch, seed, chs):
+        self.torch = torch
+        self.g = torch.Generator(device="cuda")
+        self.g.manual_seed(seed)
+        self.chs = torch.from_numpy(chs).cuda()
+
+    def kv(self, B, H, n, D):
+        t = self.torch
+        k = t.randn((B, H, n, D), generator=self.g, device="cuda")
+        k.mul_(self.chs[None, :, None, :])
+        v = t.randn((B, H, n, D), generator=self.g, device="cuda")
+        return k, v
+
+    def q(self, n):
+        return self.torch.randn(n, generator=self.g, device="cuda")
+
+
+def host(t):
+    return t.cpu().numpy().reshape(-1)
+
+
+def prefill(cache, ocache, src, B, H, D, tokens):
+    """Chunked appends of `tokens` tokens to both (appends are chunk-invariant,
+    tests/cache.rs:78-104); chunks of about 256 MB of keys."""
+    chunk = max(128, (256 << 20) // (B * H * D * 4) // 128 * 128)
+    done = 0
+    while done < tokens:
+        n = min(chunk, tokens - done)
+        k, v = src.kv(B, H, n, D)
+        cache.append_dev(k, v, n)
+        ocache.append(host(k), host(v), n)
+        done += n
+        del k, v
+
+
+def assert_streams_equal(cache, ocache, streams):
+    for hi in streams:
+        for axis in (0, 1):
+            gc, gp = cache.export_stream(hi, axis)
+            oc, op = ocache.export_stream(hi, axis)
+            assert gc.shape == oc.shape and (gc == oc).all(), (hi, axis)
+            assert (gp.view(np.uint32) == op.view(np.uint32)).all(), (hi, axis)
+
+
+def assert_memory_equal(cache, ocache):
+    gm, om = cache.memory(), ocache.memory()
+    for k, v in om.items():
+        assert getattr(gm, k) == v, k
+
+
+def check_attention(case, got, ref, ref64):
+    """The bars hold against the exact (fp64) evaluation of the same quantized
+    cache; against the reference's fp32 output the gap may not exceed the
+    reference's own fp32 error plus the bar.  At these sizes the reference's
+    sequential fp32 sums are themselves further from the exact value than the
+    bars (config 2: 1.3e-4 rel-L2, 4.7e-4 max-abs), so no faithful parallel
+    evaluation can sit within 1e-4 of its fp32 output."""
+    abs64, abs32 = max_abs(got, ref64), max_abs(got, ref)
+    rel64, rel32 = rel_l2(got, ref64), rel_l2(got, ref)
+    own_abs, own_rel = max_abs(ref, ref64), rel_l2(ref, ref64)
+    _log(case, max_abs_vs_fp64=abs64, rel_l2_vs_fp64=rel64, max_abs_vs_fp32=abs32,
+         rel_l2_vs_fp32=rel32, reference_fp32_max_abs_vs_fp64=own_abs,
+         reference_fp32_rel_l2_vs_fp64=own_rel)
+    assert np.isfinite(got).all()
+    assert abs64 <= ATOL, (abs64, own_abs)
+    assert rel64 <= RTOL_L2, (rel64, own_rel)
+    assert abs32 <= own_abs + ATOL, (abs32, own_abs)
+    assert rel32 <= own_rel + RTOL_L2, (rel32, own_rel)
+
+
+def decode_case(env, case, B, H, Hq, bits, ctx, outlier, seed):
+    """Prefill ctx - 1 tokens, then one decode step (RuntimeKv::decode,
+    runtime.rs:46-56) whose append completes the key residual (ctx is a
+    multiple of R = 128) and flushes it."""
+    torch, K = env
+    D = 128
+    cfg = K.KiviConfig.try_new(bits, 32, 128)
+    cache = K.KiviCache(cfg, B, H, D)
+    cache.reserve(ctx)
+    ocache = O.KiviCache(O.KiviConfig(bits, 32, 128), B, H, D)
+    src = Source(torch, seed, channel_scales(seed + 1, H, D, outlier))
+    prefill(cache, ocache, src, B, H, D, ctx - 1)
+    assert cache.key_residual_len() == 127
+    k, v = src.kv(B, H, 1, D)
+    q = src.q(B * Hq * D)
+    scale = float(np.float32(1.0) / np.sqrt(np.float32(D)))
+    out = torch.empty(B * Hq * D, device="cuda")
+    cache.decode_dev(k, v, q, Hq, scale, out)
+    torch.cuda.synchronize()
+    K.device_wait_status(0)
+    got = host(out)
+    ocache.append(host(k), host(v), 1)
+    assert cache.key_residual_len() == 0 and ocache.key_residual_len() == 0  # flushed
+    assert cache.quantized_key_tokens() == ctx
+    qh = host(q)
+    ref = ocache.attention(qh, Hq, scale, threads=HOST_THREADS)
+    ref64 = ocache.attention_f64(qh, Hq, scale, threads=HOST_THREADS)
+    n = B * H
+    assert_streams_equal(cache, ocache, sorted({0, n // 3, n - 1}))
+    assert_memory_equal(cache, ocache)
+    check_attention(case, got, ref, ref64)
+
+
+def test_config1_full_size_decode_step(env):
+    decode_case(env, "config1", 16, 8, 32, 2, 32768, "lognormal", 101)
+
+
+def test_config2_full_size_decode_step(env):
+    decode_case(env, "config2", 8, 8, 64, 4, 131072, "x20", 202)
+
+
+def test_config4_full_size_decode_step_on_one_gpu(env):
+    decode_case(env, "config4", 1, 8, 32, 2, 1 << 20, "lognormal", 404)
+
+
+def test_config3_full_size_sessions_decode_step(env):
+    """A 65536-token document frozen as a SharedPrefix, 32 RagSessions with
+    64-token suffixes appended in one batched call, then one decode step of
+    every session (one token appended to each suffix, then attention over
+    prefix + suffix) in one batched call (prefix.rs:173-290)."""
+    torch, K = env
+    B, H, Hq, D, doc, S, suf = 1, 8, 32, 128, 65536, 32, 64
+    cache = K.KiviCache(K.KiviConfig(), B, H, D)
+    cache.reserve(doc)
+    ocache = O.KiviCache(O.KiviConfig(), B, H, D)
+    src = Source(torch, 303, channel_scales(304, H, D, "lognormal"))
+    prefill(cache, ocache, src, B, H, D, doc)
+    prefix, oprefix = cache.share_prefix(), ocache.share_prefix()
+    sessions = [prefix.session() for _ in range(S)]
+    osessions = [oprefix.session() for _ in range(S)]
+    for s in sessions:
+        s.reserve(suf + 1)
+    ks, vs = src.kv(S, B * H, suf, D)  # [session, b*h, token, d]
+    K.sessions_append(sessions, host(ks), host(vs), suf)
+    for i, o in enumerate(osessions):
+        o.append(host(ks[i]), host(vs[i]), suf)
+    k1, v1 = src.kv(S, B * H, 1, D)
+    q = src.q(S * B * Hq * D)
+    scale = float(np.float32(1.0) / np.sqrt(np.float32(D)))
+    got = K.sessions_decode_batched(sessions, host(k1), host(v1), host(q), Hq, scale)
+    K.device_wait_status(0)
+    qh = host(q).reshape(S, -1)
+    got = got.reshape(S, -1)
+    ref = np.empty_like(got)
+    ref64 = np.empty(got.shape, np.float64)
+    for i, o in enumerate(osessions):
+        o.append(host(k1[i]), host(v1[i]), 1)
+        ref[i] = o.attention(qh[i], Hq, scale, threads=HOST_THREADS)
+        ref64[i] = o.attention_f64(qh[i], Hq, scale, threads=HOST_THREADS)
+    for s in sessions:
+        assert s.question_tokens() == suf + 1
+    assert_streams_equal(cache, ocache, [0, H - 1])
+    check_attention("config3", got.reshape(-1), ref.reshape(-1), ref64.reshape(-1))
+    for i in range(S):  # and session by session
+        assert max_abs(got[i], ref64[i]) <= ATOL
+        assert rel_l2(got[i], ref64[i]) <= RTOL_L2
