@@ -13,15 +13,15 @@
 // reference's PackedStream order, quant.rs:37-44) from HBM into its own
 // shared-memory stages with bulk async copies (cp.async.bulk + mbarrier
 // complete_tx, each copy into this CTA only), one group ahead of the one it
-// computes, and first rewrites each landed group's parameters in place
-// (scaled scales, folded zero points).
+// computes, and reads the landed (scale, zero) pairs as they are.
 //
 // Per group, with mid = 2^(bits-1) (an integer, so every constant below is an
 // exact fp16), the dequantize-and-dot of attention.rs:143-269 is
 //     logit[t][h] = sum_d (code[t][d] - mid) s_k[d] q[h][d] + sum_d q[h][d] z'_k[d]
 //     o[h][d]    += sum_t (code[t][d] - mid) s_v[t] p[t][h] + sum_t p[t][h] z'_v[t]
-// with z' = z + mid * s (folded when the stage lands).  The code sums run on the
-// tensor cores as m16n8k16 f16 MMAs with fp32 accumulation:
+// with z' = z + mid * s (folded per channel or token as the parameters are
+// read).  The code sums run on the tensor cores as m16n8k16 f16 MMAs with fp32
+// accumulation:
 //   * A = codes, exact: one byte permute gathers the byte holding four
 //     (2-bit) or two (4-bit) codes of two K neighbours into the two fp16
 //     halves of a register; per code position one LOP3 ORs the code into the
@@ -31,10 +31,16 @@
 //     significant bits): the fp32 value truncated to 11 bits and the exact
 //     remainder, each in its own N column, so the tensor-core product carries
 //     ~22 bits of the fp32 operand.  Power-of-two scales keep B in fp16
-//     range: 2^(14 - e_q) per query head (|q| < 2^e_q), 2^-e_s per key group
-//     (s_k < 2^e_s) and 2^(3 - e_v) per value group (s_v < 2^e_v, and
-//     p < 2^11 under the lazy softmax rescale below); each is undone exactly
-//     on the fp32 side.
+//     range: 2^(14 - e_q) per query head (|q| < 2^e_q), 2^-e_s per stream
+//     (every key scale of the stream < 2^e_s) and 2^(3 - e_v) per stream
+//     (every value scale < 2^e_v, and p < 2^11 under the lazy softmax
+//     rescale below), the stream bounds kept by the append kernels
+//     (Store::kbound / vbound); each is undone exactly on the fp32 side (the
+//     value factor rides in the softmax weights and the slot's m).  The codes
+//     must stay centred: with codes 0..levels as exact fp16 subnormals (one AND
+//     per register instead of LOP3 + HFMA2) the larger, cancelling sums lost
+//     an order of magnitude of accuracy on the B200 (3.7e-5 rel-L2 against
+//     fp64 at 32k tokens, against 0.9e-6 centred).
 // The zero-point sums and the online softmax stay in fp32 on the CUDA cores.
 // The softmax reference point moves only when a logit exceeds it by more than
 // 2^11 (in exp2 units), which skips almost every rescale of the accumulators.
@@ -275,42 +281,6 @@ template <int BITS> struct Perm {
     }
 };
 
-// Rewrite of one landed stage's parameters by the warp that consumes it (all
-// 32 lanes; the stage belongs to that warp alone).  Keys (s, z) per channel ->
-// (s * 2^-e_s, z + mid s) in place.  Values: entry (token t, channel group g)
-// -> s' = s * 2^(3 - e_v), z' = z + mid s, stored per token as two float4
-// halves (s'0, s'1, z'0, z'1) and (s'2, s'3, z'2, z'3), the halves swapped for
-// tokens with bit 3 set so that the consumers' loads of eight tokens
-// (c + 8 par) hit distinct banks.  exps = (e_s, e_v).
-template <int BITS>
-__device__ __forceinline__ void prep_stage(unsigned char *base, int2 *exps, int lane) {
-    using TG = TcGeom<BITS>;
-    constexpr float kMid = BITS == 2 ? 2.0f : 8.0f;
-    float4 *kp = reinterpret_cast<float4 *>(base + TG::KC_BYTES);
-    float4 *vp = reinterpret_cast<float4 *>(base + TG::KC_BYTES + TG::KP_BYTES + TG::VC_BYTES);
-    // float4 index l and l + 32 (conflict-free): keys channels 2l, 2l+1 and
-    // 64 + 2l, 65 + 2l; values token l/2 and 16 + l/2, channel groups 2(l&1), +1
-    const float4 k0 = kp[lane], k1 = kp[lane + 32], v0 = vp[lane], v1 = vp[lane + 32];
-    float ks = fmaxf(fmaxf(fabsf(k0.x), fabsf(k0.z)), fmaxf(fabsf(k1.x), fabsf(k1.z)));
-    float vs = fmaxf(fmaxf(fabsf(v0.x), fabsf(v0.z)), fmaxf(fabsf(v1.x), fabsf(v1.z)));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        ks = fmaxf(ks, __shfl_xor_sync(0xffffffffu, ks, o));
-        vs = fmaxf(vs, __shfl_xor_sync(0xffffffffu, vs, o));
-    }
-    const int es = exp_ceil(ks), ev = exp_ceil(vs);
-    const float fk = exp2i(-es), fv = exp2i(3 - ev);
-    kp[lane] = make_float4(k0.x * fk, fmaf(kMid, k0.x, k0.y), k0.z * fk, fmaf(kMid, k0.z, k0.w));
-    kp[lane + 32] =
-        make_float4(k1.x * fk, fmaf(kMid, k1.x, k1.y), k1.z * fk, fmaf(kMid, k1.z, k1.w));
-    const int t0 = lane >> 1, h = lane & 1;     // token t0 (bit 3 of t0 and t0 + 16 agree)
-    const int slot = 2 * t0 + (h ^ ((t0 >> 3) & 1));
-    vp[slot] = make_float4(v0.x * fv, v0.z * fv, fmaf(kMid, v0.x, v0.y), fmaf(kMid, v0.z, v0.w));
-    vp[slot + 32] =
-        make_float4(v1.x * fv, v1.z * fv, fmaf(kMid, v1.x, v1.y), fmaf(kMid, v1.z, v1.w));
-    if (lane == 0) *exps = make_int2(es, ev);
-}
-
 // Issues the four bulk copies of one group (stream s, group g) into stage dst.
 template <int BITS>
 __device__ __forceinline__ void issue_group(const TcArgs &a, int64_t s, int64_t g,
@@ -338,8 +308,7 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_
     constexpr int kHeads = NT * 4;
     extern __shared__ __align__(128) unsigned char smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * TG::STAGE);
-    int2 *gexp = reinterpret_cast<int2 *>(full + kStages);                // [stage] (e_s, e_v)
-    float *pbuf = reinterpret_cast<float *>(gexp + kStages);              // [warp][kHeads][kPStride]
+    float *pbuf = reinterpret_cast<float *>(full + kStages);              // [warp][kHeads][kPStride]
     float *Ow = pbuf + kConsumers * kHeads * kPStride;                   // [warp][kHeads][128]
     float *Mw = Ow + kConsumers * kHeads * kD;                           // [warp][kHeads]
     float *Lw = Mw + kConsumers * kHeads;                                // [warp][kHeads]
@@ -378,14 +347,13 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_
     const int r = lane >> 2, c = lane & 3;
     const int par = r & 1, hb = r >> 1;
     const Perm<BITS> perm(r);
+    constexpr float kMid = BITS == 2 ? 2.0f : 8.0f;
     // lane's code-word offsets inside a stage (words): keys channel 2c, word
     // holding tokens 4r..4r+3; values token c, word holding channels 4r..4r+3
     const int kw = 2 * c * IPC + (BITS == 2 ? (r >> 2) : (r >> 1));
     const int vw = c * 4 * IPC + (BITS == 2 ? (r >> 2) : (r >> 1));
     // K position (value tiles) of this lane's logit tokens 4r + j: 2j + koff
     const int koff = 16 * (r >> 2) + ((r & 1) ? 1 : 0) + ((r & 2) ? 8 : 0);
-    // value parameter halves of this lane's tokens (see prep_stage)
-    const int vsw = par; // tokens 8par + c (+4) have bit 3 = par
     float *pw = pbuf + warp * (kHeads * kPStride);
     bool ok = true;
 
@@ -396,9 +364,19 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_
         const int n_seg = (int)(seg_end - f);
         const int b = (int)(s / a.H), kvh = (int)(s - (int64_t)b * a.H);
 
-        // ---- query rows of this stream: q' = q * 2^(14 - e_q) per head
+        // ---- the stream's operand range factors: |key scale| < 2^es and
+        // |value scale| < 2^ev over all its packed groups (kept by the append
+        // kernels), so that q'' s < 2^14 with q'' = q 2^(14 - e_q - es), and
+        // p' s_v < 2^14 with p' = p 2^cv, cv = 3 - ev (p < 2^11 under the lazy
+        // softmax rescale below)
+        const int es = exp_ceil(__uint_as_float(a.kbound[s]));
+        const int ev = exp_ceil(__uint_as_float(a.vbound[s]));
+        const float fk = exp2i(-es);
+        const float cv = (float)(3 - min(max(ev, -120), 120));
+
+        // ---- query rows of this stream: q'' = q * 2^(14 - e_q) * 2^-es per head
         float qv[NT][8][2];
-        float fh[NT]; // per lane head c: 2^(e_q - 14) * scale * log2(e)
+        float fh[NT]; // per lane head c: 2^(e_q - 14 + es) * scale * log2(e)
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
             const int h = nt * 4 + hb;
@@ -419,11 +397,11 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_
             const float sq = exp2i(14 - eq);
 #pragma unroll
             for (int kt = 0; kt < 8; ++kt) {
-                qv[nt][kt][0] *= sq;
-                qv[nt][kt][1] *= sq;
+                qv[nt][kt][0] = qv[nt][kt][0] * sq * fk;
+                qv[nt][kt][1] = qv[nt][kt][1] * sq * fk;
             }
             const int eqc = __shfl_sync(0xffffffffu, eq, 8 * c); // head nt*4 + c
-            fh[nt] = exp2i(eqc - 14) * (a.scale * 1.4426950408889634f);
+            fh[nt] = exp2i(eqc - 14) * exp2i(es) * (a.scale * 1.4426950408889634f);
         }
 
         float mref[NT], l[NT];
@@ -446,17 +424,14 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_
                 ok = false;
                 break;
             }
-            prep_stage<BITS>(smem + st * TG::STAGE, &gexp[st], lane);
-            __syncwarp();
             const unsigned char *base = smem + st * TG::STAGE;
             const uint32_t *KC = reinterpret_cast<const uint32_t *>(base);
             const float4 *KP4 = reinterpret_cast<const float4 *>(base + TG::KC_BYTES);
             const uint32_t *VC = reinterpret_cast<const uint32_t *>(base + TG::KC_BYTES + TG::KP_BYTES);
             const float4 *VP4 = reinterpret_cast<const float4 *>(base + TG::KC_BYTES + TG::KP_BYTES +
                                                                  TG::VC_BYTES);
-            const int2 ex = gexp[st];
 
-            // ---------------- keys: B = q' s' (split), zero term q' . z'
+            // ---------------- keys: B = q'' s (split), zero term q'' . (z + mid s)
             uint32_t bk[NT][8][2];
             float zc[NT];
 #pragma unroll
@@ -464,10 +439,11 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_
 #pragma unroll
             for (int kt = 0; kt < 8; ++kt) {
                 const float4 kpz = KP4[8 * kt + c + 4 * par]; // channels 16kt + 2c + 8par (+1)
+                const float z0 = fmaf(kMid, kpz.x, kpz.y), z1 = fmaf(kMid, kpz.z, kpz.w);
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
-                    zc[nt] = fmaf(qv[nt][kt][0], kpz.y, zc[nt]);
-                    zc[nt] = fmaf(qv[nt][kt][1], kpz.w, zc[nt]);
+                    zc[nt] = fmaf(qv[nt][kt][0], z0, zc[nt]);
+                    zc[nt] = fmaf(qv[nt][kt][1], z1, zc[nt]);
                     b_frag(qv[nt][kt][0] * kpz.x, qv[nt][kt][1] * kpz.z, par, bk[nt][kt][0],
                            bk[nt][kt][1]);
                 }
@@ -479,7 +455,7 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_
                 zc[nt] += __shfl_xor_sync(0xffffffffu, zc[nt], 4);
             }
 
-            // ---------------- keys: A = codes, D = code sums per (token, head part)
+            // ---------------- keys: A = codes - mid (exact), D = code sums per (token, head part)
             float4 dk[NT][2];
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) dk[nt][0] = dk[nt][1] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -496,15 +472,14 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_
             }
 
             // ---------------- logits (exp2 units) + lazy online softmax, lane head nt*4 + c
-            const float fs = exp2i(ex.x);
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-                const float zz = __shfl_sync(0xffffffffu, zc[nt], 8 * c);
+                const float zz = __shfl_sync(0xffffffffu, zc[nt], 8 * c) * fh[nt];
                 float x[4];
-                x[0] = fmaf(dk[nt][0].x + dk[nt][0].y, fs, zz) * fh[nt]; // token 4r
-                x[1] = fmaf(dk[nt][0].z + dk[nt][0].w, fs, zz) * fh[nt]; // token 4r + 1
-                x[2] = fmaf(dk[nt][1].x + dk[nt][1].y, fs, zz) * fh[nt]; // token 4r + 2
-                x[3] = fmaf(dk[nt][1].z + dk[nt][1].w, fs, zz) * fh[nt]; // token 4r + 3
+                x[0] = fmaf(dk[nt][0].x + dk[nt][0].y, fh[nt], zz); // token 4r
+                x[1] = fmaf(dk[nt][0].z + dk[nt][0].w, fh[nt], zz); // token 4r + 1
+                x[2] = fmaf(dk[nt][1].x + dk[nt][1].y, fh[nt], zz); // token 4r + 2
+                x[3] = fmaf(dk[nt][1].z + dk[nt][1].w, fh[nt], zz); // token 4r + 3
                 float gmax = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
                 gmax = fmaxf(gmax, __shfl_xor_sync(0xffffffffu, gmax, 4));
                 gmax = fmaxf(gmax, __shfl_xor_sync(0xffffffffu, gmax, 8));
@@ -526,9 +501,11 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_
 #pragma unroll
                     for (int cg = 0; cg < 4; ++cg) zv[nt][cg] *= ab;
                 }
+                // p' = p 2^cv = 2^(x - (mref - cv))
+                const float mp = mref[nt] - cv;
                 float p[4];
 #pragma unroll
-                for (int jj = 0; jj < 4; ++jj) p[jj] = exp2f(x[jj] - mref[nt]);
+                for (int jj = 0; jj < 4; ++jj) p[jj] = exp2f(x[jj] - mp);
                 l[nt] += (p[0] + p[1]) + (p[2] + p[3]);
                 float *ph = pw + (nt * 4 + c) * kPStride + koff;
 #pragma unroll
@@ -536,32 +513,33 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_
             }
             __syncwarp();
 
-            // ---------------- values: B = p s'_v (split), zero term p . z'_v
+            // ---------------- values: B = p' s_v (split), zero term p' . (z_v + mid s_v)
             uint32_t bv[2][NT][4][2];
 #pragma unroll
             for (int kk = 0; kk < 2; ++kk) {
                 const int t0 = 16 * kk + 8 * par + c; // own K pair: tokens t0, t0 + 4
-                // halves (s'0, s'1, z'0, z'1) and (s'2, s'3, z'2, z'3) of t0 and t0 + 4
-                const float4 e00 = VP4[2 * t0 + vsw], e01 = VP4[2 * t0 + (vsw ^ 1)];
-                const float4 e10 = VP4[2 * t0 + 8 + vsw], e11 = VP4[2 * t0 + 8 + (vsw ^ 1)];
+                // (s, z) of channel groups 0, 1 and 2, 3 of tokens t0 and t0 + 4
+                const float4 e0 = VP4[2 * t0], e1 = VP4[2 * t0 + 1];
+                const float4 f0 = VP4[2 * t0 + 8], f1 = VP4[2 * t0 + 9];
+                float sa[4], sb[4], za[4], zb[4];
+                sa[0] = e0.x, za[0] = fmaf(kMid, e0.x, e0.y), sa[1] = e0.z, za[1] = fmaf(kMid, e0.z, e0.w);
+                sa[2] = e1.x, za[2] = fmaf(kMid, e1.x, e1.y), sa[3] = e1.z, za[3] = fmaf(kMid, e1.z, e1.w);
+                sb[0] = f0.x, zb[0] = fmaf(kMid, f0.x, f0.y), sb[1] = f0.z, zb[1] = fmaf(kMid, f0.z, f0.w);
+                sb[2] = f1.x, zb[2] = fmaf(kMid, f1.x, f1.y), sb[3] = f1.z, zb[3] = fmaf(kMid, f1.z, f1.w);
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                     const float2 pp = *reinterpret_cast<const float2 *>(
                         pw + (nt * 4 + hb) * kPStride + 16 * kk + 2 * c + 8 * par);
 #pragma unroll
                     for (int cg = 0; cg < 4; ++cg) {
-                        const float4 a0 = (cg < 2) ? e00 : e01, a1 = (cg < 2) ? e10 : e11;
-                        const float s0 = (cg & 1) ? a0.y : a0.x, z0 = (cg & 1) ? a0.w : a0.z;
-                        const float s1 = (cg & 1) ? a1.y : a1.x, z1 = (cg & 1) ? a1.w : a1.z;
-                        zv[nt][cg] = fmaf(pp.x, z0, zv[nt][cg]);
-                        zv[nt][cg] = fmaf(pp.y, z1, zv[nt][cg]);
-                        b_frag(pp.x * s0, pp.y * s1, par, bv[kk][nt][cg][0], bv[kk][nt][cg][1]);
+                        zv[nt][cg] = fmaf(pp.x, za[cg], zv[nt][cg]);
+                        zv[nt][cg] = fmaf(pp.y, zb[cg], zv[nt][cg]);
+                        b_frag(pp.x * sa[cg], pp.y * sb[cg], par, bv[kk][nt][cg][0], bv[kk][nt][cg][1]);
                     }
                 }
             }
 
             // ---------------- values: A = codes (channels x tokens), fresh sums per group
-            const float fvv = exp2i(ex.y - 3);
 #pragma unroll
             for (int cg = 0; cg < 4; ++cg) {
                 float4 t[NT][2];
@@ -586,15 +564,15 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_
 #pragma unroll
                     for (int jm = 0; jm < 2; ++jm) {
                         float4 &r4 = acc[nt][2 * cg + jm];
-                        r4.x = fmaf(t[nt][jm].x, fvv, r4.x);
-                        r4.y = fmaf(t[nt][jm].y, fvv, r4.y);
-                        r4.z = fmaf(t[nt][jm].z, fvv, r4.z);
-                        r4.w = fmaf(t[nt][jm].w, fvv, r4.w);
+                        r4.x += t[nt][jm].x;
+                        r4.y += t[nt][jm].y;
+                        r4.z += t[nt][jm].z;
+                        r4.w += t[nt][jm].w;
                     }
                 }
             }
-            // the stage is free: order this warp's reads and rewrites of it
-            // before the bulk copy of its group i + kStages
+            // the stage is free: order this warp's reads of it before the bulk
+            // copy of its group i + kStages
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
             issue_next();
@@ -653,8 +631,8 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_
             float *pml = a.part_ml + row * a.parts * 2;
             po[slot * kD + d] = O;
             if (d == 0) {
-                // the merge works in natural-log units
-                pml[slot * 2 + 0] = M * 0.6931471805599453f;
+                // the merge works in natural-log units; l and o carry p' = p 2^cv
+                pml[slot * 2 + 0] = (M - cv) * 0.6931471805599453f;
                 pml[slot * 2 + 1] = L;
             }
             if (last) {
@@ -685,7 +663,7 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_
 }
 
 template <int BITS, int NT> size_t tc_smem() {
-    return (size_t)kStages * TcGeom<BITS>::STAGE + kStages * (sizeof(uint64_t) + sizeof(int2)) +
+    return (size_t)kStages * TcGeom<BITS>::STAGE + kStages * sizeof(uint64_t) +
            (size_t)kConsumers * NT * 4 * (kPStride + kD + 2) * sizeof(float);
 }
 

@@ -230,6 +230,8 @@ void free_store(Store &st) {
     dfree(st.vparams);
     dfree(st.kres);
     dfree(st.vres);
+    dfree(st.kbound);
+    dfree(st.vbound);
     st.cap = 0;
 }
 
@@ -567,6 +569,8 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
                 t.part_o = part_o;
                 t.parts = parts;
                 t.rows_per_set = (int64_t)rows1;
+                t.kbound = p.st.kbound;
+                t.vbound = p.st.vbound;
                 CUDA_TRY(kivi::launch_attention_tc(t, (int)p.cfg.bits, (int)ns, stream),
                          "attention (tensor cores)");
             }
@@ -961,14 +965,19 @@ int32_t kivi_cache_new(const kivi_config *config, uint64_t batch, uint64_t num_k
     kivi_cache *h = new kivi_cache();
     h->s = s;
     const size_t res = (size_t)s.n() * s.cfg.residual_length * s.D;
+    const size_t n = (size_t)s.n();
     cudaError_t e;
     if ((e = cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking)) != cudaSuccess ||
         (e = cudaEventCreateWithFlags(&h->dev_done, cudaEventDisableTiming)) != cudaSuccess ||
         (e = cudaEventRecord(h->dev_done, h->stream)) != cudaSuccess ||
         (e = dalloc(&h->s.st.kres, res)) != cudaSuccess ||
         (e = dalloc(&h->s.st.vres, res)) != cudaSuccess ||
+        (e = dalloc(&h->s.st.kbound, n)) != cudaSuccess ||
+        (e = dalloc(&h->s.st.vbound, n)) != cudaSuccess ||
         (e = cudaMemsetAsync(h->s.st.kres, 0, res * 4, h->stream)) != cudaSuccess ||
         (e = cudaMemsetAsync(h->s.st.vres, 0, res * 4, h->stream)) != cudaSuccess ||
+        (e = cudaMemsetAsync(h->s.st.kbound, 0, n * 4, h->stream)) != cudaSuccess ||
+        (e = cudaMemsetAsync(h->s.st.vbound, 0, n * 4, h->stream)) != cudaSuccess ||
         (e = cudaStreamSynchronize(h->stream)) != cudaSuccess) {
         free_store(h->s.st);
         if (h->dev_done) cudaEventDestroy(h->dev_done);
@@ -1409,7 +1418,9 @@ int32_t kivi_cache_share_prefix(const kivi_cache *h, kivi_prefix **out, kivi_err
         (e = dalloc(&p->s.st.vcodes, n * kivi::code_stride(g, cap))) != cudaSuccess ||
         (e = dalloc(&p->s.st.vparams, n * kivi::vparam_stride(g, cap))) != cudaSuccess ||
         (e = dalloc(&p->s.st.kres, res)) != cudaSuccess ||
-        (e = dalloc(&p->s.st.vres, res)) != cudaSuccess) {
+        (e = dalloc(&p->s.st.vres, res)) != cudaSuccess ||
+        (e = dalloc(&p->s.st.kbound, n)) != cudaSuccess ||
+        (e = dalloc(&p->s.st.vbound, n)) != cudaSuccess) {
         free_store(p->s.st);
         if (p->stream) cudaStreamDestroy(p->stream);
         if (p->batch_done) cudaEventDestroy(p->batch_done);
@@ -1432,6 +1443,10 @@ int32_t kivi_cache_share_prefix(const kivi_cache *h, kivi_prefix **out, kivi_err
     CUDA_TRY(copy2d(p->s.st.vparams, kivi::vparam_stride(g, cap) * 8, c.st.vparams,
                     kivi::vparam_stride(g, oc) * 8, kivi::vparam_stride(g, c.vq) * 8), "share_prefix copy");
     CUDA_TRY(cudaMemcpyAsync(p->s.st.kres, c.st.kres, res * 4, cudaMemcpyDeviceToDevice, st),
+             "share_prefix copy");
+    CUDA_TRY(cudaMemcpyAsync(p->s.st.kbound, c.st.kbound, n * 4, cudaMemcpyDeviceToDevice, st),
+             "share_prefix copy");
+    CUDA_TRY(cudaMemcpyAsync(p->s.st.vbound, c.st.vbound, n * 4, cudaMemcpyDeviceToDevice, st),
              "share_prefix copy");
     // Linearise the value ring so the frozen window starts at slot 0.
     const uint64_t first = c.vres_len < R - c.vhead ? c.vres_len : R - c.vhead;

@@ -44,7 +44,23 @@ struct Store {
     float *kres = nullptr;
     float *vres = nullptr;
     int64_t cap = 0; // packed tokens per stream (multiple of R)
+    // Per stream: the largest |scale| among its packed keys / values so far, as
+    // float bits (non-negative floats order as unsigned integers).  Every
+    // kernel that writes parameters raises them; the tensor-core attention
+    // takes its operand range factors from them.
+    unsigned int *kbound = nullptr;
+    unsigned int *vbound = nullptr;
 };
+
+// Raises stream s's scale bound to |scale| (one atomic per warp: the lanes'
+// maximum goes to lane 0).  Every lane of the warp must call it; lanes with
+// nothing to report pass 0.  A store without bounds (the standalone codec's
+// output tensors) passes bounds == nullptr.
+__device__ __forceinline__ void raise_bound(unsigned int *bounds, int64_t s, float scale) {
+    if (bounds == nullptr) return;
+    const unsigned int b = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(scale)));
+    if ((threadIdx.x & 31) == 0 && b) atomicMax(bounds + s, b);
+}
 
 // Per-stream strides (in elements of each array).
 __host__ __device__ inline int64_t code_stride(const Geom &g, int64_t cap) {
@@ -229,6 +245,8 @@ struct TcArgs {
     float *part_o;        // [sets][B*Hq][parts][128]
     int parts;
     int64_t rows_per_set; // B * Hq
+    const unsigned int *kbound; // per stream: largest |key scale| (Store::kbound)
+    const unsigned int *vbound; // per stream: largest |value scale|
 };
 // Dense tail of the tensor-core path: tokens [main_tokens, seq_p + suf[z].len)
 // of each stream (partial group, fp32 window/residual, session z's fp32

@@ -130,8 +130,8 @@ __device__ __forceinline__ bool pack32_fast(const float (&x)[32], const Quantize
 // registers, packed by pack32_fast unless the group needs the exact path.
 // Same results as quant_key_channel.
 template <int BITS>
-__device__ __forceinline__ void quant_key_channel_g32(const float *base, int stride, int d,
-                                                      uint32_t *words, float2 *param) {
+__device__ __forceinline__ float quant_key_channel_g32(const float *base, int stride, int d,
+                                                       uint32_t *words, float2 *param) {
     constexpr float kLevels = (float)((1u << BITS) - 1u);
     float x[32];
 #pragma unroll
@@ -145,7 +145,7 @@ __device__ __forceinline__ void quant_key_channel_g32(const float *base, int str
     const float scale = scale_of(__fsub_rn(mx, mn), kLevels);
     *param = make_float2(scale, mn);
     const Quantizer qz(mn, scale, kLevels);
-    if (pack32_fast<BITS>(x, qz, words)) return;
+    if (pack32_fast<BITS>(x, qz, words)) return scale;
 #pragma unroll
     for (int w = 0; w < BITS; ++w) {
         uint32_t word = 0;
@@ -153,12 +153,13 @@ __device__ __forceinline__ void quant_key_channel_g32(const float *base, int str
         for (int k = 0; k < 32 / BITS; ++k) word |= qz.code(x[w * (32 / BITS) + k]) << (k * BITS);
         words[w] = word;
     }
+    return scale;
 }
 
 // Per-channel key quantization of one channel `d` of one group whose G rows
 // are rows[u * D] (u < G).  quant.rs:296-325.
-__device__ __forceinline__ void quant_key_channel(const Geom &g, const float *const *rows, int d,
-                                                  uint32_t *words, float2 *param) {
+__device__ __forceinline__ float quant_key_channel(const Geom &g, const float *const *rows, int d,
+                                                   uint32_t *words, float2 *param) {
     float mn = INFINITY, mx = -INFINITY;
 #pragma unroll 8
     for (int u = 0; u < g.G; ++u) {
@@ -174,13 +175,14 @@ __device__ __forceinline__ void quant_key_channel(const Geom &g, const float *co
         for (int k = 0; k < g.tpw; ++k) w |= qz.code(rows[i * g.tpw + k][d]) << (k * g.bits);
         words[i] = w;
     }
+    return scale;
 }
 
 // Per-token value quantization of one 32-channel group (BITS known at
 // compile time): the group is read as eight float4 (callers check the row is
 // 16-byte aligned), same arithmetic as the generic loop below.
 template <int BITS>
-__device__ __forceinline__ void quant_value_g32(const float *grp, uint32_t *words, float2 *param) {
+__device__ __forceinline__ float quant_value_g32(const float *grp, uint32_t *words, float2 *param) {
     constexpr float kLevels = (float)((1u << BITS) - 1u);
     const float4 *grp4 = reinterpret_cast<const float4 *>(grp);
     float x[32];
@@ -201,7 +203,7 @@ __device__ __forceinline__ void quant_value_g32(const float *grp, uint32_t *word
     const float scale = scale_of(__fsub_rn(mx, mn), kLevels);
     *param = make_float2(scale, mn);
     const Quantizer qz(mn, scale, kLevels);
-    if (pack32_fast<BITS>(x, qz, words)) return;
+    if (pack32_fast<BITS>(x, qz, words)) return scale;
 #pragma unroll
     for (int w = 0; w < BITS; ++w) {
         uint32_t word = 0;
@@ -209,12 +211,13 @@ __device__ __forceinline__ void quant_value_g32(const float *grp, uint32_t *word
         for (int k = 0; k < 32 / BITS; ++k) word |= qz.code(x[w * (32 / BITS) + k]) << (k * BITS);
         words[w] = word;
     }
+    return scale;
 }
 
 // Per-token value quantization of channel group `cg` of one token row.
 // quant.rs:349-374.
-__device__ __forceinline__ void quant_value_group(const Geom &g, const float *row, int cg,
-                                                  uint32_t *words, float2 *param) {
+__device__ __forceinline__ float quant_value_group(const Geom &g, const float *row, int cg,
+                                                   uint32_t *words, float2 *param) {
     if (g.G == 32 && (reinterpret_cast<uintptr_t>(row) & 15u) == 0) {
         if (g.bits == 2) return quant_value_g32<2>(row + cg * 32, words, param);
         if (g.bits == 4) return quant_value_g32<4>(row + cg * 32, words, param);
@@ -236,14 +239,15 @@ __device__ __forceinline__ void quant_value_group(const Geom &g, const float *ro
         for (int k = 0; k < g.tpw; ++k) word |= qz.code(grp[w * g.tpw + k]) << (k * g.bits);
         words[w] = word;
     }
+    return scale;
 }
 
 // Warp-cooperative per-token value quantization of channel group `cg` (the
 // decode-step eviction): lanes split the G channels, min/max by shuffle
 // reduction (exact, order-free), each lane codes its channels, and the packed
 // words are OR-reduced across the warp.  Same results as quant_value_group.
-__device__ __forceinline__ void quant_value_group_warp(const Geom &g, const float *row, int cg,
-                                                       uint32_t *words, float2 *param, int lane) {
+__device__ __forceinline__ float quant_value_group_warp(const Geom &g, const float *row, int cg,
+                                                        uint32_t *words, float2 *param, int lane) {
     const float *grp = row + cg * g.G;
     float mn = INFINITY, mx = -INFINITY;
     for (int i = lane; i < g.G; i += 32) {
@@ -267,6 +271,7 @@ __device__ __forceinline__ void quant_value_group_warp(const Geom &g, const floa
         for (int o = 16; o > 0; o >>= 1) part |= __shfl_xor_sync(0xffffffffu, part, o);
         if (lane == 0) words[w] = part;
     }
+    return scale;
 }
 
 constexpr int kMaxG = 256; // largest group handled by the row-pointer tables below
@@ -329,6 +334,7 @@ __global__ void __launch_bounds__(256) append_small_kernel(Geom g, Store st, con
                 for (int o = 16; o > 0; o >>= 1) part |= __shfl_xor_sync(0xffffffffu, part, o);
                 if (lane == 0) vc[w] = part;
             }
+            raise_bound(st.vbound, s, scale);
         }
         vres[(int64_t)((vhead + vres_len) % R) * D + d] = vx;
         if (qon) *qdst = qv;
@@ -345,15 +351,18 @@ __global__ void __launch_bounds__(256) append_small_kernel(Geom g, Store st, con
         uint32_t *kc = st.kcodes + (int64_t)s * code_stride(g, st.cap);
         float2 *kp = st.kparams + (int64_t)s * kparam_stride(g, st.cap);
         const int64_t g0 = kq / g.G;
+        float kmax = 0.0f;
         for (int gi = 0; gi < ngroups; ++gi) {
             if (threadIdx.x < g.G) rows[threadIdx.x] = kres + ((int64_t)gi * g.G + threadIdx.x) * D;
             __syncthreads();
             for (int d = threadIdx.x; d < D; d += blockDim.x) {
                 const int64_t og = g0 + gi;
-                quant_key_channel(g, rows, d, kc + (og * D + d) * g.ipc, kp + og * D + d);
+                kmax = fmaxf(kmax, fabsf(quant_key_channel(g, rows, d, kc + (og * D + d) * g.ipc,
+                                                           kp + og * D + d)));
             }
             __syncthreads();
         }
+        raise_bound(st.kbound, s, kmax);
         const int rest = seq - take1;
         for (int e = threadIdx.x; e < rest * D; e += blockDim.x) kres[e] = kin[(int64_t)take1 * D + e];
     }
@@ -362,13 +371,16 @@ __global__ void __launch_bounds__(256) append_small_kernel(Geom g, Store st, con
     uint32_t *vc = st.vcodes + (int64_t)s * code_stride(g, st.cap);
     float2 *vp = st.vparams + (int64_t)s * vparam_stride(g, st.cap);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    float vmax = 0.0f;
     for (int p = warp; p < drop * g.nch; p += nwarps) {
         const int j = p / g.nch, cg = p % g.nch;
         const int slot = (vhead + j) % R;
         const int64_t t = vq + j;
-        quant_value_group_warp(g, vres + (int64_t)slot * D, cg, vc + (t * g.nch + cg) * g.ipc,
-                               vp + t * g.nch + cg, lane);
+        vmax = fmaxf(vmax, fabsf(quant_value_group_warp(g, vres + (int64_t)slot * D, cg,
+                                                        vc + (t * g.nch + cg) * g.ipc,
+                                                        vp + t * g.nch + cg, lane)));
     }
+    raise_bound(st.vbound, s, vmax);
     __syncthreads();
     for (int e = threadIdx.x; e < seq * D; e += blockDim.x) {
         const int i = e / D, d = e - i * D;
@@ -393,16 +405,20 @@ __global__ void __launch_bounds__(128, 8) key_groups_kernel(Geom g, Store st, co
     uint32_t *kc = st.kcodes + (int64_t)s * code_stride(g, st.cap);
     float2 *kp = st.kparams + (int64_t)s * kparam_stride(g, st.cap);
     const int64_t og = out_group0 + gi;
+    float kmax = 0.0f;
     if (g.G == 32 && c0 >= nres) {
         // every row from the input: one contiguous span
         const float *base = in + ((int64_t)s * in_seq + (c0 - nres)) * D;
         for (int d = threadIdx.x; d < D; d += blockDim.x) {
             uint32_t *words = kc + (og * D + d) * g.ipc;
             float2 *param = kp + og * D + d;
-            if (g.bits == 2) quant_key_channel_g32<2>(base, D, d, words, param);
-            else if (g.bits == 4) quant_key_channel_g32<4>(base, D, d, words, param);
-            else quant_key_channel_g32<8>(base, D, d, words, param);
+            float sc;
+            if (g.bits == 2) sc = quant_key_channel_g32<2>(base, D, d, words, param);
+            else if (g.bits == 4) sc = quant_key_channel_g32<4>(base, D, d, words, param);
+            else sc = quant_key_channel_g32<8>(base, D, d, words, param);
+            kmax = fmaxf(kmax, fabsf(sc));
         }
+        raise_bound(st.kbound, s, kmax);
         return;
     }
     __shared__ const float *rows[kMaxG];
@@ -413,7 +429,9 @@ __global__ void __launch_bounds__(128, 8) key_groups_kernel(Geom g, Store st, co
     }
     __syncthreads();
     for (int d = threadIdx.x; d < D; d += blockDim.x)
-        quant_key_channel(g, rows, d, kc + (og * D + d) * g.ipc, kp + og * D + d);
+        kmax = fmaxf(kmax, fabsf(quant_key_channel(g, rows, d, kc + (og * D + d) * g.ipc,
+                                                   kp + og * D + d)));
+    raise_bound(st.kbound, s, kmax);
 }
 
 // ---------------------------------------------------------------- bulk values
@@ -424,15 +442,18 @@ __global__ void __launch_bounds__(128) value_tokens_kernel(Geom g, Store st, int
                                                            int64_t out_tok0) {
     const int s = blockIdx.y;
     const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (p >= ntok * g.nch) return;
-    const int64_t j = p / g.nch;
-    const int cg = (int)(p - j * g.nch);
-    const float *row = j < nwin ? st.vres + ((int64_t)s * g.R + (vhead + j) % g.R) * g.D
-                                : in + ((int64_t)s * in_seq + in_off + (j - nwin)) * g.D;
-    const int64_t t = out_tok0 + j;
-    uint32_t *vc = st.vcodes + (int64_t)s * code_stride(g, st.cap);
-    float2 *vp = st.vparams + (int64_t)s * vparam_stride(g, st.cap);
-    quant_value_group(g, row, cg, vc + (t * g.nch + cg) * g.ipc, vp + t * g.nch + cg);
+    float sc = 0.0f;
+    if (p < ntok * g.nch) {
+        const int64_t j = p / g.nch;
+        const int cg = (int)(p - j * g.nch);
+        const float *row = j < nwin ? st.vres + ((int64_t)s * g.R + (vhead + j) % g.R) * g.D
+                                    : in + ((int64_t)s * in_seq + in_off + (j - nwin)) * g.D;
+        const int64_t t = out_tok0 + j;
+        uint32_t *vc = st.vcodes + (int64_t)s * code_stride(g, st.cap);
+        float2 *vp = st.vparams + (int64_t)s * vparam_stride(g, st.cap);
+        sc = quant_value_group(g, row, cg, vc + (t * g.nch + cg) * g.ipc, vp + t * g.nch + cg);
+    }
+    raise_bound(st.vbound, s, sc);
 }
 
 // ---------------------------------------------------------------- row copies
