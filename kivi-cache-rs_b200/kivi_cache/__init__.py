@@ -28,7 +28,12 @@ VARIANTS = {
     0: "Ok", 1: "InvalidBits", 2: "MisalignedGroup", 3: "ResidualLength", 4: "HeadDim",
     5: "TokenGroup", 6: "ZeroDimension", 7: "Shape", 8: "QueryHeads", 9: "EarlyLayers",
     100: "Cuda", 101: "InvalidArgument", 102: "OutOfMemory", 103: "Unsupported",
+    104: "Comm",
 }
+# Raised by the sequence-sharding host layer (kivi_cache.sharding), not by the
+# C ABI: a peer rank that never joins, leaves, or fails a collective within the
+# bounded wait; the communicator is aborted first.
+KIVI_ERR_COMM = 104
 
 
 class KiviError(Exception):

@@ -21,12 +21,28 @@ deterministic output.
 
 The host logic here (ranges, exchange) is device-agnostic and runs on gloo/CPU
 in the tests; the CUDA work goes through the C ABI of libkivi_gpu.so.
+
+Failures between ranks surface as ``KiviError`` with variant ``Comm`` (the
+reference is single-device and returns ``Result<_, KiviError>``,
+error.rs:4-45): ``init_shard_group`` bounds the rendezvous, so a rank that
+never joins makes the others fail after ``timeout_s`` instead of waiting;
+``exchange_partials(..., timeout_s=...)`` and ``SeqShardedCache`` bound each
+exchange on the host, and a peer that has left, a failed collective or a
+wait that runs out aborts the communicator (so nothing of this rank stays
+queued on it) and raises.  A cache whose communicator was aborted refuses
+further steps with the same error.
 """
 from __future__ import annotations
 
+import time
 from dataclasses import dataclass
 
-__all__ = ["ShardPlan", "shard_plan", "exchange_partials", "SeqShardedCache"]
+__all__ = ["ShardPlan", "shard_plan", "exchange_partials", "SeqShardedCache", "init_shard_group",
+           "comm_error", "abort_group"]
+
+DEFAULT_TIMEOUT_S = 30.0
+_SPIN_S = 0.005   # poll without sleeping for this long (a decode step is ~0.1-1 ms)
+_POLL_S = 0.0005  # then sleep this long between polls
 
 
 @dataclass(frozen=True)
@@ -61,11 +77,96 @@ def shard_plan(total_tokens: int, world: int, rank: int, residual_length: int) -
     return ShardPlan(rank, world, start, end, rank == world - 1)
 
 
-def exchange_partials(local, gathered=None, group=None):
+def comm_error(message):
+    """KiviError with the Comm variant (a communication failure between ranks)."""
+    from . import KIVI_ERR_COMM, KiviError
+
+    return KiviError(KIVI_ERR_COMM, 0, 0, None, message)
+
+
+def init_shard_group(backend, rank=None, world_size=None, timeout_s=DEFAULT_TIMEOUT_S,
+                     init_method=None, device=None):
+    """torch.distributed.init_process_group with a bounded rendezvous: when a
+    rank does not join within `timeout_s` seconds the others raise
+    KiviError(Comm) instead of waiting.  The same bound becomes the group's
+    collective timeout.  rank/world_size/init_method default to the launcher's
+    environment (RANK, WORLD_SIZE, MASTER_ADDR/MASTER_PORT)."""
+    import datetime
+
+    import torch.distributed as dist
+
+    kw = dict(timeout=datetime.timedelta(seconds=float(timeout_s)))
+    if rank is not None:
+        kw["rank"] = rank
+    if world_size is not None:
+        kw["world_size"] = world_size
+    if init_method is not None:
+        kw["init_method"] = init_method
+    if device is not None:
+        kw["device_id"] = device
+    t0 = time.monotonic()
+    try:
+        dist.init_process_group(backend, **kw)
+    except Exception as e:  # store or backend rendezvous gave up
+        raise comm_error(f"process group ({backend}) not formed within {timeout_s:.1f} s "
+                         f"({time.monotonic() - t0:.1f} s): {type(e).__name__}: {e}") from e
+
+
+def abort_group(group=None):
+    """Aborts the communicator of `group` (default: the default group): work
+    of this rank queued on it is cancelled, so no collective waits for a peer
+    that is gone.  Best effort; the group must not be used afterwards."""
+    import torch.distributed as dist
+
+    if not dist.is_initialized():
+        return
+    pg = group if group is not None else dist.distributed_c10d._get_default_group()
+    try:
+        pg.abort()
+    except Exception:
+        pass
+
+
+def wait_bounded(work, timeout_s, what, group=None, stream=None):
+    """Waits for a collective's Work (and, if given, a CUDA stream that runs
+    after it) on the host for at most `timeout_s` seconds.  A failed
+    collective or a wait that runs out aborts the group and raises
+    KiviError(Comm)."""
+    start = time.monotonic()
+    deadline = start + float(timeout_s)
+    err = None
+    while True:
+        try:
+            if work is None or work.is_completed():
+                if work is not None and not work.is_success():
+                    err = work.exception()
+                    break
+                if stream is None or stream.query():
+                    return
+        except Exception as e:
+            err = e
+            break
+        now = time.monotonic()
+        if now > deadline:
+            break
+        if now - start > _SPIN_S:
+            time.sleep(_POLL_S)
+    abort_group(group)
+    if err is not None:
+        raise comm_error(f"{what} failed: {type(err).__name__}: {err}") from err
+    raise comm_error(f"{what} did not complete within {timeout_s:.1f} s; communicator aborted")
+
+
+def exchange_partials(local, gathered=None, group=None, timeout_s=None):
     """All-gather of every rank's packed partial state, in rank order, into
     `gathered` ([world, n] on local's device; allocated when None).  One
     collective: all_gather_into_tensor on NCCL, the list form elsewhere (gloo
-    has no single-buffer all-gather).  Runs on torch's current stream."""
+    has no single-buffer all-gather).  Runs on torch's current stream.
+
+    With `timeout_s` the collective is waited for on the host, for at most
+    that long (wait_bounded: a peer that left or a wait that runs out aborts
+    the group and raises KiviError(Comm)); without it the call is
+    stream-ordered and the group's own timeout applies."""
     import torch
     import torch.distributed as dist
 
@@ -75,10 +176,19 @@ def exchange_partials(local, gathered=None, group=None):
                                device=local.device)
     if world == 1:
         gathered[0].copy_(local)
-    elif dist.get_backend(group) == "nccl":
-        dist.all_gather_into_tensor(gathered, local, group=group)
-    else:
-        dist.all_gather(list(gathered.unbind(0)), local, group=group)
+        return gathered
+    bounded = timeout_s is not None
+    try:
+        if dist.get_backend(group) == "nccl":
+            work = dist.all_gather_into_tensor(gathered, local, group=group, async_op=bounded)
+        else:
+            work = dist.all_gather(list(gathered.unbind(0)), local, group=group, async_op=bounded)
+    except Exception as e:
+        abort_group(group)
+        raise comm_error(f"partial-state all-gather failed: {type(e).__name__}: {e}") from e
+    if bounded:
+        wait_bounded(work, timeout_s, "partial-state all-gather", group)
+        work.wait()  # complete already; orders torch's current stream after it
     return gathered
 
 
@@ -92,7 +202,7 @@ class SeqShardedCache:
     rank, the attention output over all shards."""
 
     def __init__(self, config, batch, num_kv_heads, head_dim, total_prefill_tokens, group=None,
-                 device=None):
+                 device=None, timeout_s=DEFAULT_TIMEOUT_S):
         import torch
         import torch.distributed as dist
 
@@ -107,6 +217,12 @@ class SeqShardedCache:
         self.batch, self.heads, self.dim = batch, num_kv_heads, head_dim
         self.cache = KiviCache(config, batch, num_kv_heads, head_dim, device=self.device)
         self._bufs = {}
+        self.timeout_s = timeout_s  # host bound of each host-path step's exchange
+        self._failed = None         # set once the communicator was aborted
+
+    def _check_alive(self):
+        if self._failed is not None:
+            raise comm_error(f"communicator aborted earlier: {self._failed}")
 
     # -- prefill
     def reserve(self, tokens):
@@ -143,24 +259,46 @@ class SeqShardedCache:
             b = self._bufs[rows] = (local, gathered)
         return b
 
-    def attention_dev(self, d_query, num_q_heads, scale, d_out, stream):
-        """Attention of every query row over all shards; the same d_out on every rank."""
+    def attention_dev(self, d_query, num_q_heads, scale, d_out, stream, timeout_s=None):
+        """Attention of every query row over all shards; the same d_out on every
+        rank.  Stream-ordered; with `timeout_s` the exchange is also waited for
+        on the host (exchange_partials)."""
         import torch
 
         from . import merge_packed_partials_dev
 
+        self._check_alive()
         rows = self.batch * num_q_heads
         local, gathered = self._buffers(rows)
         self.cache.attention_partial_packed_dev(d_query, num_q_heads, scale, local, stream=stream)
-        with torch.cuda.stream(stream):
-            exchange_partials(local, gathered, self.group)
+        try:
+            with torch.cuda.stream(stream):
+                exchange_partials(local, gathered, self.group, timeout_s=timeout_s)
+        except Exception as e:
+            self._failed = str(e)
+            raise
         merge_packed_partials_dev(self.world, rows, self.dim, gathered, d_out, stream=stream)
 
-    def decode_dev(self, d_key, d_value, d_query, num_q_heads, scale, d_out, stream):
+    def decode_dev(self, d_key, d_value, d_query, num_q_heads, scale, d_out, stream,
+                   timeout_s=None):
         """RuntimeKv::decode (runtime.rs:46-56) on the sharded cache."""
+        self._check_alive()
         if self.plan.tail:
             self.cache.append_dev(d_key, d_value, 1, stream=stream)
-        self.attention_dev(d_query, num_q_heads, scale, d_out, stream)
+        self.attention_dev(d_query, num_q_heads, scale, d_out, stream, timeout_s=timeout_s)
+
+    def synchronize(self, stream, timeout_s=None):
+        """Waits on the host, for at most `timeout_s` (default: the cache's),
+        until `stream` has run the steps queued on it; a step that does not
+        finish in time (a peer that stopped taking part in the exchange) aborts
+        the communicator and raises KiviError(Comm)."""
+        self._check_alive()
+        try:
+            wait_bounded(None, self.timeout_s if timeout_s is None else timeout_s,
+                         "sharded decode step", self.group, stream=stream)
+        except Exception as e:
+            self._failed = str(e)
+            raise
 
     def decode(self, keys, values, query, num_q_heads, scale, out=None, stream=None):
         """Host-buffer decode step (torch CPU tensors, pinned for async copies):
@@ -182,5 +320,5 @@ class SeqShardedCache:
             if out is None:
                 out = torch.empty(dout.shape, dtype=torch.float32, pin_memory=True)
             out.copy_(dout, non_blocking=True)
-        st.synchronize()
+        self.synchronize(st)
         return out

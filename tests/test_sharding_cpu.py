@@ -167,3 +167,102 @@ def test_seq_sharded_exchange_and_merge_gloo_world2():
     for rank, ok_order, err, _ in res:
         assert ok_order, f"rank {rank}: gathered row is not its own state"
         assert err <= 1e-5, f"rank {rank}: merged attention rel-L2 {err}"
+
+
+# ---------------------------------------------------------------- failures between ranks
+# A peer that never joins, leaves between steps, or stalls inside a step must
+# surface as KiviError(Comm) within the bounded wait (the reference returns
+# Result<_, KiviError>, error.rs:4-45), never as a hang.  gloo ranks on CPU.
+
+TIMEOUT = 3.0
+
+
+def _fail_worker(rank, world, port, mode, q):
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    from kivi_cache import KiviError
+    from kivi_cache.sharding import exchange_partials, init_shard_group
+
+    out = {"rank": rank}
+    try:
+        t0 = time.monotonic()
+        try:
+            init_shard_group("gloo", rank=rank, world_size=world, timeout_s=TIMEOUT,
+                             init_method=f"tcp://127.0.0.1:{port}")
+        except KiviError as e:
+            out.update(stage="init", variant=e.variant, elapsed=time.monotonic() - t0)
+            q.put(out)
+            return
+        local = torch.full((8,), float(rank))
+        g = exchange_partials(local, timeout_s=TIMEOUT)  # step 1: everyone present
+        out["step1"] = g[:, 0].tolist()
+        if mode == "leave" and rank == 1:
+            dist.destroy_process_group()  # leaves between steps, nothing in flight
+            out["stage"] = "left"
+            q.put(out)
+            return
+        if mode == "stall" and rank == 1:
+            time.sleep(3 * TIMEOUT)  # alive, but never takes part in step 2
+            out["stage"] = "stalled"
+            q.put(out)
+            return
+        if mode == "leave":
+            time.sleep(0.5)  # the peer is gone before step 2 starts
+        t0 = time.monotonic()
+        try:
+            exchange_partials(local, timeout_s=TIMEOUT)
+            out.update(stage="step2", variant="Ok", elapsed=time.monotonic() - t0)
+        except KiviError as e:
+            out.update(stage="step2", variant=e.variant, elapsed=time.monotonic() - t0,
+                       message=e.message)
+        q.put(out)
+    except Exception as e:  # reported to the parent instead of a queue timeout
+        out.update(stage="error", variant=repr(e))
+        q.put(out)
+
+
+def _run_fail(ranks, world, mode):
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fail_worker, args=(r, world, port, mode, q)) for r in ranks]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in procs:
+        r = q.get(timeout=120)
+        res[r["rank"]] = r
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    return res
+
+
+def test_rank_that_never_joins_fails_within_the_timeout():
+    res = _run_fail([0], 2, "absent")  # rank 1 of 2 is never started
+    r = res[0]
+    assert r["stage"] == "init" and r["variant"] == "Comm", r
+    assert r["elapsed"] < TIMEOUT + 10, r
+
+
+def test_rank_that_leaves_between_steps_fails_the_next_exchange():
+    res = _run_fail([0, 1], 2, "leave")
+    assert res[1]["stage"] == "left" and res[1]["step1"] == [0.0, 1.0]
+    r = res[0]
+    assert r["step1"] == [0.0, 1.0]
+    assert r["stage"] == "step2" and r["variant"] == "Comm", r
+    assert r["elapsed"] < TIMEOUT + 5, r
+
+
+def test_peer_that_stalls_in_a_step_fails_within_the_timeout():
+    res = _run_fail([0, 1], 2, "stall")
+    r = res[0]
+    assert r["stage"] == "step2" and r["variant"] == "Comm", r
+    assert TIMEOUT - 0.5 <= r["elapsed"] < TIMEOUT + 5, r
+    assert "communicator aborted" in r.get("message", "") or "failed" in r.get("message", "")
