@@ -71,6 +71,9 @@ namespace {
 #ifndef KIVI_TC_MINB1
 #define KIVI_TC_MINB1 4
 #endif
+#ifndef KIVI_TC_MINB2
+#define KIVI_TC_MINB2 2
+#endif
 constexpr int kConsumers = 4;
 constexpr int kTcThreads = kConsumers * 32;
 constexpr int kStages = KIVI_TC_STAGES; // pipeline depth (groups in flight per CTA)
@@ -302,7 +305,7 @@ __device__ __forceinline__ void issue_group(const TcArgs &a, int64_t s, int64_t 
 // keeps kStages/4 of them in flight in its own stages (i % kStages), issuing
 // the copy of group i + kStages as soon as it has finished group i.
 template <int BITS, int NT>
-__global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : 2) attn_tc_kernel(const TcArgs a) {
+__global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : KIVI_TC_MINB2) attn_tc_kernel(const TcArgs a) {
     using TG = TcGeom<BITS>;
     constexpr int IPC = TG::IPC;
     constexpr int kHeads = NT * 4;
@@ -985,14 +988,19 @@ __global__ void __launch_bounds__(kTailThreads) attn_tail_kernel(const TailArgs 
 }
 
 // One CTA per row (head_dim 128): log-sum-exp merge of the row's `parts`
-// slots.  Warp w sums slots w, w+4, ... (4 channels per lane); the four warp
-// partials and the normaliser are combined in a fixed order (deterministic).
-__global__ void __launch_bounds__(128) merge_rows_kernel(const float *part_ml, const float *part_o,
-                                                        int parts, int64_t rows, float *out,
-                                                        float *out_m, float *out_l) {
+// slots.  Warp w of NW sums slots w, w+NW, ... (4 channels per lane); the
+// warp partials and the normaliser are combined in a fixed pairwise order
+// (deterministic).  NW = 16 for rows with many slots (a long sequence split
+// over many CTAs), so every slot's load is in flight at once.
+template <int NW>
+__global__ void __launch_bounds__(32 * NW) merge_rows_kernel(const float *part_ml,
+                                                             const float *part_o, int parts,
+                                                             int64_t rows, float *out,
+                                                             float *out_m, float *out_l) {
+    constexpr int kThreads = 32 * NW;
     __shared__ float wsh[512];
-    __shared__ __align__(16) float osh[4][128];
-    __shared__ float lsh[4];
+    __shared__ __align__(16) float osh[NW][128];
+    __shared__ float lsh[NW];
     __shared__ float Msh;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t row = blockIdx.x;
@@ -1004,7 +1012,7 @@ __global__ void __launch_bounds__(128) merge_rows_kernel(const float *part_ml, c
     float4 pre[kPre];
 #pragma unroll
     for (int i = 0; i < kPre; ++i) {
-        const int c = warp + 4 * i;
+        const int c = warp + NW * i;
         if (c < parts) pre[i] = po[(int64_t)c * 32];
     }
     if (warp == 0) {
@@ -1018,7 +1026,7 @@ __global__ void __launch_bounds__(128) merge_rows_kernel(const float *part_ml, c
     __syncthreads();
     const float M = Msh;
     float Lp = 0.0f;
-    for (int c = threadIdx.x; c < parts; c += 128) {
+    for (int c = threadIdx.x; c < parts; c += kThreads) {
         const float l = ml[2 * c + 1];
         const float w = (l > 0.0f) ? expf(ml[2 * c] - M) : 0.0f;
         if (c < 512) wsh[c] = w;
@@ -1032,9 +1040,9 @@ __global__ void __launch_bounds__(128) merge_rows_kernel(const float *part_ml, c
     // slots in increasing order per warp (the prefetched ones first)
 #pragma unroll
     for (int i = 0; i < kPre; ++i) {
-        const int c = warp + 4 * i;
+        const int c = warp + NW * i;
         if (c < parts) {
-            const float w = wsh[c]; // c < 4 kPre <= 512
+            const float w = wsh[c]; // c < NW kPre <= 512
             acc.x = fmaf(pre[i].x, w, acc.x);
             acc.y = fmaf(pre[i].y, w, acc.y);
             acc.z = fmaf(pre[i].z, w, acc.z);
@@ -1042,7 +1050,7 @@ __global__ void __launch_bounds__(128) merge_rows_kernel(const float *part_ml, c
         }
     }
 #pragma unroll 4
-    for (int c = warp + 4 * kPre; c < parts; c += 4) {
+    for (int c = warp + NW * kPre; c < parts; c += NW) {
         float w;
         if (c < 512) {
             w = wsh[c];
@@ -1058,9 +1066,22 @@ __global__ void __launch_bounds__(128) merge_rows_kernel(const float *part_ml, c
     }
     reinterpret_cast<float4 *>(osh[warp])[lane] = acc;
     __syncthreads();
+    if (threadIdx.x >= 128) return;
     const int d = threadIdx.x;
-    const float o = ((osh[0][d] + osh[1][d]) + (osh[2][d] + osh[3][d]));
-    const float L = (lsh[0] + lsh[1]) + (lsh[2] + lsh[3]);
+    float ov[NW], lv[NW];
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+        ov[w] = osh[w][d];
+        lv[w] = lsh[w];
+    }
+#pragma unroll
+    for (int span = 1; span < NW; span *= 2)
+#pragma unroll
+        for (int w = 0; w + span < NW; w += 2 * span) {
+            ov[w] += ov[w + span];
+            lv[w] += lv[w + span];
+        }
+    const float o = ov[0], L = lv[0];
     if (out_m) {
         out[row * 128 + d] = o;
         if (d == 0) {
@@ -1092,7 +1113,12 @@ cudaError_t launch_merge_rows(const float *part_ml, const float *part_o, int par
                               float *out, float *out_m, float *out_l, cudaStream_t s) {
     if (rows <= 0) return cudaSuccess;
     ProfScope prof("merge", s);
-    merge_rows_kernel<<<(unsigned)rows, 128, 0, s>>>(part_ml, part_o, parts, rows, out, out_m, out_l);
+    if (parts > 32)
+        merge_rows_kernel<16><<<(unsigned)rows, 512, 0, s>>>(part_ml, part_o, parts, rows, out,
+                                                             out_m, out_l);
+    else
+        merge_rows_kernel<4><<<(unsigned)rows, 128, 0, s>>>(part_ml, part_o, parts, rows, out,
+                                                            out_m, out_l);
     count_launch();
     return cudaGetLastError();
 }

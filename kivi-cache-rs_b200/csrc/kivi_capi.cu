@@ -459,6 +459,29 @@ int32_t append_device(KvState &s, const float *dk, const float *dv, uint64_t seq
 constexpr int64_t kChunkTokens = 256;   // generic kernel: tokens per main chunk
 constexpr int64_t kTailTile = 32;       // prefix-tail tokens per CTA
 
+// A handle's second stream: the dense tail tiles of an attention run on it
+// beside the main-region kernel (they read other tokens and write other
+// partial slots), forked from and joined back into the call's stream by two
+// events, so the tail tiles fill the SMs the main kernel's wave leaves idle.
+struct SideLane {
+    cudaStream_t s = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+    cudaError_t create() {
+        cudaError_t e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&fork, cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&join, cudaEventDisableTiming);
+        return e;
+    }
+    void destroy() {
+        if (s) cudaStreamSynchronize(s);
+        if (fork) cudaEventDestroy(fork);
+        if (join) cudaEventDestroy(join);
+        if (s) cudaStreamDestroy(s);
+        s = nullptr;
+        fork = join = nullptr;
+    }
+};
+
 struct SessionView {
     const float *k;
     const float *v;
@@ -471,7 +494,7 @@ struct SessionView {
 int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, const float *d_q,
                       uint64_t Hq, float scale, float *d_out, float *d_m, float *d_l,
                       Scratch &scratch, cudaStream_t stream, kivi_error *err,
-                      const int *bounds = nullptr) {
+                      const int *bounds = nullptr, const SideLane *side = nullptr) {
     const Geom &g = p.g;
     const uint64_t Gq = Hq / p.H;
     // the tensor-core kernel reads query rows as float2
@@ -520,6 +543,14 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
             CUDA_TRY(scratch.ensure(ml_bytes + o_bytes), "attention scratch");
             float *part_ml = scratch.as<float>(), *part_o = scratch.as<float>(ml_bytes);
             const float *q = d_q + s0 * rows1 * p.D;
+            // tail tiles on the side lane when both kernels run (serial while
+            // per-kernel timing is on, so each event pair brackets one kernel)
+            const bool fork = side && side->s && NTT > 0 && (sets || NC > 0) &&
+                              !kivi::g_prof_on.load();
+            if (fork) {
+                CUDA_TRY(cudaEventRecord(side->fork, stream), "attention fork");
+                CUDA_TRY(cudaStreamWaitEvent(side->s, side->fork, 0), "attention fork");
+            }
             if (sets) {
                 kivi::SetsArgs t{};
                 t.kcodes = p.st.kcodes;
@@ -598,8 +629,13 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
                 ta.suf[i].len = sv ? (int64_t)sv[s0 + i].len : 0;
                 ta.suf[i].cap = sv ? (int64_t)sv[s0 + i].cap : 0;
             }
-            CUDA_TRY(kivi::launch_attention_tail(ta, (int)NTT, (int)(p.B * p.H), (int)ns, stream),
+            CUDA_TRY(kivi::launch_attention_tail(ta, (int)NTT, (int)(p.B * p.H), (int)ns,
+                                                 fork ? side->s : stream),
                      "attention tail");
+            if (fork) {
+                CUDA_TRY(cudaEventRecord(side->join, side->s), "attention join");
+                CUDA_TRY(cudaStreamWaitEvent(stream, side->join, 0), "attention join");
+            }
             const uint64_t off = s0 * rows1;
             CUDA_TRY(kivi::launch_merge_rows(part_ml, part_o, parts, (int64_t)rows,
                                              d_out + off * p.D, d_m ? d_m + off : nullptr,
@@ -756,6 +792,7 @@ int32_t check_query(const KvState &p, uint64_t Hq, uint64_t query_len, bool chec
 struct kivi_cache {
     KvState s;
     cudaStream_t stream = nullptr;   // own stream of the synchronous host-pointer calls
+    SideLane side;                   // second stream for the attention's tail tiles
     cudaEvent_t dev_done = nullptr;  // recorded after every `_dev` call on the caller's stream
     Scratch stage;   // host-input staging (keys, values, query, out)
     mutable Scratch part;
@@ -787,6 +824,7 @@ struct kivi_session {
     cudaStream_t stream = nullptr;
     cudaEvent_t dev_done = nullptr;
     mutable std::atomic<bool> dev_used{false}; // dev_done recorded by a `_dev` call
+    SideLane side; // second stream for the attention's tail tiles (as lead session)
     Scratch stage;
     mutable Scratch part;
     mutable std::mutex mu;
@@ -978,8 +1016,10 @@ int32_t kivi_cache_new(const kivi_config *config, uint64_t batch, uint64_t num_k
         (e = cudaMemsetAsync(h->s.st.vres, 0, res * 4, h->stream)) != cudaSuccess ||
         (e = cudaMemsetAsync(h->s.st.kbound, 0, n * 4, h->stream)) != cudaSuccess ||
         (e = cudaMemsetAsync(h->s.st.vbound, 0, n * 4, h->stream)) != cudaSuccess ||
+        (e = h->side.create()) != cudaSuccess ||
         (e = cudaStreamSynchronize(h->stream)) != cudaSuccess) {
         free_store(h->s.st);
+        h->side.destroy();
         if (h->dev_done) cudaEventDestroy(h->dev_done);
         if (h->stream) cudaStreamDestroy(h->stream);
         delete h;
@@ -994,6 +1034,7 @@ void kivi_cache_free(kivi_cache *h) {
     DeviceGuard dg(h->s.device);
     if (h->dev_done) cudaEventSynchronize(h->dev_done);
     if (h->stream) cudaStreamSynchronize(h->stream);
+    h->side.destroy();
     free_store(h->s.st);
     h->stage.release();
     h->part.release();
@@ -1113,7 +1154,8 @@ int32_t kivi_cache_attention_dev(const kivi_cache *h, const float *dq, uint64_t 
     if (h->s.seq == 0) { // cache.rs:243-246: empty cache -> zeros
         CUDA_TRY(cudaMemsetAsync(dout, 0, out_n * sizeof(float), st), "attention zeros");
     } else {
-        rc = run_attention(h->s, nullptr, 1, dq, Hq, scale, dout, nullptr, nullptr, h->part, st, err);
+        rc = run_attention(h->s, nullptr, 1, dq, Hq, scale, dout, nullptr, nullptr, h->part, st, err,
+                           nullptr, &h->side);
         if (rc) return rc;
     }
     CUDA_TRY(mark_dev(h->dev_done, st), "attention_dev");
@@ -1202,7 +1244,7 @@ int32_t kivi_cache_decode(kivi_cache *h, const float *key, uint64_t key_len, con
     int32_t rc = append_device(h->s, dk, dv, 1, h->stream, err, qc);
     if (rc) return rc;
     rc = run_attention(h->s, nullptr, 1, dq, Hq, scale, dout, nullptr, nullptr, h->part, h->stream,
-                       err);
+                       err, nullptr, &h->side);
     if (rc) return rc;
     CUDA_TRY(output_done(out, dout, stage_out, n, h->stream), "decode D2H");
     CUDA_TRY(cudaStreamSynchronize(h->stream), "decode");
@@ -1229,7 +1271,8 @@ int32_t kivi_cache_attention_partial_dev(const kivi_cache *h, const float *dq, u
         CUDA_TRY(cudaStreamSynchronize(st), "partial");
         return set_err(err, KIVI_OK);
     }
-    rc = run_attention(h->s, nullptr, 1, dq, Hq, scale, dout, dm, dl, h->part, st, err);
+    rc = run_attention(h->s, nullptr, 1, dq, Hq, scale, dout, dm, dl, h->part, st, err, nullptr,
+                       &h->side);
     if (rc) return rc;
     CUDA_TRY(mark_dev(h->dev_done, st), "attention_partial_dev");
     return set_err(err, KIVI_OK);
@@ -1517,7 +1560,9 @@ int32_t kivi_session_new(kivi_prefix *p, kivi_session **out, kivi_error *err) {
     cudaError_t e = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->dev_done, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventRecord(s->dev_done, s->stream);
+    if (e == cudaSuccess) e = s->side.create();
     if (e != cudaSuccess) {
+        s->side.destroy();
         if (s->dev_done) cudaEventDestroy(s->dev_done);
         if (s->stream) cudaStreamDestroy(s->stream);
         delete s;
@@ -1537,6 +1582,7 @@ void kivi_session_free(kivi_session *s) {
         if (s->stream) cudaStreamSynchronize(s->stream);
         dfree(s->k);
         dfree(s->v);
+        s->side.destroy();
         s->stage.release();
         s->part.release();
         if (s->dev_done) cudaEventDestroy(s->dev_done);
@@ -1782,7 +1828,7 @@ static int32_t sessions_attention_dev(const kivi_session *const *ss, uint64_t n,
         bounds = mp->bounds;
     }
     return run_attention(p->s, views.data(), n, dq, Hq, scale, dout, nullptr, nullptr, part, st, err,
-                         bounds);
+                         bounds, &ss[0]->side);
 }
 
 int32_t kivi_session_attention_dev(const kivi_session *s, const float *dq, uint64_t Hq,
