@@ -7,7 +7,7 @@ A *step* is one decode step of the reference's hot path, RuntimeKv::decode
 eviction per step), then GQA decode attention of every query head over the
 whole cache (cache.rs:224-279).
 
-Workloads (BASELINE.json configs; --config N, default 1):
+Workloads (BASELINE.json configs 0-4; --config N, default 1):
   0  batch 1, 8 kv / 8 q heads, context 4096 (the reference's CPU-sized case)
   1  batch 16, 8 kv / 32 q heads, 2-bit, context 32768            (headline)
   2  batch 8, 8 kv / 64 q heads, 4-bit, context 131072, 1% key channels x20
@@ -17,6 +17,7 @@ Workloads (--config N, default 1):
   4  batch 1, 8 kv / 32 q heads, context 2^20 - 1 (step 1 flushes keys),
      sequence-sharded over the ranks: partial softmax states + one NCCL
      all-gather + rank-ordered merge per step
+  5  (extra, not a BASELINE config) config 1's shape with 8-bit codes
 All inputs are synthetic: K/V/Q N(0,1) fp32 with lognormal (configs 0,1,3,4)
 or x20-outlier (config 2) key channel scales, generated from seeded streams.
 
@@ -62,6 +63,10 @@ CONFIGS = {
             Hq=32, bits=2, ctx=65536, sessions=32, suffix=64),
     4: dict(_BASE, name="cfg4-seqshard-b1-h8-hq32-2bit-ctx1048575", mode="seqshard", B=1,
             Hq=32, bits=2, ctx=(1 << 20) - 1),
+    # not a BASELINE config: config 1's shape with 8-bit codes (the reference
+    # accepts 2, 4 and 8 bits, config.rs:31-55)
+    5: dict(_BASE, name="cfg1shape-8bit-b16-h8-hq32-d128-g32-r128-ctx32768", mode="decode", B=16,
+            Hq=32, bits=8, ctx=32768),
 }
 
 KERNELS = ("attn_tc", "attn_sets_tc", "attn_tail", "attn_chunk", "merge", "merge_shards",
@@ -731,9 +736,13 @@ def run_gpu(args, cfgd, rank, world, local_rank):
         wl.host_step()
     e2e_s = time.perf_counter() - t0
 
-    # max over ranks
+    # max over ranks (each rank's own step time kept beside it)
     vals = torch.tensor([t_ms, e2e_s, kern_avg_ms], dtype=torch.float64, device="cuda")
+    rank_ms = [t_ms / S]
     if dist:
+        every = [torch.zeros(1, dtype=torch.float64, device="cuda") for _ in range(world)]
+        dist.all_gather(every, vals[:1].clone())
+        rank_ms = [float(x.item()) / S for x in every]
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
     t_ms, e2e_s, kern_avg_ms = (float(x) for x in vals.tolist())
     # whole-job bytes per step (sum over ranks)
@@ -791,6 +800,8 @@ def run_gpu(args, cfgd, rank, world, local_rank):
         "gpu_launches": int(launches),
         "clocks": clk.summary(),
     }
+    if world > 1:
+        result["rank_ms_per_step"] = rank_ms
     if PREFILL_MS[0] > 0:
         # bulk append (prefill) of this rank: stream-tokens/s and fp32 K+V input GB/s
         result["prefill"] = {

@@ -1,7 +1,7 @@
 // kivi_attention_tc.cu -- tensor-core fused-dequant decode attention over the
 // packed main region of a stream (sm_100a).
 //
-// Applies to head_dim 128, group 32, 2- or 4-bit codes, up to 8 query heads
+// Applies to head_dim 128, group 32, 2-, 4- or 8-bit codes, up to 8 query heads
 // per kv head.  Work split: the main regions of all streams form one flat
 // sequence of 32-token groups (stream-major); every CTA of a launch takes an
 // equal contiguous run of it (one wave of resident CTAs per query set), so a
@@ -231,7 +231,7 @@ constexpr double pow2(int k) { return k >= 0 ? double(1ull << k) : 1.0 / double(
 template <int BITS, int J> __device__ __forceinline__ uint32_t code_pair(uint32_t x) {
     constexpr uint32_t kMask = ((1u << BITS) - 1u) * 0x10001u << (BITS * J);
     constexpr double kScale = pow2(-BITS * J);
-    constexpr double kMid = BITS == 2 ? 2.0 : 8.0;
+    constexpr double kMid = double(1u << (BITS - 1));
     constexpr uint32_t kMul = half2_bits(kScale);
     constexpr uint32_t kSub = half2_bits(-(1024.0 * kScale + kMid));
     uint32_t v, out;
@@ -243,7 +243,8 @@ template <int BITS, int J> __device__ __forceinline__ uint32_t code_pair(uint32_
 // Eight A registers from four code words.  wa/wb: K neighbours 2c, 2c+1 (keys:
 // channels; values: tokens), wc/wd: K neighbours 2c+8, 2c+9.  out[0..3] come
 // from wa/wb, out[4..7] from wc/wd, in code-position order (2-bit: the four
-// codes of byte `sel`; 4-bit: the two codes of each of two bytes).
+// codes of byte `sel`; 4-bit: the two codes of each of two bytes; 8-bit: the
+// four bytes of the word, one permute each).
 template <int BITS> struct Perm {
     uint32_t s0, s1; // byte-permute selectors
     __device__ __forceinline__ explicit Perm(int r) {
@@ -251,11 +252,17 @@ template <int BITS> struct Perm {
             const uint32_t k = (uint32_t)(r & 3);
             s0 = k | (k << 4) | ((k + 4) << 8) | ((k + 4) << 12);
             s1 = s0;
-        } else {
+        } else if (BITS == 4) {
             const uint32_t k = 2u * (uint32_t)(r & 1);
             s0 = k | (k << 4) | ((k + 4) << 8) | ((k + 4) << 12);
             s1 = s0 + 0x1111u;
+        } else { // 8-bit: the selectors are fixed (byte j -> both halves' low byte)
+            s0 = s1 = 0;
         }
+    }
+    // byte j of a (low half) and of b (high half), 8-bit codes
+    template <int J> static __device__ __forceinline__ uint32_t byte_pair(uint32_t a, uint32_t b) {
+        return __byte_perm(a, b, J | (J << 4) | ((J + 4) << 8) | ((J + 4) << 12));
     }
     __device__ __forceinline__ void eight(uint32_t wa, uint32_t wb, uint32_t wc, uint32_t wd,
                                           uint32_t out[8]) const {
@@ -269,7 +276,7 @@ template <int BITS> struct Perm {
             out[5] = code_pair<2, 1>(y);
             out[6] = code_pair<2, 2>(y);
             out[7] = code_pair<2, 3>(y);
-        } else {
+        } else if (BITS == 4) {
             const uint32_t x0 = __byte_perm(wa, wb, s0), x1 = __byte_perm(wa, wb, s1);
             const uint32_t y0 = __byte_perm(wc, wd, s0), y1 = __byte_perm(wc, wd, s1);
             out[0] = code_pair<4, 0>(x0);
@@ -280,6 +287,15 @@ template <int BITS> struct Perm {
             out[5] = code_pair<4, 1>(y0);
             out[6] = code_pair<4, 0>(y1);
             out[7] = code_pair<4, 1>(y1);
+        } else {
+            out[0] = code_pair<8, 0>(byte_pair<0>(wa, wb));
+            out[1] = code_pair<8, 0>(byte_pair<1>(wa, wb));
+            out[2] = code_pair<8, 0>(byte_pair<2>(wa, wb));
+            out[3] = code_pair<8, 0>(byte_pair<3>(wa, wb));
+            out[4] = code_pair<8, 0>(byte_pair<0>(wc, wd));
+            out[5] = code_pair<8, 0>(byte_pair<1>(wc, wd));
+            out[6] = code_pair<8, 0>(byte_pair<2>(wc, wd));
+            out[7] = code_pair<8, 0>(byte_pair<3>(wc, wd));
         }
     }
 };
@@ -315,6 +331,7 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : KIVI_TC_
     float *Ow = pbuf + kConsumers * kHeads * kPStride;                   // [warp][kHeads][128]
     float *Mw = Ow + kConsumers * kHeads * kD;                           // [warp][kHeads]
     float *Lw = Mw + kConsumers * kHeads;                                // [warp][kHeads]
+    unsigned int *bnd = reinterpret_cast<unsigned int *>(Lw + kConsumers * kHeads); // [2]
 
     const int64_t rbase = (int64_t)blockIdx.z * a.rows_per_set; // this query set's first row
     const int64_t W = (int64_t)a.nstreams * a.main_groups;
@@ -350,11 +367,12 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : KIVI_TC_
     const int r = lane >> 2, c = lane & 3;
     const int par = r & 1, hb = r >> 1;
     const Perm<BITS> perm(r);
-    constexpr float kMid = BITS == 2 ? 2.0f : 8.0f;
+    constexpr float kMid = (float)(1u << (BITS - 1));
     // lane's code-word offsets inside a stage (words): keys channel 2c, word
     // holding tokens 4r..4r+3; values token c, word holding channels 4r..4r+3
-    const int kw = 2 * c * IPC + (BITS == 2 ? (r >> 2) : (r >> 1));
-    const int vw = c * 4 * IPC + (BITS == 2 ? (r >> 2) : (r >> 1));
+    constexpr int kWordShift = BITS == 2 ? 2 : (BITS == 4 ? 1 : 0);
+    const int kw = 2 * c * IPC + (r >> kWordShift);
+    const int vw = c * 4 * IPC + (r >> kWordShift);
     // K position (value tiles) of this lane's logit tokens 4r + j: 2j + koff
     const int koff = 16 * (r >> 2) + ((r & 1) ? 1 : 0) + ((r & 2) ? 8 : 0);
     float *pw = pbuf + warp * (kHeads * kPStride);
@@ -371,9 +389,17 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : KIVI_TC_
         // |value scale| < 2^ev over all its packed groups (kept by the append
         // kernels), so that q'' s < 2^14 with q'' = q 2^(14 - e_q - es), and
         // p' s_v < 2^14 with p' = p 2^cv, cv = 3 - ev (p < 2^11 under the lazy
-        // softmax rescale below)
-        const int es = exp_ceil(__uint_as_float(a.kbound[s]));
-        const int ev = exp_ceil(__uint_as_float(a.vbound[s]));
+        // softmax rescale below).  Read once for the whole CTA: an append
+        // running beside this kernel may raise them, and every value read
+        // bounds the groups read here, but the warps' partial states are
+        // combined below under one factor.
+        if (threadIdx.x == 0) {
+            bnd[0] = a.kbound[s];
+            bnd[1] = a.vbound[s];
+        }
+        __syncthreads();
+        const int es = exp_ceil(__uint_as_float(bnd[0]));
+        const int ev = exp_ceil(__uint_as_float(bnd[1]));
         const float fk = exp2i(-es);
         const float cv = (float)(3 - min(max(ev, -120), 120));
 
@@ -667,7 +693,7 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : KIVI_TC_
 
 template <int BITS, int NT> size_t tc_smem() {
     return (size_t)kStages * TcGeom<BITS>::STAGE + kStages * sizeof(uint64_t) +
-           (size_t)kConsumers * NT * 4 * (kPStride + kD + 2) * sizeof(float);
+           (size_t)kConsumers * NT * 4 * (kPStride + kD + 2) * sizeof(float) + 2 * sizeof(unsigned int);
 }
 
 template <int BITS, int NT> struct TcKernelInfo {
@@ -705,7 +731,8 @@ cudaError_t launch_tc(const TcArgs &a, int nsets, cudaStream_t s) {
 } // namespace
 
 bool attention_tc_supported(const Geom &g, int gq) {
-    return g.D == kD && g.G == kG && (g.bits == 2 || g.bits == 4) && gq >= 1 && gq <= 8;
+    return g.D == kD && g.G == kG && (g.bits == 2 || g.bits == 4 || g.bits == 8) && gq >= 1 &&
+           gq <= 8;
 }
 
 cudaError_t plan_attention_tc(int bits, int gq, int64_t nstreams, int64_t main_groups,
@@ -717,8 +744,10 @@ cudaError_t plan_attention_tc(int bits, int gq, int64_t nstreams, int64_t main_g
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     const bool two = gq > 4;
-    const int res = bits == 2 ? (two ? TcKernelInfo<2, 2>::resident(dev) : TcKernelInfo<2, 1>::resident(dev))
-                              : (two ? TcKernelInfo<4, 2>::resident(dev) : TcKernelInfo<4, 1>::resident(dev));
+    const int res =
+        bits == 2   ? (two ? TcKernelInfo<2, 2>::resident(dev) : TcKernelInfo<2, 1>::resident(dev))
+        : bits == 4 ? (two ? TcKernelInfo<4, 2>::resident(dev) : TcKernelInfo<4, 1>::resident(dev))
+                    : (two ? TcKernelInfo<8, 2>::resident(dev) : TcKernelInfo<8, 1>::resident(dev));
     if (res <= 0) return cudaErrorInvalidConfiguration;
     const int64_t W = nstreams * main_groups;
     // one wave of resident CTAs, at least kMinGroups groups each
@@ -741,7 +770,8 @@ cudaError_t launch_attention_tc(const TcArgs &a, int bits, int nsets, cudaStream
     if (nsets > 65535) return cudaErrorInvalidValue;
     const bool two = a.GQ > 4;
     if (bits == 2) return two ? launch_tc<2, 2>(a, nsets, s) : launch_tc<2, 1>(a, nsets, s);
-    return two ? launch_tc<4, 2>(a, nsets, s) : launch_tc<4, 1>(a, nsets, s);
+    if (bits == 4) return two ? launch_tc<4, 2>(a, nsets, s) : launch_tc<4, 1>(a, nsets, s);
+    return two ? launch_tc<8, 2>(a, nsets, s) : launch_tc<8, 1>(a, nsets, s);
 }
 
 namespace {
@@ -987,23 +1017,25 @@ __global__ void __launch_bounds__(kTailThreads) attn_tail_kernel(const TailArgs 
     }
 }
 
-// One CTA per row (head_dim 128): log-sum-exp merge of the row's `parts`
-// slots.  Warp w of NW sums slots w, w+NW, ... (4 channels per lane); the
-// warp partials and the normaliser are combined in a fixed pairwise order
-// (deterministic).  NW = 16 for rows with many slots (a long sequence split
-// over many CTAs), so every slot's load is in flight at once.
+// Shared-memory work area of one row's merge (NW warps).
+template <int NW> struct MergeSmem {
+    float wsh[512];
+    __align__(16) float osh[NW][128];
+    float lsh[NW];
+    float Msh;
+};
+
+// Log-sum-exp merge of one row's `parts` slots (head_dim 128) by a CTA of NW
+// warps: warp w sums slots w, w+NW, ... (4 channels per lane); the warp
+// partials and the normaliser are combined in a fixed pairwise order
+// (deterministic).  Threads 0..127 return channel threadIdx.x of the merged
+// unnormalised o; every thread gets the row's M (natural log units) and L.
 template <int NW>
-__global__ void __launch_bounds__(32 * NW) merge_rows_kernel(const float *part_ml,
-                                                             const float *part_o, int parts,
-                                                             int64_t rows, float *out,
-                                                             float *out_m, float *out_l) {
+__device__ __forceinline__ void merge_row_state(const float *part_ml, const float *part_o,
+                                                int parts, int64_t row, MergeSmem<NW> &sm,
+                                                float &o_out, float &M_out, float &L_out) {
     constexpr int kThreads = 32 * NW;
-    __shared__ float wsh[512];
-    __shared__ __align__(16) float osh[NW][128];
-    __shared__ float lsh[NW];
-    __shared__ float Msh;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t row = blockIdx.x;
     const float *ml = part_ml + row * parts * 2;
     // this warp's first kPre slots of o are loaded before the maximum and the
     // weights are known, so their memory latency overlaps those two phases
@@ -1021,20 +1053,20 @@ __global__ void __launch_bounds__(32 * NW) merge_rows_kernel(const float *part_m
             if (ml[2 * c + 1] > 0.0f) M = fmaxf(M, ml[2 * c]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-        if (lane == 0) Msh = M;
+        if (lane == 0) sm.Msh = M;
     }
     __syncthreads();
-    const float M = Msh;
+    const float M = sm.Msh;
     float Lp = 0.0f;
     for (int c = threadIdx.x; c < parts; c += kThreads) {
         const float l = ml[2 * c + 1];
         const float w = (l > 0.0f) ? expf(ml[2 * c] - M) : 0.0f;
-        if (c < 512) wsh[c] = w;
+        if (c < 512) sm.wsh[c] = w;
         Lp = fmaf(l, w, Lp);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) Lp += __shfl_xor_sync(0xffffffffu, Lp, o);
-    if (lane == 0) lsh[warp] = Lp;
+    if (lane == 0) sm.lsh[warp] = Lp;
     __syncthreads();
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     // slots in increasing order per warp (the prefetched ones first)
@@ -1042,7 +1074,7 @@ __global__ void __launch_bounds__(32 * NW) merge_rows_kernel(const float *part_m
     for (int i = 0; i < kPre; ++i) {
         const int c = warp + NW * i;
         if (c < parts) {
-            const float w = wsh[c]; // c < NW kPre <= 512
+            const float w = sm.wsh[c]; // c < NW kPre <= 512
             acc.x = fmaf(pre[i].x, w, acc.x);
             acc.y = fmaf(pre[i].y, w, acc.y);
             acc.z = fmaf(pre[i].z, w, acc.z);
@@ -1053,7 +1085,7 @@ __global__ void __launch_bounds__(32 * NW) merge_rows_kernel(const float *part_m
     for (int c = warp + NW * kPre; c < parts; c += NW) {
         float w;
         if (c < 512) {
-            w = wsh[c];
+            w = sm.wsh[c];
         } else {
             const float l = ml[2 * c + 1];
             w = (l > 0.0f) ? expf(ml[2 * c] - M) : 0.0f;
@@ -1064,24 +1096,47 @@ __global__ void __launch_bounds__(32 * NW) merge_rows_kernel(const float *part_m
         acc.z = fmaf(o.z, w, acc.z);
         acc.w = fmaf(o.w, w, acc.w);
     }
-    reinterpret_cast<float4 *>(osh[warp])[lane] = acc;
+    reinterpret_cast<float4 *>(sm.osh[warp])[lane] = acc;
     __syncthreads();
+    float o = 0.0f, L = 0.0f;
+    if (threadIdx.x < 128) {
+        const int d = threadIdx.x;
+        float ov[NW], lv[NW];
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+            ov[w] = sm.osh[w][d];
+            lv[w] = sm.lsh[w];
+        }
+#pragma unroll
+        for (int span = 1; span < NW; span *= 2)
+#pragma unroll
+            for (int w = 0; w + span < NW; w += 2 * span) {
+                ov[w] += ov[w + span];
+                lv[w] += lv[w + span];
+            }
+        o = ov[0];
+        L = lv[0];
+    }
+    o_out = o; // threads >= 128 return o = L = 0 (unused)
+    M_out = M;
+    L_out = L;
+}
+
+// One CTA per row (head_dim 128): the row's merged output (normalised), or
+// its merged (m, l, o) when out_m is given.  NW = 16 for rows with many slots
+// (a long sequence split over many CTAs), so every slot's load is in flight
+// at once.
+template <int NW>
+__global__ void __launch_bounds__(32 * NW) merge_rows_kernel(const float *part_ml,
+                                                             const float *part_o, int parts,
+                                                             int64_t rows, float *out,
+                                                             float *out_m, float *out_l) {
+    __shared__ MergeSmem<NW> sm;
+    const int64_t row = blockIdx.x;
+    float o, M, L;
+    merge_row_state<NW>(part_ml, part_o, parts, row, sm, o, M, L);
     if (threadIdx.x >= 128) return;
     const int d = threadIdx.x;
-    float ov[NW], lv[NW];
-#pragma unroll
-    for (int w = 0; w < NW; ++w) {
-        ov[w] = osh[w][d];
-        lv[w] = lsh[w];
-    }
-#pragma unroll
-    for (int span = 1; span < NW; span *= 2)
-#pragma unroll
-        for (int w = 0; w + span < NW; w += 2 * span) {
-            ov[w] += ov[w + span];
-            lv[w] += lv[w + span];
-        }
-    const float o = ov[0], L = lv[0];
     if (out_m) {
         out[row * 128 + d] = o;
         if (d == 0) {
@@ -1090,6 +1145,115 @@ __global__ void __launch_bounds__(32 * NW) merge_rows_kernel(const float *part_m
         }
     } else {
         out[row * 128 + d] = (L > 0.0f) ? o * (1.0f / L) : 0.0f;
+    }
+}
+
+// ---------------------------------------------------------------- peer exchange
+// The cross-rank step of sequence sharding as one kernel over NVLink peer
+// memory, one CTA per query row: merge this rank's partial slots of the row
+// (merge_row_state), store the merged (m, l, o) into every rank's exchange
+// buffer (plain stores to peer memory, no multicast), publish it with a
+// per-(rank, row) flag set to this step's epoch (system-scope release), wait
+// (bounded, about a second) until every rank's record of the row has arrived
+// in this rank's buffer (system-scope acquire), and merge the records in rank
+// order with the cross-shard merge's arithmetic, so the output equals the
+// all-gather path's bit for bit.  Records alternate between two buffers by
+// epoch parity: a rank can run at most one step ahead of the slowest (it
+// waits for everyone's record of the step it is in), so a record is never
+// overwritten while a peer may still read it.
+constexpr int kExRec = 2 + kD; // floats per (rank, row) record: m, l, o[128]
+constexpr unsigned kExchangeWaitCode = 8u;
+
+__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int *p) {
+    unsigned int v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned int *p, unsigned int v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Waits until *f == epoch; gives up after ~1 s (records the failure like the
+// other bounded waits) and returns false.
+__device__ __forceinline__ bool wait_epoch(const unsigned int *f, unsigned int epoch) {
+    if (ld_acquire_sys(f) == epoch) return true;
+    const long long t0 = clock64();
+    while (ld_acquire_sys(f) != epoch) {
+        if (clock64() - t0 > kWaitCycles) {
+            atomicOr(&g_tc_error, kExchangeWaitCode);
+            if (g_tc_hint) *reinterpret_cast<volatile unsigned int *>(g_tc_hint) = 1u;
+            return false;
+        }
+        __nanosleep(32);
+    }
+    return true;
+}
+
+template <int NW>
+__global__ void __launch_bounds__(32 * NW) exchange_rows_kernel(const float *part_ml,
+                                                                const float *part_o, int parts,
+                                                                int64_t rows, ExchangeArgs x,
+                                                                float *out) {
+    __shared__ MergeSmem<NW> sm;
+    __shared__ float w_sh[kMaxExchangeRanks];
+    __shared__ float L_sh;
+    __shared__ int fail;
+    const int64_t row = blockIdx.x;
+    float o, M, L;
+    merge_row_state<NW>(part_ml, part_o, parts, row, sm, o, M, L);
+    if (threadIdx.x == 0) fail = 0;
+    // 1. this rank's record of the row into every rank's buffer
+    const int64_t mine = ((int64_t)(x.parity * x.world + x.rank) * rows + row) * kExRec;
+    for (int r = 0; r < x.world; ++r) {
+        float *dst = x.data[r] + mine;
+        if (threadIdx.x < kD) dst[2 + threadIdx.x] = o;
+        if (threadIdx.x == 0) {
+            dst[0] = M;
+            dst[1] = L;
+        }
+    }
+    __syncthreads();
+    // 2. publish: thread r sets rank r's flag of (this rank, row); the barrier
+    // above orders the whole CTA's record stores before the release
+    const int64_t fmine = (int64_t)(x.parity * x.world + x.rank) * rows + row;
+    if ((int)threadIdx.x < x.world) {
+        __threadfence_system();
+        st_release_sys(x.flags[threadIdx.x] + fmine, x.epoch);
+    }
+    // 3. every rank's record of the row, in this rank's buffer
+    if ((int)threadIdx.x < x.world) {
+        const int64_t fr = (int64_t)(x.parity * x.world + threadIdx.x) * rows + row;
+        if (!wait_epoch(x.flags[x.rank] + fr, x.epoch)) fail = 1;
+    }
+    __syncthreads();
+    // 4. rank-ordered merge (the cross-shard merge's arithmetic)
+    const float *rec = x.data[x.rank] + (int64_t)x.parity * x.world * rows * kExRec;
+    if (threadIdx.x == 0) {
+        float Mx = -INFINITY;
+        for (int c = 0; c < x.world; ++c) {
+            const float *rc = rec + ((int64_t)c * rows + row) * kExRec;
+            if (rc[1] > 0.0f) Mx = fmaxf(Mx, rc[0]);
+        }
+        float Lx = 0.0f;
+        for (int c = 0; c < x.world; ++c) {
+            const float *rc = rec + ((int64_t)c * rows + row) * kExRec;
+            const float lc = rc[1];
+            const float e = (lc > 0.0f) ? expf(rc[0] - Mx) : 0.0f;
+            w_sh[c] = e;
+            Lx = __fmaf_rn(lc, e, Lx);
+        }
+        L_sh = fail ? 0.0f : Lx;
+    }
+    __syncthreads();
+    if (threadIdx.x < kD) {
+        const int d = threadIdx.x;
+        const float inv = (L_sh > 0.0f) ? 1.0f / L_sh : 0.0f;
+        float acc = 0.0f;
+        for (int c = 0; c < x.world; ++c)
+            if (w_sh[c] != 0.0f)
+                acc = __fmaf_rn(rec[((int64_t)c * rows + row) * kExRec + 2 + d], w_sh[c], acc);
+        out[row * kD + d] = acc * inv;
     }
 }
 
@@ -1103,8 +1267,25 @@ cudaError_t launch_attention_tail(const TailArgs &a, int ntiles, int nstreams, i
     const dim3 grid((unsigned)ntiles, (unsigned)nstreams, (unsigned)nsets);
     if (a.g.bits == 2)
         attn_tail_kernel<2><<<grid, kTailThreads, 0, s>>>(a);
-    else
+    else if (a.g.bits == 4)
         attn_tail_kernel<4><<<grid, kTailThreads, 0, s>>>(a);
+    else
+        attn_tail_kernel<8><<<grid, kTailThreads, 0, s>>>(a);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_exchange_rows(const float *part_ml, const float *part_o, int parts,
+                                 int64_t rows, const ExchangeArgs &x, float *out, cudaStream_t s) {
+    if (rows <= 0) return cudaSuccess;
+    if (x.world < 1 || x.world > kMaxExchangeRanks) return cudaErrorInvalidValue;
+    ProfScope prof("merge_exchange", s);
+    if (parts > 32)
+        exchange_rows_kernel<16><<<(unsigned)rows, 512, 0, s>>>(part_ml, part_o, parts, rows, x,
+                                                                out);
+    else
+        exchange_rows_kernel<4><<<(unsigned)rows, 128, 0, s>>>(part_ml, part_o, parts, rows, x,
+                                                               out);
     count_launch();
     return cudaGetLastError();
 }

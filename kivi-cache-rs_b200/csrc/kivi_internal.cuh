@@ -214,13 +214,31 @@ cudaError_t launch_merge(const float *part_ml, const float *part_o, int64_t rows
                          cudaStream_t s);
 // Most slots launch_merge takes (one float of dynamic shared memory each).
 int merge_max_parts();
+
+// Peer-memory exchange of merged partial states between the ranks of a
+// sequence-sharded cache (kivi_attention_tc.cu, exchange_rows_kernel).
+// data[r] / flags[r]: rank r's exchange buffer as this device addresses it
+// (its own allocation for r == rank, an IPC mapping otherwise): records
+// [2][world][rows][2 + 128] floats, flags [2][world][rows].
+constexpr int kMaxExchangeRanks = 16;
+struct ExchangeArgs {
+    float *data[kMaxExchangeRanks];
+    unsigned int *flags[kMaxExchangeRanks];
+    int rank, world, parity;
+    unsigned int epoch;
+};
+// Merges this rank's `parts` slots per row, exchanges the merged states with
+// every rank over peer memory and writes the rank-ordered merge of all of them
+// (normalised rows) to out.  Every rank launches it once per step.
+cudaError_t launch_exchange_rows(const float *part_ml, const float *part_o, int parts,
+                                 int64_t rows, const ExchangeArgs &x, float *out, cudaStream_t s);
 // Cross-shard merge: part c's m/l rows start at c*ml_stride, its o rows at
 // c*o_stride (floats); merged in part order.
 cudaError_t launch_merge_shards(const float *m, const float *l, const float *o, int64_t parts,
                                 int64_t rows, int D, int64_t ml_stride, int64_t o_stride,
                                 float *out, cudaStream_t s);
 // Tensor-core attention over the packed main region (kivi_attention_tc.cu):
-// head_dim 128, group 32, 2/4-bit, <= 8 query heads per kv head.  The main
+// head_dim 128, group 32, 2/4/8-bit, <= 8 query heads per kv head.  The main
 // regions of all streams (main_groups 32-token groups each) form one flat
 // stream-major sequence; CTA i takes groups [i*per, (i+1)*per) and writes one
 // partial slot per stream it touches (slot i - first CTA of that stream);

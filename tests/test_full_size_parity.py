@@ -226,3 +226,9 @@ def test_config3_full_size_sessions_decode_step(env):
     for i in range(S):  # and session by session
         assert max_abs(got[i], ref64[i]) <= ATOL
         assert rel_l2(got[i], ref64[i]) <= RTOL_L2
+
+
+def test_config1_shape_8bit_full_size_decode_step(env):
+    """BASELINE config 1's shape with 8-bit codes (KiviConfig accepts 2, 4 or
+    8 bits, config.rs:31-55): the tensor-core decode path's 8-bit form."""
+    decode_case(env, "config1_8bit", 16, 8, 32, 8, 32768, "lognormal", 505)
