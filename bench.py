@@ -70,8 +70,8 @@ CONFIGS = {
 }
 
 KERNELS = ("attn_tc", "attn_sets_tc", "attn_tail", "attn_chunk", "merge", "merge_shards",
-           "append_small", "key_groups", "value_tokens", "copy_rows", "suffix_append",
-           "prefix_bounds")
+           "merge_exchange", "append_small", "key_groups", "value_tokens", "copy_rows",
+           "suffix_append", "prefix_bounds")
 
 
 # ---------------------------------------------------------------- helpers
@@ -332,6 +332,7 @@ class DevGen:
 
 
 PREFILL_MS = [0.0, 0]  # device time of the prefill appends, tokens appended (per process)
+EXCHANGE = ["auto"]   # config 4's cross-rank exchange (--exchange)
 
 
 def prefill(cache, gen, cfgd, n_tokens, stream):
@@ -485,9 +486,24 @@ class RagWorkload:
         torch.cuda.synchronize()
 
     def _step(self, ks, vs, q):
-        self.K.sessions_append_dev(self.sessions, ks, vs, 1, stream=self.stream)
-        self.K.sessions_attention_batched_dev(self.sessions, q, self.Hq, self.scale, self.dout,
-                                              stream=self.stream)
+        # the two C calls of kivi_cache.sessions_append_dev and
+        # sessions_attention_batched_dev, their ctypes arguments built once, so
+        # that host-side argument packing stays far below a step's device time
+        K = self.K
+        if getattr(self, "_dargs", None) is None:
+            self._derr = K._Err()
+            st = self.stream.cuda_stream
+            self._dargs = (self._arr, self.S, st, ctypes.c_float(self.scale), self.dout.data_ptr(),
+                           ctypes.byref(self._derr))
+        arr, S, st, sc, dout, err = self._dargs
+        lib = K.lib()
+        rc = lib.kivi_sessions_append_dev(arr, S, ks.data_ptr(), vs.data_ptr(), 1, st, err)
+        if rc == 0:
+            rc = lib.kivi_sessions_attention_batched_dev(arr, S, q.data_ptr(), self.Hq, sc, dout,
+                                                         st, err)
+        if rc:
+            e = self._derr
+            raise K.KiviError(e.code, e.a, e.b, None, e.message.decode())
 
     def step(self, i):
         S = self.S
@@ -563,7 +579,8 @@ class SeqShardWorkload:
         self.gen = DevGen(4321 + rank, chs)
         qgen = DevGen(999, chs)  # the same queries on every rank
         cfg = K.KiviConfig.try_new(cfgd["bits"], cfgd["G"], cfgd["R"])
-        self.sc = SeqShardedCache(cfg, B, H, D, cfgd["ctx"], device=local_rank)
+        self.sc = SeqShardedCache(cfg, B, H, D, cfgd["ctx"], device=local_rank,
+                                  exchange=EXCHANGE[0])
         plan = self.sc.plan
         self.sc.reserve(plan.tokens + (nsteps + nprof + 64 + 2 * cfgd["R"] if plan.tail else 0))
         prefill(self.sc.cache, self.gen, cfgd, plan.tokens, stream)
@@ -597,6 +614,9 @@ class SeqShardWorkload:
     e2e_api = ("SeqShardedCache.decode: query H2D on every rank, K/V H2D on the tail rank, "
                "output D2H, pinned host buffers")
 
+    def close(self):
+        self.sc.close()
+
     def io_bytes(self):
         # per rank: the query, the output; K/V only on the tail rank (counted once)
         return (self.hq.numel() + (self.hk.numel() + self.hv.numel()) / self.world) * 4, \
@@ -622,8 +642,6 @@ class SeqShardWorkload:
             return self.cache_bytes() + c["B"] * c["Hq"] * c["D"] * 4
         return main_region_bytes(self.sc.cache, c["B"] * c["H"], c["B"] * c["Hq"], c)
 
-    def close(self):
-        pass
 
 
 # ---------------------------------------------------------------- GPU arm
@@ -809,6 +827,8 @@ def run_gpu(args, cfgd, rank, world, local_rank):
             "input_gbs": PREFILL_MS[1] * cfgd["D"] * 8 / (PREFILL_MS[0] / 1e3) / 1e9,
             "ms": PREFILL_MS[0], "chunk_kernel": "key_groups + value_tokens + copy_rows2",
         }
+    if mode == "decode":
+        result["noalloc"] = noalloc_microbench(K, wl, stream)
     if mode == "seqshard" and rank == 0:
         result["shard_tokens_rank0"] = wl.sc.plan.tokens
         result["key_flush"] = key_flush_microbench(K, cfgd, stream)
@@ -982,6 +1002,42 @@ def key_flush_microbench(K, cfgd, stream, reps=12):
                     "vs one that does not"}
 
 
+def noalloc_microbench(K, wl, stream, reps=16):
+    """The allocation-free attention entry (kivi_cache_attention_noalloc_dev,
+    scratch in a fixed device array) beside kivi_cache_attention_dev on the
+    same cache and query: median per-call device time (CUDA events on the
+    launching stream, L2 not flushed), and whether both give the same bits."""
+    import torch
+
+    cache, q, hq, scale = wl.cache, wl.dq[0], wl.Hq, wl.scale
+    out_a = torch.empty_like(wl.dout)
+    out_b = torch.empty_like(wl.dout)
+    err = K._Err()
+
+    def noalloc():
+        rc = K.lib().kivi_cache_attention_noalloc_dev(
+            cache._h, q.data_ptr(), hq, ctypes.c_float(scale), out_b.data_ptr(),
+            ctypes.c_void_p(stream.cuda_stream), ctypes.byref(err))
+        if rc:
+            raise K.KiviError(err.code, err.a, err.b, None, err.message.decode())
+
+    times = {"attention_dev": [], "noalloc_dev": []}
+    for _ in range(reps + 2):
+        for name, fn in (("attention_dev", lambda: cache.attention_dev(q, hq, scale, out_a,
+                                                                       stream=stream)),
+                         ("noalloc_dev", noalloc)):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            stream.synchronize()
+            times[name].append(e0.elapsed_time(e1) * 1e3)
+    return {"attention_dev_us": float(np.median(times["attention_dev"][2:])),
+            "noalloc_dev_us": float(np.median(times["noalloc_dev"][2:])),
+            "same_bits": bool(torch.equal(out_a.view(torch.int32), out_b.view(torch.int32))),
+            "reps": reps}
+
+
 def host_info():
     """CPU model and logical core count of this host."""
     model = None
@@ -1046,6 +1102,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", default="auto", choices=["auto", "p2p", "nccl"],
+                    help="config 4: peer-memory exchange kernel or NCCL all-gather")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -1053,6 +1111,7 @@ def main():
     world = env_int("WORLD_SIZE", 1)
     local_rank = env_int("LOCAL_RANK", 0)
     cfgd = CONFIGS[args.config]
+    EXCHANGE[0] = args.exchange
     if args.impl == "reference":
         res = run_reference(args, cfgd, rank, world)
     else:

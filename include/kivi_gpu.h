@@ -146,6 +146,7 @@ typedef struct kivi_cache kivi_cache;     /* KiviCache (cache.rs:71-83) */
 typedef struct kivi_prefix kivi_prefix;   /* SharedPrefix (prefix.rs:32-35), refcounted */
 typedef struct kivi_session kivi_session; /* RagSession (prefix.rs:41-46) */
 typedef struct kivi_guard kivi_guard;     /* QualityGuard (guard.rs:38-47) */
+typedef struct kivi_exchange kivi_exchange; /* peer-memory exchange of a sequence-sharded cache */
 
 /* ---------------------------------------------------------------- library */
 
@@ -282,6 +283,39 @@ int32_t kivi_cache_attention_partial_packed_dev(const kivi_cache *cache, const f
 int32_t kivi_merge_packed_partials_dev(uint64_t parts, uint64_t rows, uint64_t head_dim,
                                        const float *d_packed, float *d_out, void *stream,
                                        kivi_error *err);
+/* Peer-memory exchange for sequence sharding over the GPUs of one node (no
+ * counterpart in the reference, which is single-device).  Each rank of a
+ * sequence-sharded cache creates one exchange for its device (rows = batch *
+ * num_q_heads of the attention calls, head_dim 128), hands its 64-byte IPC
+ * handle to every other rank (any host channel; the Python layer uses the
+ * process group), and opens the handles of all ranks in rank order.  Then
+ * every rank calls kivi_cache_decode_exchange_dev once per step, in the same
+ * order: the tail rank with the step's key and value (it appends them), the
+ * others with null key and value.  Each call attends over its own shard,
+ * merges its partial states, stores the merged (m, l, o) of every query row
+ * into every rank's exchange buffer over NVLink (plain peer stores), waits for
+ * every rank's states of the row (a bounded wait: after about a second it
+ * gives up, the row's output is zero and kivi_device_wait_status reports it)
+ * and writes the rank-ordered merge, which equals the all-gather path
+ * (kivi_cache_attention_partial_packed_dev + an all-gather +
+ * kivi_merge_packed_partials_dev) bit for bit.  A rank can run at most one
+ * step ahead of the others.  Teardown: kivi_exchange_close on every rank,
+ * then (after the ranks have agreed that all have closed) kivi_exchange_free. */
+int32_t kivi_exchange_new(int32_t device, uint32_t rank, uint32_t world, uint64_t rows,
+                          uint64_t head_dim, kivi_exchange **out, kivi_error *err);
+/* this rank's buffer as a 64-byte CUDA IPC handle */
+int32_t kivi_exchange_ipc_handle(const kivi_exchange *exchange, void *handle, kivi_error *err);
+/* handles: world x 64 bytes in rank order (this rank's own entry is ignored) */
+int32_t kivi_exchange_open(kivi_exchange *exchange, const void *handles, kivi_error *err);
+void kivi_exchange_close(kivi_exchange *exchange);
+void kivi_exchange_free(kivi_exchange *exchange);
+/* One decode step of a sequence-sharded cache (RuntimeKv::decode, runtime.rs:
+ * 46-56, over all shards): d_key/d_value (tail rank) or null (other ranks). */
+int32_t kivi_cache_decode_exchange_dev(kivi_cache *cache, kivi_exchange *exchange,
+                                       const float *d_key, const float *d_value,
+                                       const float *d_query, uint64_t num_q_heads, float scale,
+                                       float *d_out, void *stream, kivi_error *err);
+
 /* Quantize the fp32 value window into the packed store (no counterpart in the
  * reference).  Used for an interior sequence shard, whose tokens a single-device
  * cache would already have evicted: the packed values are bit-identical to

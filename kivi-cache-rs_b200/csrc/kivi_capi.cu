@@ -459,6 +459,23 @@ int32_t append_device(KvState &s, const float *dk, const float *dv, uint64_t seq
 constexpr int64_t kChunkTokens = 256;   // generic kernel: tokens per main chunk
 constexpr int64_t kTailTile = 32;       // prefix-tail tokens per CTA
 
+} // namespace
+
+// Peer-memory exchange buffers of one rank of a sequence-sharded cache.
+struct kivi_exchange {
+    int device = 0;
+    uint32_t rank = 0, world = 1;
+    uint64_t rows = 0, D = 0;
+    void *base = nullptr;  // this rank's buffer: records [2][world][rows][2 + D], then flags
+    size_t rec_bytes = 0, bytes = 0;
+    void *peer[kivi::kMaxExchangeRanks] = {}; // rank r's buffer as this device addresses it
+    bool opened = false;
+    unsigned int epoch = 0; // steps exchanged so far (every rank counts the same)
+};
+
+namespace {
+
+
 // A handle's second stream: the dense tail tiles of an attention run on it
 // beside the main-region kernel (they read other tokens and write other
 // partial slots), forked from and joined back into the call's stream by two
@@ -494,7 +511,8 @@ struct SessionView {
 int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, const float *d_q,
                       uint64_t Hq, float scale, float *d_out, float *d_m, float *d_l,
                       Scratch &scratch, cudaStream_t stream, kivi_error *err,
-                      const int *bounds = nullptr, const SideLane *side = nullptr) {
+                      const int *bounds = nullptr, const SideLane *side = nullptr,
+                      int64_t main_vq = -1, kivi_exchange *ex = nullptr) {
     const Geom &g = p.g;
     const uint64_t Gq = Hq / p.H;
     // the tensor-core kernel reads query rows as float2
@@ -509,8 +527,14 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
         // frozen prefix (bounds != null) run the tcgen05 multi-set kernel,
         // which dequantizes each group once for all sets (results equal the
         // per-session ones within the attention tolerance).
+        // main_vq >= 0: a decode step whose caller recorded side->fork and
+        // made side->s wait on it *before* enqueueing the step's append on
+        // `stream`; the main region is then the groups packed before that
+        // append (the append writes only past them), it runs on side->s
+        // beside the append, and the tail tiles cover everything after it.
+        const bool pre = main_vq >= 0 && side && side->s;
         const uint64_t G = p.cfg.group_size;
-        const uint64_t main_tokens = p.vq / G * G;
+        const uint64_t main_tokens = (pre ? (uint64_t)main_vq : p.vq) / G * G;
         const int64_t main_groups = (int64_t)(main_tokens / G);
         int64_t per = 0;
         int nslots = 0;
@@ -545,8 +569,9 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
             const float *q = d_q + s0 * rows1 * p.D;
             // tail tiles on the side lane when both kernels run (serial while
             // per-kernel timing is on, so each event pair brackets one kernel)
-            const bool fork = side && side->s && NTT > 0 && (sets || NC > 0) &&
+            const bool fork = !pre && side && side->s && NTT > 0 && (sets || NC > 0) &&
                               !kivi::g_prof_on.load();
+            cudaStream_t main_st = pre ? side->s : stream;
             if (fork) {
                 CUDA_TRY(cudaEventRecord(side->fork, stream), "attention fork");
                 CUDA_TRY(cudaStreamWaitEvent(side->s, side->fork, 0), "attention fork");
@@ -576,7 +601,7 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
                 t.part_o = part_o;
                 t.parts = parts;
                 CUDA_TRY(kivi::launch_attention_sets(t, (int)p.cfg.bits, snc, (int)(p.B * p.H), nz,
-                                                     stream),
+                                                     main_st),
                          "attention (tcgen05, query sets)");
             } else if (NC > 0) {
                 kivi::TcArgs t{};
@@ -602,7 +627,7 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
                 t.rows_per_set = (int64_t)rows1;
                 t.kbound = p.st.kbound;
                 t.vbound = p.st.vbound;
-                CUDA_TRY(kivi::launch_attention_tc(t, (int)p.cfg.bits, (int)ns, stream),
+                CUDA_TRY(kivi::launch_attention_tc(t, (int)p.cfg.bits, (int)ns, main_st),
                          "attention (tensor cores)");
             }
             kivi::TailArgs ta{};
@@ -632,11 +657,27 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
             CUDA_TRY(kivi::launch_attention_tail(ta, (int)NTT, (int)(p.B * p.H), (int)ns,
                                                  fork ? side->s : stream),
                      "attention tail");
-            if (fork) {
+            if (fork || pre) {
                 CUDA_TRY(cudaEventRecord(side->join, side->s), "attention join");
                 CUDA_TRY(cudaStreamWaitEvent(stream, side->join, 0), "attention join");
             }
             const uint64_t off = s0 * rows1;
+            if (ex) { // nsess == 1: merge, exchange with every rank and merge again
+                kivi::ExchangeArgs x{};
+                for (uint32_t r = 0; r < ex->world; ++r) {
+                    x.data[r] = static_cast<float *>(ex->peer[r]);
+                    x.flags[r] = reinterpret_cast<unsigned int *>(
+                        static_cast<char *>(ex->peer[r]) + ex->rec_bytes);
+                }
+                x.rank = (int)ex->rank;
+                x.world = (int)ex->world;
+                x.epoch = ++ex->epoch;
+                x.parity = (int)(x.epoch & 1u);
+                CUDA_TRY(kivi::launch_exchange_rows(part_ml, part_o, parts, (int64_t)rows, x,
+                                                    d_out + off * p.D, stream),
+                         "attention exchange");
+                continue;
+            }
             CUDA_TRY(kivi::launch_merge_rows(part_ml, part_o, parts, (int64_t)rows,
                                              d_out + off * p.D, d_m ? d_m + off : nullptr,
                                              d_l ? d_l + off : nullptr, stream),
@@ -1143,23 +1184,29 @@ int32_t kivi_cache_append(kivi_cache *h, const float *keys, uint64_t keys_len,
     return set_err(err, KIVI_OK);
 }
 
-int32_t kivi_cache_attention_dev(const kivi_cache *h, const float *dq, uint64_t Hq, float scale,
-                                 float *dout, void *stream, kivi_error *err) {
-    if (!h) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null cache");
+// Attention over the whole cache on `st`; `side` (or null: one stream) takes
+// the tail tiles beside the main-region kernel.
+static int32_t attention_on(const kivi_cache *h, const float *dq, uint64_t Hq, float scale,
+                            float *dout, cudaStream_t st, const SideLane *side, kivi_error *err) {
     int32_t rc = check_query(h->s, Hq, 0, false, err);
     if (rc) return rc;
     DeviceGuard dg(h->s.device);
-    cudaStream_t st = pick(stream, h->stream);
     const uint64_t out_n = h->s.B * Hq * h->s.D;
     if (h->s.seq == 0) { // cache.rs:243-246: empty cache -> zeros
         CUDA_TRY(cudaMemsetAsync(dout, 0, out_n * sizeof(float), st), "attention zeros");
     } else {
         rc = run_attention(h->s, nullptr, 1, dq, Hq, scale, dout, nullptr, nullptr, h->part, st, err,
-                           nullptr, &h->side);
+                           nullptr, side);
         if (rc) return rc;
     }
     CUDA_TRY(mark_dev(h->dev_done, st), "attention_dev");
     return set_err(err, KIVI_OK);
+}
+
+int32_t kivi_cache_attention_dev(const kivi_cache *h, const float *dq, uint64_t Hq, float scale,
+                                 float *dout, void *stream, kivi_error *err) {
+    if (!h) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null cache");
+    return attention_on(h, dq, Hq, scale, dout, pick(stream, h->stream), &h->side, err);
 }
 
 int32_t kivi_cache_attention(const kivi_cache *h, const float *query, uint64_t query_len,
@@ -1179,12 +1226,72 @@ int32_t kivi_cache_attention(const kivi_cache *h, const float *query, uint64_t q
     float *dq = mh->stage.as<float>(), *stage_out = mh->stage.as<float>(n * sizeof(float));
     CUDA_TRY(input_staged(query, dq, n, h->stream), "attention H2D");
     float *dout = output_target(out, stage_out, h->s.seq > 0);
-    rc = kivi_cache_attention_dev(h, dq, Hq, scale, dout, h->stream, err);
+    rc = attention_on(h, dq, Hq, scale, dout, h->stream, nullptr, err);
     if (rc) return rc;
     CUDA_TRY(output_done(out, dout, stage_out, n, h->stream), "attention D2H");
     CUDA_TRY(cudaStreamSynchronize(h->stream), "attention");
     rc = check_device_waits(err);
     if (rc) return rc;
+    return set_err(err, KIVI_OK);
+}
+
+// One decode step on the caller's stream: append (dk/dv; none when null) and
+// attention, the main-region kernel beside the append on the side lane when
+// the geometry takes the tensor-core path; with `ex`, the merge exchanges the
+// partial states with every rank of a sequence-sharded cache.
+static int32_t decode_step(kivi_cache *h, const float *dk, const float *dv, const float *dq,
+                           uint64_t Hq, float scale, float *dout, void *stream,
+                           kivi_exchange *ex, kivi_error *err) {
+    KvState &s = h->s;
+    const bool append = dk != nullptr;
+    const bool tc = kivi::attention_tc_supported(s.g, (int)(Hq / s.H)) && (((uintptr_t)dq) & 7u) == 0;
+    // The main-region attention reads only groups packed before this step's
+    // append (which writes past them), so it runs on the side lane beside the
+    // append; the tail tiles and the merge follow the append.
+    const bool overlap = append && s.seq > 0 && h->side.s && !kivi::g_prof_on.load() && tc &&
+                         s.vq >= s.cfg.group_size;
+    DeviceGuard dg(s.device);
+    cudaStream_t st = pick(stream, h->stream);
+    int32_t rc;
+    if (!overlap && !ex) {
+        if (append) {
+            rc = kivi_cache_append_dev(h, dk, dv, 1, stream, err);
+            if (rc) return rc;
+        }
+        return kivi_cache_attention_dev(h, dq, Hq, scale, dout, stream, err);
+    }
+    int64_t vq_pre = -1;
+    if (overlap) {
+        // a capacity growth moves the store: do it before anything reads it
+        rc = ensure_capacity(s, std::max(s.kq, s.vq) + s.cfg.residual_length, st, err);
+        if (rc) return rc;
+        vq_pre = (int64_t)s.vq;
+        CUDA_TRY(cudaEventRecord(h->side.fork, st), "decode fork");
+        CUDA_TRY(cudaStreamWaitEvent(h->side.s, h->side.fork, 0), "decode fork");
+    }
+    if (append) {
+        rc = append_device(s, dk, dv, 1, st, err);
+        if (rc) return rc;
+    }
+    if (ex && s.seq == 0) { // an empty shard still publishes its (empty) state
+        kivi::ExchangeArgs x{};
+        for (uint32_t r = 0; r < ex->world; ++r) {
+            x.data[r] = static_cast<float *>(ex->peer[r]);
+            x.flags[r] =
+                reinterpret_cast<unsigned int *>(static_cast<char *>(ex->peer[r]) + ex->rec_bytes);
+        }
+        x.rank = (int)ex->rank;
+        x.world = (int)ex->world;
+        x.epoch = ++ex->epoch;
+        x.parity = (int)(x.epoch & 1u);
+        CUDA_TRY(kivi::launch_exchange_rows(nullptr, nullptr, 0, (int64_t)(s.B * Hq), x, dout, st),
+                 "attention exchange");
+    } else {
+        rc = run_attention(s, nullptr, 1, dq, Hq, scale, dout, nullptr, nullptr, h->part, st, err,
+                           nullptr, &h->side, vq_pre, ex);
+        if (rc) return rc;
+    }
+    CUDA_TRY(mark_dev(h->dev_done, st), "decode_dev");
     return set_err(err, KIVI_OK);
 }
 
@@ -1194,9 +1301,119 @@ int32_t kivi_cache_decode_dev(kivi_cache *h, const float *dk, const float *dv, c
     if (!h) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null cache");
     int32_t rc = check_query(h->s, Hq, 0, false, err);
     if (rc) return rc;
-    rc = kivi_cache_append_dev(h, dk, dv, 1, stream, err);
+    if (!dk || !dv) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null input");
+    return decode_step(h, dk, dv, dq, Hq, scale, dout, stream, nullptr, err);
+}
+
+// ---- peer-memory exchange (sequence sharding over the GPUs of one node)
+
+int32_t kivi_exchange_new(int32_t device, uint32_t rank, uint32_t world, uint64_t rows,
+                          uint64_t head_dim, kivi_exchange **out, kivi_error *err) {
+    if (!out) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null output handle");
+    *out = nullptr;
+    if (world < 1 || world > (uint32_t)kivi::kMaxExchangeRanks || rank >= world)
+        return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "rank %u of world %u (at most %d ranks)",
+                       rank, world, kivi::kMaxExchangeRanks);
+    if (head_dim != 128) return set_msg(err, KIVI_ERR_UNSUPPORTED, "exchange needs head_dim 128");
+    if (rows == 0) return set_err(err, KIVI_ERR_ZERO_DIMENSION, 0, 0, "rows");
+    DeviceGuard dg(device);
+    if (!dg.ok) return set_msg(err, KIVI_ERR_CUDA, "cannot select device %d", device);
+    install_wait_hint();
+    kivi_exchange *x = new kivi_exchange();
+    x->device = device;
+    x->rank = rank;
+    x->world = world;
+    x->rows = rows;
+    x->D = head_dim;
+    x->rec_bytes = (2 * (size_t)world * rows * (2 + head_dim) * sizeof(float) + 255) / 256 * 256;
+    x->bytes = x->rec_bytes + 2 * (size_t)world * rows * sizeof(unsigned int);
+    cudaError_t e = cudaMalloc(&x->base, x->bytes);
+    if (e == cudaSuccess) e = cudaMemset(x->base, 0, x->bytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        if (x->base) cudaFree(x->base);
+        delete x;
+        return cuda_fail(err, e, "exchange buffer");
+    }
+    x->peer[rank] = x->base;
+    *out = x;
+    return set_err(err, KIVI_OK);
+}
+
+int32_t kivi_exchange_ipc_handle(const kivi_exchange *x, void *handle, kivi_error *err) {
+    if (!x || !handle) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null argument");
+    DeviceGuard dg(x->device);
+    cudaIpcMemHandle_t h;
+    CUDA_TRY(cudaIpcGetMemHandle(&h, x->base), "exchange IPC handle");
+    std::memcpy(handle, &h, sizeof(h));
+    return set_err(err, KIVI_OK);
+}
+
+int32_t kivi_exchange_open(kivi_exchange *x, const void *handles, kivi_error *err) {
+    if (!x || !handles) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null argument");
+    if (x->opened) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "exchange already open");
+    DeviceGuard dg(x->device);
+    const unsigned char *hb = static_cast<const unsigned char *>(handles);
+    for (uint32_t r = 0; r < x->world; ++r) {
+        if (r == x->rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, hb + (size_t)r * sizeof(h), sizeof(h));
+        void *p = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (uint32_t q = 0; q < r; ++q)
+                if (q != x->rank && x->peer[q]) {
+                    cudaIpcCloseMemHandle(x->peer[q]);
+                    x->peer[q] = nullptr;
+                }
+            return cuda_fail(err, e, "exchange open peer buffer");
+        }
+        x->peer[r] = p;
+    }
+    x->opened = true;
+    return set_err(err, KIVI_OK);
+}
+
+void kivi_exchange_close(kivi_exchange *x) {
+    if (!x || !x->opened) return;
+    DeviceGuard dg(x->device);
+    cudaDeviceSynchronize();
+    for (uint32_t r = 0; r < x->world; ++r)
+        if (r != x->rank && x->peer[r]) {
+            cudaIpcCloseMemHandle(x->peer[r]);
+            x->peer[r] = nullptr;
+        }
+    x->opened = false;
+}
+
+void kivi_exchange_free(kivi_exchange *x) {
+    if (!x) return;
+    kivi_exchange_close(x);
+    DeviceGuard dg(x->device);
+    cudaDeviceSynchronize();
+    if (x->base) cudaFree(x->base);
+    delete x;
+}
+
+int32_t kivi_cache_decode_exchange_dev(kivi_cache *h, kivi_exchange *x, const float *dk,
+                                       const float *dv, const float *dq, uint64_t Hq, float scale,
+                                       float *dout, void *stream, kivi_error *err) {
+    if (!h || !x) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null handle");
+    int32_t rc = check_query(h->s, Hq, 0, false, err);
     if (rc) return rc;
-    return kivi_cache_attention_dev(h, dq, Hq, scale, dout, stream, err);
+    if (!dq || !dout) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "null buffer");
+    if ((dk == nullptr) != (dv == nullptr))
+        return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "key and value go together");
+    if (!x->opened && x->world > 1) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "exchange not open");
+    if (x->device != h->s.device) return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "exchange on another device");
+    if (x->rows != h->s.B * Hq || x->D != h->s.D)
+        return set_msg(err, KIVI_ERR_INVALID_ARGUMENT, "exchange sized for %llu rows, call has %llu",
+                       (unsigned long long)x->rows, (unsigned long long)(h->s.B * Hq));
+    if (h->s.seq > 0 &&
+        !(kivi::attention_tc_supported(h->s.g, (int)(Hq / h->s.H)) && (((uintptr_t)dq) & 7u) == 0))
+        return set_msg(err, KIVI_ERR_UNSUPPORTED,
+                       "the peer exchange takes the tensor-core geometry (head_dim 128, group 32)");
+    return decode_step(h, dk, dv, dq, Hq, scale, dout, stream, x, err);
 }
 
 int32_t kivi_cache_decode(kivi_cache *h, const float *key, uint64_t key_len, const float *value,
@@ -1243,8 +1460,10 @@ int32_t kivi_cache_decode(kivi_cache *h, const float *key, uint64_t key_len, con
     float *dout = output_target(out, stage_out, true);
     int32_t rc = append_device(h->s, dk, dv, 1, h->stream, err, qc);
     if (rc) return rc;
+    // host calls wait for their result, so the side-stream fork only adds
+    // event latency here: the launches run in order on the cache's stream.
     rc = run_attention(h->s, nullptr, 1, dq, Hq, scale, dout, nullptr, nullptr, h->part, h->stream,
-                       err, nullptr, &h->side);
+                       err, nullptr, nullptr);
     if (rc) return rc;
     CUDA_TRY(output_done(out, dout, stage_out, n, h->stream), "decode D2H");
     CUDA_TRY(cudaStreamSynchronize(h->stream), "decode");
@@ -1786,7 +2005,7 @@ int32_t kivi_session_append_dev(kivi_session *s, const float *dk, const float *d
 
 static int32_t sessions_attention_dev(const kivi_session *const *ss, uint64_t n, const float *dq,
                                       uint64_t Hq, float scale, float *dout, cudaStream_t st,
-                                      Scratch &part, kivi_error *err) {
+                                      Scratch &part, bool fork, kivi_error *err) {
     const kivi_prefix *p = ss[0]->prefix;
     for (uint64_t i = 0; i < n; ++i)
         if (!ss[i] || ss[i]->prefix != p)
@@ -1828,7 +2047,7 @@ static int32_t sessions_attention_dev(const kivi_session *const *ss, uint64_t n,
         bounds = mp->bounds;
     }
     return run_attention(p->s, views.data(), n, dq, Hq, scale, dout, nullptr, nullptr, part, st, err,
-                         bounds, &ss[0]->side);
+                         bounds, fork ? &ss[0]->side : nullptr);
 }
 
 int32_t kivi_session_attention_dev(const kivi_session *s, const float *dq, uint64_t Hq,
@@ -1837,7 +2056,7 @@ int32_t kivi_session_attention_dev(const kivi_session *s, const float *dq, uint6
     DeviceGuard dg(s->prefix->s.device);
     const kivi_session *arr[1] = {s};
     cudaStream_t st = pick(stream, s->stream);
-    int32_t rc = sessions_attention_dev(arr, 1, dq, Hq, scale, dout, st, s->part, err);
+    int32_t rc = sessions_attention_dev(arr, 1, dq, Hq, scale, dout, st, s->part, true, err);
     if (rc) return rc;
     CUDA_TRY(mark_dev(s->dev_done, st), "session attention_dev");
     s->dev_used.store(true);
@@ -1863,7 +2082,7 @@ int32_t kivi_session_attention(const kivi_session *s, const float *query, uint64
     CUDA_TRY(input_staged(query, dq, n, s->stream), "session H2D");
     float *dout = output_target(out, stage_out, p.seq > 0 || s->len > 0);
     const kivi_session *arr[1] = {s};
-    rc = sessions_attention_dev(arr, 1, dq, Hq, scale, dout, s->stream, ms->part, err);
+    rc = sessions_attention_dev(arr, 1, dq, Hq, scale, dout, s->stream, ms->part, false, err);
     if (rc) return rc;
     CUDA_TRY(output_done(out, dout, stage_out, n, s->stream), "session D2H");
     CUDA_TRY(cudaStreamSynchronize(s->stream), "session attention");
@@ -1879,7 +2098,7 @@ int32_t kivi_sessions_attention_batched_dev(const kivi_session *const *ss, uint6
     DeviceGuard dg(ss[0]->prefix->s.device);
     kivi_session *lead = const_cast<kivi_session *>(ss[0]);
     cudaStream_t st = pick(stream, lead->stream);
-    int32_t rc = sessions_attention_dev(ss, n, dq, Hq, scale, dout, st, lead->part, err);
+    int32_t rc = sessions_attention_dev(ss, n, dq, Hq, scale, dout, st, lead->part, true, err);
     if (rc) return rc;
     CUDA_TRY(mark_dev(lead->prefix->batch_done, st), "batched attention_dev");
     lead->prefix->batch_used.store(true);
@@ -1907,7 +2126,8 @@ int32_t kivi_sessions_attention_batched(const kivi_session *const *ss, uint64_t 
     bool any = p.seq > 0;
     for (uint64_t i = 0; i < n; ++i) any = any || ss[i]->len > 0;
     float *dout = output_target(out, stage_out, any);
-    rc = sessions_attention_dev(ss, n, dq, Hq, scale, dout, lead->stream, lead->part, err);
+    rc = sessions_attention_dev(ss, n, dq, Hq, scale, dout, lead->stream, lead->part, false,
+                                err);
     if (rc) return rc;
     CUDA_TRY(output_done(out, dout, stage_out, total, lead->stream), "batched D2H");
     CUDA_TRY(cudaStreamSynchronize(lead->stream), "batched attention");
@@ -1966,7 +2186,8 @@ int32_t kivi_sessions_decode_batched(kivi_session *const *ss, uint64_t nsess, co
     float *dout = output_target(out, stage_out, true);
     int32_t rc = sessions_append_launch(ss, nsess, dk, dv, 1, lead->stream, err, qc);
     if (rc) return rc;
-    rc = sessions_attention_dev(ss, nsess, dq, Hq, scale, dout, lead->stream, lead->part, err);
+    rc = sessions_attention_dev(ss, nsess, dq, Hq, scale, dout, lead->stream, lead->part,
+                                false, err);
     if (rc) return rc;
     CUDA_TRY(output_done(out, dout, stage_out, total, lead->stream), "sessions decode D2H");
     CUDA_TRY(cudaStreamSynchronize(lead->stream), "sessions decode");

@@ -153,6 +153,12 @@ def lib():
         "kivi_selftest_bounded_wait": ([sz, e], i32),
         "kivi_selftest_bounded_wait_dev": ([sz, P, e], i32),
         "kivi_device_wait_status": ([i32, e], i32),
+        "kivi_exchange_new": ([i32, C.c_uint32, C.c_uint32, sz, sz, C.POINTER(P), e], i32),
+        "kivi_exchange_ipc_handle": ([P, P, e], i32),
+        "kivi_exchange_open": ([P, P, e], i32),
+        "kivi_exchange_close": ([P], None),
+        "kivi_exchange_free": ([P], None),
+        "kivi_cache_decode_exchange_dev": ([P, P, P, P, P, sz, f32, P, P, e], i32),
         "kivi_session_reserve": ([P, sz, e], i32),
         "kivi_packed_partials_floats": ([sz, sz], sz),
         "kivi_cache_attention_partial_packed_dev": ([P, P, sz, f32, P, P, e], i32),
@@ -418,6 +424,16 @@ class KiviCache:
         _check(lib().kivi_cache_decode_dev(self._h, _ptr(d_key), _ptr(d_value), _ptr(d_query),
                                            num_q_heads, C.c_float(scale), _ptr(d_out),
                                            _stream(stream), C.byref(err)), err)
+
+    def decode_exchange_dev(self, exchange, d_key, d_value, d_query, num_q_heads, scale, d_out,
+                            stream=None):
+        """One decode step of a sequence-sharded cache over peer memory
+        (kivi_cache_decode_exchange_dev): the tail rank passes the step's
+        key/value rows, the others None; every rank gets the full output."""
+        err = _Err()
+        _check(lib().kivi_cache_decode_exchange_dev(
+            self._h, exchange._h, _ptr(d_key), _ptr(d_value), _ptr(d_query), num_q_heads,
+            C.c_float(scale), _ptr(d_out), _stream(stream), C.byref(err)), err)
 
     def attention_partial_dev(self, d_query, num_q_heads, scale, d_m, d_l, d_o, stream=None):
         err = _Err()
@@ -717,6 +733,45 @@ def merge_partials_dev(parts, rows, head_dim, d_m, d_l, d_o, d_out, stream=None)
     err = _Err()
     _check(lib().kivi_merge_partials_dev(parts, rows, head_dim, _ptr(d_m), _ptr(d_l), _ptr(d_o),
                                          _ptr(d_out), _stream(stream), C.byref(err)), err)
+
+
+class PeerExchange:
+    """Peer-memory exchange buffers of one rank of a sequence-sharded cache
+    (kivi_exchange_new): each rank creates one, the ranks swap their 64-byte
+    IPC handles, and open() maps every other rank's buffer.  Teardown:
+    close() on every rank, then (once all have closed) free()."""
+
+    HANDLE_BYTES = 64
+
+    def __init__(self, device, rank, world, rows, head_dim=128):
+        h = C.c_void_p()
+        err = _Err()
+        _check(lib().kivi_exchange_new(int(device), int(rank), int(world), int(rows),
+                                       int(head_dim), C.byref(h), C.byref(err)), err)
+        self._h = h.value
+        self.rank, self.world, self.rows = rank, world, rows
+
+    def ipc_handle(self):
+        buf = (C.c_ubyte * self.HANDLE_BYTES)()
+        err = _Err()
+        _check(lib().kivi_exchange_ipc_handle(self._h, buf, C.byref(err)), err)
+        return bytes(buf)
+
+    def open(self, handles):
+        """handles: the ranks' ipc_handle() bytes, concatenated in rank order."""
+        assert len(handles) == self.world * self.HANDLE_BYTES
+        buf = (C.c_ubyte * len(handles)).from_buffer_copy(handles)
+        err = _Err()
+        _check(lib().kivi_exchange_open(self._h, buf, C.byref(err)), err)
+
+    def close(self):
+        if self._h:
+            lib().kivi_exchange_close(self._h)
+
+    def free(self):
+        if self._h:
+            lib().kivi_exchange_free(self._h)
+            self._h = None
 
 
 def packed_partials_floats(rows, head_dim):

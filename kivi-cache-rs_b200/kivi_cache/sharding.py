@@ -14,10 +14,14 @@ token axis is split into contiguous ranges, one per rank (one process per GPU):
   only one that appends while decoding.
 
 Attention (cache.rs:224-279) becomes: each rank computes the partial softmax
-state (m, l, o) of its tokens for every query row, one all-gather exchanges the
-packed states (rows * (head_dim + 2) floats per rank), and every rank merges
-them in rank order with the same log-sum-exp merge, so all ranks hold the same,
-deterministic output.
+state (m, l, o) of its tokens for every query row, the ranks exchange those
+states (rows * (head_dim + 2) floats per rank), and every rank merges them in
+rank order with the same log-sum-exp merge, so all ranks hold the same,
+deterministic output.  The exchange runs either inside one kernel over NVLink
+peer memory (exchange="p2p": kivi_cache_decode_exchange_dev stores each
+rank's merged states straight into every peer's buffer, no collective call)
+or as an NCCL all-gather between two kernels (exchange="nccl"); both give the
+same bits.
 
 The host logic here (ranges, exchange) is device-agnostic and runs on gloo/CPU
 in the tests; the CUDA work goes through the C ABI of libkivi_gpu.so.
@@ -138,9 +142,9 @@ def wait_bounded(work, timeout_s, what, group=None, stream=None):
     while True:
         try:
             if work is None or work.is_completed():
-                if work is not None and not work.is_success():
-                    err = work.exception()
-                    break
+                if work is not None:
+                    work.wait()  # complete: raises the collective's error, if it failed
+                    work = None
                 if stream is None or stream.query():
                     return
         except Exception as e:
@@ -202,7 +206,7 @@ class SeqShardedCache:
     rank, the attention output over all shards."""
 
     def __init__(self, config, batch, num_kv_heads, head_dim, total_prefill_tokens, group=None,
-                 device=None, timeout_s=DEFAULT_TIMEOUT_S):
+                 device=None, timeout_s=DEFAULT_TIMEOUT_S, exchange="auto"):
         import torch
         import torch.distributed as dist
 
@@ -219,6 +223,12 @@ class SeqShardedCache:
         self._bufs = {}
         self.timeout_s = timeout_s  # host bound of each host-path step's exchange
         self._failed = None         # set once the communicator was aborted
+        if exchange == "auto":
+            exchange = "p2p" if self.world > 1 and dist.get_backend(group) == "nccl" else "nccl"
+        if exchange not in ("p2p", "nccl"):
+            raise ValueError(f"exchange must be 'p2p', 'nccl' or 'auto', not {exchange!r}")
+        self.exchange = exchange
+        self._peer = {}  # rows -> PeerExchange
 
     def _check_alive(self):
         if self._failed is not None:
@@ -279,10 +289,36 @@ class SeqShardedCache:
             raise
         merge_packed_partials_dev(self.world, rows, self.dim, gathered, d_out, stream=stream)
 
+    def _peer_exchange(self, rows):
+        """This rank's peer-memory exchange for `rows` query rows, set up
+        collectively on first use (every rank makes the same calls)."""
+        import torch
+        import torch.distributed as dist
+
+        from . import PeerExchange
+
+        ex = self._peer.get(rows)
+        if ex is None:
+            ex = PeerExchange(self.device, self.rank, self.world, rows, self.dim)
+            mine = torch.tensor(list(ex.ipc_handle()), dtype=torch.uint8,
+                                device=f"cuda:{self.device}")
+            every = torch.empty((self.world, mine.numel()), dtype=torch.uint8, device=mine.device)
+            exchange_partials(mine, every, self.group, timeout_s=self.timeout_s)
+            ex.open(bytes(every.cpu().numpy().reshape(-1)))
+            dist.barrier(group=self.group)  # every rank has mapped every buffer
+            self._peer[rows] = ex
+        return ex
+
     def decode_dev(self, d_key, d_value, d_query, num_q_heads, scale, d_out, stream,
                    timeout_s=None):
         """RuntimeKv::decode (runtime.rs:46-56) on the sharded cache."""
         self._check_alive()
+        if self.exchange == "p2p":
+            ex = self._peer_exchange(self.batch * num_q_heads)
+            self.cache.decode_exchange_dev(ex, d_key if self.plan.tail else None,
+                                           d_value if self.plan.tail else None, d_query,
+                                           num_q_heads, scale, d_out, stream=stream)
+            return
         if self.plan.tail:
             self.cache.append_dev(d_key, d_value, 1, stream=stream)
         self.attention_dev(d_query, num_q_heads, scale, d_out, stream, timeout_s=timeout_s)
@@ -292,13 +328,34 @@ class SeqShardedCache:
         until `stream` has run the steps queued on it; a step that does not
         finish in time (a peer that stopped taking part in the exchange) aborts
         the communicator and raises KiviError(Comm)."""
+        from . import KiviError, device_wait_status
+
         self._check_alive()
         try:
             wait_bounded(None, self.timeout_s if timeout_s is None else timeout_s,
                          "sharded decode step", self.group, stream=stream)
+            try:  # a peer exchange whose bounded wait gave up leaves a device flag
+                device_wait_status(self.device)
+            except KiviError as e:
+                abort_group(self.group)
+                raise comm_error(f"peer exchange gave up waiting for a rank: {e.message}") from e
         except Exception as e:
             self._failed = str(e)
             raise
+
+    def close(self):
+        """Releases the peer exchanges (collective: every rank calls it)."""
+        import torch.distributed as dist
+
+        if not self._peer:
+            return
+        for ex in self._peer.values():
+            ex.close()
+        if self._failed is None and dist.is_initialized():
+            dist.barrier(group=self.group)  # no rank still maps a buffer about to be freed
+        for ex in self._peer.values():
+            ex.free()
+        self._peer = {}
 
     def decode(self, keys, values, query, num_q_heads, scale, out=None, stream=None):
         """Host-buffer decode step (torch CPU tensors, pinned for async copies):

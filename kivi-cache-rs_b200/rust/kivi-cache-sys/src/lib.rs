@@ -169,6 +169,11 @@ pub struct kivi_session {
 pub struct kivi_guard {
     _private: [u8; 0],
 }
+/// Peer-memory exchange of one rank of a sequence-sharded cache, opaque.
+#[repr(C)]
+pub struct kivi_exchange {
+    _private: [u8; 0],
+}
 
 #[link(name = "kivi_gpu")]
 extern "C" {
@@ -199,6 +204,12 @@ extern "C" {
     pub fn kivi_packed_partials_floats(rows: u64, head_dim: u64) -> u64;
     pub fn kivi_cache_attention_partial_packed_dev(cache: *const kivi_cache, d_query: *const f32, num_q_heads: u64, scale: f32, d_packed: *mut f32, stream: *mut c_void, err: *mut kivi_error) -> i32;
     pub fn kivi_merge_packed_partials_dev(parts: u64, rows: u64, head_dim: u64, d_packed: *const f32, d_out: *mut f32, stream: *mut c_void, err: *mut kivi_error) -> i32;
+    pub fn kivi_exchange_new(device: i32, rank: u32, world: u32, rows: u64, head_dim: u64, out: *mut *mut kivi_exchange, err: *mut kivi_error) -> i32;
+    pub fn kivi_exchange_ipc_handle(exchange: *const kivi_exchange, handle: *mut c_void, err: *mut kivi_error) -> i32;
+    pub fn kivi_exchange_open(exchange: *mut kivi_exchange, handles: *const c_void, err: *mut kivi_error) -> i32;
+    pub fn kivi_exchange_close(exchange: *mut kivi_exchange);
+    pub fn kivi_exchange_free(exchange: *mut kivi_exchange);
+    pub fn kivi_cache_decode_exchange_dev(cache: *mut kivi_cache, exchange: *mut kivi_exchange, d_key: *const f32, d_value: *const f32, d_query: *const f32, num_q_heads: u64, scale: f32, d_out: *mut f32, stream: *mut c_void, err: *mut kivi_error) -> i32;
     pub fn kivi_cache_seal(cache: *mut kivi_cache, err: *mut kivi_error) -> i32;
     pub fn kivi_cache_dequantize(cache: *const kivi_cache, keys: *mut f32, values: *mut f32, len: u64, err: *mut kivi_error) -> i32;
     pub fn kivi_cache_memory(cache: *const kivi_cache, out: *mut kivi_memory_report) -> i32;
@@ -241,5 +252,4 @@ extern "C" {
     pub fn kivi_guard_cache(guard: *const kivi_guard) -> *const kivi_cache;
     pub fn kivi_guard_policy(guard: *const kivi_guard) -> i32;
     pub fn kivi_guard_sequence_length(guard: *const kivi_guard) -> u64;
-
 }
