@@ -333,6 +333,7 @@ class DevGen:
 
 PREFILL_MS = [0.0, 0]  # device time of the prefill appends, tokens appended (per process)
 EXCHANGE = ["auto"]   # config 4's cross-rank exchange (--exchange)
+TAIL_DISCOUNT = [0]   # config 4: tokens moved off the last rank (--tail-discount)
 
 
 def prefill(cache, gen, cfgd, n_tokens, stream):
@@ -580,7 +581,7 @@ class SeqShardWorkload:
         qgen = DevGen(999, chs)  # the same queries on every rank
         cfg = K.KiviConfig.try_new(cfgd["bits"], cfgd["G"], cfgd["R"])
         self.sc = SeqShardedCache(cfg, B, H, D, cfgd["ctx"], device=local_rank,
-                                  exchange=EXCHANGE[0])
+                                  exchange=EXCHANGE[0], tail_discount=TAIL_DISCOUNT[0])
         plan = self.sc.plan
         self.sc.reserve(plan.tokens + (nsteps + nprof + 64 + 2 * cfgd["R"] if plan.tail else 0))
         prefill(self.sc.cache, self.gen, cfgd, plan.tokens, stream)
@@ -735,7 +736,16 @@ def run_gpu(args, cfgd, rank, world, local_rank):
         if nl_.value:
             kernels[name] = {"launches": int(nl_.value), "total_ms": ms_.value,
                              "avg_ms": ms_.value / nl_.value}
+    rank_kernel_us = None
     if dist:
+        # every rank's own per-kernel averages (the ranks' shares differ under
+        # sequence sharding: the last one also appends and attends the tail)
+        kv = torch.tensor([kernels[n]["avg_ms"] if n in kernels else 0.0 for n in KERNELS],
+                          dtype=torch.float64, device="cuda")
+        allk = [torch.zeros_like(kv) for _ in range(world)]
+        dist.all_gather(allk, kv)
+        rank_kernel_us = [{n: round(float(x) * 1e3, 2) for n, x in zip(KERNELS, t.tolist()) if x > 0}
+                          for t in allk]
         dist.barrier()
     ms_all = sum(v["total_ms"] for v in kernels.values())
     kernel = max(kernels, key=lambda k: kernels[k]["total_ms"])
@@ -820,6 +830,7 @@ def run_gpu(args, cfgd, rank, world, local_rank):
     }
     if world > 1:
         result["rank_ms_per_step"] = rank_ms
+        result["rank_kernel_us"] = rank_kernel_us
     if PREFILL_MS[0] > 0:
         # bulk append (prefill) of this rank: stream-tokens/s and fp32 K+V input GB/s
         result["prefill"] = {
@@ -1104,6 +1115,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--exchange", default="auto", choices=["auto", "p2p", "nccl"],
                     help="config 4: peer-memory exchange kernel or NCCL all-gather")
+    ap.add_argument("--tail-discount", type=int, default=0,
+                    help="config 4: tokens moved off the last rank (it also appends)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -1112,6 +1125,7 @@ def main():
     local_rank = env_int("LOCAL_RANK", 0)
     cfgd = CONFIGS[args.config]
     EXCHANGE[0] = args.exchange
+    TAIL_DISCOUNT[0] = args.tail_discount
     if args.impl == "reference":
         res = run_reference(args, cfgd, rank, world)
     else:

@@ -38,9 +38,12 @@
 //     (Store::kbound / vbound); each is undone exactly on the fp32 side (the
 //     value factor rides in the softmax weights and the slot's m).  The codes
 //     must stay centred: with codes 0..levels as exact fp16 subnormals (one AND
-//     per register instead of LOP3 + HFMA2) the larger, cancelling sums lost
-//     an order of magnitude of accuracy on the B200 (3.7e-5 rel-L2 against
-//     fp64 at 32k tokens, against 0.9e-6 centred).
+//     per register instead of LOP3 + HFMA2) the attention output lost an
+//     order of magnitude of accuracy on the B200 (3.7e-5 rel-L2 against fp64
+//     at 32k tokens, against 0.9e-6 centred), and so it did with subnormal
+//     codes in the key tiles alone (3.65e-5; each code position's factor
+//     undone per token row on the fp32 side), although that form ran 5%
+//     faster.
 // The zero-point sums and the online softmax stay in fp32 on the CUDA cores.
 // The softmax reference point moves only when a logit exceeds it by more than
 // 2^11 (in exp2 units), which skips almost every rescale of the accumulators.

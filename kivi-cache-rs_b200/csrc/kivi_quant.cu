@@ -129,13 +129,19 @@ __device__ __forceinline__ bool pack32_fast(const float (&x)[32], const Quantize
 // are base + u * stride (BITS known at compile time): the 32 values held in
 // registers, packed by pack32_fast unless the group needs the exact path.
 // Same results as quant_key_channel.
-template <int BITS>
+template <int BITS, int STRIDE = 0>
 __device__ __forceinline__ float quant_key_channel_g32(const float *base, int stride, int d,
                                                        uint32_t *words, float2 *param) {
     constexpr float kLevels = (float)((1u << BITS) - 1u);
     float x[32];
+    if (STRIDE != 0) { // compile-time row pitch: 32 loads at immediate offsets
+        const float *p = base + d;
 #pragma unroll
-    for (int u = 0; u < 32; ++u) x[u] = base[(int64_t)u * stride + d];
+        for (int u = 0; u < 32; ++u) x[u] = p[u * STRIDE];
+    } else {
+#pragma unroll
+        for (int u = 0; u < 32; ++u) x[u] = base[(int64_t)u * stride + d];
+    }
     float mn = INFINITY, mx = -INFINITY;
 #pragma unroll
     for (int u = 0; u < 32; ++u) {
@@ -215,10 +221,15 @@ __device__ __forceinline__ float quant_value_g32(const float *grp, uint32_t *wor
 }
 
 // Per-token value quantization of channel group `cg` of one token row.
-// quant.rs:349-374.
+// quant.rs:349-374.  BITS != 0: the caller's cache has group 32 and BITS-bit
+// codes (the register path for 16-byte aligned rows); BITS == 0: any geometry.
+template <int BITS = 0>
 __device__ __forceinline__ float quant_value_group(const Geom &g, const float *row, int cg,
                                                    uint32_t *words, float2 *param) {
-    if (g.G == 32 && (reinterpret_cast<uintptr_t>(row) & 15u) == 0) {
+    if (BITS != 0) {
+        if ((reinterpret_cast<uintptr_t>(row) & 15u) == 0)
+            return quant_value_g32<(BITS ? BITS : 2)>(row + cg * 32, words, param);
+    } else if (g.G == 32 && (reinterpret_cast<uintptr_t>(row) & 15u) == 0) {
         if (g.bits == 2) return quant_value_g32<2>(row + cg * 32, words, param);
         if (g.bits == 4) return quant_value_g32<4>(row + cg * 32, words, param);
         if (g.bits == 8) return quant_value_g32<8>(row + cg * 32, words, param);
@@ -395,6 +406,9 @@ __global__ void __launch_bounds__(256) append_small_kernel(Geom g, Store st, con
 // quantized from registers by quant_key_channel_g32 (32 independent loads per
 // thread; 64 registers keep 8 CTAs per SM); other groups (rows from the
 // residual, other group sizes) go through the row table.
+// BITS != 0: group 32 with BITS-bit codes (one code width per instantiation
+// keeps the kernel's code small); BITS == 0: any geometry.
+template <int BITS>
 __global__ void __launch_bounds__(128, 8) key_groups_kernel(Geom g, Store st, const float *res,
                                                             int nres, const float *in,
                                                             int64_t in_seq, int64_t out_group0) {
@@ -413,7 +427,10 @@ __global__ void __launch_bounds__(128, 8) key_groups_kernel(Geom g, Store st, co
             uint32_t *words = kc + (og * D + d) * g.ipc;
             float2 *param = kp + og * D + d;
             float sc;
-            if (g.bits == 2) sc = quant_key_channel_g32<2>(base, D, d, words, param);
+            if (BITS != 0 && D == 128)
+                sc = quant_key_channel_g32<(BITS ? BITS : 2), 128>(base, D, d, words, param);
+            else if (BITS != 0) sc = quant_key_channel_g32<(BITS ? BITS : 2)>(base, D, d, words, param);
+            else if (g.bits == 2) sc = quant_key_channel_g32<2>(base, D, d, words, param);
             else if (g.bits == 4) sc = quant_key_channel_g32<4>(base, D, d, words, param);
             else sc = quant_key_channel_g32<8>(base, D, d, words, param);
             kmax = fmaxf(kmax, fabsf(sc));
@@ -436,6 +453,7 @@ __global__ void __launch_bounds__(128, 8) key_groups_kernel(Geom g, Store st, co
 
 // ---------------------------------------------------------------- bulk values
 // grid (ceil(ntok*nch/128), n): one thread per (token, channel group).
+template <int BITS>
 __global__ void __launch_bounds__(128) value_tokens_kernel(Geom g, Store st, int nwin, int vhead,
                                                            const float *in, int64_t in_seq,
                                                            int64_t in_off, int64_t ntok,
@@ -451,7 +469,7 @@ __global__ void __launch_bounds__(128) value_tokens_kernel(Geom g, Store st, int
         const int64_t t = out_tok0 + j;
         uint32_t *vc = st.vcodes + (int64_t)s * code_stride(g, st.cap);
         float2 *vp = st.vparams + (int64_t)s * vparam_stride(g, st.cap);
-        sc = quant_value_group(g, row, cg, vc + (t * g.nch + cg) * g.ipc, vp + t * g.nch + cg);
+        sc = quant_value_group<BITS>(g, row, cg, vc + (t * g.nch + cg) * g.ipc, vp + t * g.nch + cg);
     }
     raise_bound(st.vbound, s, sc);
 }
@@ -580,8 +598,15 @@ cudaError_t launch_key_groups(const Geom &g, const Store &st, int n, const float
                               int64_t out_group0, cudaStream_t s) {
     if (n <= 0 || ngroups <= 0) return cudaSuccess;
     ProfScope prof("key_groups", s);
-    key_groups_kernel<<<dim3((unsigned)ngroups, n), 128, 0, s>>>(g, st, res, nres, in, in_seq,
-                                                                   out_group0);
+    const dim3 grid((unsigned)ngroups, n);
+    if (g.G == 32 && g.bits == 2)
+        key_groups_kernel<2><<<grid, 128, 0, s>>>(g, st, res, nres, in, in_seq, out_group0);
+    else if (g.G == 32 && g.bits == 4)
+        key_groups_kernel<4><<<grid, 128, 0, s>>>(g, st, res, nres, in, in_seq, out_group0);
+    else if (g.G == 32 && g.bits == 8)
+        key_groups_kernel<8><<<grid, 128, 0, s>>>(g, st, res, nres, in, in_seq, out_group0);
+    else
+        key_groups_kernel<0><<<grid, 128, 0, s>>>(g, st, res, nres, in, in_seq, out_group0);
     count_launch();
     return cudaGetLastError();
 }
@@ -591,8 +616,19 @@ cudaError_t launch_value_tokens(const Geom &g, const Store &st, int n, int nwin,
                                 int64_t out_tok0, cudaStream_t s) {
     if (n <= 0 || ntok <= 0) return cudaSuccess;
     ProfScope prof("value_tokens", s);
-    value_tokens_kernel<<<dim3(blocks_for(ntok * g.nch, 128), n), 128, 0, s>>>(
-        g, st, nwin, vhead, in, in_seq, in_off, ntok, out_tok0);
+    const dim3 grid(blocks_for(ntok * g.nch, 128), n);
+    if (g.G == 32 && g.bits == 2)
+        value_tokens_kernel<2><<<grid, 128, 0, s>>>(g, st, nwin, vhead, in, in_seq, in_off, ntok,
+                                                    out_tok0);
+    else if (g.G == 32 && g.bits == 4)
+        value_tokens_kernel<4><<<grid, 128, 0, s>>>(g, st, nwin, vhead, in, in_seq, in_off, ntok,
+                                                    out_tok0);
+    else if (g.G == 32 && g.bits == 8)
+        value_tokens_kernel<8><<<grid, 128, 0, s>>>(g, st, nwin, vhead, in, in_seq, in_off, ntok,
+                                                    out_tok0);
+    else
+        value_tokens_kernel<0><<<grid, 128, 0, s>>>(g, st, nwin, vhead, in, in_seq, in_off, ntok,
+                                                    out_tok0);
     count_launch();
     return cudaGetLastError();
 }

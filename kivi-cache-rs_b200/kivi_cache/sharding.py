@@ -64,18 +64,33 @@ class ShardPlan:
         return self.end - self.start
 
 
-def shard_plan(total_tokens: int, world: int, rank: int, residual_length: int) -> ShardPlan:
+def shard_plan(total_tokens: int, world: int, rank: int, residual_length: int,
+               tail_discount: int = 0) -> ShardPlan:
     """R-aligned contiguous ranges: ranks 0..world-2 get `per` tokens each,
     per = floor(total / (world * R)) * R, and the last rank the rest (at least
     `per`, so at least R once total >= world * R).  When total < world * R
-    every token stays on the last rank and the others hold empty shards."""
+    every token stays on the last rank and the others hold empty shards.
+
+    tail_discount > 0 leaves the last rank (which also owns the key residual,
+    the value window and every append, so its step is longer) about that many
+    tokens fewer than each other rank: per = floor((total + tail_discount) /
+    (world * R)) * R, lowered while the last rank would keep fewer than R
+    tokens, and never below the undiscounted per."""
     if world < 1 or not 0 <= rank < world:
         raise ValueError(f"bad rank {rank} of world {world}")
     if residual_length < 1:
         raise ValueError("residual_length must be positive")
     if total_tokens < 0:
         raise ValueError("total_tokens must be non-negative")
-    per = (total_tokens // (world * residual_length)) * residual_length
+    if tail_discount < 0:
+        raise ValueError("tail_discount must be non-negative")
+    R = residual_length
+    per = (total_tokens // (world * R)) * R
+    if tail_discount > 0 and world > 1:
+        moved = ((total_tokens + tail_discount) // (world * R)) * R
+        while moved > per and total_tokens - (world - 1) * moved < R:
+            moved -= R
+        per = max(per, moved)
     start = rank * per
     end = total_tokens if rank == world - 1 else start + per
     return ShardPlan(rank, world, start, end, rank == world - 1)
@@ -206,7 +221,7 @@ class SeqShardedCache:
     rank, the attention output over all shards."""
 
     def __init__(self, config, batch, num_kv_heads, head_dim, total_prefill_tokens, group=None,
-                 device=None, timeout_s=DEFAULT_TIMEOUT_S, exchange="auto"):
+                 device=None, timeout_s=DEFAULT_TIMEOUT_S, exchange="auto", tail_discount=0):
         import torch
         import torch.distributed as dist
 
@@ -216,7 +231,7 @@ class SeqShardedCache:
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.plan = shard_plan(total_prefill_tokens, self.world, self.rank,
-                               config.residual_length)
+                               config.residual_length, tail_discount)
         self.device = torch.cuda.current_device() if device is None else device
         self.batch, self.heads, self.dim = batch, num_kv_heads, head_dim
         self.cache = KiviCache(config, batch, num_kv_heads, head_dim, device=self.device)

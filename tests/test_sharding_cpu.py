@@ -50,6 +50,32 @@ def test_shard_plan_covers_the_sequence(total, world):
         assert all(p.tokens == 0 for p in plans[:-1])
 
 
+@pytest.mark.parametrize("total,world,disc", [(1_048_575, 8, 16384), (1_048_575, 2, 40000),
+                                              (1024, 4, 4096), (300, 4, 1000), (5000, 1, 640)])
+def test_shard_plan_tail_discount(total, world, disc):
+    """The discount moves R-aligned tokens from the last rank onto the others,
+    leaving it about `disc` tokens fewer than each other rank; the ranges still
+    tile the sequence and the last rank keeps >= R tokens whenever the
+    undiscounted plan gave it that many."""
+    plans = [shard_plan(total, world, r, R, disc) for r in range(world)]
+    base = [shard_plan(total, world, r, R) for r in range(world)]
+    assert plans[0].start == 0 and plans[-1].end == total
+    for a, b in zip(plans, plans[1:]):
+        assert a.end == b.start
+    for p, q in zip(plans[:-1], base[:-1]):
+        assert p.tokens % R == 0 and p.tokens >= q.tokens and p.tokens == plans[0].tokens
+    assert plans[-1].tokens <= base[-1].tokens
+    if base[-1].tokens >= R:
+        assert plans[-1].tokens >= R
+    if world > 1:
+        gap = plans[0].tokens - plans[-1].tokens
+        assert gap <= disc
+        # short of the discount only where one more R per rank would leave the
+        # last rank fewer than R tokens
+        capped = total - (world - 1) * (plans[0].tokens + R) < R
+        assert gap >= disc - world * R or capped
+
+
 def test_shard_plan_rejects_bad_arguments():
     with pytest.raises(ValueError):
         shard_plan(10, 2, 2, R)
@@ -59,6 +85,8 @@ def test_shard_plan_rejects_bad_arguments():
         shard_plan(-1, 2, 0, R)
     with pytest.raises(ValueError):
         shard_plan(10, 2, 0, 0)
+    with pytest.raises(ValueError):
+        shard_plan(10, 2, 0, R, -1)
 
 
 # ---------------------------------------------------------------- gloo, world 2
