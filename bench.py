@@ -67,6 +67,11 @@ CONFIGS = {
     # accepts 2, 4 and 8 bits, config.rs:31-55)
     5: dict(_BASE, name="cfg1shape-8bit-b16-h8-hq32-d128-g32-r128-ctx32768", mode="decode", B=16,
             Hq=32, bits=8, ctx=32768),
+    # not a BASELINE config: config 1's shape with 64-token / 64-channel groups
+    # (the reference accepts any group with group * bits % 32 == 0): the
+    # generic CUDA-core kernel's path
+    6: dict(_BASE, name="cfg1shape-g64-b16-h8-hq32-d128-2bit-r128-ctx32768", mode="decode", B=16,
+            Hq=32, bits=2, G=64, ctx=32768),
 }
 
 KERNELS = ("attn_tc", "attn_sets_tc", "attn_tail", "attn_chunk", "merge", "merge_shards",
@@ -1032,6 +1037,11 @@ def noalloc_microbench(K, wl, stream, reps=16):
         if rc:
             raise K.KiviError(err.code, err.a, err.b, None, err.message.decode())
 
+    try:
+        noalloc()
+        stream.synchronize()
+    except K.KiviError as e:  # e.g. the generic kernel's scratch exceeds the fixed array
+        return {"unsupported": str(e)}
     times = {"attention_dev": [], "noalloc_dev": []}
     for _ in range(reps + 2):
         for name, fn in (("attention_dev", lambda: cache.attention_dev(q, hq, scale, out_a,

@@ -30,7 +30,10 @@ namespace kivi {
 namespace {
 
 constexpr int kTile = 32;   // tokens staged per step
-constexpr int kThreads = 256;
+#ifndef KIVI_CHUNK_THREADS
+#define KIVI_CHUNK_THREADS 128
+#endif
+constexpr int kThreads = KIVI_CHUNK_THREADS;
 constexpr int kWarps = kThreads / 32;
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -45,46 +48,90 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
-__device__ __forceinline__ float key_elem(const AttnArgs &a, int s, int64_t t, int d,
-                                          const SuffixRef *suf) {
-    const Geom &g = a.g;
-    if (t < a.kq) {
-        const uint32_t *kc = a.st.kcodes + (int64_t)s * code_stride(g, a.st.cap);
-        const float2 *kp = a.st.kparams + (int64_t)s * kparam_stride(g, a.st.cap);
-        const int64_t grp = t / g.G;
-        const int u = (int)(t - grp * g.G);
-        const uint32_t w = __ldg(kc + (grp * g.D + d) * g.ipc + u / g.tpw);
-        const uint32_t code = (w >> ((u % g.tpw) * g.bits)) & g.mask;
-        const float2 p = __ldg(kp + grp * g.D + d);
-        return __fmaf_rn((float)code, p.x, p.y);
-    }
-    if (t < a.seq_p) return a.st.kres[((int64_t)s * g.R + (t - a.kq)) * g.D + d];
-    return suf->k[((int64_t)s * suf->cap + (t - a.seq_p)) * g.D + d];
+// Exact float of a code (< 2^23): the code in the mantissa of 2^23, minus 2^23.
+__device__ __forceinline__ float code_float(uint32_t code) {
+    return __uint_as_float(0x4B000000u | code) - 8388608.0f;
 }
 
-__device__ __forceinline__ float value_elem(const AttnArgs &a, int s, int64_t t, int d,
-                                            const SuffixRef *suf) {
+// Stages the K and V rows of tokens [t0, t0 + nt) of stream s into Ks / Vs
+// ([kTile][DP] fp32, row pitch DP = D + 4).  Packed tokens are decoded one code
+// word per thread (fma(code, scale, zero), quant.rs:404-406): a key word holds
+// tpw tokens of one channel (tiles start on word boundaries: chunk and tail-tile
+// starts are multiples of 32, and the packed key region ends on a group
+// boundary), a value word tpw channels of one token.  fp32 rows (key residual,
+// value window, session suffix) are copied as float4.
+__device__ __forceinline__ void stage_tile(const AttnArgs &a, int s, int64_t t0, int nt,
+                                           const SuffixRef *suf, float *Ks, float *Vs, int DP) {
     const Geom &g = a.g;
-    if (t < a.vq) {
-        const uint32_t *vc = a.st.vcodes + (int64_t)s * code_stride(g, a.st.cap);
-        const float2 *vp = a.st.vparams + (int64_t)s * vparam_stride(g, a.st.cap);
-        const int cg = d / g.G, lc = d - cg * g.G;
-        const uint32_t w = __ldg(vc + (t * g.nch + cg) * g.ipc + lc / g.tpw);
-        const uint32_t code = (w >> ((lc % g.tpw) * g.bits)) & g.mask;
-        const float2 p = __ldg(vp + t * g.nch + cg);
-        return __fmaf_rn((float)code, p.x, p.y);
+    const int D = g.D, tpw = g.tpw, D4 = D >> 2;
+    // ---- keys
+    const uint32_t *kc = a.st.kcodes + (int64_t)s * code_stride(g, a.st.cap);
+    const float2 *kp = a.st.kparams + (int64_t)s * kparam_stride(g, a.st.cap);
+    const int kpk = (int)max((int64_t)0, min((int64_t)nt, a.kq - t0)); // packed key tokens
+    const int kw = (kpk + tpw - 1) / tpw;                               // their words per channel
+    for (int j = 0; j < kw; ++j) {
+        const int64_t tw = t0 + (int64_t)j * tpw;
+        const int64_t grp = tw / g.G;
+        const int i = (int)(tw - grp * g.G) / tpw;
+        const int tb = j * tpw, tn = min(tpw, kpk - tb);
+        for (int d = threadIdx.x; d < D; d += kThreads) {
+            const uint32_t w = __ldg(kc + (grp * D + d) * g.ipc + i);
+            const float2 p = __ldg(kp + grp * D + d);
+            for (int u = 0; u < tn; ++u)
+                Ks[(tb + u) * DP + d] =
+                    __fmaf_rn(code_float((w >> (u * g.bits)) & g.mask), p.x, p.y);
+        }
     }
-    if (t < a.seq_p)
-        return a.st.vres[((int64_t)s * g.R + (a.vhead + (t - a.vq)) % g.R) * g.D + d];
-    return suf->v[((int64_t)s * suf->cap + (t - a.seq_p)) * g.D + d];
+    for (int e = threadIdx.x; e < (nt - kpk) * D4; e += kThreads) {
+        const int tt = kpk + e / D4, d = (e % D4) * 4;
+        const int64_t t = t0 + tt;
+        const float *src = t < a.seq_p ? a.st.kres + ((int64_t)s * g.R + (t - a.kq)) * D
+                                       : suf->k + ((int64_t)s * suf->cap + (t - a.seq_p)) * D;
+        *reinterpret_cast<float4 *>(Ks + tt * DP + d) = *reinterpret_cast<const float4 *>(src + d);
+    }
+    // ---- values: lanes take consecutive tokens of one code word position
+    const uint32_t *vc = a.st.vcodes + (int64_t)s * code_stride(g, a.st.cap);
+    const float2 *vp = a.st.vparams + (int64_t)s * vparam_stride(g, a.st.cap);
+    const int vpk = (int)max((int64_t)0, min((int64_t)nt, a.vq - t0)); // packed value tokens
+    const int vwords = D / tpw;                                         // code words per token
+    for (int e = threadIdx.x; e < vwords * kTile; e += kThreads) {
+        const int tt = e & (kTile - 1), wi = e / kTile;
+        if (tt >= vpk) continue;
+        const int64_t t = t0 + tt;
+        const int c0 = wi * tpw, cg = c0 / g.G, i = (c0 - cg * g.G) / tpw;
+        const uint32_t w = __ldg(vc + (t * g.nch + cg) * g.ipc + i);
+        const float2 p = __ldg(vp + t * g.nch + cg);
+        float *dst = Vs + tt * DP + c0;
+        for (int u = 0; u < tpw; u += 4) {
+            float4 v;
+            v.x = __fmaf_rn(code_float((w >> (u * g.bits)) & g.mask), p.x, p.y);
+            v.y = __fmaf_rn(code_float((w >> ((u + 1) * g.bits)) & g.mask), p.x, p.y);
+            v.z = __fmaf_rn(code_float((w >> ((u + 2) * g.bits)) & g.mask), p.x, p.y);
+            v.w = __fmaf_rn(code_float((w >> ((u + 3) * g.bits)) & g.mask), p.x, p.y);
+            *reinterpret_cast<float4 *>(dst + u) = v;
+        }
+    }
+    for (int e = threadIdx.x; e < (nt - vpk) * D4; e += kThreads) {
+        const int tt = vpk + e / D4, d = (e % D4) * 4;
+        const int64_t t = t0 + tt;
+        const float *src =
+            t < a.seq_p ? a.st.vres + ((int64_t)s * g.R + (a.vhead + (t - a.vq)) % g.R) * D
+                        : suf->v + ((int64_t)s * suf->cap + (t - a.seq_p)) * D;
+        *reinterpret_cast<float4 *>(Vs + tt * DP + d) = *reinterpret_cast<const float4 *>(src + d);
+    }
 }
 
 // grid: (NC + 1 + S, B*H).  blockIdx.x < NC: main chunk; == NC: prefix tail;
 // > NC: suffix of session blockIdx.x - NC - 1.
+// Per 32-token tile: the K and V rows are staged in fp32 (stage_tile); each
+// warp takes query rows (lane = token) and forms the logit with one fma per
+// channel in channel order (attention.rs:168-169, 296: bit-identical logits),
+// then the online softmax of the row over the tile; finally every thread
+// accumulates (row, 4-channel) outputs over the tile's tokens.
 __global__ void __launch_bounds__(kThreads) attn_chunk_kernel(const AttnArgs a) {
-    extern __shared__ float sm[];
+    extern __shared__ __align__(16) float sm[];
     const Geom &g = a.g;
-    const int D = g.D, DP = D + 1;
+    const int D = g.D, DP = D + 4, D4 = D >> 2;
     const int c = blockIdx.x + a.c0;
     const int s = blockIdx.y; // stream = b * H + kvh
     const int b = s / a.H, kvh = s - b * a.H;
@@ -125,11 +172,13 @@ __global__ void __launch_bounds__(kThreads) attn_chunk_kernel(const AttnArgs a) 
     float *Vs = Ks + kTile * DP;     // [kTile][DP]
     float *Qs = Vs + kTile * DP;     // [nrows][D]
     float *Os = Qs + nrows * D;      // [nrows][D]
-    float *Ms = Os + nrows * D;      // [nrows]
+    float *Ps = Os + nrows * D;      // [nrows][kTile] softmax weights of a tile
+    float *Ms = Ps + nrows * kTile;  // [nrows]
     float *Ls = Ms + nrows;          // [nrows]
-    float *Ps = Ls + nrows;          // [kWarps][kTile] softmax weights of a tile
+    float *As = Ls + nrows;          // [nrows] rescale of the row's output this tile
 
-    // Query row r <-> (session sess0 + r / Gq, q head kvh * Gq + r % Gq).
+    // Query row r <-> (session sess0 + r / Gq, q head kvh * Gq + r % Gq); the
+    // caller's query may be only 4-byte aligned: scalar loads.
     for (int e = threadIdx.x; e < nrows * D; e += kThreads) {
         const int r = e / D, d = e - r * D;
         const int sess = a.session_base + sess0 + r / a.Gq;
@@ -145,45 +194,59 @@ __global__ void __launch_bounds__(kThreads) attn_chunk_kernel(const AttnArgs a) 
     for (int64_t t0 = lo; t0 < hi; t0 += kTile) {
         const int nt = (int)min((int64_t)kTile, hi - t0);
         __syncthreads();
-        for (int e = threadIdx.x; e < nt * D; e += kThreads) {
-            const int tt = e / D, d = e - tt * D;
-            Ks[tt * DP + d] = key_elem(a, s, t0 + tt, d, suf);
-            Vs[tt * DP + d] = value_elem(a, s, t0 + tt, d, suf);
-        }
+        stage_tile(a, s, t0, nt, suf, Ks, Vs, DP);
         __syncthreads();
         for (int r = warp; r < nrows; r += kWarps) {
-            const float *q = Qs + r * D;
             float x = -INFINITY;
             if (lane < nt) {
-                const float *kr = Ks + lane * DP;
+                const float4 *k4 = reinterpret_cast<const float4 *>(Ks + lane * DP);
+                const float4 *q4 = reinterpret_cast<const float4 *>(Qs + r * D);
                 float dot = 0.0f;
-                for (int d = 0; d < D; ++d) dot = __fmaf_rn(kr[d], q[d], dot);
+                for (int i = 0; i < D4; ++i) {
+                    const float4 kk = k4[i], qq = q4[i];
+                    dot = __fmaf_rn(kk.x, qq.x, dot);
+                    dot = __fmaf_rn(kk.y, qq.y, dot);
+                    dot = __fmaf_rn(kk.z, qq.z, dot);
+                    dot = __fmaf_rn(kk.w, qq.w, dot);
+                }
                 x = dot * a.scale;
             }
             const float m_old = Ms[r];
             const float m_new = fmaxf(m_old, warp_max(x));
-            if (m_new == -INFINITY) continue; // nothing finite seen yet
-            const float alpha = (m_old == -INFINITY) ? 0.0f : expf(m_old - m_new);
-            const float p = (lane < nt) ? expf(x - m_new) : 0.0f;
+            float alpha = 1.0f, p = 0.0f;
+            if (m_new != -INFINITY) { // else nothing finite seen yet: no update
+                alpha = (m_old == -INFINITY) ? 0.0f : expf(m_old - m_new);
+                p = (lane < nt) ? expf(x - m_new) : 0.0f;
+            }
             const float psum = warp_sum(p);
-            float *pw = Ps + warp * kTile;
-            pw[lane] = p;
-            __syncwarp();
-            float *o = Os + r * D;
-            for (int d = lane; d < D; d += 32) {
-                float acc = o[d] * alpha;
-                for (int tt = 0; tt < nt; ++tt) {
-                    const float pt = pw[tt];
-                    if (pt != 0.0f) acc = __fmaf_rn(pt, Vs[tt * DP + d], acc);
-                }
-                o[d] = acc;
-            }
-            __syncwarp();
+            Ps[r * kTile + lane] = p;
             if (lane == 0) {
-                Ms[r] = m_new;
-                Ls[r] = Ls[r] * alpha + psum;
+                if (m_new != -INFINITY) {
+                    Ms[r] = m_new;
+                    Ls[r] = Ls[r] * alpha + psum;
+                }
+                As[r] = alpha;
             }
-            __syncwarp();
+        }
+        __syncthreads();
+        for (int e = threadIdx.x; e < nrows * D4; e += kThreads) {
+            const int r = e / D4, d = (e - r * D4) * 4;
+            float4 o = *reinterpret_cast<const float4 *>(Os + r * D + d);
+            const float al = As[r];
+            o.x *= al;
+            o.y *= al;
+            o.z *= al;
+            o.w *= al;
+            const float *pr = Ps + r * kTile;
+            for (int tt = 0; tt < nt; ++tt) {
+                const float pt = pr[tt];
+                const float4 v = *reinterpret_cast<const float4 *>(Vs + tt * DP + d);
+                o.x = __fmaf_rn(pt, v.x, o.x);
+                o.y = __fmaf_rn(pt, v.y, o.y);
+                o.z = __fmaf_rn(pt, v.z, o.z);
+                o.w = __fmaf_rn(pt, v.w, o.w);
+            }
+            *reinterpret_cast<float4 *>(Os + r * D + d) = o;
         }
     }
     __syncthreads();
@@ -273,15 +336,14 @@ __global__ void merge_shards_kernel(const float *m, const float *l, const float 
 } // namespace
 
 size_t attention_smem_bytes(int D, int rows) {
-    return sizeof(float) * ((size_t)2 * kTile * (D + 1) + (size_t)2 * rows * D + 2 * (size_t)rows +
-                            (size_t)kWarps * kTile);
+    return sizeof(float) * ((size_t)2 * kTile * (D + 4) + (size_t)rows * (2 * D + kTile + 3));
 }
 
 int attention_max_rows(int D) {
     const size_t budget = 200 * 1024;
-    const size_t fixed = sizeof(float) * ((size_t)2 * kTile * (D + 1) + (size_t)kWarps * kTile);
+    const size_t fixed = sizeof(float) * (size_t)2 * kTile * (D + 4);
     if (fixed >= budget) return 0;
-    return (int)((budget - fixed) / (sizeof(float) * (2 * (size_t)D + 2)));
+    return (int)((budget - fixed) / (sizeof(float) * (2 * (size_t)D + kTile + 3)));
 }
 
 cudaError_t launch_attention_chunks(const AttnArgs &a, cudaStream_t s) {

@@ -336,7 +336,11 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : KIVI_TC_
     float *Lw = Mw + kConsumers * kHeads;                                // [warp][kHeads]
     unsigned int *bnd = reinterpret_cast<unsigned int *>(Lw + kConsumers * kHeads); // [2]
 
-    const int64_t rbase = (int64_t)blockIdx.z * a.rows_per_set; // this query set's first row
+    // blockIdx.z = query set * hsets + head set: rows of heads head0 .. head0 +
+    // nh of every kv head of the set
+    const int zq = (int)blockIdx.z / a.hsets, head0 = ((int)blockIdx.z - zq * a.hsets) * a.GQ;
+    const int nh = min(a.GQ, a.gq_stride - head0);
+    const int64_t rbase = (int64_t)zq * a.rows_per_set + head0; // + b*Hq + kvh*gq_stride + h
     const int64_t W = (int64_t)a.nstreams * a.main_groups;
     const int64_t gb = (int64_t)blockIdx.x * a.per;
     const int64_t ge = min(W, gb + a.per);
@@ -412,8 +416,8 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : KIVI_TC_
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
             const int h = nt * 4 + hb;
-            const bool okh = h < a.GQ;
-            const float *qrow = a.q + (rbase + (int64_t)b * a.Hq + kvh * a.GQ + (okh ? h : 0)) * kD;
+            const bool okh = h < nh;
+            const float *qrow = a.q + (rbase + (int64_t)b * a.Hq + kvh * a.gq_stride + (okh ? h : 0)) * kD;
             float qm = 0.0f;
 #pragma unroll
             for (int kt = 0; kt < 8; ++kt) {
@@ -642,7 +646,7 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : KIVI_TC_
         const int64_t first_cta = (s * a.main_groups) / a.per;
         const int slot = (int)(blockIdx.x - first_cta);
         const bool last = seg_end == (s + 1) * a.main_groups; // this CTA ends stream s
-        for (int e = threadIdx.x; e < a.GQ * kD; e += kTcThreads) {
+        for (int e = threadIdx.x; e < nh * kD; e += kTcThreads) {
             const int h = e / kD, d = e - h * kD;
             float M = -INFINITY;
 #pragma unroll
@@ -658,7 +662,7 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : KIVI_TC_
                     L = fmaf(lw, fw, L);
                 }
             }
-            const int64_t row = rbase + (int64_t)b * a.Hq + kvh * a.GQ + h;
+            const int64_t row = rbase + (int64_t)b * a.Hq + kvh * a.gq_stride + h;
             float *po = a.part_o + row * a.parts * kD;
             float *pml = a.part_ml + row * a.parts * 2;
             po[slot * kD + d] = O;
@@ -725,7 +729,7 @@ cudaError_t launch_tc(const TcArgs &a, int nsets, cudaStream_t s) {
     const int64_t W = (int64_t)a.nstreams * a.main_groups;
     const int nctas = (int)((W + a.per - 1) / a.per);
     ProfScope prof("attn_tc", s);
-    const dim3 grid((unsigned)nctas, 1u, (unsigned)nsets);
+    const dim3 grid((unsigned)nctas, 1u, (unsigned)(nsets * a.hsets));
     attn_tc_kernel<BITS, NT><<<grid, kTcThreads, tc_smem<BITS, NT>(), s>>>(a);
     count_launch();
     return cudaGetLastError();
@@ -735,7 +739,7 @@ cudaError_t launch_tc(const TcArgs &a, int nsets, cudaStream_t s) {
 
 bool attention_tc_supported(const Geom &g, int gq) {
     return g.D == kD && g.G == kG && (g.bits == 2 || g.bits == 4 || g.bits == 8) && gq >= 1 &&
-           gq <= 8;
+           tc_head_sets(gq) <= kMaxTcHeadSets;
 }
 
 cudaError_t plan_attention_tc(int bits, int gq, int64_t nstreams, int64_t main_groups,
@@ -770,7 +774,8 @@ cudaError_t plan_attention_tc(int bits, int gq, int64_t nstreams, int64_t main_g
 
 cudaError_t launch_attention_tc(const TcArgs &a, int bits, int nsets, cudaStream_t s) {
     if (a.main_groups <= 0 || a.nstreams <= 0 || nsets <= 0 || a.per <= 0) return cudaSuccess;
-    if (nsets > 65535) return cudaErrorInvalidValue;
+    if (a.hsets < 1 || a.hsets > kMaxTcHeadSets || (int64_t)nsets * a.hsets > 65535)
+        return cudaErrorInvalidValue;
     const bool two = a.GQ > 4;
     if (bits == 2) return two ? launch_tc<2, 2>(a, nsets, s) : launch_tc<2, 1>(a, nsets, s);
     if (bits == 4) return two ? launch_tc<4, 2>(a, nsets, s) : launch_tc<4, 1>(a, nsets, s);
@@ -875,10 +880,12 @@ __global__ void __launch_bounds__(kTailThreads) attn_tail_kernel(const TailArgs 
     __shared__ __align__(16) float Qs[8 * 128];
     __shared__ float Ps[8 * kTailTokens];
     const Geom &g = a.g;
-    const int tile = blockIdx.x, s = blockIdx.y, z = blockIdx.z;
+    const int tile = blockIdx.x, s = blockIdx.y;
+    const int z = (int)blockIdx.z / a.hsets, head0 = ((int)blockIdx.z - z * a.hsets) * a.GQ;
+    const int nh = min(a.GQ, a.gq_stride - head0);
     const int b = s / a.H, kvh = s - b * a.H;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t rbase = (int64_t)z * a.rows_per_set;
+    const int64_t rbase = (int64_t)z * a.rows_per_set + head0; // + b*Hq + kvh*gq_stride + h
     const SuffixRef suf = a.suf[z];
     const int64_t t0 = a.main_tokens + (int64_t)tile * kTailTokens;
     const int nt = (int)max((int64_t)0, min((int64_t)kTailTokens, a.seq_p + suf.len - t0));
@@ -899,7 +906,7 @@ __global__ void __launch_bounds__(kTailThreads) attn_tail_kernel(const TailArgs 
 #pragma unroll
     for (int i = 0; i < kQPer; ++i) {
         const int e = threadIdx.x + i * kTailThreads;
-        if (e < a.GQ * 128) qreg[i] = a.q[(rbase + (int64_t)b * a.Hq + kvh * a.GQ) * 128 + e];
+        if (e < nh * 128) qreg[i] = a.q[(rbase + (int64_t)b * a.Hq + kvh * a.gq_stride) * 128 + e];
     }
     // Keys: tiles start on group boundaries and the packed key region ends on
     // one (kq is a multiple of the group), so a tile is either one whole packed
@@ -933,7 +940,7 @@ __global__ void __launch_bounds__(kTailThreads) attn_tail_kernel(const TailArgs 
 #pragma unroll
     for (int i = 0; i < kQPer; ++i) {
         const int e = threadIdx.x + i * kTailThreads;
-        if (e < a.GQ * 128) Qs[e] = qreg[i];
+        if (e < nh * 128) Qs[e] = qreg[i];
     }
     if (kpacked) {
         // fma(code, scale, zero) as the packed path (quant.rs:404-406)
@@ -969,7 +976,7 @@ __global__ void __launch_bounds__(kTailThreads) attn_tail_kernel(const TailArgs 
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
         const int h = warp + 4 * hh;
-        if (h >= a.GQ) continue;
+        if (h >= nh) continue;
         float x = -INFINITY;
         if (lane < nt) {
             const float *kr = Ks + lane * kTailPitch;
@@ -1000,8 +1007,8 @@ __global__ void __launch_bounds__(kTailThreads) attn_tail_kernel(const TailArgs 
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
         const int h = warp + 4 * hh;
-        if (h >= a.GQ) continue;
-        const int64_t row = rbase + (int64_t)b * a.Hq + kvh * a.GQ + h;
+        if (h >= nh) continue;
+        const int64_t row = rbase + (int64_t)b * a.Hq + kvh * a.gq_stride + h;
         const int slot = a.slot0 + tile;
         float o[4] = {0.f, 0.f, 0.f, 0.f};
         for (int tt = 0; tt < nt; ++tt) {
@@ -1265,9 +1272,10 @@ __global__ void __launch_bounds__(32 * NW) exchange_rows_kernel(const float *par
 cudaError_t launch_attention_tail(const TailArgs &a, int ntiles, int nstreams, int nsets,
                                   cudaStream_t s) {
     if (ntiles <= 0 || nsets <= 0) return cudaSuccess;
-    if (nsets > kMaxSessionsPerLaunch) return cudaErrorInvalidValue;
+    if (nsets > kMaxSessionsPerLaunch || a.hsets < 1 || a.hsets > kMaxTcHeadSets)
+        return cudaErrorInvalidValue;
     ProfScope prof("attn_tail", s);
-    const dim3 grid((unsigned)ntiles, (unsigned)nstreams, (unsigned)nsets);
+    const dim3 grid((unsigned)ntiles, (unsigned)nstreams, (unsigned)(nsets * a.hsets));
     if (a.g.bits == 2)
         attn_tail_kernel<2><<<grid, kTailThreads, 0, s>>>(a);
     else if (a.g.bits == 4)

@@ -536,9 +536,11 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
         const uint64_t G = p.cfg.group_size;
         const uint64_t main_tokens = (pre ? (uint64_t)main_vq : p.vq) / G * G;
         const int64_t main_groups = (int64_t)(main_tokens / G);
+        // more than 8 query heads per kv head: head sets of <= 8, one pass each
+        const int hsets = kivi::tc_head_sets((int)Gq), gs = kivi::tc_set_heads((int)Gq);
         int64_t per = 0;
         int nslots = 0;
-        CUDA_TRY(kivi::plan_attention_tc((int)p.cfg.bits, (int)Gq, (int64_t)(p.B * p.H),
+        CUDA_TRY(kivi::plan_attention_tc((int)p.cfg.bits, gs, (int64_t)(p.B * p.H),
                                          main_groups, &per, &nslots),
                  "attention plan");
         const uint64_t rows1 = p.B * Hq;
@@ -614,7 +616,9 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
                 t.vp_stride = kivi::vparam_stride(g, p.st.cap);
                 t.H = (int)p.H;
                 t.Hq = (int)Hq;
-                t.GQ = (int)Gq;
+                t.GQ = gs;
+                t.gq_stride = (int)Gq;
+                t.hsets = hsets;
                 t.nstreams = (int64_t)(p.B * p.H);
                 t.main_groups = main_groups;
                 t.per = per;
@@ -635,7 +639,9 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
             ta.st = p.st;
             ta.H = (int)p.H;
             ta.Hq = (int)Hq;
-            ta.GQ = (int)Gq;
+            ta.GQ = gs;
+            ta.gq_stride = (int)Gq;
+            ta.hsets = hsets;
             ta.kq = (int64_t)p.kq;
             ta.vq = (int64_t)p.vq;
             ta.seq_p = (int64_t)p.seq;

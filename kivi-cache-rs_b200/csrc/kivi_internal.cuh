@@ -252,7 +252,9 @@ struct TcArgs {
     const uint32_t *vcodes;
     const float2 *vparams;
     int64_t code_stride, kp_stride, vp_stride; // per-stream strides (elements)
-    int H, Hq, GQ;
+    int H, Hq, GQ;        // GQ: query heads of one head set (<= 8)
+    int gq_stride;        // query heads per kv head (the q / output row layout)
+    int hsets;            // head sets per query set: blockIdx.z = set * hsets + head set
     int64_t nstreams;     // B * H
     int64_t main_groups;  // 32-token groups with packed K and V, per stream
     int64_t per;          // groups per CTA (plan_attention_tc)
@@ -270,11 +272,13 @@ struct TcArgs {
 // of each stream (partial group, fp32 window/residual, session z's fp32
 // suffix), 32 tokens per CTA, partial slots slot0 + tile; query set z =
 // blockIdx.z as in TcArgs.  Tiles past a set's end write empty states
-// (m = -inf, l = 0, o = 0).  head_dim 128, <= 8 q heads per kv head.
+// (m = -inf, l = 0, o = 0).  head_dim 128, head sets of <= 8 q heads as in
+// TcArgs (blockIdx.z = set * hsets + head set).
 struct TailArgs {
     Geom g;
     Store st;
     int H, Hq, GQ;
+    int gq_stride, hsets;
     int64_t kq, vq, seq_p;
     int vhead;
     int64_t main_tokens;
@@ -291,6 +295,12 @@ cudaError_t launch_attention_tail(const TailArgs &a, int ntiles, int nstreams, i
 cudaError_t launch_merge_rows(const float *part_ml, const float *part_o, int parts, int64_t rows,
                               float *out, float *out_m, float *out_l, cudaStream_t s);
 bool attention_tc_supported(const Geom &g, int gq);
+// Up to 8 query heads per kv head run as one head set; more are split into
+// tc_head_sets(gq) sets of tc_set_heads(gq) heads (the last may have fewer),
+// each a separate pass over the cache.
+constexpr int kMaxTcHeadSets = 16;
+inline int tc_head_sets(int gq) { return (gq + 7) / 8; }
+inline int tc_set_heads(int gq) { return (gq + tc_head_sets(gq) - 1) / tc_head_sets(gq); }
 // Work split of the tensor-core kernel on the current device: one wave of
 // resident CTAs (fewer when the work is small); a function of the stream count
 // and length only, so every query set and every call on the same cache shape

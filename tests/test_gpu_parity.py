@@ -386,6 +386,36 @@ def test_gqa_attention_matches_oracle(K, batch, kv, qh):
     assert_attention_close(g.attention(q, qh, scale), o.attention(q, qh, scale))
 
 
+@pytest.mark.parametrize("bits,batch,kv,qh,seq", [
+    (2, 1, 2, 32, 3000), (4, 2, 1, 12, 1100), (8, 1, 1, 40, 700), (2, 2, 2, 18, 4500),
+])
+def test_wide_gqa_tensor_core_head_sets(K, bits, batch, kv, qh, seq):
+    """More than 8 query heads per kv head run the tensor-core path as head
+    sets of <= 8 heads (16 -> 2 x 8, 12 -> 2 x 6, 40 -> 5 x 8, 9 -> 2 x 5);
+    attention and one decode step match the oracle, and the step runs the
+    tensor-core kernel (one launch per step, every head set in its grid)."""
+    dim = 128
+    g, o = pair(K, bits, 32, 128, batch, kv, dim)
+    keys, values, _ = synthetic_kv(qh + bits, batch, kv, seq, dim)
+    append_both(g, o, keys, values, seq)
+    q = np.random.default_rng(qh).standard_normal(batch * qh * dim, dtype=np.float32)
+    scale = float(np.float32(1.0) / np.sqrt(np.float32(dim)))
+    assert_attention_close(g.attention(q, qh, scale), o.attention(q, qh, scale))
+    k1, v1, _ = synthetic_kv(qh + 50, batch, kv, 1, dim)
+    lib = K.lib()
+    import ctypes as C
+    lib.kivi_profile_reset()
+    lib.kivi_profile_enable(1)
+    rt = K.RuntimeKv(g)
+    got = rt.decode(k1, v1, q, qh, scale)
+    lib.kivi_profile_enable(0)
+    n, ms = C.c_uint64(), C.c_double()
+    lib.kivi_profile_read(b"attn_tc", C.byref(n), C.byref(ms))
+    assert n.value == 1
+    o.append(k1, v1, 1)
+    assert_attention_close(got, o.attention(q, qh, scale))
+
+
 def test_empty_cache_and_bad_heads(K):
     """tests/attention.rs:103-114"""
     cache = K.KiviCache(K.KiviConfig(), 1, 2, 128)
