@@ -100,10 +100,14 @@ def load_peaks(key="hbm_gbs"):
         return (6650.0 if key == "hbm_gbs" else 1590.0), "fallback"
 
 
-def load_traffic(kernel, workload):
+def load_traffic(kernel, workload, world=1):
     """(bytes, note): per-launch DRAM read + write bytes of `kernel` on
     `workload` from the committed ncu summaries (profiles/traffic.json), or
-    (None, why) when no capture of that kernel on that workload exists."""
+    (None, why) when no capture of that kernel on that workload exists.  The
+    captures are of one-GPU runs: `world` > 1 (a sequence-sharded run, whose
+    per-rank launches are smaller) has none."""
+    if world > 1:
+        return None, "the ncu captures on file are of one-GPU runs"
     path = os.path.join(ROOT, "profiles", "traffic.json")
     try:
         with open(path) as f:
@@ -800,7 +804,8 @@ def run_gpu(args, cfgd, rank, world, local_rank):
     workload = cfgd["name"]
     h2d, d2h = wl.io_bytes()
     config = base_config(cfgd, world)
-    traffic, traffic_note = load_traffic(kernel, workload)
+    # configs 0-3 run the same per-rank workload at every N; config 4's shrinks
+    traffic, traffic_note = load_traffic(kernel, workload, world if strong else 1)
     l2_note = (f"cache {job_cache_bytes / world / 1e6:.0f} MB per rank on average, a shard "
                f"under 126 MB L2 on some rank: L2 flushed between steps on every rank "
                f"({FLUSH_BYTES >> 20} MB write), each step timed by its own CUDA events"

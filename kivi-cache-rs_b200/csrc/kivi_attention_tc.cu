@@ -400,6 +400,21 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : KIVI_TC_
         // running beside this kernel may raise them, and every value read
         // bounds the groups read here, but the warps' partial states are
         // combined below under one factor.
+        // the query loads go out before the bounds' barrier (one memory
+        // latency for both)
+        float qv[NT][8][2];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const int h = nt * 4 + hb;
+            const bool okh = h < nh;
+            const float *qrow = a.q + (rbase + (int64_t)b * a.Hq + kvh * a.gq_stride + (okh ? h : 0)) * kD;
+#pragma unroll
+            for (int kt = 0; kt < 8; ++kt) {
+                const float2 v = *reinterpret_cast<const float2 *>(qrow + 16 * kt + 2 * c + 8 * par);
+                qv[nt][kt][0] = okh ? v.x : 0.0f;
+                qv[nt][kt][1] = okh ? v.y : 0.0f;
+            }
+        }
         if (threadIdx.x == 0) {
             bnd[0] = a.kbound[s];
             bnd[1] = a.vbound[s];
@@ -411,21 +426,13 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : KIVI_TC_
         const float cv = (float)(3 - min(max(ev, -120), 120));
 
         // ---- query rows of this stream: q'' = q * 2^(14 - e_q) * 2^-es per head
-        float qv[NT][8][2];
         float fh[NT]; // per lane head c: 2^(e_q - 14 + es) * scale * log2(e)
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-            const int h = nt * 4 + hb;
-            const bool okh = h < nh;
-            const float *qrow = a.q + (rbase + (int64_t)b * a.Hq + kvh * a.gq_stride + (okh ? h : 0)) * kD;
             float qm = 0.0f;
 #pragma unroll
-            for (int kt = 0; kt < 8; ++kt) {
-                const float2 v = *reinterpret_cast<const float2 *>(qrow + 16 * kt + 2 * c + 8 * par);
-                qv[nt][kt][0] = okh ? v.x : 0.0f;
-                qv[nt][kt][1] = okh ? v.y : 0.0f;
+            for (int kt = 0; kt < 8; ++kt)
                 qm = fmaxf(qm, fmaxf(fabsf(qv[nt][kt][0]), fabsf(qv[nt][kt][1])));
-            }
             qm = fmaxf(qm, __shfl_xor_sync(0xffffffffu, qm, 1));
             qm = fmaxf(qm, __shfl_xor_sync(0xffffffffu, qm, 2));
             qm = fmaxf(qm, __shfl_xor_sync(0xffffffffu, qm, 4));
