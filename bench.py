@@ -292,9 +292,11 @@ def base_config(cfgd, world):
                    question_tokens_start=c["suffix"],
                    parallelism=f"independent documents per rank, dp{world}")
     else:
-        cfg.update(global_batch=c["B"],
-                   parallelism=f"sequence sharding over {world} ranks, NCCL all-gather of "
-                               f"packed (m, l, o) + rank-ordered merge")
+        how = ("NCCL all-gather of packed (m, l, o) + rank-ordered merge"
+               if EXCHANGE[0] == "nccl" or world == 1 and EXCHANGE[0] != "p2p" else
+               "peer-memory exchange kernel over NVLink: every rank's (m, l, o) stored into "
+               "every rank's buffer + rank-ordered merge")
+        cfg.update(global_batch=c["B"], parallelism=f"sequence sharding over {world} ranks, {how}")
     return cfg
 
 
@@ -1127,6 +1129,58 @@ def run_reference(args, cfgd, rank, world):
     }
 
 
+def ctx_sweep(contexts, reps=12):
+    """Per-launch device time of the decode path's kernels (attn_tc, attn_tail,
+    merge; the library's CUDA-event profiler) against the context length, on one
+    cache of 8 streams (B1, 8 kv / 32 q heads, head_dim 128, 2-bit): one JSON
+    line per context.  Each attention call runs behind a short device-side
+    hold, with L2 flushed (a 256 MB write) before it."""
+    import torch
+
+    import kivi_cache as K
+
+    B, H, Hq, D = 1, 8, 32, 128
+    st = torch.cuda.Stream()
+    flush = torch.empty(FLUSH_BYTES // 4, device="cuda")
+    for ctx in contexts:
+        c = K.KiviCache(K.KiviConfig.try_new(2, 32, 128), B, H, D)
+        c.reserve(ctx + 256)
+        g = torch.Generator(device="cuda")
+        g.manual_seed(ctx)
+        done = 0
+        while done < ctx:
+            n = min(32768, ctx - done)
+            k = torch.randn(B, H, n, D, device="cuda", generator=g)
+            v = torch.randn(B, H, n, D, device="cuda", generator=g)
+            c.append_dev(k, v, n, stream=st)
+            st.synchronize()
+            done += n
+        q = torch.randn(B * Hq * D, device="cuda", generator=g)
+        out = torch.empty(B * Hq * D, device="cuda")
+        scale = float(np.float32(1.0) / np.sqrt(np.float32(D)))
+        for _ in range(3):
+            c.attention_dev(q, Hq, scale, out, stream=st)
+        st.synchronize()
+        L = K.lib()
+        L.kivi_profile_reset()
+        L.kivi_profile_enable(1)
+        for i in range(reps):
+            with torch.cuda.stream(st):
+                flush.fill_(float(i))
+            L.kivi_profile_hold(500, ctypes.c_void_p(st.cuda_stream))
+            c.attention_dev(q, Hq, scale, out, stream=st)
+        st.synchronize()
+        L.kivi_profile_enable(0)
+        res = {"ctx_sweep": True, "context": ctx, "streams": B * H,
+               "groups": B * H * (c.quantized_value_tokens() // 32)}
+        for name in ("attn_tc", "attn_tail", "merge"):
+            nl_, ms_ = ctypes.c_uint64(), ctypes.c_double()
+            L.kivi_profile_read(name.encode(), ctypes.byref(nl_), ctypes.byref(ms_))
+            res[name + "_us"] = round(ms_.value / max(1, nl_.value) * 1e3, 2)
+        print(json.dumps(res), flush=True)
+        del c
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1140,7 +1194,12 @@ def main():
                     help="config 4: peer-memory exchange kernel or NCCL all-gather")
     ap.add_argument("--tail-discount", type=int, default=0,
                     help="config 4: tokens moved off the last rank (it also appends)")
+    ap.add_argument("--ctx-sweep", type=int, nargs="+", default=None, metavar="TOKENS",
+                    help="instead of the benchmark: decode kernels' launch time per context")
     args = ap.parse_args()
+    if args.ctx_sweep:
+        ctx_sweep(args.ctx_sweep)
+        return
     if args.warmup < 3:
         args.warmup = 3
     rank = env_int("RANK", 0)

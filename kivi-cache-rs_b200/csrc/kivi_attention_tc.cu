@@ -329,6 +329,8 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : KIVI_TC_
     constexpr int IPC = TG::IPC;
     constexpr int kHeads = NT * 4;
     extern __shared__ __align__(128) unsigned char smem[];
+    pdl_wait();
+    pdl_trigger();
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * TG::STAGE);
     float *pbuf = reinterpret_cast<float *>(full + kStages);              // [warp][kHeads][kPStride]
     float *Ow = pbuf + kConsumers * kHeads * kPStride;                   // [warp][kHeads][128]
@@ -737,9 +739,10 @@ cudaError_t launch_tc(const TcArgs &a, int nsets, cudaStream_t s) {
     const int nctas = (int)((W + a.per - 1) / a.per);
     ProfScope prof("attn_tc", s);
     const dim3 grid((unsigned)nctas, 1u, (unsigned)(nsets * a.hsets));
-    attn_tc_kernel<BITS, NT><<<grid, kTcThreads, tc_smem<BITS, NT>(), s>>>(a);
+    const cudaError_t e =
+        launch_pdl(attn_tc_kernel<BITS, NT>, grid, dim3(kTcThreads), tc_smem<BITS, NT>(), s, true, a);
     count_launch();
-    return cudaGetLastError();
+    return e;
 }
 
 } // namespace
@@ -882,6 +885,8 @@ __device__ __forceinline__ float4 tail_value4(const TailArgs &a, const uint32_t 
 
 template <int BITS>
 __global__ void __launch_bounds__(kTailThreads) attn_tail_kernel(const TailArgs a) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float Ks[kTailTokens * kTailPitch];
     __shared__ float Vs[kTailTokens * kTailPitch];
     __shared__ __align__(16) float Qs[8 * 128];
@@ -1149,6 +1154,8 @@ __global__ void __launch_bounds__(32 * NW) merge_rows_kernel(const float *part_m
                                                              int64_t rows, float *out,
                                                              float *out_m, float *out_l) {
     __shared__ MergeSmem<NW> sm;
+    pdl_wait();
+    pdl_trigger();
     const int64_t row = blockIdx.x;
     float o, M, L;
     merge_row_state<NW>(part_ml, part_o, parts, row, sm, o, M, L);
@@ -1216,6 +1223,8 @@ __global__ void __launch_bounds__(32 * NW) exchange_rows_kernel(const float *par
     __shared__ float w_sh[kMaxExchangeRanks];
     __shared__ float L_sh;
     __shared__ int fail;
+    pdl_wait();
+    pdl_trigger();
     const int64_t row = blockIdx.x;
     float o, M, L;
     merge_row_state<NW>(part_ml, part_o, parts, row, sm, o, M, L);
@@ -1277,20 +1286,18 @@ __global__ void __launch_bounds__(32 * NW) exchange_rows_kernel(const float *par
 } // namespace
 
 cudaError_t launch_attention_tail(const TailArgs &a, int ntiles, int nstreams, int nsets,
-                                  cudaStream_t s) {
+                                  cudaStream_t s, bool pdl) {
     if (ntiles <= 0 || nsets <= 0) return cudaSuccess;
     if (nsets > kMaxSessionsPerLaunch || a.hsets < 1 || a.hsets > kMaxTcHeadSets)
         return cudaErrorInvalidValue;
     ProfScope prof("attn_tail", s);
     const dim3 grid((unsigned)ntiles, (unsigned)nstreams, (unsigned)(nsets * a.hsets));
-    if (a.g.bits == 2)
-        attn_tail_kernel<2><<<grid, kTailThreads, 0, s>>>(a);
-    else if (a.g.bits == 4)
-        attn_tail_kernel<4><<<grid, kTailThreads, 0, s>>>(a);
-    else
-        attn_tail_kernel<8><<<grid, kTailThreads, 0, s>>>(a);
+    const cudaError_t e =
+        a.g.bits == 2   ? launch_pdl(attn_tail_kernel<2>, grid, dim3(kTailThreads), 0, s, pdl, a)
+        : a.g.bits == 4 ? launch_pdl(attn_tail_kernel<4>, grid, dim3(kTailThreads), 0, s, pdl, a)
+                        : launch_pdl(attn_tail_kernel<8>, grid, dim3(kTailThreads), 0, s, pdl, a);
     count_launch();
-    return cudaGetLastError();
+    return e;
 }
 
 cudaError_t launch_exchange_rows(const float *part_ml, const float *part_o, int parts,
@@ -1298,28 +1305,26 @@ cudaError_t launch_exchange_rows(const float *part_ml, const float *part_o, int 
     if (rows <= 0) return cudaSuccess;
     if (x.world < 1 || x.world > kMaxExchangeRanks) return cudaErrorInvalidValue;
     ProfScope prof("merge_exchange", s);
-    if (parts > 32)
-        exchange_rows_kernel<16><<<(unsigned)rows, 512, 0, s>>>(part_ml, part_o, parts, rows, x,
-                                                                out);
-    else
-        exchange_rows_kernel<4><<<(unsigned)rows, 128, 0, s>>>(part_ml, part_o, parts, rows, x,
-                                                               out);
+    const cudaError_t e =
+        parts > 32 ? launch_pdl(exchange_rows_kernel<16>, dim3((unsigned)rows), dim3(512), 0, s,
+                                true, part_ml, part_o, parts, rows, x, out)
+                   : launch_pdl(exchange_rows_kernel<4>, dim3((unsigned)rows), dim3(128), 0, s,
+                                true, part_ml, part_o, parts, rows, x, out);
     count_launch();
-    return cudaGetLastError();
+    return e;
 }
 
 cudaError_t launch_merge_rows(const float *part_ml, const float *part_o, int parts, int64_t rows,
                               float *out, float *out_m, float *out_l, cudaStream_t s) {
     if (rows <= 0) return cudaSuccess;
     ProfScope prof("merge", s);
-    if (parts > 32)
-        merge_rows_kernel<16><<<(unsigned)rows, 512, 0, s>>>(part_ml, part_o, parts, rows, out,
-                                                             out_m, out_l);
-    else
-        merge_rows_kernel<4><<<(unsigned)rows, 128, 0, s>>>(part_ml, part_o, parts, rows, out,
-                                                            out_m, out_l);
+    const cudaError_t e =
+        parts > 32 ? launch_pdl(merge_rows_kernel<16>, dim3((unsigned)rows), dim3(512), 0, s, true,
+                                part_ml, part_o, parts, rows, out, out_m, out_l)
+                   : launch_pdl(merge_rows_kernel<4>, dim3((unsigned)rows), dim3(128), 0, s, true,
+                                part_ml, part_o, parts, rows, out, out_m, out_l);
     count_launch();
-    return cudaGetLastError();
+    return e;
 }
 
 } // namespace kivi

@@ -660,8 +660,10 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
                 ta.suf[i].len = sv ? (int64_t)sv[s0 + i].len : 0;
                 ta.suf[i].cap = sv ? (int64_t)sv[s0 + i].cap : 0;
             }
+            // after this step's append, beside the main-region kernel (pre): a
+            // plain launch (see launch_pdl)
             CUDA_TRY(kivi::launch_attention_tail(ta, (int)NTT, (int)(p.B * p.H), (int)ns,
-                                                 fork ? side->s : stream),
+                                                 fork ? side->s : stream, !pre),
                      "attention tail");
             if (fork || pre) {
                 CUDA_TRY(cudaEventRecord(side->join, side->s), "attention join");

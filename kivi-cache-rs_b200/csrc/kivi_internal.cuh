@@ -19,6 +19,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace kivi {
 
 // Compile-time-free geometry of one cache (KiviConfig + head_dim).
@@ -112,6 +114,41 @@ struct AttnArgs {
     float *part_o;            // [rows][parts][D]
     SuffixRef suf[kMaxSessionsPerLaunch];
 };
+
+// Programmatic dependent launch: the decode step's kernels are launched with
+// cudaLaunchAttributeProgrammaticStreamSerialization, so a kernel's CTAs can be
+// scheduled while its predecessor in the stream is still running (the launch
+// latency overlaps the predecessor's last wave).  Every such kernel starts with
+// pdl_wait() -- it returns once the predecessor grid has completed and its
+// writes are visible, so nothing the kernel reads can be stale -- and lets its
+// own successor launch with pdl_trigger().  Both are no-ops for a kernel
+// launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+#ifndef KIVI_PDL
+#define KIVI_PDL 1
+#endif
+// Launches kernel<<<grid, block, smem, stream>>>(args...), with the programmatic
+// stream serialization attribute when `pdl` (KIVI_PDL = 0: never).  A launch
+// whose stream predecessor runs beside a kernel on another stream passes
+// false: its CTAs, resident early, would take SM slots from that kernel.
+template <class... KArgs, class... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, bool pdl, Args &&...args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = KIVI_PDL && pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Counts this library's kernel launches (reported as gpu_launches).
 void count_launch(int n = 1);
@@ -290,7 +327,7 @@ struct TailArgs {
     SuffixRef suf[kMaxSessionsPerLaunch]; // per set; k/v null and len 0 without suffix
 };
 cudaError_t launch_attention_tail(const TailArgs &a, int ntiles, int nstreams, int nsets,
-                                  cudaStream_t s);
+                                  cudaStream_t s, bool pdl = true);
 // One warp per row merge for head_dim 128 (mode: out_m == null -> normalised rows).
 cudaError_t launch_merge_rows(const float *part_ml, const float *part_o, int parts, int64_t rows,
                               float *out, float *out_m, float *out_l, cudaStream_t s);

@@ -296,6 +296,8 @@ __global__ void __launch_bounds__(256) append_small_kernel(Geom g, Store st, con
                                                            const float *values, int seq,
                                                            int kres_len, int64_t kq, int vres_len,
                                                            int64_t vq, int vhead, QueryCopy qc) {
+    pdl_wait();
+    pdl_trigger();
     const int s = blockIdx.x;
     const int D = g.D, R = g.R;
     const float *kin = keys + (int64_t)s * seq * D;
@@ -582,10 +584,10 @@ cudaError_t launch_append_small(const Geom &g, const Store &st, int n, const flo
     if (n <= 0 || seq <= 0) return cudaSuccess;
     if (qc.per != 0 && !append_query_fusable(qc.dst, qc.src, qc.per)) return cudaErrorInvalidValue;
     ProfScope prof("append_small", s);
-    append_small_kernel<<<n, 256, 0, s>>>(g, st, keys, values, seq, kres_len, kq, vres_len, vq,
-                                          vhead, qc);
+    const cudaError_t e = launch_pdl(append_small_kernel, dim3(n), dim3(256), 0, s, true, g, st,
+                                     keys, values, seq, kres_len, kq, vres_len, vq, vhead, qc);
     count_launch();
-    return cudaGetLastError();
+    return e;
 }
 
 bool append_query_fusable(const float *dst, const float *src, int64_t per) {
