@@ -75,7 +75,7 @@ CONFIGS = {
 }
 
 KERNELS = ("attn_tc", "attn_sets_tc", "attn_tail", "attn_chunk", "merge", "merge_shards",
-           "merge_exchange", "append_small", "key_groups", "value_tokens", "copy_rows",
+           "merge_exchange", "attn_ptail", "append_small", "key_groups", "value_tokens", "copy_rows",
            "suffix_append", "prefix_bounds")
 
 
@@ -713,6 +713,10 @@ def run_gpu(args, cfgd, rank, world, local_rank):
     torch.cuda.synchronize()
     clk.mark_start()
     if flush_l2:
+        # the device waits (a bounded spin) until every step is enqueued, so a
+        # host stall between a step's start event and its launches cannot land
+        # inside a timed span
+        K.lib().kivi_profile_hold(min(100000, 150 * S), ctypes.c_void_p(stream.cuda_stream))
         with torch.cuda.stream(stream):
             for k, i in enumerate(range(W, W + S)):
                 flush_buf.fill_(float(k))

@@ -538,10 +538,28 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
         const int64_t main_groups = (int64_t)(main_tokens / G);
         // more than 8 query heads per kv head: head sets of <= 8, one pass each
         const int hsets = kivi::tc_head_sets((int)Gq), gs = kivi::tc_set_heads((int)Gq);
+        // A short decode step's main-region kernel (pre; at most 128 groups per
+        // CTA, where the append and the tail tiles cost more than the slots)
+        // leaves CTA slots free for the step's append (one CTA per stream) and
+        // tail tiles when they fit in an eighth of the wave, so that both run
+        // beside it instead of after it.
+#ifndef KIVI_TC_RESERVE
+#define KIVI_TC_RESERVE 1
+#endif
+        int reserve = 0;
+        if (KIVI_TC_RESERVE && pre && !sv) {
+            const int64_t extra = (int64_t)(p.B * p.H) *
+                                  (1 + ((int64_t)p.seq + 1 - (int64_t)main_tokens + kTailTile - 1) /
+                                           kTailTile);
+            const int res = kivi::attention_tc_resident((int)p.cfg.bits, gs);
+            if (res > 0 && extra <= res / 8 &&
+                (int64_t)(p.B * p.H) * main_groups <= 128 * (res - extra))
+                reserve = (int)extra;
+        }
         int64_t per = 0;
         int nslots = 0;
         CUDA_TRY(kivi::plan_attention_tc((int)p.cfg.bits, gs, (int64_t)(p.B * p.H),
-                                         main_groups, &per, &nslots),
+                                         main_groups, &per, &nslots, reserve),
                  "attention plan");
         const uint64_t rows1 = p.B * Hq;
         for (uint64_t s0 = 0; s0 < nsess; s0 += kivi::kMaxSessionsPerLaunch) {
@@ -660,10 +678,27 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
                 ta.suf[i].len = sv ? (int64_t)sv[s0 + i].len : 0;
                 ta.suf[i].cap = sv ? (int64_t)sv[s0 + i].cap : 0;
             }
+            cudaStream_t tail_st = fork ? side->s : stream;
+            // Many sessions of a frozen prefix: the tail tiles wholly inside the
+            // prefix hold the same keys and values for every session and are
+            // read once for all of them.
+#ifndef KIVI_PREFIX_TAIL
+#define KIVI_PREFIX_TAIL 1
+#endif
+            const int64_t NPT = KIVI_PREFIX_TAIL && sets
+                                    ? std::min<int64_t>(NTT, ((int64_t)p.seq - (int64_t)main_tokens) /
+                                                                 kTailTile)
+                                    : 0;
+            if (NPT > 0) {
+                CUDA_TRY(kivi::launch_attention_prefix_tail(ta, (int)NPT, (int)(p.B * p.H), (int)ns,
+                                                            tail_st),
+                         "attention prefix tail");
+                ta.tile0 = (int)NPT;
+            }
             // after this step's append, beside the main-region kernel (pre): a
             // plain launch (see launch_pdl)
-            CUDA_TRY(kivi::launch_attention_tail(ta, (int)NTT, (int)(p.B * p.H), (int)ns,
-                                                 fork ? side->s : stream, !pre),
+            CUDA_TRY(kivi::launch_attention_tail(ta, (int)(NTT - NPT), (int)(p.B * p.H), (int)ns,
+                                                 tail_st, !pre),
                      "attention tail");
             if (fork || pre) {
                 CUDA_TRY(cudaEventRecord(side->join, side->s), "attention join");

@@ -323,11 +323,17 @@ struct TailArgs {
     float scale;
     float *part_ml, *part_o;
     int parts, slot0;
+    int tile0;            // first tile of this launch (tile = blockIdx.x + tile0)
     int64_t rows_per_set;
     SuffixRef suf[kMaxSessionsPerLaunch]; // per set; k/v null and len 0 without suffix
 };
 cudaError_t launch_attention_tail(const TailArgs &a, int ntiles, int nstreams, int nsets,
                                   cudaStream_t s, bool pdl = true);
+// The tiles [0, ntiles) of TailArgs that lie wholly inside the prefix (the same
+// keys and values for every query set), one CTA per (tile, stream, head set)
+// for all `nsets` sets at once.
+cudaError_t launch_attention_prefix_tail(const TailArgs &a, int ntiles, int nstreams, int nsets,
+                                         cudaStream_t s);
 // One warp per row merge for head_dim 128 (mode: out_m == null -> normalised rows).
 cudaError_t launch_merge_rows(const float *part_ml, const float *part_o, int parts, int64_t rows,
                               float *out, float *out_m, float *out_l, cudaStream_t s);
@@ -342,8 +348,11 @@ inline int tc_set_heads(int gq) { return (gq + tc_head_sets(gq) - 1) / tc_head_s
 // resident CTAs (fewer when the work is small); a function of the stream count
 // and length only, so every query set and every call on the same cache shape
 // splits identically.
+// `reserve` CTA slots are left free for kernels that run beside this one.
 cudaError_t plan_attention_tc(int bits, int gq, int64_t nstreams, int64_t main_groups,
-                              int64_t *per, int *nslots);
+                              int64_t *per, int *nslots, int reserve = 0);
+// Resident CTAs of the tensor-core kernel on the current device (one wave).
+int attention_tc_resident(int bits, int gq);
 cudaError_t launch_attention_tc(const TcArgs &a, int bits, int nsets, cudaStream_t s);
 // Flag a bounded device wait records when it gives up in the self-test.
 constexpr unsigned kWaitProbeCode = 0x40000000u;
