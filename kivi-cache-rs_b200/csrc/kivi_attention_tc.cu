@@ -894,7 +894,10 @@ __device__ __forceinline__ float4 tail_value4(const TailArgs &a, const uint32_t 
     return *reinterpret_cast<const float4 *>(sv + (t - a.seq_p) * 128 + d);
 }
 
-template <int BITS>
+// SPLIT (at most 2 query heads per kv head): the four warps share each head's
+// work (channel quarters for the logits, one channel per thread for the
+// output) instead of one warp per head.
+template <int BITS, bool SPLIT>
 __global__ void __launch_bounds__(kTailThreads) attn_tail_kernel(const TailArgs a) {
     pdl_wait();
     pdl_trigger();
@@ -994,6 +997,54 @@ __global__ void __launch_bounds__(kTailThreads) attn_tail_kernel(const TailArgs 
         }
     }
     __syncthreads();
+
+    if (SPLIT) {
+        __shared__ float Sp[4][2][kTailTokens]; // partial logits per channel quarter
+        __shared__ float Msh[2], Lsh[2];
+        for (int h = 0; h < nh; ++h) {
+            float d = 0.0f;
+            if (lane < nt) {
+                const float *kr = Ks + lane * kTailPitch + 32 * warp;
+                const float *q = Qs + h * 128 + 32 * warp;
+#pragma unroll 8
+                for (int i = 0; i < 32; ++i) d = fmaf(kr[i], q[i], d);
+            }
+            Sp[warp][h][lane] = d;
+        }
+        __syncthreads();
+        if (warp < nh) {
+            const int h = warp;
+            float x = -INFINITY;
+            if (lane < nt)
+                x = ((Sp[0][h][lane] + Sp[1][h][lane]) + (Sp[2][h][lane] + Sp[3][h][lane])) * a.scale;
+            float m = x;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            const float p = (lane < nt && m != -INFINITY) ? expf(x - m) : 0.0f;
+            float l = p;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+            Ps[h * kTailTokens + lane] = p;
+            if (lane == 0) {
+                Msh[h] = m;
+                Lsh[h] = l;
+            }
+        }
+        __syncthreads();
+        const int d = threadIdx.x;
+        const int slot = a.slot0 + tile;
+        for (int h = 0; h < nh; ++h) {
+            float o = 0.0f;
+            for (int tt = 0; tt < nt; ++tt) o = fmaf(Ps[h * kTailTokens + tt], Vs[tt * kTailPitch + d], o);
+            const int64_t row = rbase + (int64_t)b * a.Hq + kvh * a.gq_stride + h;
+            a.part_o[(row * a.parts + slot) * 128 + d] = o;
+            if (d == 0) {
+                a.part_ml[(row * a.parts + slot) * 2 + 0] = Msh[h];
+                a.part_ml[(row * a.parts + slot) * 2 + 1] = Lsh[h];
+            }
+        }
+        return;
+    }
 
     float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
 #pragma unroll
@@ -1424,10 +1475,18 @@ cudaError_t launch_attention_tail(const TailArgs &a, int ntiles, int nstreams, i
         return cudaErrorInvalidValue;
     ProfScope prof("attn_tail", s);
     const dim3 grid((unsigned)ntiles, (unsigned)nstreams, (unsigned)(nsets * a.hsets));
+#ifndef KIVI_TAIL_SPLIT
+#define KIVI_TAIL_SPLIT 1
+#endif
+    const bool split = KIVI_TAIL_SPLIT && a.GQ <= 2;
+    const dim3 blk(kTailThreads);
     const cudaError_t e =
-        a.g.bits == 2   ? launch_pdl(attn_tail_kernel<2>, grid, dim3(kTailThreads), 0, s, pdl, a)
-        : a.g.bits == 4 ? launch_pdl(attn_tail_kernel<4>, grid, dim3(kTailThreads), 0, s, pdl, a)
-                        : launch_pdl(attn_tail_kernel<8>, grid, dim3(kTailThreads), 0, s, pdl, a);
+        split ? (a.g.bits == 2   ? launch_pdl(attn_tail_kernel<2, true>, grid, blk, 0, s, pdl, a)
+                 : a.g.bits == 4 ? launch_pdl(attn_tail_kernel<4, true>, grid, blk, 0, s, pdl, a)
+                                 : launch_pdl(attn_tail_kernel<8, true>, grid, blk, 0, s, pdl, a))
+              : (a.g.bits == 2   ? launch_pdl(attn_tail_kernel<2, false>, grid, blk, 0, s, pdl, a)
+                 : a.g.bits == 4 ? launch_pdl(attn_tail_kernel<4, false>, grid, blk, 0, s, pdl, a)
+                                 : launch_pdl(attn_tail_kernel<8, false>, grid, blk, 0, s, pdl, a));
     count_launch();
     return e;
 }
