@@ -75,7 +75,7 @@ CONFIGS = {
 }
 
 KERNELS = ("attn_tc", "attn_sets_tc", "attn_tail", "attn_chunk", "merge", "merge_shards",
-           "merge_exchange", "attn_ptail", "append_small", "key_groups", "value_tokens", "copy_rows",
+           "merge_exchange", "append_small", "key_groups", "value_tokens", "copy_rows",
            "suffix_append", "prefix_bounds")
 
 
@@ -716,7 +716,7 @@ def run_gpu(args, cfgd, rank, world, local_rank):
         # the device waits (a bounded spin) until every step is enqueued, so a
         # host stall between a step's start event and its launches cannot land
         # inside a timed span
-        K.lib().kivi_profile_hold(min(100000, 150 * S), ctypes.c_void_p(stream.cuda_stream))
+        K.lib().kivi_profile_hold(min(100000, 400 * S), ctypes.c_void_p(stream.cuda_stream))
         with torch.cuda.stream(stream):
             for k, i in enumerate(range(W, W + S)):
                 flush_buf.fill_(float(k))
@@ -735,7 +735,8 @@ def run_gpu(args, cfgd, rank, world, local_rank):
     if dist:
         dist.barrier()
     launches = K.kernel_launches() - launches0
-    t_ms = sum(a.elapsed_time(b) for a, b in evs) if flush_l2 else ev0.elapsed_time(ev1)
+    step_ms = [a.elapsed_time(b) for a, b in evs] if flush_l2 else []
+    t_ms = sum(step_ms) if flush_l2 else ev0.elapsed_time(ev1)
     del flush_buf
     bytes_step1 = wl.step_bytes()
 
@@ -852,6 +853,11 @@ def run_gpu(args, cfgd, rank, world, local_rank):
         "gpu_launches": int(launches),
         "clocks": clk.summary(),
     }
+    if step_ms:
+        q = np.percentile(np.array(step_ms), [50, 90, 99])
+        result["step_ms_distribution"] = {"p50": float(q[0]), "p90": float(q[1]),
+                                          "p99": float(q[2]), "max": float(max(step_ms)),
+                                          "rank": rank}
     if world > 1:
         result["rank_ms_per_step"] = rank_ms
         result["rank_kernel_us"] = rank_kernel_us

@@ -906,7 +906,7 @@ __global__ void __launch_bounds__(kTailThreads) attn_tail_kernel(const TailArgs 
     __shared__ __align__(16) float Qs[8 * 128];
     __shared__ float Ps[8 * kTailTokens];
     const Geom &g = a.g;
-    const int tile = blockIdx.x + a.tile0, s = blockIdx.y;
+    const int tile = blockIdx.x, s = blockIdx.y;
     const int z = (int)blockIdx.z / a.hsets, head0 = ((int)blockIdx.z - z * a.hsets) * a.GQ;
     const int nh = min(a.GQ, a.gq_stride - head0);
     const int b = s / a.H, kvh = s - b * a.H;
@@ -1345,127 +1345,6 @@ __global__ void __launch_bounds__(32 * NW) exchange_rows_kernel(const float *par
     }
 }
 
-// Prefix tiles for many query sets at once: the tile's keys and values are
-// staged once per CTA (fp32, as in attn_tail_kernel) and a chunk of 32 query
-// rows of the kv head (rows of every set: set-major) is scored against them as
-// a small matrix product on the CUDA cores: each thread takes one row x 4
-// tokens of the logits and one row x 16 channels of the output (tokens j,
-// j+8, ...; channels 4c + 32k: conflict-free shared-memory reads).  Each row's
-// partial state (m, l, o) over the tile goes to slot slot0 + tile.
-// grid (tiles, streams, head sets x row chunks).
-constexpr int kPtThreads = 256;
-constexpr int kPtRows = 32;    // query rows per CTA
-constexpr int kPtPitch = 132;  // fp32 row pitch of K, V and Q in shared memory
-constexpr int kPtPPitch = 33;  // softmax weights [row][token]
-
-template <int BITS>
-__global__ void __launch_bounds__(kPtThreads) attn_prefix_tail_kernel(const TailArgs a, int nsets,
-                                                                       int nchunks) {
-    pdl_wait();
-    pdl_trigger();
-    extern __shared__ __align__(16) float pts[];
-    float *Ks = pts;                         // [32][kPtPitch]
-    float *Vs = Ks + kTailTokens * kPtPitch; // [32][kPtPitch]
-    float *Qs = Vs + kTailTokens * kPtPitch; // [kPtRows][kPtPitch]
-    float *Ps = Qs + kPtRows * kPtPitch;     // [kPtRows][kPtPPitch]
-    const Geom &g = a.g;
-    const int tile = blockIdx.x, s = blockIdx.y;
-    const int hs = (int)blockIdx.z / nchunks, chunk = (int)blockIdx.z - hs * nchunks;
-    const int head0 = hs * a.GQ;
-    const int nh = min(a.GQ, a.gq_stride - head0);
-    const int b = s / a.H, kvh = s - b * a.H;
-    const int tid = threadIdx.x;
-    const int64_t t0 = a.main_tokens + (int64_t)tile * kTailTokens; // whole tile < seq_p
-    const int r0 = chunk * kPtRows, nr = min(kPtRows, nsets * nh - r0);
-
-    const uint32_t *kc = a.st.kcodes + (int64_t)s * code_stride(g, a.st.cap);
-    const float2 *kp = a.st.kparams + (int64_t)s * kparam_stride(g, a.st.cap);
-    const uint32_t *vc = a.st.vcodes + (int64_t)s * code_stride(g, a.st.cap);
-    const float2 *vp = a.st.vparams + (int64_t)s * vparam_stride(g, a.st.cap);
-    const float *kres = a.st.kres + (int64_t)s * g.R * g.D;
-    const float *vres = a.st.vres + (int64_t)s * g.R * g.D;
-    for (int e = tid; e < kTailTokens * 32; e += kPtThreads) {
-        const int tt = e >> 5, d = (e & 31) * 4;
-        *reinterpret_cast<float4 *>(Ks + tt * kPtPitch + d) =
-            tail_key4<BITS>(a, kc, kp, kres, nullptr, t0 + tt, d);
-        *reinterpret_cast<float4 *>(Vs + tt * kPtPitch + d) =
-            tail_value4<BITS>(a, vc, vp, vres, nullptr, t0 + tt, d);
-    }
-    for (int e = tid; e < nr * 32; e += kPtThreads) {
-        const int r = e >> 5, d = (e & 31) * 4, rr = r0 + r;
-        const int z = rr / nh, h = rr - z * nh;
-        const float *q = a.q + ((int64_t)z * a.rows_per_set + (int64_t)b * a.Hq + kvh * a.gq_stride +
-                                head0 + h) * 128 + d;
-        *reinterpret_cast<float4 *>(Qs + r * kPtPitch + d) = make_float4(q[0], q[1], q[2], q[3]);
-    }
-    __syncthreads();
-    const int tr = tid >> 3, tc = tid & 7; // row tr; tokens tc + 8j; channels 4tc + 32k
-    // ---- logits x[j] = q(row tr) . k(token tc + 8j) * scale
-    float x[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 8
-    for (int d = 0; d < 128; d += 4) {
-        const float4 qv = *reinterpret_cast<const float4 *>(Qs + tr * kPtPitch + d);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float4 kv = *reinterpret_cast<const float4 *>(Ks + (tc + 8 * j) * kPtPitch + d);
-            x[j] = fmaf(qv.x, kv.x, x[j]);
-            x[j] = fmaf(qv.y, kv.y, x[j]);
-            x[j] = fmaf(qv.z, kv.z, x[j]);
-            x[j] = fmaf(qv.w, kv.w, x[j]);
-        }
-    }
-    // ---- the row's max and sum over the tile's 32 tokens (8 lanes x 4)
-    float m = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        x[j] *= a.scale;
-        m = fmaxf(m, x[j]);
-    }
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
-    float l = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const float p = expf(x[j] - m);
-        Ps[tr * kPtPPitch + tc + 8 * j] = p;
-        l += p;
-    }
-    l += __shfl_xor_sync(0xffffffffu, l, 1);
-    l += __shfl_xor_sync(0xffffffffu, l, 2);
-    l += __shfl_xor_sync(0xffffffffu, l, 4);
-    __syncwarp(); // the row's weights come from this warp's own lanes
-    // ---- o[row tr][channels 4tc + 32k .. +3] = sum_j p v
-    float4 o[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) o[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-    for (int j = 0; j < kTailTokens; ++j) {
-        const float pr = Ps[tr * kPtPPitch + j];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const float4 v = *reinterpret_cast<const float4 *>(Vs + j * kPtPitch + 4 * tc + 32 * k);
-            o[k].x = fmaf(pr, v.x, o[k].x);
-            o[k].y = fmaf(pr, v.y, o[k].y);
-            o[k].z = fmaf(pr, v.z, o[k].z);
-            o[k].w = fmaf(pr, v.w, o[k].w);
-        }
-    }
-    if (tr < nr) {
-        const int rr = r0 + tr, z = rr / nh, h = rr - z * nh;
-        const int64_t row = (int64_t)z * a.rows_per_set + (int64_t)b * a.Hq + kvh * a.gq_stride +
-                            head0 + h;
-        const int slot = a.slot0 + tile;
-        float *dst = a.part_o + (row * a.parts + slot) * 128;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) *reinterpret_cast<float4 *>(dst + 4 * tc + 32 * k) = o[k];
-        if (tc == 0) {
-            a.part_ml[(row * a.parts + slot) * 2 + 0] = m;
-            a.part_ml[(row * a.parts + slot) * 2 + 1] = l;
-        }
-    }
-}
-
 } // namespace
 
 cudaError_t launch_attention_tail(const TailArgs &a, int ntiles, int nstreams, int nsets,
@@ -1487,42 +1366,6 @@ cudaError_t launch_attention_tail(const TailArgs &a, int ntiles, int nstreams, i
               : (a.g.bits == 2   ? launch_pdl(attn_tail_kernel<2, false>, grid, blk, 0, s, pdl, a)
                  : a.g.bits == 4 ? launch_pdl(attn_tail_kernel<4, false>, grid, blk, 0, s, pdl, a)
                                  : launch_pdl(attn_tail_kernel<8, false>, grid, blk, 0, s, pdl, a));
-    count_launch();
-    return e;
-}
-
-cudaError_t launch_attention_prefix_tail(const TailArgs &a, int ntiles, int nstreams, int nsets,
-                                         cudaStream_t s) {
-    if (ntiles <= 0 || nsets <= 0) return cudaSuccess;
-    if (nsets > kMaxSessionsPerLaunch || a.hsets < 1 || a.hsets > kMaxTcHeadSets)
-        return cudaErrorInvalidValue;
-    const int nchunks = (nsets * a.GQ + kPtRows - 1) / kPtRows;
-    constexpr size_t smem =
-        sizeof(float) * ((size_t)(2 * kTailTokens + kPtRows) * kPtPitch + (size_t)kPtRows * kPtPPitch);
-    static bool configured[3][64] = {};
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    const int bi = a.g.bits == 2 ? 0 : a.g.bits == 4 ? 1 : 2;
-    if (!configured[bi][dev]) {
-        const cudaError_t e =
-            bi == 0 ? cudaFuncSetAttribute(attn_prefix_tail_kernel<2>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
-            : bi == 1 ? cudaFuncSetAttribute(attn_prefix_tail_kernel<4>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
-                      : cudaFuncSetAttribute(attn_prefix_tail_kernel<8>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        configured[bi][dev] = true;
-    }
-    ProfScope prof("attn_ptail", s);
-    const dim3 grid((unsigned)ntiles, (unsigned)nstreams, (unsigned)(a.hsets * nchunks));
-    const cudaError_t e =
-        bi == 0   ? launch_pdl(attn_prefix_tail_kernel<2>, grid, dim3(kPtThreads), smem, s, true,
-                               a, nsets, nchunks)
-        : bi == 1 ? launch_pdl(attn_prefix_tail_kernel<4>, grid, dim3(kPtThreads), smem, s, true,
-                               a, nsets, nchunks)
-                  : launch_pdl(attn_prefix_tail_kernel<8>, grid, dim3(kPtThreads), smem, s, true,
-                               a, nsets, nchunks);
     count_launch();
     return e;
 }

@@ -679,26 +679,10 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
                 ta.suf[i].cap = sv ? (int64_t)sv[s0 + i].cap : 0;
             }
             cudaStream_t tail_st = fork ? side->s : stream;
-            // Many sessions of a frozen prefix: the tail tiles wholly inside the
-            // prefix hold the same keys and values for every session and are
-            // read once for all of them.
-#ifndef KIVI_PREFIX_TAIL
-#define KIVI_PREFIX_TAIL 1
-#endif
-            const int64_t NPT = KIVI_PREFIX_TAIL && sets
-                                    ? std::min<int64_t>(NTT, ((int64_t)p.seq - (int64_t)main_tokens) /
-                                                                 kTailTile)
-                                    : 0;
-            if (NPT > 0) {
-                CUDA_TRY(kivi::launch_attention_prefix_tail(ta, (int)NPT, (int)(p.B * p.H), (int)ns,
-                                                            tail_st),
-                         "attention prefix tail");
-                ta.tile0 = (int)NPT;
-            }
             // after this step's append, beside the main-region kernel (pre): a
             // plain launch (see launch_pdl)
-            CUDA_TRY(kivi::launch_attention_tail(ta, (int)(NTT - NPT), (int)(p.B * p.H), (int)ns,
-                                                 tail_st, !pre),
+            CUDA_TRY(kivi::launch_attention_tail(ta, (int)NTT, (int)(p.B * p.H), (int)ns, tail_st,
+                                                 !pre),
                      "attention tail");
             if (fork || pre) {
                 CUDA_TRY(cudaEventRecord(side->join, side->s), "attention join");

@@ -323,17 +323,12 @@ struct TailArgs {
     float scale;
     float *part_ml, *part_o;
     int parts, slot0;
-    int tile0;            // first tile of this launch (tile = blockIdx.x + tile0)
     int64_t rows_per_set;
     SuffixRef suf[kMaxSessionsPerLaunch]; // per set; k/v null and len 0 without suffix
 };
 cudaError_t launch_attention_tail(const TailArgs &a, int ntiles, int nstreams, int nsets,
                                   cudaStream_t s, bool pdl = true);
-// The tiles [0, ntiles) of TailArgs that lie wholly inside the prefix (the same
-// keys and values for every query set), one CTA per (tile, stream, head set)
-// for all `nsets` sets at once.
-cudaError_t launch_attention_prefix_tail(const TailArgs &a, int ntiles, int nstreams, int nsets,
-                                         cudaStream_t s);
+
 // One warp per row merge for head_dim 128 (mode: out_m == null -> normalised rows).
 cudaError_t launch_merge_rows(const float *part_ml, const float *part_o, int parts, int64_t rows,
                               float *out, float *out_m, float *out_l, cudaStream_t s);

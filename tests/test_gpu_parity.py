@@ -75,6 +75,18 @@ def assert_store_equal(g, o):
         assert getattr(gm, k) == v, k
 
 
+def assert_attention_close_f64(got, ref, ref64):
+    """The bars against the exact (fp64) evaluation of the same quantized cache;
+    against the reference's fp32 output the gap may not exceed the reference's
+    own fp32 error plus the bars (its sequential fp32 sums drift from the exact
+    value over long contexts)."""
+    assert np.isfinite(got).all()
+    assert max_abs(got, ref64) <= ATOL, (max_abs(got, ref64), max_abs(ref, ref64))
+    assert rel_l2(got, ref64) <= RTOL_L2, (rel_l2(got, ref64), rel_l2(ref, ref64))
+    assert max_abs(got, ref) <= max_abs(ref, ref64) + ATOL
+    assert rel_l2(got, ref) <= rel_l2(ref, ref64) + RTOL_L2
+
+
 def assert_attention_close(got, ref, ref64=None):
     """max-abs <= 1e-4 against the reference's fp32 output, and rel-L2 <= 1e-5.
 
@@ -414,6 +426,61 @@ def test_wide_gqa_tensor_core_head_sets(K, bits, batch, kv, qh, seq):
     assert n.value == 1
     o.append(k1, v1, 1)
     assert_attention_close(got, o.attention(q, qh, scale))
+
+
+def test_decode_dev_short_main_region_leaves_slots(K):
+    """A short cache of 8 streams (the last shard of a sequence-sharded cache):
+    kivi_cache_decode_dev plans its main-region kernel with CTA slots left free
+    for the step's append and tail tiles; every step matches the oracle through
+    a key flush and value evictions."""
+    torch = pytest.importorskip("torch")
+    batch, kv, qh, dim, prompt = 1, 8, 32, 128, 20000
+    g, o = pair(K, 2, 32, 128, batch, kv, dim)
+    keys, values, _ = synthetic_kv(31, batch, kv, prompt, dim)
+    append_both(g, o, keys, values, prompt)
+    rng = np.random.default_rng(9)
+    scale = float(np.float32(1.0) / np.sqrt(np.float32(dim)))
+    out = torch.empty(batch * qh * dim, device="cuda")
+    for step in range(130):  # crosses a key flush (residual of 128)
+        k = rng.standard_normal(batch * kv * dim, dtype=np.float32)
+        v = rng.standard_normal(batch * kv * dim, dtype=np.float32)
+        q = rng.standard_normal(batch * qh * dim, dtype=np.float32)
+        dk, dv, dq = (torch.from_numpy(t).cuda() for t in (k, v, q))
+        g.decode_dev(dk, dv, dq, qh, scale, out)
+        torch.cuda.synchronize()
+        o.append(k, v, 1)
+        if step % 16 == 0 or step >= 126:
+            # 20k tokens: the reference's own fp32 sums drift past the bars, so
+            # they are taken against the oracle's fp64 evaluation (as at full size)
+            assert_attention_close_f64(out.cpu().numpy(), o.attention(q, qh, scale),
+                                       o.attention_f64(q, qh, scale))
+    K.device_wait_status(0)
+
+
+def test_wide_gqa_sessions_with_prefix_tail(K):
+    """Five sessions of a frozen prefix with 16 query heads per kv head: the
+    tcgen05 multi-set kernel, the shared prefix-tail tiles (two head sets,
+    read once for all sessions) and the per-session suffix tiles match the
+    oracle's RagSession::attention."""
+    kv, qh, dim, doc, n = 2, 32, 128, 3000, 5
+    keys, values, _ = synthetic_kv(17, 1, kv, doc, dim)
+    cache, ocache = pair(K, 2, 32, 128, 1, kv, dim)
+    append_both(cache, ocache, keys, values, doc)
+    prefix, oprefix = cache.share_prefix(), ocache.share_prefix()
+    sess = [prefix.session() for _ in range(n)]
+    osess = [oprefix.session() for _ in range(n)]
+    rng = np.random.default_rng(13)
+    x = rng.standard_normal((n, 1, kv, 37, dim), dtype=np.float32)
+    K.sessions_append(sess, x, x, 37)
+    for i in range(n):
+        osess[i].append(x[i].reshape(-1), x[i].reshape(-1), 37)
+    q = rng.standard_normal((n, 1, qh, dim), dtype=np.float32)
+    scale = float(np.float32(1.0) / np.sqrt(np.float32(dim)))
+    got = K.sessions_attention_batched(sess, q, qh, scale).reshape(n, -1)
+    for i in range(n):
+        qi = q[i].reshape(-1)
+        assert_attention_close_f64(got[i], osess[i].attention(qi, qh, scale),
+                                   osess[i].attention_f64(qi, qh, scale))
 
 
 def test_empty_cache_and_bad_heads(K):
