@@ -480,11 +480,21 @@ namespace {
 // beside the main-region kernel (they read other tokens and write other
 // partial slots), forked from and joined back into the call's stream by two
 // events, so the tail tiles fill the SMs the main kernel's wave leaves idle.
+// The second stream of a handle, created at the device's highest priority: the
+// large main-region kernel runs on it, the tail tiles (and a decode step's
+// append) on the caller's stream, so the block scheduler gives pending CTAs of
+// the main kernel (the multi-session kernel's second wave) precedence over the
+// tail's.
 struct SideLane {
     cudaStream_t s = nullptr;
     cudaEvent_t fork = nullptr, join = nullptr;
     cudaError_t create() {
-        cudaError_t e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+        int least = 0, greatest = 0;
+        if (cudaDeviceGetStreamPriorityRange(&least, &greatest) != cudaSuccess) {
+            (void)cudaGetLastError();
+            greatest = 0;
+        }
+        cudaError_t e = cudaStreamCreateWithPriority(&s, cudaStreamNonBlocking, greatest);
         if (e == cudaSuccess) e = cudaEventCreateWithFlags(&fork, cudaEventDisableTiming);
         if (e == cudaSuccess) e = cudaEventCreateWithFlags(&join, cudaEventDisableTiming);
         return e;
@@ -587,11 +597,12 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
             CUDA_TRY(scratch.ensure(ml_bytes + o_bytes), "attention scratch");
             float *part_ml = scratch.as<float>(), *part_o = scratch.as<float>(ml_bytes);
             const float *q = d_q + s0 * rows1 * p.D;
-            // tail tiles on the side lane when both kernels run (serial while
-            // per-kernel timing is on, so each event pair brackets one kernel)
+            // the main-region kernel on the side lane and the tail tiles on the
+            // caller's stream when both run (serial while per-kernel timing is
+            // on, so each event pair brackets one kernel)
             const bool fork = !pre && side && side->s && NTT > 0 && (sets || NC > 0) &&
                               !kivi::g_prof_on.load();
-            cudaStream_t main_st = pre ? side->s : stream;
+            cudaStream_t main_st = (pre || fork) ? side->s : stream;
             if (fork) {
                 CUDA_TRY(cudaEventRecord(side->fork, stream), "attention fork");
                 CUDA_TRY(cudaStreamWaitEvent(side->s, side->fork, 0), "attention fork");
@@ -678,11 +689,11 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
                 ta.suf[i].len = sv ? (int64_t)sv[s0 + i].len : 0;
                 ta.suf[i].cap = sv ? (int64_t)sv[s0 + i].cap : 0;
             }
-            cudaStream_t tail_st = fork ? side->s : stream;
-            // after this step's append, beside the main-region kernel (pre): a
-            // plain launch (see launch_pdl)
+            cudaStream_t tail_st = stream;
+            // beside the main-region kernel (pre, fork): a plain launch (see
+            // launch_pdl)
             CUDA_TRY(kivi::launch_attention_tail(ta, (int)NTT, (int)(p.B * p.H), (int)ns, tail_st,
-                                                 !pre),
+                                                 !(pre || fork)),
                      "attention tail");
             if (fork || pre) {
                 CUDA_TRY(cudaEventRecord(side->join, side->s), "attention join");
