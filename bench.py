@@ -689,12 +689,6 @@ def run_gpu(args, cfgd, rank, world, local_rank):
     for i in range(W):
         wl.step(i)
     stream.synchronize()
-    # host time to enqueue one step (sizes the device hold below)
-    th0 = time.perf_counter()
-    for i in range(W - 2, W):
-        wl.step(i)
-    host_step_s = (time.perf_counter() - th0) / 2
-    stream.synchronize()
 
     bytes_step0 = wl.step_bytes()
     cache_b0 = wl.cache_bytes()
@@ -718,29 +712,22 @@ def run_gpu(args, cfgd, rank, world, local_rank):
         dist.barrier()
     torch.cuda.synchronize()
     clk.mark_start()
-    hold_covered = None
     if flush_l2:
-        # The device waits (bounded spins, 100 ms each) until every step is
-        # enqueued, so a host stall between a step's start event and its
-        # launches cannot land inside a timed span: three times the measured
-        # host time of the whole loop; two untimed steps then bring the device
-        # back from the idle spin before the first timed one.  hold_covered
-        # reports whether the spins outlasted the enqueueing.
-        hold_us = min(500000, max(20000, int(3e6 * host_step_s * (S + 2))))
-        for _ in range((hold_us + 99999) // 100000):
-            K.lib().kivi_profile_hold(min(100000, hold_us), ctypes.c_void_p(stream.cuda_stream))
-        ev_hold = torch.cuda.Event()
-        ev_hold.record(stream)
+        # Each step: a bounded device spin (1 ms) while the host enqueues the
+        # step, the L2 flush, then the step between its own events.  The host
+        # cannot enqueue a whole loop ahead (the launch queue fills and blocks),
+        # so without the spin a host stall between a step's start event and
+        # its launches landed inside the timed span (78 ms once on config 3).
         with torch.cuda.stream(stream):
             for i in range(W - 2, W):
                 flush_buf.fill_(0.0)
                 wl.step(i)
             for k, i in enumerate(range(W, W + S)):
+                K.lib().kivi_profile_hold(1000, ctypes.c_void_p(stream.cuda_stream))
                 flush_buf.fill_(float(k))
                 evs[k][0].record(stream)
                 wl.step(i)
                 evs[k][1].record(stream)
-        hold_covered = not ev_hold.query()
     else:
         ev0.record(stream)
         for i in range(W, W + S):
@@ -875,8 +862,7 @@ def run_gpu(args, cfgd, rank, world, local_rank):
         q = np.percentile(np.array(step_ms), [50, 90, 99])
         result["step_ms_distribution"] = {"p50": float(q[0]), "p90": float(q[1]),
                                           "p99": float(q[2]), "max": float(max(step_ms)),
-                                          "rank": rank, "host_enqueue_us_per_step":
-                                          host_step_s * 1e6, "hold_covered_enqueue": hold_covered}
+                                          "rank": rank}
     if world > 1:
         result["rank_ms_per_step"] = rank_ms
         result["rank_kernel_us"] = rank_kernel_us
