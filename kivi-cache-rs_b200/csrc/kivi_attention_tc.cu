@@ -752,17 +752,8 @@ bool attention_tc_supported(const Geom &g, int gq) {
            tc_head_sets(gq) <= kMaxTcHeadSets;
 }
 
-int attention_tc_resident(int bits, int gq) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
-    const bool two = gq > 4;
-    return bits == 2   ? (two ? TcKernelInfo<2, 2>::resident(dev) : TcKernelInfo<2, 1>::resident(dev))
-           : bits == 4 ? (two ? TcKernelInfo<4, 2>::resident(dev) : TcKernelInfo<4, 1>::resident(dev))
-                       : (two ? TcKernelInfo<8, 2>::resident(dev) : TcKernelInfo<8, 1>::resident(dev));
-}
-
 cudaError_t plan_attention_tc(int bits, int gq, int64_t nstreams, int64_t main_groups,
-                              int64_t *per, int *nslots, int reserve) {
+                              int64_t *per, int *nslots) {
     *per = 0;
     *nslots = 0;
     if (nstreams <= 0 || main_groups <= 0) return cudaSuccess;
@@ -778,9 +769,7 @@ cudaError_t plan_attention_tc(int bits, int gq, int64_t nstreams, int64_t main_g
     const int64_t W = nstreams * main_groups;
     // one wave of resident CTAs, at least kMinGroups groups each
     constexpr int64_t kMinGroups = 8;
-    reserve = std::max(0, std::min(reserve, res / 2));
-    int64_t nctas = std::min<int64_t>((int64_t)res * KIVI_TC_WAVES - reserve,
-                                      (W + kMinGroups - 1) / kMinGroups);
+    int64_t nctas = std::min<int64_t>((int64_t)res * KIVI_TC_WAVES, (W + kMinGroups - 1) / kMinGroups);
     if (nctas < 1) nctas = 1;
     const int64_t p = (W + nctas - 1) / nctas;
     int ms = 0;

@@ -548,28 +548,10 @@ int32_t run_attention(const KvState &p, const SessionView *sv, uint64_t nsess, c
         const int64_t main_groups = (int64_t)(main_tokens / G);
         // more than 8 query heads per kv head: head sets of <= 8, one pass each
         const int hsets = kivi::tc_head_sets((int)Gq), gs = kivi::tc_set_heads((int)Gq);
-        // A short decode step's main-region kernel (pre; at most 128 groups per
-        // CTA, where the append and the tail tiles cost more than the slots)
-        // leaves CTA slots free for the step's append (one CTA per stream) and
-        // tail tiles when they fit in an eighth of the wave, so that both run
-        // beside it instead of after it.
-#ifndef KIVI_TC_RESERVE
-#define KIVI_TC_RESERVE 1
-#endif
-        int reserve = 0;
-        if (KIVI_TC_RESERVE && pre && !sv) {
-            const int64_t extra = (int64_t)(p.B * p.H) *
-                                  (1 + ((int64_t)p.seq + 1 - (int64_t)main_tokens + kTailTile - 1) /
-                                           kTailTile);
-            const int res = kivi::attention_tc_resident((int)p.cfg.bits, gs);
-            if (res > 0 && extra <= res / 8 &&
-                (int64_t)(p.B * p.H) * main_groups <= 128 * (res - extra))
-                reserve = (int)extra;
-        }
         int64_t per = 0;
         int nslots = 0;
         CUDA_TRY(kivi::plan_attention_tc((int)p.cfg.bits, gs, (int64_t)(p.B * p.H),
-                                         main_groups, &per, &nslots, reserve),
+                                         main_groups, &per, &nslots),
                  "attention plan");
         const uint64_t rows1 = p.B * Hq;
         for (uint64_t s0 = 0; s0 < nsess; s0 += kivi::kMaxSessionsPerLaunch) {

@@ -343,11 +343,8 @@ inline int tc_set_heads(int gq) { return (gq + tc_head_sets(gq) - 1) / tc_head_s
 // resident CTAs (fewer when the work is small); a function of the stream count
 // and length only, so every query set and every call on the same cache shape
 // splits identically.
-// `reserve` CTA slots are left free for kernels that run beside this one.
 cudaError_t plan_attention_tc(int bits, int gq, int64_t nstreams, int64_t main_groups,
-                              int64_t *per, int *nslots, int reserve = 0);
-// Resident CTAs of the tensor-core kernel on the current device (one wave).
-int attention_tc_resident(int bits, int gq);
+                              int64_t *per, int *nslots);
 cudaError_t launch_attention_tc(const TcArgs &a, int bits, int nsets, cudaStream_t s);
 // Flag a bounded device wait records when it gives up in the self-test.
 constexpr unsigned kWaitProbeCode = 0x40000000u;

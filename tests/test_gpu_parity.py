@@ -428,11 +428,11 @@ def test_wide_gqa_tensor_core_head_sets(K, bits, batch, kv, qh, seq):
     assert_attention_close(got, o.attention(q, qh, scale))
 
 
-def test_decode_dev_short_main_region_leaves_slots(K):
-    """A short cache of 8 streams (the last shard of a sequence-sharded cache):
-    kivi_cache_decode_dev plans its main-region kernel with CTA slots left free
-    for the step's append and tail tiles; every step matches the oracle through
-    a key flush and value evictions."""
+def test_decode_dev_short_cache_tracks_oracle(K):
+    """A short cache of 8 streams (the size of the last shard of an 8-way
+    sequence-sharded config 4): kivi_cache_decode_dev, whose main-region kernel
+    runs on the second stream beside the step's append, matches the oracle
+    step after step through a key flush and value evictions."""
     torch = pytest.importorskip("torch")
     batch, kv, qh, dim, prompt = 1, 8, 32, 128, 20000
     g, o = pair(K, 2, 32, 128, batch, kv, dim)
