@@ -80,85 +80,212 @@ struct Quantizer {
     }
 };
 
-// Sum over the code positions k of a word of 2^23's bit pattern times
-// 2^(BITS*k), modulo 2^32 (what pack32_fast's multiply-adds add on top of the
-// codes).
-__host__ __device__ constexpr uint32_t magic_word(int bits) {
-    uint64_t acc = 0;
-    for (int k = 0; k < 32 / bits; ++k) acc += (uint64_t)0x4B000000u << (bits * k);
-    return (uint32_t)acc;
+// ---------------------------------------------------------------- paired packer
+// Blackwell's packed fp32 pair instructions (__fadd2_rn/__ffma2_rn: two IEEE
+// operations, each rounded as its scalar form) and three-input min/max carry
+// the packers below, which quantize two values per instruction.
+__device__ __forceinline__ float min3f(float a, float b, float c) {
+    float d;
+    asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+// NaN-propagating: any NaN operand gives NaN.
+__device__ __forceinline__ float max3_nan(float a, float b, float c) {
+    float d;
+    asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
 }
 
-// The 32 codes of one group packed into BITS words (LSB-first, quant.rs:
-// 296-325 / 349-374) without a branch per value: with q = (x - zero) * (1 /
-// scale), q + 2^23 rounds q to the nearest integer (ties to even) into the low
-// mantissa bits, and each word is accumulated as acc * 2^BITS + bits(q + 2^23)
-// from its last code down, the 2^23 patterns removed at the end.  q >= 0 up
-// to a NaN (x >= zero, the group's minimum), which fmaxf turns into code 0 as
-// the reference's clamp does, and q < levels + 1/2 (x <= the maximum), so no
-// upper clamp is needed.  Returns false, writing nothing, when the group needs
-// Quantizer::code's exact path: no normal reciprocal (scale 0 included), or a
-// quotient within 2^-12 of a half-integer.
+// Minimum and maximum of 32 values v(0..31), NaN operands ignored (fminf /
+// fmaxf semantics; the result is NaN only when every value is), as four
+// independent chains of eight joined at the end.
+template <typename V>
+__device__ __forceinline__ void minmax32(V v, float &mn, float &mx) {
+    float lo[4], hi[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        float a = min3f(v(8 * c), v(8 * c + 1), v(8 * c + 2));
+        float b = max3f(v(8 * c), v(8 * c + 1), v(8 * c + 2));
+        a = min3f(a, v(8 * c + 3), v(8 * c + 4));
+        b = max3f(b, v(8 * c + 3), v(8 * c + 4));
+        a = min3f(a, v(8 * c + 5), v(8 * c + 6));
+        b = max3f(b, v(8 * c + 5), v(8 * c + 6));
+        lo[c] = fminf(a, v(8 * c + 7));
+        hi[c] = fmaxf(b, v(8 * c + 7));
+    }
+    mn = fminf(min3f(lo[0], lo[1], lo[2]), lo[3]);
+    mx = fmaxf(max3f(hi[0], hi[1], hi[2]), hi[3]);
+}
+
+// One step of the paired packer for a pair of values with differences d from
+// their zeros: rm = d * rcp + 2^23 in one rounding puts round-half-even(d *
+// rcp) in the low mantissa bits, nr = 2^23 - rm = -that integer (exact), and
+// e = d * rcp + nr (one rounding) is the distance of the exact product from
+// it.  The code chain is acc = acc * base + nr, exact below 2^24.
+__device__ __forceinline__ void pair_step(float2 d, float2 rcp, float2 &acc, float2 base,
+                                          float &dev) {
+    const float2 magic = make_float2(8388608.0f, 8388608.0f);
+    const float2 rm = __ffma2_rn(d, rcp, magic);
+    const float2 nr = __ffma2_rn(rm, make_float2(-1.0f, -1.0f), magic);
+    const float2 e = __ffma2_rn(d, rcp, nr);
+    dev = max3_nan(dev, fabsf(e.x), fabsf(e.y));
+    acc = __ffma2_rn(acc, base, nr);
+}
+
+// A finished chain holds -X, X < 2^16 the chain's codes laid out at their
+// bit positions; -X - 2^23 = -(2^23 + X) is exact and the low 16 bits of its
+// pattern are X.  Returns lo's X | hi's X << 16 per lane.
+__device__ __forceinline__ void pair_words(float2 lo, float2 hi, uint32_t &wx, uint32_t &wy) {
+    const float2 nm = make_float2(-8388608.0f, -8388608.0f);
+    lo = __fadd2_rn(lo, nm);
+    hi = __fadd2_rn(hi, nm);
+    wx = __byte_perm(__float_as_uint(lo.x), __float_as_uint(hi.x), 0x5410);
+    wy = __byte_perm(__float_as_uint(lo.y), __float_as_uint(hi.y), 0x5410);
+}
+
+// Why the paired packers give the reference's codes (quant.rs:461-485): with
+// x >= zero (x not NaN), d = fl(x - zero) >= 0, and the exact product d * rcp
+// is within 2^-24 * q of d / scale (rcp = fl(1 / scale)); the reference's
+// quotient fl(d / scale) is within another 2^-24 * q, and q < 2^BITS, so the
+// two differ by less than 2^(BITS-23).  When |e| <= 1/2 - 2^(BITS-22)
+// (tie_margin), the exact product lies at least 2^(BITS-22) - 2^-25 (e's own
+// rounding) > 2^(BITS-23) from every half-integer, so it, the exact quotient
+// and fl(d / scale) round to the same integer, which is rm's; that integer lies
+// in [0, levels] because d <= fl(max - min) = scale * levels up to the same
+// 2^-24 factor.  A NaN x makes e NaN, and max3_nan carries it to dev: the
+// caller then takes the exact per-value path (Quantizer::code), as for any
+// |e| above the margin.  The margin is what keeps that path rare: a margin m
+// sends a value there with probability 2m, and a warp runs the path when any
+// of its 32 lanes' 32 values needs it (with 2^-12 for every width, about 40%
+// of the warps of a 2-bit launch; with 2^-20, 0.2%).
 template <int BITS>
-__device__ __forceinline__ bool pack32_fast(const float (&x)[32], const Quantizer &qz,
-                                            uint32_t *words) {
-    constexpr int TPW = 32 / BITS;
-    if (!qz.fast) return false;
+__device__ __forceinline__ constexpr float tie_margin() {
+    return (float)(1u << BITS) * 0x1p-22f;
+}
+
+// The 32 codes of one per-token group held as 16 pairs (x[2j], x[2j + 1])
+// with one quantizer: BITS words LSB-first (quant.rs:349-374).  Lane x of a
+// pair carries the even code positions of a word, lane y the odd ones, each
+// half word (16 bits) one chain.  False when the group needs the exact path.
+template <int BITS>
+__device__ __forceinline__ bool pack_token_pairs(const float2 (&x)[16], float zero, float rcp,
+                                                 uint32_t (&w)[BITS]) {
+    constexpr int TPW = 32 / BITS; // codes per word
+    constexpr int PPW = TPW / 2;   // pairs per word
+    constexpr int L = PPW / 2;     // pairs per half-word chain
+    const float2 nz = make_float2(-zero, -zero), rc = make_float2(rcp, rcp);
+    const float2 base = make_float2((float)(1u << (2 * BITS)), (float)(1u << (2 * BITS)));
     float dev = 0.0f;
-    uint32_t w[BITS];
 #pragma unroll
     for (int wi = 0; wi < BITS; ++wi) {
-        uint32_t acc = 0;
+        float2 acc[2];
 #pragma unroll
-        for (int k = TPW - 1; k >= 0; --k) {
-            const float q = __fmul_rn(__fsub_rn(x[wi * TPW + k], qz.zero), qz.rcp);
-            const float rm = __fadd_rn(fmaxf(q, 0.0f), 8388608.0f);
-            dev = fmaxf(dev, fabsf(__fsub_rn(q, __fsub_rn(rm, 8388608.0f))));
-            acc = acc * (1u << BITS) + __float_as_uint(rm);
+        for (int h = 0; h < 2; ++h) {
+            acc[h] = make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int j = L - 1; j >= 0; --j)
+                pair_step(__fadd2_rn(x[wi * PPW + h * L + j], nz), rc, acc[h], base, dev);
         }
-        constexpr uint32_t kMagic = magic_word(BITS);
-        w[wi] = acc - kMagic;
+        uint32_t ev, od;
+        pair_words(acc[0], acc[1], ev, od);
+        w[wi] = ev + (od << BITS);
     }
-    if (dev > 0.5f - 0x1p-12f) return false;
+    return dev <= 0.5f - tie_margin<BITS>();
+}
+
+// The 32 rows of one channel of a per-channel key group held as 16 pairs
+// (row p, row p + 16): BITS words LSB-first (quant.rs:296-325), lane x
+// carrying words 0 .. BITS/2 - 1 (rows 0-15) and lane y the rest (rows
+// 16-31), each half word one chain per lane.  False when the group needs the
+// exact path.
+template <int BITS>
+__device__ __forceinline__ bool pack_channel_rows(const float2 (&x)[16], float zero, float rcp,
+                                                  uint32_t (&w)[BITS]) {
+    constexpr int TPW = 32 / BITS; // rows per word
+    constexpr int L = TPW / 2;     // rows per half-word chain
+    const float2 nz = make_float2(-zero, -zero), rc = make_float2(rcp, rcp);
+    const float2 base = make_float2((float)(1u << BITS), (float)(1u << BITS));
+    float dev = 0.0f;
 #pragma unroll
-    for (int wi = 0; wi < BITS; ++wi) words[wi] = w[wi];
-    return true;
+    for (int wi = 0; wi < BITS / 2; ++wi) {
+        float2 acc[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            acc[h] = make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int j = L - 1; j >= 0; --j)
+                pair_step(__fadd2_rn(x[wi * TPW + h * L + j], nz), rc, acc[h], base, dev);
+        }
+        pair_words(acc[0], acc[1], w[wi], w[wi + BITS / 2]);
+    }
+    return dev <= 0.5f - tie_margin<BITS>();
+}
+
+// BITS code words to `words`, as one or more vector stores when aligned.
+template <int BITS>
+__device__ __forceinline__ void store_words(uint32_t *words, const uint32_t (&w)[BITS]) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(words);
+    if constexpr (BITS == 2) {
+        if ((a & 7u) == 0) {
+            *reinterpret_cast<uint2 *>(words) = make_uint2(w[0], w[1]);
+            return;
+        }
+    } else {
+        if ((a & 15u) == 0) {
+#pragma unroll
+            for (int i = 0; i < BITS; i += 4)
+                *reinterpret_cast<uint4 *>(words + i) = make_uint4(w[i], w[i + 1], w[i + 2], w[i + 3]);
+            return;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < BITS; ++i) words[i] = w[i];
 }
 
 // Per-channel key quantization of channel `d` of one 32-row group whose rows
 // are base + u * stride (BITS known at compile time): the 32 values held in
-// registers, packed by pack32_fast unless the group needs the exact path.
-// Same results as quant_key_channel.
+// registers as (row p, row p + 16) pairs, min/max by minmax32, codes by
+// pack_channel_rows unless the group needs the exact path.  Same results as
+// quant_key_channel.
 template <int BITS, int STRIDE = 0>
 __device__ __forceinline__ float quant_key_channel_g32(const float *base, int stride, int d,
                                                        uint32_t *words, float2 *param) {
     constexpr float kLevels = (float)((1u << BITS) - 1u);
-    float x[32];
+    float2 x[16];
     if (STRIDE != 0) { // compile-time row pitch: 32 loads at immediate offsets
         const float *p = base + d;
 #pragma unroll
-        for (int u = 0; u < 32; ++u) x[u] = p[u * STRIDE];
+        for (int u = 0; u < 16; ++u) x[u] = make_float2(p[u * STRIDE], p[(u + 16) * STRIDE]);
     } else {
 #pragma unroll
-        for (int u = 0; u < 32; ++u) x[u] = base[(int64_t)u * stride + d];
+        for (int u = 0; u < 16; ++u)
+            x[u] = make_float2(base[(int64_t)u * stride + d], base[(int64_t)(u + 16) * stride + d]);
     }
-    float mn = INFINITY, mx = -INFINITY;
-#pragma unroll
-    for (int u = 0; u < 32; ++u) {
-        mn = fminf(mn, x[u]);
-        mx = fmaxf(mx, x[u]);
-    }
+    float mn, mx;
+    minmax32([&](int i) { return i < 16 ? x[i].x : x[i - 16].y; }, mn, mx);
     const float scale = scale_of(__fsub_rn(mx, mn), kLevels);
     *param = make_float2(scale, mn);
     const Quantizer qz(mn, scale, kLevels);
-    if (pack32_fast<BITS>(x, qz, words)) return scale;
+    uint32_t w[BITS];
+    if (!(qz.fast && pack_channel_rows<BITS>(x, mn, qz.rcp, w))) {
+        constexpr int TPW = 32 / BITS;
 #pragma unroll
-    for (int w = 0; w < BITS; ++w) {
-        uint32_t word = 0;
+        for (int wi = 0; wi < BITS; ++wi) {
+            uint32_t word = 0;
 #pragma unroll
-        for (int k = 0; k < 32 / BITS; ++k) word |= qz.code(x[w * (32 / BITS) + k]) << (k * BITS);
-        words[w] = word;
+            for (int k = 0; k < TPW; ++k) {
+                const int u = wi * TPW + k;
+                word |= qz.code(u < 16 ? x[u].x : x[u - 16].y) << (k * BITS);
+            }
+            w[wi] = word;
+        }
     }
+    store_words<BITS>(words, w);
     return scale;
 }
 
@@ -185,39 +312,48 @@ __device__ __forceinline__ float quant_key_channel(const Geom &g, const float *c
 }
 
 // Per-token value quantization of one 32-channel group (BITS known at
-// compile time): the group is read as eight float4 (callers check the row is
-// 16-byte aligned), same arithmetic as the generic loop below.
+// compile time) held as 16 pairs: min/max by minmax32 and the codes by
+// pack_token_pairs; groups that need the exact path take the generic loop's
+// arithmetic.  quant_value_g32 reads the group as eight float4 (callers check
+// the row is 16-byte aligned).
 template <int BITS>
-__device__ __forceinline__ float quant_value_g32(const float *grp, uint32_t *words, float2 *param) {
+__device__ __forceinline__ float quant_value_pairs(const float2 (&x)[16], uint32_t *words,
+                                                   float2 *param) {
     constexpr float kLevels = (float)((1u << BITS) - 1u);
-    const float4 *grp4 = reinterpret_cast<const float4 *>(grp);
-    float x[32];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const float4 v = grp4[i];
-        x[4 * i] = v.x;
-        x[4 * i + 1] = v.y;
-        x[4 * i + 2] = v.z;
-        x[4 * i + 3] = v.w;
-    }
-    float mn = INFINITY, mx = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-        mn = fminf(mn, x[i]);
-        mx = fmaxf(mx, x[i]);
-    }
+    float mn, mx;
+    minmax32([&](int i) { return (i & 1) ? x[i >> 1].y : x[i >> 1].x; }, mn, mx);
     const float scale = scale_of(__fsub_rn(mx, mn), kLevels);
     *param = make_float2(scale, mn);
     const Quantizer qz(mn, scale, kLevels);
-    if (pack32_fast<BITS>(x, qz, words)) return scale;
+    uint32_t w[BITS];
+    if (!(qz.fast && pack_token_pairs<BITS>(x, mn, qz.rcp, w))) {
 #pragma unroll
-    for (int w = 0; w < BITS; ++w) {
-        uint32_t word = 0;
+        for (int wi = 0; wi < BITS; ++wi) {
+            uint32_t word = 0;
 #pragma unroll
-        for (int k = 0; k < 32 / BITS; ++k) word |= qz.code(x[w * (32 / BITS) + k]) << (k * BITS);
-        words[w] = word;
+            for (int k = 0; k < 32 / BITS; k += 2) {
+                const float2 v = x[(wi * (32 / BITS) + k) >> 1];
+                word |= qz.code(v.x) << (k * BITS);
+                word |= qz.code(v.y) << ((k + 1) * BITS);
+            }
+            w[wi] = word;
+        }
     }
+    store_words<BITS>(words, w);
     return scale;
+}
+
+template <int BITS>
+__device__ __forceinline__ float quant_value_g32(const float *grp, uint32_t *words, float2 *param) {
+    const float4 *grp4 = reinterpret_cast<const float4 *>(grp);
+    float2 x[16];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 v = grp4[i];
+        x[2 * i] = make_float2(v.x, v.y);
+        x[2 * i + 1] = make_float2(v.z, v.w);
+    }
+    return quant_value_pairs<BITS>(x, words, param);
 }
 
 // Per-token value quantization of channel group `cg` of one token row.
@@ -409,7 +545,7 @@ __global__ void __launch_bounds__(256) append_small_kernel(Geom g, Store st, con
 // thread; 64 registers keep 8 CTAs per SM); other groups (rows from the
 // residual, other group sizes) go through the row table.
 // BITS != 0: group 32 with BITS-bit codes (one code width per instantiation
-// keeps the kernel's code small); BITS == 0: any geometry.
+// keeps the kernel's code small); BITS == 0: any other geometry.
 template <int BITS>
 __global__ void __launch_bounds__(128, 8) key_groups_kernel(Geom g, Store st, const float *res,
                                                             int nres, const float *in,
@@ -422,19 +558,15 @@ __global__ void __launch_bounds__(128, 8) key_groups_kernel(Geom g, Store st, co
     float2 *kp = st.kparams + (int64_t)s * kparam_stride(g, st.cap);
     const int64_t og = out_group0 + gi;
     float kmax = 0.0f;
-    if (g.G == 32 && c0 >= nres) {
+    if (BITS != 0 && c0 >= nres) {
         // every row from the input: one contiguous span
         const float *base = in + ((int64_t)s * in_seq + (c0 - nres)) * D;
         for (int d = threadIdx.x; d < D; d += blockDim.x) {
             uint32_t *words = kc + (og * D + d) * g.ipc;
             float2 *param = kp + og * D + d;
-            float sc;
-            if (BITS != 0 && D == 128)
-                sc = quant_key_channel_g32<(BITS ? BITS : 2), 128>(base, D, d, words, param);
-            else if (BITS != 0) sc = quant_key_channel_g32<(BITS ? BITS : 2)>(base, D, d, words, param);
-            else if (g.bits == 2) sc = quant_key_channel_g32<2>(base, D, d, words, param);
-            else if (g.bits == 4) sc = quant_key_channel_g32<4>(base, D, d, words, param);
-            else sc = quant_key_channel_g32<8>(base, D, d, words, param);
+            const float sc =
+                D == 128 ? quant_key_channel_g32<(BITS ? BITS : 2), 128>(base, D, d, words, param)
+                         : quant_key_channel_g32<(BITS ? BITS : 2)>(base, D, d, words, param);
             kmax = fmaxf(kmax, fabsf(sc));
         }
         raise_bound(st.kbound, s, kmax);

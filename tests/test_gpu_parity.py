@@ -172,6 +172,23 @@ def test_codec_near_ties_bit_exact(K, bits, group, axis):
     assert (qt.codes == oc).all()
 
 
+@pytest.mark.parametrize("bits", [2, 4, 8])
+@pytest.mark.parametrize("axis", [0, 1])
+def test_codec_nan_values_bit_exact(K, bits, axis):
+    """NaN inputs code to 0 (quant.rs:474-485, Rust's saturating `as u32`) and
+    are skipped by the group min/max (f32::min/max); groups with and without
+    NaNs, every code width, both axes (the paired packers' exact-path hand-off)."""
+    rng = np.random.default_rng(77 + bits + 10 * axis)
+    batch, heads, tokens, dim = 2, 2, 128, 128
+    data = (rng.standard_normal((batch, heads, tokens, dim)) * 3).astype(np.float32)
+    data[rng.random(data.shape) < 0.01] = np.nan
+    fn = K.quantize_per_channel if axis == 0 else K.quantize_per_token
+    qt = fn(data, batch, heads, tokens, dim, bits, 32)
+    oc, op = O.quantize(axis == 0, data, batch, heads, tokens, dim, bits, 32)
+    assert (qt.params.view(np.uint32) == op.view(np.uint32)).all()
+    assert (qt.codes == oc).all()
+
+
 def test_pytorch_golden_words(K):
     """tests/quant.rs:13-41, examples/pytorch_golden.rs:16-67"""
     dim, seq = 32, 64
