@@ -343,15 +343,32 @@ __device__ __forceinline__ float quant_value_pairs(const float2 (&x)[16], uint32
     return scale;
 }
 
+// Eight consecutive floats at a 32-byte aligned address in one 256-bit load
+// (sm_100): a warp reading one 128-byte group per thread then makes four
+// requests of the L1 instead of eight.  Read-only path without L1 allocation:
+// the bulk append's inputs are read once and nothing writes them meanwhile.
+__device__ __forceinline__ void load8_pairs(const float *p, float2 &a, float2 &b, float2 &c,
+                                            float2 &d) {
+    asm("ld.global.nc.L1::no_allocate.v8.f32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+        : "=f"(a.x), "=f"(a.y), "=f"(b.x), "=f"(b.y), "=f"(c.x), "=f"(c.y), "=f"(d.x), "=f"(d.y)
+        : "l"(p));
+}
+
 template <int BITS>
 __device__ __forceinline__ float quant_value_g32(const float *grp, uint32_t *words, float2 *param) {
-    const float4 *grp4 = reinterpret_cast<const float4 *>(grp);
     float2 x[16];
+    if ((reinterpret_cast<uintptr_t>(grp) & 31u) == 0) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const float4 v = grp4[i];
-        x[2 * i] = make_float2(v.x, v.y);
-        x[2 * i + 1] = make_float2(v.z, v.w);
+        for (int i = 0; i < 4; ++i)
+            load8_pairs(grp + 8 * i, x[4 * i], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]);
+    } else {
+        const float4 *grp4 = reinterpret_cast<const float4 *>(grp);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 v = grp4[i];
+            x[2 * i] = make_float2(v.x, v.y);
+            x[2 * i + 1] = make_float2(v.z, v.w);
+        }
     }
     return quant_value_pairs<BITS>(x, words, param);
 }
