@@ -168,6 +168,17 @@ __device__ __forceinline__ void mma16816(float4 &d, uint32_t a0, uint32_t a1, ui
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// The first tile of a fresh sum: D = A B with a zero C operand (D is
+// written, not read, so its registers need no zero fill).
+__device__ __forceinline__ void mma16816_first(float4 &d, uint32_t a0, uint32_t a1, uint32_t a2,
+                                               uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%10,%10,%10,%10};"
+        : "=f"(d.x), "=f"(d.y), "=f"(d.z), "=f"(d.w)
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
+}
+
 // 2^k as a float for k in [-126, 127].
 __device__ __forceinline__ float exp2i(int k) {
     k = max(-126, min(127, k));
@@ -503,16 +514,19 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : KIVI_TC_
             // ---------------- keys: A = codes - mid (exact), D = code sums per (token, head part)
             float4 dk[NT][2];
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) dk[nt][0] = dk[nt][1] = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
             for (int kt = 0; kt < 8; ++kt) {
                 const uint32_t *w = KC + kw + 16 * kt * IPC;
                 uint32_t av[8];
                 perm.eight(w[0], w[IPC], w[8 * IPC], w[9 * IPC], av);
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
-                    mma16816(dk[nt][0], av[0], av[1], av[4], av[5], bk[nt][kt][0], bk[nt][kt][1]);
-                    mma16816(dk[nt][1], av[2], av[3], av[6], av[7], bk[nt][kt][0], bk[nt][kt][1]);
+                    if (kt == 0) {
+                        mma16816_first(dk[nt][0], av[0], av[1], av[4], av[5], bk[nt][kt][0], bk[nt][kt][1]);
+                        mma16816_first(dk[nt][1], av[2], av[3], av[6], av[7], bk[nt][kt][0], bk[nt][kt][1]);
+                    } else {
+                        mma16816(dk[nt][0], av[0], av[1], av[4], av[5], bk[nt][kt][0], bk[nt][kt][1]);
+                        mma16816(dk[nt][1], av[2], av[3], av[6], av[7], bk[nt][kt][0], bk[nt][kt][1]);
+                    }
                 }
             }
 
@@ -589,8 +603,6 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : KIVI_TC_
             for (int cg = 0; cg < 4; ++cg) {
                 float4 t[NT][2];
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt) t[nt][0] = t[nt][1] = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
                 for (int kk = 0; kk < 2; ++kk) {
                     // tokens 16kk + c, +4, +8, +12 (K positions 2c, 2c+1, 2c+8, 2c+9)
                     const uint32_t *w = VC + vw + (16 * kk) * 4 * IPC + cg * IPC;
@@ -598,21 +610,31 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : KIVI_TC_
                     perm.eight(w[0], w[16 * IPC], w[32 * IPC], w[48 * IPC], av);
 #pragma unroll
                     for (int nt = 0; nt < NT; ++nt) {
-                        mma16816(t[nt][0], av[0], av[1], av[4], av[5], bv[kk][nt][cg][0],
-                                 bv[kk][nt][cg][1]);
-                        mma16816(t[nt][1], av[2], av[3], av[6], av[7], bv[kk][nt][cg][0],
-                                 bv[kk][nt][cg][1]);
+                        if (kk == 0) {
+                            mma16816_first(t[nt][0], av[0], av[1], av[4], av[5], bv[kk][nt][cg][0],
+                                           bv[kk][nt][cg][1]);
+                            mma16816_first(t[nt][1], av[2], av[3], av[6], av[7], bv[kk][nt][cg][0],
+                                           bv[kk][nt][cg][1]);
+                        } else {
+                            mma16816(t[nt][0], av[0], av[1], av[4], av[5], bv[kk][nt][cg][0],
+                                     bv[kk][nt][cg][1]);
+                            mma16816(t[nt][1], av[2], av[3], av[6], av[7], bv[kk][nt][cg][0],
+                                     bv[kk][nt][cg][1]);
+                        }
                     }
                 }
+                // the group's sums into the accumulators, two lanes of a
+                // float4 per packed add (each the scalar IEEE add)
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
                     for (int jm = 0; jm < 2; ++jm) {
                         float4 &r4 = acc[nt][2 * cg + jm];
-                        r4.x += t[nt][jm].x;
-                        r4.y += t[nt][jm].y;
-                        r4.z += t[nt][jm].z;
-                        r4.w += t[nt][jm].w;
+                        const float2 lo = __fadd2_rn(make_float2(r4.x, r4.y),
+                                                     make_float2(t[nt][jm].x, t[nt][jm].y));
+                        const float2 hi = __fadd2_rn(make_float2(r4.z, r4.w),
+                                                     make_float2(t[nt][jm].z, t[nt][jm].w));
+                        r4 = make_float4(lo.x, lo.y, hi.x, hi.y);
                     }
                 }
             }
