@@ -198,11 +198,14 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
 
 // Splits (x0, x1) into fp16 high parts (x truncated to 11 significant bits)
 // and low parts (exact remainders); returns the pair of packed registers.
+// The remainders are one packed fma, x - t = t * -1 + x (exact product, one
+// rounding: the scalar subtraction's result).
 __device__ __forceinline__ void split2(float x0, float x1, uint32_t &hi, uint32_t &lo) {
     const float t0 = __uint_as_float(__float_as_uint(x0) & 0xFFFFE000u);
     const float t1 = __uint_as_float(__float_as_uint(x1) & 0xFFFFE000u);
     hi = pack_half2(t0, t1);
-    lo = pack_half2(x0 - t0, x1 - t1);
+    const float2 r = __ffma2_rn(make_float2(t0, t1), make_float2(-1.0f, -1.0f), make_float2(x0, x1));
+    lo = pack_half2(r.x, r.y);
 }
 
 // B fragment of one 16-deep K tile for a (head, part) column pair: lanes with
@@ -562,9 +565,16 @@ __global__ void __launch_bounds__(kTcThreads, NT == 1 ? KIVI_TC_MINB1 : KIVI_TC_
                 }
                 // p' = p 2^cv = 2^(x - (mref - cv))
                 const float mp = mref[nt] - cv;
+                // x - mp for two tokens per packed fma (mp * -1 + x, the
+                // scalar subtraction's result)
+                const float2 nmp = make_float2(-1.0f, -1.0f), mp2 = make_float2(mp, mp);
+                const float2 d01 = __ffma2_rn(mp2, nmp, make_float2(x[0], x[1]));
+                const float2 d23 = __ffma2_rn(mp2, nmp, make_float2(x[2], x[3]));
                 float p[4];
-#pragma unroll
-                for (int jj = 0; jj < 4; ++jj) p[jj] = exp2f(x[jj] - mp);
+                p[0] = exp2f(d01.x);
+                p[1] = exp2f(d01.y);
+                p[2] = exp2f(d23.x);
+                p[3] = exp2f(d23.y);
                 l[nt] += (p[0] + p[1]) + (p[2] + p[3]);
                 float *ph = pw + (nt * 4 + c) * kPStride + koff;
 #pragma unroll
