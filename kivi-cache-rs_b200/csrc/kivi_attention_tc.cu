@@ -917,9 +917,14 @@ __device__ __forceinline__ float4 tail_value4(const TailArgs &a, const uint32_t 
 
 // SPLIT (at most 2 query heads per kv head): the four warps share each head's
 // work (channel quarters for the logits, one channel per thread for the
-// output) instead of one warp per head.
+// output) instead of one warp per head.  Register budgets: the 2-bit
+// one-warp-per-head form is held to 5 CTAs per SM (at most 102 registers;
+// left free, the compiler's allocation of it moved with unrelated code in this
+// file: 96 registers in one build, 127 in another, 4 CTAs per SM and a slower
+// tail), the other forms to 4 (at most 128).
 template <int BITS, bool SPLIT>
-__global__ void __launch_bounds__(kTailThreads) attn_tail_kernel(const TailArgs a) {
+__global__ void __launch_bounds__(kTailThreads, (BITS == 2 && !SPLIT) ? 5 : 4)
+    attn_tail_kernel(const TailArgs a) {
     pdl_wait();
     pdl_trigger();
     __shared__ float Ks[kTailTokens * kTailPitch];
