@@ -1,16 +1,20 @@
 // kivi_quant.cu -- KIVI quantize-and-pack kernels for sm_100a.
 //
 // Bit-exactness with the reference codec (quant.rs:275-377, 453-485):
-//   * group min/max with fminf/fmaxf (Rust f32::min/max ignore a NaN operand
-//     the same way) -- exact, so reduction order is free;
+//   * group min/max with fminf/fmaxf or three-input min/max (Rust
+//     f32::min/max ignore a NaN operand the same way) -- exact, so reduction
+//     order is free;
 //   * scale = (max - min) / levels with IEEE division (__fdiv_rn), 0 when the
 //     span is 0 (quant.rs:453-459);
 //   * code = clamp(round_half_even((x - zero) / scale), 0, levels): the
 //     quotient is >= 0, and rintf (round-to-nearest-even) equals the
 //     reference's floor/frac/parity rounding (quant.rs:474-485) for every
 //     finite input; NaN -> 0 like Rust's saturating `as u32`.  The quotient
-//     comes from a reciprocal multiply, redone with IEEE division whenever it
-//     lies close enough to a rounding boundary to matter (Quantizer below);
+//     comes from a reciprocal multiply (the bulk kernels' paired packers round
+//     the exact product d * rcp, two values per packed fp32 instruction), and
+//     any group with a quotient close enough to a rounding boundary to matter
+//     takes the per-value path that redoes it with IEEE division (Quantizer
+//     below);
 //   * codes packed first-element-in-low-bits (quant.rs:312-322);
 //   * dequantization is one fused multiply-add fma(code, scale, zero)
 //     (quant.rs:404-406).
@@ -559,8 +563,10 @@ __global__ void __launch_bounds__(256) append_small_kernel(Geom g, Store st, con
 // grid (ngroups, n): one CTA per (key group, stream), one thread per channel.
 // A 32-row group whose rows all come from the input (one contiguous span) is
 // quantized from registers by quant_key_channel_g32 (32 independent loads per
-// thread; 64 registers keep 8 CTAs per SM); other groups (rows from the
-// residual, other group sizes) go through the row table.
+// thread; 64 registers keep 8 CTAs per SM, at the cost of a few bytes of
+// spill at 2 and 8 bits, which measured faster than 6 CTAs per SM without);
+// other groups (rows from the residual, other group sizes) go through the row
+// table.
 // BITS != 0: group 32 with BITS-bit codes (one code width per instantiation
 // keeps the kernel's code small); BITS == 0: any other geometry.
 template <int BITS>
